@@ -1,0 +1,358 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 backend for the torch-pyodide hot path.
+
+Default workload: the fused AdamW optimizer step over 64 parameter tensors
+cycling [4096,4096], [4096], [1024,4096], [4096,1024] (402,718,720 fp32
+elements), params ~N(0,0.02), grads ~N(0,1e-3), moments zero-initialised and
+warmed for 3 steps.  One step = one fused multi-tensor AdamW launch over the
+whole group; the metric is algorithmic HBM bandwidth, 28 B per element (read
+param, grad, exp_avg, exp_avg_sq; write param, exp_avg, exp_avg_sq).  The
+working set (11.3 GB per step) is ~90x the 126 MB L2, so no flush is needed.
+
+Multi-GPU: the optimizer step does not shard (each rank updates its own
+replica), so --gpus N runs N independent replicas, one process per GPU; value is
+the bytes all ranks moved divided by the slowest rank's time.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "torch-pyodide_b200"))
+
+SHAPES = [[4096, 4096], [4096], [1024, 4096], [4096, 1024]]
+NTENSORS = 64
+BYTES_PER_ELEM = 28
+LR, B1, B2, EPS, WD = 1e-3, 0.9, 0.999, 1e-8, 0.01
+
+
+def numel(s):
+    r = 1
+    for v in s:
+        r *= v
+    return r
+
+
+def adam_scalars(step):
+    bc1 = 1.0 - B1 ** step
+    bc2 = 1.0 - B2 ** step
+    return LR / bc1, 1.0 / math.sqrt(bc2)  # optim/__init__.py:385-388
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples (200 ms) taken while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[4:8]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(gpus):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != gpus:
+        raise SystemExit(f"--gpus {gpus} but WORLD_SIZE={world}: launch with torchrun --nproc-per-node {gpus}")
+    return rank, world, local
+
+
+# ---------------------------------------------------------------------------
+# CPU arms: the oracle (a C/OpenMP restatement of adamw_step.wgsl)
+
+def cpu_adamw(sample_tensors: int, steps: int) -> dict:
+    """Time the oracle's AdamW on the first `sample_tensors` tensors of the
+    workload with all host threads; returns GB/s of algorithmic traffic."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import oracle_runtime as O
+    L = O.lib()
+    rng = np.random.default_rng(0)
+    ts = []
+    for i in range(sample_tensors):
+        n = numel(SHAPES[i % 4])
+        p = (rng.standard_normal(n, dtype=np.float32) * 0.02)
+        g = (rng.standard_normal(n, dtype=np.float32) * 1e-3)
+        ts.append((p, g, np.zeros(n, np.float32), np.zeros(n, np.float32)))
+    elems = sum(t[0].size for t in ts)
+
+    def step(k):
+        ss, isb = adam_scalars(k)
+        for p, g, m, v in ts:
+            L.or_adamw_step(O.fp(p), O.fp(g), O.fp(m), O.fp(v), p.size, LR, B1, B2, EPS, WD, ss, isb)
+
+    step(1)  # warm-up
+    times = []
+    for k in range(steps):
+        t0 = time.perf_counter()
+        step(k + 2)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {"gbs": BYTES_PER_ELEM * elems / t / 1e9, "elems": elems, "sec": t, "times": times}
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference algorithm on host cores (the WGSL
+    shaders cannot run here: no WebGPU), same metric."""
+    if rank != 0:
+        return
+    cores = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+    sample = 8
+    r = cpu_adamw(sample, max(1, args.steps))
+    elems = r["elems"]
+    line = {
+        "impl": "reference", "metric": "fused AdamW HBM GB/s", "value": round(r["gbs"], 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(r["sec"] * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "adamw 64 tensors cycling [4096,4096],[4096],[1024,4096],[4096,1024]",
+                   "sample": f"first {sample} tensors ({elems} elements) per step"},
+        "cpu_baseline": {"value": round(r["gbs"], 3), "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": f"{sample} of 64 tensors, {elems} elements, median of {len(r['times'])} steps"},
+        "e2e": {"value": round(r["gbs"], 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+
+def run_ours(args, rank, world, local):
+    import ctypes
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", init_method="env://", device_id=torch.device("cuda", local),
+                                timeout=__import__("datetime").timedelta(seconds=300))
+    from tpcuda import CudaRuntime
+    from tpcuda._lib import check
+    rt = CudaRuntime(local)
+    lib = rt.lib
+    stream = torch.cuda.ExternalStream(rt.stream(), device=torch.device("cuda", local))
+
+    # parameters and state, built with the library's own creation kernels
+    rt.setSeed(1000 + rank)
+    P, G, M, V = [], [], [], []
+    nt = args.tensors
+    for i in range(nt):
+        s = SHAPES[i % 4]
+        P.append(rt.normal(s, "float32", 0.0, 0.02))
+        G.append(rt.normal(s, "float32", 0.0, 1e-3))
+        M.append(rt.zeros(s, "float32"))
+        V.append(rt.zeros(s, "float32"))
+    elems = sum(numel(h["shape"]) for h in P)
+    ptr = lambda hs: (ctypes.c_void_p * len(hs))(*[rt.devicePtr(h["id"]) for h in hs])  # noqa: E731
+    numels = (ctypes.c_int64 * nt)(*[numel(h["shape"]) for h in P])
+    group = ctypes.c_int64(0)
+    check(lib.tpk_group_create(nt, ptr(P), ptr(G), ptr(M), ptr(V), numels, ctypes.byref(group)))
+
+    step_no = [0]
+
+    def step():
+        step_no[0] += 1
+        ss, isb = adam_scalars(step_no[0])
+        check(lib.tpk_adam_group(group.value, 0, LR, B1, B2, EPS, WD, ss, isb))
+
+    # 3 warm steps of the moments with regenerated grads (seed + step)
+    for k in range(3):
+        for i, h in enumerate(G):
+            rt.destroy(h["id"])
+        rt.setSeed(2000 + 97 * rank + k)
+        G = [rt.normal(SHAPES[i % 4], "float32", 0.0, 1e-3) for i in range(nt)]
+        check(lib.tpk_group_destroy(group.value))
+        check(lib.tpk_group_create(nt, ptr(P), ptr(G), ptr(M), ptr(V), numels, ctypes.byref(group)))
+        step()
+    for _ in range(args.warmup):
+        step()
+    rt.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        rt.synchronize()
+
+    # ---- device-resident timed region ----
+    clocks = ClockSampler(local)
+    barrier()
+    clocks.start()
+    launches0 = rt.kernelLaunches()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    e1.synchronize()
+    launches = rt.kernelLaunches() - launches0
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    ms_step = ms_max / args.steps
+    total_bytes = BYTES_PER_ELEM * elems * world
+    value = total_bytes / (ms_step * 1e-3) / 1e9
+    kernel_gbs = BYTES_PER_ELEM * elems / (ms / args.steps * 1e-3) / 1e9
+
+    # ---- end to end through the handle-level C ABI, grads from pinned host ----
+    host_g = [torch.empty(numel(SHAPES[i % 4]), dtype=torch.float32, pin_memory=True) for i in range(nt)]
+    for i, hg in enumerate(host_g):
+        hg.normal_(0.0, 1e-3)
+    ids = lambda hs: [h["id"] for h in hs]  # noqa: E731
+    gptr = [rt.devicePtr(h["id"]) for h in G]
+    readback = np.zeros(1, np.float32)
+    h2d = sum(hg.numel() * 4 for hg in host_g)
+    e2e_steps = max(2, min(args.steps, 10))
+
+    def e2e_step():
+        for i, hg in enumerate(host_g):
+            check(lib.tp_memcpy_h2d(ctypes.c_void_p(gptr[i]), ctypes.c_void_p(hg.data_ptr()), hg.numel() * 4))
+        step_no[0] += 1
+        ss, isb = adam_scalars(step_no[0])
+        rt.adamWStepMulti(ids(P), ids(G), ids(M), ids(V), LR, B1, B2, EPS, WD, ss, isb)
+        check(lib.tp_memcpy_d2h(readback.ctypes.data_as(ctypes.c_void_p), ctypes.c_void_p(rt.devicePtr(P[0]["id"])),
+                                4))
+
+    e2e_step()
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    f1.record(stream)
+    f1.synchronize()
+    t2 = torch.tensor([f0.elapsed_time(f1)], device="cuda")
+    if world > 1:
+        dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t2.item()) / e2e_steps
+    e2e_value = total_bytes / (e2e_ms * 1e-3) / 1e9
+
+    line = None
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        line = {
+            "metric": "fused AdamW HBM GB/s", "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": "adamw 64 tensors cycling [4096,4096],[4096],[1024,4096],[4096,1024]",
+                       "elements_per_rank": elems, "bytes_per_element": BYTES_PER_ELEM,
+                       "l2": "working set 11.3 GB per step >> 126 MB L2, no flush",
+                       "parallelism": f"replicas x{world}", "lr": LR, "betas": [B1, B2], "eps": EPS,
+                       "weight_decay": WD},
+            "gpu_launches": int(launches),
+            "clocks": clk,
+            "roofline": {"bound": "hbm", "achieved": round(kernel_gbs, 2), "peak": peak, "unit": "GB/s",
+                         "frac": round(kernel_gbs / peak, 4), "traffic": None,
+                         "peak_source": f"{peak_kind} hbm_gbs", "kernel": "k_adam_multi<true>"},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": 4,
+                    "path": "tp_memcpy_h2d(pinned grads) + tp_adamw_step_multi(ids) + tp_memcpy_d2h"},
+        }
+        tf = os.path.join(ROOT, "profiles", "adamw_traffic.json")
+        if os.path.exists(tf):
+            line["roofline"]["traffic"] = json.load(open(tf)).get("bytes_per_launch")
+    check(lib.tpk_group_destroy(group.value))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        if world == 1 and not args.no_cpu_baseline:
+            os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
+            r = cpu_adamw(8, 5)
+            line["cpu_baseline"] = {"value": round(r["gbs"], 3), "unit": "GB/s", "cores": os.cpu_count() or 1,
+                                    "kind": "port",
+                                    "sample": f"oracle AdamW on 8 of 64 tensors ({r['elems']} elements), "
+                                              f"median of 5 steps"}
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tensors", type=int, default=NTENSORS,
+                    help="number of parameter tensors (64 = the benchmark; fewer for profiler captures)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank, world, local = dist_setup(args.gpus)
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+    else:
+        run_ours(args, rank, world, local)
+
+
+if __name__ == "__main__":
+    main()

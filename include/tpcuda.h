@@ -1,0 +1,231 @@
+/*
+ * libtpcuda: C ABI of the B200 CUDA backend for the torch-pyodide tensor-op
+ * hot path.
+ *
+ * It replaces the bridge python/torch/_runtime.py:15-39 -> runtime.mjs
+ * (TorchPyodideRuntime, runtime/src/runtime.ts:17-1212) -> WGSL compute
+ * shaders.  Two layers are exported:
+ *
+ *   tp_*   handle level: one entry per hot runtime.ts method, same argument
+ *          order and meaning, tensors named by int64 ids owned by the library
+ *          (the reference's TensorRegistry, runtime/src/ops/tensorRegistry.ts).
+ *          Each op writes the new tensor's {id, shape, dtype} into a tp_handle
+ *          (the reference's TensorHandle, runtime/src/ops/types.ts:10-15).
+ *   tpk_*  pointer level: the same kernels on caller-owned device pointers
+ *          with plain sizes, asynchronous on the library stream, no allocation
+ *          (the step driver captures these in CUDA graphs).
+ *
+ * Every function returns 0 (TP_OK) or a negative status; tp_last_error()
+ * gives the message for the calling thread.  A JS Error in the reference
+ * becomes a non-zero status here and a RuntimeError in the Python shim, so the
+ * reference's try/except fallbacks keep working (python/torch/optim/
+ * __init__.py:193,298,404).
+ *
+ * Storage: every dtype is stored as float32 (runtime/src/ops/device.ts:
+ * 362-364); the dtype code is a tag.  Index outputs of the new max-pool and
+ * max-along-dim entries are physically int32.
+ *
+ * Ordering: all work runs on one CUDA stream per process (tp_get_stream); the
+ * only host synchronisation points are tp_to_host and tp_synchronize, as in
+ * the reference where readbacks are the only syncs (runtime.ts:1046-1050).
+ * Not re-entrant across threads, like the single-threaded JS event loop.
+ */
+#ifndef TPCUDA_H
+#define TPCUDA_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TP_API __attribute__((visibility("default")))
+#define TP_MAX_DIMS 8
+
+/* status codes */
+enum {
+  TP_OK = 0,
+  TP_ERR_ARG = -1,      /* bad shape / id / argument (a JS Error("...") in the reference) */
+  TP_ERR_CUDA = -2,     /* CUDA runtime error */
+  TP_ERR_OOM = -3,      /* device or host allocation failed */
+  TP_ERR_NCCL = -4,     /* collective failed or timed out */
+  TP_ERR_TIMEOUT = -5,  /* a bounded device-side wait gave up */
+  TP_ERR_INTERNAL = -6
+};
+
+/* dtype tags, the SupportedDType list of runtime/src/ops/types.ts:17-29 */
+enum {
+  TP_FLOAT32 = 0, TP_FLOAT16 = 1, TP_BFLOAT16 = 2, TP_INT8 = 3, TP_INT16 = 4, TP_INT32 = 5,
+  TP_INT64 = 6, TP_UINT8 = 7, TP_UINT16 = 8, TP_UINT32 = 9, TP_UINT64 = 10, TP_BOOL = 11
+};
+
+/* the reference TensorHandle {id, shape, dtype} (runtime/src/ops/types.ts:10-15) */
+typedef struct tp_handle {
+  int64_t id;
+  int32_t ndim;
+  int32_t dtype;
+  int64_t shape[TP_MAX_DIMS];
+} tp_handle;
+
+/* ---- device, errors, stream --------------------------------------------- */
+/* runtime.ts:49-51 init / device.ts:126-188 ensureReady */
+TP_API int tp_init(int device);
+/* runtime.ts:1056-1058 isAvailable: 1 if a CUDA device is present */
+TP_API int tp_is_available(void);
+/* runtime.ts:1064-1066 deviceCount */
+TP_API int tp_device_count(int* out);
+TP_API const char* tp_last_error(void);
+TP_API int tp_synchronize(void);
+/* the library's CUDA stream (cudaStream_t) for interop and event timing */
+TP_API int tp_get_stream(void** out);
+/* runtime.ts:1084-1090 memoryAllocated / memoryReserved */
+TP_API int tp_memory_allocated(int64_t* out);
+TP_API int tp_memory_reserved(int64_t* out);
+/* runtime.ts:1076-1082 getDeviceName */
+TP_API int tp_device_name(char* buf, int len);
+/* number of kernels this library has launched since load (a counter kept on
+ * the host at every launch site) */
+TP_API int tp_kernel_launches(int64_t* out);
+
+/* ---- registry ------------------------------------------------------------- */
+/* creationOps.ts:25-37 tensorFromData (values already coerced to f32) */
+TP_API int tp_tensor_from_data(const float* host, const int64_t* shape, int ndim, int dtype, tp_handle* out);
+/* runtime.ts:1046-1050 toList: copies numel f32 values (int32 index tensors
+ * are converted to f32) into host memory and synchronises */
+TP_API int tp_to_host(int64_t id, float* dst, int64_t numel);
+/* runtime.ts:1052-1054 destroy */
+TP_API int tp_destroy(int64_t id);
+TP_API int tp_meta(int64_t id, tp_handle* out);
+/* the device pointer behind an id (for pointer-level calls) */
+TP_API int tp_device_ptr(int64_t id, void** out);
+/* raw HBM allocations from the library's pool, for pointer-level calls; the
+ * memcpy/memset helpers below are ordered on the library stream and
+ * tp_memcpy_d2h synchronises */
+TP_API int tp_alloc(int64_t bytes, void** out);
+TP_API int tp_free(void* ptr);
+TP_API int tp_memcpy_h2d(void* dst, const void* src, int64_t bytes);
+TP_API int tp_memcpy_d2h(void* dst, const void* src, int64_t bytes);
+TP_API int tp_memcpy_d2d(void* dst, const void* src, int64_t bytes);
+TP_API int tp_memset(void* dst, int value, int64_t bytes);
+
+/* ---- creation (creationOps.ts, random.wgsl, fill.wgsl) -------------------- */
+/* zeros/ones/full/empty: creationOps.ts:39-45,107-145 (fill.wgsl) */
+TP_API int tp_full(const int64_t* shape, int ndim, int dtype, float value, tp_handle* out);
+/* fullLike/zerosLike/onesLike/emptyLike: creationOps.ts:111-145; dtype -1 = same */
+TP_API int tp_full_like(int64_t id, int dtype, float value, tp_handle* out);
+/* unaryOps.ts:171-179 fill: a new tensor of the same shape and dtype */
+TP_API int tp_fill(int64_t id, float value, tp_handle* out);
+/* creationOps.ts:21-23 setSeed (the counter starts at 42) */
+TP_API int tp_set_seed(uint32_t seed);
+/* creationOps.ts:47-101 rand/randn/normal/sampleOp: kind 0 rand, 1 randn, 2 normal(p0,p1),
+ * 3 bernoulli(p0), 4 exponential(p0); consumes one seed (random.wgsl:23-91) */
+TP_API int tp_random(const int64_t* shape, int ndim, int dtype, int kind, float p0, float p1, tp_handle* out);
+
+/* ---- element-wise (arithmeticOps.ts, broadcastOps.ts, compareOps.ts, unaryOps.ts) */
+/* binary op codes (elementwise.wgsl entry points; compare.wgsl) */
+enum {
+  TP_ADD = 0, TP_SUB = 1, TP_MUL = 2, TP_DIV = 3, TP_POW = 4, TP_MAXIMUM = 5, TP_MINIMUM = 6,
+  TP_EQ = 10, TP_NE = 11, TP_LT = 12, TP_LE = 13, TP_GT = 14, TP_GE = 15
+};
+/* unary op codes (unary.wgsl entry points) */
+enum {
+  TP_NEG = 0, TP_ABS = 1, TP_SQRT = 2, TP_EXP = 3, TP_LOG = 4, TP_RELU = 5, TP_RSQRT = 6,
+  TP_RECIPROCAL = 7, TP_SQUARE = 8, TP_SIGMOID = 9, TP_TANH = 10
+};
+/* add/sub/mul/div/pow/maximum/minimum/eq/ne/lt/le/gt/ge with right-aligned
+ * broadcasting (arithmeticOps.ts:342-355, broadcastOps.ts:21-82); the
+ * broadcast operand is read in place, never materialised */
+TP_API int tp_binary(int op, int64_t a, int64_t b, tp_handle* out);
+TP_API int tp_add(int64_t a, int64_t b, tp_handle* out);
+TP_API int tp_sub(int64_t a, int64_t b, tp_handle* out);
+TP_API int tp_mul(int64_t a, int64_t b, tp_handle* out);
+TP_API int tp_div(int64_t a, int64_t b, tp_handle* out);
+TP_API int tp_pow(int64_t a, int64_t b, tp_handle* out);
+TP_API int tp_gt(int64_t a, int64_t b, tp_handle* out);
+/* arithmeticOps.ts:206-219 mulScalar */
+TP_API int tp_mul_scalar(int64_t a, float value, tp_handle* out);
+/* unaryOps.ts:156-169 unary dispatch (relu, rsqrt, neg, ...) */
+TP_API int tp_unary(int op, int64_t a, tp_handle* out);
+TP_API int tp_relu(int64_t a, tp_handle* out);
+TP_API int tp_rsqrt(int64_t a, tp_handle* out);
+TP_API int tp_neg(int64_t a, tp_handle* out);
+
+/* ---- shape (shapeOps.ts) ------------------------------------------------- */
+/* shapeOps.ts:72-81 reshape (flatten/squeeze/unsqueeze reduce to it) */
+TP_API int tp_reshape(int64_t id, const int64_t* shape, int ndim, tp_handle* out);
+/* shapeOps.ts:715-725 transpose2d */
+TP_API int tp_transpose2d(int64_t id, tp_handle* out);
+/* shapeOps.ts:125-154 permute */
+TP_API int tp_permute(int64_t id, const int32_t* dims, int ndim, tp_handle* out);
+/* shapeOps.ts:305-329 expand */
+TP_API int tp_expand(int64_t id, const int64_t* shape, int ndim, tp_handle* out);
+
+/* ---- reductions (reductionOps.ts) ----------------------------------------- */
+/* reductionOps.ts:161-213 reduceAll: mode 0 sum, 1 mean, 2 max; the scalar
+ * stays in HBM (no host readback, unlike the reference) */
+TP_API int tp_reduce_all(int64_t id, int mode, tp_handle* out);
+TP_API int tp_sum(int64_t id, tp_handle* out);
+TP_API int tp_mean(int64_t id, tp_handle* out);
+TP_API int tp_max(int64_t id, tp_handle* out);
+/* reductionOps.ts:215-251 reduceDim: mode 0 sum, 1 mean */
+TP_API int tp_reduce_dim(int64_t id, int dim, int keepdim, int mode, tp_handle* out);
+TP_API int tp_sum_dim(int64_t id, int dim, int keepdim, tp_handle* out);
+TP_API int tp_mean_dim(int64_t id, int dim, int keepdim, tp_handle* out);
+/* max along a dim with first-index ties (the reference sorts instead,
+ * python/torch/tensor_ops.py:1531-1537); writes values and int32 indices */
+TP_API int tp_max_dim(int64_t id, int dim, int keepdim, tp_handle* values, tp_handle* indices);
+/* reductionOps.ts:119-138 argmax over the last dim (argmax.wgsl) */
+TP_API int tp_argmax(int64_t id, tp_handle* out);
+/* reductionOps.ts:300-328 softmax (softmax.wgsl) */
+TP_API int tp_softmax(int64_t id, int dim, tp_handle* out);
+/* reductionOps.ts:357-388 logSoftmax (log_softmax.wgsl) */
+TP_API int tp_log_softmax(int64_t id, int dim, tp_handle* out);
+/* reductionOps.ts:416-443 softmaxBackward (softmax_backward.wgsl) */
+TP_API int tp_softmax_backward(int64_t grad_out, int64_t softmax, int64_t batch, int64_t classes, tp_handle* out);
+/* reductionOps.ts:390-414 logSoftmaxBackward (log_softmax_backward.wgsl) */
+TP_API int tp_log_softmax_backward(int64_t grad_out, int64_t softmax, int64_t batch, int64_t classes,
+                                   tp_handle* out);
+/* reductionOps.ts:471-489 crossEntropy: per-row loss [B] (cross_entropy.wgsl) */
+TP_API int tp_cross_entropy(int64_t input, int64_t targets, tp_handle* out);
+/* reductionOps.ts:491-531 crossEntropyBackward: reduction 0 none, 1 sum, 2 mean */
+TP_API int tp_cross_entropy_backward(int64_t grad_out, int64_t input, int64_t targets, int reduction,
+                                     tp_handle* out);
+
+/* ---- optimizer steps (reductionOps.ts:533-653), in place ------------------- */
+/* adamw_step.wgsl */
+TP_API int tp_adamw_step(int64_t param, int64_t grad, int64_t exp_avg, int64_t exp_avg_sq, float lr, float beta1,
+                         float beta2, float eps, float weight_decay, float step_size, float inv_sqrt_bc2);
+/* adam_step.wgsl */
+TP_API int tp_adam_step(int64_t param, int64_t grad, int64_t exp_avg, int64_t exp_avg_sq, float lr, float beta1,
+                        float beta2, float eps, float weight_decay, float step_size, float inv_sqrt_bc2);
+/* sgd_step.wgsl */
+TP_API int tp_sgd_step(int64_t param, int64_t grad, int64_t momentum_buf, float lr, float momentum,
+                       float weight_decay, float dampening, int nesterov);
+/* New: one fused launch for a whole parameter group (the per-parameter loops
+ * of optim/__init__.py:158-205,238-312,345-418 become one kernel). */
+TP_API int tp_adamw_step_multi(const int64_t* params, const int64_t* grads, const int64_t* exp_avgs,
+                               const int64_t* exp_avg_sqs, int n, float lr, float beta1, float beta2, float eps,
+                               float weight_decay, float step_size, float inv_sqrt_bc2);
+TP_API int tp_adam_step_multi(const int64_t* params, const int64_t* grads, const int64_t* exp_avgs,
+                              const int64_t* exp_avg_sqs, int n, float lr, float beta1, float beta2, float eps,
+                              float weight_decay, float step_size, float inv_sqrt_bc2);
+TP_API int tp_sgd_step_multi(const int64_t* params, const int64_t* grads, const int64_t* momentum_bufs, int n,
+                             float lr, float momentum, float weight_decay, float dampening, int nesterov);
+
+/* ---- pointer-level optimizer kernels ---------------------------------------- */
+/* A tensor group is a device-side table of n (param, grad, state0, state1,
+ * numel) rows built once; steps then take only hyper-parameters. */
+TP_API int tpk_group_create(int n, float* const* params, float* const* grads, float* const* state0,
+                            float* const* state1, const int64_t* numels, int64_t* out_group);
+TP_API int tpk_group_destroy(int64_t group);
+/* kind 0 AdamW, 1 Adam */
+TP_API int tpk_adam_group(int64_t group, int kind, float lr, float beta1, float beta2, float eps,
+                          float weight_decay, float step_size, float inv_sqrt_bc2);
+/* grad_scale multiplies each gradient on read (1/world for averaged DP grads) */
+TP_API int tpk_sgd_group(int64_t group, float lr, float momentum, float weight_decay, float dampening,
+                         int nesterov, float grad_scale);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TPCUDA_H */

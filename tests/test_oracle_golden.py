@@ -1,0 +1,44 @@
+"""The CPU oracle against the reference's own recorded outputs.
+
+tests/golden/reference_examples.json holds, for each pinned playground example
+(runtime/playground/example-results.json), the value the reference recorded in
+its browser run and the value the unmodified reference package produced on the
+oracle through the shim (tests/golden/make_golden.py).  The RNG example is
+bit-exact (integer xorshift + one rounding); transcendental paths carry the
+ulp differences between the browser's WGSL math and the host libm.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+GOLDEN = json.load(open(os.path.join(HERE, "golden", "reference_examples.json")))
+
+# relative tolerance per example: rand is bit-exact; randn goes through
+# log/sqrt/cos; autograd_conv2d sums randn values.
+RTOL = {"rand_tensor": 0.0, "randn_tensor": 2e-6, "autograd_conv2d": 2e-6}
+
+
+@pytest.mark.parametrize("name", sorted(GOLDEN))
+def test_oracle_matches_reference_recording(name):
+    g = GOLDEN[name]
+    rtol = RTOL.get(name, 0.0)
+    for key in g["keys"]:
+        rec, got = g["recorded"][key], g["oracle"][key]
+        if isinstance(rec, (list, float, int)) and not isinstance(rec, bool):
+            a = np.asarray(rec, dtype=np.float64)
+            b = np.asarray(got, dtype=np.float64)
+            assert a.shape == b.shape, (name, key)
+            np.testing.assert_allclose(b, a, rtol=rtol, atol=0.0, err_msg=f"{name}.{key}")
+        else:
+            assert rec == got, (name, key)
+
+
+def test_oracle_rand_reproduces_recording_directly():
+    """rand at the initial seed 42 (creationOps.ts:17) restated in C is bit-exact."""
+    import oracle_runtime as O
+    vals = O.random(6, 42, 0)
+    rec = np.asarray(GOLDEN["rand_tensor"]["recorded"]["values"], np.float32).reshape(-1)
+    assert np.array_equal(vals, rec)

@@ -1,0 +1,296 @@
+// libtpcuda core: device init, stream, HBM pool, handle table, errors and the
+// registry / copy entry points of the C ABI.
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstring>
+#include <mutex>
+#include <unordered_map>
+
+#include "tp_core.h"
+
+namespace tp {
+
+static thread_local std::string g_err;
+static int g_device = -1;
+static cudaStream_t g_stream = nullptr;
+static int g_sms = 148;
+static std::unordered_map<int64_t, Tensor> g_tensors;
+static int64_t g_next_id = 1;
+static int64_t g_allocated = 0;
+static void* g_scratch = nullptr;
+static size_t g_scratch_bytes = 0;
+std::atomic<int64_t> g_launches{0};
+
+void set_error(const char* msg) { g_err = msg ? msg : ""; }
+
+void fail(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  throw Error(code, buf);
+}
+
+void ensure_init() {
+  if (g_device >= 0) return;
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess || n == 0) fail(TP_ERR_CUDA, "no CUDA device available (%s)", cudaGetErrorString(e));
+  int dev = 0;
+  TP_CUDA(cudaGetDevice(&dev));
+  TP_CUDA(cudaSetDevice(dev));
+  TP_CUDA(cudaStreamCreateWithFlags(&g_stream, cudaStreamNonBlocking));
+  cudaDeviceProp prop;
+  TP_CUDA(cudaGetDeviceProperties(&prop, dev));
+  g_sms = prop.multiProcessorCount;
+  // Keep freed blocks cached in the pool (a caching allocator on top of the
+  // driver's stream-ordered pool).
+  cudaMemPool_t pool;
+  TP_CUDA(cudaDeviceGetDefaultMemPool(&pool, dev));
+  uint64_t thr = UINT64_MAX;
+  TP_CUDA(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr));
+  g_device = dev;
+}
+
+cudaStream_t stream() {
+  ensure_init();
+  return g_stream;
+}
+int device() {
+  ensure_init();
+  return g_device;
+}
+int sm_count() {
+  ensure_init();
+  return g_sms;
+}
+
+void* dalloc(size_t bytes) {
+  ensure_init();
+  if (bytes == 0) bytes = 4;
+  void* p = nullptr;
+  cudaError_t e = cudaMallocAsync(&p, bytes, g_stream);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    fail(TP_ERR_OOM, "device allocation of %zu bytes failed: %s", bytes, cudaGetErrorString(e));
+  }
+  return p;
+}
+
+void dfree(void* p) {
+  if (p) TP_CUDA(cudaFreeAsync(p, g_stream));
+}
+
+void* scratch(size_t bytes) {
+  if (bytes > g_scratch_bytes) {
+    if (g_scratch) dfree(g_scratch);
+    size_t nb = bytes < (1u << 20) ? (1u << 20) : bytes;
+    g_scratch = dalloc(nb);
+    g_scratch_bytes = nb;
+  }
+  return g_scratch;
+}
+
+int64_t prod(const int64_t* s, int n) {
+  int64_t r = 1;
+  for (int i = 0; i < n; ++i) r *= s[i];
+  return r;
+}
+
+Tensor& get(int64_t id) {
+  auto it = g_tensors.find(id);
+  if (it == g_tensors.end()) fail(TP_ERR_ARG, "Unknown tensor id: %lld.", (long long)id);
+  return it->second;
+}
+
+int64_t put(const Tensor& t) {
+  int64_t id = g_next_id++;
+  g_tensors.emplace(id, t);
+  g_allocated += (int64_t)t.bytes;
+  return id;
+}
+
+Tensor make(const int64_t* shape, int ndim, int dtype, int phys) {
+  TP_REQUIRE(ndim >= 0 && ndim <= TP_MAX_DIMS, "tensor rank %d exceeds %d", ndim, TP_MAX_DIMS);
+  TP_REQUIRE(dtype >= TP_FLOAT32 && dtype <= TP_BOOL, "Unsupported dtype code: %d.", dtype);
+  Tensor t;
+  t.ndim = ndim;
+  t.dtype = dtype;
+  t.phys = phys;
+  for (int i = 0; i < ndim; ++i) {
+    TP_REQUIRE(shape[i] >= 0, "negative dimension %lld", (long long)shape[i]);
+    t.shape[i] = shape[i];
+  }
+  t.numel = prod(shape, ndim);
+  t.bytes = (size_t)(t.numel > 0 ? t.numel : 1) * 4;
+  t.ptr = dalloc(t.bytes);
+  return t;
+}
+
+Tensor make_like_shape(const std::vector<int64_t>& shape, int dtype, int phys) {
+  return make(shape.data(), (int)shape.size(), dtype, phys);
+}
+
+std::vector<int64_t> shape_of(const Tensor& t) { return std::vector<int64_t>(t.shape, t.shape + t.ndim); }
+
+void fill_handle(const Tensor& t, int64_t id, tp_handle* out) {
+  if (!out) return;
+  out->id = id;
+  out->ndim = t.ndim;
+  out->dtype = t.dtype;
+  for (int i = 0; i < TP_MAX_DIMS; ++i) out->shape[i] = i < t.ndim ? t.shape[i] : 0;
+}
+
+int64_t emit(const Tensor& t, tp_handle* out) {
+  int64_t id = put(t);
+  fill_handle(t, id, out);
+  return id;
+}
+
+__global__ void k_i32_to_f32(const int32_t* in, float* out, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = (float)in[i];
+}
+
+}  // namespace tp
+
+using namespace tp;
+
+extern "C" {
+
+TP_API const char* tp_last_error(void) { return g_err.c_str(); }
+
+TP_API int tp_init(int dev) {
+  return guard([&] {
+    if (g_device < 0 && dev >= 0) TP_CUDA(cudaSetDevice(dev));
+    ensure_init();
+  });
+}
+
+TP_API int tp_is_available(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n > 0 ? 1 : 0;
+}
+
+TP_API int tp_device_count(int* out) {
+  return guard([&] {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
+    }
+    *out = n;
+  });
+}
+
+TP_API int tp_synchronize(void) { return guard([&] { TP_CUDA(cudaStreamSynchronize(stream())); }); }
+
+TP_API int tp_get_stream(void** out) { return guard([&] { *out = (void*)stream(); }); }
+
+TP_API int tp_memory_allocated(int64_t* out) { return guard([&] { *out = g_allocated; }); }
+
+TP_API int tp_memory_reserved(int64_t* out) {
+  return guard([&] {
+    cudaMemPool_t pool;
+    TP_CUDA(cudaDeviceGetDefaultMemPool(&pool, device()));
+    uint64_t v = 0;
+    TP_CUDA(cudaMemPoolGetAttribute(pool, cudaMemPoolAttrReservedMemCurrent, &v));
+    *out = (int64_t)v;
+  });
+}
+
+TP_API int tp_device_name(char* buf, int len) {
+  return guard([&] {
+    cudaDeviceProp prop;
+    TP_CUDA(cudaGetDeviceProperties(&prop, device()));
+    snprintf(buf, (size_t)len, "%s", prop.name);
+  });
+}
+
+TP_API int tp_kernel_launches(int64_t* out) { return guard([&] { *out = g_launches.load(); }); }
+
+TP_API int tp_tensor_from_data(const float* host, const int64_t* shape, int ndim, int dtype, tp_handle* out) {
+  return guard([&] {
+    Tensor t = make(shape, ndim, dtype);
+    if (t.numel > 0) TP_CUDA(cudaMemcpyAsync(t.ptr, host, (size_t)t.numel * 4, cudaMemcpyHostToDevice, stream()));
+    emit(t, out);
+  });
+}
+
+TP_API int tp_to_host(int64_t id, float* dst, int64_t numel) {
+  return guard([&] {
+    Tensor& t = get(id);
+    TP_REQUIRE(numel == t.numel, "toList: buffer holds %lld values, tensor has %lld", (long long)numel,
+               (long long)t.numel);
+    if (t.numel == 0) return;
+    if (t.phys == PHYS_I32) {
+      float* tmp = (float*)dalloc((size_t)t.numel * 4);
+      k_i32_to_f32<<<grid_for(t.numel, 256), 256, 0, stream()>>>(t.i(), tmp, t.numel);
+      g_launches++;
+      TP_LAUNCH_CHECK();
+      TP_CUDA(cudaMemcpyAsync(dst, tmp, (size_t)t.numel * 4, cudaMemcpyDeviceToHost, stream()));
+      dfree(tmp);
+    } else {
+      TP_CUDA(cudaMemcpyAsync(dst, t.ptr, (size_t)t.numel * 4, cudaMemcpyDeviceToHost, stream()));
+    }
+    TP_CUDA(cudaStreamSynchronize(stream()));
+  });
+}
+
+TP_API int tp_destroy(int64_t id) {
+  return guard([&] {
+    auto it = g_tensors.find(id);
+    if (it == g_tensors.end()) return;  // destroying twice is a no-op (device.ts:466-468)
+    g_allocated -= (int64_t)it->second.bytes;
+    dfree(it->second.ptr);
+    g_tensors.erase(it);
+  });
+}
+
+TP_API int tp_meta(int64_t id, tp_handle* out) {
+  return guard([&] { fill_handle(get(id), id, out); });
+}
+
+TP_API int tp_device_ptr(int64_t id, void** out) { return guard([&] { *out = get(id).ptr; }); }
+
+TP_API int tp_alloc(int64_t bytes, void** out) {
+  return guard([&] {
+    TP_REQUIRE(bytes >= 0, "negative allocation size");
+    *out = dalloc((size_t)bytes);
+  });
+}
+
+TP_API int tp_free(void* p) { return guard([&] { dfree(p); }); }
+
+TP_API int tp_memcpy_h2d(void* dst, const void* src, int64_t bytes) {
+  return guard([&] {
+    if (bytes > 0) TP_CUDA(cudaMemcpyAsync(dst, src, (size_t)bytes, cudaMemcpyHostToDevice, stream()));
+  });
+}
+
+TP_API int tp_memcpy_d2h(void* dst, const void* src, int64_t bytes) {
+  return guard([&] {
+    if (bytes > 0) TP_CUDA(cudaMemcpyAsync(dst, src, (size_t)bytes, cudaMemcpyDeviceToHost, stream()));
+    TP_CUDA(cudaStreamSynchronize(stream()));
+  });
+}
+
+TP_API int tp_memcpy_d2d(void* dst, const void* src, int64_t bytes) {
+  return guard([&] {
+    if (bytes > 0) TP_CUDA(cudaMemcpyAsync(dst, src, (size_t)bytes, cudaMemcpyDeviceToDevice, stream()));
+  });
+}
+
+TP_API int tp_memset(void* dst, int value, int64_t bytes) {
+  return guard([&] {
+    if (bytes > 0) TP_CUDA(cudaMemsetAsync(dst, value, (size_t)bytes, stream()));
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,557 @@
+// Batch and layer normalisation.
+//
+// Reference: batchnorm.wgsl:20-36 is inference-only and its host side reads
+// weight, bias and running stats back to the CPU every call
+// (normalizationOps.ts:20-126); training-mode BN and differentiable LN are
+// ~15 Python-composed dispatches each (python/torch/tensor_nn_ops.py:92-254,
+// 363-453), whose backward has the defects D3/D4 (autograd_rules.py:1082,
+// 1116-1124, 1171-1209).  Here:
+//   * BN eval: one element-wise pass, parameters read on the device;
+//   * BN train forward: per-channel sum / sum-of-squares accumulated in f64
+//     over the N x spatial plane (split across CTAs, finished in a fixed
+//     order), then one normalise(+ReLU) pass; running stats updated on the
+//     device with momentum and the unbiased variance (tensor_nn_ops.py:206-217);
+//   * BN backward (PyTorch rule): per-channel sum(dy), sum(dy*x_hat) then one
+//     element-wise pass; an optional ReLU mask folds the activation backward in;
+//   * LN forward/backward: one CTA per row with the row in registers; dgamma /
+//     dbeta via per-CTA column partials reduced in a fixed order.
+#include <cuda_runtime.h>
+
+#include "tp_core.h"
+
+namespace tp {
+
+// ---- BatchNorm eval (batchnorm.wgsl:20-36) ------------------------------------------
+__global__ void k_bn_eval(const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ b,
+                          const float* __restrict__ rm, const float* __restrict__ rv, float* __restrict__ y,
+                          int64_t total, int64_t C, int64_t S, float eps) {
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
+    int64_t c = (i / S) % C;
+    float wt = w ? w[c] : 1.0f, bs = b ? b[c] : 0.0f, mean = rm ? rm[c] : 0.0f, var = rv ? rv[c] : 1.0f;
+    float inv_std = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+    y[i] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x[i], mean), inv_std), wt), bs);
+  }
+}
+
+// ---- BatchNorm train: statistics ---------------------------------------------------
+// grid (C, splits).  Split s of channel c covers images [n0, n1).
+__global__ void k_bn_stats(const float* __restrict__ x, int64_t N, int64_t C, int64_t S, int splits,
+                           double* __restrict__ part) {
+  __shared__ double sh_s[32], sh_q[32];
+  int64_t c = blockIdx.x;
+  int split = blockIdx.y;
+  int64_t per = (N + splits - 1) / splits;
+  int64_t n0 = split * per, n1 = n0 + per < N ? n0 + per : N;
+  double s = 0.0, q = 0.0;
+  bool vec = (S & 3) == 0;
+  for (int64_t n = n0; n < n1; ++n) {
+    const float* p = x + (n * C + c) * S;
+    if (vec) {
+      const float4* p4 = reinterpret_cast<const float4*>(p);
+      for (int64_t i = threadIdx.x; i < (S >> 2); i += blockDim.x) {
+        float4 v = p4[i];
+        s += (double)v.x + (double)v.y + (double)v.z + (double)v.w;
+        q += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+      }
+    } else {
+      for (int64_t i = threadIdx.x; i < S; i += blockDim.x) {
+        double v = p[i];
+        s += v;
+        q += v * v;
+      }
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    s += __shfl_xor_sync(0xffffffffu, s, o);
+    q += __shfl_xor_sync(0xffffffffu, q, o);
+  }
+  int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if (lane == 0) {
+    sh_s[w] = s;
+    sh_q[w] = q;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double ts = 0.0, tq = 0.0;
+    for (int k = 0; k < nw; ++k) {
+      ts += sh_s[k];
+      tq += sh_q[k];
+    }
+    part[(c * splits + split) * 2] = ts;
+    part[(c * splits + split) * 2 + 1] = tq;
+  }
+}
+
+// Per channel: mean, biased var -> inv_std; running stats with the unbiased
+// variance.  Writes save_mean / save_invstd (f32) for the normalise pass.
+__global__ void k_bn_finish(const double* __restrict__ part, int64_t C, int splits, double M, float eps,
+                            float momentum, float* __restrict__ save_mean, float* __restrict__ save_invstd,
+                            float* __restrict__ rm, float* __restrict__ rv) {
+  int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  double s = 0.0, q = 0.0;
+  for (int k = 0; k < splits; ++k) {
+    s += part[(c * splits + k) * 2];
+    q += part[(c * splits + k) * 2 + 1];
+  }
+  double mean = s / M;
+  double var = q / M - mean * mean;
+  if (var < 0.0) var = 0.0;
+  save_mean[c] = (float)mean;
+  save_invstd[c] = (float)(1.0 / sqrt(var + (double)eps));
+  if (rm) rm[c] = (float)(mean * momentum + (double)rm[c] * (1.0 - momentum));
+  if (rv) rv[c] = (float)(var * M / (M - 1.0) * momentum + (double)rv[c] * (1.0 - momentum));
+}
+
+// y = (x - mean) * invstd * w + b, optionally ReLU'd.
+__global__ void k_bn_apply(const float* __restrict__ x, const float* __restrict__ mean,
+                           const float* __restrict__ invstd, const float* __restrict__ w, const float* __restrict__ b,
+                           float* __restrict__ y, int64_t N, int64_t C, int64_t S, int relu) {
+  int64_t total = N * C * S;
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  if ((S & 3) == 0) {
+    int64_t t4 = total >> 2, S4 = S >> 2;
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    float4* y4 = reinterpret_cast<float4*>(y);
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < t4; i += stride) {
+      int64_t c = (i / S4) % C;
+      float mu = mean[c], is = invstd[c], wt = w ? w[c] : 1.0f, bs = b ? b[c] : 0.0f;
+      float sc = is * wt;
+      float4 v = x4[i];
+      float r0 = (v.x - mu) * sc + bs, r1 = (v.y - mu) * sc + bs, r2 = (v.z - mu) * sc + bs,
+            r3 = (v.w - mu) * sc + bs;
+      if (relu) {
+        r0 = fmaxf(r0, 0.0f);
+        r1 = fmaxf(r1, 0.0f);
+        r2 = fmaxf(r2, 0.0f);
+        r3 = fmaxf(r3, 0.0f);
+      }
+      y4[i] = make_float4(r0, r1, r2, r3);
+    }
+  } else {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
+      int64_t c = (i / S) % C;
+      float wt = w ? w[c] : 1.0f, bs = b ? b[c] : 0.0f;
+      float r = (x[i] - mean[c]) * (invstd[c] * wt) + bs;
+      y[i] = relu ? fmaxf(r, 0.0f) : r;
+    }
+  }
+}
+
+// ---- BatchNorm backward ---------------------------------------------------------------
+// part[c][split] = (sum dy, sum dy*x_hat); relu_src: if given, dy is masked by
+// relu_src > 0 (the backward of a ReLU applied to the BN output).
+__global__ void k_bn_bwd_stats(const float* __restrict__ dy, const float* __restrict__ x,
+                               const float* __restrict__ relu_src, const float* __restrict__ mean,
+                               const float* __restrict__ invstd, int64_t N, int64_t C, int64_t S, int splits,
+                               double* __restrict__ part) {
+  __shared__ double sh_a[32], sh_b[32];
+  int64_t c = blockIdx.x;
+  int split = blockIdx.y;
+  int64_t per = (N + splits - 1) / splits;
+  int64_t n0 = split * per, n1 = n0 + per < N ? n0 + per : N;
+  float mu = mean[c], is = invstd[c];
+  double a = 0.0, bsum = 0.0;
+  for (int64_t n = n0; n < n1; ++n) {
+    int64_t base = (n * C + c) * S;
+    for (int64_t i = threadIdx.x; i < S; i += blockDim.x) {
+      float g = dy[base + i];
+      if (relu_src && !(relu_src[base + i] > 0.0f)) g = 0.0f;
+      float xh = (x[base + i] - mu) * is;
+      a += g;
+      bsum += (double)g * xh;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    a += __shfl_xor_sync(0xffffffffu, a, o);
+    bsum += __shfl_xor_sync(0xffffffffu, bsum, o);
+  }
+  int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if (lane == 0) {
+    sh_a[w] = a;
+    sh_b[w] = bsum;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double ta = 0.0, tb = 0.0;
+    for (int k = 0; k < nw; ++k) {
+      ta += sh_a[k];
+      tb += sh_b[k];
+    }
+    part[(c * splits + split) * 2] = ta;
+    part[(c * splits + split) * 2 + 1] = tb;
+  }
+}
+
+// coef[c] = {w*invstd, sum_dy/M, sum_dyxh/M}; dw, db written here.
+__global__ void k_bn_bwd_finish(const double* __restrict__ part, int64_t C, int splits, double M,
+                                const float* __restrict__ w, const float* __restrict__ invstd,
+                                float* __restrict__ coef, float* __restrict__ dw, float* __restrict__ db) {
+  int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  double a = 0.0, b = 0.0;
+  for (int k = 0; k < splits; ++k) {
+    a += part[(c * splits + k) * 2];
+    b += part[(c * splits + k) * 2 + 1];
+  }
+  coef[c * 3] = (w ? w[c] : 1.0f) * invstd[c];
+  coef[c * 3 + 1] = (float)(a / M);
+  coef[c * 3 + 2] = (float)(b / M);
+  if (dw) dw[c] = (float)b;
+  if (db) db[c] = (float)a;
+}
+
+__global__ void k_bn_bwd_apply(const float* __restrict__ dy, const float* __restrict__ x,
+                               const float* __restrict__ relu_src, const float* __restrict__ mean,
+                               const float* __restrict__ invstd, const float* __restrict__ coef,
+                               float* __restrict__ dx, int64_t N, int64_t C, int64_t S) {
+  int64_t total = N * C * S;
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
+    int64_t c = (i / S) % C;
+    float g = dy[i];
+    if (relu_src && !(relu_src[i] > 0.0f)) g = 0.0f;
+    float xh = (x[i] - mean[c]) * invstd[c];
+    dx[i] = coef[c * 3] * (g - coef[c * 3 + 1] - xh * coef[c * 3 + 2]);
+  }
+}
+
+static int bn_splits(int64_t C, int64_t N) {
+  int64_t target = (int64_t)sm_count() * 4;
+  int splits = 1;
+  while (C * splits < target && splits * 2 <= N) splits *= 2;
+  return splits;
+}
+
+void launch_bn_train(const float* x, const float* w, const float* b, float* rm, float* rv, float* y,
+                     float* save_mean, float* save_invstd, int64_t N, int64_t C, int64_t S, float eps,
+                     float momentum, bool relu) {
+  int splits = bn_splits(C, N);
+  double* part = (double*)scratch((size_t)C * splits * 2 * sizeof(double));
+  TP_LAUNCH(k_bn_stats, dim3((unsigned)C, (unsigned)splits), 256, 0, x, N, C, S, splits, part);
+  TP_LAUNCH(k_bn_finish, (unsigned)((C + 127) / 128), 128, 0, part, C, splits, (double)(N * S), eps, momentum,
+            save_mean, save_invstd, rm, rv);
+  TP_LAUNCH(k_bn_apply, grid_for(N * C * S, 256, 4), 256, 0, x, save_mean, save_invstd, w, b, y, N, C, S,
+            relu ? 1 : 0);
+}
+
+void launch_bn_backward(const float* dy, const float* x, const float* relu_src, const float* w, const float* mean,
+                        const float* invstd, float* dx, float* dw, float* db, int64_t N, int64_t C, int64_t S) {
+  int splits = bn_splits(C, N);
+  size_t pb = (size_t)C * splits * 2 * sizeof(double);
+  char* ws = (char*)scratch(pb + (size_t)C * 3 * sizeof(float) + 64);
+  double* part = (double*)ws;
+  float* coef = (float*)(ws + ((pb + 15) & ~(size_t)15));
+  TP_LAUNCH(k_bn_bwd_stats, dim3((unsigned)C, (unsigned)splits), 256, 0, dy, x, relu_src, mean, invstd, N, C, S,
+            splits, part);
+  TP_LAUNCH(k_bn_bwd_finish, (unsigned)((C + 127) / 128), 128, 0, part, C, splits, (double)(N * S), w, invstd, coef,
+            dw, db);
+  TP_LAUNCH(k_bn_bwd_apply, grid_for(N * C * S, 256), 256, 0, dy, x, relu_src, mean, invstd, coef, dx, N, C, S);
+}
+
+// ---- LayerNorm --------------------------------------------------------------------------
+// One CTA (256 threads) per row; up to PER values per thread in registers.
+template <int PER>
+__global__ void __launch_bounds__(256) k_ln_fwd(const float* __restrict__ x, const float* __restrict__ g,
+                                                const float* __restrict__ b, float* __restrict__ y,
+                                                float* __restrict__ smean, float* __restrict__ srstd, int64_t D,
+                                                float eps) {
+  __shared__ float sh[32];
+  const float* xr = x + (int64_t)blockIdx.x * D;
+  float* yr = y + (int64_t)blockIdx.x * D;
+  float v[PER];
+  float s = 0.0f;
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    int64_t i = threadIdx.x + (int64_t)k * 256;
+    v[k] = i < D ? xr[i] : 0.0f;
+    s += v[k];
+  }
+  // block sum
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  if (lane == 0) sh[w] = s;
+  __syncthreads();
+  float tot = 0.0f;
+  for (int k = 0; k < 8; ++k) tot += sh[k];
+  float mean = tot / (float)D;
+  __syncthreads();
+  float q = 0.0f;
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    int64_t i = threadIdx.x + (int64_t)k * 256;
+    float d = i < D ? v[k] - mean : 0.0f;
+    q += d * d;
+  }
+  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+  if (lane == 0) sh[w] = q;
+  __syncthreads();
+  float tq = 0.0f;
+  for (int k = 0; k < 8; ++k) tq += sh[k];
+  float var = tq / (float)D;
+  float rstd = __fdiv_rn(1.0f, __fsqrt_rn(var + eps));
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    int64_t i = threadIdx.x + (int64_t)k * 256;
+    if (i < D) {
+      float nrm = (v[k] - mean) * rstd;
+      yr[i] = (g ? g[i] : 1.0f) * nrm + (b ? b[i] : 0.0f);
+    }
+  }
+  if (threadIdx.x == 0) {
+    if (smean) smean[blockIdx.x] = mean;
+    if (srstd) srstd[blockIdx.x] = rstd;
+  }
+}
+
+// Rows too long for registers: three passes from global memory.
+__global__ void k_ln_fwd_long(const float* __restrict__ x, const float* __restrict__ g,
+                              const float* __restrict__ b, float* __restrict__ y, float* __restrict__ smean,
+                              float* __restrict__ srstd, int64_t D, float eps) {
+  __shared__ float sh[32];
+  const float* xr = x + (int64_t)blockIdx.x * D;
+  float* yr = y + (int64_t)blockIdx.x * D;
+  float s = 0.0f;
+  for (int64_t i = threadIdx.x; i < D; i += blockDim.x) s += xr[i];
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if (lane == 0) sh[w] = s;
+  __syncthreads();
+  float tot = 0.0f;
+  for (int k = 0; k < nw; ++k) tot += sh[k];
+  float mean = tot / (float)D;
+  __syncthreads();
+  float q = 0.0f;
+  for (int64_t i = threadIdx.x; i < D; i += blockDim.x) {
+    float d = xr[i] - mean;
+    q += d * d;
+  }
+  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+  if (lane == 0) sh[w] = q;
+  __syncthreads();
+  float tq = 0.0f;
+  for (int k = 0; k < nw; ++k) tq += sh[k];
+  float rstd = __fdiv_rn(1.0f, __fsqrt_rn(tq / (float)D + eps));
+  for (int64_t i = threadIdx.x; i < D; i += blockDim.x)
+    yr[i] = (g ? g[i] : 1.0f) * ((xr[i] - mean) * rstd) + (b ? b[i] : 0.0f);
+  if (threadIdx.x == 0) {
+    if (smean) smean[blockIdx.x] = mean;
+    if (srstd) srstd[blockIdx.x] = rstd;
+  }
+}
+
+// LN backward: CTA handles `rpb` consecutive rows; dx per row, and per-CTA
+// column partials of dy*x_hat and dy (ws[blk][0..D) and ws[blk][D..2D)).
+__global__ void k_ln_bwd(const float* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ g,
+                         const float* __restrict__ smean, const float* __restrict__ srstd, float* __restrict__ dx,
+                         float* __restrict__ ws, int64_t rows, int64_t D, int rpb) {
+  __shared__ float sh[2][32];
+  int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int64_t r0 = (int64_t)blockIdx.x * rpb;
+  float* pg = ws ? ws + (int64_t)blockIdx.x * 2 * D : nullptr;
+  for (int64_t i = threadIdx.x; pg && i < D; i += blockDim.x) {
+    pg[i] = 0.0f;
+    pg[D + i] = 0.0f;
+  }
+  for (int64_t r = r0; r < r0 + rpb && r < rows; ++r) {
+    const float* dyr = dy + r * D;
+    const float* xr = x + r * D;
+    float mu = smean[r], rs = srstd[r];
+    float a = 0.0f, bb = 0.0f;
+    for (int64_t i = threadIdx.x; i < D; i += blockDim.x) {
+      float xh = (xr[i] - mu) * rs;
+      float gd = (g ? g[i] : 1.0f) * dyr[i];
+      a += gd;
+      bb += gd * xh;
+      if (pg) {
+        pg[i] += dyr[i] * xh;
+        pg[D + i] += dyr[i];
+      }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+      a += __shfl_xor_sync(0xffffffffu, a, o);
+      bb += __shfl_xor_sync(0xffffffffu, bb, o);
+    }
+    if (lane == 0) {
+      sh[0][w] = a;
+      sh[1][w] = bb;
+    }
+    __syncthreads();
+    float ta = 0.0f, tb = 0.0f;
+    for (int k = 0; k < nw; ++k) {
+      ta += sh[0][k];
+      tb += sh[1][k];
+    }
+    __syncthreads();
+    float inv_d = 1.0f / (float)D;
+    for (int64_t i = threadIdx.x; i < D; i += blockDim.x) {
+      float xh = (xr[i] - mu) * rs;
+      float gd = (g ? g[i] : 1.0f) * dyr[i];
+      dx[r * D + i] = rs * (gd - ta * inv_d - xh * tb * inv_d);
+    }
+  }
+}
+
+__global__ void k_colsum_partials(const float* __restrict__ ws, int nblk, int64_t D, float* __restrict__ dg,
+                                  float* __restrict__ db) {
+  int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= D) return;
+  float sg = 0.0f, sb = 0.0f;
+  for (int k = 0; k < nblk; ++k) {
+    sg += ws[(int64_t)k * 2 * D + i];
+    sb += ws[(int64_t)k * 2 * D + D + i];
+  }
+  if (dg) dg[i] = sg;
+  if (db) db[i] = sb;
+}
+
+void launch_ln_fwd(const float* x, const float* g, const float* b, float* y, float* sm, float* sr, int64_t rows,
+                   int64_t D, float eps) {
+  if (rows == 0 || D == 0) return;
+  unsigned gr = (unsigned)rows;
+  if (D <= 256 * 4) TP_LAUNCH(k_ln_fwd<4>, gr, 256, 0, x, g, b, y, sm, sr, D, eps);
+  else if (D <= 256 * 8) TP_LAUNCH(k_ln_fwd<8>, gr, 256, 0, x, g, b, y, sm, sr, D, eps);
+  else if (D <= 256 * 16) TP_LAUNCH(k_ln_fwd<16>, gr, 256, 0, x, g, b, y, sm, sr, D, eps);
+  else if (D <= 256 * 32) TP_LAUNCH(k_ln_fwd<32>, gr, 256, 0, x, g, b, y, sm, sr, D, eps);
+  else TP_LAUNCH(k_ln_fwd_long, gr, 256, 0, x, g, b, y, sm, sr, D, eps);
+}
+
+void launch_ln_bwd(const float* dy, const float* x, const float* g, const float* sm, const float* sr, float* dx,
+                   float* dg, float* db, int64_t rows, int64_t D) {
+  if (rows == 0 || D == 0) return;
+  int64_t target = (int64_t)sm_count() * 2;
+  int rpb = (int)((rows + target - 1) / target);
+  if (rpb < 1) rpb = 1;
+  int nblk = (int)((rows + rpb - 1) / rpb);
+  float* ws = (dg || db) ? (float*)scratch((size_t)nblk * 2 * D * sizeof(float)) : nullptr;
+  TP_LAUNCH(k_ln_bwd, (unsigned)nblk, 256, 0, dy, x, g, sm, sr, dx, ws, rows, D, rpb);
+  if (ws) TP_LAUNCH(k_colsum_partials, (unsigned)((D + 255) / 256), 256, 0, ws, nblk, D, dg, db);
+}
+
+static void nchw_dims(const Tensor& x, int64_t& N, int64_t& C, int64_t& S) {
+  TP_REQUIRE(x.ndim >= 2, "batch_norm needs at least 2D input");
+  N = x.shape[0];
+  C = x.shape[1];
+  S = prod(x.shape + 2, x.ndim - 2);
+}
+
+static const float* opt_ptr(int64_t id, int64_t expect) {
+  if (id == 0) return nullptr;
+  Tensor& t = get(id);
+  TP_REQUIRE(t.numel == expect, "norm parameter has %lld values, expected %lld", (long long)t.numel,
+             (long long)expect);
+  return t.f();
+}
+
+}  // namespace tp
+
+using namespace tp;
+
+extern "C" {
+
+TP_API int tp_batch_norm(int64_t input, int64_t weight, int64_t bias, int64_t running_mean, int64_t running_var,
+                         float eps, tp_handle* out) {
+  return guard([&] {
+    Tensor& x = get(input);
+    int64_t N, C, S;
+    nchw_dims(x, N, C, S);
+    const float* w = opt_ptr(weight, C);
+    const float* b = opt_ptr(bias, C);
+    const float* rm = opt_ptr(running_mean, C);
+    const float* rv = opt_ptr(running_var, C);
+    Tensor y = make(x.shape, x.ndim, x.dtype);
+    if (y.numel > 0)
+      TP_LAUNCH(k_bn_eval, grid_for(y.numel, 256), 256, 0, x.f(), w, b, rm, rv, y.f(), y.numel, C, S, eps);
+    emit(y, out);
+  });
+}
+
+TP_API int tp_batch_norm_train(int64_t input, int64_t weight, int64_t bias, int64_t running_mean,
+                               int64_t running_var, float eps, float momentum, int fuse_relu, tp_handle* out,
+                               tp_handle* save_mean, tp_handle* save_invstd) {
+  return guard([&] {
+    Tensor& x = get(input);
+    int64_t N, C, S;
+    nchw_dims(x, N, C, S);
+    TP_REQUIRE(N * S > 1, "batch_norm training needs more than one value per channel");
+    const float* w = opt_ptr(weight, C);
+    const float* b = opt_ptr(bias, C);
+    float* rm = (float*)opt_ptr(running_mean, C);
+    float* rv = (float*)opt_ptr(running_var, C);
+    Tensor y = make(x.shape, x.ndim, x.dtype);
+    int64_t cs[1] = {C};
+    Tensor sm = make(cs, 1, x.dtype), si = make(cs, 1, x.dtype);
+    launch_bn_train(x.f(), w, b, rm, rv, y.f(), sm.f(), si.f(), N, C, S, eps, momentum, fuse_relu != 0);
+    emit(y, out);
+    emit(sm, save_mean);
+    emit(si, save_invstd);
+  });
+}
+
+TP_API int tp_batch_norm_backward(int64_t grad_out, int64_t input, int64_t weight, int64_t save_mean,
+                                  int64_t save_invstd, int64_t relu_out, tp_handle* dx, tp_handle* dweight,
+                                  tp_handle* dbias) {
+  return guard([&] {
+    Tensor& dy = get(grad_out);
+    Tensor& x = get(input);
+    int64_t N, C, S;
+    nchw_dims(x, N, C, S);
+    TP_REQUIRE(dy.numel == x.numel, "batch_norm_backward: grad and input differ in size");
+    const float* w = opt_ptr(weight, C);
+    const float* rs = relu_out ? opt_ptr(relu_out, x.numel) : nullptr;
+    Tensor gx = make(x.shape, x.ndim, x.dtype);
+    int64_t cs[1] = {C};
+    Tensor gw = make(cs, 1, x.dtype), gb = make(cs, 1, x.dtype);
+    launch_bn_backward(dy.f(), x.f(), rs, w, opt_ptr(save_mean, C), opt_ptr(save_invstd, C), gx.f(), gw.f(),
+                       gb.f(), N, C, S);
+    emit(gx, dx);
+    emit(gw, dweight);
+    emit(gb, dbias);
+  });
+}
+
+TP_API int tp_layer_norm(int64_t input, int64_t normalized_size, int64_t gamma, int64_t beta, float eps,
+                         tp_handle* out, tp_handle* save_mean, tp_handle* save_rstd) {
+  return guard([&] {
+    Tensor& x = get(input);
+    int64_t D = normalized_size;
+    TP_REQUIRE(D > 0 && x.numel % D == 0, "layer_norm: normalized size %lld does not divide %lld", (long long)D,
+               (long long)x.numel);
+    int64_t rows = x.numel / D;
+    const float* g = opt_ptr(gamma, D);
+    const float* b = opt_ptr(beta, D);
+    Tensor y = make(x.shape, x.ndim, x.dtype);
+    int64_t rs_[1] = {rows};
+    Tensor sm, sr;
+    if (save_mean) sm = make(rs_, 1, x.dtype);
+    if (save_rstd) sr = make(rs_, 1, x.dtype);
+    launch_ln_fwd(x.f(), g, b, y.f(), save_mean ? sm.f() : nullptr, save_rstd ? sr.f() : nullptr, rows, D, eps);
+    emit(y, out);
+    if (save_mean) emit(sm, save_mean);
+    if (save_rstd) emit(sr, save_rstd);
+  });
+}
+
+TP_API int tp_layer_norm_backward(int64_t grad_out, int64_t input, int64_t normalized_size, int64_t gamma,
+                                  int64_t save_mean, int64_t save_rstd, tp_handle* dx, tp_handle* dgamma,
+                                  tp_handle* dbeta) {
+  return guard([&] {
+    Tensor& dy = get(grad_out);
+    Tensor& x = get(input);
+    int64_t D = normalized_size;
+    TP_REQUIRE(D > 0 && x.numel % D == 0 && dy.numel == x.numel, "layer_norm_backward: shape mismatch");
+    int64_t rows = x.numel / D;
+    const float* g = opt_ptr(gamma, D);
+    Tensor gx = make(x.shape, x.ndim, x.dtype);
+    int64_t ds[1] = {D};
+    Tensor gg = make(ds, 1, x.dtype), gb = make(ds, 1, x.dtype);
+    launch_ln_bwd(dy.f(), x.f(), g, opt_ptr(save_mean, rows), opt_ptr(save_rstd, rows), gx.f(), gg.f(), gb.f(),
+                  rows, D);
+    emit(gx, dx);
+    emit(gg, dgamma);
+    emit(gb, dbeta);
+  });
+}
+
+}  // extern "C"

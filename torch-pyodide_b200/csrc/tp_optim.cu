@@ -1,0 +1,339 @@
+// Fused optimizer steps: one multi-tensor launch per parameter group.
+//
+// Reference: adam_step.wgsl / adamw_step.wgsl / sgd_step.wgsl update one
+// parameter per dispatch (three uniform buffers each, reductionOps.ts:533-653)
+// and the Python optimizers loop over parameters (optim/__init__.py:158-205,
+// 238-312, 345-418).  Here a device table lists every tensor of the group and a
+// chunk table splits them into 64K-element chunks; a grid sized to the SM
+// count walks the chunks with 128-bit loads, reading param, grad and state
+// once and writing param and state once (AdamW: 28 B per element, SGD with
+// momentum: 20 B).
+//
+// The per-element arithmetic is the WGSL's, operation by operation, with
+// explicit round-to-nearest intrinsics so no multiply-add is contracted: the
+// result is bit-identical to the CPU oracle's restatement compiled with
+// -ffp-contract=off (sqrt and division are IEEE-rounded in both).
+#include <cuda_runtime.h>
+
+#include <unordered_map>
+
+#include "tp_core.h"
+
+namespace tp {
+
+constexpr int64_t OPT_CHUNK = 65536;
+
+struct OptRow {
+  float* p;
+  const float* g;
+  float* s0;
+  float* s1;
+  int64_t n;
+};
+struct OptChunk {
+  int32_t row;
+  int32_t len;
+  int64_t start;
+};
+
+struct AdamHP {
+  float lr, b1, b2, eps, wd, step_size, inv_sqrt_bc2, omb1, omb2, lrwd;
+};
+
+// adamw_step.wgsl:26-39 (ADAMW) and adam_step.wgsl:25-38 (ADAM).
+template <bool ADAMW>
+__device__ __forceinline__ void adam_elem(float& p, float g, float& m, float& v, const AdamHP& h) {
+  if (ADAMW) {
+    if (h.wd != 0.0f) p = __fsub_rn(p, __fmul_rn(h.lrwd, p));
+  } else {
+    if (h.wd != 0.0f) g = __fadd_rn(g, __fmul_rn(h.wd, p));
+  }
+  m = __fadd_rn(__fmul_rn(m, h.b1), __fmul_rn(h.omb1, g));
+  v = __fadd_rn(__fmul_rn(v, h.b2), __fmul_rn(__fmul_rn(h.omb2, g), g));
+  float denom = __fadd_rn(__fmul_rn(__fsqrt_rn(v), h.inv_sqrt_bc2), h.eps);
+  float upd = __fmul_rn(__fdiv_rn(m, denom), h.step_size);
+  p = __fsub_rn(p, upd);
+}
+
+template <bool ADAMW>
+__global__ void __launch_bounds__(256) k_adam_multi(const OptRow* __restrict__ rows, const OptChunk* __restrict__ chunks,
+                                                    int nchunks, AdamHP h) {
+  for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
+    OptChunk ch = chunks[c];
+    OptRow r = rows[ch.row];
+    float* __restrict__ P = r.p + ch.start;
+    const float* __restrict__ G = r.g + ch.start;
+    float* __restrict__ M = r.s0 + ch.start;
+    float* __restrict__ V = r.s1 + ch.start;
+    int len = ch.len;
+    int len4 = len >> 2;
+    float4* P4 = reinterpret_cast<float4*>(P);
+    const float4* G4 = reinterpret_cast<const float4*>(G);
+    float4* M4 = reinterpret_cast<float4*>(M);
+    float4* V4 = reinterpret_cast<float4*>(V);
+    int i = threadIdx.x;
+    // two float4 per thread per iteration, loads issued before the math
+    for (; i + (int)blockDim.x < len4; i += 2 * blockDim.x) {
+      int j = i + blockDim.x;
+      float4 p0 = P4[i], g0 = G4[i], m0 = M4[i], v0 = V4[i];
+      float4 p1 = P4[j], g1 = G4[j], m1 = M4[j], v1 = V4[j];
+      adam_elem<ADAMW>(p0.x, g0.x, m0.x, v0.x, h);
+      adam_elem<ADAMW>(p0.y, g0.y, m0.y, v0.y, h);
+      adam_elem<ADAMW>(p0.z, g0.z, m0.z, v0.z, h);
+      adam_elem<ADAMW>(p0.w, g0.w, m0.w, v0.w, h);
+      adam_elem<ADAMW>(p1.x, g1.x, m1.x, v1.x, h);
+      adam_elem<ADAMW>(p1.y, g1.y, m1.y, v1.y, h);
+      adam_elem<ADAMW>(p1.z, g1.z, m1.z, v1.z, h);
+      adam_elem<ADAMW>(p1.w, g1.w, m1.w, v1.w, h);
+      P4[i] = p0; M4[i] = m0; V4[i] = v0;
+      P4[j] = p1; M4[j] = m1; V4[j] = v1;
+    }
+    for (; i < len4; i += blockDim.x) {
+      float4 p0 = P4[i], g0 = G4[i], m0 = M4[i], v0 = V4[i];
+      adam_elem<ADAMW>(p0.x, g0.x, m0.x, v0.x, h);
+      adam_elem<ADAMW>(p0.y, g0.y, m0.y, v0.y, h);
+      adam_elem<ADAMW>(p0.z, g0.z, m0.z, v0.z, h);
+      adam_elem<ADAMW>(p0.w, g0.w, m0.w, v0.w, h);
+      P4[i] = p0; M4[i] = m0; V4[i] = v0;
+    }
+    for (int k = (len4 << 2) + threadIdx.x; k < len; k += blockDim.x) {
+      float p = P[k], m = M[k], v = V[k];
+      adam_elem<ADAMW>(p, G[k], m, v, h);
+      P[k] = p; M[k] = m; V[k] = v;
+    }
+  }
+}
+
+struct SgdHP {
+  float lr, mom, wd, omd, scale;
+  int has_m, nesterov;
+};
+
+// sgd_step.wgsl:21-41; `scale` (1 for the reference op) multiplies the grad on
+// read so averaged data-parallel gradients need no separate pass.
+__device__ __forceinline__ void sgd_elem(float& p, float g, float& buf, const SgdHP& h) {
+  if (h.scale != 1.0f) g = __fmul_rn(g, h.scale);
+  if (h.wd != 0.0f) g = __fadd_rn(g, __fmul_rn(h.wd, p));
+  float upd = g;
+  if (h.has_m) {
+    buf = __fadd_rn(__fmul_rn(buf, h.mom), __fmul_rn(g, h.omd));
+    upd = h.nesterov ? __fadd_rn(g, __fmul_rn(h.mom, buf)) : buf;
+  }
+  p = __fsub_rn(p, __fmul_rn(h.lr, upd));
+}
+
+__global__ void __launch_bounds__(256) k_sgd_multi(const OptRow* __restrict__ rows, const OptChunk* __restrict__ chunks,
+                                                   int nchunks, SgdHP h) {
+  for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
+    OptChunk ch = chunks[c];
+    OptRow r = rows[ch.row];
+    float* __restrict__ P = r.p + ch.start;
+    const float* __restrict__ G = r.g + ch.start;
+    float* __restrict__ B = r.s0 + ch.start;
+    int len = ch.len, len4 = len >> 2;
+    float4* P4 = reinterpret_cast<float4*>(P);
+    const float4* G4 = reinterpret_cast<const float4*>(G);
+    float4* B4 = reinterpret_cast<float4*>(B);
+    int i = threadIdx.x;
+    for (; i + (int)blockDim.x < len4; i += 2 * blockDim.x) {
+      int j = i + blockDim.x;
+      float4 p0 = P4[i], g0 = G4[i], p1 = P4[j], g1 = G4[j];
+      float4 b0 = h.has_m ? B4[i] : make_float4(0, 0, 0, 0);
+      float4 b1 = h.has_m ? B4[j] : make_float4(0, 0, 0, 0);
+      sgd_elem(p0.x, g0.x, b0.x, h); sgd_elem(p0.y, g0.y, b0.y, h);
+      sgd_elem(p0.z, g0.z, b0.z, h); sgd_elem(p0.w, g0.w, b0.w, h);
+      sgd_elem(p1.x, g1.x, b1.x, h); sgd_elem(p1.y, g1.y, b1.y, h);
+      sgd_elem(p1.z, g1.z, b1.z, h); sgd_elem(p1.w, g1.w, b1.w, h);
+      P4[i] = p0; P4[j] = p1;
+      if (h.has_m) { B4[i] = b0; B4[j] = b1; }
+    }
+    for (; i < len4; i += blockDim.x) {
+      float4 p0 = P4[i], g0 = G4[i];
+      float4 b0 = h.has_m ? B4[i] : make_float4(0, 0, 0, 0);
+      sgd_elem(p0.x, g0.x, b0.x, h); sgd_elem(p0.y, g0.y, b0.y, h);
+      sgd_elem(p0.z, g0.z, b0.z, h); sgd_elem(p0.w, g0.w, b0.w, h);
+      P4[i] = p0;
+      if (h.has_m) B4[i] = b0;
+    }
+    for (int k = (len4 << 2) + threadIdx.x; k < len; k += blockDim.x) {
+      float p = P[k], b = h.has_m ? B[k] : 0.0f;
+      sgd_elem(p, G[k], b, h);
+      P[k] = p;
+      if (h.has_m) B[k] = b;
+    }
+  }
+}
+
+// ---- groups --------------------------------------------------------------------
+
+struct Group {
+  OptRow* rows = nullptr;
+  OptChunk* chunks = nullptr;
+  int nrows = 0;
+  int nchunks = 0;
+};
+
+static std::unordered_map<int64_t, Group> g_groups;
+static int64_t g_next_group = 1;
+
+static Group build_group(const std::vector<OptRow>& rows) {
+  std::vector<OptChunk> chunks;
+  for (size_t r = 0; r < rows.size(); ++r) {
+    const OptRow& x = rows[r];
+    TP_REQUIRE((((uintptr_t)x.p | (uintptr_t)x.g | (uintptr_t)x.s0 | (uintptr_t)x.s1) & 15) == 0,
+               "optimizer tensors must be 16-byte aligned");
+    for (int64_t s = 0; s < x.n; s += OPT_CHUNK) {
+      OptChunk c;
+      c.row = (int32_t)r;
+      c.start = s;
+      c.len = (int32_t)(x.n - s < OPT_CHUNK ? x.n - s : OPT_CHUNK);
+      chunks.push_back(c);
+    }
+  }
+  Group g;
+  g.nrows = (int)rows.size();
+  g.nchunks = (int)chunks.size();
+  size_t rb = rows.size() * sizeof(OptRow), cb = chunks.size() * sizeof(OptChunk);
+  char* buf = (char*)dalloc(rb + cb + 16);
+  g.rows = (OptRow*)buf;
+  g.chunks = (OptChunk*)(buf + ((rb + 15) & ~(size_t)15));
+  if (rb) TP_CUDA(cudaMemcpyAsync(g.rows, rows.data(), rb, cudaMemcpyHostToDevice, stream()));
+  if (cb) TP_CUDA(cudaMemcpyAsync(g.chunks, chunks.data(), cb, cudaMemcpyHostToDevice, stream()));
+  return g;
+}
+
+static void free_group(Group& g) {
+  dfree(g.rows);
+  g.rows = nullptr;
+}
+
+static unsigned opt_grid(int nchunks) {
+  unsigned cap = (unsigned)sm_count() * 4;
+  return (unsigned)(nchunks < (int)cap ? (nchunks > 0 ? nchunks : 1) : cap);
+}
+
+static AdamHP adam_hp(float lr, float b1, float b2, float eps, float wd, float ss, float isb) {
+  AdamHP h;
+  h.lr = lr; h.b1 = b1; h.b2 = b2; h.eps = eps; h.wd = wd; h.step_size = ss; h.inv_sqrt_bc2 = isb;
+  h.omb1 = 1.0f - b1;  // f32 uniform arithmetic, as in the shader
+  h.omb2 = 1.0f - b2;
+  h.lrwd = lr * wd;
+  return h;
+}
+
+void launch_adam_group(const Group& g, bool adamw, const AdamHP& h) {
+  if (g.nchunks == 0) return;
+  if (adamw) TP_LAUNCH(k_adam_multi<true>, opt_grid(g.nchunks), 256, 0, g.rows, g.chunks, g.nchunks, h);
+  else TP_LAUNCH(k_adam_multi<false>, opt_grid(g.nchunks), 256, 0, g.rows, g.chunks, g.nchunks, h);
+}
+
+void launch_sgd_group(const Group& g, const SgdHP& h) {
+  if (g.nchunks == 0) return;
+  TP_LAUNCH(k_sgd_multi, opt_grid(g.nchunks), 256, 0, g.rows, g.chunks, g.nchunks, h);
+}
+
+static std::vector<OptRow> rows_from_ids(const int64_t* p, const int64_t* gr, const int64_t* s0, const int64_t* s1,
+                                         int n, const char* what) {
+  std::vector<OptRow> rows((size_t)n);
+  for (int i = 0; i < n; ++i) {
+    Tensor& tp_ = get(p[i]);
+    Tensor& tg = get(gr[i]);
+    Tensor& t0 = get(s0[i]);
+    Tensor* t1 = s1 ? &get(s1[i]) : nullptr;
+    if (tg.numel != tp_.numel || t0.numel != tp_.numel || (t1 && t1->numel != tp_.numel))
+      fail(TP_ERR_ARG, "%s: tensor lengths must match", what);
+    rows[i] = OptRow{tp_.f(), tg.f(), t0.f(), t1 ? t1->f() : t0.f(), tp_.numel};
+  }
+  return rows;
+}
+
+}  // namespace tp
+
+using namespace tp;
+
+extern "C" {
+
+TP_API int tp_adamw_step_multi(const int64_t* p, const int64_t* g, const int64_t* m, const int64_t* v, int n,
+                               float lr, float b1, float b2, float eps, float wd, float ss, float isb) {
+  return guard([&] {
+    Group grp = build_group(rows_from_ids(p, g, m, v, n, "adamWStep"));
+    launch_adam_group(grp, true, adam_hp(lr, b1, b2, eps, wd, ss, isb));
+    free_group(grp);
+  });
+}
+
+TP_API int tp_adam_step_multi(const int64_t* p, const int64_t* g, const int64_t* m, const int64_t* v, int n,
+                              float lr, float b1, float b2, float eps, float wd, float ss, float isb) {
+  return guard([&] {
+    Group grp = build_group(rows_from_ids(p, g, m, v, n, "adamStep"));
+    launch_adam_group(grp, false, adam_hp(lr, b1, b2, eps, wd, ss, isb));
+    free_group(grp);
+  });
+}
+
+TP_API int tp_adamw_step(int64_t p, int64_t g, int64_t m, int64_t v, float lr, float b1, float b2, float eps,
+                         float wd, float ss, float isb) {
+  return tp_adamw_step_multi(&p, &g, &m, &v, 1, lr, b1, b2, eps, wd, ss, isb);
+}
+
+TP_API int tp_adam_step(int64_t p, int64_t g, int64_t m, int64_t v, float lr, float b1, float b2, float eps, float wd,
+                        float ss, float isb) {
+  return tp_adam_step_multi(&p, &g, &m, &v, 1, lr, b1, b2, eps, wd, ss, isb);
+}
+
+TP_API int tp_sgd_step_multi(const int64_t* p, const int64_t* g, const int64_t* b, int n, float lr, float mom,
+                             float wd, float damp, int nesterov) {
+  return guard([&] {
+    Group grp = build_group(rows_from_ids(p, g, b, nullptr, n, "sgdStep"));
+    SgdHP h{lr, mom, wd, 1.0f - damp, 1.0f, mom != 0.0f ? 1 : 0, nesterov ? 1 : 0};
+    launch_sgd_group(grp, h);
+    free_group(grp);
+  });
+}
+
+TP_API int tp_sgd_step(int64_t p, int64_t g, int64_t b, float lr, float mom, float wd, float damp, int nesterov) {
+  return tp_sgd_step_multi(&p, &g, &b, 1, lr, mom, wd, damp, nesterov);
+}
+
+TP_API int tpk_group_create(int n, float* const* params, float* const* grads, float* const* state0,
+                            float* const* state1, const int64_t* numels, int64_t* out_group) {
+  return guard([&] {
+    TP_REQUIRE(n >= 0, "negative group size");
+    std::vector<OptRow> rows((size_t)n);
+    for (int i = 0; i < n; ++i)
+      rows[i] = OptRow{params[i], grads[i], state0[i], state1 ? state1[i] : state0[i], numels[i]};
+    Group g = build_group(rows);
+    int64_t id = g_next_group++;
+    g_groups[id] = g;
+    *out_group = id;
+  });
+}
+
+TP_API int tpk_group_destroy(int64_t group) {
+  return guard([&] {
+    auto it = g_groups.find(group);
+    if (it == g_groups.end()) return;
+    free_group(it->second);
+    g_groups.erase(it);
+  });
+}
+
+TP_API int tpk_adam_group(int64_t group, int kind, float lr, float b1, float b2, float eps, float wd, float ss,
+                          float isb) {
+  return guard([&] {
+    auto it = g_groups.find(group);
+    TP_REQUIRE(it != g_groups.end(), "unknown tensor group %lld", (long long)group);
+    launch_adam_group(it->second, kind == 0, adam_hp(lr, b1, b2, eps, wd, ss, isb));
+  });
+}
+
+TP_API int tpk_sgd_group(int64_t group, float lr, float mom, float wd, float damp, int nesterov, float grad_scale) {
+  return guard([&] {
+    auto it = g_groups.find(group);
+    TP_REQUIRE(it != g_groups.end(), "unknown tensor group %lld", (long long)group);
+    SgdHP h{lr, mom, wd, 1.0f - damp, grad_scale, mom != 0.0f ? 1 : 0, nesterov ? 1 : 0};
+    launch_sgd_group(it->second, h);
+  });
+}
+
+}  // extern "C"

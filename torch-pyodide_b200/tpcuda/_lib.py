@@ -1,0 +1,156 @@
+"""ctypes binding of libtpcuda.so (include/tpcuda.h).
+
+The library is built in-tree by ``tpcuda.build.build()`` (nvcc, sm_100a) next
+to this file.  There is no fallback: if the shared library is missing or no
+CUDA device is visible, loading raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libtpcuda.so")
+
+MAX_DIMS = 8
+
+DTYPES = ["float32", "float16", "bfloat16", "int8", "int16", "int32", "int64", "uint8", "uint16", "uint32",
+          "uint64", "bool"]
+DTYPE_CODE = {name: i for i, name in enumerate(DTYPES)}
+
+# status codes
+TP_OK = 0
+
+
+class Handle(ctypes.Structure):
+    """tp_handle: the reference TensorHandle {id, shape, dtype}."""
+
+    _fields_ = [("id", ctypes.c_int64), ("ndim", ctypes.c_int32), ("dtype", ctypes.c_int32),
+                ("shape", ctypes.c_int64 * MAX_DIMS)]
+
+    def to_dict(self) -> dict:
+        return {"id": int(self.id), "shape": [int(self.shape[i]) for i in range(self.ndim)],
+                "dtype": DTYPES[self.dtype]}
+
+
+class TpError(RuntimeError):
+    """A non-zero status from libtpcuda (the reference's JS Error)."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(message)
+        self.status = status
+
+
+I64 = ctypes.c_int64
+I32 = ctypes.c_int32
+F32 = ctypes.c_float
+P = ctypes.c_void_p
+HP = ctypes.POINTER(Handle)
+I64P = ctypes.POINTER(ctypes.c_int64)
+I32P = ctypes.POINTER(ctypes.c_int32)
+F32P = ctypes.POINTER(ctypes.c_float)
+PP = ctypes.POINTER(ctypes.c_void_p)
+INT = ctypes.c_int
+
+# name -> argtypes (restype int unless listed in _RESTYPE)
+SIGNATURES: dict[str, list] = {
+    "tp_init": [INT],
+    "tp_is_available": [],
+    "tp_device_count": [ctypes.POINTER(INT)],
+    "tp_last_error": [],
+    "tp_synchronize": [],
+    "tp_get_stream": [PP],
+    "tp_memory_allocated": [I64P],
+    "tp_memory_reserved": [I64P],
+    "tp_device_name": [ctypes.c_char_p, INT],
+    "tp_kernel_launches": [I64P],
+    "tp_tensor_from_data": [P, I64P, INT, INT, HP],
+    "tp_to_host": [I64, P, I64],
+    "tp_destroy": [I64],
+    "tp_meta": [I64, HP],
+    "tp_device_ptr": [I64, PP],
+    "tp_alloc": [I64, PP],
+    "tp_free": [P],
+    "tp_memcpy_h2d": [P, P, I64],
+    "tp_memcpy_d2h": [P, P, I64],
+    "tp_memcpy_d2d": [P, P, I64],
+    "tp_memset": [P, INT, I64],
+    "tp_full": [I64P, INT, INT, F32, HP],
+    "tp_full_like": [I64, INT, F32, HP],
+    "tp_fill": [I64, F32, HP],
+    "tp_set_seed": [ctypes.c_uint32],
+    "tp_random": [I64P, INT, INT, INT, F32, F32, HP],
+    "tp_binary": [INT, I64, I64, HP],
+    "tp_add": [I64, I64, HP],
+    "tp_sub": [I64, I64, HP],
+    "tp_mul": [I64, I64, HP],
+    "tp_div": [I64, I64, HP],
+    "tp_pow": [I64, I64, HP],
+    "tp_gt": [I64, I64, HP],
+    "tp_mul_scalar": [I64, F32, HP],
+    "tp_unary": [INT, I64, HP],
+    "tp_relu": [I64, HP],
+    "tp_rsqrt": [I64, HP],
+    "tp_neg": [I64, HP],
+    "tp_reshape": [I64, I64P, INT, HP],
+    "tp_transpose2d": [I64, HP],
+    "tp_permute": [I64, I32P, INT, HP],
+    "tp_expand": [I64, I64P, INT, HP],
+    "tp_reduce_all": [I64, INT, HP],
+    "tp_sum": [I64, HP],
+    "tp_mean": [I64, HP],
+    "tp_max": [I64, HP],
+    "tp_reduce_dim": [I64, INT, INT, INT, HP],
+    "tp_sum_dim": [I64, INT, INT, HP],
+    "tp_mean_dim": [I64, INT, INT, HP],
+    "tp_max_dim": [I64, INT, INT, HP, HP],
+    "tp_argmax": [I64, HP],
+    "tp_softmax": [I64, INT, HP],
+    "tp_log_softmax": [I64, INT, HP],
+    "tp_softmax_backward": [I64, I64, I64, I64, HP],
+    "tp_log_softmax_backward": [I64, I64, I64, I64, HP],
+    "tp_cross_entropy": [I64, I64, HP],
+    "tp_cross_entropy_backward": [I64, I64, I64, INT, HP],
+    "tp_adamw_step": [I64, I64, I64, I64] + [F32] * 7,
+    "tp_adam_step": [I64, I64, I64, I64] + [F32] * 7,
+    "tp_sgd_step": [I64, I64, I64, F32, F32, F32, F32, INT],
+    "tp_adamw_step_multi": [I64P, I64P, I64P, I64P, INT] + [F32] * 7,
+    "tp_adam_step_multi": [I64P, I64P, I64P, I64P, INT] + [F32] * 7,
+    "tp_sgd_step_multi": [I64P, I64P, I64P, INT, F32, F32, F32, F32, INT],
+    "tpk_group_create": [INT, PP, PP, PP, PP, I64P, I64P],
+    "tpk_group_destroy": [I64],
+    "tpk_adam_group": [I64, INT] + [F32] * 7,
+    "tpk_sgd_group": [I64, F32, F32, F32, F32, INT, F32],
+}
+
+_RESTYPE = {"tp_last_error": ctypes.c_char_p}
+
+_lib = None
+
+
+def load(path: str | None = None):
+    """Load libtpcuda.so and declare every exported signature."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    p = path or LIB_PATH
+    if not os.path.exists(p):
+        raise ImportError(f"libtpcuda.so not found at {p}; build it with tpcuda.build.build()")
+    L = ctypes.CDLL(p)
+    for name, args in SIGNATURES.items():
+        fn = getattr(L, name)
+        fn.argtypes = args
+        fn.restype = _RESTYPE.get(name, ctypes.c_int)
+    _lib = L
+    return L
+
+
+def check(status: int) -> None:
+    if status != TP_OK:
+        msg = _lib.tp_last_error().decode("utf-8", "replace") if _lib is not None else "libtpcuda error"
+        raise TpError(status, msg)
+
+
+def i64arr(vals) -> ctypes.Array:
+    vals = [int(v) for v in vals]
+    return (ctypes.c_int64 * max(1, len(vals)))(*vals)

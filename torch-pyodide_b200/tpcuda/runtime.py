@@ -1,0 +1,412 @@
+"""CudaRuntime: the reference runtime's method surface over libtpcuda.
+
+``TorchPyodideRuntime`` (runtime/src/runtime.ts:17-1212) is what the reference
+``torch`` package calls for every tensor op; ``CudaRuntime`` exposes the same
+camelCase methods with the same arguments, returning the same
+``{"id", "shape", "dtype"}`` dicts (runtime/src/ops/types.ts:10-15), so
+``tpcuda.shim.install(CudaRuntime())`` lets the unmodified reference package
+run on a B200.  Every method is one ctypes call into libtpcuda.so; errors come
+back as ``TpError`` (a RuntimeError), which is what the reference's
+try/except fallbacks expect.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import Sequence
+
+import numpy as np
+
+from . import _lib
+from ._lib import DTYPE_CODE, DTYPES, Handle, check, i64arr
+
+BIN = {"add": 0, "sub": 1, "mul": 2, "div": 3, "pow": 4, "maximum": 5, "minimum": 6,
+       "eq": 10, "ne": 11, "lt": 12, "le": 13, "gt": 14, "ge": 15}
+UN = {"neg": 0, "abs": 1, "sqrt": 2, "exp": 3, "log": 4, "relu": 5, "rsqrt": 6, "reciprocal": 7,
+      "square": 8, "sigmoid": 9, "tanh": 10}
+
+
+def _prod(shape) -> int:
+    r = 1
+    for s in shape:
+        r *= int(s)
+    return r
+
+
+def _dtype_code(dtype: str | None) -> int:
+    if dtype is None:
+        return -1
+    try:
+        return DTYPE_CODE[str(dtype)]
+    except KeyError:
+        raise _lib.TpError(-1, f"Unsupported dtype: {dtype}. Supported dtypes: {', '.join(DTYPES)}.") from None
+
+
+class CudaRuntime:
+    """Host mirror of TorchPyodideRuntime over the CUDA backend."""
+
+    def __init__(self, device: int = 0) -> None:
+        self.lib = _lib.load()
+        check(self.lib.tp_init(int(device)))
+        self._h = Handle()
+
+    # ---- helpers ----------------------------------------------------------
+    def _out(self) -> dict:
+        return self._h.to_dict()
+
+    def _call(self, fn, *args) -> dict:
+        check(fn(*args, ctypes.byref(self._h)))
+        return self._h.to_dict()
+
+    # ---- device / frames (runtime.ts:1025-1090) ---------------------------
+    def init(self, *_a) -> None:
+        return None
+
+    def isAvailable(self) -> bool:
+        return bool(self.lib.tp_is_available())
+
+    def isInitialized(self) -> bool:
+        return True
+
+    def deviceCount(self) -> int:
+        n = ctypes.c_int(0)
+        check(self.lib.tp_device_count(ctypes.byref(n)))
+        return int(n.value)
+
+    def currentDevice(self) -> int:
+        return 0
+
+    def getDeviceName(self, *_a) -> str:
+        buf = ctypes.create_string_buffer(256)
+        check(self.lib.tp_device_name(buf, 256))
+        return buf.value.decode()
+
+    def getDeviceProperties(self, *_a) -> dict:
+        return {"name": self.getDeviceName(), "backend": "cuda"}
+
+    def memoryAllocated(self, *_a) -> int:
+        v = ctypes.c_int64(0)
+        check(self.lib.tp_memory_allocated(ctypes.byref(v)))
+        return int(v.value)
+
+    def memoryReserved(self, *_a) -> int:
+        v = ctypes.c_int64(0)
+        check(self.lib.tp_memory_reserved(ctypes.byref(v)))
+        return int(v.value)
+
+    def beginFrame(self) -> None:
+        """Frames batch nothing here either: every op is already queued on one stream."""
+
+    def endFrame(self) -> None:
+        return None
+
+    def cancelFrame(self) -> None:
+        return None
+
+    def synchronize(self) -> None:
+        check(self.lib.tp_synchronize())
+
+    def stream(self) -> int:
+        p = ctypes.c_void_p()
+        check(self.lib.tp_get_stream(ctypes.byref(p)))
+        return int(p.value or 0)
+
+    def kernelLaunches(self) -> int:
+        v = ctypes.c_int64(0)
+        check(self.lib.tp_kernel_launches(ctypes.byref(v)))
+        return int(v.value)
+
+    def devicePtr(self, tid: int) -> int:
+        p = ctypes.c_void_p()
+        check(self.lib.tp_device_ptr(int(tid), ctypes.byref(p)))
+        return int(p.value or 0)
+
+    # ---- creation (creationOps.ts) -----------------------------------------
+    def tensorFromData(self, data, shape, dtype):
+        code = _dtype_code(dtype)
+        n = _prod(shape)
+        if isinstance(data, np.ndarray):
+            arr = np.ascontiguousarray(data, dtype=np.float32).reshape(-1)
+        else:
+            vals = list(data)
+            if dtype == "bool":
+                vals = [1.0 if v else 0.0 for v in vals]
+            elif dtype.startswith("uint"):
+                vals = [float(max(0, math.trunc(v))) for v in vals]
+            elif dtype.startswith("int"):
+                vals = [float(math.trunc(v)) for v in vals]
+            arr = np.asarray(vals, dtype=np.float32)
+        if arr.size != n:
+            raise _lib.TpError(-1, f"tensorFromData expected {n} values, got {arr.size}.")
+        return self._call(self.lib.tp_tensor_from_data, arr.ctypes.data_as(ctypes.c_void_p), i64arr(shape),
+                          len(shape), code)
+
+    def full(self, shape, value, dtype):
+        return self._call(self.lib.tp_full, i64arr(shape), len(shape), _dtype_code(dtype), float(value))
+
+    def zeros(self, shape, dtype):
+        return self.full(shape, 0.0, dtype)
+
+    def ones(self, shape, dtype):
+        return self.full(shape, 1.0, dtype)
+
+    def empty(self, shape, dtype):
+        return self.full(shape, 0.0, dtype)
+
+    def fullLike(self, tid, value, dtype=None):
+        return self._call(self.lib.tp_full_like, int(tid), _dtype_code(dtype), float(value))
+
+    def zerosLike(self, tid, dtype=None):
+        return self.fullLike(tid, 0.0, dtype)
+
+    def onesLike(self, tid, dtype=None):
+        return self.fullLike(tid, 1.0, dtype)
+
+    def emptyLike(self, tid, dtype=None):
+        return self.fullLike(tid, 0.0, dtype)
+
+    def fill(self, tid, value):
+        return self._call(self.lib.tp_fill, int(tid), float(value))
+
+    def setSeed(self, seed) -> None:
+        check(self.lib.tp_set_seed(int(seed) & 0xFFFFFFFF))
+
+    def _sample(self, shape, dtype, kind, p0=0.0, p1=1.0):
+        return self._call(self.lib.tp_random, i64arr(shape), len(shape), _dtype_code(dtype), kind, float(p0),
+                          float(p1))
+
+    def rand(self, shape, dtype):
+        return self._sample(shape, dtype, 0)
+
+    def randn(self, shape, dtype):
+        return self._sample(shape, dtype, 1)
+
+    def normal(self, shape, dtype, mean, std):
+        return self._sample(shape, dtype, 2, mean, std)
+
+    def bernoulli(self, shape, dtype, p):
+        return self._sample(shape, dtype, 3, p)
+
+    def exponential(self, shape, dtype, rate):
+        return self._sample(shape, dtype, 4, rate)
+
+    # ---- element-wise --------------------------------------------------------
+    def _bin(self, op, a, b):
+        return self._call(self.lib.tp_binary, BIN[op], int(a), int(b))
+
+    def add(self, a, b):
+        return self._bin("add", a, b)
+
+    def sub(self, a, b):
+        return self._bin("sub", a, b)
+
+    def mul(self, a, b):
+        return self._bin("mul", a, b)
+
+    def div(self, a, b):
+        return self._bin("div", a, b)
+
+    def pow(self, a, b):
+        return self._bin("pow", a, b)
+
+    def maximum(self, a, b):
+        return self._bin("maximum", a, b)
+
+    def minimum(self, a, b):
+        return self._bin("minimum", a, b)
+
+    def eq(self, a, b):
+        return self._bin("eq", a, b)
+
+    def ne(self, a, b):
+        return self._bin("ne", a, b)
+
+    def lt(self, a, b):
+        return self._bin("lt", a, b)
+
+    def le(self, a, b):
+        return self._bin("le", a, b)
+
+    def gt(self, a, b):
+        return self._bin("gt", a, b)
+
+    def ge(self, a, b):
+        return self._bin("ge", a, b)
+
+    def mulScalar(self, tid, value):
+        return self._call(self.lib.tp_mul_scalar, int(tid), float(value))
+
+    def _un(self, op, tid):
+        return self._call(self.lib.tp_unary, UN[op], int(tid))
+
+    def relu(self, t):
+        return self._un("relu", t)
+
+    def rsqrt(self, t):
+        return self._un("rsqrt", t)
+
+    def neg(self, t):
+        return self._un("neg", t)
+
+    def abs(self, t):
+        return self._un("abs", t)
+
+    def sqrt(self, t):
+        return self._un("sqrt", t)
+
+    def exp(self, t):
+        return self._un("exp", t)
+
+    def log(self, t):
+        return self._un("log", t)
+
+    def reciprocal(self, t):
+        return self._un("reciprocal", t)
+
+    def square(self, t):
+        return self._un("square", t)
+
+    def sigmoid(self, t):
+        return self._un("sigmoid", t)
+
+    def tanh(self, t):
+        return self._un("tanh", t)
+
+    # ---- shape (shapeOps.ts) ----------------------------------------------------
+    def _meta(self, tid) -> dict:
+        h = Handle()
+        check(self.lib.tp_meta(int(tid), ctypes.byref(h)))
+        return h.to_dict()
+
+    def reshape(self, tid, shape):
+        shape = [int(s) for s in shape]
+        return self._call(self.lib.tp_reshape, int(tid), i64arr(shape), len(shape))
+
+    def flatten(self, tid, startDim=0, endDim=-1):
+        shape = self._meta(tid)["shape"]
+        r = len(shape)
+        s = startDim + r if startDim < 0 else startDim
+        e = endDim + r if endDim < 0 else endDim
+        return self.reshape(tid, shape[:s] + [_prod(shape[s:e + 1])] + shape[e + 1:])
+
+    def squeeze(self, tid, dim=None):
+        shape = self._meta(tid)["shape"]
+        if dim is not None:
+            d = dim + len(shape) if dim < 0 else dim
+            new = [s for i, s in enumerate(shape) if not (i == d and s == 1)]
+        else:
+            new = [s for s in shape if s != 1]
+        return self.reshape(tid, new if new else [1])
+
+    def unsqueeze(self, tid, dim):
+        shape = self._meta(tid)["shape"]
+        d = dim + len(shape) + 1 if dim < 0 else dim
+        return self.reshape(tid, shape[:d] + [1] + shape[d:])
+
+    def transpose2d(self, tid):
+        return self.transpose(tid, 0, 1)
+
+    def transpose(self, tid, d0, d1):
+        shape = self._meta(tid)["shape"]
+        r = len(shape)
+        if r == 2:
+            return self._call(self.lib.tp_transpose2d, int(tid))
+        d0 = d0 + r if d0 < 0 else d0
+        d1 = d1 + r if d1 < 0 else d1
+        dims = list(range(r))
+        dims[d0], dims[d1] = dims[d1], dims[d0]
+        return self.permute(tid, dims)
+
+    def permute(self, tid, dims):
+        arr = (ctypes.c_int32 * max(1, len(dims)))(*[int(d) for d in dims])
+        return self._call(self.lib.tp_permute, int(tid), arr, len(dims))
+
+    def expand(self, tid, shape):
+        shape = [int(s) for s in shape]
+        return self._call(self.lib.tp_expand, int(tid), i64arr(shape), len(shape))
+
+    # ---- reductions (reductionOps.ts) ---------------------------------------------
+    def sum(self, tid):
+        return self._call(self.lib.tp_reduce_all, int(tid), 0)
+
+    def mean(self, tid):
+        return self._call(self.lib.tp_reduce_all, int(tid), 1)
+
+    def max(self, tid):
+        return self._call(self.lib.tp_reduce_all, int(tid), 2)
+
+    def sumDim(self, tid, dim, keepdim):
+        return self._call(self.lib.tp_reduce_dim, int(tid), int(dim), 1 if keepdim else 0, 0)
+
+    def meanDim(self, tid, dim, keepdim):
+        return self._call(self.lib.tp_reduce_dim, int(tid), int(dim), 1 if keepdim else 0, 1)
+
+    def maxDim(self, tid, dim, keepdim):
+        hv, hi = Handle(), Handle()
+        check(self.lib.tp_max_dim(int(tid), int(dim), 1 if keepdim else 0, ctypes.byref(hv), ctypes.byref(hi)))
+        return [hv.to_dict(), hi.to_dict()]
+
+    def argmax(self, tid):
+        return self._call(self.lib.tp_argmax, int(tid))
+
+    def softmax(self, tid, dim):
+        return self._call(self.lib.tp_softmax, int(tid), int(dim))
+
+    def logSoftmax(self, tid, dim):
+        return self._call(self.lib.tp_log_softmax, int(tid), int(dim))
+
+    def softmaxBackward(self, go, s, batchSize, numClasses):
+        return self._call(self.lib.tp_softmax_backward, int(go), int(s), int(batchSize), int(numClasses))
+
+    def logSoftmaxBackward(self, go, s, batchSize, numClasses):
+        return self._call(self.lib.tp_log_softmax_backward, int(go), int(s), int(batchSize), int(numClasses))
+
+    def crossEntropy(self, inp, tgt):
+        return self._call(self.lib.tp_cross_entropy, int(inp), int(tgt))
+
+    def crossEntropyBackward(self, go, inp, tgt, reduction):
+        red = {"none": 0, "sum": 1, "mean": 2}[str(reduction)]
+        return self._call(self.lib.tp_cross_entropy_backward, int(go), int(inp), int(tgt), red)
+
+    # ---- optimizer steps (in place, return None) ---------------------------------
+    def adamWStep(self, p, g, m, v, lr, b1, b2, eps, wd, stepSize, invSqrtBc2):
+        check(self.lib.tp_adamw_step(int(p), int(g), int(m), int(v), lr, b1, b2, eps, wd, stepSize, invSqrtBc2))
+
+    def adamStep(self, p, g, m, v, lr, b1, b2, eps, wd, stepSize, invSqrtBc2):
+        check(self.lib.tp_adam_step(int(p), int(g), int(m), int(v), lr, b1, b2, eps, wd, stepSize, invSqrtBc2))
+
+    def sgdStep(self, p, g, buf, lr, momentum, wd, dampening, nesterov):
+        check(self.lib.tp_sgd_step(int(p), int(g), int(buf), lr, momentum, wd, dampening, 1 if nesterov else 0))
+
+    def adamWStepMulti(self, ps, gs, ms, vs, lr, b1, b2, eps, wd, stepSize, invSqrtBc2):
+        check(self.lib.tp_adamw_step_multi(i64arr(ps), i64arr(gs), i64arr(ms), i64arr(vs), len(ps), lr, b1, b2, eps,
+                                           wd, stepSize, invSqrtBc2))
+
+    def adamStepMulti(self, ps, gs, ms, vs, lr, b1, b2, eps, wd, stepSize, invSqrtBc2):
+        check(self.lib.tp_adam_step_multi(i64arr(ps), i64arr(gs), i64arr(ms), i64arr(vs), len(ps), lr, b1, b2, eps,
+                                          wd, stepSize, invSqrtBc2))
+
+    def sgdStepMulti(self, ps, gs, bufs, lr, momentum, wd, dampening, nesterov):
+        check(self.lib.tp_sgd_step_multi(i64arr(ps), i64arr(gs), i64arr(bufs), len(ps), lr, momentum, wd, dampening,
+                                         1 if nesterov else 0))
+
+    # ---- readback / lifetime (runtime.ts:1046-1054) -------------------------------
+    def toNumpy(self, tid) -> np.ndarray:
+        meta = self._meta(tid)
+        n = _prod(meta["shape"])
+        out = np.empty(n, np.float32)
+        check(self.lib.tp_to_host(int(tid), out.ctypes.data_as(ctypes.c_void_p), n))
+        return out
+
+    def toList(self, tid):
+        meta = self._meta(tid)
+        vals = self.toNumpy(tid).tolist()
+        dt = meta["dtype"]
+        if dt == "bool":
+            return [1 if v != 0 else 0 for v in vals]
+        if dt.startswith("int") or dt.startswith("uint"):
+            return [int(math.trunc(v)) for v in vals]
+        return vals
+
+    def destroy(self, tid) -> None:
+        check(self.lib.tp_destroy(int(tid)))
