@@ -191,6 +191,66 @@ TP_API int tp_cross_entropy(int64_t input, int64_t targets, tp_handle* out);
 TP_API int tp_cross_entropy_backward(int64_t grad_out, int64_t input, int64_t targets, int reduction,
                                      tp_handle* out);
 
+/* ---- dense contractions (arithmeticOps.ts:260-340, convOps.ts) ---------------- */
+/* arithmeticOps.ts:260-308 matmul / mm / bmm / mv shape rules (matmul.wgsl:52-85) */
+TP_API int tp_matmul(int64_t a, int64_t b, tp_handle* out);
+/* New: y = x . W^T + b (nn.Linear, python/torch/nn/functional.py:95-101 issues a
+ * transpose, a matmul, a reshape and a broadcast add); bias id 0 = none */
+TP_API int tp_linear(int64_t x, int64_t weight, int64_t bias, tp_handle* out);
+/* convOps.ts:17-62 conv2d (conv.wgsl:25-60): bias is a host list of Cout values
+ * or NULL; dilation is accepted and ignored, as in the reference */
+TP_API int tp_conv2d(int64_t input, int64_t weight, const float* bias, int nbias, const int64_t* stride, int ns,
+                     const int64_t* padding, int np, const int64_t* dilation, int nd, int groups, tp_handle* out);
+/* convOps.ts:64-108 conv2dInputBackward (conv_backward.wgsl:24-61) */
+TP_API int tp_conv2d_input_backward(int64_t grad_out, int64_t weight, const int64_t* input_shape,
+                                    const int64_t* grad_out_shape, const int64_t* stride, int ns,
+                                    const int64_t* padding, int np, tp_handle* out);
+/* convOps.ts:110-155 conv2dWeightBackward (conv_backward.wgsl:66-101) */
+TP_API int tp_conv2d_weight_backward(int64_t grad_out, int64_t input, const int64_t* weight_shape,
+                                     const int64_t* grad_out_shape, const int64_t* input_shape, const int64_t* stride,
+                                     int ns, const int64_t* padding, int np, tp_handle* out);
+/* convOps.ts:157-198 conv2dBiasBackward (conv_backward.wgsl:103-119) */
+TP_API int tp_conv2d_bias_backward(int64_t grad_out, int64_t out_ch, const int64_t* grad_out_shape, tp_handle* out);
+
+/* ---- pooling (poolingOps.ts:18-48, max_pool2d.wgsl:22-49) ------------------------ */
+TP_API int tp_max_pool2d(int64_t input, const int64_t* kernel, int nk, const int64_t* stride, int ns,
+                         const int64_t* padding, int np, const int64_t* dilation, int nd, tp_handle* out);
+/* New: also writes the flat ih*W+iw of each window's first maximum (int32) */
+TP_API int tp_max_pool2d_with_indices(int64_t input, const int64_t* kernel, int nk, const int64_t* stride, int ns,
+                                      const int64_t* padding, int np, const int64_t* dilation, int nd,
+                                      tp_handle* out, tp_handle* indices);
+/* New: the reference has no max-pool backward (tensor_nn_ops.py:57-72) */
+TP_API int tp_max_pool2d_backward(int64_t grad_out, int64_t indices, const int64_t* input_shape,
+                                  const int64_t* kernel, int nk, const int64_t* stride, int ns,
+                                  const int64_t* padding, int np, const int64_t* dilation, int nd, tp_handle* out);
+
+/* ---- normalisation (normalizationOps.ts, tensor_nn_ops.py) ------------------------ */
+/* normalizationOps.ts:20-126 batchNorm (inference, batchnorm.wgsl:20-36); ids of
+ * 0 mean "null" (weight 1, bias 0, mean 0, var 1) */
+TP_API int tp_batch_norm(int64_t input, int64_t weight, int64_t bias, int64_t running_mean, int64_t running_var,
+                         float eps, tp_handle* out);
+/* New: training-mode forward of tensor_nn_ops.py:92-254 in three launches;
+ * updates running stats in place, returns y and the saved mean / inv_std;
+ * fuse_relu applies ReLU to y */
+TP_API int tp_batch_norm_train(int64_t input, int64_t weight, int64_t bias, int64_t running_mean,
+                               int64_t running_var, float eps, float momentum, int fuse_relu, tp_handle* out,
+                               tp_handle* save_mean, tp_handle* save_invstd);
+/* New: backward with PyTorch's rule (the reference's autograd_rules.py:
+ * 1049-1130 throws for W != C and scales dweight/dbias by weight); relu_out id
+ * != 0 masks grad_out by relu_out > 0 first */
+TP_API int tp_batch_norm_backward(int64_t grad_out, int64_t input, int64_t weight, int64_t save_mean,
+                                  int64_t save_invstd, int64_t relu_out, tp_handle* dx, tp_handle* dweight,
+                                  tp_handle* dbias);
+/* normalizationOps.ts:128-171 layerNorm (layernorm.wgsl:14-42) over the last
+ * normalized_size values; save_mean / save_rstd may be NULL */
+TP_API int tp_layer_norm(int64_t input, int64_t normalized_size, int64_t gamma, int64_t beta, float eps,
+                         tp_handle* out, tp_handle* save_mean, tp_handle* save_rstd);
+/* New: LN backward, PyTorch's rule (autograd_rules.py:1133-1209 scales
+ * dgamma/dbeta by gamma) */
+TP_API int tp_layer_norm_backward(int64_t grad_out, int64_t input, int64_t normalized_size, int64_t gamma,
+                                  int64_t save_mean, int64_t save_rstd, tp_handle* dx, tp_handle* dgamma,
+                                  tp_handle* dbeta);
+
 /* ---- optimizer steps (reductionOps.ts:533-653), in place ------------------- */
 /* adamw_step.wgsl */
 TP_API int tp_adamw_step(int64_t param, int64_t grad, int64_t exp_avg, int64_t exp_avg_sq, float lr, float beta1,
@@ -224,6 +284,49 @@ TP_API int tpk_adam_group(int64_t group, int kind, float lr, float beta1, float 
 /* grad_scale multiplies each gradient on read (1/world for averaged DP grads) */
 TP_API int tpk_sgd_group(int64_t group, float lr, float momentum, float weight_decay, float dampening,
                          int nesterov, float grad_scale);
+
+/* ---- pointer-level kernels for a step driver (no allocation) ----------------- */
+/* conv2d forward / data-gradient / weight-gradient on NCHW device buffers
+ * (the kernels behind tp_conv2d, tp_conv2d_input_backward and
+ * tp_conv2d_weight_backward; groups = 1) */
+TP_API int tpk_conv2d_fwd(const float* x, const float* w, const float* bias, float* y, int64_t N, int64_t Cin,
+                          int64_t H, int64_t W, int64_t Cout, int KH, int KW, int SH, int SW, int PH, int PW);
+TP_API int tpk_conv2d_dgrad(const float* dy, const float* w, float* dx, int64_t N, int64_t Cin, int64_t H, int64_t W,
+                            int64_t Cout, int KH, int KW, int SH, int SW, int PH, int PW);
+TP_API int tpk_conv2d_wgrad(const float* dy, const float* x, float* dw, int64_t N, int64_t Cin, int64_t H, int64_t W,
+                            int64_t Cout, int KH, int KW, int SH, int SW, int PH, int PW);
+/* per-channel sum over N and the spatial dims (the conv bias gradient) */
+TP_API int tpk_channel_sum(const float* x, int64_t N, int64_t C, int64_t P, float* out);
+/* the kernels behind tp_batch_norm_train / tp_batch_norm_backward */
+TP_API int tpk_bn_train(const float* x, const float* w, const float* b, float* running_mean, float* running_var,
+                        float* y, float* save_mean, float* save_invstd, int64_t N, int64_t C, int64_t S, float eps,
+                        float momentum, int relu);
+TP_API int tpk_bn_backward(const float* dy, const float* x, const float* relu_src, const float* w, const float* mean,
+                           const float* invstd, float* dx, float* dw, float* db, int64_t N, int64_t C, int64_t S);
+/* square-window max-pool with int32 indices, and its backward */
+TP_API int tpk_maxpool_fwd(const float* x, float* y, int32_t* idx, int64_t N, int64_t C, int64_t H, int64_t W, int k,
+                           int s, int p);
+TP_API int tpk_maxpool_bwd(const float* dy, const int32_t* idx, float* dx, int64_t N, int64_t C, int64_t H, int64_t W,
+                           int k, int s, int p);
+/* C[M,N] = op(A) op(B) (+ bias[N]); a_t: A stored [K,M]; b_t: B stored [N,K] */
+TP_API int tpk_gemm(const float* A, int a_t, const float* B, int b_t, float* C, int64_t M, int64_t N, int64_t K,
+                    const float* bias);
+/* cross-entropy per row and its mean, both left in HBM (the reference reads
+ * the mean back to the host, reductionOps.ts:203-212) */
+TP_API int tpk_cross_entropy_mean(const float* logits, const float* targets, float* loss_rows, float* loss_mean,
+                                  int64_t B, int64_t C);
+/* grad = (softmax(logits) - onehot(target)) * scale (cross_entropy_backward.wgsl) */
+TP_API int tpk_cross_entropy_backward(const float* logits, const float* targets, float* grad, int64_t B, int64_t C,
+                                      float scale);
+TP_API int tpk_fill(float* x, int64_t n, float value);
+
+/* ---- CUDA graphs of the library stream ------------------------------------------ */
+/* capture every launch made between begin and end into one graph; call the
+ * same sequence once before capturing so scratch buffers have their size */
+TP_API int tp_graph_begin(void);
+TP_API int tp_graph_end(int64_t* out_graph);
+TP_API int tp_graph_launch(int64_t graph);
+TP_API int tp_graph_destroy(int64_t graph);
 
 #ifdef __cplusplus
 }

@@ -128,11 +128,14 @@ def _child(reference: str, mode: str, out_path: str) -> None:
     if mode == "examples":
         for ex_id, script, _keys in EXAMPLES:
             start = len(rt.trace)
+            seed0 = object.__getattribute__(rt, "_seed")
             buf = io.StringIO()
             with contextlib.redirect_stdout(buf):
                 exec(compile(open(os.path.join(ex_dir, script)).read(), script, "exec"), {"__name__": "__main__"})
             results[ex_id] = json.loads(buf.getvalue())
-            traces[ex_id] = rt.trace[start:]
+            # the playground runs examples in one page session, so the seed
+            # counter carries over; a trace starts by restoring it
+            traces[ex_id] = [{"m": "setSeed", "a": [seed0], "r": None}] + rt.trace[start:]
     else:
         batch, steps = (64, 10) if mode == "tiny_cnn" else (8, 2)
         src = TINY_CNN.replace("BATCH", str(batch)).replace("STEPS", str(steps))

@@ -1,0 +1,306 @@
+// Dense contractions of the hot path: matmul / linear and conv2d forward,
+// data-gradient, weight-gradient and bias-gradient, all as gather-GEMMs.
+//
+// Reference: matmul.wgsl:52-85 (one thread per output, sequential k, the tiled
+// entry :17-50 unused), conv.wgsl:25-60 and conv_backward.wgsl:24-119 (one
+// thread per output / input / weight element with serial loops).  The
+// implicit-GEMM mappings (tp_gemm.cuh) never materialise im2col or a
+// transposed operand.
+#include <cuda_runtime.h>
+
+#include <vector>
+
+#include "tp_core.h"
+#include "tp_launch.h"
+#include "tp_gemm.cuh"
+#include "tp_gemm_simt.cuh"
+
+namespace tp {
+
+// ---- per-channel sum of an NCHW tensor (conv_backward.wgsl:103-119) ---------------
+__global__ void k_channel_sum_part(const float* __restrict__ x, int64_t N, int64_t C, int64_t P, int splits,
+                                   double* __restrict__ part) {
+  __shared__ double sh[32];
+  int64_t c = blockIdx.x;
+  int split = blockIdx.y;
+  int64_t per = (N + splits - 1) / splits;
+  int64_t n0 = split * per, n1 = n0 + per < N ? n0 + per : N;
+  double s = 0.0;
+  for (int64_t n = n0; n < n1; ++n) {
+    const float* p = x + (n * C + c) * P;
+    for (int64_t i = threadIdx.x; i < P; i += blockDim.x) s += p[i];
+  }
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if (lane == 0) sh[w] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int k = 0; k < nw; ++k) t += sh[k];
+    part[c * splits + split] = t;
+  }
+}
+
+__global__ void k_channel_sum_finish(const double* __restrict__ part, int64_t C, int splits,
+                                     float* __restrict__ out) {
+  int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  double s = 0.0;
+  for (int k = 0; k < splits; ++k) s += part[c * splits + k];
+  out[c] = (float)s;
+}
+
+void launch_channel_sum(const float* x, int64_t N, int64_t C, int64_t P, float* out) {
+  if (C == 0) return;
+  int splits = 1;
+  while (C * splits < (int64_t)sm_count() * 4 && splits * 2 <= N) splits *= 2;
+  double* part = (double*)scratch((size_t)C * splits * sizeof(double));
+  TP_LAUNCH(k_channel_sum_part, dim3((unsigned)C, (unsigned)splits), 256, 0, x, N, C, P, splits, part);
+  TP_LAUNCH(k_channel_sum_finish, (unsigned)((C + 127) / 128), 128, 0, part, C, splits, out);
+}
+
+// ---- convolution launchers (pointer level) -------------------------------------------
+ConvShape conv_shape(int64_t N, int64_t Cin, int64_t H, int64_t W, int64_t Cout, int KH, int KW, int SH, int SW,
+                     int PH, int PW, int groups) {
+  TP_REQUIRE(SH > 0 && SW > 0 && PH >= 0 && PW >= 0 && KH > 0 && KW > 0, "conv2d: invalid stride/padding/kernel");
+  TP_REQUIRE(groups >= 1 && Cin % groups == 0 && Cout % groups == 0, "conv2d: channels not divisible by groups");
+  ConvShape s;
+  s.N = N;
+  s.Cin = Cin;
+  s.H = H;
+  s.W = W;
+  s.Cout = Cout;
+  s.KH = KH;
+  s.KW = KW;
+  s.SH = SH;
+  s.SW = SW;
+  s.PH = PH;
+  s.PW = PW;
+  s.icpg = (int)(Cin / groups);
+  s.ocpg = (int)(Cout / groups);
+  s.OH = (H + 2 * PH - KH) / SH + 1;  // convOps.ts:35-36 (dilation ignored)
+  s.OW = (W + 2 * PW - KW) / SW + 1;
+  TP_REQUIRE(s.OH > 0 && s.OW > 0, "conv2d: output would be empty");
+  return s;
+}
+
+void conv_fwd(const ConvShape& s, const float* x, const float* w, const float* bias, float* y) {
+  int groups = (int)(s.Cin / s.icpg);
+  LdConvIm2col la{x, s};
+  LdConvWeight lb{w, (int64_t)s.icpg * s.KH * s.KW, s.ocpg};
+  EpNCHW ep{y, bias, s.Cout, s.OH * s.OW, s.ocpg};
+  gemm_simt(la, lb, ep, s.N * s.OH * s.OW, s.ocpg, (int64_t)s.icpg * s.KH * s.KW, groups);
+}
+
+void conv_dgrad(const ConvShape& s, const float* dy, const float* w, float* dx) {
+  LdConvDgradA la{dy, s};
+  LdConvDgradB lb{w, s};
+  EpNCHW ep{dx, nullptr, s.Cin, s.H * s.W, (int)s.Cin};
+  gemm_simt(la, lb, ep, s.N * s.H * s.W, s.Cin, s.Cout * s.KH * s.KW, 1);
+}
+
+void conv_wgrad(const ConvShape& s, const float* dy, const float* x, float* dw) {
+  LdConvWgradA la{dy, s};
+  LdConvWgradB lb{x, s};
+  int64_t R = s.Cin * s.KH * s.KW;
+  EpRowMajor ep{dw, R, 0, nullptr, 0};
+  gemm_simt(la, lb, ep, s.Cout, R, s.N * s.OH * s.OW, 1);
+}
+
+// matmul.wgsl semantics: C[b] = A[b] (M x K) . B[b or shared] (K x N), row-major.
+void matmul_launch(const float* A, const float* B, float* C, int64_t batch, int64_t M, int64_t K, int64_t N,
+                   bool b_batched) {
+  LdRowMajor la{A, K, M * K};
+  LdColMajor lb{B, N, b_batched ? K * N : 0};
+  EpRowMajor ep{C, N, M * N, nullptr, 0};
+  TP_REQUIRE(batch <= 65535, "matmul: batch exceeds the grid limit");
+  gemm_simt(la, lb, ep, M, N, K, (int)batch);
+}
+
+// y[M, N] = x[M, K] . W[N, K]^T (+ bias[N]) (+ ReLU): nn.Linear without the
+// transpose / expand / add dispatches of functional.py:95-101.
+void linear_launch(const float* x, const float* w, const float* bias, float* y, int64_t M, int64_t K, int64_t N,
+                   bool relu) {
+  LdRowMajor la{x, K, 0};
+  LdRowMajor lb{w, K, 0};
+  EpRowMajor ep{y, N, 0, bias, relu ? 1 : 0};
+  gemm_simt(la, lb, ep, M, N, K, 1);
+}
+
+void gemm_launch(const float* A, bool a_t, const float* B, bool b_t, float* C, int64_t M, int64_t N, int64_t K,
+                 const float* bias) {
+  EpRowMajor ep{C, N, 0, bias, 0};
+  if (!a_t && b_t) gemm_simt(LdRowMajor{A, K, 0}, LdRowMajor{B, K, 0}, ep, M, N, K, 1);
+  else if (!a_t && !b_t) gemm_simt(LdRowMajor{A, K, 0}, LdColMajor{B, N, 0}, ep, M, N, K, 1);
+  else if (a_t && b_t) gemm_simt(LdColMajor{A, M, 0}, LdRowMajor{B, K, 0}, ep, M, N, K, 1);
+  else gemm_simt(LdColMajor{A, M, 0}, LdColMajor{B, N, 0}, ep, M, N, K, 1);
+}
+
+static int at(const int64_t* v, int n, int i, int dflt) { return n > i ? (int)v[i] : (n > 0 ? (int)v[0] : dflt); }
+
+}  // namespace tp
+
+using namespace tp;
+
+extern "C" {
+
+TP_API int tp_matmul(int64_t a, int64_t b, tp_handle* out) {
+  return guard([&] {
+    Tensor& A = get(a);
+    Tensor& B = get(b);
+    // arithmeticOps.ts:260-308 shape rules
+    if (A.ndim == 2 && B.ndim == 1) {
+      int64_t m = A.shape[0], k = A.shape[1];
+      TP_REQUIRE(k == B.shape[0], "matmul dimension mismatch: [%lld,%lld] x [%lld].", (long long)m, (long long)k,
+                 (long long)B.shape[0]);
+      int64_t s[2] = {m, 1};
+      Tensor C = make(s, 2, A.dtype);
+      matmul_launch(A.f(), B.f(), C.f(), 1, m, k, 1, false);
+      emit(C, out);
+    } else if (A.ndim == 1 && B.ndim == 2) {
+      int64_t k = A.shape[0], n = B.shape[1];
+      TP_REQUIRE(k == B.shape[0], "matmul dimension mismatch: [%lld] x [%lld,%lld].", (long long)k,
+                 (long long)B.shape[0], (long long)n);
+      int64_t s[2] = {1, n};
+      Tensor C = make(s, 2, B.dtype);
+      matmul_launch(A.f(), B.f(), C.f(), 1, 1, k, n, false);
+      emit(C, out);
+    } else if (A.ndim == 3 && B.ndim == 3) {
+      int64_t bt = A.shape[0], m = A.shape[1], k = A.shape[2], n = B.shape[2];
+      TP_REQUIRE(bt == B.shape[0], "matmul batch dim mismatch: %lld vs %lld.", (long long)bt, (long long)B.shape[0]);
+      TP_REQUIRE(k == B.shape[1], "matmul dimension mismatch: [%lld,%lld,%lld] x [%lld,%lld,%lld].", (long long)bt,
+                 (long long)m, (long long)k, (long long)B.shape[0], (long long)B.shape[1], (long long)n);
+      int64_t s[3] = {bt, m, n};
+      Tensor C = make(s, 3, A.dtype);
+      matmul_launch(A.f(), B.f(), C.f(), bt, m, k, n, true);
+      emit(C, out);
+    } else if (A.ndim == 2 && B.ndim == 2) {
+      int64_t m = A.shape[0], k = A.shape[1], n = B.shape[1];
+      TP_REQUIRE(k == B.shape[0], "matmul dimension mismatch: [%lld,%lld] x [%lld,%lld].", (long long)m,
+                 (long long)k, (long long)B.shape[0], (long long)n);
+      int64_t s[2] = {m, n};
+      Tensor C = make(s, 2, A.dtype);
+      matmul_launch(A.f(), B.f(), C.f(), 1, m, k, n, false);
+      emit(C, out);
+    } else if (A.ndim >= 3 && B.ndim == 2) {
+      int64_t bt = prod(A.shape, A.ndim - 2), m = A.shape[A.ndim - 2], k = A.shape[A.ndim - 1], n = B.shape[1];
+      TP_REQUIRE(k == B.shape[0], "matmul dimension mismatch: [...,%lld,%lld] x [%lld,%lld].", (long long)m,
+                 (long long)k, (long long)B.shape[0], (long long)n);
+      int64_t s[3] = {bt, m, n};
+      Tensor C = make(s, 3, A.dtype);
+      // one GEMM over the flattened rows: B is shared by every batch
+      matmul_launch(A.f(), B.f(), C.f(), 1, bt * m, k, n, false);
+      emit(C, out);
+    } else {
+      fail(TP_ERR_ARG, "matmul unsupported shapes: rank %d and rank %d.", A.ndim, B.ndim);
+    }
+  });
+}
+
+TP_API int tp_linear(int64_t x, int64_t w, int64_t bias, tp_handle* out) {
+  return guard([&] {
+    Tensor& X = get(x);
+    Tensor& Wt = get(w);
+    TP_REQUIRE(Wt.ndim == 2 && X.ndim >= 1, "linear expects weight [out, in]");
+    int64_t K = Wt.shape[1], N = Wt.shape[0];
+    TP_REQUIRE(X.shape[X.ndim - 1] == K, "linear: input features %lld != weight in_features %lld",
+               (long long)X.shape[X.ndim - 1], (long long)K);
+    const float* bp = nullptr;
+    if (bias) {
+      Tensor& B = get(bias);
+      TP_REQUIRE(B.numel == N, "linear: bias has %lld values, expected %lld", (long long)B.numel, (long long)N);
+      bp = B.f();
+    }
+    std::vector<int64_t> s(X.shape, X.shape + X.ndim);
+    s.back() = N;
+    Tensor Y = make_like_shape(s, X.dtype);
+    linear_launch(X.f(), Wt.f(), bp, Y.f(), X.numel / K, K, N, false);
+    emit(Y, out);
+  });
+}
+
+// convOps.ts:17-62: bias arrives as a host list (or null), dilation is ignored.
+TP_API int tp_conv2d(int64_t input, int64_t weight, const float* bias, int nbias, const int64_t* stride, int ns,
+                     const int64_t* padding, int np, const int64_t* dilation, int nd, int groups, tp_handle* out) {
+  (void)dilation;
+  (void)nd;
+  return guard([&] {
+    Tensor& X = get(input);
+    Tensor& Wt = get(weight);
+    TP_REQUIRE(X.ndim == 4 && Wt.ndim == 4, "conv2d expects NCHW input and OIHW weight");
+    int g = groups > 0 ? groups : 1;
+    TP_REQUIRE(Wt.shape[1] * g == X.shape[1], "conv2d: weight in_channels %lld x groups %d != input channels %lld",
+               (long long)Wt.shape[1], g, (long long)X.shape[1]);
+    ConvShape s = conv_shape(X.shape[0], X.shape[1], X.shape[2], X.shape[3], Wt.shape[0], (int)Wt.shape[2],
+                             (int)Wt.shape[3], at(stride, ns, 0, 1), at(stride, ns, 1, 1), at(padding, np, 0, 0),
+                             at(padding, np, 1, 0), g);
+    float* db = nullptr;
+    if (bias && nbias > 0) {
+      TP_REQUIRE(nbias == s.Cout, "conv2d: bias has %d values, expected %lld", nbias, (long long)s.Cout);
+      db = (float*)dalloc((size_t)nbias * 4);  // its own block: the GEMM may grow the shared scratch
+      TP_CUDA(cudaMemcpyAsync(db, bias, (size_t)nbias * 4, cudaMemcpyHostToDevice, stream()));
+    }
+    int64_t shp[4] = {s.N, s.Cout, s.OH, s.OW};
+    Tensor Y = make(shp, 4, X.dtype);
+    conv_fwd(s, X.f(), Wt.f(), db, Y.f());
+    if (db) dfree(db);  // stream-ordered: released after the convolution ran
+    emit(Y, out);
+  });
+}
+
+// convOps.ts:64-108 (groups forced to 1 by the reference).
+TP_API int tp_conv2d_input_backward(int64_t grad_out, int64_t weight, const int64_t* input_shape,
+                                    const int64_t* grad_out_shape, const int64_t* stride, int ns,
+                                    const int64_t* padding, int np, tp_handle* out) {
+  return guard([&] {
+    Tensor& G = get(grad_out);
+    Tensor& Wt = get(weight);
+    TP_REQUIRE(Wt.ndim == 4, "conv2dInputBackward expects an OIHW weight");
+    ConvShape s = conv_shape(input_shape[0], input_shape[1], input_shape[2], input_shape[3], grad_out_shape[1],
+                             (int)Wt.shape[2], (int)Wt.shape[3], at(stride, ns, 0, 1), at(stride, ns, 1, 1),
+                             at(padding, np, 0, 0), at(padding, np, 1, 0), 1);
+    s.OH = grad_out_shape[2];
+    s.OW = grad_out_shape[3];
+    TP_REQUIRE(G.numel == s.N * s.Cout * s.OH * s.OW, "conv2dInputBackward: grad_output size mismatch");
+    TP_REQUIRE(Wt.numel == s.Cout * s.Cin * s.KH * s.KW, "conv2dInputBackward: weight size mismatch");
+    Tensor X = make(input_shape, 4, G.dtype);
+    conv_dgrad(s, G.f(), Wt.f(), X.f());
+    emit(X, out);
+  });
+}
+
+// convOps.ts:110-155.
+TP_API int tp_conv2d_weight_backward(int64_t grad_out, int64_t input, const int64_t* weight_shape,
+                                     const int64_t* grad_out_shape, const int64_t* input_shape, const int64_t* stride,
+                                     int ns, const int64_t* padding, int np, tp_handle* out) {
+  return guard([&] {
+    Tensor& G = get(grad_out);
+    Tensor& X = get(input);
+    ConvShape s = conv_shape(input_shape[0], input_shape[1], input_shape[2], input_shape[3], weight_shape[0],
+                             (int)weight_shape[2], (int)weight_shape[3], at(stride, ns, 0, 1), at(stride, ns, 1, 1),
+                             at(padding, np, 0, 0), at(padding, np, 1, 0), 1);
+    s.OH = grad_out_shape[2];
+    s.OW = grad_out_shape[3];
+    TP_REQUIRE(G.numel == s.N * s.Cout * s.OH * s.OW, "conv2dWeightBackward: grad_output size mismatch");
+    TP_REQUIRE(X.numel == s.N * s.Cin * s.H * s.W, "conv2dWeightBackward: input size mismatch");
+    TP_REQUIRE(weight_shape[1] == s.Cin, "conv2dWeightBackward: groups are not supported (as in the reference)");
+    Tensor Wg = make(weight_shape, 4, G.dtype);
+    conv_wgrad(s, G.f(), X.f(), Wg.f());
+    emit(Wg, out);
+  });
+}
+
+// convOps.ts:157-198.
+TP_API int tp_conv2d_bias_backward(int64_t grad_out, int64_t out_ch, const int64_t* grad_out_shape, tp_handle* out) {
+  return guard([&] {
+    Tensor& G = get(grad_out);
+    int64_t N = grad_out_shape[0], P = grad_out_shape[2] * grad_out_shape[3];
+    TP_REQUIRE(G.numel == N * out_ch * P, "conv2dBiasBackward: grad_output size mismatch");
+    int64_t s[1] = {out_ch};
+    Tensor B = make(s, 1, G.dtype);
+    launch_channel_sum(G.f(), N, out_ch, P, B.f());
+    emit(B, out);
+  });
+}
+
+}  // extern "C"

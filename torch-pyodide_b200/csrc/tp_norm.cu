@@ -18,6 +18,7 @@
 #include <cuda_runtime.h>
 
 #include "tp_core.h"
+#include "tp_launch.h"
 
 namespace tp {
 

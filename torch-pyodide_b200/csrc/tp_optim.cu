@@ -18,6 +18,7 @@
 #include <unordered_map>
 
 #include "tp_core.h"
+#include "tp_launch.h"
 
 namespace tp {
 

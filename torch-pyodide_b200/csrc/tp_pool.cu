@@ -8,13 +8,9 @@
 #include <cuda_runtime.h>
 
 #include "tp_core.h"
+#include "tp_launch.h"
 
 namespace tp {
-
-struct PoolGeom {
-  int64_t N, C, H, W, OH, OW;
-  int KH, KW, SH, SW, PH, PW, DH, DW;
-};
 
 __global__ void k_maxpool_fwd(const float* __restrict__ x, float* __restrict__ y, int32_t* __restrict__ idx,
                               PoolGeom g, int64_t total) {

@@ -19,6 +19,7 @@
 #include <cmath>
 
 #include "tp_core.h"
+#include "tp_launch.h"
 
 namespace tp {
 

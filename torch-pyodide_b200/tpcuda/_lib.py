@@ -111,6 +111,20 @@ SIGNATURES: dict[str, list] = {
     "tp_log_softmax_backward": [I64, I64, I64, I64, HP],
     "tp_cross_entropy": [I64, I64, HP],
     "tp_cross_entropy_backward": [I64, I64, I64, INT, HP],
+    "tp_matmul": [I64, I64, HP],
+    "tp_linear": [I64, I64, I64, HP],
+    "tp_conv2d": [I64, I64, F32P, INT, I64P, INT, I64P, INT, I64P, INT, INT, HP],
+    "tp_conv2d_input_backward": [I64, I64, I64P, I64P, I64P, INT, I64P, INT, HP],
+    "tp_conv2d_weight_backward": [I64, I64, I64P, I64P, I64P, I64P, INT, I64P, INT, HP],
+    "tp_conv2d_bias_backward": [I64, I64, I64P, HP],
+    "tp_max_pool2d": [I64, I64P, INT, I64P, INT, I64P, INT, I64P, INT, HP],
+    "tp_max_pool2d_with_indices": [I64, I64P, INT, I64P, INT, I64P, INT, I64P, INT, HP, HP],
+    "tp_max_pool2d_backward": [I64, I64, I64P, I64P, INT, I64P, INT, I64P, INT, I64P, INT, HP],
+    "tp_batch_norm": [I64, I64, I64, I64, I64, F32, HP],
+    "tp_batch_norm_train": [I64, I64, I64, I64, I64, F32, F32, INT, HP, HP, HP],
+    "tp_batch_norm_backward": [I64, I64, I64, I64, I64, I64, HP, HP, HP],
+    "tp_layer_norm": [I64, I64, I64, I64, F32, HP, HP, HP],
+    "tp_layer_norm_backward": [I64, I64, I64, I64, I64, I64, HP, HP, HP],
     "tp_adamw_step": [I64, I64, I64, I64] + [F32] * 7,
     "tp_adam_step": [I64, I64, I64, I64] + [F32] * 7,
     "tp_sgd_step": [I64, I64, I64, F32, F32, F32, F32, INT],
@@ -121,6 +135,22 @@ SIGNATURES: dict[str, list] = {
     "tpk_group_destroy": [I64],
     "tpk_adam_group": [I64, INT] + [F32] * 7,
     "tpk_sgd_group": [I64, F32, F32, F32, F32, INT, F32],
+    "tpk_conv2d_fwd": [P, P, P, P, I64, I64, I64, I64, I64, INT, INT, INT, INT, INT, INT],
+    "tpk_conv2d_dgrad": [P, P, P, I64, I64, I64, I64, I64, INT, INT, INT, INT, INT, INT],
+    "tpk_conv2d_wgrad": [P, P, P, I64, I64, I64, I64, I64, INT, INT, INT, INT, INT, INT],
+    "tpk_channel_sum": [P, I64, I64, I64, P],
+    "tpk_bn_train": [P, P, P, P, P, P, P, P, I64, I64, I64, F32, F32, INT],
+    "tpk_bn_backward": [P, P, P, P, P, P, P, P, P, I64, I64, I64],
+    "tpk_maxpool_fwd": [P, P, P, I64, I64, I64, I64, INT, INT, INT],
+    "tpk_maxpool_bwd": [P, P, P, I64, I64, I64, I64, INT, INT, INT],
+    "tpk_gemm": [P, INT, P, INT, P, I64, I64, I64, P],
+    "tpk_cross_entropy_mean": [P, P, P, P, I64, I64],
+    "tpk_cross_entropy_backward": [P, P, P, I64, I64, F32],
+    "tpk_fill": [P, I64, F32],
+    "tp_graph_begin": [],
+    "tp_graph_end": [I64P],
+    "tp_graph_launch": [I64],
+    "tp_graph_destroy": [I64],
 }
 
 _RESTYPE = {"tp_last_error": ctypes.c_char_p}

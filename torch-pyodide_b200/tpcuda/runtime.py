@@ -368,6 +368,106 @@ class CudaRuntime:
         red = {"none": 0, "sum": 1, "mean": 2}[str(reduction)]
         return self._call(self.lib.tp_cross_entropy_backward, int(go), int(inp), int(tgt), red)
 
+    # ---- dense contractions (arithmeticOps.ts:260-340, convOps.ts) --------------
+    def matmul(self, a, b):
+        return self._call(self.lib.tp_matmul, int(a), int(b))
+
+    mm = matmul
+    bmm = matmul
+    mv = matmul
+
+    def linear(self, x, weight, bias=None):
+        return self._call(self.lib.tp_linear, int(x), int(weight), int(bias) if bias is not None else 0)
+
+    def conv2d(self, inp, weight, bias, stride, padding, dilation, groups):
+        if bias is not None:
+            barr = np.asarray(list(bias), dtype=np.float32)
+            bp, nb = barr.ctypes.data_as(_lib.F32P), int(barr.size)
+        else:
+            barr, bp, nb = None, None, 0
+        st, pd, dl = list(stride), list(padding), list(dilation)
+        return self._call(self.lib.tp_conv2d, int(inp), int(weight), bp, nb, i64arr(st), len(st), i64arr(pd),
+                          len(pd), i64arr(dl), len(dl), int(groups))
+
+    def conv2dInputBackward(self, go, weight, inputShape, gradOutputShape, stride, padding):
+        st, pd = list(stride), list(padding)
+        return self._call(self.lib.tp_conv2d_input_backward, int(go), int(weight), i64arr(inputShape),
+                          i64arr(gradOutputShape), i64arr(st), len(st), i64arr(pd), len(pd))
+
+    def conv2dWeightBackward(self, go, inp, weightShape, gradOutputShape, inputShape, stride, padding):
+        st, pd = list(stride), list(padding)
+        return self._call(self.lib.tp_conv2d_weight_backward, int(go), int(inp), i64arr(weightShape),
+                          i64arr(gradOutputShape), i64arr(inputShape), i64arr(st), len(st), i64arr(pd), len(pd))
+
+    def conv2dBiasBackward(self, go, outCh, gradOutputShape):
+        return self._call(self.lib.tp_conv2d_bias_backward, int(go), int(outCh), i64arr(gradOutputShape))
+
+    # ---- pooling (poolingOps.ts:18-48) ----------------------------------------------
+    @staticmethod
+    def _pool_args(kernelSize, stride, padding, dilation):
+        k, s, p, d = (list(v) if v is not None else [] for v in (kernelSize, stride, padding, dilation))
+        return [i64arr(k), len(k), i64arr(s), len(s), i64arr(p), len(p), i64arr(d), len(d)]
+
+    def maxPool2d(self, inp, kernelSize, stride, padding, dilation):
+        return self._call(self.lib.tp_max_pool2d, int(inp), *self._pool_args(kernelSize, stride, padding, dilation))
+
+    def maxPool2dWithIndices(self, inp, kernelSize, stride, padding, dilation):
+        hy, hi = Handle(), Handle()
+        check(self.lib.tp_max_pool2d_with_indices(int(inp), *self._pool_args(kernelSize, stride, padding, dilation),
+                                                  ctypes.byref(hy), ctypes.byref(hi)))
+        return [hy.to_dict(), hi.to_dict()]
+
+    def maxPool2dBackward(self, go, indices, inputShape, kernelSize, stride, padding, dilation):
+        return self._call(self.lib.tp_max_pool2d_backward, int(go), int(indices), i64arr(inputShape),
+                          *self._pool_args(kernelSize, stride, padding, dilation))
+
+    # ---- normalisation (normalizationOps.ts, tensor_nn_ops.py) --------------------
+    @staticmethod
+    def _opt(tid):
+        return int(tid) if tid is not None else 0
+
+    def batchNorm(self, inp, weight, bias, runningMean, runningVar, eps):
+        o = self._opt
+        return self._call(self.lib.tp_batch_norm, int(inp), o(weight), o(bias), o(runningMean), o(runningVar),
+                          float(eps))
+
+    def batchNormTrain(self, inp, weight, bias, runningMean, runningVar, eps, momentum, fuseRelu=False):
+        o = self._opt
+        hs = [Handle(), Handle(), Handle()]
+        check(self.lib.tp_batch_norm_train(int(inp), o(weight), o(bias), o(runningMean), o(runningVar), float(eps),
+                                           float(momentum), 1 if fuseRelu else 0, *[ctypes.byref(h) for h in hs]))
+        return [h.to_dict() for h in hs]
+
+    def batchNormBackward(self, go, inp, weight, saveMean, saveInvstd, reluOut=None):
+        o = self._opt
+        hs = [Handle(), Handle(), Handle()]
+        check(self.lib.tp_batch_norm_backward(int(go), int(inp), o(weight), int(saveMean), int(saveInvstd),
+                                              o(reluOut), *[ctypes.byref(h) for h in hs]))
+        return [h.to_dict() for h in hs]
+
+    def layerNorm(self, inp, normalizedShape, gamma, beta, eps):
+        h = Handle()
+        check(self.lib.tp_layer_norm(int(inp), _prod(normalizedShape), self._opt(gamma), self._opt(beta),
+                                     float(eps), ctypes.byref(h), None, None))
+        return h.to_dict()
+
+    def _call3(self, fn, *args):
+        hs = [Handle(), Handle(), Handle()]
+        check(fn(*args, *[ctypes.byref(h) for h in hs]))
+        return [h.to_dict() for h in hs]
+
+    def layerNormForward(self, inp, normalizedShape, gamma, beta, eps):
+        return self._call3(self.lib.tp_layer_norm, int(inp), _prod(normalizedShape), self._opt(gamma),
+                           self._opt(beta), float(eps))
+
+    def layerNormBackward(self, go, inp, normalizedShape, gamma, saveMean, saveRstd):
+        hs = self._call3(self.lib.tp_layer_norm_backward, int(go), int(inp), _prod(normalizedShape),
+                         self._opt(gamma), int(saveMean), int(saveRstd))
+        nshape = [int(s) for s in normalizedShape]
+        for h in hs[1:]:
+            h["shape"] = nshape
+        return hs
+
     # ---- optimizer steps (in place, return None) ---------------------------------
     def adamWStep(self, p, g, m, v, lr, b1, b2, eps, wd, stepSize, invSqrtBc2):
         check(self.lib.tp_adamw_step(int(p), int(g), int(m), int(v), lr, b1, b2, eps, wd, stepSize, invSqrtBc2))
