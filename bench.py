@@ -335,12 +335,201 @@ def run_ours(args, rank, world, local):
         print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# VGG-11-BN data-parallel training: global batch 1024 split over the ranks
+
+VGG_GLOBAL_BATCH = 1024
+VGG_WORKLOAD = ("vgg11-bn train step, x[B,3,32,32]~N(0,1), y~U{0..9}, SGD mom 0.9 wd 5e-4 lr 0.05, "
+                "global batch 1024")
+
+
+def tf32x3_peak():
+    """3xTF32 dense peak derived from the measured bf16 GEMM rate: TF32 runs at
+    half the bf16 rate on Blackwell tensor cores and 3xTF32 issues three MMAs
+    per product."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["bf16_tflops"]) / 2 / 3, float(d["bf16_tflops"]), "measured"
+    return 1590.0 / 2 / 3, 1590.0, "fallback"
+
+
+def cpu_vgg(batch: int, steps: int) -> dict:
+    """The oracle composition of the same training step, on host cores."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    from oracle_runtime import OracleRuntime
+    from vgg_oracle import oracle_step
+
+    class Plan:  # the block plan of tpcuda.vgg without touching the GPU
+        blocks = []
+
+    cfg = [64, "M", 128, "M", 256, 256, "M", 512, 512, "M", 512, 512, "M"]
+    cin, H, i = 3, 32, 0
+    while i < len(cfg):
+        pool = i + 1 < len(cfg) and cfg[i + 1] == "M"
+        Plan.blocks.append({"cin": cin, "cout": cfg[i], "H": H, "W": H, "pool": pool})
+        cin = cfg[i]
+        H = H // 2 if pool else H
+        i += 2 if pool else 1
+    rng = np.random.default_rng(0)
+    params = {"fc.w": (rng.uniform(-0.04, 0.04, 5120).astype(np.float32), [10, 512]),
+              "fc.b": (np.zeros(10, np.float32), [10])}
+    stats = []
+    for li, b in enumerate(Plan.blocks):
+        bound = 1 / (b["cin"] * 9) ** 0.5
+        params[f"conv{li}.w"] = (rng.uniform(-bound, bound, b["cout"] * b["cin"] * 9).astype(np.float32),
+                                 [b["cout"], b["cin"], 3, 3])
+        params[f"conv{li}.b"] = (np.zeros(b["cout"], np.float32), [b["cout"]])
+        params[f"bn{li}.g"] = (np.ones(b["cout"], np.float32), [b["cout"]])
+        params[f"bn{li}.b"] = (np.zeros(b["cout"], np.float32), [b["cout"]])
+        stats.append((np.zeros(b["cout"], np.float32), np.ones(b["cout"], np.float32)))
+    x = rng.standard_normal((batch, 3, 32, 32)).astype(np.float32)
+    y = rng.integers(0, 10, batch).astype(np.float32)
+    orc = OracleRuntime()
+    times = []
+    for _ in range(steps + 1):
+        t0 = time.perf_counter()
+        oracle_step(orc, Plan, params, x, y, stats, 0.05, 0.9, 5e-4)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times[1:])
+    return {"imgs_per_s": batch / t, "sec": t, "batch": batch}
+
+
+def run_vgg(args, rank, world, local):
+    import ctypes
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", init_method="env://", device_id=torch.device("cuda", local),
+                                timeout=__import__("datetime").timedelta(seconds=300))
+    from tpcuda import CudaRuntime
+    from tpcuda.dp import comm_from_torch_dist
+    from tpcuda.vgg import VGG11BN
+    rt = CudaRuntime(local)
+    stream = torch.cuda.ExternalStream(rt.stream(), device=torch.device("cuda", local))
+    comm = comm_from_torch_dist(rt.lib)
+    B = VGG_GLOBAL_BATCH // world
+    model = VGG11BN(rt, B, seed=0, world=world, comm=comm)
+    rng = np.random.default_rng(100 + rank)
+    hx = torch.from_numpy(rng.standard_normal((B, 3, 32, 32)).astype(np.float32)).pin_memory()
+    hy = torch.from_numpy(rng.integers(0, 10, B).astype(np.float32)).pin_memory()
+    model.set_batch_device(hx.data_ptr(), hy.data_ptr())
+    model.capture()
+    for _ in range(args.warmup):
+        model.step()
+    rt.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        rt.synchronize()
+
+    def tmax(ms):
+        t = torch.tensor([ms], device="cuda")
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident timed region: graph replays of the whole step ----
+    clocks = ClockSampler(local)
+    barrier()
+    clocks.start()
+    launches0 = rt.kernelLaunches()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        model.step()
+    e1.record(stream)
+    e1.synchronize()
+    launches = rt.kernelLaunches() - launches0
+    clk = clocks.stop()
+    ms_step = tmax(e0.elapsed_time(e1)) / args.steps
+    value = VGG_GLOBAL_BATCH / (ms_step * 1e-3)
+    loss_after = model.read_loss()
+
+    # ---- end to end: pinned host batch -> HBM, step, loss back to host ----
+    e2e_steps = max(3, min(args.steps, 20))
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(e2e_steps):
+        model.set_batch_device(hx.data_ptr(), hy.data_ptr())
+        model.step()
+        model.read_loss()
+    f1.record(stream)
+    f1.synchronize()
+    e2e_ms = tmax(f0.elapsed_time(f1)) / e2e_steps
+    e2e_value = VGG_GLOBAL_BATCH / (e2e_ms * 1e-3)
+
+    # ---- dominant kernel: the implicit-GEMM convolution of block 4 (256->256 @ 8x8),
+    # timed alone with events on the library stream ----
+    b4 = model.blocks[3]
+    lib = rt.lib
+    flops = 2.0 * B * b4["cout"] * b4["H"] * b4["W"] * b4["cin"] * 9
+    reps = 20
+    xin = model.blocks[2]["out"]
+    conv_args = (ctypes.c_void_p(xin), ctypes.c_void_p(model.p("conv3.w")), ctypes.c_void_p(model.p("conv3.b")),
+                 ctypes.c_void_p(b4["z"]), B, b4["cin"], b4["H"], b4["W"], b4["cout"], 3, 3, 1, 1, 1, 1)
+    lib.tpk_conv2d_fwd(*conv_args)
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record(stream)
+    for _ in range(reps):
+        lib.tpk_conv2d_fwd(*conv_args)
+    g1.record(stream)
+    g1.synchronize()
+    k_ms = g0.elapsed_time(g1) / reps
+    achieved = flops / (k_ms * 1e-3) / 1e12
+    peak3, bf16, peak_kind = tf32x3_peak()
+
+    if comm is not None:
+        comm.sync(60000)
+    model.close()
+    if comm is not None:
+        comm.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": "VGG-11-BN train imgs/s", "value": round(value, 1), "unit": "imgs/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": VGG_WORKLOAD, "global_batch": VGG_GLOBAL_BATCH, "per_rank_batch": B,
+                   "parallelism": f"dp{world}", "l2": "per-step activations ~1.6 GB per rank at batch 1024 > L2",
+                   "loss_after_timed_steps": round(loss_after, 5)},
+        "gpu_launches": int(launches),
+        "clocks": clk,
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak3, 1), "unit": "TFLOP/s",
+                     "frac": round(achieved / peak3, 4), "traffic": None,
+                     "peak_source": f"{peak_kind} bf16_tflops {bf16} / 2 (tf32) / 3 (3xTF32)",
+                     "kernel": "conv3x3 forward gather-GEMM, block 4 (256->256 @ 8x8)",
+                     "kernel_ms": round(k_ms, 4), "step_tflops": round(model.step_flops() * world / 1e12, 4)},
+        "e2e": {"value": round(e2e_value, 1), "unit": "imgs/s", "h2d_bytes_per_step": int(hx.numel() * 4 + hy.numel() * 4),
+                "d2h_bytes_per_step": 4, "path": "tp_memcpy_h2d(pinned batch) + tp_graph_launch(step) + loss readback"},
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
+        r = cpu_vgg(2, 2)
+        line["cpu_baseline"] = {"value": round(r["imgs_per_s"], 4), "unit": "imgs/s", "cores": os.cpu_count() or 1,
+                                "kind": "port", "sample": "oracle composition of the same step at batch 2, "
+                                                          "median of 2 steps"}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["adamw", "vgg"], default="adamw")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tensors", type=int, default=NTENSORS,
                     help="number of parameter tensors (64 = the benchmark; fewer for profiler captures)")
@@ -350,6 +539,8 @@ def main():
     rank, world, local = dist_setup(args.gpus)
     if args.impl == "reference":
         run_reference(args, rank, world)
+    elif args.workload == "vgg":
+        run_vgg(args, rank, world, local)
     else:
         run_ours(args, rank, world, local)
 

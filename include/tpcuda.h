@@ -320,6 +320,21 @@ TP_API int tpk_cross_entropy_backward(const float* logits, const float* targets,
                                       float scale);
 TP_API int tpk_fill(float* x, int64_t n, float value);
 
+/* ---- data-parallel gradient exchange (new: the reference has no parallelism) ---- */
+/* NCCL unique id of rank 0 (128 bytes) to hand to every rank */
+TP_API int tp_comm_unique_id(char* out, int len);
+TP_API int tp_comm_init(int rank, int world, const char* unique_id, int len);
+/* in-place sum over ranks, queued after the work already on the library stream,
+ * run on the communication stream */
+TP_API int tp_comm_allreduce_async(float* ptr, int64_t count);
+/* the library stream waits for every all-reduce issued so far */
+TP_API int tp_comm_wait(void);
+/* host wait for the library stream with a communicator watchdog: on an NCCL
+ * error or after timeout_ms the communicator is aborted and an error returned */
+TP_API int tp_comm_sync(int timeout_ms);
+TP_API int tp_comm_destroy(void);
+TP_API int tp_comm_info(int* rank, int* world);
+
 /* ---- CUDA graphs of the library stream ------------------------------------------ */
 /* capture every launch made between begin and end into one graph; call the
  * same sequence once before capturing so scratch buffers have their size */

@@ -1,0 +1,68 @@
+"""VGG-11-BN training step composed from the CPU oracle's op restatements.
+
+TEST INFRASTRUCTURE ONLY: the checker for tpcuda.vgg (tests/test_gpu_vgg.py)
+and the CPU baseline of bench.py.  Each op is the oracle restatement of the
+reference shader (conv.wgsl, conv_backward.wgsl, max_pool2d.wgsl, ...) or of
+the intended training semantics the reference composes in Python
+(tensor_nn_ops.py:92-254 BN training; PyTorch's BN / max-pool backward rules).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+
+def oracle_step(orc, model, params, x, y, bn_stats, lr, mom, wd):
+    """One step of the same network on the oracle; returns (loss, new params, running stats)."""
+    B = x.shape[0]
+
+    def T(a, shape=None):
+        a = np.ascontiguousarray(a, np.float32)
+        return orc.tensorFromData(a.ravel().tolist(), list(shape or a.shape), "float32")["id"]
+
+    P = {k: T(v, s) for k, (v, s) in params.items()}
+    xin = T(x)
+    saved = []
+    h = xin
+    for li, b in enumerate(model.blocks):
+        rm, rv = T(bn_stats[li][0]), T(bn_stats[li][1])
+        z = orc.conv2d(h, P[f"conv{li}.w"], orc.toList(P[f"conv{li}.b"]), [1], [1], [1], 1)["id"]
+        yb, mean, inv = [r["id"] for r in orc.batchNormTrain(z, P[f"bn{li}.g"], P[f"bn{li}.b"], rm, rv, 1e-5, 0.1)]
+        a = orc.relu(yb)["id"]
+        rec = {"x": h, "z": z, "a": a, "mean": mean, "inv": inv, "rm": rm, "rv": rv}
+        if b["pool"]:
+            pm, idx = [r["id"] for r in orc.maxPool2dWithIndices(a, [2], [2], [0], [1])]
+            rec["idx"] = idx
+            h = pm
+        else:
+            h = a
+        saved.append(rec)
+    feat = orc.reshape(h, [B, 512])["id"]
+    logits = orc.add(orc.matmul(feat, orc.transpose2d(P["fc.w"])["id"])["id"], P["fc.b"])["id"]
+    yt = T(y)
+    loss = orc.toList(orc.mean(orc.crossEntropy(logits, yt)["id"])["id"])[0]
+    one = T(np.ones(1))
+    dlog = orc.crossEntropyBackward(one, logits, yt, "mean")["id"]
+    G = {"fc.w": orc.matmul(orc.transpose2d(dlog)["id"], feat)["id"], "fc.b": orc.sumDim(dlog, 0, False)["id"]}
+    g = orc.reshape(orc.matmul(dlog, P["fc.w"])["id"], [B, 512, 1, 1])["id"]
+    zero = T(np.zeros(1))
+    for li in reversed(range(len(model.blocks))):
+        b, rec = model.blocks[li], saved[li]
+        C, H, W = b["cout"], b["H"], b["W"]
+        ashape = [B, C, H, W]
+        if b["pool"]:
+            g = orc.maxPool2dBackward(g, rec["idx"], ashape, [2], [2], [0], [1])["id"]
+        g = orc.mul(g, orc.gt(rec["a"], zero)["id"])["id"]
+        dz, dgm, dbt = [r["id"] for r in orc.batchNormBackward(g, rec["z"], P[f"bn{li}.g"], rec["mean"], rec["inv"])]
+        G[f"bn{li}.g"], G[f"bn{li}.b"] = dgm, dbt
+        G[f"conv{li}.b"] = orc.conv2dBiasBackward(dz, C, ashape)["id"]
+        xshape = [B, b["cin"], H, W]
+        G[f"conv{li}.w"] = orc.conv2dWeightBackward(dz, rec["x"], [C, b["cin"], 3, 3], ashape, xshape, [1], [1])["id"]
+        if li > 0:
+            g = orc.conv2dInputBackward(dz, P[f"conv{li}.w"], xshape, ashape, [1], [1])["id"]
+    names = list(params)
+    moms = [T(np.zeros(int(np.prod(params[n][1])))) for n in names]
+    orc.sgdStepMulti([P[n] for n in names], [G[n] for n in names], moms, lr, mom, wd, 0.0, False)
+    new = {n: np.asarray(orc.toList(P[n]), np.float32) for n in names}
+    stats = [(np.asarray(orc.toList(r["rm"]), np.float32), np.asarray(orc.toList(r["rv"]), np.float32))
+             for r in saved]
+    return loss, new, stats

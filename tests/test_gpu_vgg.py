@@ -1,0 +1,90 @@
+"""The VGG-11-BN training step (tpcuda.vgg) against the same step composed from
+the CPU oracle's op restatements: conv2d, BN training forward/backward, ReLU,
+max-pool with indices, linear, cross-entropy and the fused SGD step.
+
+Checks the loss, every parameter after the update and the BN running stats,
+at 1e-4 relative to each tensor's scale (the bar for conv / norm / matmul).
+"""
+import math
+
+import numpy as np
+import pytest
+
+from vgg_oracle import oracle_step
+
+pytestmark = pytest.mark.gpu
+
+
+def close(a, b, rel=1e-4):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    scale = max(1e-12, float(np.max(np.abs(b))))
+    return float(np.max(np.abs(a - b))) <= rel * scale
+
+
+@pytest.mark.parametrize("batch", [4, 16])
+def test_vgg_step_matches_oracle_composition(cuda_rt, oracle_rt, batch):
+    from tpcuda.vgg import VGG11BN
+    m = VGG11BN(cuda_rt, batch, seed=3)
+    rng = np.random.default_rng(7)
+    x = rng.standard_normal((batch, 3, 32, 32)).astype(np.float32)
+    y = rng.integers(0, 10, batch).astype(np.float32)
+    m._h2d(m.x, x)
+    m._h2d(m.y, y)
+    params = {n: (m.param_array(n), s) for n, s, _ in m.param_specs}
+    stats = [(m.read(b["rm"], b["cout"]), m.read(b["rv"], b["cout"])) for b in m.blocks]
+    loss_o, new_o, stats_o = oracle_step(oracle_rt, m, params, x, y, stats, m.lr, m.momentum, m.wd)
+    m.step_eager()
+    loss_c = m.read_loss()
+    assert math.isclose(loss_c, loss_o, rel_tol=1e-5), (loss_c, loss_o)
+    # the update moves each parameter by lr * (grad + wd * p); compare the
+    # update itself, relative to the largest update of the step (a conv bias
+    # feeding a BN has a gradient that is zero up to rounding, so a per-tensor
+    # relative bound would compare rounding noise)
+    upd_c = {n: m.param_array(n) - params[n][0] for n in params}
+    upd_o = {n: new_o[n] - params[n][0] for n in params}
+    top = max(float(np.max(np.abs(u))) for u in upd_o.values())
+    for n in params:
+        err = float(np.max(np.abs(upd_c[n] - upd_o[n])))
+        assert err <= 1e-4 * top, (n, err, top)
+        assert close(m.param_array(n), new_o[n], 1e-5), n
+    for li, b in enumerate(m.blocks):
+        assert close(m.read(b["rm"], b["cout"]), stats_o[li][0], 1e-4)
+        assert close(m.read(b["rv"], b["cout"]), stats_o[li][1], 1e-4)
+    m.close()
+
+
+def test_vgg_graph_replay_matches_eager(cuda_rt):
+    from tpcuda.vgg import VGG11BN
+    rng = np.random.default_rng(9)
+    x = rng.standard_normal((8, 3, 32, 32)).astype(np.float32)
+    y = rng.integers(0, 10, 8).astype(np.float32)
+    a, b = VGG11BN(cuda_rt, 8, seed=5), VGG11BN(cuda_rt, 8, seed=5)
+    for mdl in (a, b):
+        mdl._h2d(mdl.x, x)
+        mdl._h2d(mdl.y, y)
+    for _ in range(3):
+        a.step_eager()
+    b.capture()  # runs one eager step, then records (does not run) the step
+    b.step()     # steps two and three replay the graph
+    b.step()
+    cuda_rt.synchronize()
+    assert a.read_loss() == b.read_loss()
+    for n, _, _ in a.param_specs:
+        assert np.array_equal(a.param_array(n), b.param_array(n)), n
+    a.close()
+    b.close()
+
+
+def test_vgg_loss_decreases(cuda_rt):
+    from tpcuda.vgg import VGG11BN
+    rng = np.random.default_rng(11)
+    m = VGG11BN(cuda_rt, 32, seed=1, lr=0.02)
+    m._h2d(m.x, rng.standard_normal((32, 3, 32, 32)).astype(np.float32))
+    m._h2d(m.y, rng.integers(0, 10, 32).astype(np.float32))
+    losses = []
+    for _ in range(8):
+        m.step_eager()
+        losses.append(m.read_loss())
+    assert losses[-1] < losses[0] * 0.7, losses
+    m.close()

@@ -147,6 +147,13 @@ SIGNATURES: dict[str, list] = {
     "tpk_cross_entropy_mean": [P, P, P, P, I64, I64],
     "tpk_cross_entropy_backward": [P, P, P, I64, I64, F32],
     "tpk_fill": [P, I64, F32],
+    "tp_comm_unique_id": [ctypes.c_char_p, INT],
+    "tp_comm_init": [INT, INT, ctypes.c_char_p, INT],
+    "tp_comm_allreduce_async": [P, I64],
+    "tp_comm_wait": [],
+    "tp_comm_sync": [INT],
+    "tp_comm_destroy": [],
+    "tp_comm_info": [ctypes.POINTER(INT), ctypes.POINTER(INT)],
     "tp_graph_begin": [],
     "tp_graph_end": [I64P],
     "tp_graph_launch": [I64],
