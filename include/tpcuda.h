@@ -212,6 +212,13 @@ TP_API int tp_conv2d_weight_backward(int64_t grad_out, int64_t input, const int6
 /* convOps.ts:157-198 conv2dBiasBackward (conv_backward.wgsl:103-119) */
 TP_API int tp_conv2d_bias_backward(int64_t grad_out, int64_t out_ch, const int64_t* grad_out_shape, tp_handle* out);
 
+/* contraction engine: 0 = tcgen05 tensor cores with the 3xTF32 split (default
+ * where M >= 64), 1 = the CUDA-core fp32 kernel everywhere (cross-check) */
+TP_API int tp_set_gemm_path(int path);
+/* synchronises, then reports the tensor-core kernel's status word: 0 = ok,
+ * else the code of a bounded wait that expired; reset != 0 clears it */
+TP_API int tp_gemm_status(int* out, int reset);
+
 /* ---- pooling (poolingOps.ts:18-48, max_pool2d.wgsl:22-49) ------------------------ */
 TP_API int tp_max_pool2d(int64_t input, const int64_t* kernel, int nk, const int64_t* stride, int ns,
                          const int64_t* padding, int np, const int64_t* dilation, int nd, tp_handle* out);

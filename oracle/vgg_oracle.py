@@ -66,3 +66,49 @@ def oracle_step(orc, model, params, x, y, bn_stats, lr, mom, wd):
     stats = [(np.asarray(orc.toList(r["rm"]), np.float32), np.asarray(orc.toList(r["rv"]), np.float32))
              for r in saved]
     return loss, new, stats
+
+
+def oracle_backward(orc, model, params, x, y, saved, logits):
+    """The backward of the same step on the oracle, driven by forward state
+    taken from the device run (teacher forcing): per block the conv output z,
+    the BN+ReLU output a, the pool argmax indices, the batch mean / inv_std,
+    and the logits.  ReLU masks and max-pool routing are then the device's own
+    decisions, so near-ties cannot send a gradient down a different path; what
+    remains to compare is the arithmetic of every backward op.
+    Returns {parameter name: gradient array}."""
+    B = x.shape[0]
+
+    def T(a, shape=None):
+        a = np.ascontiguousarray(a, np.float32)
+        return orc.tensorFromData(a.ravel().tolist(), list(shape or a.shape), "float32")["id"]
+
+    P = {k: T(v, s) for k, (v, s) in params.items()}
+    yt = T(y)
+    lg = T(logits, [B, 10])
+    last = model.blocks[-1]
+    feat = T(saved[-1]["p"], [B, 512])
+    one = T(np.ones(1))
+    dlog = orc.crossEntropyBackward(one, lg, yt, "mean")["id"]
+    G = {"fc.w": orc.matmul(orc.transpose2d(dlog)["id"], feat)["id"], "fc.b": orc.sumDim(dlog, 0, False)["id"]}
+    g = orc.reshape(orc.matmul(dlog, P["fc.w"])["id"], [B, 512, 1, 1])["id"]
+    zero = T(np.zeros(1))
+    for li in reversed(range(len(model.blocks))):
+        b, sv = model.blocks[li], saved[li]
+        C, H, W = b["cout"], b["H"], b["W"]
+        ashape = [B, C, H, W]
+        a = T(sv["a"], ashape)
+        z = T(sv["z"], ashape)
+        if b["pool"]:
+            idx = T(sv["idx"].astype(np.float32), [B, C, H // 2, W // 2])
+            g = orc.maxPool2dBackward(g, idx, ashape, [2], [2], [0], [1])["id"]
+        g = orc.mul(g, orc.gt(a, zero)["id"])["id"]
+        dz, dgm, dbt = [r["id"] for r in orc.batchNormBackward(g, z, P[f"bn{li}.g"], T(sv["mean"]),
+                                                                T(sv["invstd"]))]
+        G[f"bn{li}.g"], G[f"bn{li}.b"] = dgm, dbt
+        G[f"conv{li}.b"] = orc.conv2dBiasBackward(dz, C, ashape)["id"]
+        xshape = [B, b["cin"], H, W]
+        xin = T(x) if li == 0 else T(saved[li - 1]["out"], xshape)
+        G[f"conv{li}.w"] = orc.conv2dWeightBackward(dz, xin, [C, b["cin"], 3, 3], ashape, xshape, [1], [1])["id"]
+        if li > 0:
+            g = orc.conv2dInputBackward(dz, P[f"conv{li}.w"], xshape, ashape, [1], [1])["id"]
+    return {n: np.asarray(orc.toList(G[n]), np.float32) for n in params}

@@ -10,7 +10,7 @@ import math
 import numpy as np
 import pytest
 
-from vgg_oracle import oracle_step
+from vgg_oracle import oracle_backward, oracle_step
 
 pytestmark = pytest.mark.gpu
 
@@ -22,8 +22,30 @@ def close(a, b, rel=1e-4):
     return float(np.max(np.abs(a - b))) <= rel * scale
 
 
+def device_forward_state(m):
+    """Per-block forward tensors of the last device step (for teacher forcing)."""
+    import ctypes
+    out = []
+    for b in m.blocks:
+        n = m.B * b["cout"] * b["H"] * b["W"]
+        sv = {"z": m.read(b["z"], n), "a": m.read(b["a"], n), "mean": m.read(b["mean"], b["cout"]),
+              "invstd": m.read(b["invstd"], b["cout"])}
+        if b["pool"]:
+            raw = np.zeros(n // 4, np.int32)
+            assert m.lib.tp_memcpy_d2h(raw.ctypes.data_as(ctypes.c_void_p), ctypes.c_void_p(b["idx"]),
+                                       raw.nbytes) == 0
+            sv["idx"] = raw
+            sv["p"] = m.read(b["p"], n // 4)
+        sv["out"] = sv["p"] if b["pool"] else sv["a"]
+        out.append(sv)
+    return out
+
+
 @pytest.mark.parametrize("batch", [4, 16])
 def test_vgg_step_matches_oracle_composition(cuda_rt, oracle_rt, batch):
+    """Forward (activations, loss, running stats) against the oracle's own
+    forward; backward against the oracle backward driven by the device's
+    forward state; then the SGD update (bit-exact given the gradients)."""
     from tpcuda.vgg import VGG11BN
     m = VGG11BN(cuda_rt, batch, seed=3)
     rng = np.random.default_rng(7)
@@ -35,22 +57,32 @@ def test_vgg_step_matches_oracle_composition(cuda_rt, oracle_rt, batch):
     stats = [(m.read(b["rm"], b["cout"]), m.read(b["rv"], b["cout"])) for b in m.blocks]
     loss_o, new_o, stats_o = oracle_step(oracle_rt, m, params, x, y, stats, m.lr, m.momentum, m.wd)
     m.step_eager()
+    # forward: loss and BN running statistics
     loss_c = m.read_loss()
     assert math.isclose(loss_c, loss_o, rel_tol=1e-5), (loss_c, loss_o)
-    # the update moves each parameter by lr * (grad + wd * p); compare the
-    # update itself, relative to the largest update of the step (a conv bias
-    # feeding a BN has a gradient that is zero up to rounding, so a per-tensor
-    # relative bound would compare rounding noise)
-    upd_c = {n: m.param_array(n) - params[n][0] for n in params}
-    upd_o = {n: new_o[n] - params[n][0] for n in params}
-    top = max(float(np.max(np.abs(u))) for u in upd_o.values())
-    for n in params:
-        err = float(np.max(np.abs(upd_c[n] - upd_o[n])))
-        assert err <= 1e-4 * top, (n, err, top)
-        assert close(m.param_array(n), new_o[n], 1e-5), n
     for li, b in enumerate(m.blocks):
         assert close(m.read(b["rm"], b["cout"]), stats_o[li][0], 1e-4)
         assert close(m.read(b["rv"], b["cout"]), stats_o[li][1], 1e-4)
+    # backward, teacher-forced: every gradient within 1e-4 of its tensor's scale
+    saved = device_forward_state(m)
+    logits = m.read(m.logits, batch * 10)
+    grads_o = oracle_backward(oracle_rt, m, params, x, y, saved, logits)
+    for n in params:
+        o, k = m.offsets[n]
+        g_c = m.read(m.grads + 4 * o, k)
+        if n.startswith("conv") and n.endswith(".b"):
+            # a conv bias feeding a BN has a gradient that is zero up to rounding
+            assert float(np.max(np.abs(g_c - grads_o[n]))) <= 1e-6 * max(1.0, float(np.max(np.abs(g_c)))), n
+        else:
+            assert close(g_c, grads_o[n], 1e-4), (n, float(np.max(np.abs(g_c - grads_o[n]))),
+                                                  float(np.max(np.abs(grads_o[n]))))
+    # update: param - lr * (grad + wd * param) with the momentum buffer starting at 0
+    for n in params:
+        o, k = m.offsets[n]
+        g_c = m.read(m.grads + 4 * o, k)
+        p0 = params[n][0]
+        want = p0 - np.float32(m.lr) * (g_c + np.float32(m.wd) * p0)
+        assert close(m.param_array(n), want, 1e-6), n
     m.close()
 
 

@@ -14,8 +14,39 @@
 #include "tp_launch.h"
 #include "tp_gemm.cuh"
 #include "tp_gemm_simt.cuh"
+#include "tp_gemm_tc.cuh"
 
 namespace tp {
+
+// 0: tensor cores (tcgen05, 3xTF32) where the shape allows; 1: CUDA cores only.
+static int g_gemm_path = 0;
+
+int tc_status(bool reset) {
+  int v = 0;
+  TP_CUDA(cudaMemcpyFromSymbol(&v, tc::g_status, sizeof(int)));
+  if (reset && v) {
+    int z = 0;
+    TP_CUDA(cudaMemcpyToSymbol(tc::g_status, &z, sizeof(int)));
+  }
+  return v;
+}
+
+// Tensor-core kernel with the N tile following N (K > 0).
+template <class LA, class LB, class EP>
+void gemm_tc(const LA& la, const LB& lb, const EP& ep, int64_t M, int64_t N, int64_t K, int batch) {
+  if (M == 0 || N == 0 || batch == 0) return;
+  if (N <= 32) gemm_tc_launch<LA, LB, EP, 32, 4>(la, lb, ep, M, N, K, batch);
+  else if (N <= 64) gemm_tc_launch<LA, LB, EP, 64, 4>(la, lb, ep, M, N, K, batch);
+  else gemm_tc_launch<LA, LB, EP, 128, 3>(la, lb, ep, M, N, K, batch);
+}
+
+// Tensor-core path for M >= 64 with K > 0, else the CUDA-core kernel.
+template <class LA, class LB, class EP>
+void gemm_auto(const LA& la, const LB& lb, const EP& ep, int64_t M, int64_t N, int64_t K, int batch) {
+  if (M == 0 || N == 0 || batch == 0) return;
+  if (g_gemm_path == 1 || K == 0 || M < 64) gemm_simt(la, lb, ep, M, N, K, batch);
+  else gemm_tc(la, lb, ep, M, N, K, batch);
+}
 
 // ---- per-channel sum of an NCHW tensor (conv_backward.wgsl:103-119) ---------------
 __global__ void k_channel_sum_part(const float* __restrict__ x, int64_t N, int64_t C, int64_t P, int splits,
@@ -84,27 +115,80 @@ ConvShape conv_shape(int64_t N, int64_t Cin, int64_t H, int64_t W, int64_t Cout,
   return s;
 }
 
+// Repack filters for the filter-major K order k = (kh, kw, c):
+//   mode 0 (forward):  wp[o][tap][c] = w[o][c][tap]             (o < Cout, c < icpg)
+//   mode 1 (dgrad):    wp[i][tap][o] = w[o][i][KHW-1-tap]        (flipped, in/out swapped)
+__global__ void k_pack_filters(const float* __restrict__ w, float* __restrict__ wp, int64_t Cout, int64_t Cin_pg,
+                               int khw, int mode) {
+  int64_t total = Cout * Cin_pg * khw;
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
+    int tap = (int)(i % khw);
+    int64_t t = i / khw;
+    int64_t c = t % Cin_pg, o = t / Cin_pg;  // w index i = (o*Cin_pg + c)*khw + tap
+    float v = w[i];
+    if (mode == 0) wp[(o * khw + tap) * Cin_pg + c] = v;
+    else wp[(c * khw + (khw - 1 - tap)) * Cout + o] = v;
+  }
+}
+
+static bool tc_ok(int64_t M) { return g_gemm_path == 0 && M >= 64; }
+
 void conv_fwd(const ConvShape& s, const float* x, const float* w, const float* bias, float* y) {
   int groups = (int)(s.Cin / s.icpg);
-  LdConvIm2col la{x, s};
-  LdConvWeight lb{w, (int64_t)s.icpg * s.KH * s.KW, s.ocpg};
+  int khw = s.KH * s.KW;
+  int64_t M = s.N * s.OH * s.OW, K = (int64_t)s.icpg * khw;
   EpNCHW ep{y, bias, s.Cout, s.OH * s.OW, s.ocpg};
-  gemm_simt(la, lb, ep, s.N * s.OH * s.OW, s.ocpg, (int64_t)s.icpg * s.KH * s.KW, groups);
+  if (tc_ok(M) && s.icpg % 32 == 0) {
+    // filter-major K: each 32-wide k-block is one tap x 32 channels
+    float* wp = (float*)scratch2((size_t)s.Cout * K * sizeof(float));
+    TP_LAUNCH(k_pack_filters, grid_for(s.Cout * K, 256), 256, 0, w, wp, s.Cout, (int64_t)s.icpg, khw, 0);
+    LdConvFM la{x, s.Cin, s.icpg, s.H, s.W, s.OH, s.OW, s.KW, s.SH, s.SW, s.PH, s.PW};
+    LdRowMajor lb{wp, K, (int64_t)s.ocpg * K};
+    gemm_tc(la, lb, ep, M, s.ocpg, K, groups);
+    return;
+  }
+  LdConvIm2col la{x, s};
+  LdConvWeight lb{w, K, s.ocpg};
+  gemm_auto(la, lb, ep, M, s.ocpg, K, groups);
 }
 
 void conv_dgrad(const ConvShape& s, const float* dy, const float* w, float* dx) {
+  int khw = s.KH * s.KW;
+  int64_t M = s.N * s.H * s.W, K = s.Cout * khw;
+  EpNCHW ep{dx, nullptr, s.Cin, s.H * s.W, (int)s.Cin};
+  if (tc_ok(M) && s.SH == 1 && s.SW == 1 && s.Cout % 32 == 0 && s.PH <= s.KH - 1 && s.PW <= s.KW - 1 &&
+      s.OH == s.H + 2 * s.PH - s.KH + 1 && s.OW == s.W + 2 * s.PW - s.KW + 1) {
+    // stride 1: dx = forward convolution of dy with the flipped, transposed
+    // filters and padding K-1-P
+    float* wp = (float*)scratch2((size_t)s.Cin * K * sizeof(float));
+    TP_LAUNCH(k_pack_filters, grid_for(s.Cout * s.Cin * khw, 256), 256, 0, w, wp, s.Cout, s.Cin, khw, 1);
+    LdConvFM la{dy, s.Cout, (int)s.Cout, s.OH, s.OW, s.H, s.W, s.KW, 1, 1, s.KH - 1 - s.PH, s.KW - 1 - s.PW};
+    LdRowMajor lb{wp, K, 0};
+    gemm_tc(la, lb, ep, M, s.Cin, K, 1);
+    return;
+  }
   LdConvDgradA la{dy, s};
   LdConvDgradB lb{w, s};
-  EpNCHW ep{dx, nullptr, s.Cin, s.H * s.W, (int)s.Cin};
-  gemm_simt(la, lb, ep, s.N * s.H * s.W, s.Cin, s.Cout * s.KH * s.KW, 1);
+  gemm_auto(la, lb, ep, M, s.Cin, K, 1);
 }
 
 void conv_wgrad(const ConvShape& s, const float* dy, const float* x, float* dw) {
+  int khw = s.KH * s.KW;
+  int64_t K = s.N * s.OH * s.OW;
+  if (tc_ok(s.Cout) && s.icpg == s.Cin) {
+    // one GEMM per filter tap (batch index): C_tap[oc][ic] = sum_(n,p) dy . x shifted
+    LdWgradTapDy la{dy, s.Cout, s.OH * s.OW};
+    LdWgradTapX lb{x, s.Cin, s.H, s.W, s.OH, s.OW, s.KW, s.SH, s.SW, s.PH, s.PW};
+    EpWgradTap ep{dw, s.Cin, khw};
+    gemm_tc(la, lb, ep, s.Cout, s.Cin, K, khw);
+    return;
+  }
   LdConvWgradA la{dy, s};
   LdConvWgradB lb{x, s};
-  int64_t R = s.Cin * s.KH * s.KW;
+  int64_t R = s.Cin * khw;
   EpRowMajor ep{dw, R, 0, nullptr, 0};
-  gemm_simt(la, lb, ep, s.Cout, R, s.N * s.OH * s.OW, 1);
+  gemm_auto(la, lb, ep, s.Cout, R, K, 1);
 }
 
 // matmul.wgsl semantics: C[b] = A[b] (M x K) . B[b or shared] (K x N), row-major.
@@ -114,7 +198,7 @@ void matmul_launch(const float* A, const float* B, float* C, int64_t batch, int6
   LdColMajor lb{B, N, b_batched ? K * N : 0};
   EpRowMajor ep{C, N, M * N, nullptr, 0};
   TP_REQUIRE(batch <= 65535, "matmul: batch exceeds the grid limit");
-  gemm_simt(la, lb, ep, M, N, K, (int)batch);
+  gemm_auto(la, lb, ep, M, N, K, (int)batch);
 }
 
 // y[M, N] = x[M, K] . W[N, K]^T (+ bias[N]) (+ ReLU): nn.Linear without the
@@ -124,16 +208,16 @@ void linear_launch(const float* x, const float* w, const float* bias, float* y, 
   LdRowMajor la{x, K, 0};
   LdRowMajor lb{w, K, 0};
   EpRowMajor ep{y, N, 0, bias, relu ? 1 : 0};
-  gemm_simt(la, lb, ep, M, N, K, 1);
+  gemm_auto(la, lb, ep, M, N, K, 1);
 }
 
 void gemm_launch(const float* A, bool a_t, const float* B, bool b_t, float* C, int64_t M, int64_t N, int64_t K,
                  const float* bias) {
   EpRowMajor ep{C, N, 0, bias, 0};
-  if (!a_t && b_t) gemm_simt(LdRowMajor{A, K, 0}, LdRowMajor{B, K, 0}, ep, M, N, K, 1);
-  else if (!a_t && !b_t) gemm_simt(LdRowMajor{A, K, 0}, LdColMajor{B, N, 0}, ep, M, N, K, 1);
-  else if (a_t && b_t) gemm_simt(LdColMajor{A, M, 0}, LdRowMajor{B, K, 0}, ep, M, N, K, 1);
-  else gemm_simt(LdColMajor{A, M, 0}, LdColMajor{B, N, 0}, ep, M, N, K, 1);
+  if (!a_t && b_t) gemm_auto(LdRowMajor{A, K, 0}, LdRowMajor{B, K, 0}, ep, M, N, K, 1);
+  else if (!a_t && !b_t) gemm_auto(LdRowMajor{A, K, 0}, LdColMajor{B, N, 0}, ep, M, N, K, 1);
+  else if (a_t && b_t) gemm_auto(LdColMajor{A, M, 0}, LdRowMajor{B, K, 0}, ep, M, N, K, 1);
+  else gemm_auto(LdColMajor{A, M, 0}, LdColMajor{B, N, 0}, ep, M, N, K, 1);
 }
 
 static int at(const int64_t* v, int n, int i, int dflt) { return n > i ? (int)v[i] : (n > 0 ? (int)v[0] : dflt); }
@@ -143,6 +227,20 @@ static int at(const int64_t* v, int n, int i, int dflt) { return n > i ? (int)v[
 using namespace tp;
 
 extern "C" {
+
+TP_API int tp_set_gemm_path(int path) {
+  return guard([&] {
+    TP_REQUIRE(path == 0 || path == 1, "gemm path must be 0 (tensor cores) or 1 (CUDA cores)");
+    g_gemm_path = path;
+  });
+}
+
+TP_API int tp_gemm_status(int* out, int reset) {
+  return guard([&] {
+    TP_CUDA(cudaStreamSynchronize(stream()));
+    *out = tc_status(reset != 0);
+  });
+}
 
 TP_API int tp_matmul(int64_t a, int64_t b, tp_handle* out) {
   return guard([&] {

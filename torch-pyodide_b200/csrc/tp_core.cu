@@ -93,6 +93,19 @@ void* scratch(size_t bytes) {
   return g_scratch;
 }
 
+static void* g_scratch2 = nullptr;
+static size_t g_scratch2_bytes = 0;
+
+void* scratch2(size_t bytes) {
+  if (bytes > g_scratch2_bytes) {
+    if (g_scratch2) dfree(g_scratch2);
+    size_t nb = bytes < (1u << 20) ? (1u << 20) : bytes;
+    g_scratch2 = dalloc(nb);
+    g_scratch2_bytes = nb;
+  }
+  return g_scratch2;
+}
+
 int64_t prod(const int64_t* s, int n) {
   int64_t r = 1;
   for (int i = 0; i < n; ++i) r *= s[i];

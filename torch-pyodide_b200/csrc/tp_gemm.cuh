@@ -4,11 +4,21 @@
 // Every contraction on the hot path is C[m, n] = sum_k A(m, k) * B(n, k) where
 // A and B are *gathered* from a tensor: a dense matrix in either layout, or an
 // im2col view of an NCHW activation (forward and data-gradient) or of the
-// (activation, output-gradient) pair (weight-gradient).  Loader functors give
-// A(b, m, k) / B(b, n, k) (b = batch or conv group) and report which index is
-// contiguous in memory; epilogue functors place C(b, m, n) (row-major matrix,
-// NCHW plane with bias, ...).  The tcgen05 kernel and the CUDA-core kernel use
-// the same functors.
+// (activation, output-gradient) pair (weight-gradient).  Nothing is
+// materialised: im2col, transposes and flipped filters exist only as index
+// maps.  b = batch index (matmul batch, conv group, or filter tap).
+//
+// A loader gives element access three ways:
+//   operator()(b, r, k)            any element (CUDA-core kernel);
+//   row(b, r, rows) + fill(row, k0, kend, v[32])
+//                                  for loaders contiguous along r: one thread
+//                                  per tile row gathers 32 consecutive k with
+//                                  the row's index math hoisted (kContigK false);
+//   kctx(b, k, kend) + at(b, r, kctx)
+//                                  for loaders contiguous along k: lane = k,
+//                                  the k decomposition is done once per lane
+//                                  and each row costs one load (kContigK true).
+// Epilogue functors place C(b, m, n).
 #pragma once
 
 #include <cuda_runtime.h>
@@ -16,21 +26,39 @@
 
 namespace tp {
 
-// ---- loaders -------------------------------------------------------------------------------
-// Dense row-major [rows, K] (leading dim ld): contiguous along k.
+constexpr int GB_K = 32;  // k values per producer block
+
+// ---- dense matrices ----------------------------------------------------------------------
+// Row-major [rows, K] (leading dim ld, batch stride bs): contiguous along k.
 struct LdRowMajor {
   const float* p;
   int64_t ld, bs;
   static constexpr bool kContigK = true;
   __device__ __forceinline__ float operator()(int b, int64_t r, int64_t k) const { return p[b * bs + r * ld + k]; }
+  struct Kc {
+    int64_t off;
+    bool ok;
+  };
+  __device__ __forceinline__ Kc kctx(int b, int64_t k, int64_t kend) const { return Kc{b * bs + k, k < kend}; }
+  __device__ __forceinline__ float at(int, int64_t r, const Kc& c) const { return c.ok ? p[c.off + r * ld] : 0.0f; }
 };
 
-// Dense column-major view: element (r, k) at p[k*ld + r]: contiguous along r.
+// Column-major view: element (r, k) at p[k*ld + r]: contiguous along r.
 struct LdColMajor {
   const float* p;
   int64_t ld, bs;
   static constexpr bool kContigK = false;
   __device__ __forceinline__ float operator()(int b, int64_t r, int64_t k) const { return p[b * bs + k * ld + r]; }
+  struct Row {
+    const float* q;
+    bool ok;
+  };
+  __device__ __forceinline__ Row row(int b, int64_t r, int64_t rows) const { return Row{p + b * bs + r, r < rows}; }
+  __device__ __forceinline__ void fill(const Row& w, int64_t k0, int64_t kend, float (&v)[GB_K]) const {
+    const float* q = w.q + k0 * ld;
+#pragma unroll
+    for (int j = 0; j < GB_K; ++j) v[j] = (w.ok && k0 + j < kend) ? q[j * ld] : 0.0f;
+  }
 };
 
 struct ConvShape {
@@ -39,6 +67,7 @@ struct ConvShape {
   int icpg, ocpg;  // channels per group
 };
 
+// ---- convolution, reference K order k = (ic, kh, kw) (any shape) ---------------------------
 // Forward A: m = (n, oh, ow), k = (ic_in_group, kh, kw) -> x[n, g*icpg+ic, ih, iw]
 // (conv.wgsl:35-54 taps, zero outside the image).  Contiguous along m.
 struct LdConvIm2col {
@@ -55,6 +84,42 @@ struct LdConvIm2col {
     if (ih < 0 || ih >= s.H || iw < 0 || iw >= s.W) return 0.0f;
     return x[((n * s.Cin + ic) * s.H + ih) * s.W + iw];
   }
+  struct Row {
+    const float* q;  // x at (n, group channel 0, 0, 0)
+    int ih0, iw0;
+    bool ok;
+  };
+  __device__ __forceinline__ Row row(int g, int64_t m, int64_t rows) const {
+    Row w;
+    w.ok = m < rows;
+    int64_t mm = w.ok ? m : 0;
+    int ow = (int)(mm % s.OW);
+    int64_t t = mm / s.OW;
+    int oh = (int)(t % s.OH);
+    int64_t n = t / s.OH;
+    w.q = x + (n * s.Cin + (int64_t)g * s.icpg) * s.H * s.W;
+    w.ih0 = oh * s.SH - s.PH;
+    w.iw0 = ow * s.SW - s.PW;
+    return w;
+  }
+  __device__ __forceinline__ void fill(const Row& w, int64_t k0, int64_t kend, float (&v)[GB_K]) const {
+    int khw = s.KH * s.KW;
+    int ic = (int)(k0 / khw), tap = (int)(k0 - (int64_t)ic * khw);
+    int kh = tap / s.KW, kw = tap - kh * s.KW;
+#pragma unroll
+    for (int j = 0; j < GB_K; ++j) {
+      int ih = w.ih0 + kh, iw = w.iw0 + kw;
+      bool in = w.ok && k0 + j < kend && ih >= 0 && ih < s.H && iw >= 0 && iw < s.W;
+      v[j] = in ? w.q[((int64_t)ic * s.H + ih) * s.W + iw] : 0.0f;
+      if (++kw == s.KW) {
+        kw = 0;
+        if (++kh == s.KH) {
+          kh = 0;
+          ++ic;
+        }
+      }
+    }
+  }
 };
 
 // Forward B: weights [Cout, icpg*KH*KW], row n = output channel (of group g).
@@ -66,9 +131,62 @@ struct LdConvWeight {
   __device__ __forceinline__ float operator()(int g, int64_t n, int64_t k) const {
     return w[((int64_t)g * ocpg + n) * K + k];
   }
+  struct Kc {
+    int64_t off;
+    bool ok;
+  };
+  __device__ __forceinline__ Kc kctx(int g, int64_t k, int64_t kend) const {
+    return Kc{(int64_t)g * ocpg * K + k, k < kend};
+  }
+  __device__ __forceinline__ float at(int, int64_t n, const Kc& c) const { return c.ok ? w[c.off + n * K] : 0.0f; }
 };
 
-// Data-gradient A: m = (n, ih, iw), k = (oc, kh, kw) -> dy[n, oc, oh, ow] where
+// ---- convolution, filter-major K order k = (kh, kw, c) with C % 32 == 0 ---------------------
+// A 32-wide k-block then covers one tap and 32 consecutive channels: one
+// bounds check per row per block and a strided load per element.  Used for
+// the forward (input x, channels icpg) and for the stride-1 data gradient
+// written as a forward convolution of dy with flipped, transposed filters
+// (input dy, channels Cout, padding K-1-P).  B is the filter repacked to
+// [out][kh][kw][c] (k_pack_filters).
+struct LdConvFM {
+  const float* x;
+  int64_t Ctot;      // channels of the input tensor
+  int C;             // channels per group (multiple of 32)
+  int64_t H, W, OH, OW;
+  int KW, SH, SW, PH, PW;
+  static constexpr bool kContigK = false;
+  struct Row {
+    const float* q;
+    int ih0, iw0;
+    bool ok;
+  };
+  __device__ __forceinline__ Row row(int g, int64_t m, int64_t rows) const {
+    Row w;
+    w.ok = m < rows;
+    int64_t mm = w.ok ? m : 0;
+    int ow = (int)(mm % OW);
+    int64_t t = mm / OW;
+    int oh = (int)(t % OH);
+    int64_t n = t / OH;
+    w.q = x + (n * Ctot + (int64_t)g * C) * H * W;
+    w.ih0 = oh * SH - PH;
+    w.iw0 = ow * SW - PW;
+    return w;
+  }
+  __device__ __forceinline__ void fill(const Row& w, int64_t k0, int64_t kend, float (&v)[GB_K]) const {
+    int tap = (int)(k0 / C), c0 = (int)(k0 - (int64_t)tap * C);
+    int kh = tap / KW, kw = tap - kh * KW;
+    int ih = w.ih0 + kh, iw = w.iw0 + kw;
+    bool in = w.ok && k0 < kend && ih >= 0 && ih < H && iw >= 0 && iw < W;
+    const int64_t hw = H * W;
+    const float* q = w.q + (int64_t)c0 * hw + (int64_t)ih * W + iw;
+#pragma unroll
+    for (int j = 0; j < GB_K; ++j) v[j] = in ? q[j * hw] : 0.0f;
+  }
+};
+
+// ---- data gradient, general stride --------------------------------------------------------
+// A: m = (n, ih, iw), k = (oc, kh, kw) -> dy[n, oc, oh, ow] where
 // ih + PH - kh = oh*SH and iw + PW - kw = ow*SW (conv_backward.wgsl:24-61).
 struct LdConvDgradA {
   const float* dy;
@@ -86,9 +204,18 @@ struct LdConvDgradA {
     if (oh >= s.OH || ow >= s.OW) return 0.0f;
     return dy[((n * s.Cout + oc) * s.OH + oh) * s.OW + ow];
   }
+  struct Row {
+    int64_t m;
+    bool ok;
+  };
+  __device__ __forceinline__ Row row(int, int64_t m, int64_t rows) const { return Row{m, m < rows}; }
+  __device__ __forceinline__ void fill(const Row& w, int64_t k0, int64_t kend, float (&v)[GB_K]) const {
+#pragma unroll 4
+    for (int j = 0; j < GB_K; ++j) v[j] = (w.ok && k0 + j < kend) ? (*this)(0, w.m, k0 + j) : 0.0f;
+  }
 };
 
-// Data-gradient B: row n = input channel ic, k = (oc, kh, kw) -> w[oc, ic, kh, kw].
+// B: row n = input channel ic, k = (oc, kh, kw) -> w[oc, ic, kh, kw].
 struct LdConvDgradB {
   const float* w;
   ConvShape s;
@@ -97,9 +224,23 @@ struct LdConvDgradB {
     int64_t khw = k % ((int64_t)s.KH * s.KW), oc = k / ((int64_t)s.KH * s.KW);
     return w[(oc * s.Cin + ic) * s.KH * s.KW + khw];
   }
+  struct Kc {
+    int64_t off;
+    bool ok;
+  };
+  __device__ __forceinline__ Kc kctx(int, int64_t k, int64_t kend) const {
+    int64_t kk = (int64_t)s.KH * s.KW;
+    int64_t oc = k / kk;
+    return Kc{oc * s.Cin * kk + (k - oc * kk), k < kend};
+  }
+  __device__ __forceinline__ float at(int, int64_t ic, const Kc& c) const {
+    return c.ok ? w[c.off + ic * s.KH * s.KW] : 0.0f;
+  }
 };
 
-// Weight-gradient A: row m = oc, k = (n, oh, ow) -> dy[n, oc, oh, ow].
+// ---- weight gradient ------------------------------------------------------------------------
+// Reference K order (CUDA-core path): row m = oc, k = (n, oh, ow) -> dy[n, oc, oh, ow];
+// row n = (ic, kh, kw), k = (n, oh, ow) -> x[n, ic, ih, iw] (conv_backward.wgsl:66-101).
 struct LdConvWgradA {
   const float* dy;
   ConvShape s;
@@ -108,10 +249,20 @@ struct LdConvWgradA {
     int64_t p = k % (s.OH * s.OW), n = k / (s.OH * s.OW);
     return dy[(n * s.Cout + oc) * s.OH * s.OW + p];
   }
+  struct Kc {
+    int64_t off;
+    bool ok;
+  };
+  __device__ __forceinline__ Kc kctx(int, int64_t k, int64_t kend) const {
+    int64_t P = s.OH * s.OW;
+    int64_t n = k / P;
+    return Kc{n * s.Cout * P + (k - n * P), k < kend};
+  }
+  __device__ __forceinline__ float at(int, int64_t oc, const Kc& c) const {
+    return c.ok ? dy[c.off + oc * s.OH * s.OW] : 0.0f;
+  }
 };
 
-// Weight-gradient B: row n = (ic, kh, kw), k = (n, oh, ow) -> x[n, ic, ih, iw]
-// (conv_backward.wgsl:66-101 taps).
 struct LdConvWgradB {
   const float* x;
   ConvShape s;
@@ -125,6 +276,52 @@ struct LdConvWgradB {
     int64_t ih = oh * s.SH + kh - s.PH, iw = ow * s.SW + kw - s.PW;
     if (ih < 0 || ih >= s.H || iw < 0 || iw >= s.W) return 0.0f;
     return x[((n * s.Cin + ic) * s.H + ih) * s.W + iw];
+  }
+  struct Kc {
+    int64_t k;
+    bool ok;
+  };
+  __device__ __forceinline__ Kc kctx(int, int64_t k, int64_t kend) const { return Kc{k, k < kend}; }
+  __device__ __forceinline__ float at(int b, int64_t r, const Kc& c) const { return c.ok ? (*this)(b, r, c.k) : 0.0f; }
+};
+
+// Per-tap weight gradient for the tensor-core path: batch index = tap (kh, kw).
+// A(oc, k = (n, p)) = dy[n, oc, p];  B(ic, k = (n, oh, ow)) = x[n, ic, oh*SH+kh-PH, ow*SW+kw-PW].
+struct LdWgradTapDy {
+  const float* dy;
+  int64_t Cout, P;
+  static constexpr bool kContigK = true;
+  struct Kc {
+    int64_t off;
+    bool ok;
+  };
+  __device__ __forceinline__ Kc kctx(int, int64_t k, int64_t kend) const {
+    int64_t n = k / P;
+    return Kc{n * Cout * P + (k - n * P), k < kend};
+  }
+  __device__ __forceinline__ float at(int, int64_t oc, const Kc& c) const { return c.ok ? dy[c.off + oc * P] : 0.0f; }
+};
+
+struct LdWgradTapX {
+  const float* x;
+  int64_t Cin, H, W, OH, OW;
+  int KW, SH, SW, PH, PW;
+  static constexpr bool kContigK = true;
+  struct Kc {
+    int64_t off;
+    bool ok;
+  };
+  __device__ __forceinline__ Kc kctx(int tap, int64_t k, int64_t kend) const {
+    int kh = tap / KW, kw = tap - kh * KW;
+    int64_t P = OH * OW;
+    int64_t n = k / P, p = k - n * P;
+    int oh = (int)(p / OW), ow = (int)(p - (int64_t)oh * OW);
+    int ih = oh * SH + kh - PH, iw = ow * SW + kw - PW;
+    bool ok = k < kend && ih >= 0 && ih < H && iw >= 0 && iw < W;
+    return Kc{ok ? (n * Cin * H + ih) * W + iw : 0, ok};
+  }
+  __device__ __forceinline__ float at(int, int64_t ic, const Kc& c) const {
+    return c.ok ? x[c.off + ic * H * W] : 0.0f;
   }
 };
 
@@ -153,6 +350,16 @@ struct EpNCHW {
     if (bias) v += bias[c];
     int64_t img = m / P, p = m % P;
     out[(img * C + c) * P + p] = v;
+  }
+};
+
+// Per-tap weight gradient: C_tap[oc][ic] -> dW[oc, ic, tap].
+struct EpWgradTap {
+  float* dw;
+  int64_t Cin;
+  int KHW;
+  __device__ __forceinline__ void operator()(int tap, int64_t oc, int64_t ic, float v) const {
+    dw[(oc * Cin + ic) * KHW + tap] = v;
   }
 };
 

@@ -111,6 +111,8 @@ SIGNATURES: dict[str, list] = {
     "tp_log_softmax_backward": [I64, I64, I64, I64, HP],
     "tp_cross_entropy": [I64, I64, HP],
     "tp_cross_entropy_backward": [I64, I64, I64, INT, HP],
+    "tp_set_gemm_path": [INT],
+    "tp_gemm_status": [ctypes.POINTER(INT), INT],
     "tp_matmul": [I64, I64, HP],
     "tp_linear": [I64, I64, I64, HP],
     "tp_conv2d": [I64, I64, F32P, INT, I64P, INT, I64P, INT, I64P, INT, INT, HP],
