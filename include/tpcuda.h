@@ -322,6 +322,17 @@ TP_API int tpk_gemm(const float* A, int a_t, const float* B, int b_t, float* C, 
  * the mean back to the host, reductionOps.ts:203-212) */
 TP_API int tpk_cross_entropy_mean(const float* logits, const float* targets, float* loss_rows, float* loss_mean,
                                   int64_t B, int64_t C);
+/* No counterpart in the reference.  The same mean cross-entropy as
+ * tpk_cross_entropy_mean for callers that cannot allocate device memory (a
+ * process whose HBM budget is fixed at start-up, a latency-critical loop): the
+ * caller passes only inputs and the one-float output; the per-row losses and
+ * reduction partials live in a fixed device array reserved when the library
+ * loads (about 1 MB per GPU, kept until exit), so B <= 262144 rows, larger B is
+ * rejected with TP_ERR_ARG.  The first call on a device looks up that array's
+ * address; make it before any stream capture.  Calls share the array: calls
+ * that overlap on the GPU race. */
+TP_API int tpk_cross_entropy_mean_noalloc(const float* logits, const float* targets, float* loss_mean, int64_t B,
+                                          int64_t C);
 /* grad = (softmax(logits) - onehot(target)) * scale (cross_entropy_backward.wgsl) */
 TP_API int tpk_cross_entropy_backward(const float* logits, const float* targets, float* grad, int64_t B, int64_t C,
                                       float scale);

@@ -512,6 +512,33 @@ void launch_cross_entropy_bwd(const float* go, int go_scalar, const float* x, co
   TP_LAUNCH(k_cross_entropy_bwd, (unsigned)((B * 32 + 255) / 256), 256, 0, go, go_scalar, x, tgt, gi, B, C, scale);
 }
 
+// ---- allocation-free cross-entropy mean ------------------------------------------------
+// Working memory for tpk_cross_entropy_mean_noalloc, reserved when the library
+// is loaded: the per-row losses, the per-block partial sums of the mean and the
+// last-block ticket.  Every GPU that loads the library keeps this array
+// (about 1 MB) until the process exits.
+constexpr int64_t CE_NOALLOC_MAX_ROWS = 262144;
+constexpr int64_t CE_NOALLOC_FLOATS = CE_NOALLOC_MAX_ROWS + RED_MAX_BLOCKS + 64;
+static __device__ __align__(256) float g_ce_noalloc_scratch[CE_NOALLOC_FLOATS];
+
+// Device address of the array, looked up once per device with that device
+// current (host code cannot use the symbol itself as a device pointer).
+static float* g_ce_noalloc_addr[64] = {};
+
+static float* ce_noalloc_scratch() {
+  int dev = -1;
+  TP_CUDA(cudaGetDevice(&dev));
+  TP_REQUIRE(dev >= 0 && dev < 64, "device ordinal %d out of range", dev);
+  if (!g_ce_noalloc_addr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_ce_noalloc_scratch);
+    if (e != cudaSuccess) fail(TP_ERR_CUDA, "cudaGetSymbolAddress(g_ce_noalloc_scratch) failed: %s",
+                               cudaGetErrorString(e));
+    g_ce_noalloc_addr[dev] = static_cast<float*>(p);
+  }
+  return g_ce_noalloc_addr[dev];
+}
+
 static void split_dims(const Tensor& t, int dim, int64_t& outer, int64_t& red, int64_t& inner) {
   outer = prod(t.shape, dim);
   red = t.shape[dim];
@@ -664,6 +691,38 @@ TP_API int tp_cross_entropy(int64_t input, int64_t targets, tp_handle* out) {
     Tensor o = make(s, 1, x.dtype);
     launch_cross_entropy(x.f(), t.f(), o.f(), B, C);
     emit(o, out);
+  });
+}
+
+// Mean cross-entropy loss of B rows of C logits, for callers that must not
+// allocate device memory: a process that reserves its whole HBM budget at
+// start-up and forbids allocation afterwards, or a latency-critical loop where
+// an allocation could block or fail.  Inputs and the one-float output are the
+// caller's; the per-row losses and reduction partials live in a fixed
+// file-scope device array, so B is limited to CE_NOALLOC_MAX_ROWS.  The first
+// call on a device looks up that array's device address (cudaGetSymbolAddress);
+// make that first call before any stream capture.  All calls share the one
+// array, which keeps the last call's contents: the ticket is cleared before
+// every launch, and calls whose work overlaps on the GPU (other streams,
+// other threads) race on it.  Calls on the library stream are ordered.
+TP_API int tpk_cross_entropy_mean_noalloc(const float* logits, const float* targets, float* loss_mean, int64_t B,
+                                          int64_t C) {
+  return guard([&] {
+    TP_REQUIRE(B >= 1 && B <= CE_NOALLOC_MAX_ROWS,
+               "cross_entropy_mean_noalloc: %lld rows is outside [1, %lld], the size of its fixed work area",
+               (long long)B, (long long)CE_NOALLOC_MAX_ROWS);
+    TP_REQUIRE(C >= 1, "cross_entropy_mean_noalloc: need at least one class");
+    float* base = ce_noalloc_scratch();
+    float* rows = base;
+    float* partials = base + CE_NOALLOC_MAX_ROWS;
+    unsigned int* ticket = reinterpret_cast<unsigned int*>(partials + RED_MAX_BLOCKS);
+    TP_CUDA(cudaMemsetAsync(ticket, 0, sizeof(unsigned int), stream()));
+    TP_LAUNCH(k_cross_entropy, (unsigned)((B * 32 + 255) / 256), 256, 0, logits, targets, rows, B, C);
+    unsigned blocks = grid_for(B, 256, 8);
+    unsigned cap = (unsigned)sm_count() * 4;
+    if (blocks > cap) blocks = cap;
+    if (blocks > RED_MAX_BLOCKS) blocks = RED_MAX_BLOCKS;
+    TP_LAUNCH(k_reduce_all, blocks, 256, 0, rows, B, 1, loss_mean, partials, ticket);
   });
 }
 
