@@ -13,6 +13,27 @@ import numpy as np
 
 def oracle_step(orc, model, params, x, y, bn_stats, lr, mom, wd):
     """One step of the same network on the oracle; returns (loss, new params, running stats)."""
+    loss, G, P, stats = _forward_backward(orc, model, params, x, y, bn_stats)
+    names = list(params)
+    moms = [_tensor(orc, np.zeros(int(np.prod(params[n][1])))) for n in names]
+    orc.sgdStepMulti([P[n] for n in names], [G[n] for n in names], moms, lr, mom, wd, 0.0, False)
+    new = {n: np.asarray(orc.toList(P[n]), np.float32) for n in names}
+    return loss, new, stats
+
+
+def oracle_grads(orc, model, params, x, y, bn_stats):
+    """Forward and backward of the same network on the oracle (free running);
+    returns (loss, {parameter name: gradient array})."""
+    loss, G, _, _ = _forward_backward(orc, model, params, x, y, bn_stats)
+    return loss, {n: np.asarray(orc.toList(G[n]), np.float32) for n in params}
+
+
+def _tensor(orc, a, shape=None):
+    a = np.ascontiguousarray(a, np.float32)
+    return orc.tensorFromData(a.ravel().tolist(), list(shape or a.shape), "float32")["id"]
+
+
+def _forward_backward(orc, model, params, x, y, bn_stats):
     B = x.shape[0]
 
     def T(a, shape=None):
@@ -59,13 +80,9 @@ def oracle_step(orc, model, params, x, y, bn_stats, lr, mom, wd):
         G[f"conv{li}.w"] = orc.conv2dWeightBackward(dz, rec["x"], [C, b["cin"], 3, 3], ashape, xshape, [1], [1])["id"]
         if li > 0:
             g = orc.conv2dInputBackward(dz, P[f"conv{li}.w"], xshape, ashape, [1], [1])["id"]
-    names = list(params)
-    moms = [T(np.zeros(int(np.prod(params[n][1])))) for n in names]
-    orc.sgdStepMulti([P[n] for n in names], [G[n] for n in names], moms, lr, mom, wd, 0.0, False)
-    new = {n: np.asarray(orc.toList(P[n]), np.float32) for n in names}
     stats = [(np.asarray(orc.toList(r["rm"]), np.float32), np.asarray(orc.toList(r["rv"]), np.float32))
              for r in saved]
-    return loss, new, stats
+    return loss, G, P, stats
 
 
 def oracle_backward(orc, model, params, x, y, saved, logits):

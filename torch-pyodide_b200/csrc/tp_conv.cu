@@ -15,6 +15,7 @@
 #include "tp_gemm.cuh"
 #include "tp_gemm_simt.cuh"
 #include "tp_gemm_tc.cuh"
+#include "tp_chanred.cuh"
 
 namespace tp {
 
@@ -49,44 +50,21 @@ void gemm_auto(const LA& la, const LB& lb, const EP& ep, int64_t M, int64_t N, i
 }
 
 // ---- per-channel sum of an NCHW tensor (conv_backward.wgsl:103-119) ---------------
-__global__ void k_channel_sum_part(const float* __restrict__ x, int64_t N, int64_t C, int64_t P, int splits,
-                                   double* __restrict__ part) {
-  __shared__ double sh[32];
-  int64_t c = blockIdx.x;
-  int split = blockIdx.y;
-  int64_t per = (N + splits - 1) / splits;
-  int64_t n0 = split * per, n1 = n0 + per < N ? n0 + per : N;
-  double s = 0.0;
-  for (int64_t n = n0; n < n1; ++n) {
-    const float* p = x + (n * C + c) * P;
-    for (int64_t i = threadIdx.x; i < P; i += blockDim.x) s += p[i];
-  }
-  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  if (lane == 0) sh[w] = s;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    double t = 0.0;
-    for (int k = 0; k < nw; ++k) t += sh[k];
-    part[c * splits + split] = t;
-  }
-}
-
 __global__ void k_channel_sum_finish(const double* __restrict__ part, int64_t C, int splits,
                                      float* __restrict__ out) {
   int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (c >= C) return;
   double s = 0.0;
-  for (int k = 0; k < splits; ++k) s += part[c * splits + k];
+  for (int k = 0; k < splits; ++k) s += part[(c * splits + k) * 2];
   out[c] = (float)s;
 }
 
 void launch_channel_sum(const float* x, int64_t N, int64_t C, int64_t P, float* out) {
   if (C == 0) return;
-  int splits = 1;
-  while (C * splits < (int64_t)sm_count() * 4 && splits * 2 <= N) splits *= 2;
-  double* part = (double*)scratch((size_t)C * splits * sizeof(double));
-  TP_LAUNCH(k_channel_sum_part, dim3((unsigned)C, (unsigned)splits), 256, 0, x, N, C, P, splits, part);
+  int splits = chan_splits(C, N, P, sm_count());
+  double* part = (double*)scratch((size_t)C * splits * 2 * sizeof(double));
+  auto kcs = k_chan_reduce<ChanSumF>;
+  TP_LAUNCH(kcs, dim3((unsigned)C, (unsigned)splits), 256, 0, ChanSumF{x}, N, C, P, splits, part);
   TP_LAUNCH(k_channel_sum_finish, (unsigned)((C + 127) / 128), 128, 0, part, C, splits, out);
 }
 
@@ -176,7 +154,7 @@ void conv_dgrad(const ConvShape& s, const float* dy, const float* w, float* dx) 
 void conv_wgrad(const ConvShape& s, const float* dy, const float* x, float* dw) {
   int khw = s.KH * s.KW;
   int64_t K = s.N * s.OH * s.OW;
-  if (tc_ok(s.Cout) && s.icpg == s.Cin) {
+  if (tc_ok(s.Cout) && s.icpg == s.Cin && s.Cin >= 32) {
     // one GEMM per filter tap (batch index): C_tap[oc][ic] = sum_(n,p) dy . x shifted
     LdWgradTapDy la{dy, s.Cout, s.OH * s.OW};
     LdWgradTapX lb{x, s.Cin, s.H, s.W, s.OH, s.OW, s.KW, s.SH, s.SW, s.PH, s.PW};

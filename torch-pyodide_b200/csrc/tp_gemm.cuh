@@ -277,12 +277,33 @@ struct LdConvWgradB {
     if (ih < 0 || ih >= s.H || iw < 0 || iw >= s.W) return 0.0f;
     return x[((n * s.Cin + ic) * s.H + ih) * s.W + iw];
   }
+  // per lane: the image and output position of k; per row: the tap and channel
   struct Kc {
-    int64_t k;
+    const float* xn;
+    int ih0, iw0;
     bool ok;
   };
-  __device__ __forceinline__ Kc kctx(int, int64_t k, int64_t kend) const { return Kc{k, k < kend}; }
-  __device__ __forceinline__ float at(int b, int64_t r, const Kc& c) const { return c.ok ? (*this)(b, r, c.k) : 0.0f; }
+  __device__ __forceinline__ Kc kctx(int, int64_t k, int64_t kend) const {
+    Kc c;
+    c.ok = k < kend;
+    int64_t kk = c.ok ? k : 0;
+    int64_t P = s.OH * s.OW;
+    int64_t n = kk / P;
+    int p = (int)(kk - n * P);
+    int oh = p / (int)s.OW, ow = p - oh * (int)s.OW;
+    c.xn = x + n * s.Cin * s.H * s.W;
+    c.ih0 = oh * s.SH - s.PH;
+    c.iw0 = ow * s.SW - s.PW;
+    return c;
+  }
+  __device__ __forceinline__ float at(int, int64_t r, const Kc& c) const {
+    int ri = (int)r;
+    int t = ri / s.KW, kw = ri - t * s.KW;
+    int ic = t / s.KH, kh = t - ic * s.KH;
+    int ih = c.ih0 + kh, iw = c.iw0 + kw;
+    bool in = c.ok && ih >= 0 && ih < s.H && iw >= 0 && iw < s.W;
+    return in ? c.xn[((int64_t)ic * s.H + ih) * s.W + iw] : 0.0f;
+  }
 };
 
 // Per-tap weight gradient for the tensor-core path: batch index = tap (kh, kw).

@@ -156,14 +156,20 @@ struct Smem {
   static constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
 };
 
-// One producer group (128 threads, gtid 0..127) fills `rows` tile rows of a
-// stage from a loader contiguous along the row index: thread = row.
+// A producer group (128 threads, gtid 0..127) fills one operand tile of a
+// stage in two halves, load (global -> registers) and store (split into hi/lo
+// -> swizzled shared memory), so the next k-block's loads can be in flight
+// while the current one is stored.  REGS values per thread.
+//
+// Loader contiguous along the row index: thread = tile row, 32 values of k.
 template <class LD>
-__device__ __forceinline__ void produce_rows(const LD& ld, const typename LD::Row& rw, bool mine, int gtid,
-                                             int64_t k0, int64_t kend, uint8_t* hi, uint8_t* lo) {
+__device__ __forceinline__ void load_rows(const LD& ld, const typename LD::Row& rw, bool mine, int64_t k0,
+                                          int64_t kend, float (&v)[BK]) {
+  if (mine) ld.fill(rw, k0, kend, v);
+}
+
+__device__ __forceinline__ void store_rows(const float (&v)[BK], bool mine, int gtid, uint8_t* hi, uint8_t* lo) {
   if (!mine) return;
-  float v[BK];
-  ld.fill(rw, k0, kend, v);
 #pragma unroll
   for (int c = 0; c < BK / 4; ++c) {
     float4 h, l;
@@ -177,21 +183,24 @@ __device__ __forceinline__ void produce_rows(const LD& ld, const typename LD::Ro
   }
 }
 
-// ... from a loader contiguous along k: lane = k, the group's 4 warps take
-// rows round-robin; all of a lane's loads are issued before any store.
+// Loader contiguous along k: lane = k, the group's 4 warps take rows
+// round-robin (ROWS/4 values per thread).
 template <class LD, int ROWS>
-__device__ __forceinline__ void produce_kcontig(const LD& ld, int b, int64_t r0, int64_t rows_total, int gwarp,
-                                                int lane, int64_t k0, int64_t kend, uint8_t* hi, uint8_t* lo) {
+__device__ __forceinline__ void load_kcontig(const LD& ld, int b, int64_t r0, int64_t rows_total, int gwarp,
+                                             int lane, int64_t k0, int64_t kend, float (&v)[ROWS / 4]) {
   typename LD::Kc kc = ld.kctx(b, k0 + lane, kend);
-  constexpr int PER = ROWS / 4;
-  float v[PER];
 #pragma unroll
-  for (int i = 0; i < PER; ++i) {
+  for (int i = 0; i < ROWS / 4; ++i) {
     int r = gwarp + 4 * i;
     v[i] = (r0 + r < rows_total) ? ld.at(b, r0 + r, kc) : 0.0f;
   }
+}
+
+template <int ROWS>
+__device__ __forceinline__ void store_kcontig(const float (&v)[ROWS / 4], int gwarp, int lane, uint8_t* hi,
+                                              uint8_t* lo) {
 #pragma unroll
-  for (int i = 0; i < PER; ++i) {
+  for (int i = 0; i < ROWS / 4; ++i) {
     int r = gwarp + 4 * i;
     float h, l;
     split_tf32(v[i], h, l);
@@ -200,6 +209,12 @@ __device__ __forceinline__ void produce_kcontig(const LD& ld, int b, int64_t r0,
     *reinterpret_cast<float*>(lo + off) = l;
   }
 }
+
+// Registers per thread for one operand tile of ROWS rows.
+template <class LD, int ROWS>
+struct TileRegs {
+  static constexpr int N = LD::kContigK ? ROWS / 4 : BK;
+};
 
 // Per-thread row context of a loader contiguous along the row index (none for
 // loaders contiguous along k).
@@ -258,23 +273,33 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     typename RowOf<LB>::type rb{};
     if constexpr (!LA::kContigK) ra = la.row(b, m0 + gtid, M);
     if constexpr (!LB::kContigK) rb = lb.row(b, n0 + (gtid < BN ? gtid : 0), N);
-    for (int kb = group; kb < nk && ok; kb += 2) {
+    const bool bmine = gtid < BN;
+    float va[1][TileRegs<LA, BM>::N], vb[1][TileRegs<LB, BN>::N];
+    auto load = [&](int kb, int slot) {
+      int64_t k0 = kb0 + (int64_t)kb * BK;
+      if constexpr (LA::kContigK) load_kcontig<LA, BM>(la, b, m0, M, gwarp, lane, k0, kend, va[slot]);
+      else load_rows(la, ra, true, k0, kend, va[slot]);
+      if constexpr (LB::kContigK) load_kcontig<LB, BN>(lb, b, n0, N, gwarp, lane, k0, kend, vb[slot]);
+      else load_rows(lb, rb, bmine, k0, kend, vb[slot]);
+    };
+    auto store = [&](int kb, int slot) {
       int s = kb % STAGES;
       ok = mbar_wait(&empty[s], (uint32_t)((kb / STAGES) & 1) ^ 1u, 1);
-      if (!ok) break;
+      if (!ok) return;
       uint8_t* st = smem + s * S::STAGE;
-      int64_t k0 = kb0 + (int64_t)kb * BK;
-      if constexpr (LA::kContigK)
-        produce_kcontig<LA, BM>(la, b, m0, M, gwarp, lane, k0, kend, st, st + S::A_BYTES);
-      else
-        produce_rows(la, ra, true, gtid, k0, kend, st, st + S::A_BYTES);
       uint8_t* bh = st + 2 * S::A_BYTES;
-      if constexpr (LB::kContigK)
-        produce_kcontig<LB, BN>(lb, b, n0, N, gwarp, lane, k0, kend, bh, bh + S::B_BYTES);
-      else
-        produce_rows(lb, rb, gtid < BN, gtid, k0, kend, bh, bh + S::B_BYTES);
+      if constexpr (LA::kContigK) store_kcontig<BM>(va[slot], gwarp, lane, st, st + S::A_BYTES);
+      else store_rows(va[slot], true, gtid, st, st + S::A_BYTES);
+      if constexpr (LB::kContigK) store_kcontig<BN>(vb[slot], gwarp, lane, bh, bh + S::B_BYTES);
+      else store_rows(vb[slot], bmine, gtid, bh, bh + S::B_BYTES);
       fence_proxy_async();
       mbar_arrive(&full[s]);
+    };
+    // the loads of a k-block are issued before its stage is waited for, so
+    // their latency overlaps the wait
+    for (int kb = group; kb < nk && ok; kb += 2) {
+      load(kb, 0);
+      store(kb, 0);
     }
   } else if (lane == 0) {
     // ---- MMA issuer ----

@@ -19,6 +19,7 @@
 
 #include "tp_core.h"
 #include "tp_launch.h"
+#include "tp_chanred.cuh"
 
 namespace tp {
 
@@ -35,55 +36,7 @@ __global__ void k_bn_eval(const float* __restrict__ x, const float* __restrict__
   }
 }
 
-// ---- BatchNorm train: statistics ---------------------------------------------------
-// grid (C, splits).  Split s of channel c covers images [n0, n1).
-__global__ void k_bn_stats(const float* __restrict__ x, int64_t N, int64_t C, int64_t S, int splits,
-                           double* __restrict__ part) {
-  __shared__ double sh_s[32], sh_q[32];
-  int64_t c = blockIdx.x;
-  int split = blockIdx.y;
-  int64_t per = (N + splits - 1) / splits;
-  int64_t n0 = split * per, n1 = n0 + per < N ? n0 + per : N;
-  double s = 0.0, q = 0.0;
-  bool vec = (S & 3) == 0;
-  for (int64_t n = n0; n < n1; ++n) {
-    const float* p = x + (n * C + c) * S;
-    if (vec) {
-      const float4* p4 = reinterpret_cast<const float4*>(p);
-      for (int64_t i = threadIdx.x; i < (S >> 2); i += blockDim.x) {
-        float4 v = p4[i];
-        s += (double)v.x + (double)v.y + (double)v.z + (double)v.w;
-        q += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
-      }
-    } else {
-      for (int64_t i = threadIdx.x; i < S; i += blockDim.x) {
-        double v = p[i];
-        s += v;
-        q += v * v;
-      }
-    }
-  }
-  for (int o = 16; o > 0; o >>= 1) {
-    s += __shfl_xor_sync(0xffffffffu, s, o);
-    q += __shfl_xor_sync(0xffffffffu, q, o);
-  }
-  int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  if (lane == 0) {
-    sh_s[w] = s;
-    sh_q[w] = q;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    double ts = 0.0, tq = 0.0;
-    for (int k = 0; k < nw; ++k) {
-      ts += sh_s[k];
-      tq += sh_q[k];
-    }
-    part[(c * splits + split) * 2] = ts;
-    part[(c * splits + split) * 2 + 1] = tq;
-  }
-}
-
+// ---- BatchNorm train: statistics (k_chan_reduce in tp_chanred.cuh) -------------------
 // Per channel: mean, biased var -> inv_std; running stats with the unbiased
 // variance.  Writes save_mean / save_invstd (f32) for the normalise pass.
 __global__ void k_bn_finish(const double* __restrict__ part, int64_t C, int splits, double M, float eps,
@@ -140,51 +93,7 @@ __global__ void k_bn_apply(const float* __restrict__ x, const float* __restrict_
   }
 }
 
-// ---- BatchNorm backward ---------------------------------------------------------------
-// part[c][split] = (sum dy, sum dy*x_hat); relu_src: if given, dy is masked by
-// relu_src > 0 (the backward of a ReLU applied to the BN output).
-__global__ void k_bn_bwd_stats(const float* __restrict__ dy, const float* __restrict__ x,
-                               const float* __restrict__ relu_src, const float* __restrict__ mean,
-                               const float* __restrict__ invstd, int64_t N, int64_t C, int64_t S, int splits,
-                               double* __restrict__ part) {
-  __shared__ double sh_a[32], sh_b[32];
-  int64_t c = blockIdx.x;
-  int split = blockIdx.y;
-  int64_t per = (N + splits - 1) / splits;
-  int64_t n0 = split * per, n1 = n0 + per < N ? n0 + per : N;
-  float mu = mean[c], is = invstd[c];
-  double a = 0.0, bsum = 0.0;
-  for (int64_t n = n0; n < n1; ++n) {
-    int64_t base = (n * C + c) * S;
-    for (int64_t i = threadIdx.x; i < S; i += blockDim.x) {
-      float g = dy[base + i];
-      if (relu_src && !(relu_src[base + i] > 0.0f)) g = 0.0f;
-      float xh = (x[base + i] - mu) * is;
-      a += g;
-      bsum += (double)g * xh;
-    }
-  }
-  for (int o = 16; o > 0; o >>= 1) {
-    a += __shfl_xor_sync(0xffffffffu, a, o);
-    bsum += __shfl_xor_sync(0xffffffffu, bsum, o);
-  }
-  int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  if (lane == 0) {
-    sh_a[w] = a;
-    sh_b[w] = bsum;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    double ta = 0.0, tb = 0.0;
-    for (int k = 0; k < nw; ++k) {
-      ta += sh_a[k];
-      tb += sh_b[k];
-    }
-    part[(c * splits + split) * 2] = ta;
-    part[(c * splits + split) * 2 + 1] = tb;
-  }
-}
-
+// ---- BatchNorm backward: sums (k_chan_reduce with ChanBnBwdF) ---------------------------
 // coef[c] = {w*invstd, sum_dy/M, sum_dyxh/M}; dw, db written here.
 __global__ void k_bn_bwd_finish(const double* __restrict__ part, int64_t C, int splits, double M,
                                 const float* __restrict__ w, const float* __restrict__ invstd,
@@ -218,19 +127,15 @@ __global__ void k_bn_bwd_apply(const float* __restrict__ dy, const float* __rest
   }
 }
 
-static int bn_splits(int64_t C, int64_t N) {
-  int64_t target = (int64_t)sm_count() * 4;
-  int splits = 1;
-  while (C * splits < target && splits * 2 <= N) splits *= 2;
-  return splits;
-}
+
 
 void launch_bn_train(const float* x, const float* w, const float* b, float* rm, float* rv, float* y,
                      float* save_mean, float* save_invstd, int64_t N, int64_t C, int64_t S, float eps,
                      float momentum, bool relu) {
-  int splits = bn_splits(C, N);
+  int splits = chan_splits(C, N, S, sm_count());
   double* part = (double*)scratch((size_t)C * splits * 2 * sizeof(double));
-  TP_LAUNCH(k_bn_stats, dim3((unsigned)C, (unsigned)splits), 256, 0, x, N, C, S, splits, part);
+  auto kst = k_chan_reduce<ChanStatsF>;
+  TP_LAUNCH(kst, dim3((unsigned)C, (unsigned)splits), 256, 0, ChanStatsF{x}, N, C, S, splits, part);
   TP_LAUNCH(k_bn_finish, (unsigned)((C + 127) / 128), 128, 0, part, C, splits, (double)(N * S), eps, momentum,
             save_mean, save_invstd, rm, rv);
   TP_LAUNCH(k_bn_apply, grid_for(N * C * S, 256, 4), 256, 0, x, save_mean, save_invstd, w, b, y, N, C, S,
@@ -239,12 +144,13 @@ void launch_bn_train(const float* x, const float* w, const float* b, float* rm, 
 
 void launch_bn_backward(const float* dy, const float* x, const float* relu_src, const float* w, const float* mean,
                         const float* invstd, float* dx, float* dw, float* db, int64_t N, int64_t C, int64_t S) {
-  int splits = bn_splits(C, N);
+  int splits = chan_splits(C, N, S, sm_count());
   size_t pb = (size_t)C * splits * 2 * sizeof(double);
   char* ws = (char*)scratch(pb + (size_t)C * 3 * sizeof(float) + 64);
   double* part = (double*)ws;
   float* coef = (float*)(ws + ((pb + 15) & ~(size_t)15));
-  TP_LAUNCH(k_bn_bwd_stats, dim3((unsigned)C, (unsigned)splits), 256, 0, dy, x, relu_src, mean, invstd, N, C, S,
+  auto kbs = k_chan_reduce<ChanBnBwdF>;
+  TP_LAUNCH(kbs, dim3((unsigned)C, (unsigned)splits), 256, 0, ChanBnBwdF{dy, x, relu_src, mean, invstd}, N, C, S,
             splits, part);
   TP_LAUNCH(k_bn_bwd_finish, (unsigned)((C + 127) / 128), 128, 0, part, C, splits, (double)(N * S), w, invstd, coef,
             dw, db);

@@ -95,14 +95,77 @@ static PoolGeom pool_geom(const Tensor& x, const int64_t* k, int nk, const int64
   return g;
 }
 
+// 2x2 windows, stride 2, no padding, even H and W (every VGG pool): windows
+// tile the input exactly, so each input element belongs to one window.  One
+// thread per output reads its window as two 8-byte rows; the backward writes
+// the whole window (the gradient at the recorded maximum, zero elsewhere).
+// Same visiting order and strict > as the general kernel.
+__global__ void k_maxpool2x2_fwd(const float* __restrict__ x, float* __restrict__ y, int32_t* __restrict__ idx,
+                                 int64_t planes, int H, int W) {
+  const int OH = H >> 1, OW = W >> 1;
+  const int64_t total = planes * OH * OW;
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
+    int ow = (int)(i % OW);
+    int64_t t = i / OW;
+    int oh = (int)(t % OH);
+    int64_t bc = t / OH;
+    const float* xp = x + bc * H * W;
+    int r0 = 2 * oh * W + 2 * ow;
+    float2 a = *reinterpret_cast<const float2*>(xp + r0);
+    float2 b = *reinterpret_cast<const float2*>(xp + r0 + W);
+    float m = -3.402823e+38f;
+    int mi = -1;
+    if (a.x > m) { m = a.x; mi = r0; }
+    if (a.y > m) { m = a.y; mi = r0 + 1; }
+    if (b.x > m) { m = b.x; mi = r0 + W; }
+    if (b.y > m) { m = b.y; mi = r0 + W + 1; }
+    y[i] = m;
+    if (idx) idx[i] = mi;
+  }
+}
+
+__global__ void k_maxpool2x2_bwd(const float* __restrict__ gy, const int32_t* __restrict__ idx,
+                                 float* __restrict__ gx, int64_t planes, int H, int W) {
+  const int OH = H >> 1, OW = W >> 1;
+  const int64_t total = planes * OH * OW;
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
+    int ow = (int)(i % OW);
+    int64_t t = i / OW;
+    int oh = (int)(t % OH);
+    int64_t bc = t / OH;
+    float g = gy[i];
+    int j = idx[i];
+    int r0 = 2 * oh * W + 2 * ow;
+    float* gp = gx + bc * H * W;
+    *reinterpret_cast<float2*>(gp + r0) = make_float2(j == r0 ? g : 0.0f, j == r0 + 1 ? g : 0.0f);
+    *reinterpret_cast<float2*>(gp + r0 + W) = make_float2(j == r0 + W ? g : 0.0f, j == r0 + W + 1 ? g : 0.0f);
+  }
+}
+
+static bool is_2x2(const PoolGeom& g) {
+  return g.KH == 2 && g.KW == 2 && g.SH == 2 && g.SW == 2 && g.PH == 0 && g.PW == 0 && g.DH == 1 && g.DW == 1 &&
+         (g.H % 2) == 0 && (g.W % 2) == 0 && g.H * g.W <= (int64_t)1 << 30;
+}
+
 void launch_maxpool_fwd(const float* x, float* y, int32_t* idx, const PoolGeom& g) {
   int64_t total = g.N * g.C * g.OH * g.OW;
-  if (total > 0) TP_LAUNCH(k_maxpool_fwd, grid_for(total, 256), 256, 0, x, y, idx, g, total);
+  if (total == 0) return;
+  if (is_2x2(g) && ((uintptr_t)x & 7) == 0)
+    TP_LAUNCH(k_maxpool2x2_fwd, grid_for(total, 256), 256, 0, x, y, idx, g.N * g.C, (int)g.H, (int)g.W);
+  else
+    TP_LAUNCH(k_maxpool_fwd, grid_for(total, 256), 256, 0, x, y, idx, g, total);
 }
 
 void launch_maxpool_bwd(const float* gy, const int32_t* idx, float* gx, const PoolGeom& g) {
   int64_t total = g.N * g.C * g.H * g.W;
-  if (total > 0) TP_LAUNCH(k_maxpool_bwd, grid_for(total, 256), 256, 0, gy, idx, gx, g, total);
+  if (total == 0) return;
+  if (is_2x2(g) && ((uintptr_t)gx & 7) == 0)
+    TP_LAUNCH(k_maxpool2x2_bwd, grid_for(g.N * g.C * g.OH * g.OW, 256), 256, 0, gy, idx, gx, g.N * g.C, (int)g.H,
+              (int)g.W);
+  else
+    TP_LAUNCH(k_maxpool_bwd, grid_for(total, 256), 256, 0, gy, idx, gx, g, total);
 }
 
 }  // namespace tp

@@ -39,6 +39,86 @@ def _vp(x: int):
     return ctypes.c_void_p(int(x)) if x else None
 
 
+def plan_blocks(cfg=CFG, in_ch: int = 3, size: int = 32) -> list[dict]:
+    """One dict per conv block: cin, cout, H, W (the conv's spatial size) and
+    whether a 2x2 max-pool follows."""
+    blocks = []
+    cin, H = in_ch, size
+    i = 0
+    while i < len(cfg):
+        cout = cfg[i]
+        pool = i + 1 < len(cfg) and cfg[i + 1] == "M"
+        blocks.append({"cin": cin, "cout": cout, "H": H, "W": H, "pool": pool})
+        cin = cout
+        if pool:
+            H //= 2
+            i += 2
+        else:
+            i += 1
+    return blocks
+
+
+def plan_params(blocks: list[dict], feat: int) -> tuple[list, dict, int]:
+    """Parameter specs (name, shape, init) in the order backward finishes
+    them (fc first, conv1 last), their (offset, numel) in the flat buffers
+    (each tensor starts on a 256-byte boundary) and the flat length."""
+    specs = []
+    specs.append(("fc.w", [NUM_CLASSES, feat], ("kaiming", feat)))
+    specs.append(("fc.b", [NUM_CLASSES], ("bias", feat)))
+    for li in reversed(range(len(blocks))):
+        b = blocks[li]
+        fan_in = b["cin"] * 9
+        specs.append((f"bn{li}.g", [b["cout"]], ("const", 1.0)))
+        specs.append((f"bn{li}.b", [b["cout"]], ("const", 0.0)))
+        specs.append((f"conv{li}.b", [b["cout"]], ("bias", fan_in)))
+        specs.append((f"conv{li}.w", [b["cout"], b["cin"], 3, 3], ("kaiming", fan_in)))
+    offsets = {}
+    off = 0
+    for name, shape, _ in specs:
+        n = int(np.prod(shape))
+        offsets[name] = (off, n)
+        off += (n + 63) // 64 * 64
+    return specs, offsets, off
+
+
+def init_params(specs: list, offsets: dict, flat_len: int, seed: int) -> np.ndarray:
+    """The flat parameter buffer on the host: PyTorch's default Conv2d/Linear
+    init (kaiming_uniform_ with a=sqrt(5), i.e. U(+-1/sqrt(fan_in)), for
+    weights and biases), BN gamma 1 and beta 0; padding zero."""
+    rng = np.random.default_rng(seed)
+    host = np.zeros(flat_len, np.float32)
+    for name, _, init in specs:
+        o, n = offsets[name]
+        if init[0] in ("kaiming", "bias"):
+            bound = 1.0 / math.sqrt(init[1])
+            host[o:o + n] = rng.uniform(-bound, bound, n)
+        else:
+            host[o:o + n] = init[1]
+    return host
+
+
+def plan_buckets(offsets: dict, nblocks: int, flat_len: int, bucket_bytes: int) -> list[tuple[int, int, str]]:
+    """Split the flat gradient buffer into contiguous buckets of at least
+    bucket_bytes (the last one takes the rest), each closing after the layer
+    whose gradients end it: (start element, element count, layer key), keys
+    "fc" and "blk<i>", in backward order.  Together the buckets cover
+    [0, flat_len) exactly once."""
+    buckets = []
+    order = ["fc"] + [f"blk{li}" for li in reversed(range(nblocks))]
+    ends = {"fc": offsets["fc.b"][0] + offsets["fc.b"][1]}
+    for li in range(nblocks):
+        o, n = offsets[f"conv{li}.w"]
+        ends[f"blk{li}"] = o + n
+    start = 0
+    limit = max(1, bucket_bytes // 4)
+    for key in order:
+        end = ends[key]
+        if end - start >= limit or key == order[-1]:
+            buckets.append((start, (flat_len if key == order[-1] else end) - start, key))
+            start = end
+    return buckets
+
+
 class VGG11BN:
     """Buffers, parameters and the step sequence of VGG-11-BN on 32x32 inputs."""
 
@@ -52,62 +132,22 @@ class VGG11BN:
         self.bucket_bytes = bucket_bytes
         self._allocs = []
         self.graph = None
-        rng = np.random.default_rng(seed)
-
         # ---- layer plan ----
-        self.blocks = []  # dicts: cin, cout, H, W, pool
-        cin, H = 3, 32
-        i = 0
-        while i < len(CFG):
-            cout = CFG[i]
-            pool = i + 1 < len(CFG) and CFG[i + 1] == "M"
-            self.blocks.append({"cin": cin, "cout": cout, "H": H, "W": H, "pool": pool})
-            cin = cout
-            if pool:
-                H //= 2
-                i += 2
-            else:
-                i += 1
-        self.feat = cin * H * H  # 512
+        self.blocks = plan_blocks()
+        last = self.blocks[-1]
+        self.feat = last["cout"] * (last["H"] // 2) ** 2  # 512
         assert self.feat == 512
 
         # ---- parameters, gradients, momentum: one flat buffer each, laid out in
-        # the order backward finishes them (fc first, conv1 last) so gradient
-        # buckets close in backward order ----
-        specs = []  # (name, shape, init)
-        specs.append(("fc.w", [NUM_CLASSES, self.feat], ("kaiming", self.feat)))
-        specs.append(("fc.b", [NUM_CLASSES], ("bias", self.feat)))
-        for li in reversed(range(len(self.blocks))):
-            b = self.blocks[li]
-            fan_in = b["cin"] * 9
-            specs.append((f"bn{li}.g", [b["cout"]], ("const", 1.0)))
-            specs.append((f"bn{li}.b", [b["cout"]], ("const", 0.0)))
-            specs.append((f"conv{li}.b", [b["cout"]], ("bias", fan_in)))
-            specs.append((f"conv{li}.w", [b["cout"], b["cin"], 3, 3], ("kaiming", fan_in)))
+        # the order backward finishes them so gradient buckets close in
+        # backward order ----
+        specs, self.offsets, self.flat_len = plan_params(self.blocks, self.feat)
         self.param_specs = specs
         self.nparams = sum(int(np.prod(s)) for _, s, _ in specs)
-        self.offsets = {}
-        off = 0
-        for name, shape, _ in specs:
-            n = int(np.prod(shape))
-            self.offsets[name] = (off, n)
-            off += (n + 63) // 64 * 64  # 256-byte aligned tensors inside the flat buffers
-        self.flat_len = off
         self.params = self._alloc(self.flat_len * 4)
         self.grads = self._alloc(self.flat_len * 4)
         self.moms = self._alloc(self.flat_len * 4)
-        host = np.zeros(self.flat_len, np.float32)
-        for name, shape, init in specs:
-            o, n = self.offsets[name]
-            if init[0] == "kaiming":  # kaiming_uniform_(a=sqrt(5)): bound = 1/sqrt(fan_in)
-                bound = 1.0 / math.sqrt(init[1])
-                host[o:o + n] = rng.uniform(-bound, bound, n)
-            elif init[0] == "bias":
-                bound = 1.0 / math.sqrt(init[1])
-                host[o:o + n] = rng.uniform(-bound, bound, n)
-            else:
-                host[o:o + n] = init[1]
-        self._h2d(self.params, host)
+        self._h2d(self.params, init_params(specs, self.offsets, self.flat_len, seed))
         check(self.lib.tp_memset(_vp(self.grads), 0, self.flat_len * 4))
         check(self.lib.tp_memset(_vp(self.moms), 0, self.flat_len * 4))
 
@@ -174,22 +214,7 @@ class VGG11BN:
         return self.grads + 4 * self.offsets[name][0]
 
     def _plan_buckets(self) -> None:
-        """Split the flat gradient buffer into buckets of about bucket_bytes,
-        each closing after the layer whose gradients end it."""
-        self.buckets = []  # (start_elem, count, layer index that completes it)
-        order = ["fc"] + [f"blk{li}" for li in reversed(range(len(self.blocks)))]
-        ends = {}
-        ends["fc"] = self.offsets["fc.b"][0] + self.offsets["fc.b"][1]
-        for li in range(len(self.blocks)):
-            o, n = self.offsets[f"conv{li}.w"]
-            ends[f"blk{li}"] = o + n
-        start = 0
-        limit = max(1, self.bucket_bytes // 4)
-        for key in order:
-            end = ends[key]
-            if end - start >= limit or key == order[-1]:
-                self.buckets.append((start, (self.flat_len if key == order[-1] else end) - start, key))
-                start = end
+        self.buckets = plan_buckets(self.offsets, len(self.blocks), self.flat_len, self.bucket_bytes)
         self.bucket_after = {b[2]: b for b in self.buckets}
 
     # ---- the step ----------------------------------------------------------------------
