@@ -475,12 +475,16 @@ def run_vgg(args, rank, world, local):
     reps = 20
     xin = model.blocks[2]["out"]
     conv_args = (ctypes.c_void_p(xin), ctypes.c_void_p(model.p("conv3.w")), ctypes.c_void_p(model.p("conv3.b")),
-                 ctypes.c_void_p(b4["z"]), B, b4["cin"], b4["H"], b4["W"], b4["cout"], 3, 3, 1, 1, 1, 1)
-    lib.tpk_conv2d_fwd(*conv_args)
+                 ctypes.c_void_p(b4["z"]), B, b4["cin"], b4["H"], b4["W"], b4["cout"], 3, 3)
+    if model.layout == "nhwc":
+        conv_fn, conv_args = lib.tpk_conv2d_fwd_nhwc, conv_args + (1, 1)
+    else:
+        conv_fn, conv_args = lib.tpk_conv2d_fwd, conv_args + (1, 1, 1, 1)
+    conv_fn(*conv_args)
     g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     g0.record(stream)
     for _ in range(reps):
-        lib.tpk_conv2d_fwd(*conv_args)
+        conv_fn(*conv_args)
     g1.record(stream)
     g1.synchronize()
     k_ms = g0.elapsed_time(g1) / reps
@@ -509,7 +513,9 @@ def run_vgg(args, rank, world, local):
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak3, 1), "unit": "TFLOP/s",
                      "frac": round(achieved / peak3, 4), "traffic": None,
                      "peak_source": f"{peak_kind} bf16_tflops {bf16} / 2 (tf32) / 3 (3xTF32)",
-                     "kernel": "conv3x3 forward gather-GEMM, block 4 (256->256 @ 8x8)",
+                     "kernel": ("conv3x3 forward, TMA-fed tcgen05 implicit GEMM, channels-last"
+                                if model.layout == "nhwc" else "conv3x3 forward, gather-GEMM, NCHW")
+                     + ", block 4 (256->256 @ 8x8)",
                      "kernel_ms": round(k_ms, 4), "step_tflops": round(model.step_flops() * world / 1e12, 4)},
         "e2e": {"value": round(e2e_value, 1), "unit": "imgs/s", "h2d_bytes_per_step": int(hx.numel() * 4 + hy.numel() * 4),
                 "d2h_bytes_per_step": 4, "path": "tp_memcpy_h2d(pinned batch) + tp_graph_launch(step) + loss readback"},

@@ -213,7 +213,9 @@ TP_API int tp_conv2d_weight_backward(int64_t grad_out, int64_t input, const int6
 TP_API int tp_conv2d_bias_backward(int64_t grad_out, int64_t out_ch, const int64_t* grad_out_shape, tp_handle* out);
 
 /* contraction engine: 0 = tcgen05 tensor cores with the 3xTF32 split (default
- * where M >= 64), 1 = the CUDA-core fp32 kernel everywhere (cross-check) */
+ * where M >= 64), operand tiles brought in by TMA where the operands allow it;
+ * 1 = the CUDA-core fp32 kernel everywhere (cross-check); 2 = tensor cores
+ * with gathered operand tiles only (no TMA; cross-check of the TMA path) */
 TP_API int tp_set_gemm_path(int path);
 /* synchronises, then reports the tensor-core kernel's status word: 0 = ok,
  * else the code of a bounded wait that expired; reset != 0 clears it */
@@ -302,6 +304,37 @@ TP_API int tpk_conv2d_dgrad(const float* dy, const float* w, float* dx, int64_t 
                             int64_t Cout, int KH, int KW, int SH, int SW, int PH, int PW);
 TP_API int tpk_conv2d_wgrad(const float* dy, const float* x, float* dw, int64_t N, int64_t Cin, int64_t H, int64_t W,
                             int64_t Cout, int KH, int KW, int SH, int SW, int PH, int PW);
+/* The same three on channels-last buffers: x [N][H][W][Cin], y / dy
+ * [N][OH][OW][Cout], stride 1, dilation 1, groups 1, OH = H + 2PH - KH + 1.
+ * Filters w and the filter gradient dw keep the reference layout
+ * [Cout][Cin][KH][KW].  No reference counterpart: the reference's shaders are
+ * NCHW only (conv.wgsl:25-60, conv_backward.wgsl:24-101); these serve a
+ * training step that keeps its activations channels-last (tpcuda.vgg). */
+TP_API int tpk_conv2d_fwd_nhwc(const float* x, const float* w, const float* bias, float* y, int64_t N, int64_t Cin,
+                               int64_t H, int64_t W, int64_t Cout, int KH, int KW, int PH, int PW);
+TP_API int tpk_conv2d_dgrad_nhwc(const float* dy, const float* w, float* dx, int64_t N, int64_t Cin, int64_t H,
+                                 int64_t W, int64_t Cout, int KH, int KW, int PH, int PW);
+TP_API int tpk_conv2d_wgrad_nhwc(const float* dy, const float* x, float* dw, int64_t N, int64_t Cin, int64_t H,
+                                 int64_t W, int64_t Cout, int KH, int KW, int PH, int PW);
+/* Channels-last ([P][C], P = pixels) companions of tpk_bn_train,
+ * tpk_bn_backward, tpk_channel_sum and tpk_maxpool_fwd / _bwd (2x2, stride
+ * 2), for the same step; C % 4 == 0 and 16-byte aligned buffers.  Pool
+ * indices are plane offsets h*W + w as in the NCHW kernels.  No reference
+ * counterpart (NCHW only: batchnorm / max_pool2d shaders,
+ * tensor_nn_ops.py:57-254). */
+TP_API int tpk_bn_train_nhwc(const float* x, const float* w, const float* b, float* running_mean,
+                             float* running_var, float* y, float* save_mean, float* save_invstd, int64_t P, int64_t C,
+                             float eps, float momentum, int relu);
+TP_API int tpk_bn_backward_nhwc(const float* dy, const float* x, const float* relu_src, const float* w,
+                                const float* mean, const float* invstd, float* dx, float* dw, float* db, int64_t P,
+                                int64_t C);
+TP_API int tpk_channel_sum_nhwc(const float* x, int64_t P, int64_t C, float* out);
+TP_API int tpk_maxpool2x2_nhwc_fwd(const float* x, float* y, int32_t* idx, int64_t N, int64_t H, int64_t W,
+                                   int64_t C);
+TP_API int tpk_maxpool2x2_nhwc_bwd(const float* dy, const int32_t* idx, float* dx, int64_t N, int64_t H, int64_t W,
+                                   int64_t C);
+/* NCHW [N][C][H][W] -> channels-last [N][H][W][Cpad], channels >= C zero */
+TP_API int tpk_nchw_to_nhwc(const float* x, float* y, int64_t N, int64_t C, int64_t H, int64_t W, int64_t Cpad);
 /* per-channel sum over N and the spatial dims (the conv bias gradient) */
 TP_API int tpk_channel_sum(const float* x, int64_t N, int64_t C, int64_t P, float* out);
 /* the kernels behind tp_batch_norm_train / tp_batch_norm_backward */

@@ -1,5 +1,6 @@
-"""Both contraction engines (tcgen05 3xTF32 tensor-core kernel, CUDA-core fp32
-kernel) against the oracle, plus the tensor-core kernel's status word."""
+"""The contraction engines (tcgen05 3xTF32 tensor-core kernel with TMA-fed or
+gathered operand tiles, CUDA-core fp32 kernel) against the oracle, plus the
+tensor-core kernel's status word."""
 import ctypes
 
 import numpy as np
@@ -17,7 +18,7 @@ def status(rt):
     return v.value
 
 
-@pytest.fixture(params=[0, 1], ids=["tcgen05", "cuda_cores"])
+@pytest.fixture(params=[0, 1, 2], ids=["tcgen05_tma", "cuda_cores", "tcgen05_gather"])
 def path(request, cuda_rt):
     assert cuda_rt.lib.tp_set_gemm_path(request.param) == 0
     yield request.param

@@ -1,0 +1,172 @@
+"""TMA-fed tensor-core GEMM (tp_gemm_tma.cuh) and the channels-last
+convolutions built on it (tpk_conv2d_*_nhwc).
+
+The TMA kernel splits operands and issues MMAs exactly like the gather
+kernel, so for the same tile shape and split-K the two must agree bit for bit:
+every dense case compares engine 0 (TMA where the operands allow) with engine 2
+(gather only) for exact equality, and both against a float64 product.  The
+channels-last convolutions are checked against the NCHW kernels (themselves
+checked against the oracle) after a layout transpose, and directly against the
+oracle for one shape per pass."""
+import ctypes
+
+import numpy as np
+import pytest
+
+from test_gpu_gemm_paths import status
+
+pytestmark = pytest.mark.gpu
+
+
+def dev(rt, arr):
+    arr = np.ascontiguousarray(arr, np.float32)
+    p = ctypes.c_void_p()
+    assert rt.lib.tp_alloc(max(4, arr.nbytes), ctypes.byref(p)) == 0
+    if arr.size:
+        assert rt.lib.tp_memcpy_h2d(p, arr.ctypes.data_as(ctypes.c_void_p), arr.nbytes) == 0
+    return p.value
+
+
+def empty(rt, n):
+    p = ctypes.c_void_p()
+    assert rt.lib.tp_alloc(max(4, n * 4), ctypes.byref(p)) == 0
+    return p.value
+
+
+def read(rt, p, shape):
+    out = np.zeros(int(np.prod(shape)), np.float32)
+    assert rt.lib.tp_memcpy_d2h(out.ctypes.data_as(ctypes.c_void_p), ctypes.c_void_p(p), out.nbytes) == 0
+    return out.reshape(shape)
+
+
+def free(rt, *ps):
+    for p in ps:
+        rt.lib.tp_free(ctypes.c_void_p(p))
+
+
+@pytest.fixture
+def engine(cuda_rt):
+    def set_path(p):
+        assert cuda_rt.lib.tp_set_gemm_path(p) == 0
+    yield set_path
+    cuda_rt.lib.tp_set_gemm_path(0)
+
+
+def close64(got, ref, rel=1e-4):
+    scale = max(1e-30, float(np.max(np.abs(ref))))
+    err = float(np.max(np.abs(got.astype(np.float64) - ref)))
+    assert err <= rel * scale, (err, scale)
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 128, 32), (200, 52, 68), (64, 16, 1000), (512, 384, 4096),
+                                   (1000, 300, 36), (300, 1000, 2048), (96, 40, 8)])
+@pytest.mark.parametrize("a_t", [0, 1])
+@pytest.mark.parametrize("b_t", [0, 1])
+def test_gemm_tma_bitwise_equals_gather(cuda_rt, engine, M, N, K, a_t, b_t):
+    rt = cuda_rt
+    rng = np.random.default_rng(M * 7 + N * 3 + K + 2 * a_t + b_t)
+    A = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    B = rng.uniform(-1, 1, (K, N)).astype(np.float32)
+    bias = rng.uniform(-1, 1, N).astype(np.float32)
+    pa = dev(rt, A.T if a_t else A)
+    pb = dev(rt, B.T if b_t else B)
+    pbias = dev(rt, bias)
+    outs = []
+    for path in (0, 2):
+        engine(path)
+        pc = empty(rt, M * N)
+        assert rt.lib.tpk_gemm(ctypes.c_void_p(pa), a_t, ctypes.c_void_p(pb), b_t, ctypes.c_void_p(pc), M, N, K,
+                               ctypes.c_void_p(pbias)) == 0
+        outs.append(read(rt, pc, (M, N)))
+        free(rt, pc)
+        assert status(rt) == 0
+    free(rt, pa, pb, pbias)
+    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+    close64(outs[0], A.astype(np.float64) @ B.astype(np.float64) + bias)
+
+
+def test_matmul_handle_tma_long_k(cuda_rt, oracle_rt):
+    """K = 8192 through the handle API on the TMA kernel: fp32 accuracy holds."""
+    from test_gpu_dense import close_scaled
+    from test_gpu_ops import both
+    rng = np.random.default_rng(5)
+    ca, oa = both(cuda_rt, oracle_rt, rng.uniform(-1, 1, (256, 8192)))
+    cb, ob = both(cuda_rt, oracle_rt, rng.uniform(-1, 1, (8192, 256)))
+    close_scaled(cuda_rt, oracle_rt, cuda_rt.matmul(ca["id"], cb["id"]), oracle_rt.matmul(oa["id"], ob["id"]),
+                 rel=2e-5)
+    assert status(cuda_rt) == 0
+
+
+# (Cin, Cout, H=W) of every VGG-11-BN conv, plus shapes off the TMA tiling
+NHWC_SHAPES = [(3, 64, 32), (64, 128, 16), (128, 256, 8), (256, 256, 8), (256, 512, 4), (512, 512, 4),
+               (512, 512, 2), (32, 64, 6), (48, 96, 8)]
+
+
+def nchw(a):
+    return np.ascontiguousarray(a.transpose(0, 3, 1, 2))
+
+
+def nhwc(a):
+    return np.ascontiguousarray(a.transpose(0, 2, 3, 1))
+
+
+@pytest.mark.parametrize("cin,cout,hw", NHWC_SHAPES)
+@pytest.mark.parametrize("batch", [4, 16])
+def test_conv_nhwc_matches_nchw(cuda_rt, engine, cin, cout, hw, batch):
+    rt = cuda_rt
+    rng = np.random.default_rng(cin + 3 * cout + hw + batch)
+    x = rng.standard_normal((batch, cin, hw, hw)).astype(np.float32)
+    w = (rng.standard_normal((cout, cin, 3, 3)) * 0.05).astype(np.float32)
+    b = rng.standard_normal(cout).astype(np.float32)
+    dy = rng.standard_normal((batch, cout, hw, hw)).astype(np.float32)
+    px, pxn, pw, pb, pdy, pdyn = dev(rt, x), dev(rt, nhwc(x)), dev(rt, w), dev(rt, b), dev(rt, dy), dev(rt, nhwc(dy))
+    n_y, n_x, n_w = batch * cout * hw * hw, batch * cin * hw * hw, cout * cin * 9
+    y0, y1, dx0, dx1, dw0, dw1 = (empty(rt, n) for n in (n_y, n_y, n_x, n_x, n_w, n_w))
+    L = rt.lib
+    vp = ctypes.c_void_p
+    engine(2)  # NCHW reference side on the gather kernels
+    assert L.tpk_conv2d_fwd(vp(px), vp(pw), vp(pb), vp(y0), batch, cin, hw, hw, cout, 3, 3, 1, 1, 1, 1) == 0
+    assert L.tpk_conv2d_dgrad(vp(pdy), vp(pw), vp(dx0), batch, cin, hw, hw, cout, 3, 3, 1, 1, 1, 1) == 0
+    assert L.tpk_conv2d_wgrad(vp(pdy), vp(px), vp(dw0), batch, cin, hw, hw, cout, 3, 3, 1, 1, 1, 1) == 0
+    engine(0)
+    assert L.tpk_conv2d_fwd_nhwc(vp(pxn), vp(pw), vp(pb), vp(y1), batch, cin, hw, hw, cout, 3, 3, 1, 1) == 0
+    assert L.tpk_conv2d_dgrad_nhwc(vp(pdyn), vp(pw), vp(dx1), batch, cin, hw, hw, cout, 3, 3, 1, 1) == 0
+    assert L.tpk_conv2d_wgrad_nhwc(vp(pdyn), vp(pxn), vp(dw1), batch, cin, hw, hw, cout, 3, 3, 1, 1) == 0
+    assert status(rt) == 0
+    ref_y = read(rt, y0, (batch, cout, hw, hw))
+    got_y = nchw(read(rt, y1, (batch, hw, hw, cout)))
+    ref_dx = read(rt, dx0, (batch, cin, hw, hw))
+    got_dx = nchw(read(rt, dx1, (batch, hw, hw, cin)))
+    ref_dw = read(rt, dw0, (cout, cin, 3, 3))
+    got_dw = read(rt, dw1, (cout, cin, 3, 3))
+    free(rt, px, pxn, pw, pb, pdy, pdyn, y0, y1, dx0, dx1, dw0, dw1)
+    for got, ref in ((got_y, ref_y), (got_dx, ref_dx), (got_dw, ref_dw)):
+        close64(got, ref.astype(np.float64), rel=1e-5)
+
+
+@pytest.mark.parametrize("cin,cout,hw,batch", [(64, 128, 16, 4), (256, 256, 8, 8), (3, 64, 32, 2)])
+def test_conv_nhwc_against_oracle(cuda_rt, oracle_rt, cin, cout, hw, batch):
+    rt, orc = cuda_rt, oracle_rt
+    rng = np.random.default_rng(cin * cout + hw)
+    x = rng.standard_normal((batch, cin, hw, hw)).astype(np.float32)
+    w = (rng.standard_normal((cout, cin, 3, 3)) * 0.05).astype(np.float32)
+    dy = rng.standard_normal((batch, cout, hw, hw)).astype(np.float32)
+    T = lambda a: orc.tensorFromData(a.ravel().tolist(), list(a.shape), "float32")["id"]  # noqa: E731
+    ox, ow, ody = T(x), T(w), T(dy)
+    ref_y = np.asarray(orc.toList(orc.conv2d(ox, ow, None, [1], [1], [1], 1)["id"]), np.float64).reshape(dy.shape)
+    ref_dx = np.asarray(orc.toList(orc.conv2dInputBackward(ody, ow, list(x.shape), list(dy.shape), [1], [1])["id"]),
+                        np.float64).reshape(x.shape)
+    ref_dw = np.asarray(orc.toList(orc.conv2dWeightBackward(ody, ox, list(w.shape), list(dy.shape), list(x.shape),
+                                                            [1], [1])["id"]), np.float64).reshape(w.shape)
+    pxn, pw, pdyn = dev(rt, nhwc(x)), dev(rt, w), dev(rt, nhwc(dy))
+    y, dx, dw = empty(rt, dy.size), empty(rt, x.size), empty(rt, w.size)
+    vp = ctypes.c_void_p
+    L = rt.lib
+    assert L.tpk_conv2d_fwd_nhwc(vp(pxn), vp(pw), None, vp(y), batch, cin, hw, hw, cout, 3, 3, 1, 1) == 0
+    assert L.tpk_conv2d_dgrad_nhwc(vp(pdyn), vp(pw), vp(dx), batch, cin, hw, hw, cout, 3, 3, 1, 1) == 0
+    assert L.tpk_conv2d_wgrad_nhwc(vp(pdyn), vp(pxn), vp(dw), batch, cin, hw, hw, cout, 3, 3, 1, 1) == 0
+    assert status(rt) == 0
+    close64(nchw(read(rt, y, (batch, hw, hw, cout))), ref_y)
+    close64(nchw(read(rt, dx, (batch, hw, hw, cin))), ref_dx)
+    close64(read(rt, dw, w.shape), ref_dw)
+    free(rt, pxn, pw, pdyn, y, dx, dw)

@@ -23,31 +23,29 @@ def close(a, b, rel=1e-4):
 
 
 def device_forward_state(m):
-    """Per-block forward tensors of the last device step (for teacher forcing)."""
-    import ctypes
+    """Per-block forward tensors of the last device step as NCHW arrays (for
+    teacher forcing), whatever layout the step keeps them in."""
     out = []
     for b in m.blocks:
-        n = m.B * b["cout"] * b["H"] * b["W"]
-        sv = {"z": m.read(b["z"], n), "a": m.read(b["a"], n), "mean": m.read(b["mean"], b["cout"]),
-              "invstd": m.read(b["invstd"], b["cout"])}
+        C, H, W = b["cout"], b["H"], b["W"]
+        sv = {"z": m.activation(b["z"], C, H, W).ravel(), "a": m.activation(b["a"], C, H, W).ravel(),
+              "mean": m.read(b["mean"], C), "invstd": m.read(b["invstd"], C)}
         if b["pool"]:
-            raw = np.zeros(n // 4, np.int32)
-            assert m.lib.tp_memcpy_d2h(raw.ctypes.data_as(ctypes.c_void_p), ctypes.c_void_p(b["idx"]),
-                                       raw.nbytes) == 0
-            sv["idx"] = raw
-            sv["p"] = m.read(b["p"], n // 4)
+            sv["idx"] = m.activation(b["idx"], C, H // 2, W // 2, np.int32).ravel()
+            sv["p"] = m.activation(b["p"], C, H // 2, W // 2).ravel()
         sv["out"] = sv["p"] if b["pool"] else sv["a"]
         out.append(sv)
     return out
 
 
 @pytest.mark.parametrize("batch", [4, 16])
-def test_vgg_step_matches_oracle_composition(cuda_rt, oracle_rt, batch):
+@pytest.mark.parametrize("layout", ["nhwc", "nchw"])
+def test_vgg_step_matches_oracle_composition(cuda_rt, oracle_rt, batch, layout):
     """Forward (activations, loss, running stats) against the oracle's own
     forward; backward against the oracle backward driven by the device's
     forward state; then the SGD update (bit-exact given the gradients)."""
     from tpcuda.vgg import VGG11BN
-    m = VGG11BN(cuda_rt, batch, seed=3)
+    m = VGG11BN(cuda_rt, batch, seed=3, layout=layout)
     rng = np.random.default_rng(7)
     x = rng.standard_normal((batch, 3, 32, 32)).astype(np.float32)
     y = rng.integers(0, 10, batch).astype(np.float32)
@@ -68,8 +66,7 @@ def test_vgg_step_matches_oracle_composition(cuda_rt, oracle_rt, batch):
     logits = m.read(m.logits, batch * 10)
     grads_o = oracle_backward(oracle_rt, m, params, x, y, saved, logits)
     for n in params:
-        o, k = m.offsets[n]
-        g_c = m.read(m.grads + 4 * o, k)
+        g_c = m.grad_array(n)
         if n.startswith("conv") and n.endswith(".b"):
             # a conv bias feeding a BN has a gradient that is zero up to rounding
             assert float(np.max(np.abs(g_c - grads_o[n]))) <= 1e-6 * max(1.0, float(np.max(np.abs(g_c)))), n
@@ -78,11 +75,15 @@ def test_vgg_step_matches_oracle_composition(cuda_rt, oracle_rt, batch):
                                                   float(np.max(np.abs(grads_o[n]))))
     # update: param - lr * (grad + wd * param) with the momentum buffer starting at 0
     for n in params:
-        o, k = m.offsets[n]
-        g_c = m.read(m.grads + 4 * o, k)
+        g_c = m.grad_array(n)
         p0 = params[n][0]
         want = p0 - np.float32(m.lr) * (g_c + np.float32(m.wd) * p0)
         assert close(m.param_array(n), want, 1e-6), n
+    if layout == "nhwc":
+        # the first conv's padded input channels keep exactly zero filters
+        o, k = m.offsets["conv0.w"]
+        stored = m.read(m.params + 4 * o, k).reshape(64, m.cin0, 3, 3)
+        assert not np.any(stored[:, 3:])
     m.close()
 
 

@@ -12,15 +12,15 @@
 
 #include "tp_core.h"
 #include "tp_launch.h"
-#include "tp_gemm.cuh"
-#include "tp_gemm_simt.cuh"
-#include "tp_gemm_tc.cuh"
+#include "tp_gemm_dispatch.cuh"
 #include "tp_chanred.cuh"
 
 namespace tp {
 
-// 0: tensor cores (tcgen05, 3xTF32) where the shape allows; 1: CUDA cores only.
+// Kernel selection (tp_gemm_dispatch.cuh): 0 TMA / gather tensor cores, 1 CUDA
+// cores only, 2 gather tensor cores without TMA.
 static int g_gemm_path = 0;
+int gemm_path() { return g_gemm_path; }
 
 int tc_status(bool reset) {
   int v = 0;
@@ -30,23 +30,6 @@ int tc_status(bool reset) {
     TP_CUDA(cudaMemcpyToSymbol(tc::g_status, &z, sizeof(int)));
   }
   return v;
-}
-
-// Tensor-core kernel with the N tile following N (K > 0).
-template <class LA, class LB, class EP>
-void gemm_tc(const LA& la, const LB& lb, const EP& ep, int64_t M, int64_t N, int64_t K, int batch) {
-  if (M == 0 || N == 0 || batch == 0) return;
-  if (N <= 32) gemm_tc_launch<LA, LB, EP, 32, 4>(la, lb, ep, M, N, K, batch);
-  else if (N <= 64) gemm_tc_launch<LA, LB, EP, 64, 4>(la, lb, ep, M, N, K, batch);
-  else gemm_tc_launch<LA, LB, EP, 128, 3>(la, lb, ep, M, N, K, batch);
-}
-
-// Tensor-core path for M >= 64 with K > 0, else the CUDA-core kernel.
-template <class LA, class LB, class EP>
-void gemm_auto(const LA& la, const LB& lb, const EP& ep, int64_t M, int64_t N, int64_t K, int batch) {
-  if (M == 0 || N == 0 || batch == 0) return;
-  if (g_gemm_path == 1 || K == 0 || M < 64) gemm_simt(la, lb, ep, M, N, K, batch);
-  else gemm_tc(la, lb, ep, M, N, K, batch);
 }
 
 // ---- per-channel sum of an NCHW tensor (conv_backward.wgsl:103-119) ---------------
@@ -110,7 +93,7 @@ __global__ void k_pack_filters(const float* __restrict__ w, float* __restrict__ 
   }
 }
 
-static bool tc_ok(int64_t M) { return g_gemm_path == 0 && M >= 64; }
+static bool tc_ok(int64_t M) { return g_gemm_path != 1 && M >= 64; }
 
 void conv_fwd(const ConvShape& s, const float* x, const float* w, const float* bias, float* y) {
   int groups = (int)(s.Cin / s.icpg);
@@ -176,6 +159,9 @@ void matmul_launch(const float* A, const float* B, float* C, int64_t batch, int6
   LdColMajor lb{B, N, b_batched ? K * N : 0};
   EpRowMajor ep{C, N, M * N, nullptr, 0};
   TP_REQUIRE(batch <= 65535, "matmul: batch exceeds the grid limit");
+  if (gemm_tma(MatOp{A, false, K, M * K, batch > 1}, MatOp{B, true, N, K * N, b_batched && batch > 1}, ep, M, N, K,
+               (int)batch))
+    return;
   gemm_auto(la, lb, ep, M, N, K, (int)batch);
 }
 
@@ -186,12 +172,14 @@ void linear_launch(const float* x, const float* w, const float* bias, float* y, 
   LdRowMajor la{x, K, 0};
   LdRowMajor lb{w, K, 0};
   EpRowMajor ep{y, N, 0, bias, relu ? 1 : 0};
+  if (gemm_tma(MatOp{x, false, K, 0, false}, MatOp{w, false, K, 0, false}, ep, M, N, K, 1)) return;
   gemm_auto(la, lb, ep, M, N, K, 1);
 }
 
 void gemm_launch(const float* A, bool a_t, const float* B, bool b_t, float* C, int64_t M, int64_t N, int64_t K,
                  const float* bias) {
   EpRowMajor ep{C, N, 0, bias, 0};
+  if (gemm_tma(MatOp{A, a_t, a_t ? M : K, 0, false}, MatOp{B, !b_t, b_t ? K : N, 0, false}, ep, M, N, K, 1)) return;
   if (!a_t && b_t) gemm_auto(LdRowMajor{A, K, 0}, LdRowMajor{B, K, 0}, ep, M, N, K, 1);
   else if (!a_t && !b_t) gemm_auto(LdRowMajor{A, K, 0}, LdColMajor{B, N, 0}, ep, M, N, K, 1);
   else if (a_t && b_t) gemm_auto(LdColMajor{A, M, 0}, LdRowMajor{B, K, 0}, ep, M, N, K, 1);
@@ -208,7 +196,9 @@ extern "C" {
 
 TP_API int tp_set_gemm_path(int path) {
   return guard([&] {
-    TP_REQUIRE(path == 0 || path == 1, "gemm path must be 0 (tensor cores) or 1 (CUDA cores)");
+    TP_REQUIRE(path >= 0 && path <= 2,
+               "gemm path must be 0 (tensor cores, TMA-fed where possible), 1 (CUDA cores) or 2 (tensor cores "
+               "without TMA)");
     g_gemm_path = path;
   });
 }

@@ -1,0 +1,249 @@
+// Channels-last ([N][H][W][C]) stride-1 convolution: forward, data gradient
+// and per-tap weight gradient on the TMA-fed tensor-core kernel.
+//
+// The reference's conv shaders work on NCHW (conv.wgsl:25-60,
+// conv_backward.wgsl:24-101) and the per-op C ABI keeps that layout
+// (tp_conv.cu).  A training step that owns its activations (tpcuda.vgg) keeps
+// them channels-last instead: every im2col tile of 128 output pixels x 32
+// channels of one tap is then one TMA box whose origin carries the tap shift
+// and whose zero fill is the padding, and the weight gradient reads dy and
+// the shifted x as MN-major boxes.  Filters and filter gradients stay in the
+// reference layout [Cout][Cin][KH][KW]; filters are repacked per call.
+//
+// Shapes the TMA tiling cannot express (channels not a multiple of 32, pixel
+// grids that 128 / 32 pixel boxes do not tile) run on gather loaders over the
+// same layout.
+#include <cuda_runtime.h>
+
+#include "tp_core.h"
+#include "tp_gemm_dispatch.cuh"
+#include "tp_launch.h"
+
+namespace tp {
+
+// ---- gather loaders over channels-last tensors (fallback) ---------------------------------
+
+// Forward im2col: m = (n, oh, ow), k = (kh, kw, c) -> x[n, oh+kh-PH, ow+kw-PW, c].
+struct LdNhwcIm2col {
+  const float* x;
+  int64_t H, W, C, OH, OW;
+  int KW, PH, PW;
+  static constexpr bool kContigK = true;
+  __device__ __forceinline__ float load(int64_t m, int c, int kh, int kw) const {
+    int64_t ow = m % OW, t = m / OW, oh = t % OH, n = t / OH;
+    int64_t ih = oh + kh - PH, iw = ow + kw - PW;
+    if (ih < 0 || ih >= H || iw < 0 || iw >= W) return 0.0f;
+    return x[((n * H + ih) * W + iw) * C + c];
+  }
+  __device__ __forceinline__ float operator()(int, int64_t m, int64_t k) const {
+    int c = (int)(k % C), tap = (int)(k / C);
+    return load(m, c, tap / KW, tap % KW);
+  }
+  struct Kc {
+    int c, kh, kw;
+    bool ok;
+  };
+  __device__ __forceinline__ Kc kctx(int, int64_t k, int64_t kend) const {
+    Kc r;
+    r.ok = k < kend;
+    int64_t kk = r.ok ? k : 0;
+    r.c = (int)(kk % C);
+    int tap = (int)(kk / C);
+    r.kh = tap / KW;
+    r.kw = tap % KW;
+    return r;
+  }
+  __device__ __forceinline__ float at(int, int64_t m, const Kc& c) const {
+    return c.ok && m < rows ? load(m, c.c, c.kh, c.kw) : 0.0f;
+  }
+  int64_t rows;  // N * OH * OW
+};
+
+// Weight gradient B operand: row r = (ci, kh, kw) (reference filter order),
+// k = output pixel (n, oh, ow) -> x[n, oh+kh-PH, ow+kw-PW, ci].
+struct LdNhwcWgradB {
+  const float* x;
+  int64_t H, W, C, OH, OW, P;
+  int KH, KW, PH, PW;
+  static constexpr bool kContigK = true;
+  struct Kc {
+    int64_t n;
+    int oh, ow;
+    bool ok;
+  };
+  __device__ __forceinline__ Kc kctx(int, int64_t k, int64_t kend) const {
+    Kc r;
+    r.ok = k < kend && k < P;
+    int64_t kk = r.ok ? k : 0;
+    r.ow = (int)(kk % OW);
+    int64_t t = kk / OW;
+    r.oh = (int)(t % OH);
+    r.n = t / OH;
+    return r;
+  }
+  __device__ __forceinline__ float at(int, int64_t r, const Kc& c) const {
+    if (!c.ok || r >= C * KH * KW) return 0.0f;
+    int kw = (int)(r % KW);
+    int64_t t = r / KW;
+    int kh = (int)(t % KH);
+    int64_t ci = t / KH;
+    int64_t ih = c.oh + kh - PH, iw = c.ow + kw - PW;
+    if (ih < 0 || ih >= H || iw < 0 || iw >= W) return 0.0f;
+    return x[((c.n * H + ih) * W + iw) * C + ci];
+  }
+  __device__ __forceinline__ float operator()(int b, int64_t r, int64_t k) const { return at(b, r, kctx(b, k, P)); }
+};
+
+// ---- TMA maps over channels-last tensors ---------------------------------------------------
+
+// Box extents (W, H, N) covering `rows` consecutive pixels of an OH x OW grid
+// starting at any multiple of `rows`; false if the grid does not tile so.
+static bool pixel_box(int64_t OH, int64_t OW, int rows, uint32_t box[3]) {
+  int64_t hw = OH * OW;
+  if (OW > rows || OW > 256) return false;
+  if (hw >= rows) {
+    if (hw % rows || rows % OW) return false;
+    box[0] = (uint32_t)OW;
+    box[1] = (uint32_t)(rows / OW);
+    box[2] = 1;
+  } else {
+    if (rows % hw) return false;
+    box[0] = (uint32_t)OW;
+    box[1] = (uint32_t)OH;
+    box[2] = (uint32_t)(rows / hw);
+  }
+  return box[1] <= 256 && box[2] <= 256;
+}
+
+static bool nhwc_map(CUtensorMap* m, const float* t, int64_t N, int64_t H, int64_t W, int64_t C, const uint32_t pix[3],
+                     bool make, bool mn = false) {
+  uint64_t dims[4] = {(uint64_t)C, (uint64_t)W, (uint64_t)H, (uint64_t)N};
+  uint64_t st[3] = {(uint64_t)C * 4, (uint64_t)(W * C) * 4, (uint64_t)(H * W * C) * 4};
+  if (!tma_aligned(t, st, 3)) return false;
+  if (N > 0x7fffffff || H * W > 0x7fffffff) return false;
+  if (make) {
+    uint32_t box[4] = {32, pix[0], pix[1], pix[2]};
+    make_map_f32(m, t, 4, dims, st, box, mn);
+  }
+  return true;
+}
+
+static bool nhwc_tma_ok() { return gemm_path() == 0; }
+
+// ---- launchers -------------------------------------------------------------------------------
+
+struct NhwcShape {
+  int64_t N, Cin, H, W, Cout, OH, OW;
+  int KH, KW, PH, PW;
+};
+
+static NhwcShape nhwc_shape(int64_t N, int64_t Cin, int64_t H, int64_t W, int64_t Cout, int KH, int KW, int PH,
+                            int PW) {
+  TP_REQUIRE(N >= 0 && Cin > 0 && H > 0 && W > 0 && Cout > 0, "conv2d (channels-last): bad shape");
+  TP_REQUIRE(KH > 0 && KW > 0 && PH >= 0 && PW >= 0, "conv2d (channels-last): bad kernel or padding");
+  NhwcShape s{N, Cin, H, W, Cout, H + 2 * PH - KH + 1, W + 2 * PW - KW + 1, KH, KW, PH, PW};
+  TP_REQUIRE(s.OH > 0 && s.OW > 0, "conv2d (channels-last): output would be empty");
+  return s;
+}
+
+__global__ void k_pack_filters(const float* __restrict__ w, float* __restrict__ wp, int64_t Cout, int64_t Cin_pg,
+                               int khw, int mode);
+
+// y[N][OH][OW][Cout] = conv(x[N][H][W][Cin], w) + bias
+static void conv_fwd_nhwc(const NhwcShape& s, const float* x, const float* w, const float* bias, float* y) {
+  const int khw = s.KH * s.KW;
+  const int64_t M = s.N * s.OH * s.OW, K = s.Cin * khw;
+  if (M == 0) return;
+  float* wp = (float*)scratch2((size_t)s.Cout * K * sizeof(float));
+  TP_LAUNCH(k_pack_filters, grid_for(s.Cout * K, 256), 256, 0, w, wp, s.Cout, s.Cin, khw, 0);
+  EpRowMajor ep{y, s.Cout, 0, bias, 0};
+  uint32_t pix[3];
+  MatOp b{wp, false, K, 0, false};
+  if (nhwc_tma_ok() && M >= 64 && s.Cin % 32 == 0 && pixel_box(s.OH, s.OW, tc::BM, pix) &&
+      nhwc_map(nullptr, x, s.N, s.H, s.W, s.Cin, pix, false) && mat_tma_ok(b)) {
+    CUtensorMap ma, mb;
+    nhwc_map(&ma, x, s.N, s.H, s.W, s.Cin, pix, true);
+    mat_map(&mb, b, s.Cout, K, 1, tma_bn(s.Cout));
+    tma::SrcConvK sa{(int)s.OH, (int)s.OW, (int)(s.Cin / 32), s.KW, s.PH, s.PW};
+    gemm_tma_bn(ma, mb, sa, tma::SrcK{0}, ep, M, s.Cout, K, 1);
+    return;
+  }
+  LdNhwcIm2col la{x, s.H, s.W, s.Cin, s.OH, s.OW, s.KW, s.PH, s.PW, M};
+  gemm_auto(la, LdRowMajor{wp, K, 0}, ep, M, s.Cout, K, 1);
+}
+
+// dx[N][H][W][Cin] from dy[N][OH][OW][Cout]: the forward convolution of dy
+// with the flipped, transposed filters and padding K-1-P.
+static void conv_dgrad_nhwc(const NhwcShape& s, const float* dy, const float* w, float* dx) {
+  const int khw = s.KH * s.KW;
+  const int64_t M = s.N * s.H * s.W, K = s.Cout * khw;
+  if (M == 0) return;
+  TP_REQUIRE(s.PH <= s.KH - 1 && s.PW <= s.KW - 1, "conv2d data gradient (channels-last): padding exceeds kernel-1");
+  float* wp = (float*)scratch2((size_t)s.Cin * K * sizeof(float));
+  TP_LAUNCH(k_pack_filters, grid_for(s.Cout * s.Cin * khw, 256), 256, 0, w, wp, s.Cout, s.Cin, khw, 1);
+  EpRowMajor ep{dx, s.Cin, 0, nullptr, 0};
+  const int qh = s.KH - 1 - s.PH, qw = s.KW - 1 - s.PW;
+  uint32_t pix[3];
+  MatOp b{wp, false, K, 0, false};
+  if (nhwc_tma_ok() && M >= 64 && s.Cout % 32 == 0 && pixel_box(s.H, s.W, tc::BM, pix) &&
+      nhwc_map(nullptr, dy, s.N, s.OH, s.OW, s.Cout, pix, false) && mat_tma_ok(b)) {
+    CUtensorMap ma, mb;
+    nhwc_map(&ma, dy, s.N, s.OH, s.OW, s.Cout, pix, true);
+    mat_map(&mb, b, s.Cin, K, 1, tma_bn(s.Cin));
+    tma::SrcConvK sa{(int)s.H, (int)s.W, (int)(s.Cout / 32), s.KW, qh, qw};
+    gemm_tma_bn(ma, mb, sa, tma::SrcK{0}, ep, M, s.Cin, K, 1);
+    return;
+  }
+  LdNhwcIm2col la{dy, s.OH, s.OW, s.Cout, s.H, s.W, s.KW, qh, qw, M};
+  gemm_auto(la, LdRowMajor{wp, K, 0}, ep, M, s.Cin, K, 1);
+}
+
+// dw[Cout][Cin][KH][KW] = sum over output pixels of dy x (x shifted by the tap)
+static void conv_wgrad_nhwc(const NhwcShape& s, const float* dy, const float* x, float* dw) {
+  const int khw = s.KH * s.KW;
+  const int64_t P = s.N * s.OH * s.OW;
+  uint32_t pix[3];
+  if (nhwc_tma_ok() && s.Cout >= 64 && P > 0 && pixel_box(s.OH, s.OW, 32, pix) &&
+      nhwc_map(nullptr, dy, s.N, s.OH, s.OW, s.Cout, pix, false) &&
+      nhwc_map(nullptr, x, s.N, s.H, s.W, s.Cin, pix, false)) {
+    CUtensorMap ma, mb;
+    nhwc_map(&ma, dy, s.N, s.OH, s.OW, s.Cout, pix, true, true);
+    nhwc_map(&mb, x, s.N, s.H, s.W, s.Cin, pix, true, true);
+    tma::SrcPixMN sa{(int)s.OH, (int)s.OW, s.KW, s.PH, s.PW, 0};
+    tma::SrcPixMN sb{(int)s.OH, (int)s.OW, s.KW, s.PH, s.PW, 1};
+    EpWgradTap ep{dw, s.Cin, khw};
+    gemm_tma_bn(ma, mb, sa, sb, ep, s.Cout, s.Cin, P, khw);
+    return;
+  }
+  const int64_t R = s.Cin * khw;
+  EpRowMajor ep{dw, R, 0, nullptr, 0};
+  if (P == 0) {
+    launch_fill(dw, s.Cout * R, 0.0f);
+    return;
+  }
+  LdNhwcWgradB lb{x, s.H, s.W, s.Cin, s.OH, s.OW, P, s.KH, s.KW, s.PH, s.PW};
+  gemm_auto(LdColMajor{dy, s.Cout, 0}, lb, ep, s.Cout, R, P, 1);
+}
+
+}  // namespace tp
+
+using namespace tp;
+
+extern "C" {
+
+TP_API int tpk_conv2d_fwd_nhwc(const float* x, const float* w, const float* bias, float* y, int64_t N, int64_t Cin,
+                               int64_t H, int64_t W, int64_t Cout, int KH, int KW, int PH, int PW) {
+  return guard([&] { conv_fwd_nhwc(nhwc_shape(N, Cin, H, W, Cout, KH, KW, PH, PW), x, w, bias, y); });
+}
+
+TP_API int tpk_conv2d_dgrad_nhwc(const float* dy, const float* w, float* dx, int64_t N, int64_t Cin, int64_t H,
+                                 int64_t W, int64_t Cout, int KH, int KW, int PH, int PW) {
+  return guard([&] { conv_dgrad_nhwc(nhwc_shape(N, Cin, H, W, Cout, KH, KW, PH, PW), dy, w, dx); });
+}
+
+TP_API int tpk_conv2d_wgrad_nhwc(const float* dy, const float* x, float* dw, int64_t N, int64_t Cin, int64_t H,
+                                 int64_t W, int64_t Cout, int KH, int KW, int PH, int PW) {
+  return guard([&] { conv_wgrad_nhwc(nhwc_shape(N, Cin, H, W, Cout, KH, KW, PH, PW), dy, x, dw); });
+}
+
+}  // extern "C"

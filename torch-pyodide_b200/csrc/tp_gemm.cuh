@@ -358,6 +358,32 @@ struct EpRowMajor {
     if (relu) v = fmaxf(v, 0.0f);
     c[b * bs + m * ldc + n] = v;
   }
+  // 16 consecutive columns of row m (columns >= N skipped); 128-bit stores
+  // when the row segment is whole and 16-byte aligned
+  __device__ __forceinline__ void row16(int b, int64_t m, int64_t n0, int64_t N, const float (&v)[16]) const {
+    float* dst = c + b * bs + m * ldc + n0;
+    if (n0 + 16 <= N && ((uintptr_t)dst & 15) == 0) {
+#pragma unroll
+      for (int i = 0; i < 16; i += 4) {
+        float4 o;
+        o.x = bias ? v[i] + bias[n0 + i] : v[i];
+        o.y = bias ? v[i + 1] + bias[n0 + i + 1] : v[i + 1];
+        o.z = bias ? v[i + 2] + bias[n0 + i + 2] : v[i + 2];
+        o.w = bias ? v[i + 3] + bias[n0 + i + 3] : v[i + 3];
+        if (relu) {
+          o.x = fmaxf(o.x, 0.0f);
+          o.y = fmaxf(o.y, 0.0f);
+          o.z = fmaxf(o.z, 0.0f);
+          o.w = fmaxf(o.w, 0.0f);
+        }
+        *reinterpret_cast<float4*>(dst + i) = o;
+      }
+      return;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      if (n0 + i < N) (*this)(b, m, n0 + i, v[i]);
+  }
 };
 
 // NCHW output plane: m = (img, p), n = channel within group b -> out[img, b*ocpg+n, p] (+ bias).
@@ -372,6 +398,11 @@ struct EpNCHW {
     int64_t img = m / P, p = m % P;
     out[(img * C + c) * P + p] = v;
   }
+  __device__ __forceinline__ void row16(int b, int64_t m, int64_t n0, int64_t N, const float (&v)[16]) const {
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      if (n0 + i < N) (*this)(b, m, n0 + i, v[i]);
+  }
 };
 
 // Per-tap weight gradient: C_tap[oc][ic] -> dW[oc, ic, tap].
@@ -381,6 +412,11 @@ struct EpWgradTap {
   int KHW;
   __device__ __forceinline__ void operator()(int tap, int64_t oc, int64_t ic, float v) const {
     dw[(oc * Cin + ic) * KHW + tap] = v;
+  }
+  __device__ __forceinline__ void row16(int b, int64_t m, int64_t n0, int64_t N, const float (&v)[16]) const {
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      if (n0 + i < N) (*this)(b, m, n0 + i, v[i]);
   }
 };
 

@@ -1,0 +1,98 @@
+// GEMM kernel selection shared by the contraction translation units.
+//
+//   gemm_path() == 0   TMA-fed tensor-core kernel where both operands can be
+//                      described by tensor maps, else the gather tensor-core
+//                      kernel (M >= 64, K > 0), else the CUDA-core kernel
+//   gemm_path() == 1   CUDA-core kernel only
+//   gemm_path() == 2   gather tensor-core kernel where it applies, no TMA
+#pragma once
+
+#include "tp_gemm.cuh"
+#include "tp_gemm_simt.cuh"
+#include "tp_gemm_tc.cuh"
+#include "tp_gemm_tma.cuh"
+#include "tp_tma.h"
+
+namespace tp {
+
+int gemm_path();
+
+// Gather tensor-core kernel with the N tile following N (K > 0).
+template <class LA, class LB, class EP>
+void gemm_tc(const LA& la, const LB& lb, const EP& ep, int64_t M, int64_t N, int64_t K, int batch) {
+  if (M == 0 || N == 0 || batch == 0) return;
+  if (N <= 32) gemm_tc_launch<LA, LB, EP, 32, 4>(la, lb, ep, M, N, K, batch);
+  else if (N <= 64) gemm_tc_launch<LA, LB, EP, 64, 4>(la, lb, ep, M, N, K, batch);
+  else gemm_tc_launch<LA, LB, EP, 128, 3>(la, lb, ep, M, N, K, batch);
+}
+
+// Gather tensor-core path for M >= 64 with K > 0, else the CUDA-core kernel.
+template <class LA, class LB, class EP>
+void gemm_auto(const LA& la, const LB& lb, const EP& ep, int64_t M, int64_t N, int64_t K, int batch) {
+  if (M == 0 || N == 0 || batch == 0) return;
+  if (gemm_path() == 1 || K == 0 || M < 64) gemm_simt(la, lb, ep, M, N, K, batch);
+  else gemm_tc(la, lb, ep, M, N, K, batch);
+}
+
+// TMA kernel with the N tile following N; the maps' B box must match.
+template <class SA, class SB, class EP>
+void gemm_tma_bn(const CUtensorMap& ma, const CUtensorMap& mb, const SA& sa, const SB& sb, const EP& ep, int64_t M,
+                 int64_t N, int64_t K, int batch) {
+  if (N <= 32) gemm_tma_launch<SA, SB, EP, 32, 4>(ma, mb, sa, sb, ep, M, N, K, batch);
+  else if (N <= 64) gemm_tma_launch<SA, SB, EP, 64, 4>(ma, mb, sa, sb, ep, M, N, K, batch);
+  else gemm_tma_launch<SA, SB, EP, 128, 3>(ma, mb, sa, sb, ep, M, N, K, batch);
+}
+
+inline uint32_t tma_bn(int64_t N) { return N <= 32 ? 32u : (N <= 64 ? 64u : 128u); }
+
+// A dense operand: element (r, k) of batch b at p[b*bs + r*ld + k] (K-major)
+// or p[b*bs + k*ld + r] (mn: MN-major); batched = false shares it across the
+// batch.
+struct MatOp {
+  const float* p;
+  bool mn;
+  int64_t ld, bs;
+  bool batched;
+};
+
+inline bool mat_tma_ok(const MatOp& o) {
+  if (o.ld <= 0 || o.ld % 4 || (o.batched && o.bs % 4)) return false;
+  uint64_t st[2] = {(uint64_t)o.ld * 4, (uint64_t)(o.batched ? o.bs : o.ld) * 4};
+  return tma_aligned(o.p, st, 2);
+}
+
+// Map over the operand (rows x K per batch); box rows for a K-major operand.
+inline void mat_map(CUtensorMap* m, const MatOp& o, int64_t rows, int64_t K, int batch, uint32_t box_rows) {
+  uint64_t inner = (uint64_t)(o.mn ? rows : K), outer = (uint64_t)(o.mn ? K : rows);
+  uint64_t dims[3] = {inner, outer, (uint64_t)(o.batched ? batch : 1)};
+  uint64_t st[2] = {(uint64_t)o.ld * 4, (uint64_t)(o.batched ? o.bs : o.ld * (int64_t)outer) * 4};
+  uint32_t box[3] = {32, o.mn ? 32u : box_rows, 1};
+  make_map_f32(m, o.p, 3, dims, st, box, o.mn);
+}
+
+template <class SA, class SB, class EP>
+void gemm_tma_mat(const MatOp& a, const MatOp& b, const EP& ep, int64_t M, int64_t N, int64_t K, int batch) {
+  CUtensorMap ma, mb;
+  mat_map(&ma, a, M, K, batch, (uint32_t)tc::BM);
+  mat_map(&mb, b, N, K, batch, tma_bn(N));
+  gemm_tma_bn(ma, mb, SA{a.batched ? 1 : 0}, SB{b.batched ? 1 : 0}, ep, M, N, K, batch);
+}
+
+// C = A . B^T through the TMA kernel when the path and the operands allow;
+// returns false (nothing launched) otherwise.
+template <class EP>
+bool gemm_tma(const MatOp& a, const MatOp& b, const EP& ep, int64_t M, int64_t N, int64_t K, int batch) {
+  if (gemm_path() != 0 || K <= 0 || M < 64 || N <= 0 || batch <= 0) return false;
+  if (K > 0x7fffffff || M > 0x7fffffff || N > 0x7fffffff) return false;
+  if (!mat_tma_ok(a) || !mat_tma_ok(b)) return false;
+  if (a.mn) {
+    if (b.mn) gemm_tma_mat<tma::SrcMN, tma::SrcMN>(a, b, ep, M, N, K, batch);
+    else gemm_tma_mat<tma::SrcMN, tma::SrcK>(a, b, ep, M, N, K, batch);
+  } else {
+    if (b.mn) gemm_tma_mat<tma::SrcK, tma::SrcMN>(a, b, ep, M, N, K, batch);
+    else gemm_tma_mat<tma::SrcK, tma::SrcK>(a, b, ep, M, N, K, batch);
+  }
+  return true;
+}
+
+}  // namespace tp

@@ -382,6 +382,26 @@ __global__ void k_splitk_reduce_b(const float* __restrict__ ws, int splits, int6
 // Host side: read (and optionally clear) the device status word.
 int tc_status(bool reset);
 
+// Split-K factor shared by the tensor-core launchers: the fewest splits whose
+// CTA count fills the SMs in whole waves (each split keeps >= 8 k-blocks).
+inline int gemm_splits(int64_t tiles, int64_t K, int sms) {
+  if (K <= 0 || tiles <= 0) return 1;
+  int64_t maxs = K / 256;
+  if (maxs > 32) maxs = 32;
+  if (maxs <= 1 || tiles >= sms) return 1;
+  int best = 1;
+  double best_t = 1e30;
+  for (int s = 1; s <= maxs; ++s) {
+    int64_t waves = (tiles * s + sms - 1) / sms;
+    double t = (double)waves / s + 0.02 * s;  // per-split cost: partial writes and the reduce
+    if (t < best_t - 1e-9) {
+      best_t = t;
+      best = s;
+    }
+  }
+  return best;
+}
+
 template <class LA, class LB, class EP, int BN, int STAGES>
 void gemm_tc_launch(const LA& la, const LB& lb, const EP& ep, int64_t M, int64_t N, int64_t K, int batch) {
   using S = tc::Smem<BN, STAGES>;
@@ -394,15 +414,7 @@ void gemm_tc_launch(const LA& la, const LB& lb, const EP& ep, int64_t M, int64_t
     attr = true;
   }
   // split K when the tile grid cannot fill the SMs
-  int splits = 1;
-  int64_t tiles = gm * gn * batch;
-  if (K > 0) {
-    int64_t want = ((int64_t)sm_count() + tiles - 1) / tiles;
-    int64_t maxs = K / 256;
-    splits = (int)(want < maxs ? want : maxs);
-    if (splits > 32) splits = 32;
-    if (splits < 1) splits = 1;
-  }
+  int splits = gemm_splits(gm * gn * batch, K, sm_count());
   int64_t kps = (K + splits - 1) / splits;
   kps = (kps + tc::BK - 1) / tc::BK * tc::BK;
   splits = K > 0 ? (int)((K + kps - 1) / kps) : 1;

@@ -1,0 +1,345 @@
+// TMA-fed tensor-core GEMM for sm_100a: tcgen05.mma (kind::tf32), accumulator
+// in TMEM, 3xTF32 split for fp32 accuracy.
+//
+//   C(m, n) = sum_k A(m, k) B(n, k),   a*b ~= ah*bh + ah*bl + al*bh
+//
+// Operand tiles arrive by TMA (cp.async.bulk.tensor, no multicast) straight
+// into 128-byte-swizzled shared memory, so no thread computes a gather
+// address.  Each operand is either K-major (a tile row = 32 consecutive k of
+// one m/n, the same canonical layout as the gather kernel) or MN-major (32
+// consecutive m/n per 128-byte row, one row per k, 32-byte-atom swizzle;
+// 32-wide column groups LBO = 4 KB apart, 4-row k groups SBO = 512 B apart),
+// chosen by the source
+// functor, so transposed operands and channels-last convolution operands are
+// read in place.
+//
+// CTA = 320 threads:
+//   warp 9, one lane   TMA producer: waits empty[s], arms full[s] with the
+//                      stage's byte count, issues the A and B boxes
+//   warps 0-7          splitters: wait full[s], rewrite each fp32 in place as
+//                      its tf32-rounded hi and store lo = x - hi beside it,
+//                      fence to the async proxy, arrive on ready[s]; after the
+//                      last k-block they run the epilogue out of TMEM
+//   warp 8             allocates TMEM; one lane issues 3 MMAs per 8-wide
+//                      k-step once ready[s] completes and commits to empty[s]
+// The split is the same integer rounding as the gather kernel (tp_gemm_tc.cuh)
+// and the MMA sequence is the same, so both kernels produce identical bits for
+// the same tile shape and split-K.
+//
+// Every wait is bounded (2 s by %globaltimer): on expiry the kernel records a
+// code in tc::g_status, stops issuing, waits (bounded) for the boxes and MMAs
+// it already issued and frees its TMEM.
+#pragma once
+
+#include <cuda.h>
+
+#include "tp_gemm_tc.cuh"
+
+namespace tp {
+
+namespace tma {
+
+using tc::BK;
+using tc::BM;
+constexpr int NTHREADS = 320;
+constexpr int NSPLIT = 256;  // splitter threads (warps 0-7)
+constexpr int MMA_WARP = 8;
+constexpr int TMA_WARP = 9;
+
+__device__ __forceinline__ void expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc::smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void load3(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(dst),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(tc::smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void load4(uint32_t dst, const CUtensorMap* map, int x, int y, int z, int w,
+                                      uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+      "%5}], [%6];" ::"r"(dst),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(w), "r"(tc::smem_u32(bar))
+      : "memory");
+}
+
+// MN-major descriptor for tf32: layout SWIZZLE_128B_BASE32B (32-byte chunks
+// of each 128-byte row permuted over 4-row periods), column groups of 32 fp32
+// LBO = 4 KB apart, 4-row k groups SBO = 512 B apart.
+__device__ __forceinline__ uint64_t mn_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)(4096 >> 4) << 16;
+  d |= (uint64_t)(512 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)1 << 61;
+  return d;
+}
+
+// ---- operand sources: issue the boxes of one ROWS x 32 tile --------------------------------------
+
+// K-major rows of a row-major [batch][rows][K] tensor; map dims (K, rows, batch), box (32, ROWS, 1).
+// bmul = 0 when every batch shares the matrix.
+struct SrcK {
+  static constexpr bool kMN = false;
+  int bmul;
+  template <int ROWS>
+  __device__ __forceinline__ void issue(const CUtensorMap* map, uint32_t dst, uint64_t* bar, int b, int64_t r0,
+                                        int64_t k0) const {
+    load3(dst, map, (int)k0, (int)r0, b * bmul, bar);
+  }
+};
+
+// MN-major: a row-major [batch][K][rows] tensor (rows contiguous); map dims
+// (rows, K, batch), box (32, 32, 1), one box per 32 rows of the tile.
+struct SrcMN {
+  static constexpr bool kMN = true;
+  int bmul;
+  template <int ROWS>
+  __device__ __forceinline__ void issue(const CUtensorMap* map, uint32_t dst, uint64_t* bar, int b, int64_t r0,
+                                        int64_t k0) const {
+#pragma unroll
+    for (int j = 0; j < ROWS / 32; ++j) load3(dst + j * 4096, map, (int)r0 + 32 * j, (int)k0, b * bmul, bar);
+  }
+};
+
+// K-major implicit-GEMM operand of a stride-1 convolution over a channels-last
+// [N][H][W][C] input: tile rows = 128 consecutive output pixels (n, oh, ow) of
+// the OH x OW grid, k-block = (tap, 32 channels) with taps outermost.  Map
+// dims (C, W, H, N), box (32, OW, rows, images); the tap shift moves the box
+// origin and the zero fill outside the input is the padding.
+struct SrcConvK {
+  static constexpr bool kMN = false;
+  int OH, OW, cblocks, KW, PH, PW;
+  template <int ROWS>
+  __device__ __forceinline__ void issue(const CUtensorMap* map, uint32_t dst, uint64_t* bar, int, int64_t r0,
+                                        int64_t k0) const {
+    const int64_t hw = (int64_t)OH * OW;
+    const int n0 = (int)(r0 / hw), oh0 = (int)((r0 - (int64_t)n0 * hw) / OW);
+    const int kb = (int)(k0 >> 5), tap = kb / cblocks, c0 = (kb - tap * cblocks) * 32;
+    const int kh = tap / KW, kw = tap - kh * KW;
+    load4(dst, map, c0, kw - PW, oh0 + kh - PH, n0, bar);
+  }
+};
+
+// MN-major operand of the per-tap weight gradient over a channels-last tensor:
+// tile rows = channels, k = output pixels (n, oh, ow), 32 per k-block.  Batch
+// index b = tap; with `shift` the pixel reads move by the tap offset (the
+// input x), without it they do not (the output gradient dy).  Map dims
+// (C, W, H, N), box (32, OW, rows, images) covering 32 pixels.
+struct SrcPixMN {
+  static constexpr bool kMN = true;
+  int OH, OW, KW, PH, PW, shift;
+  template <int ROWS>
+  __device__ __forceinline__ void issue(const CUtensorMap* map, uint32_t dst, uint64_t* bar, int b, int64_t r0,
+                                        int64_t k0) const {
+    const int64_t hw = (int64_t)OH * OW;
+    const int n0 = (int)(k0 / hw), oh0 = (int)((k0 - (int64_t)n0 * hw) / OW);
+    int dh = 0, dw = 0;
+    if (shift) {
+      dh = b / KW - PH;
+      dw = b - (b / KW) * KW - PW;
+    }
+#pragma unroll
+    for (int j = 0; j < ROWS / 32; ++j) load4(dst + j * 4096, map, (int)r0 + 32 * j, dw, oh0 + dh, n0, bar);
+  }
+};
+
+template <int BN, int STAGES>
+struct Smem {
+  static constexpr uint32_t A_BYTES = BM * BK * 4;
+  static constexpr uint32_t B_BYTES = BN * BK * 4;
+  static constexpr uint32_t HI = A_BYTES + B_BYTES;  // raw (then hi) A and B of one stage
+  static constexpr uint32_t STAGE = 2 * HI;          // + lo A and B
+  static constexpr uint32_t TILES = STAGES * STAGE;
+  static constexpr uint32_t BYTES = TILES + 256 + 1024;
+  static constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
+  static_assert(STAGE % 1024 == 0, "stages must keep 1 KB swizzle alignment");
+};
+
+template <class SA, class SB, class EP, int BN, int STAGES>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    k_gemm_tma(const __grid_constant__ CUtensorMap ma, const __grid_constant__ CUtensorMap mb, SA sa, SB sb, EP ep,
+               int64_t M, int64_t N, int64_t K, int64_t k_per_split, int splits, float* __restrict__ ws) {
+  using S = Smem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::TILES);
+  uint64_t* ready = full + STAGES;
+  uint64_t* empty = ready + STAGES;
+  uint64_t* done = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t m0 = (int64_t)blockIdx.x * BM, n0 = (int64_t)blockIdx.y * BN;
+  const int b = (int)(blockIdx.z / splits), split = (int)(blockIdx.z % splits);
+  const int64_t kb0 = (int64_t)split * k_per_split;
+  const int64_t kend = kb0 + k_per_split < K ? kb0 + k_per_split : K;
+  const int nk = kend > kb0 ? (int)((kend - kb0 + BK - 1) / BK) : 0;
+
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&ready[s], NSPLIT);
+      tc::mbar_init(&empty[s], 1);
+    }
+    tc::mbar_init(done, 1);
+    tc::fence_barrier_init();
+  }
+  if (warp == MMA_WARP) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     tc::smem_u32(tmem_slot)),
+                 "r"((uint32_t)S::TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool ok = true;
+
+  if (warp == TMA_WARP) {
+    if (lane == 0) {
+      int last[STAGES];
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) last[s] = -1;
+      for (int kb = 0; kb < nk && ok; ++kb) {
+        const int s = kb % STAGES;
+        ok = tc::mbar_wait(&empty[s], (uint32_t)((kb / STAGES) & 1) ^ 1u, 11);
+        if (!ok) break;
+        const uint32_t st = tc::smem_u32(smem + s * S::STAGE);
+        const int64_t k0 = kb0 + (int64_t)kb * BK;
+        expect_tx(&full[s], S::HI);
+        sa.template issue<BM>(&ma, st, &full[s], b, m0, k0);
+        sb.template issue<BN>(&mb, st + S::A_BYTES, &full[s], b, n0, k0);
+        last[s] = kb;
+      }
+      // no box may still be landing when the CTA exits
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s)
+        if (last[s] >= 0) tc::mbar_wait(&full[s], (uint32_t)((last[s] / STAGES) & 1), 12);
+    }
+  } else if (warp == MMA_WARP) {
+    if (lane == 0) {
+      const uint32_t idesc = tc::idesc_tf32<BN>() | ((uint32_t)SA::kMN << 15) | ((uint32_t)SB::kMN << 16);
+      for (int kb = 0; kb < nk && ok; ++kb) {
+        const int s = kb % STAGES;
+        ok = tc::mbar_wait(&ready[s], (uint32_t)((kb / STAGES) & 1), 13);
+        if (!ok) break;
+        tc::tc_fence_after();
+        const uint32_t base = tc::smem_u32(smem + s * S::STAGE);
+        const uint32_t a_hi = base, b_hi = base + S::A_BYTES, a_lo = base + S::HI, b_lo = base + S::HI + S::A_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < BK / 8; ++kk) {
+          // k-step of 8: +32 B inside a K-major row, +1 KB (8 rows) when MN-major
+          const uint32_t da = SA::kMN ? kk * 1024 : kk * 32, db = SB::kMN ? kk * 1024 : kk * 32;
+          const uint64_t ah = SA::kMN ? mn_desc(a_hi + da) : tc::sw128_desc(a_hi + da);
+          const uint64_t al = SA::kMN ? mn_desc(a_lo + da) : tc::sw128_desc(a_lo + da);
+          const uint64_t bh = SB::kMN ? mn_desc(b_hi + db) : tc::sw128_desc(b_hi + db);
+          const uint64_t bl = SB::kMN ? mn_desc(b_lo + db) : tc::sw128_desc(b_lo + db);
+          tc::mma_tf32(tmem, ah, bh, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          tc::mma_tf32(tmem, ah, bl, idesc, 1u);
+          tc::mma_tf32(tmem, al, bh, idesc, 1u);
+        }
+        tc::mma_commit(&empty[s]);
+      }
+      tc::mma_commit(done);
+    }
+  } else {
+    // ---- splitters: x -> (hi in place, lo beside it) ----
+    for (int kb = 0; kb < nk && ok; ++kb) {
+      const int s = kb % STAGES;
+      ok = tc::mbar_wait(&full[s], (uint32_t)((kb / STAGES) & 1), 14);
+      if (!ok) break;
+      float4* hi = reinterpret_cast<float4*>(smem + s * S::STAGE);
+      float4* lo = hi + S::HI / 16;
+#pragma unroll
+      for (int i = tid; i < (int)(S::HI / 16); i += NSPLIT) {
+        float4 v = hi[i], h, l;
+        tc::split_tf32(v.x, h.x, l.x);
+        tc::split_tf32(v.y, h.y, l.y);
+        tc::split_tf32(v.z, h.z, l.z);
+        tc::split_tf32(v.w, h.w, l.w);
+        hi[i] = h;
+        lo[i] = l;
+      }
+      tc::fence_proxy_async();
+      tc::mbar_arrive(&ready[s]);
+    }
+  }
+  __syncwarp();
+
+  // ---- epilogue: warps 0-7; TMEM lane quadrant warp%4 = tile rows, column half warp/4 ----
+  if (warp < 8) {
+    bool fin = nk > 0 && tc::mbar_wait(done, 0, 15);
+    bool have = __all_sync(0xffffffffu, ok && fin);
+    tc::tc_fence_after();
+    const int q = warp & 3, h = warp >> 2;
+    const int64_t m = m0 + q * 32 + lane;
+    constexpr int HALF = BN / 2;
+#pragma unroll 1
+    for (int c0 = h * HALF; c0 < (h + 1) * HALF; c0 += 16) {
+      float v[16];
+      if (have) {
+        tc::tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = 0.0f;
+      }
+      if (m < M && (have || nk == 0)) {
+        if (splits > 1) {
+          float* w = ws + (((int64_t)b * splits + split) * M + m) * N;
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (n0 + c0 + i < N) w[n0 + c0 + i] = v[i];
+        } else {
+          ep.row16(b, m, n0 + c0, N, v);
+        }
+      }
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == MMA_WARP) {
+    tc::tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)S::TMEM_COLS));
+  }
+}
+
+}  // namespace tma
+
+template <class SA, class SB, class EP, int BN, int STAGES>
+void gemm_tma_launch(const CUtensorMap& ma, const CUtensorMap& mb, const SA& sa, const SB& sb, const EP& ep,
+                     int64_t M, int64_t N, int64_t K, int batch) {
+  using S = tma::Smem<BN, STAGES>;
+  int64_t gm = (M + tma::BM - 1) / tma::BM, gn = (N + BN - 1) / BN;
+  TP_REQUIRE(gn <= 65535 && gm <= 0x7fffffff, "gemm: tile grid exceeds the launch limits");
+  auto kfn = tma::k_gemm_tma<SA, SB, EP, BN, STAGES>;
+  static bool attr = false;
+  if (!attr) {
+    TP_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::BYTES));
+    attr = true;
+  }
+  int splits = gemm_splits(gm * gn * batch, K, sm_count());
+  int64_t kps = (K + splits - 1) / splits;
+  kps = (kps + tma::BK - 1) / tma::BK * tma::BK;
+  splits = K > 0 ? (int)((K + kps - 1) / kps) : 1;
+  TP_REQUIRE((int64_t)batch * splits <= 65535, "gemm: batch x splits exceeds the grid limit");
+  float* ws = nullptr;
+  if (splits > 1) ws = (float*)scratch((size_t)batch * splits * M * N * sizeof(float));
+  TP_LAUNCH(kfn, dim3((unsigned)gm, (unsigned)gn, (unsigned)(batch * splits)), tma::NTHREADS, S::BYTES, ma, mb, sa,
+            sb, ep, M, N, K, kps, splits, ws);
+  if (splits > 1) {
+    auto rfn = tc::k_splitk_reduce_b<EP>;
+    unsigned gx = (unsigned)((M * N + 255) / 256);
+    if (gx > 1024) gx = 1024;
+    TP_LAUNCH(rfn, dim3(gx, (unsigned)batch), 256, 0, ws, splits, M, N, ep);
+  }
+}
+
+}  // namespace tp

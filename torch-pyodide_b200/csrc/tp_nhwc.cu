@@ -1,0 +1,347 @@
+// Channels-last ([pixels][C]) companions of the NCHW norm / pool / bias
+// kernels, for a training step that keeps its activations channels-last:
+// BatchNorm train forward (+ReLU) and backward (+ReLU mask), the per-channel
+// sum (conv bias gradient), 2x2 / stride-2 max pooling with indices, and the
+// NCHW -> channels-last input conversion.
+//
+// Same arithmetic as the NCHW kernels in tp_norm.cu / tp_pool.cu (which follow
+// the reference's intended BatchNorm training semantics, tensor_nn_ops.py:92-254
+// and autograd_rules.py:1049-1130, and max_pool2d.wgsl:22-49): f64 partial
+// sums per channel combined in a fixed order by the same finishing kernels,
+// identical per-element formulas, strict > with row-major window order for
+// the pool.  Only the memory order differs: channels are contiguous, so every
+// kernel moves 16-byte vectors of 4 channels and a per-channel reduction is a
+// column reduction over pixel rows.
+#include <cuda_runtime.h>
+
+#include "tp_core.h"
+#include "tp_launch.h"
+
+namespace tp {
+
+__global__ void k_bn_finish(const double* __restrict__ part, int64_t C, int splits, double M, float eps,
+                            float momentum, float* __restrict__ save_mean, float* __restrict__ save_invstd,
+                            float* __restrict__ rm, float* __restrict__ rv);
+__global__ void k_bn_bwd_finish(const double* __restrict__ part, int64_t C, int splits, double M,
+                                const float* __restrict__ w, const float* __restrict__ invstd,
+                                float* __restrict__ coef, float* __restrict__ dw, float* __restrict__ db);
+__global__ void k_channel_sum_finish(const double* __restrict__ part, int64_t C, int splits, float* __restrict__ out);
+
+// ---- column reductions over [P][C] ----------------------------------------------------------
+// Thread t: channel group g = t % G (4 channels, G = C/4), row lane r = t / G;
+// CTA `split` covers rows [p0, p1).  Per-thread f64 sums are combined over row
+// lanes in shared memory in lane order, giving part[(c*splits + split)*2 + {0,1}]
+// (the layout the finishing kernels read).
+
+struct ColStatsF {  // a += x, b += x*x
+  const float* x;
+  __device__ __forceinline__ void acc(int64_t i4, int, double (&a)[4], double (&b)[4]) const {
+    float4 v = reinterpret_cast<const float4*>(x)[i4];
+    a[0] += v.x, a[1] += v.y, a[2] += v.z, a[3] += v.w;
+    b[0] += (double)v.x * v.x, b[1] += (double)v.y * v.y, b[2] += (double)v.z * v.z, b[3] += (double)v.w * v.w;
+  }
+};
+
+struct ColSumF {  // a += x
+  const float* x;
+  __device__ __forceinline__ void acc(int64_t i4, int, double (&a)[4], double (&)[4]) const {
+    float4 v = reinterpret_cast<const float4*>(x)[i4];
+    a[0] += v.x, a[1] += v.y, a[2] += v.z, a[3] += v.w;
+  }
+};
+
+struct ColBnBwdF {  // g = dy masked by relu_src > 0; a += g, b += g * x_hat
+  const float* dy;
+  const float* x;
+  const float* relu_src;
+  const float* mean;
+  const float* invstd;
+  __device__ __forceinline__ void acc(int64_t i4, int c0, double (&a)[4], double (&b)[4]) const {
+    float4 g = reinterpret_cast<const float4*>(dy)[i4];
+    float4 xv = reinterpret_cast<const float4*>(x)[i4];
+    if (relu_src) {
+      float4 r = reinterpret_cast<const float4*>(relu_src)[i4];
+      if (!(r.x > 0.0f)) g.x = 0.0f;
+      if (!(r.y > 0.0f)) g.y = 0.0f;
+      if (!(r.z > 0.0f)) g.z = 0.0f;
+      if (!(r.w > 0.0f)) g.w = 0.0f;
+    }
+    a[0] += g.x, a[1] += g.y, a[2] += g.z, a[3] += g.w;
+    b[0] += (double)g.x * ((xv.x - mean[c0]) * invstd[c0]);
+    b[1] += (double)g.y * ((xv.y - mean[c0 + 1]) * invstd[c0 + 1]);
+    b[2] += (double)g.z * ((xv.z - mean[c0 + 2]) * invstd[c0 + 2]);
+    b[3] += (double)g.w * ((xv.w - mean[c0 + 3]) * invstd[c0 + 3]);
+  }
+};
+
+constexpr int COL_THREADS = 256;
+
+template <class F>
+__global__ void __launch_bounds__(COL_THREADS) k_col_reduce(F f, int64_t P, int C, int64_t rows_per_split,
+                                                            int splits, double* __restrict__ part) {
+  extern __shared__ double sh[];  // [R][C][2]
+  const int G = C >> 2, R = COL_THREADS / G;
+  const int t = threadIdx.x, g = t % G, r = t / G;
+  const int split = blockIdx.x;
+  const int64_t p0 = (int64_t)split * rows_per_split;
+  const int64_t p1 = p0 + rows_per_split < P ? p0 + rows_per_split : P;
+  double a[4] = {0.0, 0.0, 0.0, 0.0}, b[4] = {0.0, 0.0, 0.0, 0.0};
+  if (r < R)
+    for (int64_t p = p0 + r; p < p1; p += R) f.acc(p * G + g, 4 * g, a, b);
+  if (r < R) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      sh[((int64_t)r * C + 4 * g + j) * 2] = a[j];
+      sh[((int64_t)r * C + 4 * g + j) * 2 + 1] = b[j];
+    }
+  }
+  __syncthreads();
+  for (int c = t; c < C; c += COL_THREADS) {
+    double sa = 0.0, sb = 0.0;
+    for (int k = 0; k < R; ++k) {
+      sa += sh[((int64_t)k * C + c) * 2];
+      sb += sh[((int64_t)k * C + c) * 2 + 1];
+    }
+    part[((int64_t)c * splits + split) * 2] = sa;
+    part[((int64_t)c * splits + split) * 2 + 1] = sb;
+  }
+}
+
+// Row splits: a few waves of CTAs, each with >= 64 rows per row lane.
+static int col_splits(int64_t P, int C) {
+  const int R = COL_THREADS / (C / 4);
+  int64_t want = (int64_t)sm_count() * 4;
+  int64_t maxs = P / ((int64_t)R * 64);
+  if (maxs < 1) maxs = 1;
+  return (int)(want < maxs ? want : maxs);
+}
+
+template <class F>
+static double* col_reduce(const F& f, int64_t P, int C, int& splits) {
+  TP_REQUIRE(C % 4 == 0 && C >= 4 && C <= 4 * COL_THREADS, "channels-last reduction needs C %% 4 == 0, C <= %d",
+             4 * COL_THREADS);
+  splits = col_splits(P, C);
+  int64_t rows = (P + splits - 1) / splits;
+  splits = (int)((P + rows - 1) / rows);
+  if (splits < 1) splits = 1;
+  double* part = (double*)scratch((size_t)C * splits * 2 * sizeof(double) + (size_t)C * 3 * sizeof(float) + 64);
+  const int R = COL_THREADS / (C / 4);
+  size_t shb = (size_t)R * C * 2 * sizeof(double);
+  auto kfn = k_col_reduce<F>;
+  TP_LAUNCH(kfn, (unsigned)splits, COL_THREADS, shb, f, P, C, rows, splits, part);
+  return part;
+}
+
+// ---- element-wise passes (float4 over 4 consecutive channels) ---------------------------------
+
+__global__ void k_bn_apply_nhwc(const float4* __restrict__ x, const float* __restrict__ mean,
+                                const float* __restrict__ invstd, const float* __restrict__ w,
+                                const float* __restrict__ b, float4* __restrict__ y, int64_t n4, int G, int relu) {
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
+    const int c = 4 * (int)(i % G);
+    float4 v = x[i];
+    float r[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float wt = w ? w[c + j] : 1.0f, bs = b ? b[c + j] : 0.0f;
+      r[j] = (r[j] - mean[c + j]) * (invstd[c + j] * wt) + bs;
+      if (relu) r[j] = fmaxf(r[j], 0.0f);
+    }
+    y[i] = make_float4(r[0], r[1], r[2], r[3]);
+  }
+}
+
+__global__ void k_bn_bwd_apply_nhwc(const float4* __restrict__ dy, const float4* __restrict__ x,
+                                    const float4* __restrict__ relu_src, const float* __restrict__ mean,
+                                    const float* __restrict__ invstd, const float* __restrict__ coef,
+                                    float4* __restrict__ dx, int64_t n4, int G) {
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
+    const int c = 4 * (int)(i % G);
+    float4 gv = dy[i], xv = x[i];
+    float g[4] = {gv.x, gv.y, gv.z, gv.w}, xs[4] = {xv.x, xv.y, xv.z, xv.w}, o[4];
+    if (relu_src) {
+      float4 rv = relu_src[i];
+      float rs[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (!(rs[j] > 0.0f)) g[j] = 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float xh = (xs[j] - mean[c + j]) * invstd[c + j];
+      o[j] = coef[(c + j) * 3] * (g[j] - coef[(c + j) * 3 + 1] - xh * coef[(c + j) * 3 + 2]);
+    }
+    dx[i] = make_float4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// 2x2 windows, stride 2: one thread per (n, oh, ow, 4 channels).  idx holds the
+// plane offset h*W + w of the maximum (the NCHW kernels' index), visiting the
+// window row-major with strict >.
+__global__ void k_maxpool2x2_nhwc_fwd(const float4* __restrict__ x, float4* __restrict__ y, int4* __restrict__ idx,
+                                      int64_t n4, int H, int W, int G) {
+  const int OH = H >> 1, OW = W >> 1;
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
+    const int g = (int)(i % G);
+    int64_t t = i / G;
+    const int ow = (int)(t % OW);
+    t /= OW;
+    const int oh = (int)(t % OH);
+    const int64_t n = t / OH;
+    float m[4] = {-3.402823e+38f, -3.402823e+38f, -3.402823e+38f, -3.402823e+38f};
+    int mi[4] = {-1, -1, -1, -1};
+#pragma unroll
+    for (int kh = 0; kh < 2; ++kh)
+#pragma unroll
+      for (int kw = 0; kw < 2; ++kw) {
+        const int h = 2 * oh + kh, w = 2 * ow + kw;
+        float4 v = x[((n * H + h) * W + w) * G + g];
+        float vs[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (vs[j] > m[j]) {
+            m[j] = vs[j];
+            mi[j] = h * W + w;
+          }
+      }
+    y[i] = make_float4(m[0], m[1], m[2], m[3]);
+    if (idx) idx[i] = make_int4(mi[0], mi[1], mi[2], mi[3]);
+  }
+}
+
+__global__ void k_maxpool2x2_nhwc_bwd(const float4* __restrict__ gy, const int4* __restrict__ idx,
+                                      float4* __restrict__ gx, int64_t n4, int H, int W, int G) {
+  const int OH = H >> 1, OW = W >> 1;
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
+    const int g = (int)(i % G);
+    int64_t t = i / G;
+    const int ow = (int)(t % OW);
+    t /= OW;
+    const int oh = (int)(t % OH);
+    const int64_t n = t / OH;
+    float4 v = gy[i];
+    int4 ix = idx[i];
+#pragma unroll
+    for (int kh = 0; kh < 2; ++kh)
+#pragma unroll
+      for (int kw = 0; kw < 2; ++kw) {
+        const int h = 2 * oh + kh, w = 2 * ow + kw, me = h * W + w;
+        gx[((n * H + h) * W + w) * G + g] =
+            make_float4(ix.x == me ? v.x : 0.0f, ix.y == me ? v.y : 0.0f, ix.z == me ? v.z : 0.0f,
+                        ix.w == me ? v.w : 0.0f);
+      }
+  }
+}
+
+// NCHW [N][C][H][W] -> channels-last [N][H][W][Cp], channels C..Cp-1 zero.
+__global__ void k_nchw_to_nhwc(const float* __restrict__ x, float* __restrict__ y, int64_t N, int C, int64_t HW,
+                               int Cp) {
+  int64_t total = N * HW * Cp;
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int c = (int)(i % Cp);
+    const int64_t t = i / Cp, p = t % HW, n = t / HW;
+    y[i] = c < C ? x[(n * C + c) * HW + p] : 0.0f;
+  }
+}
+
+static void check_vec(const void* p, const char* what) {
+  TP_REQUIRE(((uintptr_t)p & 15) == 0, "%s: channels-last buffers must be 16-byte aligned", what);
+}
+
+}  // namespace tp
+
+using namespace tp;
+
+extern "C" {
+
+TP_API int tpk_bn_train_nhwc(const float* x, const float* w, const float* b, float* running_mean,
+                             float* running_var, float* y, float* save_mean, float* save_invstd, int64_t P, int64_t C,
+                             float eps, float momentum, int relu) {
+  return guard([&] {
+    TP_REQUIRE(P > 1, "batch_norm training needs more than one value per channel");
+    check_vec(x, "batch_norm");
+    check_vec(y, "batch_norm");
+    int splits = 1;
+    double* part = col_reduce(ColStatsF{x}, P, (int)C, splits);
+    TP_LAUNCH(k_bn_finish, (unsigned)((C + 127) / 128), 128, 0, part, C, splits, (double)P, eps, momentum,
+              save_mean, save_invstd, running_mean, running_var);
+    int64_t n4 = P * C / 4;
+    TP_LAUNCH(k_bn_apply_nhwc, grid_for(n4, 256), 256, 0, reinterpret_cast<const float4*>(x), save_mean,
+              save_invstd, w, b, reinterpret_cast<float4*>(y), n4, (int)(C / 4), relu ? 1 : 0);
+  });
+}
+
+TP_API int tpk_bn_backward_nhwc(const float* dy, const float* x, const float* relu_src, const float* w,
+                                const float* mean, const float* invstd, float* dx, float* dw, float* db, int64_t P,
+                                int64_t C) {
+  return guard([&] {
+    check_vec(dy, "batch_norm backward");
+    check_vec(x, "batch_norm backward");
+    check_vec(dx, "batch_norm backward");
+    if (relu_src) check_vec(relu_src, "batch_norm backward");
+    int splits = 1;
+    double* part = col_reduce(ColBnBwdF{dy, x, relu_src, mean, invstd}, P, (int)C, splits);
+    float* coef = (float*)((char*)part + (((size_t)C * splits * 2 * sizeof(double) + 15) & ~(size_t)15));
+    TP_LAUNCH(k_bn_bwd_finish, (unsigned)((C + 127) / 128), 128, 0, part, C, splits, (double)P, w, invstd, coef,
+              dw, db);
+    int64_t n4 = P * C / 4;
+    TP_LAUNCH(k_bn_bwd_apply_nhwc, grid_for(n4, 256), 256, 0, reinterpret_cast<const float4*>(dy),
+              reinterpret_cast<const float4*>(x), reinterpret_cast<const float4*>(relu_src), mean, invstd, coef,
+              reinterpret_cast<float4*>(dx), n4, (int)(C / 4));
+  });
+}
+
+TP_API int tpk_channel_sum_nhwc(const float* x, int64_t P, int64_t C, float* out) {
+  return guard([&] {
+    check_vec(x, "channel sum");
+    int splits = 1;
+    double* part = col_reduce(ColSumF{x}, P, (int)C, splits);
+    TP_LAUNCH(k_channel_sum_finish, (unsigned)((C + 127) / 128), 128, 0, part, C, splits, out);
+  });
+}
+
+TP_API int tpk_maxpool2x2_nhwc_fwd(const float* x, float* y, int32_t* idx, int64_t N, int64_t H, int64_t W,
+                                   int64_t C) {
+  return guard([&] {
+    TP_REQUIRE(H % 2 == 0 && W % 2 == 0 && C % 4 == 0 && H * W < ((int64_t)1 << 31),
+               "2x2 max-pool (channels-last) needs even H, W and C %% 4 == 0");
+    check_vec(x, "max_pool2d");
+    check_vec(y, "max_pool2d");
+    if (idx) check_vec(idx, "max_pool2d");
+    int64_t n4 = N * (H / 2) * (W / 2) * C / 4;
+    if (n4 == 0) return;
+    TP_LAUNCH(k_maxpool2x2_nhwc_fwd, grid_for(n4, 256), 256, 0, reinterpret_cast<const float4*>(x),
+              reinterpret_cast<float4*>(y), reinterpret_cast<int4*>(idx), n4, (int)H, (int)W, (int)(C / 4));
+  });
+}
+
+TP_API int tpk_maxpool2x2_nhwc_bwd(const float* dy, const int32_t* idx, float* dx, int64_t N, int64_t H, int64_t W,
+                                   int64_t C) {
+  return guard([&] {
+    TP_REQUIRE(H % 2 == 0 && W % 2 == 0 && C % 4 == 0 && H * W < ((int64_t)1 << 31),
+               "2x2 max-pool (channels-last) needs even H, W and C %% 4 == 0");
+    check_vec(dy, "max_pool2d backward");
+    check_vec(idx, "max_pool2d backward");
+    check_vec(dx, "max_pool2d backward");
+    int64_t n4 = N * (H / 2) * (W / 2) * C / 4;
+    if (n4 == 0) return;
+    TP_LAUNCH(k_maxpool2x2_nhwc_bwd, grid_for(n4, 256), 256, 0, reinterpret_cast<const float4*>(dy),
+              reinterpret_cast<const int4*>(idx), reinterpret_cast<float4*>(dx), n4, (int)H, (int)W, (int)(C / 4));
+  });
+}
+
+TP_API int tpk_nchw_to_nhwc(const float* x, float* y, int64_t N, int64_t C, int64_t H, int64_t W, int64_t Cpad) {
+  return guard([&] {
+    TP_REQUIRE(Cpad >= C && C > 0, "nchw_to_nhwc: padded channel count below C");
+    int64_t total = N * H * W * Cpad;
+    if (total == 0) return;
+    TP_LAUNCH(k_nchw_to_nhwc, grid_for(total, 256), 256, 0, x, y, N, (int)C, H * W, (int)Cpad);
+  });
+}
+
+}  // extern "C"

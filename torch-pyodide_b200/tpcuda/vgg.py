@@ -16,6 +16,15 @@ fused kernels on preallocated HBM buffers:
             as each block's gradients are final); one fused SGD-momentum launch
             over all parameters with the 1/world averaging folded in
 
+Activations are channels-last ([N][H][W][C], layout="nhwc", the default):
+each implicit-GEMM tile of the convolutions is then one TMA box, and the
+norm / pool passes move 16-byte vectors of 4 channels.  The input batch
+arrives NCHW and is converted on the device into a channels-last buffer whose
+3 channels are zero-padded to 32 (one k-block of the tensor-core kernel); the
+first conv's filters are stored with the same padding, their padded channels
+stay exactly zero (zero input, zero gradient, zero decay).  layout="nchw" runs
+the same step on the NCHW kernels of the per-op API, as a cross-check.
+
 The whole step is captured once into a CUDA graph and replayed.  Semantics:
 PyTorch's (SGD momentum 0.9 with weight decay 5e-4, dampening 0; BN momentum
 0.1, eps 1e-5, unbiased running variance), which is what the reference's
@@ -58,10 +67,15 @@ def plan_blocks(cfg=CFG, in_ch: int = 3, size: int = 32) -> list[dict]:
     return blocks
 
 
-def plan_params(blocks: list[dict], feat: int) -> tuple[list, dict, int]:
+CIN0_PAD = 32  # channels of the first conv's input as stored channels-last
+
+
+def plan_params(blocks: list[dict], feat: int, cin0_store: int = 3) -> tuple[list, dict, int]:
     """Parameter specs (name, shape, init) in the order backward finishes
-    them (fc first, conv1 last), their (offset, numel) in the flat buffers
-    (each tensor starts on a 256-byte boundary) and the flat length."""
+    them (fc first, conv1 last), their (offset, stored numel) in the flat
+    buffers (each tensor starts on a 256-byte boundary) and the flat length.
+    The first conv's filters are stored as [Cout][cin0_store][3][3] (input
+    channels zero-padded when cin0_store > 3)."""
     specs = []
     specs.append(("fc.w", [NUM_CLASSES, feat], ("kaiming", feat)))
     specs.append(("fc.b", [NUM_CLASSES], ("bias", feat)))
@@ -75,25 +89,40 @@ def plan_params(blocks: list[dict], feat: int) -> tuple[list, dict, int]:
     offsets = {}
     off = 0
     for name, shape, _ in specs:
-        n = int(np.prod(shape))
+        n = int(np.prod(store_shape(name, shape, cin0_store)))
         offsets[name] = (off, n)
         off += (n + 63) // 64 * 64
     return specs, offsets, off
 
 
-def init_params(specs: list, offsets: dict, flat_len: int, seed: int) -> np.ndarray:
+def store_shape(name: str, shape: list, cin0_store: int) -> list:
+    """Stored shape of a parameter (the first conv's filters may be padded)."""
+    if name == "conv0.w" and cin0_store != shape[1]:
+        return [shape[0], cin0_store, shape[2], shape[3]]
+    return list(shape)
+
+
+def init_params(specs: list, offsets: dict, flat_len: int, seed: int, cin0_store: int = 3) -> np.ndarray:
     """The flat parameter buffer on the host: PyTorch's default Conv2d/Linear
     init (kaiming_uniform_ with a=sqrt(5), i.e. U(+-1/sqrt(fan_in)), for
-    weights and biases), BN gamma 1 and beta 0; padding zero."""
+    weights and biases), BN gamma 1 and beta 0; padding zero.  The values do
+    not depend on the storage padding."""
     rng = np.random.default_rng(seed)
     host = np.zeros(flat_len, np.float32)
-    for name, _, init in specs:
-        o, n = offsets[name]
+    for name, shape, init in specs:
+        o, n_store = offsets[name]
+        n = int(np.prod(shape))
         if init[0] in ("kaiming", "bias"):
             bound = 1.0 / math.sqrt(init[1])
-            host[o:o + n] = rng.uniform(-bound, bound, n)
+            v = rng.uniform(-bound, bound, n).astype(np.float32)
         else:
-            host[o:o + n] = init[1]
+            v = np.full(n, init[1], np.float32)
+        st = store_shape(name, shape, cin0_store)
+        if st != list(shape):
+            w = np.zeros(st, np.float32)
+            w[:, :shape[1]] = v.reshape(shape)
+            v = w.ravel()
+        host[o:o + n_store] = v
     return host
 
 
@@ -123,7 +152,12 @@ class VGG11BN:
     """Buffers, parameters and the step sequence of VGG-11-BN on 32x32 inputs."""
 
     def __init__(self, rt, batch: int, seed: int = 0, lr: float = 0.05, momentum: float = 0.9,
-                 weight_decay: float = 5e-4, world: int = 1, comm=None, bucket_bytes: int = 8 << 20):
+                 weight_decay: float = 5e-4, world: int = 1, comm=None, bucket_bytes: int = 8 << 20,
+                 layout: str = "nhwc"):
+        if layout not in ("nhwc", "nchw"):
+            raise ValueError(f"layout must be 'nhwc' or 'nchw', got {layout!r}")
+        self.layout = layout
+        self.cin0 = CIN0_PAD if layout == "nhwc" else 3
         self.rt, self.lib = rt, rt.lib
         self.B = int(batch)
         self.lr, self.momentum, self.wd = lr, momentum, weight_decay
@@ -141,13 +175,13 @@ class VGG11BN:
         # ---- parameters, gradients, momentum: one flat buffer each, laid out in
         # the order backward finishes them so gradient buckets close in
         # backward order ----
-        specs, self.offsets, self.flat_len = plan_params(self.blocks, self.feat)
+        specs, self.offsets, self.flat_len = plan_params(self.blocks, self.feat, self.cin0)
         self.param_specs = specs
         self.nparams = sum(int(np.prod(s)) for _, s, _ in specs)
         self.params = self._alloc(self.flat_len * 4)
         self.grads = self._alloc(self.flat_len * 4)
         self.moms = self._alloc(self.flat_len * 4)
-        self._h2d(self.params, init_params(specs, self.offsets, self.flat_len, seed))
+        self._h2d(self.params, init_params(specs, self.offsets, self.flat_len, seed, self.cin0))
         check(self.lib.tp_memset(_vp(self.grads), 0, self.flat_len * 4))
         check(self.lib.tp_memset(_vp(self.moms), 0, self.flat_len * 4))
 
@@ -163,9 +197,11 @@ class VGG11BN:
 
         # ---- activations ----
         Bn = self.B
-        self.x = self._alloc(Bn * 3 * 32 * 32 * 4)
+        self.x = self._alloc(Bn * 3 * 32 * 32 * 4)  # the batch as it arrives (NCHW)
         self.y = self._alloc(Bn * 4)
-        max_act = 0
+        # first conv input: channels-last, zero-padded channels (NCHW: the batch itself)
+        self.x0 = self._alloc(Bn * self.cin0 * 32 * 32 * 4) if layout == "nhwc" else self.x
+        max_act = Bn * self.cin0 * 32 * 32
         for b in self.blocks:
             n = Bn * b["cout"] * b["H"] * b["W"]
             max_act = max(max_act, n, Bn * b["cin"] * b["H"] * b["W"])
@@ -221,17 +257,28 @@ class VGG11BN:
     def _forward(self) -> None:
         L = self.lib
         Bn = self.B
-        x = self.x
+        nhwc = self.layout == "nhwc"
+        if nhwc:
+            check(L.tpk_nchw_to_nhwc(_vp(self.x), _vp(self.x0), Bn, 3, 32, 32, self.cin0))
+        x = self.x0
         for li, b in enumerate(self.blocks):
             C, H, W = b["cout"], b["H"], b["W"]
-            check(L.tpk_conv2d_fwd(_vp(x), _vp(self.p(f"conv{li}.w")), _vp(self.p(f"conv{li}.b")), _vp(b["z"]), Bn,
-                                   b["cin"], H, W, C, 3, 3, 1, 1, 1, 1))
-            check(L.tpk_bn_train(_vp(b["z"]), _vp(self.p(f"bn{li}.g")), _vp(self.p(f"bn{li}.b")), _vp(b["rm"]),
-                                 _vp(b["rv"]), _vp(b["a"]), _vp(b["mean"]), _vp(b["invstd"]), Bn, C, H * W, 1e-5,
-                                 0.1, 1))
-            if b["pool"]:
-                check(L.tpk_maxpool_fwd(_vp(b["a"]), _vp(b["p"]), _vp(b["idx"]), Bn, C, H, W, 2, 2, 0))
+            cin = self.cin0 if li == 0 else b["cin"]
+            w, bias = _vp(self.p(f"conv{li}.w")), _vp(self.p(f"conv{li}.b"))
+            gam, bet = _vp(self.p(f"bn{li}.g")), _vp(self.p(f"bn{li}.b"))
+            stats = (_vp(b["rm"]), _vp(b["rv"]), _vp(b["a"]), _vp(b["mean"]), _vp(b["invstd"]))
+            if nhwc:
+                check(L.tpk_conv2d_fwd_nhwc(_vp(x), w, bias, _vp(b["z"]), Bn, cin, H, W, C, 3, 3, 1, 1))
+                check(L.tpk_bn_train_nhwc(_vp(b["z"]), gam, bet, *stats, Bn * H * W, C, 1e-5, 0.1, 1))
+                if b["pool"]:
+                    check(L.tpk_maxpool2x2_nhwc_fwd(_vp(b["a"]), _vp(b["p"]), _vp(b["idx"]), Bn, H, W, C))
+            else:
+                check(L.tpk_conv2d_fwd(_vp(x), w, bias, _vp(b["z"]), Bn, cin, H, W, C, 3, 3, 1, 1, 1, 1))
+                check(L.tpk_bn_train(_vp(b["z"]), gam, bet, *stats, Bn, C, H * W, 1e-5, 0.1, 1))
+                if b["pool"]:
+                    check(L.tpk_maxpool_fwd(_vp(b["a"]), _vp(b["p"]), _vp(b["idx"]), Bn, C, H, W, 2, 2, 0))
             x = b["out"]
+        # the last block ends at 1x1, where both layouts are [B][512]
         self.feat_ptr = x
         check(L.tpk_gemm(_vp(x), 0, _vp(self.p("fc.w")), 1, _vp(self.logits), Bn, NUM_CLASSES, self.feat,
                          _vp(self.p("fc.b"))))
@@ -246,6 +293,7 @@ class VGG11BN:
     def _backward(self) -> None:
         L = self.lib
         Bn = self.B
+        nhwc = self.layout == "nhwc"
         check(L.tpk_cross_entropy_backward(_vp(self.logits), _vp(self.y), _vp(self.dlogits), Bn, NUM_CLASSES,
                                            1.0 / Bn))
         check(L.tpk_gemm(_vp(self.dlogits), 1, _vp(self.feat_ptr), 0, _vp(self.g("fc.w")), NUM_CLASSES, self.feat,
@@ -259,27 +307,39 @@ class VGG11BN:
         for li in reversed(range(len(self.blocks))):
             b = self.blocks[li]
             C, H, W = b["cout"], b["H"], b["W"]
+            P = Bn * H * W
+            cin = self.cin0 if li == 0 else b["cin"]
             if b["pool"]:
                 da = self.gbuf[buf]
                 buf ^= 1
-                check(L.tpk_maxpool_bwd(_vp(gout), _vp(b["idx"]), _vp(da), Bn, C, H, W, 2, 2, 0))
+                if nhwc:
+                    check(L.tpk_maxpool2x2_nhwc_bwd(_vp(gout), _vp(b["idx"]), _vp(da), Bn, H, W, C))
+                else:
+                    check(L.tpk_maxpool_bwd(_vp(gout), _vp(b["idx"]), _vp(da), Bn, C, H, W, 2, 2, 0))
             else:
                 da = gout
             dz = self.gbuf[buf]
             buf ^= 1
-            check(L.tpk_bn_backward(_vp(da), _vp(b["z"]), _vp(b["a"]), _vp(self.p(f"bn{li}.g")), _vp(b["mean"]),
-                                    _vp(b["invstd"]), _vp(dz), _vp(self.g(f"bn{li}.g")), _vp(self.g(f"bn{li}.b")), Bn,
-                                    C, H * W))
-            check(L.tpk_channel_sum(_vp(dz), Bn, C, H * W, _vp(self.g(f"conv{li}.b"))))
-            xin = self.x if li == 0 else self.blocks[li - 1]["out"]
-            check(L.tpk_conv2d_wgrad(_vp(dz), _vp(xin), _vp(self.g(f"conv{li}.w")), Bn, b["cin"], H, W, C, 3, 3, 1,
-                                     1, 1, 1))
+            bn_args = (_vp(da), _vp(b["z"]), _vp(b["a"]), _vp(self.p(f"bn{li}.g")), _vp(b["mean"]), _vp(b["invstd"]),
+                       _vp(dz), _vp(self.g(f"bn{li}.g")), _vp(self.g(f"bn{li}.b")))
+            xin = self.x0 if li == 0 else self.blocks[li - 1]["out"]
+            w, dw, db = _vp(self.p(f"conv{li}.w")), _vp(self.g(f"conv{li}.w")), _vp(self.g(f"conv{li}.b"))
+            if nhwc:
+                check(L.tpk_bn_backward_nhwc(*bn_args, P, C))
+                check(L.tpk_channel_sum_nhwc(_vp(dz), P, C, db))
+                check(L.tpk_conv2d_wgrad_nhwc(_vp(dz), _vp(xin), dw, Bn, cin, H, W, C, 3, 3, 1, 1))
+            else:
+                check(L.tpk_bn_backward(*bn_args, Bn, C, H * W))
+                check(L.tpk_channel_sum(_vp(dz), Bn, C, H * W, db))
+                check(L.tpk_conv2d_wgrad(_vp(dz), _vp(xin), dw, Bn, cin, H, W, C, 3, 3, 1, 1, 1, 1))
             self._reduce(f"blk{li}")
             if li > 0:
                 dx = self.gbuf[buf]
                 buf ^= 1
-                check(L.tpk_conv2d_dgrad(_vp(dz), _vp(self.p(f"conv{li}.w")), _vp(dx), Bn, b["cin"], H, W, C, 3, 3, 1,
-                                         1, 1, 1))
+                if nhwc:
+                    check(L.tpk_conv2d_dgrad_nhwc(_vp(dz), w, _vp(dx), Bn, cin, H, W, C, 3, 3, 1, 1))
+                else:
+                    check(L.tpk_conv2d_dgrad(_vp(dz), w, _vp(dx), Bn, cin, H, W, C, 3, 3, 1, 1, 1, 1))
                 gout = dx
 
     def _update(self) -> None:
@@ -326,9 +386,31 @@ class VGG11BN:
         check(self.lib.tp_memcpy_d2h(out.ctypes.data_as(ctypes.c_void_p), _vp(ptr), n * 4))
         return out
 
-    def param_array(self, name: str) -> np.ndarray:
+    def _logical(self, base: int, name: str) -> np.ndarray:
         o, n = self.offsets[name]
-        return self.read(self.params + 4 * o, n)
+        v = self.read(base + 4 * o, n)
+        shape = dict((nm, s) for nm, s, _ in self.param_specs)[name]
+        st = store_shape(name, shape, self.cin0)
+        if st != list(shape):
+            v = np.ascontiguousarray(v.reshape(st)[:, :shape[1]]).ravel()
+        return v
+
+    def param_array(self, name: str) -> np.ndarray:
+        """Parameter `name` in its logical (reference) layout."""
+        return self._logical(self.params, name)
+
+    def grad_array(self, name: str) -> np.ndarray:
+        """Gradient of `name` from the last step, logical layout."""
+        return self._logical(self.grads, name)
+
+    def activation(self, ptr: int, C: int, H: int, W: int, dtype=np.float32) -> np.ndarray:
+        """A [B][C][H][W] activation (or int32 pool index) read back as NCHW."""
+        n = self.B * C * H * W
+        out = np.zeros(n, dtype)
+        check(self.lib.tp_memcpy_d2h(out.ctypes.data_as(ctypes.c_void_p), _vp(ptr), out.nbytes))
+        if self.layout == "nhwc":
+            return np.ascontiguousarray(out.reshape(self.B, H, W, C).transpose(0, 3, 1, 2))
+        return out.reshape(self.B, C, H, W)
 
     def close(self) -> None:
         if self.graph is not None:
