@@ -325,9 +325,11 @@ TP_API int tpk_conv2d_wgrad_nhwc(const float* dy, const float* x, float* dw, int
 TP_API int tpk_bn_train_nhwc(const float* x, const float* w, const float* b, float* running_mean,
                              float* running_var, float* y, float* save_mean, float* save_invstd, int64_t P, int64_t C,
                              float eps, float momentum, int relu);
+/* dx_sum (optional): the per-channel sum of dx, which is the gradient of a
+ * bias added just before the BatchNorm (the conv bias), from the same pass */
 TP_API int tpk_bn_backward_nhwc(const float* dy, const float* x, const float* relu_src, const float* w,
-                                const float* mean, const float* invstd, float* dx, float* dw, float* db, int64_t P,
-                                int64_t C);
+                                const float* mean, const float* invstd, float* dx, float* dw, float* db,
+                                float* dx_sum, int64_t P, int64_t C);
 TP_API int tpk_channel_sum_nhwc(const float* x, int64_t P, int64_t C, float* out);
 TP_API int tpk_maxpool2x2_nhwc_fwd(const float* x, float* y, int32_t* idx, int64_t N, int64_t H, int64_t W,
                                    int64_t C);

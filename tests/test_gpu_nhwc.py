@@ -44,9 +44,16 @@ def test_bn_nhwc_matches_nchw(cuda_rt, n, c, hw):
         else:
             assert L.tpk_bn_train_nhwc(vp(px), vp(pg), vp(pb), vp(rm), vp(rv), vp(y), vp(mean), vp(inv), P, c, 1e-5,
                                        0.1, 1) == 0
+            dxs = empty(rt, c)
             assert L.tpk_bn_backward_nhwc(vp(pdy), vp(px), vp(y), vp(pg), vp(mean), vp(inv), vp(dx), vp(dg), vp(db),
-                                          P, c) == 0
+                                          vp(dxs), P, c) == 0
             assert L.tpk_channel_sum_nhwc(vp(pdy), P, c, vp(cs)) == 0
+            dxn = nchw(read(rt, dx, (n, hw, hw, c)))
+            # the fused per-channel sum of dx equals a separate sum of dx
+            got_sum = read(rt, dxs, (c,)).astype(np.float64)
+            want_sum = dxn.astype(np.float64).sum(axis=(0, 2, 3))
+            assert np.max(np.abs(got_sum - want_sum)) <= 1e-4 * max(1.0, float(np.max(np.abs(dxn)))) * 8
+            free(rt, dxs)
             back = lambda p: nchw(read(rt, p, (n, hw, hw, c)))  # noqa: E731
         outs[lay] = {"y": back(y), "dx": back(dx), "mean": read(rt, mean, (c,)), "inv": read(rt, inv, (c,)),
                      "rm": read(rt, rm, (c,)), "rv": read(rt, rv, (c,)), "dg": read(rt, dg, (c,)),

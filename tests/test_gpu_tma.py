@@ -97,9 +97,10 @@ def test_matmul_handle_tma_long_k(cuda_rt, oracle_rt):
     assert status(cuda_rt) == 0
 
 
-# (Cin, Cout, H=W) of every VGG-11-BN conv, plus shapes off the TMA tiling
-NHWC_SHAPES = [(3, 64, 32), (64, 128, 16), (128, 256, 8), (256, 256, 8), (256, 512, 4), (512, 512, 4),
-               (512, 512, 2), (32, 64, 6), (48, 96, 8)]
+# (Cin, Cout, H=W) of every VGG-11-BN conv (the first with its input padded to 4
+# channels too), plus shapes off the TMA tiling
+NHWC_SHAPES = [(3, 64, 32), (4, 64, 32), (4, 16, 7), (64, 128, 16), (128, 256, 8), (256, 256, 8), (256, 512, 4),
+               (512, 512, 4), (512, 512, 2), (32, 64, 6), (48, 96, 8)]
 
 
 def nchw(a):
@@ -144,7 +145,7 @@ def test_conv_nhwc_matches_nchw(cuda_rt, engine, cin, cout, hw, batch):
         close64(got, ref.astype(np.float64), rel=1e-5)
 
 
-@pytest.mark.parametrize("cin,cout,hw,batch", [(64, 128, 16, 4), (256, 256, 8, 8), (3, 64, 32, 2)])
+@pytest.mark.parametrize("cin,cout,hw,batch", [(64, 128, 16, 4), (256, 256, 8, 8), (3, 64, 32, 2), (4, 64, 32, 2)])
 def test_conv_nhwc_against_oracle(cuda_rt, oracle_rt, cin, cout, hw, batch):
     rt, orc = cuda_rt, oracle_rt
     rng = np.random.default_rng(cin * cout + hw)

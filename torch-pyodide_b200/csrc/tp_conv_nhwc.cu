@@ -10,9 +10,10 @@
 // the shifted x as MN-major boxes.  Filters and filter gradients stay in the
 // reference layout [Cout][Cin][KH][KW]; filters are repacked per call.
 //
-// Shapes the TMA tiling cannot express (channels not a multiple of 32, pixel
-// grids that 128 / 32 pixel boxes do not tile) run on gather loaders over the
-// same layout.
+// A 4-channel input (an RGB first layer padded to 4) runs on the CUDA-core
+// kernels of tp_conv_small.cu.  Other shapes the TMA tiling cannot express
+// (channels not a multiple of 32, pixel grids that 128 / 32 pixel boxes do
+// not tile) run on gather loaders over the same layout.
 #include <cuda_runtime.h>
 
 #include "tp_core.h"
@@ -149,11 +150,22 @@ static NhwcShape nhwc_shape(int64_t N, int64_t Cin, int64_t H, int64_t W, int64_
 __global__ void k_pack_filters(const float* __restrict__ w, float* __restrict__ wp, int64_t Cout, int64_t Cin_pg,
                                int khw, int mode);
 
+// tp_conv_small.cu: 4-channel first-layer kernels on the CUDA cores
+bool conv_c4_ok(int64_t Cin, int KH, int KW, int64_t Cout, const void* a, const void* b);
+void conv_c4_fwd(const float* x, const float* w, const float* bias, float* y, int64_t N, int64_t H, int64_t W,
+                 int64_t Cout, int PH, int PW);
+void conv_c4_wgrad(const float* dy, const float* x, float* dw, int64_t N, int64_t H, int64_t W, int64_t Cout, int PH,
+                   int PW);
+
 // y[N][OH][OW][Cout] = conv(x[N][H][W][Cin], w) + bias
 static void conv_fwd_nhwc(const NhwcShape& s, const float* x, const float* w, const float* bias, float* y) {
   const int khw = s.KH * s.KW;
   const int64_t M = s.N * s.OH * s.OW, K = s.Cin * khw;
   if (M == 0) return;
+  if (conv_c4_ok(s.Cin, s.KH, s.KW, s.Cout, x, y) && (bias == nullptr || ((uintptr_t)bias & 15) == 0)) {
+    conv_c4_fwd(x, w, bias, y, s.N, s.H, s.W, s.Cout, s.PH, s.PW);
+    return;
+  }
   float* wp = (float*)scratch2((size_t)s.Cout * K * sizeof(float));
   TP_LAUNCH(k_pack_filters, grid_for(s.Cout * K, 256), 256, 0, w, wp, s.Cout, s.Cin, khw, 0);
   EpRowMajor ep{y, s.Cout, 0, bias, 0};
@@ -202,6 +214,10 @@ static void conv_dgrad_nhwc(const NhwcShape& s, const float* dy, const float* w,
 static void conv_wgrad_nhwc(const NhwcShape& s, const float* dy, const float* x, float* dw) {
   const int khw = s.KH * s.KW;
   const int64_t P = s.N * s.OH * s.OW;
+  if (conv_c4_ok(s.Cin, s.KH, s.KW, s.Cout, x, dy)) {
+    conv_c4_wgrad(dy, x, dw, s.N, s.H, s.W, s.Cout, s.PH, s.PW);
+    return;
+  }
   uint32_t pix[3];
   if (nhwc_tma_ok() && s.Cout >= 64 && P > 0 && pixel_box(s.OH, s.OW, 32, pix) &&
       nhwc_map(nullptr, dy, s.N, s.OH, s.OW, s.Cout, pix, false) &&

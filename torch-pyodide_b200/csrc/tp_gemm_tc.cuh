@@ -242,7 +242,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t m0 = (int64_t)blockIdx.x * BM, n0 = (int64_t)blockIdx.y * BN;
-  const int b = (int)(blockIdx.z / splits), split = (int)(blockIdx.z % splits);
+  // z = split * batch + b: the batches (filter taps) of one k range run side by side and share L2
+  const int batch = (int)(gridDim.z / splits);
+  const int b = (int)(blockIdx.z % batch), split = (int)(blockIdx.z / batch);
   const int64_t kb0 = (int64_t)split * k_per_split;
   const int64_t kend = kb0 + k_per_split < K ? kb0 + k_per_split : K;
   const int nk = kend > kb0 ? (int)((kend - kb0 + BK - 1) / BK) : 0;
@@ -364,15 +366,36 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   }
 }
 
-// Sum the split-K partials of batch b in split order and apply the epilogue.
+// Sum the split-K partials of batch b in split order and apply the epilogue
+// (16-byte partial loads when N % 4 == 0).
 template <class EP>
 __global__ void k_splitk_reduce_b(const float* __restrict__ ws, int splits, int64_t M, int64_t N, EP ep) {
-  int b = blockIdx.y;
-  const float* base = ws + (int64_t)b * splits * M * N;
-  int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < M * N; i += stride) {
+  const int b = blockIdx.y;
+  const int64_t MN = M * N;
+  const float* base = ws + (int64_t)b * splits * MN;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  if ((N & 3) == 0) {
+    const int64_t n4 = MN >> 2;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
+      float4 s = reinterpret_cast<const float4*>(base)[i];
+      for (int z = 1; z < splits; ++z) {
+        float4 v = reinterpret_cast<const float4*>(base + (int64_t)z * MN)[i];
+        s.x += v.x;
+        s.y += v.y;
+        s.z += v.z;
+        s.w += v.w;
+      }
+      const int64_t e = i * 4, m = e / N, n = e - m * N;
+      ep(b, m, n, s.x);
+      ep(b, m, n + 1, s.y);
+      ep(b, m, n + 2, s.z);
+      ep(b, m, n + 3, s.w);
+    }
+    return;
+  }
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < MN; i += stride) {
     float s = 0.0f;
-    for (int z = 0; z < splits; ++z) s += base[(int64_t)z * M * N + i];
+    for (int z = 0; z < splits; ++z) s += base[(int64_t)z * MN + i];
     ep(b, i / N, i % N, s);
   }
 }
@@ -382,19 +405,23 @@ __global__ void k_splitk_reduce_b(const float* __restrict__ ws, int splits, int6
 // Host side: read (and optionally clear) the device status word.
 int tc_status(bool reset);
 
-// Split-K factor shared by the tensor-core launchers: the fewest splits whose
-// CTA count fills the SMs in whole waves (each split keeps >= 8 k-blocks).
-inline int gemm_splits(int64_t tiles, int64_t K, int sms) {
+// Split-K factor shared by the tensor-core launchers: minimise the k-blocks
+// one SM runs (waves x k-blocks per split) plus the split-K partial traffic
+// (each split writes and the reduce reads out_elems floats; one unit ~ one
+// k-block of time per ~0.7 M floats of the whole GPU's traffic), keeping
+// >= 8 k-blocks per split.
+inline int gemm_splits(int64_t tiles, int64_t K, int sms, int64_t out_elems) {
   if (K <= 0 || tiles <= 0) return 1;
-  int64_t maxs = K / 256;
-  if (maxs > 32) maxs = 32;
-  if (maxs <= 1 || tiles >= sms) return 1;
+  const int64_t nk = (K + 31) / 32;
+  int64_t maxs = nk / 8;
+  if (maxs > 64) maxs = 64;
+  if (maxs <= 1) return 1;
   int best = 1;
-  double best_t = 1e30;
+  double best_t = 1e300;
   for (int s = 1; s <= maxs; ++s) {
-    int64_t waves = (tiles * s + sms - 1) / sms;
-    double t = (double)waves / s + 0.02 * s;  // per-split cost: partial writes and the reduce
-    if (t < best_t - 1e-9) {
+    const int64_t waves = (tiles * s + sms - 1) / sms;
+    const double t = (double)waves * (double)((nk + s - 1) / s) + (s > 1 ? 1.4e-6 * (double)out_elems * s : 0.0);
+    if (t < best_t * (1.0 - 1e-9)) {
       best_t = t;
       best = s;
     }
@@ -414,7 +441,7 @@ void gemm_tc_launch(const LA& la, const LB& lb, const EP& ep, int64_t M, int64_t
     attr = true;
   }
   // split K when the tile grid cannot fill the SMs
-  int splits = gemm_splits(gm * gn * batch, K, sm_count());
+  int splits = gemm_splits(gm * gn * batch, K, sm_count(), M * N * batch);
   int64_t kps = (K + splits - 1) / splits;
   kps = (kps + tc::BK - 1) / tc::BK * tc::BK;
   splits = K > 0 ? (int)((K + kps - 1) / kps) : 1;
@@ -425,8 +452,8 @@ void gemm_tc_launch(const LA& la, const LB& lb, const EP& ep, int64_t M, int64_t
             M, N, K, kps, splits, ws);
   if (splits > 1) {
     auto rfn = tc::k_splitk_reduce_b<EP>;
-    unsigned gx = (unsigned)((M * N + 255) / 256);
-    if (gx > 1024) gx = 1024;
+    unsigned gx = (unsigned)((M * N / 4 + 255) / 256 + 1);
+    if (gx > (unsigned)sm_count() * 8) gx = (unsigned)sm_count() * 8;
     TP_LAUNCH(rfn, dim3(gx, (unsigned)batch), 256, 0, ws, splits, M, N, ep);
   }
 }

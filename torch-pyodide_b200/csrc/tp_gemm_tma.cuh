@@ -177,7 +177,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t m0 = (int64_t)blockIdx.x * BM, n0 = (int64_t)blockIdx.y * BN;
-  const int b = (int)(blockIdx.z / splits), split = (int)(blockIdx.z % splits);
+  // z = split * batch + b: the batches (filter taps) of one k range run side by side and share L2
+  const int batch = (int)(gridDim.z / splits);
+  const int b = (int)(blockIdx.z % batch), split = (int)(blockIdx.z / batch);
   const int64_t kb0 = (int64_t)split * k_per_split;
   const int64_t kend = kb0 + k_per_split < K ? kb0 + k_per_split : K;
   const int nk = kend > kb0 ? (int)((kend - kb0 + BK - 1) / BK) : 0;
@@ -325,7 +327,7 @@ void gemm_tma_launch(const CUtensorMap& ma, const CUtensorMap& mb, const SA& sa,
     TP_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::BYTES));
     attr = true;
   }
-  int splits = gemm_splits(gm * gn * batch, K, sm_count());
+  int splits = gemm_splits(gm * gn * batch, K, sm_count(), M * N * batch);
   int64_t kps = (K + splits - 1) / splits;
   kps = (kps + tma::BK - 1) / tma::BK * tma::BK;
   splits = K > 0 ? (int)((K + kps - 1) / kps) : 1;
@@ -336,8 +338,8 @@ void gemm_tma_launch(const CUtensorMap& ma, const CUtensorMap& mb, const SA& sa,
             sb, ep, M, N, K, kps, splits, ws);
   if (splits > 1) {
     auto rfn = tc::k_splitk_reduce_b<EP>;
-    unsigned gx = (unsigned)((M * N + 255) / 256);
-    if (gx > 1024) gx = 1024;
+    unsigned gx = (unsigned)((M * N / 4 + 255) / 256 + 1);
+    if (gx > (unsigned)sm_count() * 8) gx = (unsigned)sm_count() * 8;
     TP_LAUNCH(rfn, dim3(gx, (unsigned)batch), 256, 0, ws, splits, M, N, ep);
   }
 }

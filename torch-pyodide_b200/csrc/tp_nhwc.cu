@@ -7,11 +7,13 @@
 // Same arithmetic as the NCHW kernels in tp_norm.cu / tp_pool.cu (which follow
 // the reference's intended BatchNorm training semantics, tensor_nn_ops.py:92-254
 // and autograd_rules.py:1049-1130, and max_pool2d.wgsl:22-49): f64 partial
-// sums per channel combined in a fixed order by the same finishing kernels,
-// identical per-element formulas, strict > with row-major window order for
-// the pool.  Only the memory order differs: channels are contiguous, so every
-// kernel moves 16-byte vectors of 4 channels and a per-channel reduction is a
-// column reduction over pixel rows.
+// sums per channel combined in a fixed order, identical per-element formulas,
+// strict > with row-major window order for the pool.  Only the memory order
+// differs: channels are contiguous, so every kernel moves 16-byte vectors of 4
+// channels and a per-channel reduction is a column reduction over pixel rows.
+// The BatchNorm backward's normalising pass also sums its output per channel,
+// which is the gradient of the conv bias feeding the BatchNorm, so that bias
+// gradient costs no extra pass over the activations.
 #include <cuda_runtime.h>
 
 #include "tp_core.h"
@@ -19,23 +21,83 @@
 
 namespace tp {
 
-__global__ void k_bn_finish(const double* __restrict__ part, int64_t C, int splits, double M, float eps,
-                            float momentum, float* __restrict__ save_mean, float* __restrict__ save_invstd,
-                            float* __restrict__ rm, float* __restrict__ rv);
-__global__ void k_bn_bwd_finish(const double* __restrict__ part, int64_t C, int splits, double M,
-                                const float* __restrict__ w, const float* __restrict__ invstd,
-                                float* __restrict__ coef, float* __restrict__ dw, float* __restrict__ db);
-__global__ void k_channel_sum_finish(const double* __restrict__ part, int64_t C, int splits, float* __restrict__ out);
+// ---- finishing: one warp per channel sums its splits' f64 partials (lane-strided,
+// then a fixed xor-shuffle tree, so the order is the same on every run) ----------------------
+__device__ __forceinline__ void warp_part_sum(const double* __restrict__ part, int64_t c, int splits, double& a,
+                                              double& b) {
+  const int lane = threadIdx.x & 31;
+  a = 0.0;
+  b = 0.0;
+  for (int k = lane; k < splits; k += 32) {
+    a += part[(c * splits + k) * 2];
+    b += part[(c * splits + k) * 2 + 1];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a += __shfl_xor_sync(0xffffffffu, a, o);
+    b += __shfl_xor_sync(0xffffffffu, b, o);
+  }
+}
+
+// mean, biased var -> inv_std; running stats with the unbiased variance
+// (the formulas of the NCHW finishing kernel in tp_norm.cu)
+__global__ void k_col_bn_finish(const double* __restrict__ part, int64_t C, int splits, double M, float eps,
+                                float momentum, float* __restrict__ save_mean, float* __restrict__ save_invstd,
+                                float* __restrict__ rm, float* __restrict__ rv) {
+  const int64_t c = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (c >= C) return;
+  double s, q;
+  warp_part_sum(part, c, splits, s, q);
+  if ((threadIdx.x & 31) != 0) return;
+  double mean = s / M;
+  double var = q / M - mean * mean;
+  if (var < 0.0) var = 0.0;
+  save_mean[c] = (float)mean;
+  save_invstd[c] = (float)(1.0 / sqrt(var + (double)eps));
+  if (rm) rm[c] = (float)(mean * momentum + (double)rm[c] * (1.0 - momentum));
+  if (rv) rv[c] = (float)(var * M / (M - 1.0) * momentum + (double)rv[c] * (1.0 - momentum));
+}
+
+// coef[c] = {w*invstd, sum_dy/M, sum_dyxh/M}; dw, db
+__global__ void k_col_bn_bwd_finish(const double* __restrict__ part, int64_t C, int splits, double M,
+                                    const float* __restrict__ w, const float* __restrict__ invstd,
+                                    float* __restrict__ coef, float* __restrict__ dw, float* __restrict__ db) {
+  const int64_t c = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (c >= C) return;
+  double a, b;
+  warp_part_sum(part, c, splits, a, b);
+  if ((threadIdx.x & 31) != 0) return;
+  coef[c * 3] = (w ? w[c] : 1.0f) * invstd[c];
+  coef[c * 3 + 1] = (float)(a / M);
+  coef[c * 3 + 2] = (float)(b / M);
+  if (dw) dw[c] = (float)b;
+  if (db) db[c] = (float)a;
+}
+
+__global__ void k_col_sum_finish(const double* __restrict__ part, int64_t C, int splits, float* __restrict__ out) {
+  const int64_t c = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (c >= C) return;
+  double a, b;
+  warp_part_sum(part, c, splits, a, b);
+  if ((threadIdx.x & 31) == 0) out[c] = (float)a;
+}
+
+static unsigned finish_grid(int64_t C) { return (unsigned)((C + 7) / 8); }
 
 // ---- column reductions over [P][C] ----------------------------------------------------------
 // Thread t: channel group g = t % G (4 channels, G = C/4), row lane r = t / G;
 // CTA `split` covers rows [p0, p1).  Per-thread f64 sums are combined over row
-// lanes in shared memory in lane order, giving part[(c*splits + split)*2 + {0,1}]
-// (the layout the finishing kernels read).
+// lanes in shared memory in lane order, giving part[(c*splits + split)*2 + {0,1}].
+
+// Functors: ctx(c0) loads what the thread's 4 channels need once; acc()
+// handles the float4 at index i4.
+struct NoCtx {};
 
 struct ColStatsF {  // a += x, b += x*x
   const float* x;
-  __device__ __forceinline__ void acc(int64_t i4, int, double (&a)[4], double (&b)[4]) const {
+  using Ctx = NoCtx;
+  __device__ __forceinline__ Ctx ctx(int) const { return {}; }
+  __device__ __forceinline__ void acc(int64_t i4, const Ctx&, double (&a)[4], double (&b)[4]) const {
     float4 v = reinterpret_cast<const float4*>(x)[i4];
     a[0] += v.x, a[1] += v.y, a[2] += v.z, a[3] += v.w;
     b[0] += (double)v.x * v.x, b[1] += (double)v.y * v.y, b[2] += (double)v.z * v.z, b[3] += (double)v.w * v.w;
@@ -44,11 +106,24 @@ struct ColStatsF {  // a += x, b += x*x
 
 struct ColSumF {  // a += x
   const float* x;
-  __device__ __forceinline__ void acc(int64_t i4, int, double (&a)[4], double (&)[4]) const {
+  using Ctx = NoCtx;
+  __device__ __forceinline__ Ctx ctx(int) const { return {}; }
+  __device__ __forceinline__ void acc(int64_t i4, const Ctx&, double (&a)[4], double (&)[4]) const {
     float4 v = reinterpret_cast<const float4*>(x)[i4];
     a[0] += v.x, a[1] += v.y, a[2] += v.z, a[3] += v.w;
   }
 };
+
+__device__ __forceinline__ float4 relu_mask(float4 g, const float* relu_src, int64_t i4) {
+  if (relu_src) {
+    float4 r = reinterpret_cast<const float4*>(relu_src)[i4];
+    if (!(r.x > 0.0f)) g.x = 0.0f;
+    if (!(r.y > 0.0f)) g.y = 0.0f;
+    if (!(r.z > 0.0f)) g.z = 0.0f;
+    if (!(r.w > 0.0f)) g.w = 0.0f;
+  }
+  return g;
+}
 
 struct ColBnBwdF {  // g = dy masked by relu_src > 0; a += g, b += g * x_hat
   const float* dy;
@@ -56,21 +131,65 @@ struct ColBnBwdF {  // g = dy masked by relu_src > 0; a += g, b += g * x_hat
   const float* relu_src;
   const float* mean;
   const float* invstd;
-  __device__ __forceinline__ void acc(int64_t i4, int c0, double (&a)[4], double (&b)[4]) const {
-    float4 g = reinterpret_cast<const float4*>(dy)[i4];
-    float4 xv = reinterpret_cast<const float4*>(x)[i4];
-    if (relu_src) {
-      float4 r = reinterpret_cast<const float4*>(relu_src)[i4];
-      if (!(r.x > 0.0f)) g.x = 0.0f;
-      if (!(r.y > 0.0f)) g.y = 0.0f;
-      if (!(r.z > 0.0f)) g.z = 0.0f;
-      if (!(r.w > 0.0f)) g.w = 0.0f;
+  struct Ctx {
+    float mu[4], is[4];
+  };
+  __device__ __forceinline__ Ctx ctx(int c0) const {
+    Ctx c;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      c.mu[j] = mean[c0 + j];
+      c.is[j] = invstd[c0 + j];
     }
+    return c;
+  }
+  __device__ __forceinline__ void acc(int64_t i4, const Ctx& c, double (&a)[4], double (&b)[4]) const {
+    float4 g = relu_mask(reinterpret_cast<const float4*>(dy)[i4], relu_src, i4);
+    float4 xv = reinterpret_cast<const float4*>(x)[i4];
     a[0] += g.x, a[1] += g.y, a[2] += g.z, a[3] += g.w;
-    b[0] += (double)g.x * ((xv.x - mean[c0]) * invstd[c0]);
-    b[1] += (double)g.y * ((xv.y - mean[c0 + 1]) * invstd[c0 + 1]);
-    b[2] += (double)g.z * ((xv.z - mean[c0 + 2]) * invstd[c0 + 2]);
-    b[3] += (double)g.w * ((xv.w - mean[c0 + 3]) * invstd[c0 + 3]);
+    b[0] += (double)g.x * ((xv.x - c.mu[0]) * c.is[0]);
+    b[1] += (double)g.y * ((xv.y - c.mu[1]) * c.is[1]);
+    b[2] += (double)g.z * ((xv.z - c.mu[2]) * c.is[2]);
+    b[3] += (double)g.w * ((xv.w - c.mu[3]) * c.is[3]);
+  }
+};
+
+// dx = coef0 * (g - coef1 - x_hat * coef2) (the NCHW backward's formula),
+// stored; a += dx (the gradient of a bias added before the BatchNorm)
+struct ColBnBwdApplyF {
+  const float* dy;
+  const float* x;
+  const float* relu_src;
+  const float* mean;
+  const float* invstd;
+  const float* coef;
+  float* dx;
+  struct Ctx {
+    float mu[4], is[4], k0[4], k1[4], k2[4];
+  };
+  __device__ __forceinline__ Ctx ctx(int c0) const {
+    Ctx c;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      c.mu[j] = mean[c0 + j];
+      c.is[j] = invstd[c0 + j];
+      c.k0[j] = coef[(c0 + j) * 3];
+      c.k1[j] = coef[(c0 + j) * 3 + 1];
+      c.k2[j] = coef[(c0 + j) * 3 + 2];
+    }
+    return c;
+  }
+  __device__ __forceinline__ void acc(int64_t i4, const Ctx& c, double (&a)[4], double (&)[4]) const {
+    float4 gv = relu_mask(reinterpret_cast<const float4*>(dy)[i4], relu_src, i4);
+    float4 xv = reinterpret_cast<const float4*>(x)[i4];
+    float g[4] = {gv.x, gv.y, gv.z, gv.w}, xs[4] = {xv.x, xv.y, xv.z, xv.w}, o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float xh = (xs[j] - c.mu[j]) * c.is[j];
+      o[j] = c.k0[j] * (g[j] - c.k1[j] - xh * c.k2[j]);
+      a[j] += o[j];
+    }
+    reinterpret_cast<float4*>(dx)[i4] = make_float4(o[0], o[1], o[2], o[3]);
   }
 };
 
@@ -86,9 +205,9 @@ __global__ void __launch_bounds__(COL_THREADS) k_col_reduce(F f, int64_t P, int 
   const int64_t p0 = (int64_t)split * rows_per_split;
   const int64_t p1 = p0 + rows_per_split < P ? p0 + rows_per_split : P;
   double a[4] = {0.0, 0.0, 0.0, 0.0}, b[4] = {0.0, 0.0, 0.0, 0.0};
-  if (r < R)
-    for (int64_t p = p0 + r; p < p1; p += R) f.acc(p * G + g, 4 * g, a, b);
   if (r < R) {
+    const typename F::Ctx cx = f.ctx(4 * g);
+    for (int64_t p = p0 + r; p < p1; p += R) f.acc(p * G + g, cx, a, b);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       sh[((int64_t)r * C + 4 * g + j) * 2] = a[j];
@@ -108,28 +227,35 @@ __global__ void __launch_bounds__(COL_THREADS) k_col_reduce(F f, int64_t P, int 
 }
 
 // Row splits: a few waves of CTAs, each with >= 64 rows per row lane.
-static int col_splits(int64_t P, int C) {
+struct ColPlan {
+  int splits;
+  int64_t rows;
+  size_t part_bytes;  // C * splits * 2 doubles, rounded up to 256 bytes
+};
+
+static ColPlan col_plan(int64_t P, int C) {
+  TP_REQUIRE(C % 4 == 0 && C >= 4 && C <= 4 * COL_THREADS, "channels-last reduction needs C %% 4 == 0, C <= %d",
+             4 * COL_THREADS);
   const int R = COL_THREADS / (C / 4);
   int64_t want = (int64_t)sm_count() * 4;
   int64_t maxs = P / ((int64_t)R * 64);
   if (maxs < 1) maxs = 1;
-  return (int)(want < maxs ? want : maxs);
+  ColPlan pl;
+  int64_t s = want < maxs ? want : maxs;
+  pl.rows = (P + s - 1) / s;
+  if (pl.rows < 1) pl.rows = 1;
+  pl.splits = (int)((P + pl.rows - 1) / pl.rows);
+  if (pl.splits < 1) pl.splits = 1;
+  pl.part_bytes = ((size_t)C * pl.splits * 2 * sizeof(double) + 255) & ~(size_t)255;
+  return pl;
 }
 
 template <class F>
-static double* col_reduce(const F& f, int64_t P, int C, int& splits) {
-  TP_REQUIRE(C % 4 == 0 && C >= 4 && C <= 4 * COL_THREADS, "channels-last reduction needs C %% 4 == 0, C <= %d",
-             4 * COL_THREADS);
-  splits = col_splits(P, C);
-  int64_t rows = (P + splits - 1) / splits;
-  splits = (int)((P + rows - 1) / rows);
-  if (splits < 1) splits = 1;
-  double* part = (double*)scratch((size_t)C * splits * 2 * sizeof(double) + (size_t)C * 3 * sizeof(float) + 64);
+static void col_launch(const F& f, int64_t P, int C, const ColPlan& pl, double* part) {
   const int R = COL_THREADS / (C / 4);
   size_t shb = (size_t)R * C * 2 * sizeof(double);
   auto kfn = k_col_reduce<F>;
-  TP_LAUNCH(kfn, (unsigned)splits, COL_THREADS, shb, f, P, C, rows, splits, part);
-  return part;
+  TP_LAUNCH(kfn, (unsigned)pl.splits, COL_THREADS, shb, f, P, C, pl.rows, pl.splits, part);
 }
 
 // ---- element-wise passes (float4 over 4 consecutive channels) ---------------------------------
@@ -149,31 +275,6 @@ __global__ void k_bn_apply_nhwc(const float4* __restrict__ x, const float* __res
       if (relu) r[j] = fmaxf(r[j], 0.0f);
     }
     y[i] = make_float4(r[0], r[1], r[2], r[3]);
-  }
-}
-
-__global__ void k_bn_bwd_apply_nhwc(const float4* __restrict__ dy, const float4* __restrict__ x,
-                                    const float4* __restrict__ relu_src, const float* __restrict__ mean,
-                                    const float* __restrict__ invstd, const float* __restrict__ coef,
-                                    float4* __restrict__ dx, int64_t n4, int G) {
-  int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
-    const int c = 4 * (int)(i % G);
-    float4 gv = dy[i], xv = x[i];
-    float g[4] = {gv.x, gv.y, gv.z, gv.w}, xs[4] = {xv.x, xv.y, xv.z, xv.w}, o[4];
-    if (relu_src) {
-      float4 rv = relu_src[i];
-      float rs[4] = {rv.x, rv.y, rv.z, rv.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        if (!(rs[j] > 0.0f)) g[j] = 0.0f;
-    }
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float xh = (xs[j] - mean[c + j]) * invstd[c + j];
-      o[j] = coef[(c + j) * 3] * (g[j] - coef[(c + j) * 3 + 1] - xh * coef[(c + j) * 3 + 2]);
-    }
-    dx[i] = make_float4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -266,10 +367,11 @@ TP_API int tpk_bn_train_nhwc(const float* x, const float* w, const float* b, flo
     TP_REQUIRE(P > 1, "batch_norm training needs more than one value per channel");
     check_vec(x, "batch_norm");
     check_vec(y, "batch_norm");
-    int splits = 1;
-    double* part = col_reduce(ColStatsF{x}, P, (int)C, splits);
-    TP_LAUNCH(k_bn_finish, (unsigned)((C + 127) / 128), 128, 0, part, C, splits, (double)P, eps, momentum,
-              save_mean, save_invstd, running_mean, running_var);
+    ColPlan pl = col_plan(P, (int)C);
+    double* part = (double*)scratch(pl.part_bytes);
+    col_launch(ColStatsF{x}, P, (int)C, pl, part);
+    TP_LAUNCH(k_col_bn_finish, finish_grid(C), 256, 0, part, C, pl.splits, (double)P, eps, momentum, save_mean,
+              save_invstd, running_mean, running_var);
     int64_t n4 = P * C / 4;
     TP_LAUNCH(k_bn_apply_nhwc, grid_for(n4, 256), 256, 0, reinterpret_cast<const float4*>(x), save_mean,
               save_invstd, w, b, reinterpret_cast<float4*>(y), n4, (int)(C / 4), relu ? 1 : 0);
@@ -277,31 +379,32 @@ TP_API int tpk_bn_train_nhwc(const float* x, const float* w, const float* b, flo
 }
 
 TP_API int tpk_bn_backward_nhwc(const float* dy, const float* x, const float* relu_src, const float* w,
-                                const float* mean, const float* invstd, float* dx, float* dw, float* db, int64_t P,
-                                int64_t C) {
+                                const float* mean, const float* invstd, float* dx, float* dw, float* db,
+                                float* dx_sum, int64_t P, int64_t C) {
   return guard([&] {
     check_vec(dy, "batch_norm backward");
     check_vec(x, "batch_norm backward");
     check_vec(dx, "batch_norm backward");
     if (relu_src) check_vec(relu_src, "batch_norm backward");
-    int splits = 1;
-    double* part = col_reduce(ColBnBwdF{dy, x, relu_src, mean, invstd}, P, (int)C, splits);
-    float* coef = (float*)((char*)part + (((size_t)C * splits * 2 * sizeof(double) + 15) & ~(size_t)15));
-    TP_LAUNCH(k_bn_bwd_finish, (unsigned)((C + 127) / 128), 128, 0, part, C, splits, (double)P, w, invstd, coef,
-              dw, db);
-    int64_t n4 = P * C / 4;
-    TP_LAUNCH(k_bn_bwd_apply_nhwc, grid_for(n4, 256), 256, 0, reinterpret_cast<const float4*>(dy),
-              reinterpret_cast<const float4*>(x), reinterpret_cast<const float4*>(relu_src), mean, invstd, coef,
-              reinterpret_cast<float4*>(dx), n4, (int)(C / 4));
+    ColPlan pl = col_plan(P, (int)C);
+    char* ws = (char*)scratch(2 * pl.part_bytes + (((size_t)C * 3 * sizeof(float) + 255) & ~(size_t)255));
+    double* part = (double*)ws;
+    double* part2 = (double*)(ws + pl.part_bytes);
+    float* coef = (float*)(ws + 2 * pl.part_bytes);
+    col_launch(ColBnBwdF{dy, x, relu_src, mean, invstd}, P, (int)C, pl, part);
+    TP_LAUNCH(k_col_bn_bwd_finish, finish_grid(C), 256, 0, part, C, pl.splits, (double)P, w, invstd, coef, dw, db);
+    col_launch(ColBnBwdApplyF{dy, x, relu_src, mean, invstd, coef, dx}, P, (int)C, pl, part2);
+    if (dx_sum) TP_LAUNCH(k_col_sum_finish, finish_grid(C), 256, 0, part2, C, pl.splits, dx_sum);
   });
 }
 
 TP_API int tpk_channel_sum_nhwc(const float* x, int64_t P, int64_t C, float* out) {
   return guard([&] {
     check_vec(x, "channel sum");
-    int splits = 1;
-    double* part = col_reduce(ColSumF{x}, P, (int)C, splits);
-    TP_LAUNCH(k_channel_sum_finish, (unsigned)((C + 127) / 128), 128, 0, part, C, splits, out);
+    ColPlan pl = col_plan(P, (int)C);
+    double* part = (double*)scratch(pl.part_bytes);
+    col_launch(ColSumF{x}, P, (int)C, pl, part);
+    TP_LAUNCH(k_col_sum_finish, finish_grid(C), 256, 0, part, C, pl.splits, out);
   });
 }
 

@@ -20,9 +20,10 @@ Activations are channels-last ([N][H][W][C], layout="nhwc", the default):
 each implicit-GEMM tile of the convolutions is then one TMA box, and the
 norm / pool passes move 16-byte vectors of 4 channels.  The input batch
 arrives NCHW and is converted on the device into a channels-last buffer whose
-3 channels are zero-padded to 32 (one k-block of the tensor-core kernel); the
-first conv's filters are stored with the same padding, their padded channels
-stay exactly zero (zero input, zero gradient, zero decay).  layout="nchw" runs
+3 channels are zero-padded to 4 (one 16-byte vector per pixel, the form the
+first layer's CUDA-core kernels read); the first conv's filters are stored
+with the same padding, their padded channel stays exactly zero (zero input,
+zero gradient, zero decay).  layout="nchw" runs
 the same step on the NCHW kernels of the per-op API, as a cross-check.
 
 The whole step is captured once into a CUDA graph and replayed.  Semantics:
@@ -67,7 +68,7 @@ def plan_blocks(cfg=CFG, in_ch: int = 3, size: int = 32) -> list[dict]:
     return blocks
 
 
-CIN0_PAD = 32  # channels of the first conv's input as stored channels-last
+CIN0_PAD = 4  # channels of the first conv's input as stored channels-last
 
 
 def plan_params(blocks: list[dict], feat: int, cin0_store: int = 3) -> tuple[list, dict, int]:
@@ -325,8 +326,8 @@ class VGG11BN:
             xin = self.x0 if li == 0 else self.blocks[li - 1]["out"]
             w, dw, db = _vp(self.p(f"conv{li}.w")), _vp(self.g(f"conv{li}.w")), _vp(self.g(f"conv{li}.b"))
             if nhwc:
-                check(L.tpk_bn_backward_nhwc(*bn_args, P, C))
-                check(L.tpk_channel_sum_nhwc(_vp(dz), P, C, db))
+                # the conv bias gradient (the per-channel sum of dz) comes out of the BN backward pass
+                check(L.tpk_bn_backward_nhwc(*bn_args, db, P, C))
                 check(L.tpk_conv2d_wgrad_nhwc(_vp(dz), _vp(xin), dw, Bn, cin, H, W, C, 3, 3, 1, 1))
             else:
                 check(L.tpk_bn_backward(*bn_args, Bn, C, H * W))
