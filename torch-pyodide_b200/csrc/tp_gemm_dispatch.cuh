@@ -40,7 +40,7 @@ void gemm_tma_bn(const CUtensorMap& ma, const CUtensorMap& mb, const SA& sa, con
                  int64_t N, int64_t K, int batch) {
   if (N <= 32) gemm_tma_launch<SA, SB, EP, 32, 4>(ma, mb, sa, sb, ep, M, N, K, batch);
   else if (N <= 64) gemm_tma_launch<SA, SB, EP, 64, 4>(ma, mb, sa, sb, ep, M, N, K, batch);
-  else gemm_tma_launch<SA, SB, EP, 128, 3>(ma, mb, sa, sb, ep, M, N, K, batch);
+  else gemm_tma_launch<SA, SB, EP, 128, 4>(ma, mb, sa, sb, ep, M, N, K, batch);
 }
 
 inline uint32_t tma_bn(int64_t N) { return N <= 32 ? 32u : (N <= 64 ? 64u : 128u); }

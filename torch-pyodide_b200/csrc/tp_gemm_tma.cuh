@@ -13,15 +13,20 @@
 // functor, so transposed operands and channels-last convolution operands are
 // read in place.
 //
-// CTA = 320 threads:
+// CTA = 320 threads, one CTA per SM (it allocates all 512 TMEM columns):
 //   warp 9, one lane   TMA producer: waits empty[s], arms full[s] with the
 //                      stage's byte count, issues the A and B boxes
-//   warps 0-7          splitters: wait full[s], rewrite each fp32 in place as
-//                      its tf32-rounded hi and store lo = x - hi beside it,
-//                      fence to the async proxy, arrive on ready[s]; after the
-//                      last k-block they run the epilogue out of TMEM
+//   warps 0-7          splitters: wait full[s]; split each A value into its
+//                      tf32-rounded hi and lo = x - hi and store both into
+//                      TMEM (tcgen05.st; thread = tile row, 16 k each), rewrite
+//                      B in place as hi with lo beside it; fence, arrive on
+//                      ready[s]; after the last k-block they run the epilogue
 //   warp 8             allocates TMEM; one lane issues 3 MMAs per 8-wide
-//                      k-step once ready[s] completes and commits to empty[s]
+//                      k-step, A read from TMEM and B from shared memory, once
+//                      ready[s] completes, and commits to empty[s]
+// With A in TMEM the tensor core reads only B from shared memory, which is
+// what bounds this kernel: per k-block and 128-wide N tile, 144 KB of shared
+// memory traffic instead of 224 KB with both operands there.
 // The split is the same integer rounding as the gather kernel (tp_gemm_tc.cuh)
 // and the MMA sequence is the same, so both kernels produce identical bits for
 // the same tile shape and split-K.
@@ -152,15 +157,65 @@ struct SrcPixMN {
 
 template <int BN, int STAGES>
 struct Smem {
-  static constexpr uint32_t A_BYTES = BM * BK * 4;
+  static constexpr uint32_t A_BYTES = BM * BK * 4;  // raw A (TMA); its hi/lo go to TMEM
   static constexpr uint32_t B_BYTES = BN * BK * 4;
-  static constexpr uint32_t HI = A_BYTES + B_BYTES;  // raw (then hi) A and B of one stage
-  static constexpr uint32_t STAGE = 2 * HI;          // + lo A and B
+  static constexpr uint32_t STAGE = A_BYTES + 2 * B_BYTES;  // raw A | B raw -> hi | B lo
   static constexpr uint32_t TILES = STAGES * STAGE;
-  static constexpr uint32_t BYTES = TILES + 256 + 1024;
-  static constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
+  // at least 120 KB so one CTA holds an SM (it allocates all of TMEM)
+  static constexpr uint32_t BYTES = TILES + 1280 > 122880u ? TILES + 1280 : 122880u;
   static_assert(STAGE % 1024 == 0, "stages must keep 1 KB swizzle alignment");
+  static_assert(STAGES <= 4 && BN <= 256, "TMEM holds the accumulator (256 columns) and 4 A stages");
 };
+
+// TMEM columns: the accumulator at [0, BN); stage s of A at 256 + 64 s (hi: +0..31, lo: +32..63).
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t A_TMEM0 = 256;
+
+__device__ __forceinline__ void mma_tf32_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc,
+                                            uint32_t acc) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(b), "r"(idesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+// 32 lanes x 16 consecutive 32-bit TMEM columns from registers.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+// Values k = k0..k0+15 of tile row r of a raw A tile: K-major 128-byte swizzle
+// (row r: 8 chunks of 16 B at chunk ^ (r & 7)) or MN-major 32-byte-atom
+// swizzle (32-row groups 4 KB apart, one 128-byte row per k, 32-byte chunk
+// ^ (k & 3)).
+template <bool MN>
+__device__ __forceinline__ void read_a16(const uint8_t* tile, int r, int k0, float (&v)[16]) {
+  if constexpr (!MN) {
+    const uint8_t* row = tile + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int chunk = (k0 >> 2) + c;
+      float4 q = *reinterpret_cast<const float4*>(row + ((chunk ^ (r & 7)) << 4));
+      v[4 * c] = q.x;
+      v[4 * c + 1] = q.y;
+      v[4 * c + 2] = q.z;
+      v[4 * c + 3] = q.w;
+    }
+  } else {
+    const uint8_t* grp = tile + (r >> 5) * 4096;
+    const int rr = r & 31;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int k = k0 + i;
+      v[i] = *reinterpret_cast<const float*>(grp + k * 128 + ((((rr >> 3) ^ (k & 3)) << 5) | ((rr & 7) << 2)));
+    }
+  }
+}
 
 template <class SA, class SB, class EP, int BN, int STAGES>
 __global__ void __launch_bounds__(NTHREADS, 1)
@@ -196,7 +251,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   if (warp == MMA_WARP) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      tc::smem_u32(tmem_slot)),
-                 "r"((uint32_t)S::TMEM_COLS));
+                 "r"(TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   tc::tc_fence_before();
@@ -216,7 +271,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (!ok) break;
         const uint32_t st = tc::smem_u32(smem + s * S::STAGE);
         const int64_t k0 = kb0 + (int64_t)kb * BK;
-        expect_tx(&full[s], S::HI);
+        expect_tx(&full[s], S::A_BYTES + S::B_BYTES);
         sa.template issue<BM>(&ma, st, &full[s], b, m0, k0);
         sb.template issue<BN>(&mb, st + S::A_BYTES, &full[s], b, n0, k0);
         last[s] = kb;
@@ -228,40 +283,58 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
   } else if (warp == MMA_WARP) {
     if (lane == 0) {
-      const uint32_t idesc = tc::idesc_tf32<BN>() | ((uint32_t)SA::kMN << 15) | ((uint32_t)SB::kMN << 16);
+      const uint32_t idesc = tc::idesc_tf32<BN>() | ((uint32_t)SB::kMN << 16);
       for (int kb = 0; kb < nk && ok; ++kb) {
         const int s = kb % STAGES;
         ok = tc::mbar_wait(&ready[s], (uint32_t)((kb / STAGES) & 1), 13);
         if (!ok) break;
         tc::tc_fence_after();
         const uint32_t base = tc::smem_u32(smem + s * S::STAGE);
-        const uint32_t a_hi = base, b_hi = base + S::A_BYTES, a_lo = base + S::HI, b_lo = base + S::HI + S::A_BYTES;
+        const uint32_t b_hi = base + S::A_BYTES, b_lo = base + S::A_BYTES + S::B_BYTES;
+        const uint32_t a_hi = tmem + A_TMEM0 + 64 * s, a_lo = a_hi + 32;
 #pragma unroll
         for (int kk = 0; kk < BK / 8; ++kk) {
-          // k-step of 8: +32 B inside a K-major row, +1 KB (8 rows) when MN-major
-          const uint32_t da = SA::kMN ? kk * 1024 : kk * 32, db = SB::kMN ? kk * 1024 : kk * 32;
-          const uint64_t ah = SA::kMN ? mn_desc(a_hi + da) : tc::sw128_desc(a_hi + da);
-          const uint64_t al = SA::kMN ? mn_desc(a_lo + da) : tc::sw128_desc(a_lo + da);
+          // k-step of 8: 8 TMEM columns of A; +32 B inside a K-major B row, +1 KB (8 rows) when MN-major
+          const uint32_t db = SB::kMN ? kk * 1024 : kk * 32;
           const uint64_t bh = SB::kMN ? mn_desc(b_hi + db) : tc::sw128_desc(b_hi + db);
           const uint64_t bl = SB::kMN ? mn_desc(b_lo + db) : tc::sw128_desc(b_lo + db);
-          tc::mma_tf32(tmem, ah, bh, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
-          tc::mma_tf32(tmem, ah, bl, idesc, 1u);
-          tc::mma_tf32(tmem, al, bh, idesc, 1u);
+          mma_tf32_ts(tmem, a_hi + 8 * kk, bh, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          mma_tf32_ts(tmem, a_hi + 8 * kk, bl, idesc, 1u);
+          mma_tf32_ts(tmem, a_lo + 8 * kk, bh, idesc, 1u);
         }
         tc::mma_commit(&empty[s]);
       }
       tc::mma_commit(done);
     }
   } else {
-    // ---- splitters: x -> (hi in place, lo beside it) ----
+    // ---- splitters: A row r = 32*(warp%4) + lane, k half warp/4 -> TMEM hi/lo;
+    //      B in place (hi) and beside it (lo) ----
+    const int r = 32 * (warp & 3) + lane, kh = (warp >> 2) * 16;
+    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
     for (int kb = 0; kb < nk && ok; ++kb) {
       const int s = kb % STAGES;
       ok = tc::mbar_wait(&full[s], (uint32_t)((kb / STAGES) & 1), 14);
       if (!ok) break;
-      float4* hi = reinterpret_cast<float4*>(smem + s * S::STAGE);
-      float4* lo = hi + S::HI / 16;
+      uint8_t* st = smem + s * S::STAGE;
+      {
+        float v[16];
+        uint32_t h[16], l[16];
+        read_a16<SA::kMN>(st, r, kh, v);
 #pragma unroll
-      for (int i = tid; i < (int)(S::HI / 16); i += NSPLIT) {
+        for (int i = 0; i < 16; ++i) {
+          float hf, lf;
+          tc::split_tf32(v[i], hf, lf);
+          h[i] = __float_as_uint(hf);
+          l[i] = __float_as_uint(lf);
+        }
+        const uint32_t col = tmem + lane_base + A_TMEM0 + 64 * s + kh;
+        tmem_st16(col, h);
+        tmem_st16(col + 32, l);
+      }
+      float4* hi = reinterpret_cast<float4*>(st + S::A_BYTES);
+      float4* lo = hi + S::B_BYTES / 16;
+#pragma unroll
+      for (int i = tid; i < (int)(S::B_BYTES / 16); i += NSPLIT) {
         float4 v = hi[i], h, l;
         tc::split_tf32(v.x, h.x, l.x);
         tc::split_tf32(v.y, h.y, l.y);
@@ -270,7 +343,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         hi[i] = h;
         lo[i] = l;
       }
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc::fence_proxy_async();
+      tc::tc_fence_before();
       tc::mbar_arrive(&ready[s]);
     }
   }
@@ -309,7 +384,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   __syncthreads();
   if (warp == MMA_WARP) {
     tc::tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)S::TMEM_COLS));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
   }
 }
 
