@@ -151,7 +151,8 @@ __global__ void k_pack_filters(const float* __restrict__ w, float* __restrict__ 
                                int khw, int mode);
 
 // tp_conv_small.cu: 4-channel first-layer kernels on the CUDA cores
-bool conv_c4_ok(int64_t Cin, int KH, int KW, int64_t Cout, const void* a, const void* b);
+bool conv_c4_ok(int64_t N, int64_t H, int64_t W, int64_t Cin, int KH, int KW, int64_t Cout, const void* a,
+                const void* b);
 void conv_c4_fwd(const float* x, const float* w, const float* bias, float* y, int64_t N, int64_t H, int64_t W,
                  int64_t Cout, int PH, int PW);
 void conv_c4_wgrad(const float* dy, const float* x, float* dw, int64_t N, int64_t H, int64_t W, int64_t Cout, int PH,
@@ -162,7 +163,8 @@ static void conv_fwd_nhwc(const NhwcShape& s, const float* x, const float* w, co
   const int khw = s.KH * s.KW;
   const int64_t M = s.N * s.OH * s.OW, K = s.Cin * khw;
   if (M == 0) return;
-  if (conv_c4_ok(s.Cin, s.KH, s.KW, s.Cout, x, y) && (bias == nullptr || ((uintptr_t)bias & 15) == 0)) {
+  if (conv_c4_ok(s.N, s.H, s.W, s.Cin, s.KH, s.KW, s.Cout, x, y) &&
+      (bias == nullptr || ((uintptr_t)bias & 15) == 0)) {
     conv_c4_fwd(x, w, bias, y, s.N, s.H, s.W, s.Cout, s.PH, s.PW);
     return;
   }
@@ -214,7 +216,7 @@ static void conv_dgrad_nhwc(const NhwcShape& s, const float* dy, const float* w,
 static void conv_wgrad_nhwc(const NhwcShape& s, const float* dy, const float* x, float* dw) {
   const int khw = s.KH * s.KW;
   const int64_t P = s.N * s.OH * s.OW;
-  if (conv_c4_ok(s.Cin, s.KH, s.KW, s.Cout, x, dy)) {
+  if (conv_c4_ok(s.N, s.H, s.W, s.Cin, s.KH, s.KW, s.Cout, x, dy)) {
     conv_c4_wgrad(dy, x, dw, s.N, s.H, s.W, s.Cout, s.PH, s.PW);
     return;
   }

@@ -8,12 +8,9 @@
 // 128-row tiles; a register-tiled CUDA-core kernel that reads each pixel's 4
 // channels as one vector does the real work instead.
 //
-// Forward:  thread = (pixel lane, 4 output channels); filters in shared memory
-//           as float4 over output channels; y = bias + sum_(kh,kw,c) x w.
-// Gradient: thread = (pixel lane, input channel, 4 output channels) with the
-//           9 taps x 4 outputs in registers; per-CTA sums over pixel lanes in
-//           shared memory (fixed order), per-split partials summed in f64 in
-//           split order by a second kernel.
+// Per-CTA sums of the weight gradient are combined over pixel lanes in shared
+// memory in a fixed order and the per-CTA partials in f64 by a second kernel
+// in a fixed order, so the gradient is the same on every run.
 #include <cuda_runtime.h>
 
 #include "tp_core.h"
@@ -22,98 +19,156 @@ namespace tp {
 
 constexpr int SC_THREADS = 256;
 
-template <int KH, int KW>
-__global__ void __launch_bounds__(SC_THREADS)
+// A 16-byte shared-memory load the compiler keeps in place (so filter vectors
+// are re-read per row instead of all 36 being held in registers).
+__device__ __forceinline__ float4 lds4(const float4* p) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"((uint32_t)__cvta_generic_to_shared(p)));
+  return v;
+}
+
+// Forward: thread = (image row lane, CH consecutive output pixels of the row,
+// 4 output channels).  Per filter row kh it loads the CH + 2 input pixels
+// (16-byte vectors) once and reuses each filter vector from shared memory for
+// all CH pixels.
+template <int CH>
+__global__ void __launch_bounds__(SC_THREADS, 2)
     k_conv_c4_fwd(const float4* __restrict__ x, const float* __restrict__ w, const float* __restrict__ bias,
-                  float4* __restrict__ y, int64_t P, int H, int W, int OH, int OW, int PH, int PW, int Cout) {
+                  float4* __restrict__ y, int rows, int H, int W, int OH, int OW, int PH, int PW, int Cout) {
   extern __shared__ float4 wsm[];  // [tap][ci][G]: (w[4g..4g+3][ci][tap])
-  const int G = Cout >> 2, R = SC_THREADS / G;
-  constexpr int T = KH * KW;
-  for (int i = threadIdx.x; i < T * 4 * G; i += blockDim.x) {
+  const int G = Cout >> 2;
+  for (int i = threadIdx.x; i < 9 * 4 * G; i += blockDim.x) {
     const int g = i % G, ci = (i / G) & 3, tap = i / (4 * G);
     float4 v;
-    v.x = w[((4 * g + 0) * 4 + ci) * T + tap];
-    v.y = w[((4 * g + 1) * 4 + ci) * T + tap];
-    v.z = w[((4 * g + 2) * 4 + ci) * T + tap];
-    v.w = w[((4 * g + 3) * 4 + ci) * T + tap];
+    v.x = w[((4 * g + 0) * 4 + ci) * 9 + tap];
+    v.y = w[((4 * g + 1) * 4 + ci) * 9 + tap];
+    v.z = w[((4 * g + 2) * 4 + ci) * 9 + tap];
+    v.w = w[((4 * g + 3) * 4 + ci) * 9 + tap];
     wsm[i] = v;
   }
   __syncthreads();
-  const int g = threadIdx.x % G, r = threadIdx.x / G;
-  if (r >= R) return;
+  const int per_row = (OW / CH) * G, lanes = SC_THREADS / per_row;
+  const int rl = threadIdx.x / per_row, rem = threadIdx.x % per_row, g = rem % G, ow0 = (rem / G) * CH;
+  if (rl >= lanes) return;
   const float4 b4 = bias ? reinterpret_cast<const float4*>(bias)[g] : make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int64_t p = (int64_t)blockIdx.x * R + r; p < P; p += (int64_t)gridDim.x * R) {
-    const int ow = (int)(p % OW);
-    const int64_t t = p / OW;
-    const int oh = (int)(t % OH);
-    const int64_t n = t / OH;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int row = blockIdx.x * lanes + rl; row < rows; row += gridDim.x * lanes) {
+    const int n = row / OH, oh = row - n * OH;
+    float4 acc[CH];
 #pragma unroll
-    for (int kh = 0; kh < KH; ++kh) {
+    for (int p = 0; p < CH; ++p) acc[p] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int kh = 0; kh < 3; ++kh) {
       const int ih = oh + kh - PH;
-      if (ih < 0 || ih >= H) continue;
+      const bool rok = ih >= 0 && ih < H;
+      const float4* xr = x + ((int64_t)n * H + ih) * W;
+      float4 xv[CH + 2];
 #pragma unroll
-      for (int kw = 0; kw < KW; ++kw) {
-        const int iw = ow + kw - PW;
-        if (iw < 0 || iw >= W) continue;
-        const float4 xv = x[(n * H + ih) * W + iw];
-        const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
+      for (int j = 0; j < CH + 2; ++j) {
+        const int iw = ow0 - PW + j;
+        xv[j] = (rok && iw >= 0 && iw < W) ? xr[iw] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int kw = 0; kw < 3; ++kw) {
 #pragma unroll
         for (int ci = 0; ci < 4; ++ci) {
-          const float4 wv = wsm[((kh * KW + kw) * 4 + ci) * G + g];
-          acc.x = fmaf(xs[ci], wv.x, acc.x);
-          acc.y = fmaf(xs[ci], wv.y, acc.y);
-          acc.z = fmaf(xs[ci], wv.z, acc.z);
-          acc.w = fmaf(xs[ci], wv.w, acc.w);
+          const float4 wv = lds4(&wsm[((kh * 3 + kw) * 4 + ci) * G + g]);
+#pragma unroll
+          for (int p = 0; p < CH; ++p) {
+            const float4 q = xv[p + kw];
+            const float xs = ci == 0 ? q.x : (ci == 1 ? q.y : (ci == 2 ? q.z : q.w));
+            acc[p].x = fmaf(xs, wv.x, acc[p].x);
+            acc[p].y = fmaf(xs, wv.y, acc[p].y);
+            acc[p].z = fmaf(xs, wv.z, acc[p].z);
+            acc[p].w = fmaf(xs, wv.w, acc[p].w);
+          }
         }
       }
     }
-    y[p * G + g] = make_float4(acc.x + b4.x, acc.y + b4.y, acc.z + b4.z, acc.w + b4.w);
+    float4* yr = y + ((int64_t)row * OW + ow0) * G + g;
+#pragma unroll
+    for (int p = 0; p < CH; ++p)
+      yr[(int64_t)p * G] = make_float4(acc[p].x + b4.x, acc[p].y + b4.y, acc[p].z + b4.z, acc[p].w + b4.w);
   }
 }
 
-template <int KH, int KW>
+// Weight gradient: thread = (pixel-chunk lane r, input channel ci, 4 output
+// channels); a lane walks OW / R consecutive pixels of each image row with the
+// 3x3 input window in registers, loading one new window column (3 values) and
+// one 16-byte dy vector per pixel.  Rows [row0, row1) per CTA.
 __global__ void __launch_bounds__(SC_THREADS)
-    k_conv_c4_wgrad(const float4* __restrict__ dy, const float* __restrict__ x, float* __restrict__ part, int64_t P,
-                    int H, int W, int OH, int OW, int PH, int PW, int Cout, int64_t rows_per_split) {
-  extern __shared__ float sh[];  // [R][Cout][4][T]
-  constexpr int T = KH * KW;
+    k_conv_c4_wgrad(const float4* __restrict__ dy, const float* __restrict__ x, float* __restrict__ part, int rows,
+                    int H, int W, int OH, int OW, int PH, int PW, int Cout, int rows_per_split) {
+  extern __shared__ float sh[];  // [R][Cout][4][9]
   const int G = Cout >> 2, R = SC_THREADS / (4 * G);
   const int g = threadIdx.x % G, ci = (threadIdx.x / G) & 3, r = threadIdx.x / (4 * G);
-  const int64_t p0 = (int64_t)blockIdx.x * rows_per_split;
-  const int64_t p1 = p0 + rows_per_split < P ? p0 + rows_per_split : P;
-  float acc[T][4];
+  const int chunk = OW / R, ow0 = r * chunk;
+  const int row0 = blockIdx.x * rows_per_split, row1 = min(row0 + rows_per_split, rows);
+  float acc[9][4];
 #pragma unroll
-  for (int t = 0; t < T; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0f;
-  if (r < R) {
-    for (int64_t p = p0 + r; p < p1; p += R) {
-      const int ow = (int)(p % OW);
-      const int64_t q = p / OW;
-      const int oh = (int)(q % OH);
-      const int64_t n = q / OH;
-      const float4 d = dy[p * G + g];
+  for (int t = 0; t < 9; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0f;
+  for (int row = row0; row < row1; ++row) {
+    const int n = row / OH, oh = row - n * OH;
+    const float* xr[3];
+    bool rok[3];
 #pragma unroll
-      for (int kh = 0; kh < KH; ++kh) {
-        const int ih = oh + kh - PH;
+    for (int kh = 0; kh < 3; ++kh) {
+      const int ih = oh + kh - PH;
+      rok[kh] = ih >= 0 && ih < H;
+      xr[kh] = x + (((int64_t)n * H + ih) * W) * 4 + ci;
+    }
+    float win[3][3];
 #pragma unroll
-        for (int kw = 0; kw < KW; ++kw) {
-          const int iw = ow + kw - PW;
-          const float v = (ih >= 0 && ih < H && iw >= 0 && iw < W) ? x[((n * H + ih) * W + iw) * 4 + ci] : 0.0f;
-          const int t = kh * KW + kw;
-          acc[t][0] = fmaf(v, d.x, acc[t][0]);
-          acc[t][1] = fmaf(v, d.y, acc[t][1]);
-          acc[t][2] = fmaf(v, d.z, acc[t][2]);
-          acc[t][3] = fmaf(v, d.w, acc[t][3]);
+    for (int kh = 0; kh < 3; ++kh)
+#pragma unroll
+      for (int kw = 0; kw < 2; ++kw) {
+        const int iw = ow0 - PW + kw;
+        win[kh][kw] = (rok[kh] && iw >= 0 && iw < W) ? xr[kh][iw * 4] : 0.0f;
+      }
+    const float4* dr = dy + (int64_t)row * OW * G + g;
+    // 4 pixels per step with all their loads issued first
+    for (int ow4 = ow0; ow4 < ow0 + chunk; ow4 += 4) {
+      float col[4][3];
+      float4 d[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int iw = ow4 + q - PW + 2;
+#pragma unroll
+        for (int kh = 0; kh < 3; ++kh) col[q][kh] = (rok[kh] && iw >= 0 && iw < W) ? xr[kh][iw * 4] : 0.0f;
+        d[q] = dr[(int64_t)(ow4 + q) * G];
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+#pragma unroll
+        for (int kh = 0; kh < 3; ++kh) win[kh][2] = col[q][kh];
+#pragma unroll
+        for (int kh = 0; kh < 3; ++kh)
+#pragma unroll
+          for (int kw = 0; kw < 3; ++kw) {
+            const float v = win[kh][kw];
+            float* a = acc[kh * 3 + kw];
+            a[0] = fmaf(v, d[q].x, a[0]);
+            a[1] = fmaf(v, d[q].y, a[1]);
+            a[2] = fmaf(v, d[q].z, a[2]);
+            a[3] = fmaf(v, d[q].w, a[3]);
+          }
+#pragma unroll
+        for (int kh = 0; kh < 3; ++kh) {
+          win[kh][0] = win[kh][1];
+          win[kh][1] = win[kh][2];
         }
       }
     }
+  }
+  if (r < R) {
 #pragma unroll
-    for (int t = 0; t < T; ++t)
+    for (int t = 0; t < 9; ++t)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) sh[(((int64_t)r * Cout + 4 * g + j) * 4 + ci) * T + t] = acc[t][j];
+      for (int j = 0; j < 4; ++j) sh[(((int64_t)r * Cout + 4 * g + j) * 4 + ci) * 9 + t] = acc[t][j];
   }
   __syncthreads();
-  const int per = Cout * 4 * T;
+  const int per = Cout * 36;
   for (int i = threadIdx.x; i < per; i += blockDim.x) {
     float s = 0.0f;
     for (int k = 0; k < R; ++k) s += sh[(int64_t)k * per + i];
@@ -121,60 +176,76 @@ __global__ void __launch_bounds__(SC_THREADS)
   }
 }
 
-// dw[i] = sum over splits of part[split][i] (f64, split order); i = (co*4 + ci)*T + tap
+// dw[i] = sum over splits of part[split][i] in f64: each of a block's 8 warps
+// sums a contiguous slice of splits for 32 consecutive i, then the slices are
+// added in slice order (deterministic).  i = (co*4 + ci)*9 + tap
 __global__ void k_conv_c4_wgrad_finish(const float* __restrict__ part, int splits, int per, float* __restrict__ dw) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= per) return;
+  __shared__ double sl[8][32];
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  const int i = blockIdx.x * 32 + lane;
+  const int per_w = (splits + 7) / 8, k0 = wp * per_w, k1 = min(k0 + per_w, splits);
   double s = 0.0;
-  for (int k = 0; k < splits; ++k) s += part[(int64_t)k * per + i];
-  dw[i] = (float)s;
+  if (i < per)
+    for (int k = k0; k < k1; ++k) s += part[(int64_t)k * per + i];
+  sl[wp][lane] = s;
+  __syncthreads();
+  if (wp == 0 && i < per) {
+    double t = 0.0;
+    for (int k = 0; k < 8; ++k) t += sl[k][lane];
+    dw[i] = (float)t;
+  }
 }
 
 // True when the 4-channel kernels apply: x has exactly 4 channels, 3x3
-// filters, Cout % 4 == 0 and <= 256, 16-byte aligned buffers.
-bool conv_c4_ok(int64_t Cin, int KH, int KW, int64_t Cout, const void* a, const void* b) {
-  return Cin == 4 && KH == 3 && KW == 3 && Cout % 4 == 0 && Cout >= 4 && Cout <= 256 &&
-         ((uintptr_t)a & 15) == 0 && ((uintptr_t)b & 15) == 0;
+// filters, 64 <= Cout <= 256 with Cout % 4 == 0, output rows a multiple of 16
+// wide, 16-byte aligned buffers.
+bool conv_c4_ok(int64_t N, int64_t H, int64_t W, int64_t Cin, int KH, int KW, int64_t Cout, const void* a,
+                const void* b) {
+  (void)H;
+  return Cin == 4 && KH == 3 && KW == 3 && Cout % 4 == 0 && Cout >= 64 && Cout <= 256 && W % 16 == 0 && W <= 256 &&
+         ((uintptr_t)a & 15) == 0 && ((uintptr_t)b & 15) == 0 && N * (H + 2) * (W + 2) * Cout < ((int64_t)1 << 31);
 }
 
 void conv_c4_fwd(const float* x, const float* w, const float* bias, float* y, int64_t N, int64_t H, int64_t W,
                  int64_t Cout, int PH, int PW) {
   const int OH = (int)(H + 2 * PH - 2), OW = (int)(W + 2 * PW - 2);
-  const int64_t P = N * OH * OW;
-  if (P == 0) return;
+  const int64_t rows = N * OH;
+  if (rows == 0 || OW <= 0) return;
+  TP_REQUIRE(OW % 8 == 0, "conv2d (4 channels): output width must be a multiple of 8");
   TP_REQUIRE(bias == nullptr || ((uintptr_t)bias & 15) == 0, "conv2d: bias must be 16-byte aligned");
-  const int G = (int)(Cout / 4), R = SC_THREADS / G;
+  const int G = (int)(Cout / 4), per_row = (OW / 8) * G;
+  TP_REQUIRE(per_row <= SC_THREADS, "conv2d (4 channels): row too wide");
+  const int lanes = SC_THREADS / per_row;
   size_t shb = (size_t)9 * 4 * G * sizeof(float4);
-  int64_t blocks = (P + R - 1) / R;
-  int64_t cap = (int64_t)sm_count() * 8;
-  auto kfn = k_conv_c4_fwd<3, 3>;
+  int64_t blocks = (rows + lanes - 1) / lanes;
+  int64_t cap = (int64_t)sm_count() * 4;
+  auto kfn = k_conv_c4_fwd<8>;
   TP_LAUNCH(kfn, (unsigned)(blocks < cap ? blocks : cap), SC_THREADS, shb, reinterpret_cast<const float4*>(x), w,
-            bias, reinterpret_cast<float4*>(y), P, (int)H, (int)W, OH, OW, PH, PW, (int)Cout);
+            bias, reinterpret_cast<float4*>(y), (int)rows, (int)H, (int)W, OH, OW, PH, PW, (int)Cout);
 }
 
 void conv_c4_wgrad(const float* dy, const float* x, float* dw, int64_t N, int64_t H, int64_t W, int64_t Cout, int PH,
                    int PW) {
   const int OH = (int)(H + 2 * PH - 2), OW = (int)(W + 2 * PW - 2);
-  const int64_t P = N * OH * OW;
-  const int per = (int)(Cout * 4 * 9);
+  const int64_t rows = N * OH;
+  const int per = (int)(Cout * 36);
   const int G = (int)(Cout / 4), R = SC_THREADS / (4 * G);
-  int64_t splits = (int64_t)sm_count() * 4;
-  int64_t maxs = P / ((int64_t)R * 64);
-  if (maxs < 1) maxs = 1;
-  if (splits > maxs) splits = maxs;
-  const int64_t rows = (P + splits - 1) / splits;
-  splits = P > 0 ? (P + rows - 1) / rows : 1;
+  TP_REQUIRE(R >= 1 && OW % (4 * R) == 0, "conv2d weight gradient (4 channels): unsupported width");
+  int64_t splits = (int64_t)sm_count() * 2;
+  if (splits > rows) splits = rows;
+  if (splits < 1) splits = 1;
+  const int64_t rps = rows > 0 ? (rows + splits - 1) / splits : 1;
+  splits = rows > 0 ? (rows + rps - 1) / rps : 1;
   float* part = (float*)scratch((size_t)splits * per * sizeof(float));
-  if (P > 0) {
+  if (rows > 0 && OW > 0) {
     size_t shb = (size_t)R * per * sizeof(float);
-    auto kfn = k_conv_c4_wgrad<3, 3>;
-    TP_LAUNCH(kfn, (unsigned)splits, SC_THREADS, shb, reinterpret_cast<const float4*>(dy), x, part, P, (int)H,
-              (int)W, OH, OW, PH, PW, (int)Cout, rows);
+    TP_LAUNCH(k_conv_c4_wgrad, (unsigned)splits, SC_THREADS, shb, reinterpret_cast<const float4*>(dy), x, part,
+              (int)rows, (int)H, (int)W, OH, OW, PH, PW, (int)Cout, (int)rps);
   } else {
     TP_CUDA(cudaMemsetAsync(part, 0, (size_t)per * sizeof(float), stream()));
     splits = 1;
   }
-  TP_LAUNCH(k_conv_c4_wgrad_finish, (unsigned)((per + 255) / 256), 256, 0, part, (int)splits, per, dw);
+  TP_LAUNCH(k_conv_c4_wgrad_finish, (unsigned)((per + 31) / 32), 256, 0, part, (int)splits, per, dw);
 }
 
 }  // namespace tp
