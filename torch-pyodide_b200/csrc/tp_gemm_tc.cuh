@@ -2,8 +2,8 @@
 // accumulator in TMEM and the 3xTF32 split for fp32 accuracy.
 //
 //   C(m, n) = sum_k A(m, k) B(n, k)
-//   x = hi + lo, hi = x rounded to tf32 (10-bit mantissa), lo = x - hi (exact);
-//   a*b ~= ah*bh + ah*bl + al*bh  (the dropped al*bl is ~2^-22 relative)
+//   x = hi + lo, hi = x truncated to tf32 (10-bit mantissa), lo = x - hi (exact);
+//   a*b ~= ah*bh + ah*bl + al*bh  (the dropped al*bl is ~2^-20 relative)
 //
 // CTA = 288 threads.  Warps 0-7 are producers in two groups of four; group g
 // fills the k-blocks kb with kb % 2 == g, so two k-blocks are gathered at once.
@@ -90,11 +90,12 @@ __device__ __forceinline__ void fence_barrier_init() {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// hi = x rounded to the nearest tf32 (ties away from zero: add half an ulp of
-// the 10-bit mantissa, clear the 13 low bits); lo = x - hi, exact in fp32.
+// hi = x with the 13 low mantissa bits cleared, which is the tf32 value the
+// tensor core takes from an fp32 pattern, so an unconverted fp32 operand tile
+// already is its own hi; lo = x - hi, exact in fp32 (|lo| < 2^-10 |x|; the
+// tensor core reads it to 10 bits, so a*b is kept to ~2^-20 relative).
 __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
-  uint32_t u = (__float_as_uint(x) + 0x1000u) & 0xFFFFE000u;
-  hi = __uint_as_float(u);
+  hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
   lo = x - hi;
 }
 

@@ -17,19 +17,22 @@
 //   warp 9, one lane   TMA producer: waits empty[s], arms full[s] with the
 //                      stage's byte count, issues the A and B boxes
 //   warps 0-7          splitters: wait full[s]; split each A value into its
-//                      tf32-rounded hi and lo = x - hi and store both into
-//                      TMEM (tcgen05.st; thread = tile row, 16 k each), rewrite
-//                      B in place as hi with lo beside it; fence, arrive on
-//                      ready[s]; after the last k-block they run the epilogue
+//                      tf32 hi and lo = x - hi and store both into TMEM
+//                      (tcgen05.st; thread = tile row, 16 k each); write B's
+//                      lo beside the raw B tile, which is its own hi (the
+//                      tensor core reads fp32 as tf32 by dropping the 13 low
+//                      mantissa bits); fence, arrive on ready[s]; after the
+//                      last k-block they run the epilogue
 //   warp 8             allocates TMEM; one lane issues 3 MMAs per 8-wide
 //                      k-step, A read from TMEM and B from shared memory, once
 //                      ready[s] completes, and commits to empty[s]
 // With A in TMEM the tensor core reads only B from shared memory, which is
-// what bounds this kernel: per k-block and 128-wide N tile, 144 KB of shared
-// memory traffic instead of 224 KB with both operands there.
-// The split is the same integer rounding as the gather kernel (tp_gemm_tc.cuh)
-// and the MMA sequence is the same, so both kernels produce identical bits for
-// the same tile shape and split-K.
+// what bounds this kernel: per k-block and 128-wide N tile, 128 KB of shared
+// memory traffic (TMA writes 32, splitter reads 32 and writes 16, MMA reads
+// 48) instead of 224 KB with both operands and both halves there.
+// The split is the same as the gather kernel's (tp_gemm_tc.cuh) and the MMA
+// sequence is the same, so both kernels produce identical bits for the same
+// tile shape and split-K.
 //
 // Every wait is bounded (2 s by %globaltimer): on expiry the kernel records a
 // code in tc::g_status, stops issuing, waits (bounded) for the boxes and MMAs
@@ -308,7 +311,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
   } else {
     // ---- splitters: A row r = 32*(warp%4) + lane, k half warp/4 -> TMEM hi/lo;
-    //      B in place (hi) and beside it (lo) ----
+    //      B lo beside the raw B tile ----
     const int r = 32 * (warp & 3) + lane, kh = (warp >> 2) * 16;
     const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
     for (int kb = 0; kb < nk && ok; ++kb) {
@@ -331,8 +334,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         tmem_st16(col, h);
         tmem_st16(col + 32, l);
       }
-      float4* hi = reinterpret_cast<float4*>(st + S::A_BYTES);
-      float4* lo = hi + S::B_BYTES / 16;
+      // B: the raw tile is its own hi (the tensor core truncates fp32 to tf32); only lo is written
+      const float4* hi = reinterpret_cast<const float4*>(st + S::A_BYTES);
+      float4* lo = reinterpret_cast<float4*>(st + S::A_BYTES + S::B_BYTES);
 #pragma unroll
       for (int i = tid; i < (int)(S::B_BYTES / 16); i += NSPLIT) {
         float4 v = hi[i], h, l;
@@ -340,7 +344,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         tc::split_tf32(v.y, h.y, l.y);
         tc::split_tf32(v.z, h.z, l.z);
         tc::split_tf32(v.w, h.w, l.w);
-        hi[i] = h;
         lo[i] = l;
       }
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
