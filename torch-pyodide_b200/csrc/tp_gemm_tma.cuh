@@ -226,7 +226,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                int64_t M, int64_t N, int64_t K, int64_t k_per_split, int splits, float* __restrict__ ws) {
   using S = Smem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  // 1 KB aligned; derived from smem_raw by an offset so accesses stay shared-space loads/stores
+  uint8_t* smem = smem_raw + ((1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::TILES);
   uint64_t* ready = full + STAGES;
   uint64_t* empty = ready + STAGES;
