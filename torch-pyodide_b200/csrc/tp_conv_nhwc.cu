@@ -116,15 +116,33 @@ static bool pixel_box(int64_t OH, int64_t OW, int rows, uint32_t box[3]) {
   return box[1] <= 256 && box[2] <= 256;
 }
 
+// K-major (im2col) map: dims (C, W, H, N), box (32, pixel box).
 static bool nhwc_map(CUtensorMap* m, const float* t, int64_t N, int64_t H, int64_t W, int64_t C, const uint32_t pix[3],
-                     bool make, bool mn = false) {
+                     bool make) {
   uint64_t dims[4] = {(uint64_t)C, (uint64_t)W, (uint64_t)H, (uint64_t)N};
   uint64_t st[3] = {(uint64_t)C * 4, (uint64_t)(W * C) * 4, (uint64_t)(H * W * C) * 4};
   if (!tma_aligned(t, st, 3)) return false;
   if (N > 0x7fffffff || H * W > 0x7fffffff) return false;
   if (make) {
     uint32_t box[4] = {32, pix[0], pix[1], pix[2]};
-    make_map_f32(m, t, 4, dims, st, box, mn);
+    make_map_f32(m, t, 4, dims, st, box, false);
+  }
+  return true;
+}
+
+// MN-major map for the weight gradient: dims (32, W, H, N, C/32) with the
+// 32-channel groups outermost (stride 128 B), box (32, pixel box, rows/32);
+// C % 32 == 0.
+static bool nhwc_mn_map(CUtensorMap* m, const float* t, int64_t N, int64_t H, int64_t W, int64_t C,
+                        const uint32_t pix[3], uint32_t rows, bool make) {
+  if (C % 32) return false;
+  uint64_t dims[5] = {32, (uint64_t)W, (uint64_t)H, (uint64_t)N, (uint64_t)(C / 32)};
+  uint64_t st[4] = {(uint64_t)C * 4, (uint64_t)(W * C) * 4, (uint64_t)(H * W * C) * 4, 128};
+  if (!tma_aligned(t, st, 4)) return false;
+  if (N > 0x7fffffff || H * W > 0x7fffffff) return false;
+  if (make) {
+    uint32_t box[5] = {32, pix[0], pix[1], pix[2], rows / 32};
+    make_map_f32(m, t, 5, dims, st, box, true);
   }
   return true;
 }
@@ -174,7 +192,7 @@ static void conv_fwd_nhwc(const NhwcShape& s, const float* x, const float* w, co
   uint32_t pix[3];
   MatOp b{wp, false, K, 0, false};
   if (nhwc_tma_ok() && M >= 64 && s.Cin % 32 == 0 && pixel_box(s.OH, s.OW, tc::BM, pix) &&
-      nhwc_map(nullptr, x, s.N, s.H, s.W, s.Cin, pix, false) && mat_tma_ok(b)) {
+      nhwc_map(nullptr, x, s.N, s.H, s.W, s.Cin, pix, false) && mat_tma_ok(b, s.Cout)) {
     CUtensorMap ma, mb;
     nhwc_map(&ma, x, s.N, s.H, s.W, s.Cin, pix, true);
     mat_map(&mb, b, s.Cout, K, 1, tma_bn(s.Cout));
@@ -200,7 +218,7 @@ static void conv_dgrad_nhwc(const NhwcShape& s, const float* dy, const float* w,
   uint32_t pix[3];
   MatOp b{wp, false, K, 0, false};
   if (nhwc_tma_ok() && M >= 64 && s.Cout % 32 == 0 && pixel_box(s.H, s.W, tc::BM, pix) &&
-      nhwc_map(nullptr, dy, s.N, s.OH, s.OW, s.Cout, pix, false) && mat_tma_ok(b)) {
+      nhwc_map(nullptr, dy, s.N, s.OH, s.OW, s.Cout, pix, false) && mat_tma_ok(b, s.Cin)) {
     CUtensorMap ma, mb;
     nhwc_map(&ma, dy, s.N, s.OH, s.OW, s.Cout, pix, true);
     mat_map(&mb, b, s.Cin, K, 1, tma_bn(s.Cin));
@@ -221,12 +239,13 @@ static void conv_wgrad_nhwc(const NhwcShape& s, const float* dy, const float* x,
     return;
   }
   uint32_t pix[3];
+  const uint32_t bn = tma_bn(s.Cin);
   if (nhwc_tma_ok() && s.Cout >= 64 && P > 0 && pixel_box(s.OH, s.OW, 32, pix) &&
-      nhwc_map(nullptr, dy, s.N, s.OH, s.OW, s.Cout, pix, false) &&
-      nhwc_map(nullptr, x, s.N, s.H, s.W, s.Cin, pix, false)) {
+      nhwc_mn_map(nullptr, dy, s.N, s.OH, s.OW, s.Cout, pix, tc::BM, false) &&
+      nhwc_mn_map(nullptr, x, s.N, s.H, s.W, s.Cin, pix, bn, false)) {
     CUtensorMap ma, mb;
-    nhwc_map(&ma, dy, s.N, s.OH, s.OW, s.Cout, pix, true, true);
-    nhwc_map(&mb, x, s.N, s.H, s.W, s.Cin, pix, true, true);
+    nhwc_mn_map(&ma, dy, s.N, s.OH, s.OW, s.Cout, pix, tc::BM, true);
+    nhwc_mn_map(&mb, x, s.N, s.H, s.W, s.Cin, pix, bn, true);
     tma::SrcPixMN sa{(int)s.OH, (int)s.OW, s.KW, s.PH, s.PW, 0};
     tma::SrcPixMN sb{(int)s.OH, (int)s.OW, s.KW, s.PH, s.PW, 1};
     EpWgradTap ep{dw, s.Cin, khw};

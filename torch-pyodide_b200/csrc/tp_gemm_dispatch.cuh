@@ -55,19 +55,31 @@ struct MatOp {
   bool batched;
 };
 
-inline bool mat_tma_ok(const MatOp& o) {
+// An MN-major operand is addressed in 32-row groups (an outer map dimension
+// of stride 128 B), so its rows must be a multiple of 32.
+inline bool mat_tma_ok(const MatOp& o, int64_t rows) {
   if (o.ld <= 0 || o.ld % 4 || (o.batched && o.bs % 4)) return false;
+  if (o.mn && rows % 32) return false;
   uint64_t st[2] = {(uint64_t)o.ld * 4, (uint64_t)(o.batched ? o.bs : o.ld) * 4};
   return tma_aligned(o.p, st, 2);
 }
 
-// Map over the operand (rows x K per batch); box rows for a K-major operand.
+// Map over the operand (rows x K per batch).  K-major: dims (K, rows, batch),
+// box (32, box_rows, 1).  MN-major: dims (32, K, rows/32, batch), box
+// (32, 32, box_rows/32, 1).
 inline void mat_map(CUtensorMap* m, const MatOp& o, int64_t rows, int64_t K, int batch, uint32_t box_rows) {
-  uint64_t inner = (uint64_t)(o.mn ? rows : K), outer = (uint64_t)(o.mn ? K : rows);
-  uint64_t dims[3] = {inner, outer, (uint64_t)(o.batched ? batch : 1)};
-  uint64_t st[2] = {(uint64_t)o.ld * 4, (uint64_t)(o.batched ? o.bs : o.ld * (int64_t)outer) * 4};
-  uint32_t box[3] = {32, o.mn ? 32u : box_rows, 1};
-  make_map_f32(m, o.p, 3, dims, st, box, o.mn);
+  const uint64_t bst = (uint64_t)(o.batched ? o.bs : o.ld * (o.mn ? K : rows)) * 4;
+  if (!o.mn) {
+    uint64_t dims[3] = {(uint64_t)K, (uint64_t)rows, (uint64_t)(o.batched ? batch : 1)};
+    uint64_t st[2] = {(uint64_t)o.ld * 4, bst};
+    uint32_t box[3] = {32, box_rows, 1};
+    make_map_f32(m, o.p, 3, dims, st, box, false);
+  } else {
+    uint64_t dims[4] = {32, (uint64_t)K, (uint64_t)(rows / 32), (uint64_t)(o.batched ? batch : 1)};
+    uint64_t st[3] = {(uint64_t)o.ld * 4, 128, bst};
+    uint32_t box[4] = {32, 32, box_rows / 32, 1};
+    make_map_f32(m, o.p, 4, dims, st, box, true);
+  }
 }
 
 template <class SA, class SB, class EP>
@@ -84,7 +96,7 @@ template <class EP>
 bool gemm_tma(const MatOp& a, const MatOp& b, const EP& ep, int64_t M, int64_t N, int64_t K, int batch) {
   if (gemm_path() != 0 || K <= 0 || M < 64 || N <= 0 || batch <= 0) return false;
   if (K > 0x7fffffff || M > 0x7fffffff || N > 0x7fffffff) return false;
-  if (!mat_tma_ok(a) || !mat_tma_ok(b)) return false;
+  if (!mat_tma_ok(a, M) || !mat_tma_ok(b, N)) return false;
   if (a.mn) {
     if (b.mn) gemm_tma_mat<tma::SrcMN, tma::SrcMN>(a, b, ep, M, N, K, batch);
     else gemm_tma_mat<tma::SrcMN, tma::SrcK>(a, b, ep, M, N, K, batch);

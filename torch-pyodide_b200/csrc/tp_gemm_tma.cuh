@@ -76,6 +76,15 @@ __device__ __forceinline__ void load4(uint32_t dst, const CUtensorMap* map, int 
       : "memory");
 }
 
+__device__ __forceinline__ void load5(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3, int c4,
+                                      uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+      "%5, %6}], [%7];" ::"r"(dst),
+      "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(tc::smem_u32(bar))
+      : "memory");
+}
+
 // MN-major descriptor for tf32: layout SWIZZLE_128B_BASE32B (32-byte chunks
 // of each 128-byte row permuted over 4-row periods), column groups of 32 fp32
 // LBO = 4 KB apart, 4-row k groups SBO = 512 B apart.
@@ -103,16 +112,17 @@ struct SrcK {
   }
 };
 
-// MN-major: a row-major [batch][K][rows] tensor (rows contiguous); map dims
-// (rows, K, batch), box (32, 32, 1), one box per 32 rows of the tile.
+// MN-major: a row-major [batch][K][rows] tensor (rows contiguous).  Map dims
+// (32, K, rows/32, batch) with the 32-wide row groups as an outer dimension
+// (stride 128 B), box (32, 32, ROWS/32, 1): one box lands the tile as 32-row
+// groups 4 KB apart, each 32 k-rows of 128 B.
 struct SrcMN {
   static constexpr bool kMN = true;
   int bmul;
   template <int ROWS>
   __device__ __forceinline__ void issue(const CUtensorMap* map, uint32_t dst, uint64_t* bar, int b, int64_t r0,
                                         int64_t k0) const {
-#pragma unroll
-    for (int j = 0; j < ROWS / 32; ++j) load3(dst + j * 4096, map, (int)r0 + 32 * j, (int)k0, b * bmul, bar);
+    load4(dst, map, 0, (int)k0, (int)(r0 >> 5), b * bmul, bar);
   }
 };
 
@@ -139,7 +149,9 @@ struct SrcConvK {
 // tile rows = channels, k = output pixels (n, oh, ow), 32 per k-block.  Batch
 // index b = tap; with `shift` the pixel reads move by the tap offset (the
 // input x), without it they do not (the output gradient dy).  Map dims
-// (C, W, H, N), box (32, OW, rows, images) covering 32 pixels.
+// (32, W, H, N, C/32): channel groups of 32 as the outermost dimension
+// (stride 128 B), box (32, OW, rows, images, ROWS/32) covering 32 pixels of
+// every group of the tile in one copy.
 struct SrcPixMN {
   static constexpr bool kMN = true;
   int OH, OW, KW, PH, PW, shift;
@@ -153,8 +165,7 @@ struct SrcPixMN {
       dh = b / KW - PH;
       dw = b - (b / KW) * KW - PW;
     }
-#pragma unroll
-    for (int j = 0; j < ROWS / 32; ++j) load4(dst + j * 4096, map, (int)r0 + 32 * j, dw, oh0 + dh, n0, bar);
+    load5(dst, map, 0, dw, oh0 + dh, n0, (int)(r0 >> 5), bar);
   }
 };
 
