@@ -396,6 +396,31 @@ def cpu_vgg(batch: int, steps: int) -> dict:
     return {"imgs_per_s": batch / t, "sec": t, "batch": batch}
 
 
+def vgg_launch_list(args):
+    """Profiling aid (1 GPU): two eager VGG-11-BN steps at --batch, printing
+    the kernel-launch counts so an ncu launch list can select exactly the
+    second step (-s <first> -c <per step>)."""
+    import numpy as np
+    from tpcuda import CudaRuntime
+    from tpcuda.vgg import VGG11BN
+    rt = CudaRuntime(0)
+    B = args.batch
+    m = VGG11BN(rt, B, seed=0)
+    rng = np.random.default_rng(0)
+    m._h2d(m.x, rng.standard_normal((B, 3, 32, 32)).astype(np.float32))
+    m._h2d(m.y, rng.integers(0, 10, B).astype(np.float32))
+    n0 = rt.kernelLaunches()
+    m.step_eager()
+    rt.synchronize()
+    n1 = rt.kernelLaunches()
+    m.step_eager()
+    rt.synchronize()
+    n2 = rt.kernelLaunches()
+    print(json.dumps({"launch_list": "vgg11-bn eager step", "batch": B, "launches_before_step2": n1 - n0,
+                      "launches_per_step": n2 - n1, "loss": m.read_loss()}), flush=True)
+    m.close()
+
+
 def run_vgg(args, rank, world, local):
     import ctypes
 
@@ -537,11 +562,17 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["adamw", "vgg"], default="adamw")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--launch-list", action="store_true",
+                    help="profiling aid: two eager VGG steps at --batch with launch counts (1 GPU, no timing)")
+    ap.add_argument("--batch", type=int, default=VGG_GLOBAL_BATCH, help="per-GPU batch for --launch-list")
     ap.add_argument("--tensors", type=int, default=NTENSORS,
                     help="number of parameter tensors (64 = the benchmark; fewer for profiler captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.launch_list:
+        vgg_launch_list(args)
+        return
     rank, world, local = dist_setup(args.gpus)
     if args.impl == "reference":
         run_reference(args, rank, world)

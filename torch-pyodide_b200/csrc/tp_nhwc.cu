@@ -85,20 +85,24 @@ __global__ void k_col_sum_finish(const double* __restrict__ part, int64_t C, int
 static unsigned finish_grid(int64_t C) { return (unsigned)((C + 7) / 8); }
 
 // ---- column reductions over [P][C] ----------------------------------------------------------
-// Thread t: channel group g = t % G (4 channels, G = C/4), row lane r = t / G;
-// CTA `split` covers rows [p0, p1).  Per-thread f64 sums are combined over row
-// lanes in shared memory in lane order, giving part[(c*splits + split)*2 + {0,1}].
+// CTA (split, column block) covers rows [p0, p1) of CB channels.  Thread t:
+// channel group g = t % (CB/4) (4 channels), row lane r = t / (CB/4).  Per-thread
+// f64 sums are combined over row lanes in shared memory in lane order, giving
+// part[(c*splits + split)*2 + {0,1}].
 
-// Functors: ctx(c0) loads what the thread's 4 channels need once; acc()
-// handles the float4 at index i4.
+// Functors: ctx(c0) loads what the thread's 4 channels need once; load(i4)
+// fetches the float4 operands at index i4 and use() consumes them, so the
+// row loop can have several rows' loads in flight.
 struct NoCtx {};
 
 struct ColStatsF {  // a += x, b += x*x
   const float* x;
+  static constexpr int kUnroll = 8;
   using Ctx = NoCtx;
+  using V = float4;
   __device__ __forceinline__ Ctx ctx(int) const { return {}; }
-  __device__ __forceinline__ void acc(int64_t i4, const Ctx&, double (&a)[4], double (&b)[4]) const {
-    float4 v = reinterpret_cast<const float4*>(x)[i4];
+  __device__ __forceinline__ V load(int64_t i4) const { return reinterpret_cast<const float4*>(x)[i4]; }
+  __device__ __forceinline__ void use(int64_t, const V& v, const Ctx&, double (&a)[4], double (&b)[4]) const {
     a[0] += v.x, a[1] += v.y, a[2] += v.z, a[3] += v.w;
     b[0] += (double)v.x * v.x, b[1] += (double)v.y * v.y, b[2] += (double)v.z * v.z, b[3] += (double)v.w * v.w;
   }
@@ -106,23 +110,32 @@ struct ColStatsF {  // a += x, b += x*x
 
 struct ColSumF {  // a += x
   const float* x;
+  static constexpr int kUnroll = 8;
   using Ctx = NoCtx;
+  using V = float4;
   __device__ __forceinline__ Ctx ctx(int) const { return {}; }
-  __device__ __forceinline__ void acc(int64_t i4, const Ctx&, double (&a)[4], double (&)[4]) const {
-    float4 v = reinterpret_cast<const float4*>(x)[i4];
+  __device__ __forceinline__ V load(int64_t i4) const { return reinterpret_cast<const float4*>(x)[i4]; }
+  __device__ __forceinline__ void use(int64_t, const V& v, const Ctx&, double (&a)[4], double (&)[4]) const {
     a[0] += v.x, a[1] += v.y, a[2] += v.z, a[3] += v.w;
   }
 };
 
-__device__ __forceinline__ float4 relu_mask(float4 g, const float* relu_src, int64_t i4) {
+struct BwdV {
+  float4 g, x;
+};
+
+__device__ __forceinline__ BwdV load_bwd(const float* dy, const float* x, const float* relu_src, int64_t i4) {
+  BwdV v;
+  v.g = reinterpret_cast<const float4*>(dy)[i4];
+  v.x = reinterpret_cast<const float4*>(x)[i4];
   if (relu_src) {
     float4 r = reinterpret_cast<const float4*>(relu_src)[i4];
-    if (!(r.x > 0.0f)) g.x = 0.0f;
-    if (!(r.y > 0.0f)) g.y = 0.0f;
-    if (!(r.z > 0.0f)) g.z = 0.0f;
-    if (!(r.w > 0.0f)) g.w = 0.0f;
+    if (!(r.x > 0.0f)) v.g.x = 0.0f;
+    if (!(r.y > 0.0f)) v.g.y = 0.0f;
+    if (!(r.z > 0.0f)) v.g.z = 0.0f;
+    if (!(r.w > 0.0f)) v.g.w = 0.0f;
   }
-  return g;
+  return v;
 }
 
 struct ColBnBwdF {  // g = dy masked by relu_src > 0; a += g, b += g * x_hat
@@ -131,9 +144,11 @@ struct ColBnBwdF {  // g = dy masked by relu_src > 0; a += g, b += g * x_hat
   const float* relu_src;
   const float* mean;
   const float* invstd;
+  static constexpr int kUnroll = 4;
   struct Ctx {
     float mu[4], is[4];
   };
+  using V = BwdV;
   __device__ __forceinline__ Ctx ctx(int c0) const {
     Ctx c;
 #pragma unroll
@@ -143,14 +158,13 @@ struct ColBnBwdF {  // g = dy masked by relu_src > 0; a += g, b += g * x_hat
     }
     return c;
   }
-  __device__ __forceinline__ void acc(int64_t i4, const Ctx& c, double (&a)[4], double (&b)[4]) const {
-    float4 g = relu_mask(reinterpret_cast<const float4*>(dy)[i4], relu_src, i4);
-    float4 xv = reinterpret_cast<const float4*>(x)[i4];
-    a[0] += g.x, a[1] += g.y, a[2] += g.z, a[3] += g.w;
-    b[0] += (double)g.x * ((xv.x - c.mu[0]) * c.is[0]);
-    b[1] += (double)g.y * ((xv.y - c.mu[1]) * c.is[1]);
-    b[2] += (double)g.z * ((xv.z - c.mu[2]) * c.is[2]);
-    b[3] += (double)g.w * ((xv.w - c.mu[3]) * c.is[3]);
+  __device__ __forceinline__ V load(int64_t i4) const { return load_bwd(dy, x, relu_src, i4); }
+  __device__ __forceinline__ void use(int64_t, const V& v, const Ctx& c, double (&a)[4], double (&b)[4]) const {
+    a[0] += v.g.x, a[1] += v.g.y, a[2] += v.g.z, a[3] += v.g.w;
+    b[0] += (double)v.g.x * ((v.x.x - c.mu[0]) * c.is[0]);
+    b[1] += (double)v.g.y * ((v.x.y - c.mu[1]) * c.is[1]);
+    b[2] += (double)v.g.z * ((v.x.z - c.mu[2]) * c.is[2]);
+    b[3] += (double)v.g.w * ((v.x.w - c.mu[3]) * c.is[3]);
   }
 };
 
@@ -164,9 +178,11 @@ struct ColBnBwdApplyF {
   const float* invstd;
   const float* coef;
   float* dx;
+  static constexpr int kUnroll = 4;
   struct Ctx {
     float mu[4], is[4], k0[4], k1[4], k2[4];
   };
+  using V = BwdV;
   __device__ __forceinline__ Ctx ctx(int c0) const {
     Ctx c;
 #pragma unroll
@@ -179,10 +195,10 @@ struct ColBnBwdApplyF {
     }
     return c;
   }
-  __device__ __forceinline__ void acc(int64_t i4, const Ctx& c, double (&a)[4], double (&)[4]) const {
-    float4 gv = relu_mask(reinterpret_cast<const float4*>(dy)[i4], relu_src, i4);
-    float4 xv = reinterpret_cast<const float4*>(x)[i4];
-    float g[4] = {gv.x, gv.y, gv.z, gv.w}, xs[4] = {xv.x, xv.y, xv.z, xv.w}, o[4];
+  __device__ __forceinline__ V load(int64_t i4) const { return load_bwd(dy, x, relu_src, i4); }
+  __device__ __forceinline__ void use(int64_t i4, const V& v, const Ctx& c, double (&a)[4], double (&)[4]) const {
+    const float g[4] = {v.g.x, v.g.y, v.g.z, v.g.w}, xs[4] = {v.x.x, v.x.y, v.x.z, v.x.w};
+    float o[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       float xh = (xs[j] - c.mu[j]) * c.is[j];
@@ -196,39 +212,53 @@ struct ColBnBwdApplyF {
 constexpr int COL_THREADS = 256;
 
 template <class F>
-__global__ void __launch_bounds__(COL_THREADS) k_col_reduce(F f, int64_t P, int C, int64_t rows_per_split,
+__global__ void __launch_bounds__(COL_THREADS) k_col_reduce(F f, int64_t P, int C, int CB, int64_t rows_per_split,
                                                             int splits, double* __restrict__ part) {
-  extern __shared__ double sh[];  // [R][C][2]
-  const int G = C >> 2, R = COL_THREADS / G;
-  const int t = threadIdx.x, g = t % G, r = t / G;
+  extern __shared__ double sh[];  // [R][CB][2]
+  const int GT = C >> 2, GB = CB >> 2, R = COL_THREADS / GB;
+  const int t = threadIdx.x, g = t % GB, r = t / GB;
+  const int cg = blockIdx.y * GB + g;  // this thread's channel group
   const int split = blockIdx.x;
   const int64_t p0 = (int64_t)split * rows_per_split;
   const int64_t p1 = p0 + rows_per_split < P ? p0 + rows_per_split : P;
   double a[4] = {0.0, 0.0, 0.0, 0.0}, b[4] = {0.0, 0.0, 0.0, 0.0};
   if (r < R) {
-    const typename F::Ctx cx = f.ctx(4 * g);
-    for (int64_t p = p0 + r; p < p1; p += R) f.acc(p * G + g, cx, a, b);
+    const typename F::Ctx cx = f.ctx(4 * cg);
+    int64_t p = p0 + r;
+    // U rows per step: all their loads are issued before any is used
+    constexpr int U = F::kUnroll;
+    for (; p + (U - 1) * R < p1; p += U * R) {
+      typename F::V v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) v[u] = f.load((p + u * R) * GT + cg);
+#pragma unroll
+      for (int u = 0; u < U; ++u) f.use((p + u * R) * GT + cg, v[u], cx, a, b);
+    }
+    for (; p < p1; p += R) f.use(p * GT + cg, f.load(p * GT + cg), cx, a, b);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      sh[((int64_t)r * C + 4 * g + j) * 2] = a[j];
-      sh[((int64_t)r * C + 4 * g + j) * 2 + 1] = b[j];
+      sh[((int64_t)r * CB + 4 * g + j) * 2] = a[j];
+      sh[((int64_t)r * CB + 4 * g + j) * 2 + 1] = b[j];
     }
   }
   __syncthreads();
-  for (int c = t; c < C; c += COL_THREADS) {
+  for (int c = t; c < CB; c += COL_THREADS) {
     double sa = 0.0, sb = 0.0;
     for (int k = 0; k < R; ++k) {
-      sa += sh[((int64_t)k * C + c) * 2];
-      sb += sh[((int64_t)k * C + c) * 2 + 1];
+      sa += sh[((int64_t)k * CB + c) * 2];
+      sb += sh[((int64_t)k * CB + c) * 2 + 1];
     }
-    part[((int64_t)c * splits + split) * 2] = sa;
-    part[((int64_t)c * splits + split) * 2 + 1] = sb;
+    const int64_t ch = (int64_t)blockIdx.y * CB + c;
+    part[(ch * splits + split) * 2] = sa;
+    part[(ch * splits + split) * 2 + 1] = sb;
   }
 }
 
-// Row splits: a few waves of CTAs, each with >= 64 rows per row lane.
+// CTAs of 64 channels (all C when C <= 64 or C is not a multiple of 64) by
+// row splits: ~8 CTAs per SM, each with >= 16 rows per row lane, so enough
+// loads are in flight to cover HBM latency.
 struct ColPlan {
-  int splits;
+  int splits, cb;
   int64_t rows;
   size_t part_bytes;  // C * splits * 2 doubles, rounded up to 256 bytes
 };
@@ -236,11 +266,13 @@ struct ColPlan {
 static ColPlan col_plan(int64_t P, int C) {
   TP_REQUIRE(C % 4 == 0 && C >= 4 && C <= 4 * COL_THREADS, "channels-last reduction needs C %% 4 == 0, C <= %d",
              4 * COL_THREADS);
-  const int R = COL_THREADS / (C / 4);
-  int64_t want = (int64_t)sm_count() * 4;
-  int64_t maxs = P / ((int64_t)R * 64);
-  if (maxs < 1) maxs = 1;
   ColPlan pl;
+  pl.cb = (C > 64 && C % 64 == 0) ? 64 : C;
+  const int R = COL_THREADS / (pl.cb / 4);
+  int64_t want = (int64_t)sm_count() * 8 / (C / pl.cb);
+  if (want < 1) want = 1;
+  int64_t maxs = P / ((int64_t)R * 16);
+  if (maxs < 1) maxs = 1;
   int64_t s = want < maxs ? want : maxs;
   pl.rows = (P + s - 1) / s;
   if (pl.rows < 1) pl.rows = 1;
@@ -252,29 +284,63 @@ static ColPlan col_plan(int64_t P, int C) {
 
 template <class F>
 static void col_launch(const F& f, int64_t P, int C, const ColPlan& pl, double* part) {
-  const int R = COL_THREADS / (C / 4);
-  size_t shb = (size_t)R * C * 2 * sizeof(double);
+  const int R = COL_THREADS / (pl.cb / 4);
+  size_t shb = (size_t)R * pl.cb * 2 * sizeof(double);
   auto kfn = k_col_reduce<F>;
-  TP_LAUNCH(kfn, (unsigned)pl.splits, COL_THREADS, shb, f, P, C, pl.rows, pl.splits, part);
+  TP_LAUNCH(kfn, dim3((unsigned)pl.splits, (unsigned)(C / pl.cb)), COL_THREADS, shb, f, P, C, pl.cb, pl.rows,
+            pl.splits, part);
 }
 
 // ---- element-wise passes (float4 over 4 consecutive channels) ---------------------------------
 
+// When the grid stride is a multiple of G (256 % G == 0 and the block size
+// 256) every thread keeps one channel group, so its 4 channels' parameters
+// are loaded once; 4 vectors per step are loaded before any is stored.
+__device__ __forceinline__ float4 bn_apply4(float4 v, const float (&mu)[4], const float (&sc)[4],
+                                            const float (&bs)[4], int relu) {
+  float r[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    r[j] = (r[j] - mu[j]) * sc[j] + bs[j];
+    if (relu) r[j] = fmaxf(r[j], 0.0f);
+  }
+  return make_float4(r[0], r[1], r[2], r[3]);
+}
+
 __global__ void k_bn_apply_nhwc(const float4* __restrict__ x, const float* __restrict__ mean,
                                 const float* __restrict__ invstd, const float* __restrict__ w,
                                 const float* __restrict__ b, float4* __restrict__ y, int64_t n4, int G, int relu) {
-  int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (stride % G == 0) {
     const int c = 4 * (int)(i % G);
-    float4 v = x[i];
-    float r[4] = {v.x, v.y, v.z, v.w};
+    float mu[4], sc[4], bs[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      float wt = w ? w[c + j] : 1.0f, bs = b ? b[c + j] : 0.0f;
-      r[j] = (r[j] - mean[c + j]) * (invstd[c + j] * wt) + bs;
-      if (relu) r[j] = fmaxf(r[j], 0.0f);
+      mu[j] = mean[c + j];
+      sc[j] = invstd[c + j] * (w ? w[c + j] : 1.0f);
+      bs[j] = b ? b[c + j] : 0.0f;
     }
-    y[i] = make_float4(r[0], r[1], r[2], r[3]);
+    for (; i + 3 * stride < n4; i += 4 * stride) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = x[i + u * stride];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) y[i + u * stride] = bn_apply4(v[u], mu, sc, bs, relu);
+    }
+    for (; i < n4; i += stride) y[i] = bn_apply4(x[i], mu, sc, bs, relu);
+    return;
+  }
+  for (; i < n4; i += stride) {
+    const int c = 4 * (int)(i % G);
+    float mu[4], sc[4], bs[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      mu[j] = mean[c + j];
+      sc[j] = invstd[c + j] * (w ? w[c + j] : 1.0f);
+      bs[j] = b ? b[c + j] : 0.0f;
+    }
+    y[i] = bn_apply4(x[i], mu, sc, bs, relu);
   }
 }
 
@@ -373,7 +439,8 @@ TP_API int tpk_bn_train_nhwc(const float* x, const float* w, const float* b, flo
     TP_LAUNCH(k_col_bn_finish, finish_grid(C), 256, 0, part, C, pl.splits, (double)P, eps, momentum, save_mean,
               save_invstd, running_mean, running_var);
     int64_t n4 = P * C / 4;
-    TP_LAUNCH(k_bn_apply_nhwc, grid_for(n4, 256), 256, 0, reinterpret_cast<const float4*>(x), save_mean,
+    unsigned grid = (unsigned)((n4 + 255) / 256 < (int64_t)sm_count() * 8 ? (n4 + 255) / 256 : sm_count() * 8);
+    TP_LAUNCH(k_bn_apply_nhwc, grid, 256, 0, reinterpret_cast<const float4*>(x), save_mean,
               save_invstd, w, b, reinterpret_cast<float4*>(y), n4, (int)(C / 4), relu ? 1 : 0);
   });
 }
