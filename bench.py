@@ -396,6 +396,131 @@ def cpu_vgg(batch: int, steps: int) -> dict:
     return {"imgs_per_s": batch / t, "sec": t, "batch": batch}
 
 
+def run_ops(args):
+    """Per-op throughput of the reductions / norms and dense
+    contractions through the reference-facing runtime surface
+    (CudaRuntime, handle API, outputs allocated per call from the pool), each
+    against its roofline: HBM for the reductions and norms (algorithmic bytes:
+    every input read once, every output written once), the 3xTF32 tensor rate
+    for the contractions.  Inputs ~N(0,1) / ~U(-1,1) from the device RNG,
+    larger than L2.  One JSON line with a result per op."""
+    import torch
+    from tpcuda import CudaRuntime
+    rt = CudaRuntime(0)
+    torch.cuda.set_device(0)
+    stream = torch.cuda.ExternalStream(rt.stream())
+    hbm, _ = measured_peaks()
+    peak3, bf16, peak_kind = tf32x3_peak()
+    reps = max(3, min(args.steps, 10))
+    rt.setSeed(0)
+    results = []
+
+    def timed(fn, n_out):
+        # outputs are destroyed as soon as they are made (stream-ordered), so the
+        # pool serves every rep from the blocks of the warm-up call
+        for _ in range(2):
+            for o in fn()[:n_out]:
+                rt.destroy(o["id"])
+        rt.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            for o in fn()[:n_out]:
+                rt.destroy(o["id"])
+        e1.record(stream)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    def add(name, shape, ms, work, bound):
+        if bound == "hbm":
+            achieved = work / (ms * 1e-3) / 1e9
+            results.append({"op": name, "shape": shape, "ms": round(ms, 4), "GB/s": round(achieved, 1),
+                            "frac_of_hbm": round(achieved / hbm, 3)})
+        else:
+            achieved = work / (ms * 1e-3) / 1e12
+            results.append({"op": name, "shape": shape, "ms": round(ms, 4), "TFLOP/s": round(achieved, 2),
+                            "frac_of_3xtf32": round(achieved / peak3, 3)})
+
+    one = lambda h: [h]  # noqa: E731
+    # ---- configs[2]: reductions and norms ----
+    x = rt.randn([16384, 4096], "float32")
+    g = rt.full([4096], 1.0, "float32")
+    b = rt.full([4096], 0.0, "float32")
+    dy = rt.randn([16384, 4096], "float32")
+    nb = 16384 * 4096 * 4
+    ms = timed(lambda: rt.layerNormForward(x["id"], [4096], g["id"], b["id"], 1e-5), 3)
+    add("layer_norm fwd", [16384, 4096], ms, 2 * nb, "hbm")
+    y, sm, sr = rt.layerNormForward(x["id"], [4096], g["id"], b["id"], 1e-5)
+    ms = timed(lambda: rt.layerNormBackward(dy["id"], x["id"], [4096], g["id"], sm["id"], sr["id"]), 3)
+    add("layer_norm bwd", [16384, 4096], ms, 3 * nb, "hbm")
+    for h in (y, sm, sr, x, g, b, dy):
+        rt.destroy(h["id"])
+    x = rt.randn([32768, 8192], "float32")
+    nb = 32768 * 8192 * 4
+    add("softmax", [32768, 8192], timed(lambda: one(rt.softmax(x["id"], -1)), 1), 2 * nb, "hbm")
+    add("log_softmax", [32768, 8192], timed(lambda: one(rt.logSoftmax(x["id"], -1)), 1), 2 * nb, "hbm")
+    rt.destroy(x["id"])
+    x = rt.randn([8192, 8192], "float32")
+    nb = 8192 * 8192 * 4
+    add("sum all", [8192, 8192], timed(lambda: one(rt.sum(x["id"])), 1), nb, "hbm")
+    for d in (0, -1):
+        add(f"sum dim {d}", [8192, 8192], timed(lambda: one(rt.sumDim(x["id"], d, False)), 1), nb, "hbm")
+        add(f"mean dim {d}", [8192, 8192], timed(lambda: one(rt.meanDim(x["id"], d, False)), 1), nb, "hbm")
+        add(f"max dim {d}", [8192, 8192], timed(lambda: rt.maxDim(x["id"], d, False), 2), nb, "hbm")
+    rt.destroy(x["id"])
+    shp = [256, 128, 56, 56]
+    x = rt.randn(shp, "float32")
+    dy = rt.randn(shp, "float32")
+    g = rt.full([128], 1.0, "float32")
+    b = rt.full([128], 0.0, "float32")
+    rm = rt.full([128], 0.0, "float32")
+    rv = rt.full([128], 1.0, "float32")
+    nb = 256 * 128 * 56 * 56 * 4
+    ms = timed(lambda: rt.batchNormTrain(x["id"], g["id"], b["id"], rm["id"], rv["id"], 1e-5, 0.1), 3)
+    add("batch_norm train fwd", shp, ms, 2 * nb, "hbm")
+    y, mean, inv = rt.batchNormTrain(x["id"], g["id"], b["id"], rm["id"], rv["id"], 1e-5, 0.1)
+    ms = timed(lambda: rt.batchNormBackward(dy["id"], x["id"], g["id"], mean["id"], inv["id"]), 3)
+    add("batch_norm bwd", shp, ms, 3 * nb, "hbm")
+    for h in (y, mean, inv, x, dy, g, b, rm, rv):
+        rt.destroy(h["id"])
+    # ---- configs[3]: dense contractions ----
+    for n in (512, 2048, 8192):
+        a = rt.rand([n, n], "float32")
+        bb = rt.rand([n, n], "float32")
+        add("matmul", [n, n, n], timed(lambda: one(rt.matmul(a["id"], bb["id"])), 1), 2.0 * n ** 3, "tensor")
+        rt.destroy(a["id"])
+        rt.destroy(bb["id"])
+    xl = rt.rand([16384, 4096], "float32")
+    wl = rt.rand([11008, 4096], "float32")
+    bl = rt.rand([11008], "float32")
+    add("linear +bias", [16384, 4096, 11008], timed(lambda: one(rt.linear(xl["id"], wl["id"], bl["id"])), 1),
+        2.0 * 16384 * 4096 * 11008, "tensor")
+    for h in (xl, wl, bl):
+        rt.destroy(h["id"])
+    for xs, ws, st, pd in (([128, 64, 56, 56], [64, 64, 3, 3], 1, 1), ([128, 3, 224, 224], [64, 3, 7, 7], 2, 3)):
+        xc = rt.randn(xs, "float32")
+        wc = rt.randn(ws, "float32")
+        oh = (xs[2] + 2 * pd - ws[2]) // st + 1
+        ys = [xs[0], ws[0], oh, oh]
+        gy = rt.randn(ys, "float32")
+        fl = 2.0 * ys[0] * ys[1] * oh * oh * xs[1] * ws[2] * ws[3]
+        tag = f"{ws[2]}x{ws[3]} s{st}"
+        add(f"conv2d fwd {tag}", xs, timed(lambda: one(rt.conv2d(xc["id"], wc["id"], None, [st], [pd], [1], 1)), 1),
+            fl, "tensor")
+        add(f"conv2d dgrad {tag}", xs,
+            timed(lambda: one(rt.conv2dInputBackward(gy["id"], wc["id"], xs, ys, [st], [pd])), 1), fl, "tensor")
+        add(f"conv2d wgrad {tag}", xs,
+            timed(lambda: one(rt.conv2dWeightBackward(gy["id"], xc["id"], ws, ys, xs, [st], [pd])), 1), fl,
+            "tensor")
+        for h in (xc, wc, gy):
+            rt.destroy(h["id"])
+    print(json.dumps({"metric": "per-op throughput vs roofline (reductions/norms: GB/s of HBM; contractions: "
+                                "TFLOP/s of 3xTF32)", "n_gpus": 1, "reps": reps, "hbm_peak_gbs": hbm,
+                      "tf32x3_peak_tflops": round(peak3, 1), "peak_source": f"{peak_kind} bf16 {bf16}",
+                      "path": "CudaRuntime handle API (the reference-facing surface), NCHW",
+                      "results": results}), flush=True)
+
+
 def vgg_launch_list(args):
     """Profiling aid (1 GPU): two eager VGG-11-BN steps at --batch, printing
     the kernel-launch counts so an ncu launch list can select exactly the
@@ -560,7 +685,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["adamw", "vgg"], default="adamw")
+    ap.add_argument("--workload", choices=["adamw", "vgg", "ops"], default="adamw")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--launch-list", action="store_true",
                     help="profiling aid: two eager VGG steps at --batch with launch counts (1 GPU, no timing)")
@@ -572,6 +697,9 @@ def main():
         args.warmup = 3
     if args.launch_list:
         vgg_launch_list(args)
+        return
+    if args.workload == "ops" and args.impl == "ours":
+        run_ops(args)
         return
     rank, world, local = dist_setup(args.gpus)
     if args.impl == "reference":

@@ -47,7 +47,8 @@ def test_matmul_long_k_accuracy(cuda_rt, oracle_rt):
 
 
 @pytest.mark.parametrize("xs,ws", [([8, 64, 16, 16], [128, 64, 3, 3]), ([4, 3, 32, 32], [64, 3, 3, 3]),
-                                   ([16, 256, 4, 4], [512, 256, 3, 3])])
+                                   ([16, 256, 4, 4], [512, 256, 3, 3]), ([2, 64, 20, 20], [64, 64, 3, 3]),
+                                   ([2, 32, 9, 9], [64, 32, 5, 5])])
 def test_conv_paths(cuda_rt, oracle_rt, path, xs, ws):
     rng = np.random.default_rng(sum(xs))
     cx, ox = both(cuda_rt, oracle_rt, rng.standard_normal(xs))

@@ -98,9 +98,11 @@ def test_matmul_handle_tma_long_k(cuda_rt, oracle_rt):
 
 
 # (Cin, Cout, H=W) of every VGG-11-BN conv (the first with its input padded to 4
-# channels too), plus shapes off the TMA tiling
+# channels too), plus shapes off the TMA kernel and off whole-row pixel tiles
 NHWC_SHAPES = [(3, 64, 32), (4, 64, 32), (4, 16, 7), (64, 128, 16), (128, 256, 8), (256, 256, 8), (256, 512, 4),
-               (512, 512, 4), (512, 512, 2), (32, 64, 6), (48, 96, 8)]
+               (512, 512, 4), (512, 512, 2), (32, 64, 6), (48, 96, 8),
+               # pixel grids that 128 / 32 pixel runs do not tile: rectangle tiles
+               (64, 64, 14), (32, 64, 7), (64, 64, 20)]
 
 
 def nchw(a):

@@ -14,9 +14,18 @@
 
 namespace tp {
 
+// Each functor: acc4 / acc1 for one float4 / float at a flat index; load4 +
+// use4 split the float4 step so several loads can be in flight.
+
 // a += x, b += x*x
 struct ChanStatsF {
   const float* x;
+  using V = float4;
+  __device__ __forceinline__ V load4(int64_t i4) const { return reinterpret_cast<const float4*>(x)[i4]; }
+  __device__ __forceinline__ void use4(const V& v, int64_t, double& a, double& b) const {
+    a += (double)v.x + (double)v.y + (double)v.z + (double)v.w;
+    b += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+  }
   __device__ __forceinline__ void acc4(int64_t i4, int64_t, double& a, double& b) const {
     float4 v = reinterpret_cast<const float4*>(x)[i4];
     a += (double)v.x + (double)v.y + (double)v.z + (double)v.w;
@@ -32,6 +41,11 @@ struct ChanStatsF {
 // a += x (b unused)
 struct ChanSumF {
   const float* x;
+  using V = float4;
+  __device__ __forceinline__ V load4(int64_t i4) const { return reinterpret_cast<const float4*>(x)[i4]; }
+  __device__ __forceinline__ void use4(const V& v, int64_t, double& a, double&) const {
+    a += (double)v.x + (double)v.y + (double)v.z + (double)v.w;
+  }
   __device__ __forceinline__ void acc4(int64_t i4, int64_t, double& a, double&) const {
     float4 v = reinterpret_cast<const float4*>(x)[i4];
     a += (double)v.x + (double)v.y + (double)v.z + (double)v.w;
@@ -47,6 +61,28 @@ struct ChanBnBwdF {
   const float* mean;
   const float* invstd;
   __device__ __forceinline__ float g1(float g, float r) const { return (relu_src && !(r > 0.0f)) ? 0.0f : g; }
+  struct V {
+    float4 g, x;
+  };
+  __device__ __forceinline__ V load4(int64_t i4) const {
+    V v;
+    v.g = reinterpret_cast<const float4*>(dy)[i4];
+    v.x = reinterpret_cast<const float4*>(x)[i4];
+    if (relu_src) {
+      float4 r = reinterpret_cast<const float4*>(relu_src)[i4];
+      v.g.x = g1(v.g.x, r.x);
+      v.g.y = g1(v.g.y, r.y);
+      v.g.z = g1(v.g.z, r.z);
+      v.g.w = g1(v.g.w, r.w);
+    }
+    return v;
+  }
+  __device__ __forceinline__ void use4(const V& v, int64_t c, double& a, double& b) const {
+    float mu = mean[c], is = invstd[c];
+    a += (double)v.g.x + (double)v.g.y + (double)v.g.z + (double)v.g.w;
+    b += (double)v.g.x * ((v.x.x - mu) * is) + (double)v.g.y * ((v.x.y - mu) * is) +
+         (double)v.g.z * ((v.x.z - mu) * is) + (double)v.g.w * ((v.x.w - mu) * is);
+  }
   __device__ __forceinline__ void acc4(int64_t i4, int64_t c, double& a, double& b) const {
     float4 g = reinterpret_cast<const float4*>(dy)[i4];
     float4 xv = reinterpret_cast<const float4*>(x)[i4];
@@ -83,7 +119,20 @@ __global__ void __launch_bounds__(256) k_chan_reduce(F f, int64_t N, int64_t C, 
     if ((S & 3) == 0) {
       const uint32_t S4 = (uint32_t)(S >> 2);
       const uint32_t cnt = (uint32_t)((n1 - n0) * S4);
-      for (uint32_t i = threadIdx.x; i < cnt; i += blockDim.x) {
+      const uint32_t step = blockDim.x;
+      uint32_t i = threadIdx.x;
+      // 4 vectors per step, all loaded before any is used
+      for (; i + 3 * step < cnt; i += 4 * step) {
+        typename F::V v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint32_t ii = i + u * step, dn = ii / S4, s4 = ii - dn * S4;
+          v[u] = f.load4(((n0 + dn) * C + c) * (int64_t)S4 + s4);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) f.use4(v[u], c, a, b);
+      }
+      for (; i < cnt; i += step) {
         uint32_t dn = i / S4, s4 = i - dn * S4;
         int64_t i4 = ((n0 + dn) * C + c) * (int64_t)S4 + s4;
         f.acc4(i4, c, a, b);

@@ -96,6 +96,7 @@ __global__ void k_pack_filters(const float* __restrict__ w, float* __restrict__ 
 static bool tc_ok(int64_t M) { return g_gemm_path != 1 && M >= 64; }
 
 void conv_fwd(const ConvShape& s, const float* x, const float* w, const float* bias, float* y) {
+  if (conv_fwd_via_nhwc(s, x, w, bias, y)) return;
   int groups = (int)(s.Cin / s.icpg);
   int khw = s.KH * s.KW;
   int64_t M = s.N * s.OH * s.OW, K = (int64_t)s.icpg * khw;
@@ -115,6 +116,7 @@ void conv_fwd(const ConvShape& s, const float* x, const float* w, const float* b
 }
 
 void conv_dgrad(const ConvShape& s, const float* dy, const float* w, float* dx) {
+  if (conv_dgrad_via_nhwc(s, dy, w, dx)) return;
   int khw = s.KH * s.KW;
   int64_t M = s.N * s.H * s.W, K = s.Cout * khw;
   EpNCHW ep{dx, nullptr, s.Cin, s.H * s.W, (int)s.Cin};
@@ -135,6 +137,7 @@ void conv_dgrad(const ConvShape& s, const float* dy, const float* w, float* dx) 
 }
 
 void conv_wgrad(const ConvShape& s, const float* dy, const float* x, float* dw) {
+  if (conv_wgrad_via_nhwc(s, dy, x, dw)) return;
   int khw = s.KH * s.KW;
   int64_t K = s.N * s.OH * s.OW;
   if (tc_ok(s.Cout) && s.icpg == s.Cin && s.Cin >= 32) {

@@ -97,34 +97,86 @@ struct LdNhwcWgradB {
 
 // ---- TMA maps over channels-last tensors ---------------------------------------------------
 
-// Box extents (W, H, N) covering `rows` consecutive pixels of an OH x OW grid
-// starting at any multiple of `rows`; false if the grid does not tile so.
-static bool pixel_box(int64_t OH, int64_t OW, int rows, uint32_t box[3]) {
-  int64_t hw = OH * OW;
-  if (OW > rows || OW > 256) return false;
-  if (hw >= rows) {
-    if (hw % rows || rows % OW) return false;
-    box[0] = (uint32_t)OW;
-    box[1] = (uint32_t)(rows / OW);
-    box[2] = 1;
-  } else {
-    if (rows % hw) return false;
-    box[0] = (uint32_t)OW;
-    box[1] = (uint32_t)OH;
-    box[2] = (uint32_t)(rows / hw);
+// Pixel tiles of `rows` output pixels over an N x OH x OW grid, with the
+// number of GEMM rows (or k) they span.  Whole rows of the grid when OW
+// divides `rows` and `rows` divides OH*OW (or whole images when OH*OW
+// divides `rows`): then tile order is plain pixel order and no row is padding.
+// Otherwise TW x TH rectangles (TW a power of two) with the least padding.
+struct Tiling {
+  tma::PixTile pt;
+  int64_t span;   // tiles x rows
+  bool linear;    // tile order == pixel order, span == N*OH*OW rounded up to `rows`
+};
+
+static bool pixel_tiling(int64_t N, int64_t OH, int64_t OW, int rows, Tiling& t) {
+  if (OH <= 0 || OW <= 0 || N <= 0) return false;
+  const int64_t hw = OH * OW;
+  tma::PixTile& p = t.pt;
+  p.OH = (int)OH;
+  p.OW = (int)OW;
+  if (OW <= rows && rows % OW == 0 && hw >= rows && hw % rows == 0 && rows / OW <= 256) {
+    p.TW = (int)OW, p.TH = (int)(rows / OW), p.TN = 1, p.tiles_w = 1, p.tiles_h = (int)(OH / p.TH);
+    t.span = N * hw;
+    t.linear = true;
+    return true;
   }
-  return box[1] <= 256 && box[2] <= 256;
+  if (hw < rows && rows % hw == 0 && OW <= 256 && OH <= 256) {
+    p.TW = (int)OW, p.TH = (int)OH, p.TN = (int)(rows / hw), p.tiles_w = 1, p.tiles_h = 1;
+    t.span = (N + p.TN - 1) / p.TN * rows;
+    t.linear = true;
+    return true;
+  }
+  int64_t best = -1;
+  for (int tw = 4; tw <= rows && tw <= 256; tw *= 2) {
+    const int th = rows / tw;
+    if (th < 1 || th > 256 || tw * th != rows) continue;
+    const int64_t cw = (OW + tw - 1) / tw, ch = (OH + th - 1) / th;
+    const int64_t area = cw * ch * rows;
+    if (best < 0 || area < best) {
+      best = area;
+      p.TW = tw, p.TH = th, p.TN = 1, p.tiles_w = (int)cw, p.tiles_h = (int)ch;
+    }
+  }
+  if (best < 0) return false;
+  t.span = N * best;
+  t.linear = false;
+  return t.span < ((int64_t)1 << 31);
 }
 
-// K-major (im2col) map: dims (C, W, H, N), box (32, pixel box).
-static bool nhwc_map(CUtensorMap* m, const float* t, int64_t N, int64_t H, int64_t W, int64_t C, const uint32_t pix[3],
-                     bool make) {
+// Row-major [pixel][C] output through pixel tiles: GEMM row m -> pixel, rows
+// outside the grid are skipped.
+struct EpPixTile {
+  float* c;
+  int64_t ldc, N;
+  const float* bias;
+  tma::PixTile pt;
+  __device__ __forceinline__ bool at(int64_t m, int64_t& row) const {
+    int n, oh, ow;
+    if (!pt.pixel(m, 128, N, n, oh, ow)) return false;
+    row = ((int64_t)n * pt.OH + oh) * pt.OW + ow;
+    return true;
+  }
+  __device__ __forceinline__ void operator()(int, int64_t m, int64_t n, float v) const {
+    int64_t row;
+    if (!at(m, row)) return;
+    c[row * ldc + n] = bias ? v + bias[n] : v;
+  }
+  __device__ __forceinline__ void row16(int b, int64_t m, int64_t n0, int64_t Nn, const float (&v)[16]) const {
+    int64_t row;
+    if (!at(m, row)) return;
+    EpRowMajor{c, ldc, 0, bias, 0}.row16(b, row, n0, Nn, v);
+  }
+};
+
+// K-major (im2col) map: dims (C, W, H, N), box (32, TW, TH, TN).
+static bool nhwc_map(CUtensorMap* m, const float* t, int64_t N, int64_t H, int64_t W, int64_t C,
+                     const tma::PixTile& pt, bool make) {
   uint64_t dims[4] = {(uint64_t)C, (uint64_t)W, (uint64_t)H, (uint64_t)N};
   uint64_t st[3] = {(uint64_t)C * 4, (uint64_t)(W * C) * 4, (uint64_t)(H * W * C) * 4};
   if (!tma_aligned(t, st, 3)) return false;
   if (N > 0x7fffffff || H * W > 0x7fffffff) return false;
   if (make) {
-    uint32_t box[4] = {32, pix[0], pix[1], pix[2]};
+    uint32_t box[4] = {32, (uint32_t)pt.TW, (uint32_t)pt.TH, (uint32_t)pt.TN};
     make_map_f32(m, t, 4, dims, st, box, false);
   }
   return true;
@@ -134,14 +186,14 @@ static bool nhwc_map(CUtensorMap* m, const float* t, int64_t N, int64_t H, int64
 // 32-channel groups outermost (stride 128 B), box (32, pixel box, rows/32);
 // C % 32 == 0.
 static bool nhwc_mn_map(CUtensorMap* m, const float* t, int64_t N, int64_t H, int64_t W, int64_t C,
-                        const uint32_t pix[3], uint32_t rows, bool make) {
+                        const tma::PixTile& pt, uint32_t rows, bool make) {
   if (C % 32) return false;
   uint64_t dims[5] = {32, (uint64_t)W, (uint64_t)H, (uint64_t)N, (uint64_t)(C / 32)};
   uint64_t st[4] = {(uint64_t)C * 4, (uint64_t)(W * C) * 4, (uint64_t)(H * W * C) * 4, 128};
   if (!tma_aligned(t, st, 4)) return false;
   if (N > 0x7fffffff || H * W > 0x7fffffff) return false;
   if (make) {
-    uint32_t box[5] = {32, pix[0], pix[1], pix[2], rows / 32};
+    uint32_t box[5] = {32, (uint32_t)pt.TW, (uint32_t)pt.TH, (uint32_t)pt.TN, rows / 32};
     make_map_f32(m, t, 5, dims, st, box, true);
   }
   return true;
@@ -189,15 +241,16 @@ static void conv_fwd_nhwc(const NhwcShape& s, const float* x, const float* w, co
   float* wp = (float*)scratch2((size_t)s.Cout * K * sizeof(float));
   TP_LAUNCH(k_pack_filters, grid_for(s.Cout * K, 256), 256, 0, w, wp, s.Cout, s.Cin, khw, 0);
   EpRowMajor ep{y, s.Cout, 0, bias, 0};
-  uint32_t pix[3];
+  Tiling tl;
   MatOp b{wp, false, K, 0, false};
-  if (nhwc_tma_ok() && M >= 64 && s.Cin % 32 == 0 && pixel_box(s.OH, s.OW, tc::BM, pix) &&
-      nhwc_map(nullptr, x, s.N, s.H, s.W, s.Cin, pix, false) && mat_tma_ok(b, s.Cout)) {
+  if (nhwc_tma_ok() && M >= 64 && s.Cin % 32 == 0 && pixel_tiling(s.N, s.OH, s.OW, tc::BM, tl) &&
+      nhwc_map(nullptr, x, s.N, s.H, s.W, s.Cin, tl.pt, false) && mat_tma_ok(b, s.Cout)) {
     CUtensorMap ma, mb;
-    nhwc_map(&ma, x, s.N, s.H, s.W, s.Cin, pix, true);
+    nhwc_map(&ma, x, s.N, s.H, s.W, s.Cin, tl.pt, true);
     mat_map(&mb, b, s.Cout, K, 1, tma_bn(s.Cout));
-    tma::SrcConvK sa{(int)s.OH, (int)s.OW, (int)(s.Cin / 32), s.KW, s.PH, s.PW};
-    gemm_tma_bn(ma, mb, sa, tma::SrcK{0}, ep, M, s.Cout, K, 1);
+    tma::SrcConvK sa{tl.pt, (int)(s.Cin / 32), s.KW, s.PH, s.PW};
+    if (tl.linear) gemm_tma_bn(ma, mb, sa, tma::SrcK{0}, ep, M, s.Cout, K, 1);
+    else gemm_tma_bn(ma, mb, sa, tma::SrcK{0}, EpPixTile{y, s.Cout, s.N, bias, tl.pt}, tl.span, s.Cout, K, 1);
     return;
   }
   LdNhwcIm2col la{x, s.H, s.W, s.Cin, s.OH, s.OW, s.KW, s.PH, s.PW, M};
@@ -215,15 +268,16 @@ static void conv_dgrad_nhwc(const NhwcShape& s, const float* dy, const float* w,
   TP_LAUNCH(k_pack_filters, grid_for(s.Cout * s.Cin * khw, 256), 256, 0, w, wp, s.Cout, s.Cin, khw, 1);
   EpRowMajor ep{dx, s.Cin, 0, nullptr, 0};
   const int qh = s.KH - 1 - s.PH, qw = s.KW - 1 - s.PW;
-  uint32_t pix[3];
+  Tiling tl;
   MatOp b{wp, false, K, 0, false};
-  if (nhwc_tma_ok() && M >= 64 && s.Cout % 32 == 0 && pixel_box(s.H, s.W, tc::BM, pix) &&
-      nhwc_map(nullptr, dy, s.N, s.OH, s.OW, s.Cout, pix, false) && mat_tma_ok(b, s.Cin)) {
+  if (nhwc_tma_ok() && M >= 64 && s.Cout % 32 == 0 && pixel_tiling(s.N, s.H, s.W, tc::BM, tl) &&
+      nhwc_map(nullptr, dy, s.N, s.OH, s.OW, s.Cout, tl.pt, false) && mat_tma_ok(b, s.Cin)) {
     CUtensorMap ma, mb;
-    nhwc_map(&ma, dy, s.N, s.OH, s.OW, s.Cout, pix, true);
+    nhwc_map(&ma, dy, s.N, s.OH, s.OW, s.Cout, tl.pt, true);
     mat_map(&mb, b, s.Cin, K, 1, tma_bn(s.Cin));
-    tma::SrcConvK sa{(int)s.H, (int)s.W, (int)(s.Cout / 32), s.KW, qh, qw};
-    gemm_tma_bn(ma, mb, sa, tma::SrcK{0}, ep, M, s.Cin, K, 1);
+    tma::SrcConvK sa{tl.pt, (int)(s.Cout / 32), s.KW, qh, qw};
+    if (tl.linear) gemm_tma_bn(ma, mb, sa, tma::SrcK{0}, ep, M, s.Cin, K, 1);
+    else gemm_tma_bn(ma, mb, sa, tma::SrcK{0}, EpPixTile{dx, s.Cin, s.N, nullptr, tl.pt}, tl.span, s.Cin, K, 1);
     return;
   }
   LdNhwcIm2col la{dy, s.OH, s.OW, s.Cout, s.H, s.W, s.KW, qh, qw, M};
@@ -238,18 +292,18 @@ static void conv_wgrad_nhwc(const NhwcShape& s, const float* dy, const float* x,
     conv_c4_wgrad(dy, x, dw, s.N, s.H, s.W, s.Cout, s.PH, s.PW);
     return;
   }
-  uint32_t pix[3];
+  Tiling tl;
   const uint32_t bn = tma_bn(s.Cin);
-  if (nhwc_tma_ok() && s.Cout >= 64 && P > 0 && pixel_box(s.OH, s.OW, 32, pix) &&
-      nhwc_mn_map(nullptr, dy, s.N, s.OH, s.OW, s.Cout, pix, tc::BM, false) &&
-      nhwc_mn_map(nullptr, x, s.N, s.H, s.W, s.Cin, pix, bn, false)) {
+  if (nhwc_tma_ok() && s.Cout >= 64 && P > 0 && pixel_tiling(s.N, s.OH, s.OW, 32, tl) &&
+      nhwc_mn_map(nullptr, dy, s.N, s.OH, s.OW, s.Cout, tl.pt, tc::BM, false) &&
+      nhwc_mn_map(nullptr, x, s.N, s.H, s.W, s.Cin, tl.pt, bn, false)) {
     CUtensorMap ma, mb;
-    nhwc_mn_map(&ma, dy, s.N, s.OH, s.OW, s.Cout, pix, tc::BM, true);
-    nhwc_mn_map(&mb, x, s.N, s.H, s.W, s.Cin, pix, bn, true);
-    tma::SrcPixMN sa{(int)s.OH, (int)s.OW, s.KW, s.PH, s.PW, 0};
-    tma::SrcPixMN sb{(int)s.OH, (int)s.OW, s.KW, s.PH, s.PW, 1};
+    nhwc_mn_map(&ma, dy, s.N, s.OH, s.OW, s.Cout, tl.pt, tc::BM, true);
+    nhwc_mn_map(&mb, x, s.N, s.H, s.W, s.Cin, tl.pt, bn, true);
+    tma::SrcPixMN sa{tl.pt, s.KW, s.PH, s.PW, 0};
+    tma::SrcPixMN sb{tl.pt, s.KW, s.PH, s.PW, 1};
     EpWgradTap ep{dw, s.Cin, khw};
-    gemm_tma_bn(ma, mb, sa, sb, ep, s.Cout, s.Cin, P, khw);
+    gemm_tma_bn(ma, mb, sa, sb, ep, s.Cout, s.Cin, tl.span, khw);
     return;
   }
   const int64_t R = s.Cin * khw;
@@ -260,6 +314,57 @@ static void conv_wgrad_nhwc(const NhwcShape& s, const float* dy, const float* x,
   }
   LdNhwcWgradB lb{x, s.H, s.W, s.Cin, s.OH, s.OW, P, s.KH, s.KW, s.PH, s.PW};
   gemm_auto(LdColMajor{dy, s.Cout, 0}, lb, ep, s.Cout, R, P, 1);
+}
+
+// ---- NCHW convolutions through channels-last copies ----------------------------------------
+// The per-op API's tensors are NCHW (the reference's layout).  For shapes the
+// TMA-fed kernel takes, transposing the operands into channels-last scratch
+// copies (one coalesced pass each way) and back costs far less than the
+// gather kernel's per-element index work.
+
+static bool via_ok(const ConvShape& s) {
+  return gemm_path() == 0 && s.SH == 1 && s.SW == 1 && s.icpg == s.Cin && s.KH <= 7 && s.KW <= 7 &&
+         s.OH == s.H + 2 * s.PH - s.KH + 1 && s.OW == s.W + 2 * s.PW - s.KW + 1 && s.N * s.OH * s.OW >= 128;
+}
+
+static NhwcShape nhwc_of(const ConvShape& s) {
+  return NhwcShape{s.N, s.Cin, s.H, s.W, s.Cout, s.OH, s.OW, s.KH, s.KW, s.PH, s.PW};
+}
+
+bool conv_fwd_via_nhwc(const ConvShape& s, const float* x, const float* w, const float* bias, float* y) {
+  if (!via_ok(s) || s.Cin % 32 || s.Cout % 4 || (bias && ((uintptr_t)bias & 15))) return false;
+  float* xn = (float*)dalloc((size_t)s.N * s.H * s.W * s.Cin * 4);
+  float* yn = (float*)dalloc((size_t)s.N * s.OH * s.OW * s.Cout * 4);
+  transpose_nchw_nhwc(x, xn, s.N, s.Cin, s.H * s.W, true);
+  conv_fwd_nhwc(nhwc_of(s), xn, w, bias, yn);
+  transpose_nchw_nhwc(yn, y, s.N, s.Cout, s.OH * s.OW, false);
+  dfree(xn);
+  dfree(yn);
+  return true;
+}
+
+bool conv_dgrad_via_nhwc(const ConvShape& s, const float* dy, const float* w, float* dx) {
+  if (!via_ok(s) || s.Cout % 32 || s.Cin % 4 || s.PH > s.KH - 1 || s.PW > s.KW - 1) return false;
+  float* dyn = (float*)dalloc((size_t)s.N * s.OH * s.OW * s.Cout * 4);
+  float* dxn = (float*)dalloc((size_t)s.N * s.H * s.W * s.Cin * 4);
+  transpose_nchw_nhwc(dy, dyn, s.N, s.Cout, s.OH * s.OW, true);
+  conv_dgrad_nhwc(nhwc_of(s), dyn, w, dxn);
+  transpose_nchw_nhwc(dxn, dx, s.N, s.Cin, s.H * s.W, false);
+  dfree(dyn);
+  dfree(dxn);
+  return true;
+}
+
+bool conv_wgrad_via_nhwc(const ConvShape& s, const float* dy, const float* x, float* dw) {
+  if (!via_ok(s) || s.Cout % 32 || s.Cin % 32 || s.Cout < 64) return false;
+  float* dyn = (float*)dalloc((size_t)s.N * s.OH * s.OW * s.Cout * 4);
+  float* xn = (float*)dalloc((size_t)s.N * s.H * s.W * s.Cin * 4);
+  transpose_nchw_nhwc(dy, dyn, s.N, s.Cout, s.OH * s.OW, true);
+  transpose_nchw_nhwc(x, xn, s.N, s.Cin, s.H * s.W, true);
+  conv_wgrad_nhwc(nhwc_of(s), dyn, xn, dw);
+  dfree(dyn);
+  dfree(xn);
+  return true;
 }
 
 }  // namespace tp

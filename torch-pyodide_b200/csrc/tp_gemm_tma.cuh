@@ -126,46 +126,86 @@ struct SrcMN {
   }
 };
 
+// Pixel tiles of an OH x OW output grid (N images): a tile is a TW x TH
+// rectangle of one image (TN == 1, tiles_w x tiles_h tiles per image, the
+// last row / column of tiles may reach past the grid) or TN whole images.
+// Tile t covers GEMM rows (or k) [t*rows, (t+1)*rows) in the order w fastest,
+// then h, then image, which is the order a TMA box of extents (TW, TH, TN)
+// lands in shared memory.  With tiles_w == 1 and TW == OW the order is the
+// plain pixel order n*OH*OW + oh*OW + ow.
+struct PixTile {
+  int OH, OW, TW, TH, TN, tiles_w, tiles_h;
+  __device__ __forceinline__ void origin(int64_t t, int& n0, int& oh0, int& ow0) const {
+    if (TN > 1) {
+      n0 = (int)(t * TN);
+      oh0 = 0;
+      ow0 = 0;
+      return;
+    }
+    const int per = tiles_w * tiles_h;
+    n0 = (int)(t / per);
+    const int r = (int)(t - (int64_t)n0 * per);
+    oh0 = (r / tiles_w) * TH;
+    ow0 = (r - (r / tiles_w) * tiles_w) * TW;
+  }
+  // GEMM row m (tile = m / rows) -> pixel; false when it falls outside the grid
+  __device__ __forceinline__ bool pixel(int64_t m, int rows, int64_t N, int& n, int& oh, int& ow) const {
+    const int64_t t = m / rows;
+    const int r = (int)(m - t * rows);
+    int n0, oh0, ow0;
+    origin(t, n0, oh0, ow0);
+    const int twh = TW * TH;
+    n = n0 + r / twh;
+    const int rr = r - (r / twh) * twh;
+    oh = oh0 + rr / TW;
+    ow = ow0 + (rr - (rr / TW) * TW);
+    return n < N && oh < OH && ow < OW;
+  }
+};
+
 // K-major implicit-GEMM operand of a stride-1 convolution over a channels-last
-// [N][H][W][C] input: tile rows = 128 consecutive output pixels (n, oh, ow) of
-// the OH x OW grid, k-block = (tap, 32 channels) with taps outermost.  Map
-// dims (C, W, H, N), box (32, OW, rows, images); the tap shift moves the box
-// origin and the zero fill outside the input is the padding.
+// [N][H][W][C] input: tile rows = the 128 output pixels of one pixel tile,
+// k-block = (tap, 32 channels) with taps outermost.  Map dims (C, W, H, N),
+// box (32, TW, TH, TN); the tap shift moves the box origin and the zero fill
+// outside the input is the padding.
 struct SrcConvK {
   static constexpr bool kMN = false;
-  int OH, OW, cblocks, KW, PH, PW;
+  PixTile pt;
+  int cblocks, KW, PH, PW;
   template <int ROWS>
   __device__ __forceinline__ void issue(const CUtensorMap* map, uint32_t dst, uint64_t* bar, int, int64_t r0,
                                         int64_t k0) const {
-    const int64_t hw = (int64_t)OH * OW;
-    const int n0 = (int)(r0 / hw), oh0 = (int)((r0 - (int64_t)n0 * hw) / OW);
+    int n0, oh0, ow0;
+    pt.origin(r0 / ROWS, n0, oh0, ow0);
     const int kb = (int)(k0 >> 5), tap = kb / cblocks, c0 = (kb - tap * cblocks) * 32;
     const int kh = tap / KW, kw = tap - kh * KW;
-    load4(dst, map, c0, kw - PW, oh0 + kh - PH, n0, bar);
+    load4(dst, map, c0, ow0 + kw - PW, oh0 + kh - PH, n0, bar);
   }
 };
 
 // MN-major operand of the per-tap weight gradient over a channels-last tensor:
-// tile rows = channels, k = output pixels (n, oh, ow), 32 per k-block.  Batch
-// index b = tap; with `shift` the pixel reads move by the tap offset (the
-// input x), without it they do not (the output gradient dy).  Map dims
-// (32, W, H, N, C/32): channel groups of 32 as the outermost dimension
-// (stride 128 B), box (32, OW, rows, images, ROWS/32) covering 32 pixels of
-// every group of the tile in one copy.
+// tile rows = channels, k = output pixels in pixel-tile order, one 32-pixel
+// tile per k-block.  Batch index b = tap; with `shift` the pixel reads move by
+// the tap offset (the input x), without it they do not (the output gradient
+// dy); pixels outside the grid read zeros in dy, so they add nothing.  Map
+// dims (32, W, H, N, C/32): channel groups of 32 as the outermost dimension
+// (stride 128 B), box (32, TW, TH, TN, ROWS/32) covering every group of the
+// tile in one copy.
 struct SrcPixMN {
   static constexpr bool kMN = true;
-  int OH, OW, KW, PH, PW, shift;
+  PixTile pt;
+  int KW, PH, PW, shift;
   template <int ROWS>
   __device__ __forceinline__ void issue(const CUtensorMap* map, uint32_t dst, uint64_t* bar, int b, int64_t r0,
                                         int64_t k0) const {
-    const int64_t hw = (int64_t)OH * OW;
-    const int n0 = (int)(k0 / hw), oh0 = (int)((k0 - (int64_t)n0 * hw) / OW);
+    int n0, oh0, ow0;
+    pt.origin(k0 >> 5, n0, oh0, ow0);
     int dh = 0, dw = 0;
     if (shift) {
       dh = b / KW - PH;
       dw = b - (b / KW) * KW - PW;
     }
-    load5(dst, map, 0, dw, oh0 + dh, n0, (int)(r0 >> 5), bar);
+    load5(dst, map, 0, ow0 + dw, oh0 + dh, n0, (int)(r0 >> 5), bar);
   }
 };
 

@@ -50,6 +50,16 @@ void conv_fwd(const ConvShape& s, const float* x, const float* w, const float* b
 void conv_dgrad(const ConvShape& s, const float* dy, const float* w, float* dx);
 void conv_wgrad(const ConvShape& s, const float* dy, const float* x, float* dw);
 void launch_channel_sum(const float* x, int64_t N, int64_t C, int64_t P, float* out);
+
+// tp_nhwc.cu: [N][C][HW] <-> [N][HW][C]
+void transpose_nchw_nhwc(const float* in, float* out, int64_t N, int64_t C, int64_t HW, bool to_nhwc);
+
+// tp_conv_nhwc.cu: NCHW convolutions run through channels-last copies on the
+// TMA-fed kernel when the shape allows it (stride 1, groups 1, channel counts
+// multiples of 32); false (nothing launched) otherwise
+bool conv_fwd_via_nhwc(const ConvShape& s, const float* x, const float* w, const float* bias, float* y);
+bool conv_dgrad_via_nhwc(const ConvShape& s, const float* dy, const float* w, float* dx);
+bool conv_wgrad_via_nhwc(const ConvShape& s, const float* dy, const float* x, float* dw);
 void matmul_launch(const float* A, const float* B, float* C, int64_t batch, int64_t M, int64_t K, int64_t N,
                    bool b_batched);
 void linear_launch(const float* x, const float* w, const float* bias, float* y, int64_t M, int64_t K, int64_t N,

@@ -416,6 +416,43 @@ __global__ void k_nchw_to_nhwc(const float* __restrict__ x, float* __restrict__ 
   }
 }
 
+// [N][C][HW] <-> [N][HW][C] through 32 x 32 shared-memory tiles (both sides
+// coalesced).  grid (ceil(HW/32), ceil(C/32), N), block (32, 8).
+template <bool TO_NHWC>
+__global__ void k_transpose_cs(const float* __restrict__ in, float* __restrict__ out, int64_t C, int64_t HW) {
+  __shared__ float t[32][33];
+  const int64_t n = blockIdx.z, p0 = (int64_t)blockIdx.x * 32, c0 = (int64_t)blockIdx.y * 32;
+  const float* src = in + n * C * HW;
+  float* dst = out + n * C * HW;
+  for (int j = threadIdx.y; j < 32; j += 8) {
+    if (TO_NHWC) {  // read rows of C: in[c][p]
+      const int64_t c = c0 + j, p = p0 + threadIdx.x;
+      t[j][threadIdx.x] = (c < C && p < HW) ? src[c * HW + p] : 0.0f;
+    } else {  // read rows of HW: in[p][c]
+      const int64_t p = p0 + j, c = c0 + threadIdx.x;
+      t[j][threadIdx.x] = (c < C && p < HW) ? src[p * C + c] : 0.0f;
+    }
+  }
+  __syncthreads();
+  for (int j = threadIdx.y; j < 32; j += 8) {
+    if (TO_NHWC) {  // write out[p][c]
+      const int64_t p = p0 + j, c = c0 + threadIdx.x;
+      if (c < C && p < HW) dst[p * C + c] = t[threadIdx.x][j];
+    } else {  // write out[c][p]
+      const int64_t c = c0 + j, p = p0 + threadIdx.x;
+      if (c < C && p < HW) dst[c * HW + p] = t[threadIdx.x][j];
+    }
+  }
+}
+
+void transpose_nchw_nhwc(const float* in, float* out, int64_t N, int64_t C, int64_t HW, bool to_nhwc) {
+  if (N == 0 || C == 0 || HW == 0) return;
+  TP_REQUIRE(N <= 65535 && (C + 31) / 32 <= 65535, "layout transpose: tensor too large for the grid");
+  dim3 grid((unsigned)((HW + 31) / 32), (unsigned)((C + 31) / 32), (unsigned)N), block(32, 8);
+  if (to_nhwc) TP_LAUNCH(k_transpose_cs<true>, grid, block, 0, in, out, C, HW);
+  else TP_LAUNCH(k_transpose_cs<false>, grid, block, 0, in, out, C, HW);
+}
+
 static void check_vec(const void* p, const char* what) {
   TP_REQUIRE(((uintptr_t)p & 15) == 0, "%s: channels-last buffers must be 16-byte aligned", what);
 }

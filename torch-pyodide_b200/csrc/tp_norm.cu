@@ -300,6 +300,81 @@ __global__ void k_ln_bwd(const float* __restrict__ dy, const float* __restrict__
   }
 }
 
+// Rows of D <= 256*PER: each thread owns PER columns for all the CTA's rows, so
+// a row's dy and x are read once, and its share of dgamma / dbeta stays in
+// registers until one partial row per CTA is written.
+template <int PER>
+__global__ void __launch_bounds__(256) k_ln_bwd_reg(const float* __restrict__ dy, const float* __restrict__ x,
+                                                    const float* __restrict__ g, const float* __restrict__ smean,
+                                                    const float* __restrict__ srstd, float* __restrict__ dx,
+                                                    float* __restrict__ ws, int64_t rows, int64_t D, int rpb) {
+  __shared__ float sh[2][8];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t r0 = (int64_t)blockIdx.x * rpb;
+  float gv[PER], pgx[PER], pgd[PER];
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    const int64_t i = threadIdx.x + (int64_t)k * 256;
+    gv[k] = (i < D) ? (g ? g[i] : 1.0f) : 0.0f;
+    pgx[k] = 0.0f;
+    pgd[k] = 0.0f;
+  }
+  const float inv_d = 1.0f / (float)D;
+  for (int64_t r = r0; r < r0 + rpb && r < rows; ++r) {
+    const float* dyr = dy + r * D;
+    const float* xr = x + r * D;
+    const float mu = smean[r], rs = srstd[r];
+    float dv[PER], xh[PER];
+    float a = 0.0f, bb = 0.0f;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int64_t i = threadIdx.x + (int64_t)k * 256;
+      dv[k] = i < D ? dyr[i] : 0.0f;
+      xh[k] = i < D ? (xr[i] - mu) * rs : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const float gd = gv[k] * dv[k];
+      a += gd;
+      bb += gd * xh[k];
+      pgx[k] += dv[k] * xh[k];
+      pgd[k] += dv[k];
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+      a += __shfl_xor_sync(0xffffffffu, a, o);
+      bb += __shfl_xor_sync(0xffffffffu, bb, o);
+    }
+    if (lane == 0) {
+      sh[0][w] = a;
+      sh[1][w] = bb;
+    }
+    __syncthreads();
+    float ta = 0.0f, tb = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      ta += sh[0][k];
+      tb += sh[1][k];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int64_t i = threadIdx.x + (int64_t)k * 256;
+      if (i < D) dx[r * D + i] = rs * (gv[k] * dv[k] - ta * inv_d - xh[k] * tb * inv_d);
+    }
+  }
+  if (ws) {
+    float* pg = ws + (int64_t)blockIdx.x * 2 * D;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int64_t i = threadIdx.x + (int64_t)k * 256;
+      if (i < D) {
+        pg[i] = pgx[k];
+        pg[D + i] = pgd[k];
+      }
+    }
+  }
+}
+
 __global__ void k_colsum_partials(const float* __restrict__ ws, int nblk, int64_t D, float* __restrict__ dg,
                                   float* __restrict__ db) {
   int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
@@ -332,7 +407,11 @@ void launch_ln_bwd(const float* dy, const float* x, const float* g, const float*
   if (rpb < 1) rpb = 1;
   int nblk = (int)((rows + rpb - 1) / rpb);
   float* ws = (dg || db) ? (float*)scratch((size_t)nblk * 2 * D * sizeof(float)) : nullptr;
-  TP_LAUNCH(k_ln_bwd, (unsigned)nblk, 256, 0, dy, x, g, sm, sr, dx, ws, rows, D, rpb);
+  if (D <= 256 * 4) TP_LAUNCH(k_ln_bwd_reg<4>, (unsigned)nblk, 256, 0, dy, x, g, sm, sr, dx, ws, rows, D, rpb);
+  else if (D <= 256 * 8) TP_LAUNCH(k_ln_bwd_reg<8>, (unsigned)nblk, 256, 0, dy, x, g, sm, sr, dx, ws, rows, D, rpb);
+  else if (D <= 256 * 16)
+    TP_LAUNCH(k_ln_bwd_reg<16>, (unsigned)nblk, 256, 0, dy, x, g, sm, sr, dx, ws, rows, D, rpb);
+  else TP_LAUNCH(k_ln_bwd, (unsigned)nblk, 256, 0, dy, x, g, sm, sr, dx, ws, rows, D, rpb);
   if (ws) TP_LAUNCH(k_colsum_partials, (unsigned)((D + 255) / 256), 256, 0, ws, nblk, D, dg, db);
 }
 

@@ -184,11 +184,26 @@ __global__ void k_reduce_rows_block(const float* __restrict__ x, int64_t rows, i
   } else {
     float v = -FLT_MAX;
     int vi = INT_MAX;
-    for (int64_t i = threadIdx.x; i < red; i += blockDim.x) {
-      float t = xr[i];
-      if (vi == INT_MAX || t > v) {
-        v = t;
-        vi = (int)i;
+    if ((red & 3) == 0 && (((uintptr_t)xr) & 15) == 0) {
+      // 16-byte loads; within a vector the first maximum wins (strict >)
+      const float4* x4 = reinterpret_cast<const float4*>(xr);
+      for (int64_t i = threadIdx.x; i < (red >> 2); i += blockDim.x) {
+        const float4 q = x4[i];
+        const float t[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (vi == INT_MAX || t[j] > v) {
+            v = t[j];
+            vi = (int)(4 * i + j);
+          }
+      }
+    } else {
+      for (int64_t i = threadIdx.x; i < red; i += blockDim.x) {
+        float t = xr[i];
+        if (vi == INT_MAX || t > v) {
+          v = t;
+          vi = (int)i;
+        }
       }
     }
     warp_argmax(v, vi);
@@ -261,6 +276,93 @@ __global__ void k_reduce_cols(const float* __restrict__ x, int64_t outer, int64_
   }
 }
 
+// inner % 4 == 0: thread x takes 4 adjacent columns (16-byte loads), rows
+// step by 8 with 4 rows of loads in flight; grid (ceil(inner/128), outer,
+// splits).  Same per-column combination order as k_reduce_cols.
+__global__ void k_reduce_cols4(const float* __restrict__ x, int64_t outer, int64_t red, int64_t inner, int mode,
+                               int splits, float* __restrict__ out, int32_t* __restrict__ idx,
+                               float* __restrict__ wsv, int32_t* __restrict__ wsi) {
+  __shared__ float4 shv[8][32];
+  __shared__ int4 shi[8][32];
+  const int64_t c4 = (int64_t)blockIdx.x * 32 + threadIdx.x, col = 4 * c4;
+  const int64_t o = blockIdx.y;
+  const int split = blockIdx.z;
+  const int64_t per = (red + splits - 1) / splits;
+  const int64_t r0 = split * per, r1 = r0 + per < red ? r0 + per : red;
+  const bool is_sum = mode <= 1;
+  float acc[4];
+  int ai[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    acc[j] = is_sum ? 0.0f : -FLT_MAX;
+    ai[j] = INT_MAX;
+  }
+  if (col < inner) {
+    const float* base = x + o * red * inner + col;
+    int64_t r = r0 + threadIdx.y;
+    for (; r + 24 < r1; r += 32) {
+      float4 q[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) q[u] = *reinterpret_cast<const float4*>(base + (r + 8 * u) * inner);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float t[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (is_sum) acc[j] += t[j];
+          else if (ai[j] == INT_MAX || t[j] > acc[j]) {
+            acc[j] = t[j];
+            ai[j] = (int)(r + 8 * u);
+          }
+        }
+      }
+    }
+    for (; r < r1; r += 8) {
+      const float4 q = *reinterpret_cast<const float4*>(base + r * inner);
+      const float t[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (is_sum) acc[j] += t[j];
+        else if (ai[j] == INT_MAX || t[j] > acc[j]) {
+          acc[j] = t[j];
+          ai[j] = (int)r;
+        }
+      }
+    }
+  }
+  shv[threadIdx.y][threadIdx.x] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+  shi[threadIdx.y][threadIdx.x] = make_int4(ai[0], ai[1], ai[2], ai[3]);
+  __syncthreads();
+  if (threadIdx.y == 0 && col < inner) {
+    for (int k = 1; k < 8; ++k) {
+      const float4 qv = shv[k][threadIdx.x];
+      const int4 qi = shi[k][threadIdx.x];
+      const float v[4] = {qv.x, qv.y, qv.z, qv.w};
+      const int vi[4] = {qi.x, qi.y, qi.z, qi.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (is_sum) acc[j] += v[j];
+        else if (vi[j] != INT_MAX && (ai[j] == INT_MAX || v[j] > acc[j] || (v[j] == acc[j] && vi[j] < ai[j]))) {
+          acc[j] = v[j];
+          ai[j] = vi[j];
+        }
+      }
+    }
+    const int64_t oi = o * inner + col;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (col + j >= inner) break;
+      if (splits == 1) {
+        out[oi + j] = (mode == 1) ? acc[j] / (float)red : acc[j];
+        if (idx) idx[oi + j] = ai[j];
+      } else {
+        wsv[(int64_t)split * outer * inner + oi + j] = acc[j];
+        if (wsi) wsi[(int64_t)split * outer * inner + oi + j] = ai[j];
+      }
+    }
+  }
+}
+
 __global__ void k_reduce_cols_finish(int64_t n, int64_t red, int mode, int splits, const float* __restrict__ wsv,
                                      const int32_t* __restrict__ wsi, float* __restrict__ out,
                                      int32_t* __restrict__ idx) {
@@ -298,7 +400,7 @@ void launch_reduce_dim(const float* x, int64_t outer, int64_t red, int64_t inner
     }
     return;
   }
-  int64_t tiles = ((inner + 31) / 32) * outer;
+  int64_t tiles = ((inner + ((inner & 3) == 0 ? 127 : 31)) / ((inner & 3) == 0 ? 128 : 32)) * outer;
   int splits = 1;
   int64_t target = (int64_t)sm_count() * 8;
   while (tiles * splits < target && red / (splits * 2) >= 64 && splits < 64) splits *= 2;
@@ -311,7 +413,12 @@ void launch_reduce_dim(const float* x, int64_t outer, int64_t red, int64_t inner
     wsv = (float*)scratch(nb);
     if (need_idx) wsi = (int32_t*)(wsv + (size_t)splits * nout);
   }
-  TP_LAUNCH(k_reduce_cols, grid, dim3(32, 8), 0, x, outer, red, inner, mode, splits, out, idx, wsv, wsi);
+  if ((inner & 3) == 0 && (((uintptr_t)x) & 15) == 0) {
+    dim3 grid4((unsigned)((inner + 127) / 128), (unsigned)outer, (unsigned)splits);
+    TP_LAUNCH(k_reduce_cols4, grid4, dim3(32, 8), 0, x, outer, red, inner, mode, splits, out, idx, wsv, wsi);
+  } else {
+    TP_LAUNCH(k_reduce_cols, grid, dim3(32, 8), 0, x, outer, red, inner, mode, splits, out, idx, wsv, wsi);
+  }
   if (splits > 1)
     TP_LAUNCH(k_reduce_cols_finish, (unsigned)((nout + 255) / 256), 256, 0, nout, red, mode, splits, wsv, wsi,
               out, idx);
@@ -344,7 +451,11 @@ __global__ void __launch_bounds__(256) k_softmax_rows(const float* __restrict__ 
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
       int64_t i = threadIdx.x + (int64_t)k * 256;
-      if (i < C) s += expf(v[k] - m);
+      if (i < C) {
+        const float e = expf(v[k] - m);
+        s += e;
+        if (!LOG) v[k] = e;  // kept for the output pass: one exp per element
+      }
     }
   } else {
     for (int64_t i = threadIdx.x; i < C; i += 256) s += expf(xr[i] - m);
@@ -355,7 +466,7 @@ __global__ void __launch_bounds__(256) k_softmax_rows(const float* __restrict__ 
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
       int64_t i = threadIdx.x + (int64_t)k * 256;
-      if (i < C) yr[i] = LOG ? (v[k] - m) - lse : expf(v[k] - m) / s;
+      if (i < C) yr[i] = LOG ? (v[k] - m) - lse : v[k] / s;
     }
   } else {
     for (int64_t i = threadIdx.x; i < C; i += 256) yr[i] = LOG ? (xr[i] - m) - lse : expf(xr[i] - m) / s;
@@ -381,13 +492,17 @@ __global__ void k_softmax_rows_warp(const float* __restrict__ x, float* __restri
   float s = 0.0f;
 #pragma unroll
   for (int k = 0; k < 8; ++k)
-    if (lane + k * 32 < C) s += expf(v[k] - m);
+    if (lane + k * 32 < C) {
+      const float e = expf(v[k] - m);
+      s += e;
+      if (!LOG) v[k] = e;
+    }
   s = warp_sum(s);
   float lse = logf(s);
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
     int64_t i = lane + k * 32;
-    if (i < C) y[row * C + i] = LOG ? (v[k] - m) - lse : expf(v[k] - m) / s;
+    if (i < C) y[row * C + i] = LOG ? (v[k] - m) - lse : v[k] / s;
   }
 }
 
