@@ -87,3 +87,23 @@ def test_vgg_conv_shapes(cuda_rt, oracle_rt, path, cin, cout, hw, batch):
     close_scaled(cuda_rt, oracle_rt, cuda_rt.conv2dWeightBackward(cg["id"], cx["id"], ws, ys, xs, [1], [1]),
                  oracle_rt.conv2dWeightBackward(og["id"], ox["id"], ws, ys, xs, [1], [1]))
     assert status(cuda_rt) == 0
+
+
+@pytest.mark.parametrize("xs,ws,st,pd", [([2, 3, 20, 20], [16, 3, 7, 7], 2, 3), ([3, 2, 11, 13], [8, 2, 3, 3], 2, 1),
+                                         ([2, 4, 9, 9], [12, 4, 5, 5], 3, 2)])
+def test_conv_strided_few_channels(cuda_rt, oracle_rt, path, xs, ws, st, pd):
+    """Strided convolutions with few input channels (a network stem): forward,
+    data gradient (the phase-decomposed CUDA-core kernel on engine 0) and
+    weight gradient against the oracle."""
+    rng = np.random.default_rng(sum(xs) + st)
+    cx, ox = both(cuda_rt, oracle_rt, rng.standard_normal(xs))
+    cw, ow = both(cuda_rt, oracle_rt, rng.standard_normal(ws) * 0.1)
+    y = oracle_rt.conv2d(ox["id"], ow["id"], None, [st], [pd], [1], 1)
+    close_scaled(cuda_rt, oracle_rt, cuda_rt.conv2d(cx["id"], cw["id"], None, [st], [pd], [1], 1), y)
+    ys = y["shape"]
+    cg, og = both(cuda_rt, oracle_rt, rng.standard_normal(ys))
+    close_scaled(cuda_rt, oracle_rt, cuda_rt.conv2dInputBackward(cg["id"], cw["id"], xs, ys, [st], [pd]),
+                 oracle_rt.conv2dInputBackward(og["id"], ow["id"], xs, ys, [st], [pd]))
+    close_scaled(cuda_rt, oracle_rt, cuda_rt.conv2dWeightBackward(cg["id"], cx["id"], ws, ys, xs, [st], [pd]),
+                 oracle_rt.conv2dWeightBackward(og["id"], ox["id"], ws, ys, xs, [st], [pd]))
+    assert status(cuda_rt) == 0

@@ -117,6 +117,10 @@ void conv_fwd(const ConvShape& s, const float* x, const float* w, const float* b
 
 void conv_dgrad(const ConvShape& s, const float* dy, const float* w, float* dx) {
   if (conv_dgrad_via_nhwc(s, dy, w, dx)) return;
+  if (g_gemm_path == 0 && s.icpg == s.Cin &&
+      conv_dgrad_smallc(dy, w, dx, s.N, s.Cin, s.H, s.W, s.Cout, s.OH, s.OW, s.KH, s.KW, s.SH, s.PH, s.PW,
+                        s.SH == s.SW))
+    return;
   int khw = s.KH * s.KW;
   int64_t M = s.N * s.H * s.W, K = s.Cout * khw;
   EpNCHW ep{dx, nullptr, s.Cin, s.H * s.W, (int)s.Cin};

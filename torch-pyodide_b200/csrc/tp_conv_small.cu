@@ -14,6 +14,7 @@
 #include <cuda_runtime.h>
 
 #include "tp_core.h"
+#include "tp_launch.h"
 
 namespace tp {
 
@@ -194,6 +195,91 @@ __global__ void k_conv_c4_wgrad_finish(const float* __restrict__ part, int split
     for (int k = 0; k < 8; ++k) t += sl[k][lane];
     dw[i] = (float)t;
   }
+}
+
+// ---- data gradient for a few input channels (NCHW dx), any stride ----------------------------
+// dx[n][ci][ih][iw] = sum over (co, kh, kw) with ih + P - kh = oh*S (and the same
+// for w) of dy[n][co][oh][ow] * w[co][ci][kh][kw], dy read channels-last.
+// Input pixels are taken phase by phase (ih mod S, iw mod S), so the threads
+// of a warp share their filter taps: thread = (n, phase, y', x'), 4 input
+// channels in registers, filter taps from shared memory as float4 over ci.
+// The reference's stride-aware data-gradient shader does the same sum one
+// thread per input element (conv_backward.wgsl:24-61).
+__global__ void __launch_bounds__(256)
+    k_conv_dgrad_smallc(const float4* __restrict__ dy, const float* __restrict__ w, float* __restrict__ dx, int N,
+                        int Cin, int H, int W, int Cout, int OH, int OW, int KH, int KW, int S, int P) {
+  extern __shared__ float4 wt[];  // [kh][kw][co]: (w[co][0..3][kh][kw])
+  const int T = KH * KW, G = Cout >> 2;
+  for (int i = threadIdx.x; i < T * Cout; i += blockDim.x) {
+    const int co = i % Cout, tap = i / Cout;
+    float v[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) v[c] = c < Cin ? w[((int64_t)co * Cin + c) * T + tap] : 0.0f;
+    wt[i] = make_float4(v[0], v[1], v[2], v[3]);
+  }
+  __syncthreads();
+  // phase grid: per image S*S phases of ceil(H/S) x ceil(W/S) input pixels
+  const int HP = (H + S - 1) / S, WP = (W + S - 1) / S;
+  const int64_t per_img = (int64_t)S * S * HP * WP;
+  const int64_t total = (int64_t)N * per_img;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    const int n = (int)(t / per_img);
+    int64_t r = t - (int64_t)n * per_img;
+    const int xq = (int)(r % WP);
+    r /= WP;
+    const int yq = (int)(r % HP);
+    const int ph = (int)(r / HP);
+    const int rh = ph / S, rw = ph - (ph / S) * S;
+    const int ih = yq * S + rh, iw = xq * S + rw;
+    if (ih >= H || iw >= W) continue;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int kh = (rh + P) % S; kh < KH; kh += S) {
+      const int oh = (ih + P - kh) / S;
+      if (oh < 0 || oh >= OH) continue;
+      for (int kw = (rw + P) % S; kw < KW; kw += S) {
+        const int ow = (iw + P - kw) / S;
+        if (ow < 0 || ow >= OW) continue;
+        const float4* drow = dy + (((int64_t)n * OH + oh) * OW + ow) * G;
+        const float4* wrow = wt + (kh * KW + kw) * Cout;
+        for (int g = 0; g < G; ++g) {
+          const float4 d = drow[g];
+          const float ds[4] = {d.x, d.y, d.z, d.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float4 q = wrow[4 * g + j];
+            acc[0] = fmaf(ds[j], q.x, acc[0]);
+            acc[1] = fmaf(ds[j], q.y, acc[1]);
+            acc[2] = fmaf(ds[j], q.z, acc[2]);
+            acc[3] = fmaf(ds[j], q.w, acc[3]);
+          }
+        }
+      }
+    }
+    for (int c = 0; c < Cin; ++c) dx[(((int64_t)n * Cin + c) * H + ih) * W + iw] = acc[c];
+  }
+}
+
+// NCHW data gradient for Cin <= 4 through a channels-last copy of dy; false
+// if the shape does not qualify.
+bool conv_dgrad_smallc(const float* dy, const float* w, float* dx, int64_t N, int64_t Cin, int64_t H, int64_t W,
+                       int64_t Cout, int64_t OH, int64_t OW, int KH, int KW, int S, int PH, int PW, bool same_stride) {
+  if (Cin > 4 || Cout % 4 || Cout > 256 || KH * KW > 49 || !same_stride || PH != PW || KH != KW) return false;
+  if (N * OH * OW * Cout >= ((int64_t)1 << 31) || N * Cin * H * W >= ((int64_t)1 << 31)) return false;
+  float* dyn = (float*)dalloc((size_t)N * OH * OW * Cout * 4);
+  transpose_nchw_nhwc(dy, dyn, N, Cout, OH * OW, true);
+  const size_t shb = (size_t)KH * KW * Cout * sizeof(float4);
+  static bool attr = false;
+  if (!attr) {
+    TP_CUDA(cudaFuncSetAttribute(k_conv_dgrad_smallc, cudaFuncAttributeMaxDynamicSharedMemorySize, 49 * 256 * 16));
+    attr = true;
+  }
+  const int64_t HP = (H + S - 1) / S, WP = (W + S - 1) / S, total = N * S * S * HP * WP;
+  int64_t blocks = (total + 255) / 256, cap = (int64_t)sm_count() * 16;
+  TP_LAUNCH(k_conv_dgrad_smallc, (unsigned)(blocks < cap ? blocks : cap), 256, shb,
+            reinterpret_cast<const float4*>(dyn), w, dx, (int)N, (int)Cin, (int)H, (int)W, (int)Cout, (int)OH,
+            (int)OW, KH, KW, S, PH);
+  dfree(dyn);
+  return true;
 }
 
 // True when the 4-channel kernels apply: x has exactly 4 channels, 3x3

@@ -60,6 +60,10 @@ void transpose_nchw_nhwc(const float* in, float* out, int64_t N, int64_t C, int6
 bool conv_fwd_via_nhwc(const ConvShape& s, const float* x, const float* w, const float* bias, float* y);
 bool conv_dgrad_via_nhwc(const ConvShape& s, const float* dy, const float* w, float* dx);
 bool conv_wgrad_via_nhwc(const ConvShape& s, const float* dy, const float* x, float* dw);
+
+// tp_conv_small.cu: NCHW data gradient for Cin <= 4 (any stride) on CUDA cores
+bool conv_dgrad_smallc(const float* dy, const float* w, float* dx, int64_t N, int64_t Cin, int64_t H, int64_t W,
+                       int64_t Cout, int64_t OH, int64_t OW, int KH, int KW, int S, int PH, int PW, bool same_stride);
 void matmul_launch(const float* A, const float* B, float* C, int64_t batch, int64_t M, int64_t K, int64_t N,
                    bool b_batched);
 void linear_launch(const float* x, const float* w, const float* bias, float* y, int64_t M, int64_t K, int64_t N,
