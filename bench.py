@@ -627,7 +627,7 @@ def run_vgg(args, rank, world, local):
     conv_args = (ctypes.c_void_p(xin), ctypes.c_void_p(model.p("conv3.w")), ctypes.c_void_p(model.p("conv3.b")),
                  ctypes.c_void_p(b4["z"]), B, b4["cin"], b4["H"], b4["W"], b4["cout"], 3, 3)
     if model.layout == "nhwc":
-        conv_fn, conv_args = lib.tpk_conv2d_fwd_nhwc, conv_args + (1, 1)
+        conv_fn, conv_args = lib.tpk_conv2d_fwd_nhwc, conv_args + (1, 1, model.filter_layout(3))
     else:
         conv_fn, conv_args = lib.tpk_conv2d_fwd, conv_args + (1, 1, 1, 1)
     conv_fn(*conv_args)

@@ -306,16 +306,18 @@ TP_API int tpk_conv2d_wgrad(const float* dy, const float* x, float* dw, int64_t 
                             int64_t Cout, int KH, int KW, int SH, int SW, int PH, int PW);
 /* The same three on channels-last buffers: x [N][H][W][Cin], y / dy
  * [N][OH][OW][Cout], stride 1, dilation 1, groups 1, OH = H + 2PH - KH + 1.
- * Filters w and the filter gradient dw keep the reference layout
- * [Cout][Cin][KH][KW].  No reference counterpart: the reference's shaders are
- * NCHW only (conv.wgsl:25-60, conv_backward.wgsl:24-101); these serve a
- * training step that keeps its activations channels-last (tpcuda.vgg). */
+ * filter_layout 0: w and dw in the reference layout [Cout][Cin][KH][KW];
+ * 1: [Cout][KH][KW][Cin], which the forward uses as it is, the data gradient
+ * reads in place and the weight gradient writes with contiguous stores.  No
+ * reference counterpart: the reference's shaders are NCHW only (conv.wgsl:25-60,
+ * conv_backward.wgsl:24-101); these serve a training step that keeps its
+ * activations channels-last (tpcuda.vgg). */
 TP_API int tpk_conv2d_fwd_nhwc(const float* x, const float* w, const float* bias, float* y, int64_t N, int64_t Cin,
-                               int64_t H, int64_t W, int64_t Cout, int KH, int KW, int PH, int PW);
+                               int64_t H, int64_t W, int64_t Cout, int KH, int KW, int PH, int PW, int filter_layout);
 TP_API int tpk_conv2d_dgrad_nhwc(const float* dy, const float* w, float* dx, int64_t N, int64_t Cin, int64_t H,
-                                 int64_t W, int64_t Cout, int KH, int KW, int PH, int PW);
+                                 int64_t W, int64_t Cout, int KH, int KW, int PH, int PW, int filter_layout);
 TP_API int tpk_conv2d_wgrad_nhwc(const float* dy, const float* x, float* dw, int64_t N, int64_t Cin, int64_t H,
-                                 int64_t W, int64_t Cout, int KH, int KW, int PH, int PW);
+                                 int64_t W, int64_t Cout, int KH, int KW, int PH, int PW, int filter_layout);
 /* Channels-last ([P][C], P = pixels) companions of tpk_bn_train,
  * tpk_bn_backward, tpk_channel_sum and tpk_maxpool_fwd / _bwd (2x2, stride
  * 2), for the same step; C % 4 == 0 and 16-byte aligned buffers.  Pool

@@ -132,9 +132,9 @@ def test_conv_nhwc_matches_nchw(cuda_rt, engine, cin, cout, hw, batch):
     assert L.tpk_conv2d_dgrad(vp(pdy), vp(pw), vp(dx0), batch, cin, hw, hw, cout, 3, 3, 1, 1, 1, 1) == 0
     assert L.tpk_conv2d_wgrad(vp(pdy), vp(px), vp(dw0), batch, cin, hw, hw, cout, 3, 3, 1, 1, 1, 1) == 0
     engine(0)
-    assert L.tpk_conv2d_fwd_nhwc(vp(pxn), vp(pw), vp(pb), vp(y1), batch, cin, hw, hw, cout, 3, 3, 1, 1) == 0
-    assert L.tpk_conv2d_dgrad_nhwc(vp(pdyn), vp(pw), vp(dx1), batch, cin, hw, hw, cout, 3, 3, 1, 1) == 0
-    assert L.tpk_conv2d_wgrad_nhwc(vp(pdyn), vp(pxn), vp(dw1), batch, cin, hw, hw, cout, 3, 3, 1, 1) == 0
+    assert L.tpk_conv2d_fwd_nhwc(vp(pxn), vp(pw), vp(pb), vp(y1), batch, cin, hw, hw, cout, 3, 3, 1, 1, 0) == 0
+    assert L.tpk_conv2d_dgrad_nhwc(vp(pdyn), vp(pw), vp(dx1), batch, cin, hw, hw, cout, 3, 3, 1, 1, 0) == 0
+    assert L.tpk_conv2d_wgrad_nhwc(vp(pdyn), vp(pxn), vp(dw1), batch, cin, hw, hw, cout, 3, 3, 1, 1, 0) == 0
     assert status(rt) == 0
     ref_y = read(rt, y0, (batch, cout, hw, hw))
     got_y = nchw(read(rt, y1, (batch, hw, hw, cout)))
@@ -165,11 +165,40 @@ def test_conv_nhwc_against_oracle(cuda_rt, oracle_rt, cin, cout, hw, batch):
     y, dx, dw = empty(rt, dy.size), empty(rt, x.size), empty(rt, w.size)
     vp = ctypes.c_void_p
     L = rt.lib
-    assert L.tpk_conv2d_fwd_nhwc(vp(pxn), vp(pw), None, vp(y), batch, cin, hw, hw, cout, 3, 3, 1, 1) == 0
-    assert L.tpk_conv2d_dgrad_nhwc(vp(pdyn), vp(pw), vp(dx), batch, cin, hw, hw, cout, 3, 3, 1, 1) == 0
-    assert L.tpk_conv2d_wgrad_nhwc(vp(pdyn), vp(pxn), vp(dw), batch, cin, hw, hw, cout, 3, 3, 1, 1) == 0
+    assert L.tpk_conv2d_fwd_nhwc(vp(pxn), vp(pw), None, vp(y), batch, cin, hw, hw, cout, 3, 3, 1, 1, 0) == 0
+    assert L.tpk_conv2d_dgrad_nhwc(vp(pdyn), vp(pw), vp(dx), batch, cin, hw, hw, cout, 3, 3, 1, 1, 0) == 0
+    assert L.tpk_conv2d_wgrad_nhwc(vp(pdyn), vp(pxn), vp(dw), batch, cin, hw, hw, cout, 3, 3, 1, 1, 0) == 0
     assert status(rt) == 0
     close64(nchw(read(rt, y, (batch, hw, hw, cout))), ref_y)
     close64(nchw(read(rt, dx, (batch, hw, hw, cin))), ref_dx)
     close64(read(rt, dw, w.shape), ref_dw)
     free(rt, pxn, pw, pdyn, y, dx, dw)
+
+
+@pytest.mark.parametrize("cin,cout,hw,batch", [(64, 128, 16, 4), (256, 256, 8, 8), (512, 512, 2, 8), (32, 64, 20, 2),
+                                               (48, 96, 8, 4)])
+def test_conv_nhwc_packed_filters(cuda_rt, engine, cin, cout, hw, batch):
+    """Filters stored [Cout][KH][KW][Cin] (filter_layout 1) give the same
+    forward, data gradient and (permuted) weight gradient as the reference
+    layout."""
+    rt, L, vp = cuda_rt, cuda_rt.lib, ctypes.c_void_p
+    rng = np.random.default_rng(cin + cout + hw + batch + 7)
+    x = rng.standard_normal((batch, hw, hw, cin)).astype(np.float32)
+    w = (rng.standard_normal((cout, cin, 3, 3)) * 0.05).astype(np.float32)
+    wk = np.ascontiguousarray(w.transpose(0, 2, 3, 1))
+    b = rng.standard_normal(cout).astype(np.float32)
+    dy = rng.standard_normal((batch, hw, hw, cout)).astype(np.float32)
+    px, pw, pwk, pb, pdy = dev(rt, x), dev(rt, w), dev(rt, wk), dev(rt, b), dev(rt, dy)
+    outs = []
+    for lay, pw_ in ((0, pw), (1, pwk)):
+        y, dx, dw = empty(rt, dy.size), empty(rt, x.size), empty(rt, w.size)
+        assert L.tpk_conv2d_fwd_nhwc(vp(px), vp(pw_), vp(pb), vp(y), batch, cin, hw, hw, cout, 3, 3, 1, 1, lay) == 0
+        assert L.tpk_conv2d_dgrad_nhwc(vp(pdy), vp(pw_), vp(dx), batch, cin, hw, hw, cout, 3, 3, 1, 1, lay) == 0
+        assert L.tpk_conv2d_wgrad_nhwc(vp(pdy), vp(px), vp(dw), batch, cin, hw, hw, cout, 3, 3, 1, 1, lay) == 0
+        g = read(rt, dw, (cout, 3, 3, cin)).transpose(0, 3, 1, 2) if lay else read(rt, dw, w.shape)
+        outs.append((read(rt, y, dy.shape), read(rt, dx, x.shape), np.ascontiguousarray(g)))
+        free(rt, y, dx, dw)
+    assert status(rt) == 0
+    free(rt, px, pw, pwk, pb, pdy)
+    for a, c in zip(outs[0], outs[1]):
+        close64(c, a.astype(np.float64), rel=1e-5)

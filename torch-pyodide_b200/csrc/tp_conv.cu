@@ -79,6 +79,7 @@ ConvShape conv_shape(int64_t N, int64_t Cin, int64_t H, int64_t W, int64_t Cout,
 // Repack filters for the filter-major K order k = (kh, kw, c):
 //   mode 0 (forward):  wp[o][tap][c] = w[o][c][tap]             (o < Cout, c < icpg)
 //   mode 1 (dgrad):    wp[i][tap][o] = w[o][i][KHW-1-tap]        (flipped, in/out swapped)
+//   mode 2 (dgrad):    the same from filters stored w[o][tap][i]
 __global__ void k_pack_filters(const float* __restrict__ w, float* __restrict__ wp, int64_t Cout, int64_t Cin_pg,
                                int khw, int mode) {
   int64_t total = Cout * Cin_pg * khw;
@@ -87,6 +88,13 @@ __global__ void k_pack_filters(const float* __restrict__ w, float* __restrict__ 
     int tap = (int)(i % khw);
     int64_t t = i / khw;
     int64_t c = t % Cin_pg, o = t / Cin_pg;  // w index i = (o*Cin_pg + c)*khw + tap
+    if (mode == 2) {  // source stored [o][tap][c] (same flipped, transposed destination as mode 1)
+      const int64_t c2 = i % Cin_pg, t2 = i / Cin_pg;
+      const int tap2 = (int)(t2 % khw);
+      const int64_t o2 = t2 / khw;
+      wp[(c2 * khw + (khw - 1 - tap2)) * Cout + o2] = w[i];
+      continue;
+    }
     float v = w[i];
     if (mode == 0) wp[(o * khw + tap) * Cin_pg + c] = v;
     else wp[(c * khw + (khw - 1 - tap)) * Cout + o] = v;

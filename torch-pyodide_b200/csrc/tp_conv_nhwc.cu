@@ -60,12 +60,13 @@ struct LdNhwcIm2col {
   int64_t rows;  // N * OH * OW
 };
 
-// Weight gradient B operand: row r = (ci, kh, kw) (reference filter order),
-// k = output pixel (n, oh, ow) -> x[n, oh+kh-PH, ow+kw-PW, ci].
+// Weight gradient B operand: row r = (ci, kh, kw) (reference filter order) or
+// (kh, kw, ci), k = output pixel (n, oh, ow) -> x[n, oh+kh-PH, ow+kw-PW, ci].
 struct LdNhwcWgradB {
   const float* x;
   int64_t H, W, C, OH, OW, P;
   int KH, KW, PH, PW;
+  int khwc;  // rows r = (kh, kw, ci) (filters stored [Cout][KH][KW][Cin]) instead of (ci, kh, kw)
   static constexpr bool kContigK = true;
   struct Kc {
     int64_t n;
@@ -84,10 +85,19 @@ struct LdNhwcWgradB {
   }
   __device__ __forceinline__ float at(int, int64_t r, const Kc& c) const {
     if (!c.ok || r >= C * KH * KW) return 0.0f;
-    int kw = (int)(r % KW);
-    int64_t t = r / KW;
-    int kh = (int)(t % KH);
-    int64_t ci = t / KH;
+    int kw, kh;
+    int64_t ci;
+    if (khwc) {
+      ci = r % C;
+      const int tap = (int)(r / C);
+      kh = tap / KW;
+      kw = tap - kh * KW;
+    } else {
+      kw = (int)(r % KW);
+      int64_t t = r / KW;
+      kh = (int)(t % KH);
+      ci = t / KH;
+    }
     int64_t ih = c.oh + kh - PH, iw = c.ow + kw - PW;
     if (ih < 0 || ih >= H || iw < 0 || iw >= W) return 0.0f;
     return x[((c.n * H + ih) * W + iw) * C + ci];
@@ -206,13 +216,17 @@ static bool nhwc_tma_ok() { return gemm_path() == 0; }
 struct NhwcShape {
   int64_t N, Cin, H, W, Cout, OH, OW;
   int KH, KW, PH, PW;
+  bool khwc;  // filters stored [Cout][KH][KW][Cin] (else the reference's [Cout][Cin][KH][KW])
 };
 
 static NhwcShape nhwc_shape(int64_t N, int64_t Cin, int64_t H, int64_t W, int64_t Cout, int KH, int KW, int PH,
-                            int PW) {
+                            int PW, int filter_layout) {
   TP_REQUIRE(N >= 0 && Cin > 0 && H > 0 && W > 0 && Cout > 0, "conv2d (channels-last): bad shape");
   TP_REQUIRE(KH > 0 && KW > 0 && PH >= 0 && PW >= 0, "conv2d (channels-last): bad kernel or padding");
-  NhwcShape s{N, Cin, H, W, Cout, H + 2 * PH - KH + 1, W + 2 * PW - KW + 1, KH, KW, PH, PW};
+  TP_REQUIRE(filter_layout == 0 || filter_layout == 1,
+             "conv2d (channels-last): filter layout must be 0 ([Cout][Cin][KH][KW]) or 1 ([Cout][KH][KW][Cin])");
+  NhwcShape s{N,  Cin, H,  W,  Cout, H + 2 * PH - KH + 1, W + 2 * PW - KW + 1, KH, KW,
+              PH, PW,  filter_layout == 1};
   TP_REQUIRE(s.OH > 0 && s.OW > 0, "conv2d (channels-last): output would be empty");
   return s;
 }
@@ -233,13 +247,18 @@ static void conv_fwd_nhwc(const NhwcShape& s, const float* x, const float* w, co
   const int khw = s.KH * s.KW;
   const int64_t M = s.N * s.OH * s.OW, K = s.Cin * khw;
   if (M == 0) return;
-  if (conv_c4_ok(s.N, s.H, s.W, s.Cin, s.KH, s.KW, s.Cout, x, y) &&
+  if (!s.khwc && conv_c4_ok(s.N, s.H, s.W, s.Cin, s.KH, s.KW, s.Cout, x, y) &&
       (bias == nullptr || ((uintptr_t)bias & 15) == 0)) {
     conv_c4_fwd(x, w, bias, y, s.N, s.H, s.W, s.Cout, s.PH, s.PW);
     return;
   }
-  float* wp = (float*)scratch2((size_t)s.Cout * K * sizeof(float));
-  TP_LAUNCH(k_pack_filters, grid_for(s.Cout * K, 256), 256, 0, w, wp, s.Cout, s.Cin, khw, 0);
+  // K order (kh, kw, c): filters stored that way are used as they are
+  const float* wp = w;
+  if (!s.khwc) {
+    float* t = (float*)scratch2((size_t)s.Cout * K * sizeof(float));
+    TP_LAUNCH(k_pack_filters, grid_for(s.Cout * K, 256), 256, 0, w, t, s.Cout, s.Cin, khw, 0);
+    wp = t;
+  }
   EpRowMajor ep{y, s.Cout, 0, bias, 0};
   Tiling tl;
   MatOp b{wp, false, K, 0, false};
@@ -264,14 +283,29 @@ static void conv_dgrad_nhwc(const NhwcShape& s, const float* dy, const float* w,
   const int64_t M = s.N * s.H * s.W, K = s.Cout * khw;
   if (M == 0) return;
   TP_REQUIRE(s.PH <= s.KH - 1 && s.PW <= s.KW - 1, "conv2d data gradient (channels-last): padding exceeds kernel-1");
-  float* wp = (float*)scratch2((size_t)s.Cin * K * sizeof(float));
-  TP_LAUNCH(k_pack_filters, grid_for(s.Cout * s.Cin * khw, 256), 256, 0, w, wp, s.Cout, s.Cin, khw, 1);
   EpRowMajor ep{dx, s.Cin, 0, nullptr, 0};
   const int qh = s.KH - 1 - s.PH, qw = s.KW - 1 - s.PW;
   Tiling tl;
+  const bool tma_a = nhwc_tma_ok() && M >= 64 && s.Cout % 32 == 0 && pixel_tiling(s.N, s.H, s.W, tc::BM, tl) &&
+                     nhwc_map(nullptr, dy, s.N, s.OH, s.OW, s.Cout, tl.pt, false);
+  if (tma_a && s.khwc && s.Cin % 32 == 0 && ((uintptr_t)w & 15) == 0) {
+    // filters stored [Cout][tap][Cin] are read in place as the MN-major B
+    CUtensorMap ma, mb;
+    nhwc_map(&ma, dy, s.N, s.OH, s.OW, s.Cout, tl.pt, true);
+    uint64_t dims[4] = {32, (uint64_t)khw, (uint64_t)s.Cout, (uint64_t)(s.Cin / 32)};
+    uint64_t st[3] = {(uint64_t)s.Cin * 4, (uint64_t)(khw * s.Cin) * 4, 128};
+    uint32_t box[4] = {32, 1, 32, tma_bn(s.Cin) / 32};
+    make_map_f32(&mb, w, 4, dims, st, box, true);
+    tma::SrcConvK sa{tl.pt, (int)(s.Cout / 32), s.KW, qh, qw};
+    tma::SrcFilterMN sb{(int)(s.Cout / 32), khw};
+    if (tl.linear) gemm_tma_bn(ma, mb, sa, sb, ep, M, s.Cin, K, 1);
+    else gemm_tma_bn(ma, mb, sa, sb, EpPixTile{dx, s.Cin, s.N, nullptr, tl.pt}, tl.span, s.Cin, K, 1);
+    return;
+  }
+  float* wp = (float*)scratch2((size_t)s.Cin * K * sizeof(float));
+  TP_LAUNCH(k_pack_filters, grid_for(s.Cout * s.Cin * khw, 256), 256, 0, w, wp, s.Cout, s.Cin, khw, s.khwc ? 2 : 1);
   MatOp b{wp, false, K, 0, false};
-  if (nhwc_tma_ok() && M >= 64 && s.Cout % 32 == 0 && pixel_tiling(s.N, s.H, s.W, tc::BM, tl) &&
-      nhwc_map(nullptr, dy, s.N, s.OH, s.OW, s.Cout, tl.pt, false) && mat_tma_ok(b, s.Cin)) {
+  if (tma_a && mat_tma_ok(b, s.Cin)) {
     CUtensorMap ma, mb;
     nhwc_map(&ma, dy, s.N, s.OH, s.OW, s.Cout, tl.pt, true);
     mat_map(&mb, b, s.Cin, K, 1, tma_bn(s.Cin));
@@ -288,7 +322,7 @@ static void conv_dgrad_nhwc(const NhwcShape& s, const float* dy, const float* w,
 static void conv_wgrad_nhwc(const NhwcShape& s, const float* dy, const float* x, float* dw) {
   const int khw = s.KH * s.KW;
   const int64_t P = s.N * s.OH * s.OW;
-  if (conv_c4_ok(s.N, s.H, s.W, s.Cin, s.KH, s.KW, s.Cout, x, dy)) {
+  if (!s.khwc && conv_c4_ok(s.N, s.H, s.W, s.Cin, s.KH, s.KW, s.Cout, x, dy)) {
     conv_c4_wgrad(dy, x, dw, s.N, s.H, s.W, s.Cout, s.PH, s.PW);
     return;
   }
@@ -302,8 +336,8 @@ static void conv_wgrad_nhwc(const NhwcShape& s, const float* dy, const float* x,
     nhwc_mn_map(&mb, x, s.N, s.H, s.W, s.Cin, tl.pt, bn, true);
     tma::SrcPixMN sa{tl.pt, s.KW, s.PH, s.PW, 0};
     tma::SrcPixMN sb{tl.pt, s.KW, s.PH, s.PW, 1};
-    EpWgradTap ep{dw, s.Cin, khw};
-    gemm_tma_bn(ma, mb, sa, sb, ep, s.Cout, s.Cin, tl.span, khw);
+    if (s.khwc) gemm_tma_bn(ma, mb, sa, sb, EpWgradTapKhwc{dw, s.Cin, khw}, s.Cout, s.Cin, tl.span, khw);
+    else gemm_tma_bn(ma, mb, sa, sb, EpWgradTap{dw, s.Cin, khw}, s.Cout, s.Cin, tl.span, khw);
     return;
   }
   const int64_t R = s.Cin * khw;
@@ -312,7 +346,7 @@ static void conv_wgrad_nhwc(const NhwcShape& s, const float* dy, const float* x,
     launch_fill(dw, s.Cout * R, 0.0f);
     return;
   }
-  LdNhwcWgradB lb{x, s.H, s.W, s.Cin, s.OH, s.OW, P, s.KH, s.KW, s.PH, s.PW};
+  LdNhwcWgradB lb{x, s.H, s.W, s.Cin, s.OH, s.OW, P, s.KH, s.KW, s.PH, s.PW, s.khwc ? 1 : 0};
   gemm_auto(LdColMajor{dy, s.Cout, 0}, lb, ep, s.Cout, R, P, 1);
 }
 
@@ -328,7 +362,7 @@ static bool via_ok(const ConvShape& s) {
 }
 
 static NhwcShape nhwc_of(const ConvShape& s) {
-  return NhwcShape{s.N, s.Cin, s.H, s.W, s.Cout, s.OH, s.OW, s.KH, s.KW, s.PH, s.PW};
+  return NhwcShape{s.N, s.Cin, s.H, s.W, s.Cout, s.OH, s.OW, s.KH, s.KW, s.PH, s.PW, false};
 }
 
 bool conv_fwd_via_nhwc(const ConvShape& s, const float* x, const float* w, const float* bias, float* y) {
@@ -374,18 +408,20 @@ using namespace tp;
 extern "C" {
 
 TP_API int tpk_conv2d_fwd_nhwc(const float* x, const float* w, const float* bias, float* y, int64_t N, int64_t Cin,
-                               int64_t H, int64_t W, int64_t Cout, int KH, int KW, int PH, int PW) {
-  return guard([&] { conv_fwd_nhwc(nhwc_shape(N, Cin, H, W, Cout, KH, KW, PH, PW), x, w, bias, y); });
+                               int64_t H, int64_t W, int64_t Cout, int KH, int KW, int PH, int PW,
+                               int filter_layout) {
+  return guard(
+      [&] { conv_fwd_nhwc(nhwc_shape(N, Cin, H, W, Cout, KH, KW, PH, PW, filter_layout), x, w, bias, y); });
 }
 
 TP_API int tpk_conv2d_dgrad_nhwc(const float* dy, const float* w, float* dx, int64_t N, int64_t Cin, int64_t H,
-                                 int64_t W, int64_t Cout, int KH, int KW, int PH, int PW) {
-  return guard([&] { conv_dgrad_nhwc(nhwc_shape(N, Cin, H, W, Cout, KH, KW, PH, PW), dy, w, dx); });
+                                 int64_t W, int64_t Cout, int KH, int KW, int PH, int PW, int filter_layout) {
+  return guard([&] { conv_dgrad_nhwc(nhwc_shape(N, Cin, H, W, Cout, KH, KW, PH, PW, filter_layout), dy, w, dx); });
 }
 
 TP_API int tpk_conv2d_wgrad_nhwc(const float* dy, const float* x, float* dw, int64_t N, int64_t Cin, int64_t H,
-                                 int64_t W, int64_t Cout, int KH, int KW, int PH, int PW) {
-  return guard([&] { conv_wgrad_nhwc(nhwc_shape(N, Cin, H, W, Cout, KH, KW, PH, PW), dy, x, dw); });
+                                 int64_t W, int64_t Cout, int KH, int KW, int PH, int PW, int filter_layout) {
+  return guard([&] { conv_wgrad_nhwc(nhwc_shape(N, Cin, H, W, Cout, KH, KW, PH, PW, filter_layout), dy, x, dw); });
 }
 
 }  // extern "C"

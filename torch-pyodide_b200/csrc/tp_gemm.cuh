@@ -420,4 +420,18 @@ struct EpWgradTap {
   }
 };
 
+// Per-tap weight gradient into filters stored [Cout][KHW][Cin]:
+// C_tap[oc][ic] -> dw[oc, tap, ic] (16 consecutive ic are one contiguous run).
+struct EpWgradTapKhwc {
+  float* dw;
+  int64_t Cin;
+  int KHW;
+  __device__ __forceinline__ void operator()(int tap, int64_t oc, int64_t ic, float v) const {
+    dw[(oc * KHW + tap) * Cin + ic] = v;
+  }
+  __device__ __forceinline__ void row16(int b, int64_t m, int64_t n0, int64_t N, const float (&v)[16]) const {
+    EpRowMajor{dw + (m * KHW + b) * Cin, 0, 0, nullptr, 0}.row16(0, 0, n0, N, v);
+  }
+};
+
 }  // namespace tp

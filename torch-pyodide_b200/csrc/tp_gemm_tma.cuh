@@ -209,6 +209,21 @@ struct SrcPixMN {
   }
 };
 
+// MN-major B of the flipped-filter data gradient, read from filters stored
+// [Cout][KH*KW][Cin]: rows = input channels, k = (flipped tap, output channel)
+// with taps outermost, 32 output channels per k-block.  Map dims
+// (32, KH*KW, Cout, Cin/32), box (32, 1, 32, ROWS/32).
+struct SrcFilterMN {
+  static constexpr bool kMN = true;
+  int cblocks, KHW;
+  template <int ROWS>
+  __device__ __forceinline__ void issue(const CUtensorMap* map, uint32_t dst, uint64_t* bar, int, int64_t r0,
+                                        int64_t k0) const {
+    const int kb = (int)(k0 >> 5), tf = kb / cblocks, co0 = (kb - tf * cblocks) * 32;
+    load4(dst, map, 0, KHW - 1 - tf, co0, (int)(r0 >> 5), bar);
+  }
+};
+
 template <int BN, int STAGES>
 struct Smem {
   static constexpr uint32_t A_BYTES = BM * BK * 4;  // raw A (TMA); its hi/lo go to TMEM

@@ -146,9 +146,9 @@ SIGNATURES: dict[str, list] = {
     "tpk_maxpool2x2_nhwc_fwd": [P, P, P, I64, I64, I64, I64],
     "tpk_maxpool2x2_nhwc_bwd": [P, P, P, I64, I64, I64, I64],
     "tpk_nchw_to_nhwc": [P, P, I64, I64, I64, I64, I64],
-    "tpk_conv2d_fwd_nhwc": [P, P, P, P, I64, I64, I64, I64, I64, INT, INT, INT, INT],
-    "tpk_conv2d_dgrad_nhwc": [P, P, P, I64, I64, I64, I64, I64, INT, INT, INT, INT],
-    "tpk_conv2d_wgrad_nhwc": [P, P, P, I64, I64, I64, I64, I64, INT, INT, INT, INT],
+    "tpk_conv2d_fwd_nhwc": [P, P, P, P, I64, I64, I64, I64, I64, INT, INT, INT, INT, INT],
+    "tpk_conv2d_dgrad_nhwc": [P, P, P, I64, I64, I64, I64, I64, INT, INT, INT, INT, INT],
+    "tpk_conv2d_wgrad_nhwc": [P, P, P, I64, I64, I64, I64, I64, INT, INT, INT, INT, INT],
     "tpk_channel_sum": [P, I64, I64, I64, P],
     "tpk_bn_train": [P, P, P, P, P, P, P, P, I64, I64, I64, F32, F32, INT],
     "tpk_bn_backward": [P, P, P, P, P, P, P, P, P, I64, I64, I64],

@@ -23,8 +23,11 @@ arrives NCHW and is converted on the device into a channels-last buffer whose
 3 channels are zero-padded to 4 (one 16-byte vector per pixel, the form the
 first layer's CUDA-core kernels read); the first conv's filters are stored
 with the same padding, their padded channel stays exactly zero (zero input,
-zero gradient, zero decay).  layout="nchw" runs
-the same step on the NCHW kernels of the per-op API, as a cross-check.
+zero gradient, zero decay).  The other convs' filters are stored
+[Cout][3][3][Cin]: the forward uses them as they are, the data gradient reads
+them in place and the weight gradient writes that layout with contiguous
+stores, so no filter is repacked per step.  layout="nchw" runs the same step
+on the NCHW kernels of the per-op API, as a cross-check.
 
 The whole step is captured once into a CUDA graph and replayed.  Semantics:
 PyTorch's (SGD momentum 0.9 with weight decay 5e-4, dampening 0; BN momentum
@@ -71,12 +74,13 @@ def plan_blocks(cfg=CFG, in_ch: int = 3, size: int = 32) -> list[dict]:
 CIN0_PAD = 4  # channels of the first conv's input as stored channels-last
 
 
-def plan_params(blocks: list[dict], feat: int, cin0_store: int = 3) -> tuple[list, dict, int]:
+def plan_params(blocks: list[dict], feat: int, cin0_store: int = 3, khwc: bool = False) -> tuple[list, dict, int]:
     """Parameter specs (name, shape, init) in the order backward finishes
     them (fc first, conv1 last), their (offset, stored numel) in the flat
     buffers (each tensor starts on a 256-byte boundary) and the flat length.
     The first conv's filters are stored as [Cout][cin0_store][3][3] (input
-    channels zero-padded when cin0_store > 3)."""
+    channels zero-padded when cin0_store > 3); with khwc the other convs'
+    filters are stored [Cout][3][3][Cin] (see store_shape)."""
     specs = []
     specs.append(("fc.w", [NUM_CLASSES, feat], ("kaiming", feat)))
     specs.append(("fc.b", [NUM_CLASSES], ("bias", feat)))
@@ -90,20 +94,48 @@ def plan_params(blocks: list[dict], feat: int, cin0_store: int = 3) -> tuple[lis
     offsets = {}
     off = 0
     for name, shape, _ in specs:
-        n = int(np.prod(store_shape(name, shape, cin0_store)))
+        n = int(np.prod(store_shape(name, shape, cin0_store, khwc)))
         offsets[name] = (off, n)
         off += (n + 63) // 64 * 64
     return specs, offsets, off
 
 
-def store_shape(name: str, shape: list, cin0_store: int) -> list:
-    """Stored shape of a parameter (the first conv's filters may be padded)."""
-    if name == "conv0.w" and cin0_store != shape[1]:
-        return [shape[0], cin0_store, shape[2], shape[3]]
+def store_shape(name: str, shape: list, cin0_store: int, khwc: bool = False) -> list:
+    """Stored shape of a parameter: the first conv's filters may be padded
+    ([Cout][cin0_store][3][3]); with khwc the other convs' filters are stored
+    [Cout][KH][KW][Cin], the order the channels-last convolutions read them
+    in place."""
+    if name == "conv0.w":
+        return [shape[0], cin0_store, shape[2], shape[3]] if cin0_store != shape[1] else list(shape)
+    if khwc and name.startswith("conv") and name.endswith(".w"):
+        return [shape[0], shape[2], shape[3], shape[1]]
     return list(shape)
 
 
-def init_params(specs: list, offsets: dict, flat_len: int, seed: int, cin0_store: int = 3) -> np.ndarray:
+def to_store(name: str, v: np.ndarray, shape: list, cin0_store: int, khwc: bool = False) -> np.ndarray:
+    """A parameter's values in its logical (reference) layout -> stored layout (flat)."""
+    st = store_shape(name, shape, cin0_store, khwc)
+    if st == list(shape):
+        return np.ascontiguousarray(v, np.float32).ravel()
+    if name == "conv0.w":
+        w = np.zeros(st, np.float32)
+        w[:, :shape[1]] = v.reshape(shape)
+        return w.ravel()
+    return np.ascontiguousarray(v.reshape(shape).transpose(0, 2, 3, 1)).ravel()
+
+
+def to_logical(name: str, v: np.ndarray, shape: list, cin0_store: int, khwc: bool = False) -> np.ndarray:
+    """The inverse of to_store."""
+    st = store_shape(name, shape, cin0_store, khwc)
+    if st == list(shape):
+        return v
+    if name == "conv0.w":
+        return np.ascontiguousarray(v.reshape(st)[:, :shape[1]]).ravel()
+    return np.ascontiguousarray(v.reshape(st).transpose(0, 3, 1, 2)).ravel()
+
+
+def init_params(specs: list, offsets: dict, flat_len: int, seed: int, cin0_store: int = 3,
+                khwc: bool = False) -> np.ndarray:
     """The flat parameter buffer on the host: PyTorch's default Conv2d/Linear
     init (kaiming_uniform_ with a=sqrt(5), i.e. U(+-1/sqrt(fan_in)), for
     weights and biases), BN gamma 1 and beta 0; padding zero.  The values do
@@ -118,12 +150,7 @@ def init_params(specs: list, offsets: dict, flat_len: int, seed: int, cin0_store
             v = rng.uniform(-bound, bound, n).astype(np.float32)
         else:
             v = np.full(n, init[1], np.float32)
-        st = store_shape(name, shape, cin0_store)
-        if st != list(shape):
-            w = np.zeros(st, np.float32)
-            w[:, :shape[1]] = v.reshape(shape)
-            v = w.ravel()
-        host[o:o + n_store] = v
+        host[o:o + n_store] = to_store(name, v, shape, cin0_store, khwc)
     return host
 
 
@@ -159,6 +186,7 @@ class VGG11BN:
             raise ValueError(f"layout must be 'nhwc' or 'nchw', got {layout!r}")
         self.layout = layout
         self.cin0 = CIN0_PAD if layout == "nhwc" else 3
+        self.khwc = layout == "nhwc"  # conv filters (but the first) stored [Cout][3][3][Cin]
         self.rt, self.lib = rt, rt.lib
         self.B = int(batch)
         self.lr, self.momentum, self.wd = lr, momentum, weight_decay
@@ -176,13 +204,13 @@ class VGG11BN:
         # ---- parameters, gradients, momentum: one flat buffer each, laid out in
         # the order backward finishes them so gradient buckets close in
         # backward order ----
-        specs, self.offsets, self.flat_len = plan_params(self.blocks, self.feat, self.cin0)
+        specs, self.offsets, self.flat_len = plan_params(self.blocks, self.feat, self.cin0, self.khwc)
         self.param_specs = specs
         self.nparams = sum(int(np.prod(s)) for _, s, _ in specs)
         self.params = self._alloc(self.flat_len * 4)
         self.grads = self._alloc(self.flat_len * 4)
         self.moms = self._alloc(self.flat_len * 4)
-        self._h2d(self.params, init_params(specs, self.offsets, self.flat_len, seed, self.cin0))
+        self._h2d(self.params, init_params(specs, self.offsets, self.flat_len, seed, self.cin0, self.khwc))
         check(self.lib.tp_memset(_vp(self.grads), 0, self.flat_len * 4))
         check(self.lib.tp_memset(_vp(self.moms), 0, self.flat_len * 4))
 
@@ -269,7 +297,8 @@ class VGG11BN:
             gam, bet = _vp(self.p(f"bn{li}.g")), _vp(self.p(f"bn{li}.b"))
             stats = (_vp(b["rm"]), _vp(b["rv"]), _vp(b["a"]), _vp(b["mean"]), _vp(b["invstd"]))
             if nhwc:
-                check(L.tpk_conv2d_fwd_nhwc(_vp(x), w, bias, _vp(b["z"]), Bn, cin, H, W, C, 3, 3, 1, 1))
+                check(L.tpk_conv2d_fwd_nhwc(_vp(x), w, bias, _vp(b["z"]), Bn, cin, H, W, C, 3, 3, 1, 1,
+                                            self.filter_layout(li)))
                 check(L.tpk_bn_train_nhwc(_vp(b["z"]), gam, bet, *stats, Bn * H * W, C, 1e-5, 0.1, 1))
                 if b["pool"]:
                     check(L.tpk_maxpool2x2_nhwc_fwd(_vp(b["a"]), _vp(b["p"]), _vp(b["idx"]), Bn, H, W, C))
@@ -328,7 +357,8 @@ class VGG11BN:
             if nhwc:
                 # the conv bias gradient (the per-channel sum of dz) comes out of the BN backward pass
                 check(L.tpk_bn_backward_nhwc(*bn_args, db, P, C))
-                check(L.tpk_conv2d_wgrad_nhwc(_vp(dz), _vp(xin), dw, Bn, cin, H, W, C, 3, 3, 1, 1))
+                check(L.tpk_conv2d_wgrad_nhwc(_vp(dz), _vp(xin), dw, Bn, cin, H, W, C, 3, 3, 1, 1,
+                                              self.filter_layout(li)))
             else:
                 check(L.tpk_bn_backward(*bn_args, Bn, C, H * W))
                 check(L.tpk_channel_sum(_vp(dz), Bn, C, H * W, db))
@@ -338,7 +368,8 @@ class VGG11BN:
                 dx = self.gbuf[buf]
                 buf ^= 1
                 if nhwc:
-                    check(L.tpk_conv2d_dgrad_nhwc(_vp(dz), w, _vp(dx), Bn, cin, H, W, C, 3, 3, 1, 1))
+                    check(L.tpk_conv2d_dgrad_nhwc(_vp(dz), w, _vp(dx), Bn, cin, H, W, C, 3, 3, 1, 1,
+                                                  self.filter_layout(li)))
                 else:
                     check(L.tpk_conv2d_dgrad(_vp(dz), w, _vp(dx), Bn, cin, H, W, C, 3, 3, 1, 1, 1, 1))
                 gout = dx
@@ -389,12 +420,12 @@ class VGG11BN:
 
     def _logical(self, base: int, name: str) -> np.ndarray:
         o, n = self.offsets[name]
-        v = self.read(base + 4 * o, n)
         shape = dict((nm, s) for nm, s, _ in self.param_specs)[name]
-        st = store_shape(name, shape, self.cin0)
-        if st != list(shape):
-            v = np.ascontiguousarray(v.reshape(st)[:, :shape[1]]).ravel()
-        return v
+        return to_logical(name, self.read(base + 4 * o, n), shape, self.cin0, self.khwc)
+
+    def filter_layout(self, li: int) -> int:
+        """filter_layout argument of the channels-last conv entry points for block li."""
+        return 1 if self.khwc and li > 0 else 0
 
     def param_array(self, name: str) -> np.ndarray:
         """Parameter `name` in its logical (reference) layout."""
