@@ -332,6 +332,25 @@ TP_API int tpk_bn_train_nhwc(const float* x, const float* w, const float* b, flo
 TP_API int tpk_bn_backward_nhwc(const float* dy, const float* x, const float* relu_src, const float* w,
                                 const float* mean, const float* invstd, float* dx, float* dw, float* db,
                                 float* dx_sum, int64_t P, int64_t C);
+/* BatchNorm train forward (+ReLU when relu) fused with the 2x2 / stride-2
+ * max-pool after it: x [N][H][W][C] -> pooled y [N][H/2][W/2][C] and idx (plane
+ * offsets h*W + w of each window's maximum, as tpk_maxpool2x2_nhwc_fwd); the
+ * full-size activation a is written only when a is not NULL.  Same values as
+ * tpk_bn_train_nhwc followed by tpk_maxpool2x2_nhwc_fwd. */
+TP_API int tpk_bn_train_pool_nhwc(const float* x, const float* w, const float* b, float* running_mean,
+                                  float* running_var, float* y, int32_t* idx, float* a, float* save_mean,
+                                  float* save_invstd, int64_t N, int64_t H, int64_t W, int64_t C, float eps,
+                                  float momentum, int relu);
+/* BatchNorm backward whose ReLU mask (relu != 0) is recomputed from x with
+ * the forward's formula (gamma w, beta b), so no activation is read.  idx NULL:
+ * g is the gradient at the BN(+ReLU) output, [N][H][W][C].  idx given: g is the
+ * gradient of the 2x2 / stride-2 max-pool that followed, [N][H/2][W/2][C], with
+ * that pool's idx, and is routed to each window's argmax in place (the same
+ * values as tpk_maxpool2x2_nhwc_bwd, then tpk_bn_backward_nhwc). */
+TP_API int tpk_bn_backward_fused_nhwc(const float* g, const int32_t* idx, const float* x, const float* w,
+                                      const float* b, const float* mean, const float* invstd, float* dx, float* dw,
+                                      float* db, float* dx_sum, int64_t N, int64_t H, int64_t W, int64_t C,
+                                      int relu);
 TP_API int tpk_channel_sum_nhwc(const float* x, int64_t P, int64_t C, float* out);
 TP_API int tpk_maxpool2x2_nhwc_fwd(const float* x, float* y, int32_t* idx, int64_t N, int64_t H, int64_t W,
                                    int64_t C);

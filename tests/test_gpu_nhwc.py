@@ -90,6 +90,94 @@ def test_maxpool_nhwc_matches_nchw(cuda_rt, n, c, hw):
     free(rt, px, pxn, pgy, pgyn, y0, y1, i0, i1, gx0, gx1)
 
 
+def ints(rt, p, shape):
+    out = np.zeros(int(np.prod(shape)), np.int32)
+    assert rt.lib.tp_memcpy_d2h(out.ctypes.data_as(vp), vp(p), out.nbytes) == 0
+    return out.reshape(shape)
+
+
+@pytest.mark.parametrize("relu", [1, 0])
+@pytest.mark.parametrize("n,c,h,w", [(4, 64, 32, 32), (3, 36, 6, 10), (2, 512, 4, 4), (5, 16, 14, 2)])
+def test_bn_pool_fused_matches_unfused(cuda_rt, n, c, h, w, relu):
+    """BN train + ReLU + 2x2 pool in one pass against tpk_bn_train_nhwc then
+    tpk_maxpool2x2_nhwc_fwd (bit-exact: values, indices, statistics, the
+    optional full-size output); the fused backward (pool gradient read in
+    place, ReLU mask from the BN input) against tpk_maxpool2x2_nhwc_bwd then
+    tpk_bn_backward_nhwc (masked by the stored activation)."""
+    rt, L = cuda_rt, cuda_rt.lib
+    rng = np.random.default_rng(n * c + h * w + relu)
+    x = (rng.standard_normal((n, h, w, c)) * 2 + 0.3).astype(np.float32)
+    x[0, 0, 0, :] = x[0, 0, 1, :]  # ties inside a window: the first maximum wins
+    gam = (1 + 0.1 * rng.standard_normal(c)).astype(np.float32)
+    bet = (0.2 * rng.standard_normal(c)).astype(np.float32)
+    oh, ow = h // 2, w // 2
+    gp = rng.standard_normal((n, oh, ow, c)).astype(np.float32)
+    P, Q = n * h * w, n * oh * ow
+    px, pg, pb, pgp = dev(rt, x), dev(rt, gam), dev(rt, bet), dev(rt, gp)
+    out = {}
+    for mode in ("unfused", "fused"):
+        rm, rv = dev(rt, np.full(c, 0.1)), dev(rt, np.full(c, 0.9))
+        a, y, idx, mean, inv = empty(rt, P * c), empty(rt, Q * c), empty(rt, Q * c), empty(rt, c), empty(rt, c)
+        dx, dg, db, dxs, da = empty(rt, P * c), empty(rt, c), empty(rt, c), empty(rt, c), empty(rt, P * c)
+        if mode == "unfused":
+            assert L.tpk_bn_train_nhwc(vp(px), vp(pg), vp(pb), vp(rm), vp(rv), vp(a), vp(mean), vp(inv), P, c,
+                                       1e-5, 0.1, relu) == 0
+            assert L.tpk_maxpool2x2_nhwc_fwd(vp(a), vp(y), vp(idx), n, h, w, c) == 0
+            assert L.tpk_maxpool2x2_nhwc_bwd(vp(pgp), vp(idx), vp(da), n, h, w, c) == 0
+            assert L.tpk_bn_backward_nhwc(vp(da), vp(px), vp(a) if relu else None, vp(pg), vp(mean), vp(inv),
+                                          vp(dx), vp(dg), vp(db), vp(dxs), P, c) == 0
+        else:
+            assert L.tpk_bn_train_pool_nhwc(vp(px), vp(pg), vp(pb), vp(rm), vp(rv), vp(y), vp(idx), vp(a),
+                                            vp(mean), vp(inv), n, h, w, c, 1e-5, 0.1, relu) == 0
+            assert L.tpk_bn_backward_fused_nhwc(vp(pgp), vp(idx), vp(px), vp(pg), vp(pb), vp(mean), vp(inv),
+                                                vp(dx), vp(dg), vp(db), vp(dxs), n, h, w, c, relu) == 0
+        out[mode] = {"a": read(rt, a, (P * c,)), "y": read(rt, y, (Q * c,)), "idx": ints(rt, idx, (Q * c,)),
+                     "mean": read(rt, mean, (c,)), "inv": read(rt, inv, (c,)), "rm": read(rt, rm, (c,)),
+                     "rv": read(rt, rv, (c,)), "dx": read(rt, dx, (P * c,)), "dg": read(rt, dg, (c,)),
+                     "db": read(rt, db, (c,)), "dxs": read(rt, dxs, (c,))}
+        free(rt, rm, rv, a, y, idx, mean, inv, dx, dg, db, dxs, da)
+    free(rt, px, pg, pb, pgp)
+    u, f = out["unfused"], out["fused"]
+    for k in ("a", "y", "idx", "mean", "inv", "rm", "rv"):
+        assert np.array_equal(u[k], f[k]), k
+    # the backward sums run over windows instead of pixel rows: same terms, another order
+    for k in ("dx", "dg", "db"):
+        close(f[k], u[k], 1e-5)
+    close(f["dxs"], u["dxs"], 1e-4)
+
+
+@pytest.mark.parametrize("n,c,hw", [(4, 64, 16), (2, 512, 2)])
+def test_bn_backward_relu_from_input(cuda_rt, n, c, hw):
+    """tpk_bn_backward_fused_nhwc without a pool: the ReLU mask recomputed from
+    the BN input equals the one read from the stored activation, so every
+    output is bit-identical to tpk_bn_backward_nhwc's."""
+    rt, L = cuda_rt, cuda_rt.lib
+    rng = np.random.default_rng(c + hw)
+    x = (rng.standard_normal((n, hw, hw, c)) + 0.2).astype(np.float32)
+    dy = rng.standard_normal((n, hw, hw, c)).astype(np.float32)
+    gam = (1 + 0.1 * rng.standard_normal(c)).astype(np.float32)
+    bet = (0.3 * rng.standard_normal(c)).astype(np.float32)
+    P = n * hw * hw
+    px, pdy, pg, pb = dev(rt, x), dev(rt, dy), dev(rt, gam), dev(rt, bet)
+    rm, rv, a, mean, inv = empty(rt, c), empty(rt, c), empty(rt, P * c), empty(rt, c), empty(rt, c)
+    assert L.tpk_bn_train_nhwc(vp(px), vp(pg), vp(pb), vp(rm), vp(rv), vp(a), vp(mean), vp(inv), P, c, 1e-5, 0.1,
+                               1) == 0
+    res = []
+    for fused in (False, True):
+        dx, dg, db, dxs = empty(rt, P * c), empty(rt, c), empty(rt, c), empty(rt, c)
+        if fused:
+            assert L.tpk_bn_backward_fused_nhwc(vp(pdy), None, vp(px), vp(pg), vp(pb), vp(mean), vp(inv), vp(dx),
+                                                vp(dg), vp(db), vp(dxs), n, hw, hw, c, 1) == 0
+        else:
+            assert L.tpk_bn_backward_nhwc(vp(pdy), vp(px), vp(a), vp(pg), vp(mean), vp(inv), vp(dx), vp(dg),
+                                          vp(db), vp(dxs), P, c) == 0
+        res.append([read(rt, p, (k,)) for p, k in ((dx, P * c), (dg, c), (db, c), (dxs, c))])
+        free(rt, dx, dg, db, dxs)
+    free(rt, px, pdy, pg, pb, rm, rv, a, mean, inv)
+    for u, f in zip(*res):
+        assert np.array_equal(u, f)
+
+
 def test_nchw_to_nhwc_padded(cuda_rt):
     rt, L = cuda_rt, cuda_rt.lib
     x = np.random.default_rng(0).standard_normal((5, 3, 7, 9)).astype(np.float32)

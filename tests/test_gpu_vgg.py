@@ -45,7 +45,7 @@ def test_vgg_step_matches_oracle_composition(cuda_rt, oracle_rt, batch, layout):
     forward; backward against the oracle backward driven by the device's
     forward state; then the SGD update (bit-exact given the gradients)."""
     from tpcuda.vgg import VGG11BN
-    m = VGG11BN(cuda_rt, batch, seed=3, layout=layout)
+    m = VGG11BN(cuda_rt, batch, seed=3, layout=layout, keep_acts=True)
     rng = np.random.default_rng(7)
     x = rng.standard_normal((batch, 3, 32, 32)).astype(np.float32)
     y = rng.integers(0, 10, batch).astype(np.float32)
@@ -121,3 +121,29 @@ def test_vgg_loss_decreases(cuda_rt):
         losses.append(m.read_loss())
     assert losses[-1] < losses[0] * 0.7, losses
     m.close()
+
+
+def test_vgg_fused_pool_step_matches_kept_activations(cuda_rt):
+    """The channels-last step that writes only pooled activations (BN, ReLU and
+    pool in one pass; the pool backward read in place) gives bit-identical
+    losses and parameters to the same step that also stores every full-size
+    BN+ReLU activation (the state the oracle comparison reads)."""
+    from tpcuda.vgg import VGG11BN
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((8, 3, 32, 32)).astype(np.float32)
+    y = rng.integers(0, 10, 8).astype(np.float32)
+    res = []
+    for keep in (False, True):
+        m = VGG11BN(cuda_rt, 8, seed=5, layout="nhwc", keep_acts=keep)
+        assert all(bool(b["a"]) == (keep or not b["pool"]) for b in m.blocks)
+        m._h2d(m.x, x)
+        m._h2d(m.y, y)
+        losses = []
+        for _ in range(2):
+            m.step_eager()
+            losses.append(m.read_loss())
+        res.append((losses, {n: m.param_array(n) for n, _, _ in m.param_specs}))
+        m.close()
+    assert res[0][0] == res[1][0]
+    for n in res[0][1]:
+        assert np.array_equal(res[0][1][n], res[1][1][n]), n

@@ -22,6 +22,8 @@ namespace tp {
 static int g_gemm_path = 0;
 int gemm_path() { return g_gemm_path; }
 
+// Each translation unit that holds tensor-core kernels has its own copy of
+// tc::g_status (this one and tp_conv_nhwc.cu); the status is the first nonzero.
 int tc_status(bool reset) {
   int v = 0;
   TP_CUDA(cudaMemcpyFromSymbol(&v, tc::g_status, sizeof(int)));
@@ -29,7 +31,8 @@ int tc_status(bool reset) {
     int z = 0;
     TP_CUDA(cudaMemcpyToSymbol(tc::g_status, &z, sizeof(int)));
   }
-  return v;
+  const int w = tc_status_nhwc(reset);
+  return v ? v : w;
 }
 
 // ---- per-channel sum of an NCHW tensor (conv_backward.wgsl:103-119) ---------------

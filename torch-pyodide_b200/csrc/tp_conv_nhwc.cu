@@ -401,6 +401,16 @@ bool conv_wgrad_via_nhwc(const ConvShape& s, const float* dy, const float* x, fl
   return true;
 }
 
+int tc_status_nhwc(bool reset) {
+  int v = 0;
+  TP_CUDA(cudaMemcpyFromSymbol(&v, tc::g_status, sizeof(int)));
+  if (reset && v) {
+    int z = 0;
+    TP_CUDA(cudaMemcpyToSymbol(tc::g_status, &z, sizeof(int)));
+  }
+  return v;
+}
+
 }  // namespace tp
 
 using namespace tp;

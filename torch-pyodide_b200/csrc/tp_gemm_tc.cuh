@@ -406,6 +406,7 @@ __global__ void k_splitk_reduce_b(const float* __restrict__ ws, int splits, int6
 
 // Host side: read (and optionally clear) the device status word.
 int tc_status(bool reset);
+int tc_status_nhwc(bool reset);  // the channels-last conv module's status word
 
 // Split-K factor shared by the tensor-core launchers: minimise the k-blocks
 // one SM runs (waves x k-blocks per split) plus the split-K partial traffic

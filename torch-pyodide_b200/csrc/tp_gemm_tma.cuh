@@ -100,16 +100,26 @@ __device__ __forceinline__ uint64_t mn_desc(uint32_t saddr) {
 
 // ---- operand sources: issue the boxes of one ROWS x 32 tile --------------------------------------
 
+// Every source hands the producer lane a cursor: begin() places it at the
+// tile's first k-block (the only place that divides), issue() copies the
+// k-block it points at, next() moves it on by 32 k with additions only.
+
 // K-major rows of a row-major [batch][rows][K] tensor; map dims (K, rows, batch), box (32, ROWS, 1).
 // bmul = 0 when every batch shares the matrix.
 struct SrcK {
   static constexpr bool kMN = false;
   int bmul;
+  struct Cur {
+    int k, r, z;
+  };
   template <int ROWS>
-  __device__ __forceinline__ void issue(const CUtensorMap* map, uint32_t dst, uint64_t* bar, int b, int64_t r0,
-                                        int64_t k0) const {
-    load3(dst, map, (int)k0, (int)r0, b * bmul, bar);
+  __device__ __forceinline__ Cur begin(int b, int64_t r0, int64_t k0) const {
+    return {(int)k0, (int)r0, b * bmul};
   }
+  __device__ __forceinline__ void issue(const CUtensorMap* map, uint32_t dst, uint64_t* bar, const Cur& c) const {
+    load3(dst, map, c.k, c.r, c.z, bar);
+  }
+  __device__ __forceinline__ void next(Cur& c) const { c.k += 32; }
 };
 
 // MN-major: a row-major [batch][K][rows] tensor (rows contiguous).  Map dims
@@ -119,11 +129,17 @@ struct SrcK {
 struct SrcMN {
   static constexpr bool kMN = true;
   int bmul;
+  struct Cur {
+    int k, rg, z;
+  };
   template <int ROWS>
-  __device__ __forceinline__ void issue(const CUtensorMap* map, uint32_t dst, uint64_t* bar, int b, int64_t r0,
-                                        int64_t k0) const {
-    load4(dst, map, 0, (int)k0, (int)(r0 >> 5), b * bmul, bar);
+  __device__ __forceinline__ Cur begin(int b, int64_t r0, int64_t k0) const {
+    return {(int)k0, (int)(r0 >> 5), b * bmul};
   }
+  __device__ __forceinline__ void issue(const CUtensorMap* map, uint32_t dst, uint64_t* bar, const Cur& c) const {
+    load4(dst, map, 0, c.k, c.rg, c.z, bar);
+  }
+  __device__ __forceinline__ void next(Cur& c) const { c.k += 32; }
 };
 
 // Pixel tiles of an OH x OW output grid (N images): a tile is a TW x TH
@@ -172,14 +188,31 @@ struct SrcConvK {
   static constexpr bool kMN = false;
   PixTile pt;
   int cblocks, KW, PH, PW;
+  struct Cur {
+    int c0, kh, kw, n0, oh0, ow0;
+  };
   template <int ROWS>
-  __device__ __forceinline__ void issue(const CUtensorMap* map, uint32_t dst, uint64_t* bar, int, int64_t r0,
-                                        int64_t k0) const {
-    int n0, oh0, ow0;
-    pt.origin(r0 / ROWS, n0, oh0, ow0);
-    const int kb = (int)(k0 >> 5), tap = kb / cblocks, c0 = (kb - tap * cblocks) * 32;
-    const int kh = tap / KW, kw = tap - kh * KW;
-    load4(dst, map, c0, ow0 + kw - PW, oh0 + kh - PH, n0, bar);
+  __device__ __forceinline__ Cur begin(int, int64_t r0, int64_t k0) const {
+    Cur c;
+    pt.origin(r0 / ROWS, c.n0, c.oh0, c.ow0);
+    const int kb = (int)(k0 >> 5), tap = kb / cblocks;
+    c.c0 = (kb - tap * cblocks) * 32;
+    c.kh = tap / KW;
+    c.kw = tap - c.kh * KW;
+    return c;
+  }
+  __device__ __forceinline__ void issue(const CUtensorMap* map, uint32_t dst, uint64_t* bar, const Cur& c) const {
+    load4(dst, map, c.c0, c.ow0 + c.kw - PW, c.oh0 + c.kh - PH, c.n0, bar);
+  }
+  __device__ __forceinline__ void next(Cur& c) const {
+    c.c0 += 32;
+    if (c.c0 == cblocks * 32) {
+      c.c0 = 0;
+      if (++c.kw == KW) {
+        c.kw = 0;
+        ++c.kh;
+      }
+    }
   }
 };
 
@@ -195,17 +228,35 @@ struct SrcPixMN {
   static constexpr bool kMN = true;
   PixTile pt;
   int KW, PH, PW, shift;
+  // k-block = one 32-pixel tile (n0, tile row th, tile column tw)
+  struct Cur {
+    int n0, th, tw, dh, dw, cg;
+  };
   template <int ROWS>
-  __device__ __forceinline__ void issue(const CUtensorMap* map, uint32_t dst, uint64_t* bar, int b, int64_t r0,
-                                        int64_t k0) const {
-    int n0, oh0, ow0;
-    pt.origin(k0 >> 5, n0, oh0, ow0);
-    int dh = 0, dw = 0;
-    if (shift) {
-      dh = b / KW - PH;
-      dw = b - (b / KW) * KW - PW;
+  __device__ __forceinline__ Cur begin(int b, int64_t r0, int64_t k0) const {
+    Cur c;
+    int oh0, ow0;
+    pt.origin(k0 >> 5, c.n0, oh0, ow0);
+    c.th = pt.TN > 1 ? 0 : oh0 / pt.TH;
+    c.tw = pt.TN > 1 ? 0 : ow0 / pt.TW;
+    c.dh = shift ? b / KW - PH : 0;
+    c.dw = shift ? b - (b / KW) * KW - PW : 0;
+    c.cg = (int)(r0 >> 5);
+    return c;
+  }
+  __device__ __forceinline__ void issue(const CUtensorMap* map, uint32_t dst, uint64_t* bar, const Cur& c) const {
+    load5(dst, map, 0, c.tw * pt.TW + c.dw, c.th * pt.TH + c.dh, c.n0, c.cg, bar);
+  }
+  __device__ __forceinline__ void next(Cur& c) const {
+    if (pt.TN > 1) {
+      c.n0 += pt.TN;
+    } else if (++c.tw == pt.tiles_w) {
+      c.tw = 0;
+      if (++c.th == pt.tiles_h) {
+        c.th = 0;
+        ++c.n0;
+      }
     }
-    load5(dst, map, 0, ow0 + dw, oh0 + dh, n0, (int)(r0 >> 5), bar);
   }
 };
 
@@ -216,11 +267,23 @@ struct SrcPixMN {
 struct SrcFilterMN {
   static constexpr bool kMN = true;
   int cblocks, KHW;
+  struct Cur {
+    int tf, co0, cg;
+  };
   template <int ROWS>
-  __device__ __forceinline__ void issue(const CUtensorMap* map, uint32_t dst, uint64_t* bar, int, int64_t r0,
-                                        int64_t k0) const {
-    const int kb = (int)(k0 >> 5), tf = kb / cblocks, co0 = (kb - tf * cblocks) * 32;
-    load4(dst, map, 0, KHW - 1 - tf, co0, (int)(r0 >> 5), bar);
+  __device__ __forceinline__ Cur begin(int, int64_t r0, int64_t k0) const {
+    const int kb = (int)(k0 >> 5), tf = kb / cblocks;
+    return {tf, (kb - tf * cblocks) * 32, (int)(r0 >> 5)};
+  }
+  __device__ __forceinline__ void issue(const CUtensorMap* map, uint32_t dst, uint64_t* bar, const Cur& c) const {
+    load4(dst, map, 0, KHW - 1 - c.tf, c.co0, c.cg, bar);
+  }
+  __device__ __forceinline__ void next(Cur& c) const {
+    c.co0 += 32;
+    if (c.co0 == cblocks * 32) {
+      c.co0 = 0;
+      ++c.tf;
+    }
   }
 };
 
@@ -335,15 +398,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       int last[STAGES];
 #pragma unroll
       for (int s = 0; s < STAGES; ++s) last[s] = -1;
+      auto ca = sa.template begin<BM>(b, m0, kb0);
+      auto cb = sb.template begin<BN>(b, n0, kb0);
       for (int kb = 0; kb < nk && ok; ++kb) {
         const int s = kb % STAGES;
         ok = tc::mbar_wait(&empty[s], (uint32_t)((kb / STAGES) & 1) ^ 1u, 11);
         if (!ok) break;
         const uint32_t st = tc::smem_u32(smem + s * S::STAGE);
-        const int64_t k0 = kb0 + (int64_t)kb * BK;
         expect_tx(&full[s], S::A_BYTES + S::B_BYTES);
-        sa.template issue<BM>(&ma, st, &full[s], b, m0, k0);
-        sb.template issue<BN>(&mb, st + S::A_BYTES, &full[s], b, n0, k0);
+        sa.issue(&ma, st, &full[s], ca);
+        sb.issue(&mb, st + S::A_BYTES, &full[s], cb);
+        sa.next(ca);
+        sb.next(cb);
         last[s] = kb;
       }
       // no box may still be landing when the CTA exits

@@ -90,19 +90,28 @@ static unsigned finish_grid(int64_t C) { return (unsigned)((C + 7) / 8); }
 // f64 sums are combined over row lanes in shared memory in lane order, giving
 // part[(c*splits + split)*2 + {0,1}].
 
-// Functors: ctx(c0) loads what the thread's 4 channels need once; load(i4)
-// fetches the float4 operands at index i4 and use() consumes them, so the
-// row loop can have several rows' loads in flight.
+// The BatchNorm output value of the forward pass, also used to recompute the
+// ReLU mask in the backward: fma(x - mean, invstd*gamma, beta), so both see the
+// same float.
+__device__ __forceinline__ float bn_val(float x, float mu, float sc, float bs) { return __fmaf_rn(x - mu, sc, bs); }
+
+// Functors: ctx(c0) loads what the thread's 4 channels need once; load(p, cg)
+// fetches the operands of pixel row p, channel group cg (4 channels; GT groups
+// per row) and use() consumes them, so the row loop can have several rows'
+// loads in flight.
 struct NoCtx {};
 
 struct ColStatsF {  // a += x, b += x*x
   const float* x;
-  static constexpr int kUnroll = 8;
+  int GT;
+  static constexpr int kUnroll = 8, kMinBlocks = 4, kMinRows = 16;
   using Ctx = NoCtx;
   using V = float4;
   __device__ __forceinline__ Ctx ctx(int) const { return {}; }
-  __device__ __forceinline__ V load(int64_t i4) const { return reinterpret_cast<const float4*>(x)[i4]; }
-  __device__ __forceinline__ void use(int64_t, const V& v, const Ctx&, double (&a)[4], double (&b)[4]) const {
+  __device__ __forceinline__ V load(int64_t p, int cg) const {
+    return reinterpret_cast<const float4*>(x)[p * GT + cg];
+  }
+  __device__ __forceinline__ void use(int64_t, int, const V& v, const Ctx&, double (&a)[4], double (&b)[4]) const {
     a[0] += v.x, a[1] += v.y, a[2] += v.z, a[3] += v.w;
     b[0] += (double)v.x * v.x, b[1] += (double)v.y * v.y, b[2] += (double)v.z * v.z, b[3] += (double)v.w * v.w;
   }
@@ -110,112 +119,210 @@ struct ColStatsF {  // a += x, b += x*x
 
 struct ColSumF {  // a += x
   const float* x;
-  static constexpr int kUnroll = 8;
+  int GT;
+  static constexpr int kUnroll = 8, kMinBlocks = 4, kMinRows = 16;
   using Ctx = NoCtx;
   using V = float4;
   __device__ __forceinline__ Ctx ctx(int) const { return {}; }
-  __device__ __forceinline__ V load(int64_t i4) const { return reinterpret_cast<const float4*>(x)[i4]; }
-  __device__ __forceinline__ void use(int64_t, const V& v, const Ctx&, double (&a)[4], double (&)[4]) const {
+  __device__ __forceinline__ V load(int64_t p, int cg) const {
+    return reinterpret_cast<const float4*>(x)[p * GT + cg];
+  }
+  __device__ __forceinline__ void use(int64_t, int, const V& v, const Ctx&, double (&a)[4], double (&)[4]) const {
     a[0] += v.x, a[1] += v.y, a[2] += v.z, a[3] += v.w;
   }
 };
 
-struct BwdV {
-  float4 g, x;
+// Per-channel values a BatchNorm backward thread keeps for its 4 channels.
+struct BwdCtx {
+  float mu[4], is[4], sc[4], bs[4], k0[4], k1[4], k2[4];
 };
 
-__device__ __forceinline__ BwdV load_bwd(const float* dy, const float* x, const float* relu_src, int64_t i4) {
-  BwdV v;
-  v.g = reinterpret_cast<const float4*>(dy)[i4];
-  v.x = reinterpret_cast<const float4*>(x)[i4];
-  if (relu_src) {
-    float4 r = reinterpret_cast<const float4*>(relu_src)[i4];
-    if (!(r.x > 0.0f)) v.g.x = 0.0f;
-    if (!(r.y > 0.0f)) v.g.y = 0.0f;
-    if (!(r.z > 0.0f)) v.g.z = 0.0f;
-    if (!(r.w > 0.0f)) v.g.w = 0.0f;
+__device__ __forceinline__ BwdCtx bwd_ctx(int c0, const float* mean, const float* invstd, const float* gamma,
+                                          const float* beta, const float* coef) {
+  BwdCtx c;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    c.mu[j] = mean[c0 + j];
+    c.is[j] = invstd[c0 + j];
+    c.sc[j] = invstd[c0 + j] * (gamma ? gamma[c0 + j] : 1.0f);
+    c.bs[j] = beta ? beta[c0 + j] : 0.0f;
+    c.k0[j] = coef ? coef[(c0 + j) * 3] : 0.0f;
+    c.k1[j] = coef ? coef[(c0 + j) * 3 + 1] : 0.0f;
+    c.k2[j] = coef ? coef[(c0 + j) * 3 + 2] : 0.0f;
   }
-  return v;
+  return c;
 }
 
-struct ColBnBwdF {  // g = dy masked by relu_src > 0; a += g, b += g * x_hat
+// ReLU mask recomputed from the BatchNorm input: the forward's output
+// bn_val(x) was > 0 exactly where the stored activation is.
+__device__ __forceinline__ void relu_mask_from_x(float4& g, const float4& x, const BwdCtx& c) {
+  if (!(bn_val(x.x, c.mu[0], c.sc[0], c.bs[0]) > 0.0f)) g.x = 0.0f;
+  if (!(bn_val(x.y, c.mu[1], c.sc[1], c.bs[1]) > 0.0f)) g.y = 0.0f;
+  if (!(bn_val(x.z, c.mu[2], c.sc[2], c.bs[2]) > 0.0f)) g.z = 0.0f;
+  if (!(bn_val(x.w, c.mu[3], c.sc[3], c.bs[3]) > 0.0f)) g.w = 0.0f;
+}
+
+// Unsigned division by a runtime constant d for n < 2^31: with l = ceil(log2 d)
+// and m = floor(2^32 (2^l - d) / d) + 1, n / d = (umulhi(n, m) + n) >> l
+// (Granlund & Montgomery, "Division by invariant integers using
+// multiplication", 1994; the sum stays below 2^32 because n < 2^31).
+struct FastDiv {
+  uint32_t d, m, l;
+  __device__ __forceinline__ uint32_t div(uint32_t n) const { return (__umulhi(n, m) + n) >> l; }
+};
+
+static FastDiv fast_div(uint32_t d) {
+  uint32_t l = 0;
+  while (((uint64_t)1 << l) < d) ++l;
+  const uint64_t m = ((uint64_t)1 << 32) * (((uint64_t)1 << l) - d) / d + 1;
+  return {d, (uint32_t)m, l};
+}
+
+// Where the BatchNorm backward takes the gradient g at its output and its
+// input x.  A source's row p covers NPIX pixels; V holds their g and x and the
+// first pixel's index, and off(v, k, cg) is the float4 index of pixel k.
+//
+// PixSrc: one pixel per row, g read from dy [P][C]; the ReLU mask from the
+// stored activation (relu_src > 0) or recomputed from x (relu_from_x).
+struct PixSrc {
+  static constexpr int NPIX = 1, kUnroll = 4, kMinBlocks = 2, kMinRows = 16;
+  struct V {
+    float4 g[1], x[1];
+    int64_t base;
+  };
   const float* dy;
   const float* x;
   const float* relu_src;
-  const float* mean;
-  const float* invstd;
-  static constexpr int kUnroll = 4;
-  struct Ctx {
-    float mu[4], is[4];
-  };
-  using V = BwdV;
-  __device__ __forceinline__ Ctx ctx(int c0) const {
-    Ctx c;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      c.mu[j] = mean[c0 + j];
-      c.is[j] = invstd[c0 + j];
+  int GT, relu_from_x;
+  __device__ __forceinline__ int64_t off(const V& v, int, int cg) const { return v.base * GT + cg; }
+  __device__ __forceinline__ V load(int64_t p, int cg, const BwdCtx& c) const {
+    V v;
+    v.base = p;
+    const int64_t i4 = p * GT + cg;
+    v.x[0] = reinterpret_cast<const float4*>(x)[i4];
+    v.g[0] = reinterpret_cast<const float4*>(dy)[i4];
+    if (relu_src) {
+      const float4 r = reinterpret_cast<const float4*>(relu_src)[i4];
+      if (!(r.x > 0.0f)) v.g[0].x = 0.0f;
+      if (!(r.y > 0.0f)) v.g[0].y = 0.0f;
+      if (!(r.z > 0.0f)) v.g[0].z = 0.0f;
+      if (!(r.w > 0.0f)) v.g[0].w = 0.0f;
+    } else if (relu_from_x) {
+      relu_mask_from_x(v.g[0], v.x[0], c);
     }
-    return c;
+    return v;
   }
-  __device__ __forceinline__ V load(int64_t i4) const { return load_bwd(dy, x, relu_src, i4); }
-  __device__ __forceinline__ void use(int64_t, const V& v, const Ctx& c, double (&a)[4], double (&b)[4]) const {
-    a[0] += v.g.x, a[1] += v.g.y, a[2] += v.g.z, a[3] += v.g.w;
-    b[0] += (double)v.g.x * ((v.x.x - c.mu[0]) * c.is[0]);
-    b[1] += (double)v.g.y * ((v.x.y - c.mu[1]) * c.is[1]);
-    b[2] += (double)v.g.z * ((v.x.z - c.mu[2]) * c.is[2]);
-    b[3] += (double)v.g.w * ((v.x.w - c.mu[3]) * c.is[3]);
+};
+
+// PoolSrc: row q is a 2x2 window of a stride-2 max-pool that followed the
+// BatchNorm(+ReLU); the gradient of its 4 pixels is the pooled gradient gp
+// [N][H/2][W/2][C] where the window's argmax (idx, plane offset h*W + w) is
+// that pixel, else 0 -- the max-pool backward, read in place -- masked by the
+// ReLU recomputed from x (relu).
+struct PoolSrc {
+  // a row is 4 pixels (6 loads): fewer rows per lane, one row per step
+  static constexpr int NPIX = 4, kUnroll = 1, kMinBlocks = 2, kMinRows = 4;
+  struct V {
+    float4 g[4], x[4];
+    int64_t base;
+  };
+  const float* gp;
+  const int32_t* idx;
+  const float* x;
+  FastDiv ow_div, oh_div;  // pooled width, pooled height
+  int W, GT, relu;
+  __device__ __forceinline__ int64_t off(const V& v, int k, int cg) const {
+    return (v.base + (k >> 1) * (int64_t)W + (k & 1)) * GT + cg;
+  }
+  __device__ __forceinline__ V load(int64_t q, int cg, const BwdCtx& c) const {
+    V v;
+    const uint32_t t = ow_div.div((uint32_t)q);  // n * OH + oh
+    const uint32_t ow = (uint32_t)q - t * ow_div.d;
+    const uint32_t oh = t - oh_div.div(t) * oh_div.d;
+    v.base = (int64_t)t * 2 * W + 2 * ow;  // pixel (n, 2 oh, 2 ow)
+    const float4 g4 = reinterpret_cast<const float4*>(gp)[q * GT + cg];
+    const int4 ix = reinterpret_cast<const int4*>(idx)[q * GT + cg];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      v.x[k] = reinterpret_cast<const float4*>(x)[off(v, k, cg)];
+      const int me = (int)((2 * oh + (k >> 1)) * W + 2 * ow + (k & 1));
+      v.g[k] = make_float4(ix.x == me ? g4.x : 0.0f, ix.y == me ? g4.y : 0.0f, ix.z == me ? g4.z : 0.0f,
+                           ix.w == me ? g4.w : 0.0f);
+      if (relu) relu_mask_from_x(v.g[k], v.x[k], c);
+    }
+    return v;
+  }
+};
+
+template <class S>
+struct ColBnBwdF {  // a += g, b += g * x_hat
+  S src;
+  const float *mean, *invstd, *gamma, *beta;
+  static constexpr int kUnroll = S::kUnroll, kMinBlocks = S::kMinBlocks, kMinRows = S::kMinRows;
+  using Ctx = BwdCtx;
+  using V = typename S::V;
+  __device__ __forceinline__ Ctx ctx(int c0) const { return bwd_ctx(c0, mean, invstd, gamma, beta, nullptr); }
+  __device__ __forceinline__ V load(int64_t p, int cg, const Ctx& c) const { return src.load(p, cg, c); }
+  __device__ __forceinline__ void use(int64_t, int, const V& v, const Ctx& c, double (&a)[4], double (&b)[4]) const {
+#pragma unroll
+    for (int k = 0; k < S::NPIX; ++k) {
+      const float4 g = v.g[k], x = v.x[k];
+      a[0] += g.x, a[1] += g.y, a[2] += g.z, a[3] += g.w;
+      b[0] += (double)g.x * ((x.x - c.mu[0]) * c.is[0]);
+      b[1] += (double)g.y * ((x.y - c.mu[1]) * c.is[1]);
+      b[2] += (double)g.z * ((x.z - c.mu[2]) * c.is[2]);
+      b[3] += (double)g.w * ((x.w - c.mu[3]) * c.is[3]);
+    }
   }
 };
 
 // dx = coef0 * (g - coef1 - x_hat * coef2) (the NCHW backward's formula),
 // stored; a += dx (the gradient of a bias added before the BatchNorm)
+template <class S>
 struct ColBnBwdApplyF {
-  const float* dy;
-  const float* x;
-  const float* relu_src;
-  const float* mean;
-  const float* invstd;
-  const float* coef;
+  S src;
+  const float *mean, *invstd, *gamma, *beta, *coef;
   float* dx;
-  static constexpr int kUnroll = 4;
-  struct Ctx {
-    float mu[4], is[4], k0[4], k1[4], k2[4];
-  };
-  using V = BwdV;
-  __device__ __forceinline__ Ctx ctx(int c0) const {
-    Ctx c;
+  static constexpr int kUnroll = S::kUnroll, kMinBlocks = S::kMinBlocks, kMinRows = S::kMinRows;
+  using Ctx = BwdCtx;
+  using V = typename S::V;
+  __device__ __forceinline__ Ctx ctx(int c0) const { return bwd_ctx(c0, mean, invstd, gamma, beta, coef); }
+  __device__ __forceinline__ V load(int64_t p, int cg, const Ctx& c) const { return src.load(p, cg, c); }
+  __device__ __forceinline__ void use(int64_t, int cg, const V& v, const Ctx& c, double (&a)[4],
+                                      double (&)[4]) const {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      c.mu[j] = mean[c0 + j];
-      c.is[j] = invstd[c0 + j];
-      c.k0[j] = coef[(c0 + j) * 3];
-      c.k1[j] = coef[(c0 + j) * 3 + 1];
-      c.k2[j] = coef[(c0 + j) * 3 + 2];
-    }
-    return c;
-  }
-  __device__ __forceinline__ V load(int64_t i4) const { return load_bwd(dy, x, relu_src, i4); }
-  __device__ __forceinline__ void use(int64_t i4, const V& v, const Ctx& c, double (&a)[4], double (&)[4]) const {
-    const float g[4] = {v.g.x, v.g.y, v.g.z, v.g.w}, xs[4] = {v.x.x, v.x.y, v.x.z, v.x.w};
-    float o[4];
+    for (int k = 0; k < S::NPIX; ++k) {
+      const float g[4] = {v.g[k].x, v.g[k].y, v.g[k].z, v.g[k].w};
+      const float xs[4] = {v.x[k].x, v.x[k].y, v.x[k].z, v.x[k].w};
+      float o[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float xh = (xs[j] - c.mu[j]) * c.is[j];
-      o[j] = c.k0[j] * (g[j] - c.k1[j] - xh * c.k2[j]);
-      a[j] += o[j];
+      for (int j = 0; j < 4; ++j) {
+        float xh = (xs[j] - c.mu[j]) * c.is[j];
+        o[j] = c.k0[j] * (g[j] - c.k1[j] - xh * c.k2[j]);
+        a[j] += o[j];
+      }
+      reinterpret_cast<float4*>(dx)[src.off(v, k, cg)] = make_float4(o[0], o[1], o[2], o[3]);
     }
-    reinterpret_cast<float4*>(dx)[i4] = make_float4(o[0], o[1], o[2], o[3]);
   }
 };
+
+// load(p, cg) for functors without a context, load(p, cg, ctx) for the others
+template <class F>
+__device__ __forceinline__ auto load_of(const F& f, int64_t p, int cg, const NoCtx&) -> decltype(f.load(p, cg)) {
+  return f.load(p, cg);
+}
+template <class F>
+__device__ __forceinline__ typename F::V load_of(const F& f, int64_t p, int cg, const BwdCtx& c) {
+  return f.load(p, cg, c);
+}
 
 constexpr int COL_THREADS = 256;
 
 template <class F>
-__global__ void __launch_bounds__(COL_THREADS) k_col_reduce(F f, int64_t P, int C, int CB, int64_t rows_per_split,
+__global__ void __launch_bounds__(COL_THREADS, F::kMinBlocks) k_col_reduce(F f, int64_t P, int C, int CB, int64_t rows_per_split,
                                                             int splits, double* __restrict__ part) {
   extern __shared__ double sh[];  // [R][CB][2]
-  const int GT = C >> 2, GB = CB >> 2, R = COL_THREADS / GB;
+  const int GB = CB >> 2, R = COL_THREADS / GB;
   const int t = threadIdx.x, g = t % GB, r = t / GB;
   const int cg = blockIdx.y * GB + g;  // this thread's channel group
   const int split = blockIdx.x;
@@ -230,11 +337,11 @@ __global__ void __launch_bounds__(COL_THREADS) k_col_reduce(F f, int64_t P, int 
     for (; p + (U - 1) * R < p1; p += U * R) {
       typename F::V v[U];
 #pragma unroll
-      for (int u = 0; u < U; ++u) v[u] = f.load((p + u * R) * GT + cg);
+      for (int u = 0; u < U; ++u) v[u] = load_of(f, p + u * R, cg, cx);
 #pragma unroll
-      for (int u = 0; u < U; ++u) f.use((p + u * R) * GT + cg, v[u], cx, a, b);
+      for (int u = 0; u < U; ++u) f.use(p + u * R, cg, v[u], cx, a, b);
     }
-    for (; p < p1; p += R) f.use(p * GT + cg, f.load(p * GT + cg), cx, a, b);
+    for (; p < p1; p += R) f.use(p, cg, load_of(f, p, cg, cx), cx, a, b);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       sh[((int64_t)r * CB + 4 * g + j) * 2] = a[j];
@@ -255,7 +362,7 @@ __global__ void __launch_bounds__(COL_THREADS) k_col_reduce(F f, int64_t P, int 
 }
 
 // CTAs of 64 channels (all C when C <= 64 or C is not a multiple of 64) by
-// row splits: ~8 CTAs per SM, each with >= 16 rows per row lane, so enough
+// row splits: ~8 CTAs per SM, each with >= kMinRows rows per row lane, so enough
 // loads are in flight to cover HBM latency.
 struct ColPlan {
   int splits, cb;
@@ -263,7 +370,7 @@ struct ColPlan {
   size_t part_bytes;  // C * splits * 2 doubles, rounded up to 256 bytes
 };
 
-static ColPlan col_plan(int64_t P, int C) {
+static ColPlan col_plan(int64_t P, int C, int min_rows = 16) {
   TP_REQUIRE(C % 4 == 0 && C >= 4 && C <= 4 * COL_THREADS, "channels-last reduction needs C %% 4 == 0, C <= %d",
              4 * COL_THREADS);
   ColPlan pl;
@@ -271,7 +378,7 @@ static ColPlan col_plan(int64_t P, int C) {
   const int R = COL_THREADS / (pl.cb / 4);
   int64_t want = (int64_t)sm_count() * 8 / (C / pl.cb);
   if (want < 1) want = 1;
-  int64_t maxs = P / ((int64_t)R * 16);
+  int64_t maxs = P / ((int64_t)R * min_rows);
   if (maxs < 1) maxs = 1;
   int64_t s = want < maxs ? want : maxs;
   pl.rows = (P + s - 1) / s;
@@ -301,7 +408,7 @@ __device__ __forceinline__ float4 bn_apply4(float4 v, const float (&mu)[4], cons
   float r[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    r[j] = (r[j] - mu[j]) * sc[j] + bs[j];
+    r[j] = bn_val(r[j], mu[j], sc[j], bs[j]);
     if (relu) r[j] = fmaxf(r[j], 0.0f);
   }
   return make_float4(r[0], r[1], r[2], r[3]);
@@ -341,6 +448,76 @@ __global__ void k_bn_apply_nhwc(const float4* __restrict__ x, const float* __res
       bs[j] = b ? b[c + j] : 0.0f;
     }
     y[i] = bn_apply4(x[i], mu, sc, bs, relu);
+  }
+}
+
+// BatchNorm apply (+ReLU) fused with the 2x2 / stride-2 max-pool that follows
+// it: one thread per (pooled pixel, channel group) computes the 4 window
+// values with bn_apply4 and keeps their maximum and its plane offset h*W + w
+// (strict >, row-major window order: k_maxpool2x2_nhwc_fwd's rule), so the
+// full-size activation is written only when a is given.
+struct PoolFwd {
+  const float4* x;
+  float4* y;
+  int4* idx;
+  float4* a;
+  FastDiv ow_div, oh_div;
+  int W, G, relu;
+  __device__ __forceinline__ void run(uint32_t q, int g, const float (&mu)[4], const float (&sc)[4],
+                                      const float (&bs)[4]) const {
+    const uint32_t t = ow_div.div(q);  // n * OH + oh
+    const uint32_t ow = q - t * ow_div.d;
+    const uint32_t oh = t - oh_div.div(t) * oh_div.d;
+    const int64_t base = (int64_t)t * 2 * W + 2 * ow;
+    float4 v[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) v[k] = x[(base + (k >> 1) * (int64_t)W + (k & 1)) * G + g];
+    float m[4] = {-3.402823e+38f, -3.402823e+38f, -3.402823e+38f, -3.402823e+38f};
+    int mi[4] = {-1, -1, -1, -1};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float4 r = bn_apply4(v[k], mu, sc, bs, relu);
+      if (a) a[(base + (k >> 1) * (int64_t)W + (k & 1)) * G + g] = r;
+      const float rs[4] = {r.x, r.y, r.z, r.w};
+      const int me = (int)((2 * oh + (k >> 1)) * W + 2 * ow + (k & 1));
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (rs[j] > m[j]) {
+          m[j] = rs[j];
+          mi[j] = me;
+        }
+    }
+    y[(int64_t)q * G + g] = make_float4(m[0], m[1], m[2], m[3]);
+    idx[(int64_t)q * G + g] = make_int4(mi[0], mi[1], mi[2], mi[3]);
+  }
+};
+
+__device__ __forceinline__ void bn_params4(int c, const float* mean, const float* invstd, const float* w,
+                                           const float* b, float (&mu)[4], float (&sc)[4], float (&bs)[4]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    mu[j] = mean[c + j];
+    sc[j] = invstd[c + j] * (w ? w[c + j] : 1.0f);
+    bs[j] = b ? b[c + j] : 0.0f;
+  }
+}
+
+__global__ void __launch_bounds__(256) k_bn_pool_nhwc(PoolFwd f, const float* __restrict__ mean,
+                                                      const float* __restrict__ invstd, const float* __restrict__ w,
+                                                      const float* __restrict__ b, int64_t n4) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  float mu[4], sc[4], bs[4];
+  if (stride % f.G == 0) {  // one channel group per thread: parameters loaded once
+    const int g = (int)(i % f.G);
+    bn_params4(4 * g, mean, invstd, w, b, mu, sc, bs);
+    for (; i < n4; i += stride) f.run((uint32_t)(i / f.G), g, mu, sc, bs);
+    return;
+  }
+  for (; i < n4; i += stride) {
+    const int g = (int)(i % f.G);
+    bn_params4(4 * g, mean, invstd, w, b, mu, sc, bs);
+    f.run((uint32_t)(i / f.G), g, mu, sc, bs);
   }
 }
 
@@ -457,6 +634,24 @@ static void check_vec(const void* p, const char* what) {
   TP_REQUIRE(((uintptr_t)p & 15) == 0, "%s: channels-last buffers must be 16-byte aligned", what);
 }
 
+// The two passes of the BatchNorm backward over `rows` rows of source S
+// (M values per channel): sums of g and g*x_hat, the per-channel
+// coefficients (and dgamma, dbeta), then dx and its per-channel sum.
+template <class S>
+static void bn_backward_cols(const S& src, int64_t rows, int64_t M, int64_t C, const float* w, const float* b,
+                             const float* mean, const float* invstd, float* dx, float* dw, float* db,
+                             float* dx_sum) {
+  ColPlan pl = col_plan(rows, (int)C, S::kMinRows);
+  char* ws = (char*)scratch(2 * pl.part_bytes + (((size_t)C * 3 * sizeof(float) + 255) & ~(size_t)255));
+  double* part = (double*)ws;
+  double* part2 = (double*)(ws + pl.part_bytes);
+  float* coef = (float*)(ws + 2 * pl.part_bytes);
+  col_launch(ColBnBwdF<S>{src, mean, invstd, w, b}, rows, (int)C, pl, part);
+  TP_LAUNCH(k_col_bn_bwd_finish, finish_grid(C), 256, 0, part, C, pl.splits, (double)M, w, invstd, coef, dw, db);
+  col_launch(ColBnBwdApplyF<S>{src, mean, invstd, w, b, coef, dx}, rows, (int)C, pl, part2);
+  if (dx_sum) TP_LAUNCH(k_col_sum_finish, finish_grid(C), 256, 0, part2, C, pl.splits, dx_sum);
+}
+
 }  // namespace tp
 
 using namespace tp;
@@ -472,13 +667,41 @@ TP_API int tpk_bn_train_nhwc(const float* x, const float* w, const float* b, flo
     check_vec(y, "batch_norm");
     ColPlan pl = col_plan(P, (int)C);
     double* part = (double*)scratch(pl.part_bytes);
-    col_launch(ColStatsF{x}, P, (int)C, pl, part);
+    col_launch(ColStatsF{x, (int)(C / 4)}, P, (int)C, pl, part);
     TP_LAUNCH(k_col_bn_finish, finish_grid(C), 256, 0, part, C, pl.splits, (double)P, eps, momentum, save_mean,
               save_invstd, running_mean, running_var);
     int64_t n4 = P * C / 4;
     unsigned grid = (unsigned)((n4 + 255) / 256 < (int64_t)sm_count() * 8 ? (n4 + 255) / 256 : sm_count() * 8);
     TP_LAUNCH(k_bn_apply_nhwc, grid, 256, 0, reinterpret_cast<const float4*>(x), save_mean,
               save_invstd, w, b, reinterpret_cast<float4*>(y), n4, (int)(C / 4), relu ? 1 : 0);
+  });
+}
+
+TP_API int tpk_bn_train_pool_nhwc(const float* x, const float* w, const float* b, float* running_mean,
+                                  float* running_var, float* y, int32_t* idx, float* a, float* save_mean,
+                                  float* save_invstd, int64_t N, int64_t H, int64_t W, int64_t C, float eps,
+                                  float momentum, int relu) {
+  return guard([&] {
+    const int64_t P = N * H * W;
+    TP_REQUIRE(P > 1, "batch_norm training needs more than one value per channel");
+    TP_REQUIRE(H % 2 == 0 && W % 2 == 0 && C % 4 == 0 && P * C / 16 < ((int64_t)1 << 31),
+               "batch_norm + 2x2 max-pool (channels-last) needs even H, W, C %% 4 == 0 and fewer than 2^31 "
+               "pooled vectors");
+    check_vec(x, "batch_norm");
+    check_vec(y, "max_pool2d");
+    check_vec(idx, "max_pool2d");
+    if (a) check_vec(a, "batch_norm");
+    ColPlan pl = col_plan(P, (int)C);
+    double* part = (double*)scratch(pl.part_bytes);
+    col_launch(ColStatsF{x, (int)(C / 4)}, P, (int)C, pl, part);
+    TP_LAUNCH(k_col_bn_finish, finish_grid(C), 256, 0, part, C, pl.splits, (double)P, eps, momentum, save_mean,
+              save_invstd, running_mean, running_var);
+    const int64_t n4 = P * C / 16;
+    unsigned grid = (unsigned)((n4 + 255) / 256 < (int64_t)sm_count() * 8 ? (n4 + 255) / 256 : sm_count() * 8);
+    PoolFwd f{reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(y), reinterpret_cast<int4*>(idx),
+              reinterpret_cast<float4*>(a), fast_div((uint32_t)(W / 2)), fast_div((uint32_t)(H / 2)), (int)W,
+              (int)(C / 4), relu ? 1 : 0};
+    TP_LAUNCH(k_bn_pool_nhwc, grid, 256, 0, f, save_mean, save_invstd, w, b, n4);
   });
 }
 
@@ -490,15 +713,31 @@ TP_API int tpk_bn_backward_nhwc(const float* dy, const float* x, const float* re
     check_vec(x, "batch_norm backward");
     check_vec(dx, "batch_norm backward");
     if (relu_src) check_vec(relu_src, "batch_norm backward");
-    ColPlan pl = col_plan(P, (int)C);
-    char* ws = (char*)scratch(2 * pl.part_bytes + (((size_t)C * 3 * sizeof(float) + 255) & ~(size_t)255));
-    double* part = (double*)ws;
-    double* part2 = (double*)(ws + pl.part_bytes);
-    float* coef = (float*)(ws + 2 * pl.part_bytes);
-    col_launch(ColBnBwdF{dy, x, relu_src, mean, invstd}, P, (int)C, pl, part);
-    TP_LAUNCH(k_col_bn_bwd_finish, finish_grid(C), 256, 0, part, C, pl.splits, (double)P, w, invstd, coef, dw, db);
-    col_launch(ColBnBwdApplyF{dy, x, relu_src, mean, invstd, coef, dx}, P, (int)C, pl, part2);
-    if (dx_sum) TP_LAUNCH(k_col_sum_finish, finish_grid(C), 256, 0, part2, C, pl.splits, dx_sum);
+    bn_backward_cols(PixSrc{dy, x, relu_src, (int)(C / 4), 0}, P, P, C, w, nullptr, mean, invstd, dx, dw, db,
+                     dx_sum);
+  });
+}
+
+TP_API int tpk_bn_backward_fused_nhwc(const float* g, const int32_t* idx, const float* x, const float* w,
+                                      const float* b, const float* mean, const float* invstd, float* dx, float* dw,
+                                      float* db, float* dx_sum, int64_t N, int64_t H, int64_t W, int64_t C,
+                                      int relu) {
+  return guard([&] {
+    check_vec(g, "batch_norm backward");
+    check_vec(x, "batch_norm backward");
+    check_vec(dx, "batch_norm backward");
+    const int64_t P = N * H * W;
+    if (!idx) {
+      bn_backward_cols(PixSrc{g, x, nullptr, (int)(C / 4), relu ? 1 : 0}, P, P, C, w, b, mean, invstd, dx, dw, db,
+                       dx_sum);
+      return;
+    }
+    check_vec(idx, "batch_norm backward");
+    TP_REQUIRE(H % 2 == 0 && W % 2 == 0 && P < ((int64_t)1 << 31),
+               "batch_norm backward through a 2x2 max-pool needs even H, W and N*H*W < 2^31");
+    PoolSrc src{g, idx, x, fast_div((uint32_t)(W / 2)), fast_div((uint32_t)(H / 2)), (int)W, (int)(C / 4),
+                relu ? 1 : 0};
+    bn_backward_cols(src, P / 4, P, C, w, b, mean, invstd, dx, dw, db, dx_sum);
   });
 }
 
@@ -507,7 +746,7 @@ TP_API int tpk_channel_sum_nhwc(const float* x, int64_t P, int64_t C, float* out
     check_vec(x, "channel sum");
     ColPlan pl = col_plan(P, (int)C);
     double* part = (double*)scratch(pl.part_bytes);
-    col_launch(ColSumF{x}, P, (int)C, pl, part);
+    col_launch(ColSumF{x, (int)(C / 4)}, P, (int)C, pl, part);
     TP_LAUNCH(k_col_sum_finish, finish_grid(C), 256, 0, part, C, pl.splits, out);
   });
 }

@@ -142,6 +142,8 @@ SIGNATURES: dict[str, list] = {
     "tpk_conv2d_wgrad": [P, P, P, I64, I64, I64, I64, I64, INT, INT, INT, INT, INT, INT],
     "tpk_bn_train_nhwc": [P, P, P, P, P, P, P, P, I64, I64, F32, F32, INT],
     "tpk_bn_backward_nhwc": [P, P, P, P, P, P, P, P, P, P, I64, I64],
+    "tpk_bn_train_pool_nhwc": [P] * 10 + [I64, I64, I64, I64, F32, F32, INT],
+    "tpk_bn_backward_fused_nhwc": [P] * 11 + [I64, I64, I64, I64, INT],
     "tpk_channel_sum_nhwc": [P, I64, I64, P],
     "tpk_maxpool2x2_nhwc_fwd": [P, P, P, I64, I64, I64, I64],
     "tpk_maxpool2x2_nhwc_bwd": [P, P, P, I64, I64, I64, I64],

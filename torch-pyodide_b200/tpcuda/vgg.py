@@ -181,12 +181,16 @@ class VGG11BN:
 
     def __init__(self, rt, batch: int, seed: int = 0, lr: float = 0.05, momentum: float = 0.9,
                  weight_decay: float = 5e-4, world: int = 1, comm=None, bucket_bytes: int = 8 << 20,
-                 layout: str = "nhwc"):
+                 layout: str = "nhwc", keep_acts: bool = False):
         if layout not in ("nhwc", "nchw"):
             raise ValueError(f"layout must be 'nhwc' or 'nchw', got {layout!r}")
         self.layout = layout
         self.cin0 = CIN0_PAD if layout == "nhwc" else 3
         self.khwc = layout == "nhwc"  # conv filters (but the first) stored [Cout][3][3][Cin]
+        # channels-last blocks with a pool write only the pooled BN+ReLU values
+        # (BN, ReLU and pool in one pass); keep_acts also stores the full-size ones
+        self.fuse_pool = layout == "nhwc"
+        self.keep_acts = bool(keep_acts) or not self.fuse_pool
         self.rt, self.lib = rt, rt.lib
         self.B = int(batch)
         self.lr, self.momentum, self.wd = lr, momentum, weight_decay
@@ -235,7 +239,8 @@ class VGG11BN:
             n = Bn * b["cout"] * b["H"] * b["W"]
             max_act = max(max_act, n, Bn * b["cin"] * b["H"] * b["W"])
             b["z"] = self._alloc(n * 4)  # conv output (BN input)
-            b["a"] = self._alloc(n * 4)  # BN + ReLU output
+            # BN + ReLU output (not kept for fused pooled blocks)
+            b["a"] = self._alloc(n * 4) if (self.keep_acts or not b["pool"]) else 0
             if b["pool"]:
                 m = n // 4
                 b["p"] = self._alloc(m * 4)
@@ -299,9 +304,12 @@ class VGG11BN:
             if nhwc:
                 check(L.tpk_conv2d_fwd_nhwc(_vp(x), w, bias, _vp(b["z"]), Bn, cin, H, W, C, 3, 3, 1, 1,
                                             self.filter_layout(li)))
-                check(L.tpk_bn_train_nhwc(_vp(b["z"]), gam, bet, *stats, Bn * H * W, C, 1e-5, 0.1, 1))
                 if b["pool"]:
-                    check(L.tpk_maxpool2x2_nhwc_fwd(_vp(b["a"]), _vp(b["p"]), _vp(b["idx"]), Bn, H, W, C))
+                    check(L.tpk_bn_train_pool_nhwc(_vp(b["z"]), gam, bet, _vp(b["rm"]), _vp(b["rv"]), _vp(b["p"]),
+                                                   _vp(b["idx"]), _vp(b["a"]) if b["a"] else None, _vp(b["mean"]),
+                                                   _vp(b["invstd"]), Bn, H, W, C, 1e-5, 0.1, 1))
+                else:
+                    check(L.tpk_bn_train_nhwc(_vp(b["z"]), gam, bet, *stats, Bn * H * W, C, 1e-5, 0.1, 1))
             else:
                 check(L.tpk_conv2d_fwd(_vp(x), w, bias, _vp(b["z"]), Bn, cin, H, W, C, 3, 3, 1, 1, 1, 1))
                 check(L.tpk_bn_train(_vp(b["z"]), gam, bet, *stats, Bn, C, H * W, 1e-5, 0.1, 1))
@@ -339,27 +347,30 @@ class VGG11BN:
             C, H, W = b["cout"], b["H"], b["W"]
             P = Bn * H * W
             cin = self.cin0 if li == 0 else b["cin"]
-            if b["pool"]:
+            if b["pool"] and not nhwc:
                 da = self.gbuf[buf]
                 buf ^= 1
-                if nhwc:
-                    check(L.tpk_maxpool2x2_nhwc_bwd(_vp(gout), _vp(b["idx"]), _vp(da), Bn, H, W, C))
-                else:
-                    check(L.tpk_maxpool_bwd(_vp(gout), _vp(b["idx"]), _vp(da), Bn, C, H, W, 2, 2, 0))
+                check(L.tpk_maxpool_bwd(_vp(gout), _vp(b["idx"]), _vp(da), Bn, C, H, W, 2, 2, 0))
             else:
                 da = gout
             dz = self.gbuf[buf]
             buf ^= 1
-            bn_args = (_vp(da), _vp(b["z"]), _vp(b["a"]), _vp(self.p(f"bn{li}.g")), _vp(b["mean"]), _vp(b["invstd"]),
-                       _vp(dz), _vp(self.g(f"bn{li}.g")), _vp(self.g(f"bn{li}.b")))
             xin = self.x0 if li == 0 else self.blocks[li - 1]["out"]
             w, dw, db = _vp(self.p(f"conv{li}.w")), _vp(self.g(f"conv{li}.w")), _vp(self.g(f"conv{li}.b"))
             if nhwc:
-                # the conv bias gradient (the per-channel sum of dz) comes out of the BN backward pass
-                check(L.tpk_bn_backward_nhwc(*bn_args, db, P, C))
+                # the max-pool backward is read in place (da is the pooled gradient) and the
+                # ReLU mask is recomputed from z; the conv bias gradient (the per-channel sum
+                # of dz) comes out of the same pass
+                check(L.tpk_bn_backward_fused_nhwc(_vp(da), _vp(b["idx"]) if b["pool"] else None, _vp(b["z"]),
+                                                   _vp(self.p(f"bn{li}.g")), _vp(self.p(f"bn{li}.b")),
+                                                   _vp(b["mean"]), _vp(b["invstd"]), _vp(dz),
+                                                   _vp(self.g(f"bn{li}.g")), _vp(self.g(f"bn{li}.b")), db, Bn, H, W,
+                                                   C, 1))
                 check(L.tpk_conv2d_wgrad_nhwc(_vp(dz), _vp(xin), dw, Bn, cin, H, W, C, 3, 3, 1, 1,
                                               self.filter_layout(li)))
             else:
+                bn_args = (_vp(da), _vp(b["z"]), _vp(b["a"]), _vp(self.p(f"bn{li}.g")), _vp(b["mean"]),
+                           _vp(b["invstd"]), _vp(dz), _vp(self.g(f"bn{li}.g")), _vp(self.g(f"bn{li}.b")))
                 check(L.tpk_bn_backward(*bn_args, Bn, C, H * W))
                 check(L.tpk_channel_sum(_vp(dz), Bn, C, H * W, db))
                 check(L.tpk_conv2d_wgrad(_vp(dz), _vp(xin), dw, Bn, cin, H, W, C, 3, 3, 1, 1, 1, 1))
