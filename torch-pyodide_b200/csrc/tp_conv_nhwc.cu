@@ -264,12 +264,16 @@ static void conv_fwd_nhwc(const NhwcShape& s, const float* x, const float* w, co
   MatOp b{wp, false, K, 0, false};
   if (nhwc_tma_ok() && M >= 64 && s.Cin % 32 == 0 && pixel_tiling(s.N, s.OH, s.OW, tc::BM, tl) &&
       nhwc_map(nullptr, x, s.N, s.H, s.W, s.Cin, tl.pt, false) && mat_tma_ok(b, s.Cout)) {
-    CUtensorMap ma, mb;
+    CUtensorMap ma, mb, mbl;
     nhwc_map(&ma, x, s.N, s.H, s.W, s.Cin, tl.pt, true);
     mat_map(&mb, b, s.Cout, K, 1, tma_bn(s.Cout));
+    // every pixel tile reads all filters: split their tf32 low parts once
+    float* wlo = (float*)scratch3((size_t)s.Cout * K * sizeof(float));
+    tf32_lo_plane(wp, wlo, s.Cout * K);
+    mat_map(&mbl, MatOp{wlo, false, K, 0, false}, s.Cout, K, 1, tma_bn(s.Cout));
     tma::SrcConvK sa{tl.pt, (int)(s.Cin / 32), s.KW, s.PH, s.PW};
-    if (tl.linear) gemm_tma_bn(ma, mb, sa, tma::SrcK{0}, ep, M, s.Cout, K, 1);
-    else gemm_tma_bn(ma, mb, sa, tma::SrcK{0}, EpPixTile{y, s.Cout, s.N, bias, tl.pt}, tl.span, s.Cout, K, 1);
+    if (tl.linear) gemm_tma_bn(ma, mb, sa, tma::SrcK{0}, ep, M, s.Cout, K, 1, &mbl);
+    else gemm_tma_bn(ma, mb, sa, tma::SrcK{0}, EpPixTile{y, s.Cout, s.N, bias, tl.pt}, tl.span, s.Cout, K, 1, &mbl);
     return;
   }
   LdNhwcIm2col la{x, s.H, s.W, s.Cin, s.OH, s.OW, s.KW, s.PH, s.PW, M};
@@ -290,28 +294,35 @@ static void conv_dgrad_nhwc(const NhwcShape& s, const float* dy, const float* w,
                      nhwc_map(nullptr, dy, s.N, s.OH, s.OW, s.Cout, tl.pt, false);
   if (tma_a && s.khwc && s.Cin % 32 == 0 && ((uintptr_t)w & 15) == 0) {
     // filters stored [Cout][tap][Cin] are read in place as the MN-major B
-    CUtensorMap ma, mb;
+    CUtensorMap ma, mb, mbl;
     nhwc_map(&ma, dy, s.N, s.OH, s.OW, s.Cout, tl.pt, true);
     uint64_t dims[4] = {32, (uint64_t)khw, (uint64_t)s.Cout, (uint64_t)(s.Cin / 32)};
     uint64_t st[3] = {(uint64_t)s.Cin * 4, (uint64_t)(khw * s.Cin) * 4, 128};
     uint32_t box[4] = {32, 1, 32, tma_bn(s.Cin) / 32};
     make_map_f32(&mb, w, 4, dims, st, box, true);
+    float* wlo = (float*)scratch3((size_t)s.Cin * K * sizeof(float));
+    tf32_lo_plane(w, wlo, s.Cin * K);
+    make_map_f32(&mbl, wlo, 4, dims, st, box, true);
     tma::SrcConvK sa{tl.pt, (int)(s.Cout / 32), s.KW, qh, qw};
     tma::SrcFilterMN sb{(int)(s.Cout / 32), khw};
-    if (tl.linear) gemm_tma_bn(ma, mb, sa, sb, ep, M, s.Cin, K, 1);
-    else gemm_tma_bn(ma, mb, sa, sb, EpPixTile{dx, s.Cin, s.N, nullptr, tl.pt}, tl.span, s.Cin, K, 1);
+    if (tl.linear) gemm_tma_bn(ma, mb, sa, sb, ep, M, s.Cin, K, 1, &mbl);
+    else gemm_tma_bn(ma, mb, sa, sb, EpPixTile{dx, s.Cin, s.N, nullptr, tl.pt}, tl.span, s.Cin, K, 1, &mbl);
     return;
   }
   float* wp = (float*)scratch2((size_t)s.Cin * K * sizeof(float));
   TP_LAUNCH(k_pack_filters, grid_for(s.Cout * s.Cin * khw, 256), 256, 0, w, wp, s.Cout, s.Cin, khw, s.khwc ? 2 : 1);
   MatOp b{wp, false, K, 0, false};
   if (tma_a && mat_tma_ok(b, s.Cin)) {
-    CUtensorMap ma, mb;
+    CUtensorMap ma, mb, mbl;
     nhwc_map(&ma, dy, s.N, s.OH, s.OW, s.Cout, tl.pt, true);
     mat_map(&mb, b, s.Cin, K, 1, tma_bn(s.Cin));
+    float* wlo = (float*)scratch3((size_t)s.Cin * K * sizeof(float));
+    tf32_lo_plane(wp, wlo, s.Cin * K);
+    mat_map(&mbl, MatOp{wlo, false, K, 0, false}, s.Cin, K, 1, tma_bn(s.Cin));
     tma::SrcConvK sa{tl.pt, (int)(s.Cout / 32), s.KW, qh, qw};
-    if (tl.linear) gemm_tma_bn(ma, mb, sa, tma::SrcK{0}, ep, M, s.Cin, K, 1);
-    else gemm_tma_bn(ma, mb, sa, tma::SrcK{0}, EpPixTile{dx, s.Cin, s.N, nullptr, tl.pt}, tl.span, s.Cin, K, 1);
+    if (tl.linear) gemm_tma_bn(ma, mb, sa, tma::SrcK{0}, ep, M, s.Cin, K, 1, &mbl);
+    else gemm_tma_bn(ma, mb, sa, tma::SrcK{0}, EpPixTile{dx, s.Cin, s.N, nullptr, tl.pt}, tl.span, s.Cin, K, 1,
+                     &mbl);
     return;
   }
   LdNhwcIm2col la{dy, s.OH, s.OW, s.Cout, s.H, s.W, s.KW, qh, qw, M};

@@ -106,6 +106,19 @@ void* scratch2(size_t bytes) {
   return g_scratch2;
 }
 
+static void* g_scratch3 = nullptr;
+static size_t g_scratch3_bytes = 0;
+
+void* scratch3(size_t bytes) {
+  if (bytes > g_scratch3_bytes) {
+    if (g_scratch3) dfree(g_scratch3);
+    size_t nb = bytes < (1u << 20) ? (1u << 20) : bytes;
+    g_scratch3 = dalloc(nb);
+    g_scratch3_bytes = nb;
+  }
+  return g_scratch3;
+}
+
 int64_t prod(const int64_t* s, int n) {
   int64_t r = 1;
   for (int i = 0; i < n; ++i) r *= s[i];

@@ -113,6 +113,8 @@ inline unsigned grid_for(int64_t n, int threads, int per_thread = 1) {
 void* scratch(size_t bytes);
 // A second, independent scratch area (repacked filters), same rules.
 void* scratch2(size_t bytes);
+// A third one (the tf32 low parts of a GEMM operand), same rules.
+void* scratch3(size_t bytes);
 
 }  // namespace tp
 

@@ -37,10 +37,10 @@ void gemm_auto(const LA& la, const LB& lb, const EP& ep, int64_t M, int64_t N, i
 // TMA kernel with the N tile following N; the maps' B box must match.
 template <class SA, class SB, class EP>
 void gemm_tma_bn(const CUtensorMap& ma, const CUtensorMap& mb, const SA& sa, const SB& sb, const EP& ep, int64_t M,
-                 int64_t N, int64_t K, int batch) {
-  if (N <= 32) gemm_tma_launch<SA, SB, EP, 32, 4>(ma, mb, sa, sb, ep, M, N, K, batch);
-  else if (N <= 64) gemm_tma_launch<SA, SB, EP, 64, 4>(ma, mb, sa, sb, ep, M, N, K, batch);
-  else gemm_tma_launch<SA, SB, EP, 128, 4>(ma, mb, sa, sb, ep, M, N, K, batch);
+                 int64_t N, int64_t K, int batch, const CUtensorMap* mbl = nullptr) {
+  if (N <= 32) gemm_tma_launch<SA, SB, EP, 32, 4>(ma, mb, sa, sb, ep, M, N, K, batch, mbl);
+  else if (N <= 64) gemm_tma_launch<SA, SB, EP, 64, 4>(ma, mb, sa, sb, ep, M, N, K, batch, mbl);
+  else gemm_tma_launch<SA, SB, EP, 128, 4>(ma, mb, sa, sb, ep, M, N, K, batch, mbl);
 }
 
 inline uint32_t tma_bn(int64_t N) { return N <= 32 ? 32u : (N <= 64 ? 64u : 128u); }
@@ -84,10 +84,18 @@ inline void mat_map(CUtensorMap* m, const MatOp& o, int64_t rows, int64_t K, int
 
 template <class SA, class SB, class EP>
 void gemm_tma_mat(const MatOp& a, const MatOp& b, const EP& ep, int64_t M, int64_t N, int64_t K, int batch) {
-  CUtensorMap ma, mb;
+  CUtensorMap ma, mb, mbl;
   mat_map(&ma, a, M, K, batch, (uint32_t)tc::BM);
   mat_map(&mb, b, N, K, batch, tma_bn(N));
-  gemm_tma_bn(ma, mb, SA{a.batched ? 1 : 0}, SB{b.batched ? 1 : 0}, ep, M, N, K, batch);
+  // a dense B shared by at least 16 row tiles: split its tf32 low parts once
+  const bool pre = !b.batched && M * batch >= 16 * tc::BM && b.ld == (b.mn ? N : K);
+  if (pre) {
+    MatOp lo = b;
+    lo.p = (const float*)scratch3((size_t)N * K * sizeof(float));
+    tf32_lo_plane(b.p, (float*)lo.p, N * K);
+    mat_map(&mbl, lo, N, K, batch, tma_bn(N));
+  }
+  gemm_tma_bn(ma, mb, SA{a.batched ? 1 : 0}, SB{b.batched ? 1 : 0}, ep, M, N, K, batch, pre ? &mbl : nullptr);
 }
 
 // C = A . B^T through the TMA kernel when the path and the operands allow;

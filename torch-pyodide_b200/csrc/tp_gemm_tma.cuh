@@ -26,6 +26,10 @@
 //   warp 8             allocates TMEM; one lane issues 3 MMAs per 8-wide
 //                      k-step, A read from TMEM and B from shared memory, once
 //                      ready[s] completes, and commits to empty[s]
+// When B is reused by many tiles (conv filters) its tf32 low parts can be
+// computed once into memory (tf32_lo_plane) and loaded by TMA beside the raw
+// tile, which takes the splitters' B pass (16 + 16 KB of shared memory
+// traffic per k-block at BN = 128) off the critical path.
 // With A in TMEM the tensor core reads only B from shared memory, which is
 // what bounds this kernel: per k-block and 128-wide N tile, 128 KB of shared
 // memory traffic (TMA writes 32, splitter reads 32 and writes 16, MMA reads
@@ -351,8 +355,9 @@ __device__ __forceinline__ void read_a16(const uint8_t* tile, int r, int k0, flo
 
 template <class SA, class SB, class EP, int BN, int STAGES>
 __global__ void __launch_bounds__(NTHREADS, 1)
-    k_gemm_tma(const __grid_constant__ CUtensorMap ma, const __grid_constant__ CUtensorMap mb, SA sa, SB sb, EP ep,
-               int64_t M, int64_t N, int64_t K, int64_t k_per_split, int splits, float* __restrict__ ws) {
+    k_gemm_tma(const __grid_constant__ CUtensorMap ma, const __grid_constant__ CUtensorMap mb,
+               const __grid_constant__ CUtensorMap mbl, SA sa, SB sb, EP ep, int64_t M, int64_t N, int64_t K,
+               int64_t k_per_split, int splits, float* __restrict__ ws, int b_lo) {
   using S = Smem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   // 1 KB aligned; derived from smem_raw by an offset so accesses stay shared-space loads/stores
@@ -405,9 +410,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         ok = tc::mbar_wait(&empty[s], (uint32_t)((kb / STAGES) & 1) ^ 1u, 11);
         if (!ok) break;
         const uint32_t st = tc::smem_u32(smem + s * S::STAGE);
-        expect_tx(&full[s], S::A_BYTES + S::B_BYTES);
+        expect_tx(&full[s], S::A_BYTES + (b_lo ? 2u : 1u) * S::B_BYTES);
         sa.issue(&ma, st, &full[s], ca);
         sb.issue(&mb, st + S::A_BYTES, &full[s], cb);
+        if (b_lo) sb.issue(&mbl, st + S::A_BYTES + S::B_BYTES, &full[s], cb);
         sa.next(ca);
         sb.next(cb);
         last[s] = kb;
@@ -467,17 +473,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         tmem_st16(col, h);
         tmem_st16(col + 32, l);
       }
-      // B: the raw tile is its own hi (the tensor core truncates fp32 to tf32); only lo is written
-      const float4* hi = reinterpret_cast<const float4*>(st + S::A_BYTES);
-      float4* lo = reinterpret_cast<float4*>(st + S::A_BYTES + S::B_BYTES);
+      // B: the raw tile is its own hi (the tensor core truncates fp32 to tf32); only lo is
+      // written, unless the lo tile came from memory with the raw one (b_lo)
+      if (!b_lo) {
+        const float4* hi = reinterpret_cast<const float4*>(st + S::A_BYTES);
+        float4* lo = reinterpret_cast<float4*>(st + S::A_BYTES + S::B_BYTES);
 #pragma unroll
-      for (int i = tid; i < (int)(S::B_BYTES / 16); i += NSPLIT) {
-        float4 v = hi[i], h, l;
-        tc::split_tf32(v.x, h.x, l.x);
-        tc::split_tf32(v.y, h.y, l.y);
-        tc::split_tf32(v.z, h.z, l.z);
-        tc::split_tf32(v.w, h.w, l.w);
-        lo[i] = l;
+        for (int i = tid; i < (int)(S::B_BYTES / 16); i += NSPLIT) {
+          float4 v = hi[i], h, l;
+          tc::split_tf32(v.x, h.x, l.x);
+          tc::split_tf32(v.y, h.y, l.y);
+          tc::split_tf32(v.z, h.z, l.z);
+          tc::split_tf32(v.w, h.w, l.w);
+          lo[i] = l;
+        }
       }
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc::fence_proxy_async();
@@ -526,9 +535,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
 }  // namespace tma
 
+// mbl (optional): a map of B's tf32 low parts (tf32_lo_plane), with mb's
+// geometry; the kernel then loads them instead of computing them per tile.
 template <class SA, class SB, class EP, int BN, int STAGES>
 void gemm_tma_launch(const CUtensorMap& ma, const CUtensorMap& mb, const SA& sa, const SB& sb, const EP& ep,
-                     int64_t M, int64_t N, int64_t K, int batch) {
+                     int64_t M, int64_t N, int64_t K, int batch, const CUtensorMap* mbl = nullptr) {
   using S = tma::Smem<BN, STAGES>;
   int64_t gm = (M + tma::BM - 1) / tma::BM, gn = (N + BN - 1) / BN;
   TP_REQUIRE(gn <= 65535 && gm <= 0x7fffffff, "gemm: tile grid exceeds the launch limits");
@@ -545,8 +556,8 @@ void gemm_tma_launch(const CUtensorMap& ma, const CUtensorMap& mb, const SA& sa,
   TP_REQUIRE((int64_t)batch * splits <= 65535, "gemm: batch x splits exceeds the grid limit");
   float* ws = nullptr;
   if (splits > 1) ws = (float*)scratch((size_t)batch * splits * M * N * sizeof(float));
-  TP_LAUNCH(kfn, dim3((unsigned)gm, (unsigned)gn, (unsigned)(batch * splits)), tma::NTHREADS, S::BYTES, ma, mb, sa,
-            sb, ep, M, N, K, kps, splits, ws);
+  TP_LAUNCH(kfn, dim3((unsigned)gm, (unsigned)gn, (unsigned)(batch * splits)), tma::NTHREADS, S::BYTES, ma, mb,
+            mbl ? *mbl : mb, sa, sb, ep, M, N, K, kps, splits, ws, mbl ? 1 : 0);
   if (splits > 1) {
     auto rfn = tc::k_splitk_reduce_b<EP>;
     unsigned gx = (unsigned)((M * N / 4 + 255) / 256 + 1);

@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include "tp_core.h"
+#include "tp_launch.h"
 #include "tp_tma.h"
 
 namespace tp {
@@ -52,6 +53,31 @@ void make_map_f32(CUtensorMap* map, const void* base, int rank, const uint64_t* 
                            atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   TP_REQUIRE(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+}
+
+__global__ void k_tf32_lo(const float4* __restrict__ x, float4* __restrict__ lo, int64_t n4) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
+    const float4 v = x[i];
+    lo[i] = make_float4(v.x - __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u),
+                        v.y - __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u),
+                        v.z - __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u),
+                        v.w - __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u));
+  }
+}
+
+__global__ void k_tf32_lo_tail(const float* __restrict__ x, float* __restrict__ lo, int64_t i0, int64_t n) {
+  const int64_t i = i0 + threadIdx.x;
+  if (i < n) lo[i] = x[i] - __uint_as_float(__float_as_uint(x[i]) & 0xFFFFE000u);
+}
+
+void tf32_lo_plane(const float* x, float* lo, int64_t n) {
+  TP_REQUIRE((((uintptr_t)x | (uintptr_t)lo) & 15) == 0, "tf32 split: buffers must be 16-byte aligned");
+  const int64_t n4 = n / 4;
+  if (n4 > 0)
+    TP_LAUNCH(k_tf32_lo, grid_for(n4, 256), 256, 0, reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(lo),
+              n4);
+  if (n > n4 * 4) TP_LAUNCH(k_tf32_lo_tail, 1, 32, 0, x, lo, n4 * 4, n);
 }
 
 }  // namespace tp

@@ -20,4 +20,9 @@ void make_map_f32(CUtensorMap* map, const void* base, int rank, const uint64_t* 
 // True if TMA can address `p` with these byte strides (16-byte aligned).
 bool tma_aligned(const void* p, const uint64_t* strides, int n);
 
+// lo[i] = x[i] - tf32(x[i]) with tf32 = x with its 13 low mantissa bits
+// cleared (the 3xTF32 GEMM's split of a B operand), into `lo` (n floats, both
+// 16-byte aligned); launched on the library stream.
+void tf32_lo_plane(const float* x, float* lo, int64_t n);
+
 }  // namespace tp
