@@ -213,9 +213,12 @@ TP_API int tp_conv2d_weight_backward(int64_t grad_out, int64_t input, const int6
 TP_API int tp_conv2d_bias_backward(int64_t grad_out, int64_t out_ch, const int64_t* grad_out_shape, tp_handle* out);
 
 /* contraction engine: 0 = tcgen05 tensor cores with the 3xTF32 split (default
- * where M >= 64), operand tiles brought in by TMA where the operands allow it;
+ * where M >= 64), operand tiles brought in by TMA where the operands allow it,
+ * on CTA pairs (cta_group::2, 256 x 256 tiles) for large products with N >= 256;
  * 1 = the CUDA-core fp32 kernel everywhere (cross-check); 2 = tensor cores
- * with gathered operand tiles only (no TMA; cross-check of the TMA path) */
+ * with gathered operand tiles only (no TMA; cross-check of the TMA path);
+ * 3 = as 0 with single-CTA TMA tiles only; 4 = as 0 with CTA pairs wherever
+ * they fit (N > 32, two row tiles; cross-checks of the pair kernel) */
 TP_API int tp_set_gemm_path(int path);
 /* synchronises, then reports the tensor-core kernel's status word: 0 = ok,
  * else the code of a bounded wait that expired; reset != 0 clears it */

@@ -18,7 +18,8 @@ def status(rt):
     return v.value
 
 
-@pytest.fixture(params=[0, 1, 2], ids=["tcgen05_tma", "cuda_cores", "tcgen05_gather"])
+@pytest.fixture(params=[0, 1, 2, 3, 4],
+                ids=["tcgen05_tma", "cuda_cores", "tcgen05_gather", "tcgen05_tma_single", "tcgen05_tma_pairs"])
 def path(request, cuda_rt):
     assert cuda_rt.lib.tp_set_gemm_path(request.param) == 0
     yield request.param

@@ -59,7 +59,8 @@ def close64(got, ref, rel=1e-4):
 
 
 @pytest.mark.parametrize("M,N,K", [(128, 128, 32), (200, 52, 68), (64, 16, 1000), (512, 384, 4096),
-                                   (1000, 300, 36), (300, 1000, 2048), (96, 40, 8)])
+                                   (1000, 300, 36), (300, 1000, 2048), (96, 40, 8), (384, 96, 160),
+                                   (2048, 512, 1024)])
 @pytest.mark.parametrize("a_t", [0, 1])
 @pytest.mark.parametrize("b_t", [0, 1])
 def test_gemm_tma_bitwise_equals_gather(cuda_rt, engine, M, N, K, a_t, b_t):
@@ -72,7 +73,9 @@ def test_gemm_tma_bitwise_equals_gather(cuda_rt, engine, M, N, K, a_t, b_t):
     pb = dev(rt, B.T if b_t else B)
     pbias = dev(rt, bias)
     outs = []
-    for path in (0, 2):
+    # 3: single-CTA TMA tiles, bit-identical to the gather kernel (same tiles and
+    # split); 0: the default choice; 4: CTA pairs wherever they fit
+    for path in (3, 2, 0, 4):
         engine(path)
         pc = empty(rt, M * N)
         assert rt.lib.tpk_gemm(ctypes.c_void_p(pa), a_t, ctypes.c_void_p(pb), b_t, ctypes.c_void_p(pc), M, N, K,
@@ -82,7 +85,10 @@ def test_gemm_tma_bitwise_equals_gather(cuda_rt, engine, M, N, K, a_t, b_t):
         assert status(rt) == 0
     free(rt, pa, pb, pbias)
     assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
-    close64(outs[0], A.astype(np.float64) @ B.astype(np.float64) + bias)
+    ref = A.astype(np.float64) @ B.astype(np.float64) + bias
+    close64(outs[0], ref)
+    close64(outs[2], ref)
+    close64(outs[3], ref)
 
 
 def test_matmul_handle_tma_long_k(cuda_rt, oracle_rt):
@@ -115,7 +121,8 @@ def nhwc(a):
 
 @pytest.mark.parametrize("cin,cout,hw", NHWC_SHAPES)
 @pytest.mark.parametrize("batch", [4, 16])
-def test_conv_nhwc_matches_nchw(cuda_rt, engine, cin, cout, hw, batch):
+@pytest.mark.parametrize("nhwc_path", [0, 4], ids=["default", "cta_pairs"])
+def test_conv_nhwc_matches_nchw(cuda_rt, engine, cin, cout, hw, batch, nhwc_path):
     rt = cuda_rt
     rng = np.random.default_rng(cin + 3 * cout + hw + batch)
     x = rng.standard_normal((batch, cin, hw, hw)).astype(np.float32)
@@ -131,7 +138,7 @@ def test_conv_nhwc_matches_nchw(cuda_rt, engine, cin, cout, hw, batch):
     assert L.tpk_conv2d_fwd(vp(px), vp(pw), vp(pb), vp(y0), batch, cin, hw, hw, cout, 3, 3, 1, 1, 1, 1) == 0
     assert L.tpk_conv2d_dgrad(vp(pdy), vp(pw), vp(dx0), batch, cin, hw, hw, cout, 3, 3, 1, 1, 1, 1) == 0
     assert L.tpk_conv2d_wgrad(vp(pdy), vp(px), vp(dw0), batch, cin, hw, hw, cout, 3, 3, 1, 1, 1, 1) == 0
-    engine(0)
+    engine(nhwc_path)
     assert L.tpk_conv2d_fwd_nhwc(vp(pxn), vp(pw), vp(pb), vp(y1), batch, cin, hw, hw, cout, 3, 3, 1, 1, 0) == 0
     assert L.tpk_conv2d_dgrad_nhwc(vp(pdyn), vp(pw), vp(dx1), batch, cin, hw, hw, cout, 3, 3, 1, 1, 0) == 0
     assert L.tpk_conv2d_wgrad_nhwc(vp(pdyn), vp(pxn), vp(dw1), batch, cin, hw, hw, cout, 3, 3, 1, 1, 0) == 0
@@ -177,11 +184,13 @@ def test_conv_nhwc_against_oracle(cuda_rt, oracle_rt, cin, cout, hw, batch):
 
 @pytest.mark.parametrize("cin,cout,hw,batch", [(64, 128, 16, 4), (256, 256, 8, 8), (512, 512, 2, 8), (32, 64, 20, 2),
                                                (48, 96, 8, 4)])
-def test_conv_nhwc_packed_filters(cuda_rt, engine, cin, cout, hw, batch):
+@pytest.mark.parametrize("nhwc_path", [0, 4], ids=["default", "cta_pairs"])
+def test_conv_nhwc_packed_filters(cuda_rt, engine, cin, cout, hw, batch, nhwc_path):
     """Filters stored [Cout][KH][KW][Cin] (filter_layout 1) give the same
     forward, data gradient and (permuted) weight gradient as the reference
     layout."""
     rt, L, vp = cuda_rt, cuda_rt.lib, ctypes.c_void_p
+    engine(nhwc_path)
     rng = np.random.default_rng(cin + cout + hw + batch + 7)
     x = rng.standard_normal((batch, hw, hw, cin)).astype(np.float32)
     w = (rng.standard_normal((cout, cin, 3, 3)) * 0.05).astype(np.float32)

@@ -17,8 +17,9 @@
 
 namespace tp {
 
-// Kernel selection (tp_gemm_dispatch.cuh): 0 TMA / gather tensor cores, 1 CUDA
-// cores only, 2 gather tensor cores without TMA.
+// Kernel selection (tp_gemm_dispatch.cuh): 0 TMA (CTA pairs for large N) /
+// gather tensor cores, 1 CUDA cores only, 2 gather tensor cores without TMA, 3
+// as 0 without CTA pairs, 4 as 0 with CTA pairs wherever they fit.
 static int g_gemm_path = 0;
 int gemm_path() { return g_gemm_path; }
 
@@ -214,9 +215,9 @@ extern "C" {
 
 TP_API int tp_set_gemm_path(int path) {
   return guard([&] {
-    TP_REQUIRE(path >= 0 && path <= 2,
-               "gemm path must be 0 (tensor cores, TMA-fed where possible), 1 (CUDA cores) or 2 (tensor cores "
-               "without TMA)");
+    TP_REQUIRE(path >= 0 && path <= 4,
+               "gemm path must be 0 (tensor cores, TMA-fed where possible, CTA pairs for large N), 1 (CUDA cores), "
+               "2 (tensor cores without TMA), 3 (as 0 on single CTAs) or 4 (as 0 with CTA pairs wherever they fit)");
     g_gemm_path = path;
   });
 }

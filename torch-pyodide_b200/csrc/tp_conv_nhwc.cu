@@ -209,7 +209,7 @@ static bool nhwc_mn_map(CUtensorMap* m, const float* t, int64_t N, int64_t H, in
   return true;
 }
 
-static bool nhwc_tma_ok() { return gemm_path() == 0; }
+static bool nhwc_tma_ok() { return tma_enabled(); }
 
 // ---- launchers -------------------------------------------------------------------------------
 
@@ -265,12 +265,13 @@ static void conv_fwd_nhwc(const NhwcShape& s, const float* x, const float* w, co
   if (nhwc_tma_ok() && M >= 64 && s.Cin % 32 == 0 && pixel_tiling(s.N, s.OH, s.OW, tc::BM, tl) &&
       nhwc_map(nullptr, x, s.N, s.H, s.W, s.Cin, tl.pt, false) && mat_tma_ok(b, s.Cout)) {
     CUtensorMap ma, mb, mbl;
+    const uint32_t brows = tma_b_rows(tl.linear ? M : tl.span, s.Cout, K, 1);
     nhwc_map(&ma, x, s.N, s.H, s.W, s.Cin, tl.pt, true);
-    mat_map(&mb, b, s.Cout, K, 1, tma_bn(s.Cout));
+    mat_map(&mb, b, s.Cout, K, 1, brows);
     // every pixel tile reads all filters: split their tf32 low parts once
     float* wlo = (float*)scratch3((size_t)s.Cout * K * sizeof(float));
     tf32_lo_plane(wp, wlo, s.Cout * K);
-    mat_map(&mbl, MatOp{wlo, false, K, 0, false}, s.Cout, K, 1, tma_bn(s.Cout));
+    mat_map(&mbl, MatOp{wlo, false, K, 0, false}, s.Cout, K, 1, brows);
     tma::SrcConvK sa{tl.pt, (int)(s.Cin / 32), s.KW, s.PH, s.PW};
     if (tl.linear) gemm_tma_bn(ma, mb, sa, tma::SrcK{0}, ep, M, s.Cout, K, 1, &mbl);
     else gemm_tma_bn(ma, mb, sa, tma::SrcK{0}, EpPixTile{y, s.Cout, s.N, bias, tl.pt}, tl.span, s.Cout, K, 1, &mbl);
@@ -298,7 +299,7 @@ static void conv_dgrad_nhwc(const NhwcShape& s, const float* dy, const float* w,
     nhwc_map(&ma, dy, s.N, s.OH, s.OW, s.Cout, tl.pt, true);
     uint64_t dims[4] = {32, (uint64_t)khw, (uint64_t)s.Cout, (uint64_t)(s.Cin / 32)};
     uint64_t st[3] = {(uint64_t)s.Cin * 4, (uint64_t)(khw * s.Cin) * 4, 128};
-    uint32_t box[4] = {32, 1, 32, tma_bn(s.Cin) / 32};
+    uint32_t box[4] = {32, 1, 32, tma_b_rows(tl.linear ? M : tl.span, s.Cin, K, 1) / 32};
     make_map_f32(&mb, w, 4, dims, st, box, true);
     float* wlo = (float*)scratch3((size_t)s.Cin * K * sizeof(float));
     tf32_lo_plane(w, wlo, s.Cin * K);
@@ -314,11 +315,12 @@ static void conv_dgrad_nhwc(const NhwcShape& s, const float* dy, const float* w,
   MatOp b{wp, false, K, 0, false};
   if (tma_a && mat_tma_ok(b, s.Cin)) {
     CUtensorMap ma, mb, mbl;
+    const uint32_t brows = tma_b_rows(tl.linear ? M : tl.span, s.Cin, K, 1);
     nhwc_map(&ma, dy, s.N, s.OH, s.OW, s.Cout, tl.pt, true);
-    mat_map(&mb, b, s.Cin, K, 1, tma_bn(s.Cin));
+    mat_map(&mb, b, s.Cin, K, 1, brows);
     float* wlo = (float*)scratch3((size_t)s.Cin * K * sizeof(float));
     tf32_lo_plane(wp, wlo, s.Cin * K);
-    mat_map(&mbl, MatOp{wlo, false, K, 0, false}, s.Cin, K, 1, tma_bn(s.Cin));
+    mat_map(&mbl, MatOp{wlo, false, K, 0, false}, s.Cin, K, 1, brows);
     tma::SrcConvK sa{tl.pt, (int)(s.Cout / 32), s.KW, qh, qw};
     if (tl.linear) gemm_tma_bn(ma, mb, sa, tma::SrcK{0}, ep, M, s.Cin, K, 1, &mbl);
     else gemm_tma_bn(ma, mb, sa, tma::SrcK{0}, EpPixTile{dx, s.Cin, s.N, nullptr, tl.pt}, tl.span, s.Cin, K, 1,
@@ -338,10 +340,10 @@ static void conv_wgrad_nhwc(const NhwcShape& s, const float* dy, const float* x,
     return;
   }
   Tiling tl;
-  const uint32_t bn = tma_bn(s.Cin);
   if (nhwc_tma_ok() && s.Cout >= 64 && P > 0 && pixel_tiling(s.N, s.OH, s.OW, 32, tl) &&
       nhwc_mn_map(nullptr, dy, s.N, s.OH, s.OW, s.Cout, tl.pt, tc::BM, false) &&
-      nhwc_mn_map(nullptr, x, s.N, s.H, s.W, s.Cin, tl.pt, bn, false)) {
+      nhwc_mn_map(nullptr, x, s.N, s.H, s.W, s.Cin, tl.pt, 32, false)) {
+    const uint32_t bn = tma_b_rows(s.Cout, s.Cin, tl.span, khw);
     CUtensorMap ma, mb;
     nhwc_mn_map(&ma, dy, s.N, s.OH, s.OW, s.Cout, tl.pt, tc::BM, true);
     nhwc_mn_map(&mb, x, s.N, s.H, s.W, s.Cin, tl.pt, bn, true);
@@ -368,7 +370,7 @@ static void conv_wgrad_nhwc(const NhwcShape& s, const float* dy, const float* x,
 // gather kernel's per-element index work.
 
 static bool via_ok(const ConvShape& s) {
-  return gemm_path() == 0 && s.SH == 1 && s.SW == 1 && s.icpg == s.Cin && s.KH <= 7 && s.KW <= 7 &&
+  return tma_enabled() && s.SH == 1 && s.SW == 1 && s.icpg == s.Cin && s.KH <= 7 && s.KW <= 7 &&
          s.OH == s.H + 2 * s.PH - s.KH + 1 && s.OW == s.W + 2 * s.PW - s.KW + 1 && s.N * s.OH * s.OW >= 128;
 }
 

@@ -5,17 +5,23 @@
 //                      kernel (M >= 64, K > 0), else the CUDA-core kernel
 //   gemm_path() == 1   CUDA-core kernel only
 //   gemm_path() == 2   gather tensor-core kernel where it applies, no TMA
+//   gemm_path() == 3   as 0, but the TMA kernel on single CTAs only (no CTA pairs)
+//   gemm_path() == 4   as 0, with CTA pairs wherever they fit (N > 32, two row
+//                      tiles; cross-check of the pair kernel on small shapes)
 #pragma once
 
 #include "tp_gemm.cuh"
 #include "tp_gemm_simt.cuh"
 #include "tp_gemm_tc.cuh"
 #include "tp_gemm_tma.cuh"
+#include "tp_gemm_tma2.cuh"
 #include "tp_tma.h"
 
 namespace tp {
 
 int gemm_path();
+// paths 0 and 3 use the TMA kernels
+inline bool tma_enabled() { return gemm_path() == 0 || gemm_path() == 3 || gemm_path() == 4; }
 
 // Gather tensor-core kernel with the N tile following N (K > 0).
 template <class LA, class LB, class EP>
@@ -34,16 +40,44 @@ void gemm_auto(const LA& la, const LB& lb, const EP& ep, int64_t M, int64_t N, i
   else gemm_tc(la, lb, ep, M, N, K, batch);
 }
 
-// TMA kernel with the N tile following N; the maps' B box must match.
+inline uint32_t tma_bn(int64_t N) { return N <= 32 ? 32u : (N <= 64 ? 64u : 128u); }
+
+// The CTA-pair kernel (tp_gemm_tma2.cuh): 256 x 256 tiles, each CTA holding
+// 128 columns of B.  Its main loop does twice the work per k-block in ~1.55x
+// the time of the single-CTA kernel's, but a tile is 4x larger and its
+// epilogue 2x longer, so it is taken for N >= 256 with at least 8192 pair-tile
+// k-blocks of work (measured on the VGG convolutions: 256 -> 512 channels at
+// 4x4 1.7x faster, 512 -> 512 at 2x2 (4608 pair-tile k-blocks) 1.15x slower);
+// not yet for the wide dense products (N > 1024), whose L2 reuse it lowers.
+inline bool tma_pair(int64_t M, int64_t N, int64_t K, int batch) {
+  if (gemm_path() == 4) return M > tc::BM && N > 32;
+  if (gemm_path() != 0 || N < 256 || N > 1024 || M <= tc::BM) return false;
+  const int64_t work = ((M + 255) / 256) * ((N + 255) / 256) * batch * ((K + tc::BK - 1) / tc::BK);
+  return work >= 8192;
+}
+
+// Pair tile width: 256, or 64 / 128 for narrow N under path 4.
+inline uint32_t tma_bnp(int64_t N) { return N <= 64 ? 64u : (N <= 128 ? 128u : 256u); }
+
+// Rows of B's tensor-map box for the kernel gemm_tma_bn picks.
+inline uint32_t tma_b_rows(int64_t M, int64_t N, int64_t K, int batch) {
+  return tma_pair(M, N, K, batch) ? tma_bnp(N) / 2 : tma_bn(N);
+}
+
+// TMA kernel with the N tile following N; the maps' B box must be tma_b_rows(M, N, K, batch).
 template <class SA, class SB, class EP>
 void gemm_tma_bn(const CUtensorMap& ma, const CUtensorMap& mb, const SA& sa, const SB& sb, const EP& ep, int64_t M,
                  int64_t N, int64_t K, int batch, const CUtensorMap* mbl = nullptr) {
+  if (tma_pair(M, N, K, batch)) {
+    if (N <= 64) gemm_tma2_launch<SA, SB, EP, 32, 4>(ma, mb, sa, sb, ep, M, N, K, batch, mbl);
+    else if (N <= 128) gemm_tma2_launch<SA, SB, EP, 64, 4>(ma, mb, sa, sb, ep, M, N, K, batch, mbl);
+    else gemm_tma2_launch<SA, SB, EP, 128, 4>(ma, mb, sa, sb, ep, M, N, K, batch, mbl);
+    return;
+  }
   if (N <= 32) gemm_tma_launch<SA, SB, EP, 32, 4>(ma, mb, sa, sb, ep, M, N, K, batch, mbl);
   else if (N <= 64) gemm_tma_launch<SA, SB, EP, 64, 4>(ma, mb, sa, sb, ep, M, N, K, batch, mbl);
   else gemm_tma_launch<SA, SB, EP, 128, 4>(ma, mb, sa, sb, ep, M, N, K, batch, mbl);
 }
-
-inline uint32_t tma_bn(int64_t N) { return N <= 32 ? 32u : (N <= 64 ? 64u : 128u); }
 
 // A dense operand: element (r, k) of batch b at p[b*bs + r*ld + k] (K-major)
 // or p[b*bs + k*ld + r] (mn: MN-major); batched = false shares it across the
@@ -86,14 +120,14 @@ template <class SA, class SB, class EP>
 void gemm_tma_mat(const MatOp& a, const MatOp& b, const EP& ep, int64_t M, int64_t N, int64_t K, int batch) {
   CUtensorMap ma, mb, mbl;
   mat_map(&ma, a, M, K, batch, (uint32_t)tc::BM);
-  mat_map(&mb, b, N, K, batch, tma_bn(N));
+  mat_map(&mb, b, N, K, batch, tma_b_rows(M, N, K, batch));
   // a dense B shared by at least 16 row tiles: split its tf32 low parts once
   const bool pre = !b.batched && M * batch >= 16 * tc::BM && b.ld == (b.mn ? N : K);
   if (pre) {
     MatOp lo = b;
     lo.p = (const float*)scratch3((size_t)N * K * sizeof(float));
     tf32_lo_plane(b.p, (float*)lo.p, N * K);
-    mat_map(&mbl, lo, N, K, batch, tma_bn(N));
+    mat_map(&mbl, lo, N, K, batch, tma_b_rows(M, N, K, batch));
   }
   gemm_tma_bn(ma, mb, SA{a.batched ? 1 : 0}, SB{b.batched ? 1 : 0}, ep, M, N, K, batch, pre ? &mbl : nullptr);
 }
@@ -102,7 +136,7 @@ void gemm_tma_mat(const MatOp& a, const MatOp& b, const EP& ep, int64_t M, int64
 // returns false (nothing launched) otherwise.
 template <class EP>
 bool gemm_tma(const MatOp& a, const MatOp& b, const EP& ep, int64_t M, int64_t N, int64_t K, int batch) {
-  if (gemm_path() != 0 || K <= 0 || M < 64 || N <= 0 || batch <= 0) return false;
+  if (!tma_enabled() || K <= 0 || M < 64 || N <= 0 || batch <= 0) return false;
   if (K > 0x7fffffff || M > 0x7fffffff || N > 0x7fffffff) return false;
   if (!mat_tma_ok(a, M) || !mat_tma_ok(b, N)) return false;
   if (a.mn) {
