@@ -546,6 +546,59 @@ def vgg_launch_list(args):
     m.close()
 
 
+def run_conv_layer(args):
+    """One VGG-11-BN convolution pass on channels-last buffers with packed
+    [Cout][3][3][Cin] filters (the step's own layout and entries), timed with
+    CUDA events over --steps launches after --warmup; doubles as a small,
+    few-launch target for ncu captures of one GEMM kernel.  One JSON line."""
+    import ctypes
+    import torch
+    from tpcuda import CudaRuntime
+    from tpcuda._lib import check
+    rt = CudaRuntime(0)
+    lib = rt.lib
+    torch.cuda.set_device(0)
+    stream = torch.cuda.ExternalStream(rt.stream())
+    cin, cout, hw = (int(v) for v in args.conv.split(","))
+    B = args.batch
+    check(lib.tp_set_gemm_path(args.gemm_path))
+    rt.setSeed(0)
+    hx = rt.randn([B, hw, hw, cin], "float32")
+    hw_ = rt.randn([cout, 3, 3, cin], "float32")
+    hb = rt.randn([cout], "float32")
+    hy = rt.randn([B, hw, hw, cout], "float32")
+    hdx = rt.randn([B, hw, hw, cin], "float32")
+    hdw = rt.randn([cout, 3, 3, cin], "float32")
+    p = lambda h: ctypes.c_void_p(rt.devicePtr(h["id"]))  # noqa: E731
+    x, w, b, y, dx, dw = (p(h) for h in (hx, hw_, hb, hy, hdx, hdw))
+    if args.pass_ == "fwd":
+        fn = lambda: lib.tpk_conv2d_fwd_nhwc(x, w, b, y, B, cin, hw, hw, cout, 3, 3, 1, 1, 1)  # noqa: E731
+    elif args.pass_ == "dgrad":
+        fn = lambda: lib.tpk_conv2d_dgrad_nhwc(y, w, dx, B, cin, hw, hw, cout, 3, 3, 1, 1, 1)  # noqa: E731
+    else:
+        fn = lambda: lib.tpk_conv2d_wgrad_nhwc(y, x, dw, B, cin, hw, hw, cout, 3, 3, 1, 1, 1)  # noqa: E731
+    for _ in range(args.warmup):
+        check(fn())
+    rt.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        check(fn())
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    st = ctypes.c_int(0)
+    check(lib.tp_gemm_status(ctypes.byref(st), 1))
+    flops = 2.0 * B * hw * hw * cout * cin * 9
+    peak3, _, peak_kind = tf32x3_peak()
+    tf = flops / (ms * 1e-3) / 1e12
+    print(json.dumps({"conv": [cin, cout, hw], "pass": args.pass_, "batch": B, "gemm_path": args.gemm_path,
+                      "ms": round(ms, 4), "TFLOP/s": round(tf, 2), "frac_of_3xtf32": round(tf / peak3, 3),
+                      "peak": round(peak3, 1), "peak_source": peak_kind, "status": st.value}), flush=True)
+    for h in (hx, hw_, hb, hy, hdx, hdw):
+        rt.destroy(h["id"])
+
+
 def run_vgg(args, rank, world, local):
     import ctypes
 
@@ -685,7 +738,11 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["adamw", "vgg", "ops"], default="adamw")
+    ap.add_argument("--workload", choices=["adamw", "vgg", "ops", "conv"], default="adamw")
+    ap.add_argument("--conv", default="256,256,8", help="--workload conv: Cin,Cout,H=W of the layer")
+    ap.add_argument("--pass", dest="pass_", choices=["fwd", "dgrad", "wgrad"], default="fwd",
+                    help="--workload conv: which pass")
+    ap.add_argument("--gemm-path", type=int, default=0, help="--workload conv: tp_set_gemm_path value")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--launch-list", action="store_true",
                     help="profiling aid: two eager VGG steps at --batch with launch counts (1 GPU, no timing)")
@@ -700,6 +757,9 @@ def main():
         return
     if args.workload == "ops" and args.impl == "ours":
         run_ops(args)
+        return
+    if args.workload == "conv" and args.impl == "ours":
+        run_conv_layer(args)
         return
     rank, world, local = dist_setup(args.gpus)
     if args.impl == "reference":

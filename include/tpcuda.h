@@ -25,9 +25,11 @@
  * 362-364); the dtype code is a tag.  Index outputs of the new max-pool and
  * max-along-dim entries are physically int32.
  *
- * Ordering: all work runs on one CUDA stream per process (tp_get_stream); the
- * only host synchronisation points are tp_to_host and tp_synchronize, as in
- * the reference where readbacks are the only syncs (runtime.ts:1046-1050).
+ * Ordering: all work runs on one CUDA stream per process (tp_get_stream),
+ * except what a caller sends to the auxiliary stream between tp_aux_fork and
+ * tp_aux_return; the only host synchronisation points are tp_to_host and
+ * tp_synchronize, as in the reference where readbacks are the only syncs
+ * (runtime.ts:1046-1050).
  * Not re-entrant across threads, like the single-threaded JS event loop.
  */
 #ifndef TPCUDA_H
@@ -78,6 +80,20 @@ TP_API const char* tp_last_error(void);
 TP_API int tp_synchronize(void);
 /* the library's CUDA stream (cudaStream_t) for interop and event timing */
 TP_API int tp_get_stream(void** out);
+/* No counterpart in the reference (one WebGPU queue).  A second stream for
+ * work that may overlap: after tp_aux_fork every launch of the calling thread
+ * goes to the auxiliary stream, which first waits for all work queued on the
+ * library stream; tp_aux_return sends launches back to the library stream
+ * (no wait).  tp_aux_record(slot) marks the auxiliary stream's progress in
+ * event slot (0..63); tp_main_wait(slot) makes the library stream wait for it;
+ * tp_aux_join makes it wait for all auxiliary work.  Each stream has its own
+ * scratch space.  tp_synchronize waits for both streams.  Inside a graph
+ * capture these become the graph's fork / join edges. */
+TP_API int tp_aux_fork(void);
+TP_API int tp_aux_return(void);
+TP_API int tp_aux_record(int slot);
+TP_API int tp_main_wait(int slot);
+TP_API int tp_aux_join(void);
 /* runtime.ts:1084-1090 memoryAllocated / memoryReserved */
 TP_API int tp_memory_allocated(int64_t* out);
 TP_API int tp_memory_reserved(int64_t* out);
@@ -289,11 +305,19 @@ TP_API int tp_sgd_step_multi(const int64_t* params, const int64_t* grads, const 
  * numel) rows built once; steps then take only hyper-parameters. */
 TP_API int tpk_group_create(int n, float* const* params, float* const* grads, float* const* state0,
                             float* const* state1, const int64_t* numels, int64_t* out_group);
+/* The same with lo (NULL, or n pointers, each NULL or 16-byte aligned): the
+ * SGD step then writes lo[i] = the tf32 low parts of the updated params[i]
+ * (as tpk_tf32_lo), which the conv entries read as w_lo.  No reference
+ * counterpart (the reference has no tensor-core split). */
+TP_API int tpk_group_create_lo(int n, float* const* params, float* const* grads, float* const* state0,
+                               float* const* state1, float* const* lo, const int64_t* numels, int64_t* out_group);
 TP_API int tpk_group_destroy(int64_t group);
 /* kind 0 AdamW, 1 Adam */
 TP_API int tpk_adam_group(int64_t group, int kind, float lr, float beta1, float beta2, float eps,
                           float weight_decay, float step_size, float inv_sqrt_bc2);
-/* grad_scale multiplies each gradient on read (1/world for averaged DP grads) */
+/* grad_scale multiplies each gradient on read (1/world for averaged DP grads);
+ * rows created with a lo pointer (tpk_group_create_lo) also get the tf32 low
+ * parts of their updated parameter there */
 TP_API int tpk_sgd_group(int64_t group, float lr, float momentum, float weight_decay, float dampening,
                          int nesterov, float grad_scale);
 
@@ -321,6 +345,19 @@ TP_API int tpk_conv2d_dgrad_nhwc(const float* dy, const float* w, float* dx, int
                                  int64_t W, int64_t Cout, int KH, int KW, int PH, int PW, int filter_layout);
 TP_API int tpk_conv2d_wgrad_nhwc(const float* dy, const float* x, float* dw, int64_t N, int64_t Cin, int64_t H,
                                  int64_t W, int64_t Cout, int KH, int KW, int PH, int PW, int filter_layout);
+/* The same forward and data gradient with the filters' tf32 low parts w_lo
+ * (tpk_tf32_lo of w; NULL: computed per call) kept by the caller beside w --
+ * a step driver whose optimizer writes them (tpk_group_create_lo) saves
+ * the per-call split.  Used with filter_layout 1 (filters read in place). */
+TP_API int tpk_conv2d_fwd_nhwc_lo(const float* x, const float* w, const float* w_lo, const float* bias, float* y,
+                                  int64_t N, int64_t Cin, int64_t H, int64_t W, int64_t Cout, int KH, int KW, int PH,
+                                  int PW, int filter_layout);
+TP_API int tpk_conv2d_dgrad_nhwc_lo(const float* dy, const float* w, const float* w_lo, float* dx, int64_t N,
+                                    int64_t Cin, int64_t H, int64_t W, int64_t Cout, int KH, int KW, int PH, int PW,
+                                    int filter_layout);
+/* lo[i] = x[i] - (x[i] with its 13 low mantissa bits cleared): the low part
+ * of the 3xTF32 split (x and lo 16-byte aligned) */
+TP_API int tpk_tf32_lo(const float* x, float* lo, int64_t n);
 /* Channels-last ([P][C], P = pixels) companions of tpk_bn_train,
  * tpk_bn_backward, tpk_channel_sum and tpk_maxpool_fwd / _bwd (2x2, stride
  * 2), for the same step; C % 4 == 0 and 16-byte aligned buffers.  Pool

@@ -211,3 +211,75 @@ def test_conv_nhwc_packed_filters(cuda_rt, engine, cin, cout, hw, batch, nhwc_pa
     free(rt, px, pw, pwk, pb, pdy)
     for a, c in zip(outs[0], outs[1]):
         close64(c, a.astype(np.float64), rel=1e-5)
+
+
+@pytest.mark.parametrize("cin,cout,hw,batch", [(64, 128, 16, 4), (256, 512, 4, 8), (128, 256, 8, 2)])
+def test_conv_nhwc_filter_lo_entries(cuda_rt, cin, cout, hw, batch):
+    """The forward / data-gradient entries that take the filters' tf32 low
+    parts (tpk_tf32_lo of the filters) give the same bits as the entries that
+    split them per call."""
+    rt, L, vp = cuda_rt, cuda_rt.lib, ctypes.c_void_p
+    rng = np.random.default_rng(cin + cout + batch)
+    x = rng.standard_normal((batch, hw, hw, cin)).astype(np.float32)
+    wk = (rng.standard_normal((cout, 3, 3, cin)) * 0.05).astype(np.float32)
+    b = rng.standard_normal(cout).astype(np.float32)
+    dy = rng.standard_normal((batch, hw, hw, cout)).astype(np.float32)
+    px, pw, pb, pdy, plo = dev(rt, x), dev(rt, wk), dev(rt, b), dev(rt, dy), empty(rt, wk.size)
+    assert L.tpk_tf32_lo(vp(pw), vp(plo), wk.size) == 0
+    lo = read(rt, plo, wk.shape).astype(np.float64)
+    hi = (wk.view(np.uint32) & np.uint32(0xFFFFE000)).view(np.float32).astype(np.float64)
+    assert np.array_equal(lo, wk.astype(np.float64) - hi)
+    outs = []
+    for use_lo in (False, True):
+        y, dx = empty(rt, dy.size), empty(rt, x.size)
+        if use_lo:
+            assert L.tpk_conv2d_fwd_nhwc_lo(vp(px), vp(pw), vp(plo), vp(pb), vp(y), batch, cin, hw, hw, cout, 3, 3, 1,
+                                            1, 1) == 0
+            assert L.tpk_conv2d_dgrad_nhwc_lo(vp(pdy), vp(pw), vp(plo), vp(dx), batch, cin, hw, hw, cout, 3, 3, 1, 1,
+                                              1) == 0
+        else:
+            assert L.tpk_conv2d_fwd_nhwc(vp(px), vp(pw), vp(pb), vp(y), batch, cin, hw, hw, cout, 3, 3, 1, 1, 1) == 0
+            assert L.tpk_conv2d_dgrad_nhwc(vp(pdy), vp(pw), vp(dx), batch, cin, hw, hw, cout, 3, 3, 1, 1, 1) == 0
+        outs.append((read(rt, y, dy.shape), read(rt, dx, x.shape)))
+        free(rt, y, dx)
+    assert status(rt) == 0
+    free(rt, px, pw, pb, pdy, plo)
+    for a, c in zip(outs[0], outs[1]):
+        assert np.array_equal(a.view(np.uint32), c.view(np.uint32))
+
+
+def test_sgd_group_writes_low_parts(cuda_rt):
+    """An SGD group made with lo pointers updates params and momentum exactly as
+    one without, and leaves each updated parameter's tf32 low parts in lo."""
+    rt, L, vp = cuda_rt, cuda_rt.lib, ctypes.c_void_p
+    rng = np.random.default_rng(3)
+    sizes = [4096 * 3 + 7, 1000, 64]
+    res = []
+    for with_lo in (False, True):
+        P = [dev(rt, rng.standard_normal(n) * 0.1) if not res else dev(rt, res[0]["p0"][i]) for i, n in enumerate(sizes)]
+        if not res:
+            p0 = [read(rt, p, (n,)) for p, n in zip(P, sizes)]
+        G = [dev(rt, np.full(n, 0.01 * (i + 1), np.float32)) for i, n in enumerate(sizes)]
+        Mo = [dev(rt, np.zeros(n, np.float32)) for n in sizes]
+        LO = [empty(rt, n) for n in sizes]
+        arr = lambda ps: (ctypes.c_void_p * len(ps))(*ps)  # noqa: E731
+        numels = (ctypes.c_int64 * len(sizes))(*sizes)
+        g = ctypes.c_int64(0)
+        lo_rows = (ctypes.c_void_p * len(sizes))(LO[0], None, LO[2]) if with_lo else None
+        assert L.tpk_group_create_lo(len(sizes), arr(P), arr(G), arr(Mo), None, lo_rows, numels, ctypes.byref(g)) == 0
+        for _ in range(2):
+            assert L.tpk_sgd_group(g.value, 0.05, 0.9, 5e-4, 0.0, 0, 0.5) == 0
+        out = {"p": [read(rt, p, (n,)) for p, n in zip(P, sizes)], "m": [read(rt, m, (n,)) for m, n in zip(Mo, sizes)],
+               "lo": [read(rt, q, (n,)) for q, n in zip(LO, sizes)]}
+        if not res:
+            out["p0"] = p0
+        res.append(out)
+        assert L.tpk_group_destroy(g.value) == 0
+        free(rt, *P, *G, *Mo, *LO)
+    a, c = res
+    for i in range(len(sizes)):
+        assert np.array_equal(a["p"][i], c["p"][i]) and np.array_equal(a["m"][i], c["m"][i])
+    for i in (0, 2):
+        p = c["p"][i]
+        hi = (p.view(np.uint32) & np.uint32(0xFFFFE000)).view(np.float32)
+        assert np.array_equal(c["lo"][i], p - hi)

@@ -243,7 +243,10 @@ void conv_c4_wgrad(const float* dy, const float* x, float* dw, int64_t N, int64_
                    int PW);
 
 // y[N][OH][OW][Cout] = conv(x[N][H][W][Cin], w) + bias
-static void conv_fwd_nhwc(const NhwcShape& s, const float* x, const float* w, const float* bias, float* y) {
+// w_lo (optional): the tf32 low parts of w (tf32_lo_plane), kept by the caller
+// beside w; used when the filters are read in place (filter layout 1).
+static void conv_fwd_nhwc(const NhwcShape& s, const float* x, const float* w, const float* bias, float* y,
+                          const float* w_lo = nullptr) {
   const int khw = s.KH * s.KW;
   const int64_t M = s.N * s.OH * s.OW, K = s.Cin * khw;
   if (M == 0) return;
@@ -268,9 +271,13 @@ static void conv_fwd_nhwc(const NhwcShape& s, const float* x, const float* w, co
     const uint32_t brows = tma_b_rows(tl.linear ? M : tl.span, s.Cout, K, 1);
     nhwc_map(&ma, x, s.N, s.H, s.W, s.Cin, tl.pt, true);
     mat_map(&mb, b, s.Cout, K, 1, brows);
-    // every pixel tile reads all filters: split their tf32 low parts once
-    float* wlo = (float*)scratch3((size_t)s.Cout * K * sizeof(float));
-    tf32_lo_plane(wp, wlo, s.Cout * K);
+    // every pixel tile reads all filters: their tf32 low parts are split once
+    const float* wlo = (w_lo && wp == w) ? w_lo : nullptr;
+    if (!wlo) {
+      float* t = (float*)scratch3((size_t)s.Cout * K * sizeof(float));
+      tf32_lo_plane(wp, t, s.Cout * K);
+      wlo = t;
+    }
     mat_map(&mbl, MatOp{wlo, false, K, 0, false}, s.Cout, K, 1, brows);
     tma::SrcConvK sa{tl.pt, (int)(s.Cin / 32), s.KW, s.PH, s.PW};
     if (tl.linear) gemm_tma_bn(ma, mb, sa, tma::SrcK{0}, ep, M, s.Cout, K, 1, &mbl);
@@ -283,7 +290,8 @@ static void conv_fwd_nhwc(const NhwcShape& s, const float* x, const float* w, co
 
 // dx[N][H][W][Cin] from dy[N][OH][OW][Cout]: the forward convolution of dy
 // with the flipped, transposed filters and padding K-1-P.
-static void conv_dgrad_nhwc(const NhwcShape& s, const float* dy, const float* w, float* dx) {
+static void conv_dgrad_nhwc(const NhwcShape& s, const float* dy, const float* w, float* dx,
+                            const float* w_lo = nullptr) {
   const int khw = s.KH * s.KW;
   const int64_t M = s.N * s.H * s.W, K = s.Cout * khw;
   if (M == 0) return;
@@ -301,8 +309,13 @@ static void conv_dgrad_nhwc(const NhwcShape& s, const float* dy, const float* w,
     uint64_t st[3] = {(uint64_t)s.Cin * 4, (uint64_t)(khw * s.Cin) * 4, 128};
     uint32_t box[4] = {32, 1, 32, tma_b_rows(tl.linear ? M : tl.span, s.Cin, K, 1) / 32};
     make_map_f32(&mb, w, 4, dims, st, box, true);
-    float* wlo = (float*)scratch3((size_t)s.Cin * K * sizeof(float));
-    tf32_lo_plane(w, wlo, s.Cin * K);
+    const float* wlo = w_lo;
+    if (!wlo) {
+      float* t = (float*)scratch3((size_t)s.Cin * K * sizeof(float));
+      tf32_lo_plane(w, t, s.Cin * K);
+      wlo = t;
+    }
+    TP_REQUIRE(((uintptr_t)wlo & 15) == 0, "conv2d data gradient (channels-last): w_lo must be 16-byte aligned");
     make_map_f32(&mbl, wlo, 4, dims, st, box, true);
     tma::SrcConvK sa{tl.pt, (int)(s.Cout / 32), s.KW, qh, qw};
     tma::SrcFilterMN sb{(int)(s.Cout / 32), khw};
@@ -445,6 +458,28 @@ TP_API int tpk_conv2d_dgrad_nhwc(const float* dy, const float* w, float* dx, int
 TP_API int tpk_conv2d_wgrad_nhwc(const float* dy, const float* x, float* dw, int64_t N, int64_t Cin, int64_t H,
                                  int64_t W, int64_t Cout, int KH, int KW, int PH, int PW, int filter_layout) {
   return guard([&] { conv_wgrad_nhwc(nhwc_shape(N, Cin, H, W, Cout, KH, KW, PH, PW, filter_layout), dy, x, dw); });
+}
+
+TP_API int tpk_conv2d_fwd_nhwc_lo(const float* x, const float* w, const float* w_lo, const float* bias, float* y,
+                                  int64_t N, int64_t Cin, int64_t H, int64_t W, int64_t Cout, int KH, int KW, int PH,
+                                  int PW, int filter_layout) {
+  return guard([&] {
+    conv_fwd_nhwc(nhwc_shape(N, Cin, H, W, Cout, KH, KW, PH, PW, filter_layout), x, w, bias, y, w_lo);
+  });
+}
+
+TP_API int tpk_conv2d_dgrad_nhwc_lo(const float* dy, const float* w, const float* w_lo, float* dx, int64_t N,
+                                    int64_t Cin, int64_t H, int64_t W, int64_t Cout, int KH, int KW, int PH, int PW,
+                                    int filter_layout) {
+  return guard([&] {
+    conv_dgrad_nhwc(nhwc_shape(N, Cin, H, W, Cout, KH, KW, PH, PW, filter_layout), dy, w, dx, w_lo);
+  });
+}
+
+TP_API int tpk_tf32_lo(const float* x, float* lo, int64_t n) {
+  return guard([&] {
+    if (n > 0) tf32_lo_plane(x, lo, n);
+  });
 }
 
 }  // extern "C"

@@ -14,12 +14,18 @@ namespace tp {
 static thread_local std::string g_err;
 static int g_device = -1;
 static cudaStream_t g_stream = nullptr;
+// A second stream for work that may overlap the main one (a convolution's
+// weight gradient beside its data gradient); launches go to g_aux between
+// tp_aux_fork and tp_aux_return on the calling thread.
+static cudaStream_t g_aux = nullptr;
+static thread_local int g_cur = 0;
 static int g_sms = 148;
 static std::unordered_map<int64_t, Tensor> g_tensors;
 static int64_t g_next_id = 1;
 static int64_t g_allocated = 0;
-static void* g_scratch = nullptr;
-static size_t g_scratch_bytes = 0;
+// scratch areas per stream (index g_cur), so overlapping work never shares one
+static void* g_scratch[2] = {nullptr, nullptr};
+static size_t g_scratch_bytes[2] = {0, 0};
 std::atomic<int64_t> g_launches{0};
 
 void set_error(const char* msg) { g_err = msg ? msg : ""; }
@@ -54,9 +60,15 @@ void ensure_init() {
   g_device = dev;
 }
 
+static cudaStream_t aux_stream() {
+  ensure_init();
+  if (!g_aux) TP_CUDA(cudaStreamCreateWithFlags(&g_aux, cudaStreamNonBlocking));
+  return g_aux;
+}
+
 cudaStream_t stream() {
   ensure_init();
-  return g_stream;
+  return g_cur ? aux_stream() : g_stream;
 }
 int device() {
   ensure_init();
@@ -71,7 +83,7 @@ void* dalloc(size_t bytes) {
   ensure_init();
   if (bytes == 0) bytes = 4;
   void* p = nullptr;
-  cudaError_t e = cudaMallocAsync(&p, bytes, g_stream);
+  cudaError_t e = cudaMallocAsync(&p, bytes, stream());
   if (e != cudaSuccess) {
     cudaGetLastError();
     fail(TP_ERR_OOM, "device allocation of %zu bytes failed: %s", bytes, cudaGetErrorString(e));
@@ -80,43 +92,71 @@ void* dalloc(size_t bytes) {
 }
 
 void dfree(void* p) {
-  if (p) TP_CUDA(cudaFreeAsync(p, g_stream));
+  if (p) TP_CUDA(cudaFreeAsync(p, stream()));
 }
 
-void* scratch(size_t bytes) {
-  if (bytes > g_scratch_bytes) {
-    if (g_scratch) dfree(g_scratch);
+static void* grow(void** slot, size_t* have, size_t bytes) {
+  if (bytes > *have) {
+    if (*slot) dfree(*slot);
     size_t nb = bytes < (1u << 20) ? (1u << 20) : bytes;
-    g_scratch = dalloc(nb);
-    g_scratch_bytes = nb;
+    *slot = dalloc(nb);
+    *have = nb;
   }
-  return g_scratch;
+  return *slot;
 }
 
-static void* g_scratch2 = nullptr;
-static size_t g_scratch2_bytes = 0;
+void* scratch(size_t bytes) { return grow(&g_scratch[g_cur], &g_scratch_bytes[g_cur], bytes); }
 
-void* scratch2(size_t bytes) {
-  if (bytes > g_scratch2_bytes) {
-    if (g_scratch2) dfree(g_scratch2);
-    size_t nb = bytes < (1u << 20) ? (1u << 20) : bytes;
-    g_scratch2 = dalloc(nb);
-    g_scratch2_bytes = nb;
-  }
-  return g_scratch2;
+static void* g_scratch2[2] = {nullptr, nullptr};
+static size_t g_scratch2_bytes[2] = {0, 0};
+
+void* scratch2(size_t bytes) { return grow(&g_scratch2[g_cur], &g_scratch2_bytes[g_cur], bytes); }
+
+static void* g_scratch3[2] = {nullptr, nullptr};
+static size_t g_scratch3_bytes[2] = {0, 0};
+
+void* scratch3(size_t bytes) { return grow(&g_scratch3[g_cur], &g_scratch3_bytes[g_cur], bytes); }
+
+// ---- the auxiliary stream ----------------------------------------------------------------
+static cudaEvent_t g_fork_ev = nullptr, g_join_ev = nullptr;
+static cudaEvent_t g_slot_ev[64];
+static bool g_slot_made[64];
+
+static cudaEvent_t make_event(cudaEvent_t* e) {
+  if (!*e) TP_CUDA(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
+  return *e;
 }
 
-static void* g_scratch3 = nullptr;
-static size_t g_scratch3_bytes = 0;
+void aux_fork() {
+  TP_REQUIRE(g_cur == 0, "tp_aux_fork: already on the auxiliary stream");
+  cudaStream_t a = aux_stream();
+  TP_CUDA(cudaEventRecord(make_event(&g_fork_ev), g_stream));
+  TP_CUDA(cudaStreamWaitEvent(a, g_fork_ev, 0));
+  g_cur = 1;
+}
 
-void* scratch3(size_t bytes) {
-  if (bytes > g_scratch3_bytes) {
-    if (g_scratch3) dfree(g_scratch3);
-    size_t nb = bytes < (1u << 20) ? (1u << 20) : bytes;
-    g_scratch3 = dalloc(nb);
-    g_scratch3_bytes = nb;
+void aux_return() { g_cur = 0; }
+
+void aux_record(int slot) {
+  TP_REQUIRE(slot >= 0 && slot < 64, "event slot must be in [0, 64)");
+  if (!g_slot_made[slot]) {
+    TP_CUDA(cudaEventCreateWithFlags(&g_slot_ev[slot], cudaEventDisableTiming));
+    g_slot_made[slot] = true;
   }
-  return g_scratch3;
+  TP_CUDA(cudaEventRecord(g_slot_ev[slot], aux_stream()));
+}
+
+void main_wait(int slot) {
+  TP_REQUIRE(slot >= 0 && slot < 64 && g_slot_made[slot], "event slot %d was never recorded", slot);
+  ensure_init();
+  TP_CUDA(cudaStreamWaitEvent(g_stream, g_slot_ev[slot], 0));
+}
+
+void aux_join() {
+  ensure_init();
+  if (!g_aux) return;
+  TP_CUDA(cudaEventRecord(make_event(&g_join_ev), g_aux));
+  TP_CUDA(cudaStreamWaitEvent(g_stream, g_join_ev, 0));
 }
 
 int64_t prod(const int64_t* s, int n) {
@@ -215,7 +255,19 @@ TP_API int tp_device_count(int* out) {
   });
 }
 
-TP_API int tp_synchronize(void) { return guard([&] { TP_CUDA(cudaStreamSynchronize(stream())); }); }
+TP_API int tp_synchronize(void) {
+  return guard([&] {
+    ensure_init();
+    TP_CUDA(cudaStreamSynchronize(g_stream));
+    if (g_aux) TP_CUDA(cudaStreamSynchronize(g_aux));
+  });
+}
+
+TP_API int tp_aux_fork(void) { return guard([&] { aux_fork(); }); }
+TP_API int tp_aux_return(void) { return guard([&] { aux_return(); }); }
+TP_API int tp_aux_record(int slot) { return guard([&] { aux_record(slot); }); }
+TP_API int tp_main_wait(int slot) { return guard([&] { main_wait(slot); }); }
+TP_API int tp_aux_join(void) { return guard([&] { aux_join(); }); }
 
 TP_API int tp_get_stream(void** out) { return guard([&] { *out = (void*)stream(); }); }
 

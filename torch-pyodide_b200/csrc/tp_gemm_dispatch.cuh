@@ -32,11 +32,13 @@ void gemm_tc(const LA& la, const LB& lb, const EP& ep, int64_t M, int64_t N, int
   else gemm_tc_launch<LA, LB, EP, 128, 3>(la, lb, ep, M, N, K, batch);
 }
 
-// Gather tensor-core path for M >= 64 with K > 0, else the CUDA-core kernel.
+// Products with a side of at most 16 rows: the skinny CUDA-core kernel.  Else
+// the gather tensor-core path for M >= 64 and K > 16, else the CUDA-core kernel.
 template <class LA, class LB, class EP>
 void gemm_auto(const LA& la, const LB& lb, const EP& ep, int64_t M, int64_t N, int64_t K, int batch) {
   if (M == 0 || N == 0 || batch == 0) return;
-  if (gemm_path() == 1 || K == 0 || M < 64) gemm_simt(la, lb, ep, M, N, K, batch);
+  if (gemm_skinny_ok(M, N, batch)) gemm_skinny(la, lb, ep, M, N, K);
+  else if (gemm_path() == 1 || K <= 16 || M < 64) gemm_simt(la, lb, ep, M, N, K, batch);
   else gemm_tc(la, lb, ep, M, N, K, batch);
 }
 
@@ -136,7 +138,8 @@ void gemm_tma_mat(const MatOp& a, const MatOp& b, const EP& ep, int64_t M, int64
 // returns false (nothing launched) otherwise.
 template <class EP>
 bool gemm_tma(const MatOp& a, const MatOp& b, const EP& ep, int64_t M, int64_t N, int64_t K, int batch) {
-  if (!tma_enabled() || K <= 0 || M < 64 || N <= 0 || batch <= 0) return false;
+  if (!tma_enabled() || K <= 16 || M < 64 || N <= 0 || batch <= 0) return false;
+  if (gemm_skinny_ok(M, N, batch)) return false;
   if (K > 0x7fffffff || M > 0x7fffffff || N > 0x7fffffff) return false;
   if (!mat_tma_ok(a, M) || !mat_tma_ok(b, N)) return false;
   if (a.mn) {

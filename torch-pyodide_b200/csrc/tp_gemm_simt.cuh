@@ -158,4 +158,86 @@ void gemm_simt(const LA& la, const LB& lb, const EP& ep, int64_t M, int64_t N, i
   }
 }
 
+// ---- skinny products: one side of at most 16 rows ---------------------------------------------
+// C(m, n) = sum_k A(m, k) B(n, k) with M <= 16 (SMALL_IS_M) or N <= 16.  A
+// 128-thread CTA takes 128 rows l of the large side and a k range; per chunk
+// of 32 k the small side's values are staged in shared memory (read back as
+// broadcasts) and each thread first loads its 32 large-side values, then does
+// the S x 32 multiply-adds with its S sums in registers, so 32 loads are in
+// flight per thread instead of one at a time.  A 128 x 128 tensor-core or
+// CUDA-core tile would be more than 87% padding here (the 512 -> 10
+// classifier of a CNN, its weight gradient).  Partial sums of a k split go to
+// ws[split][M][N], which k_splitk_reduce adds in split order.
+constexpr int SK_S = 16, SK_KC = 32, SK_THREADS = 128;
+
+template <class LS, class LL, class EP, bool SMALL_IS_M>
+__global__ void __launch_bounds__(SK_THREADS) k_gemm_skinny(LS ls, LL ll, EP ep, int64_t M, int64_t N, int64_t K,
+                                                            int64_t k_per_split, int splitk, float* __restrict__ ws) {
+  __shared__ float sm[SK_KC][SK_S];
+  const int64_t S = SMALL_IS_M ? M : N, L = SMALL_IS_M ? N : M;
+  const int64_t l = (int64_t)blockIdx.x * SK_THREADS + threadIdx.x;
+  const int z = blockIdx.y;
+  const int64_t kb = (int64_t)z * k_per_split;
+  const int64_t ke = kb + k_per_split < K ? kb + k_per_split : K;
+  float acc[SK_S];
+#pragma unroll
+  for (int j = 0; j < SK_S; ++j) acc[j] = 0.0f;
+  for (int64_t k0 = kb; k0 < ke; k0 += SK_KC) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < SK_KC * SK_S; i += SK_THREADS) {
+      const int kk = i / SK_S, j = i % SK_S;
+      sm[kk][j] = (j < S && k0 + kk < ke) ? ls(0, j, k0 + kk) : 0.0f;
+    }
+    float v[SK_KC];
+#pragma unroll
+    for (int kk = 0; kk < SK_KC; ++kk) v[kk] = (l < L && k0 + kk < ke) ? ll(0, l, k0 + kk) : 0.0f;
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < SK_KC; ++kk)
+#pragma unroll
+      for (int j = 0; j < SK_S; ++j) acc[j] = fmaf(sm[kk][j], v[kk], acc[j]);
+  }
+  if (l >= L) return;
+#pragma unroll
+  for (int j = 0; j < SK_S; ++j) {
+    if (j >= S) break;
+    const int64_t m = SMALL_IS_M ? j : l, n = SMALL_IS_M ? l : j;
+    if (splitk) ws[((int64_t)z * M + m) * N + n] = acc[j];
+    else ep(0, m, n, acc[j]);
+  }
+}
+
+inline bool gemm_skinny_ok(int64_t M, int64_t N, int batch) { return batch == 1 && (M <= SK_S || N <= SK_S); }
+
+template <class LA, class LB, class EP>
+void gemm_skinny(const LA& la, const LB& lb, const EP& ep, int64_t M, int64_t N, int64_t K) {
+  if (M == 0 || N == 0) return;
+  const bool small_m = M <= SK_S;
+  const int64_t L = small_m ? N : M;
+  const int64_t lblocks = (L + SK_THREADS - 1) / SK_THREADS;
+  int splits = 1;
+  if (K > 0) {
+    // about 4 CTAs per SM, at least one 32-wide chunk of k each
+    int64_t want = (4 * (int64_t)sm_count() + lblocks - 1) / lblocks;
+    int64_t maxs = (K + SK_KC - 1) / SK_KC;
+    splits = (int)(want < maxs ? want : maxs);
+    if (splits > 256) splits = 256;
+    if (splits < 1) splits = 1;
+  }
+  int64_t kps = (K + splits - 1) / splits;
+  kps = (kps + SK_KC - 1) / SK_KC * SK_KC;
+  if (K > 0) splits = (int)((K + kps - 1) / kps);
+  TP_REQUIRE(lblocks <= 0x7fffffff, "gemm: too many rows");
+  float* ws = splits > 1 ? (float*)scratch((size_t)splits * M * N * sizeof(float)) : nullptr;
+  const dim3 grid((unsigned)lblocks, (unsigned)splits);
+  if (small_m)
+    TP_LAUNCH((k_gemm_skinny<LA, LB, EP, true>), grid, SK_THREADS, 0, la, lb, ep, M, N, K, kps, splits > 1, ws);
+  else
+    TP_LAUNCH((k_gemm_skinny<LB, LA, EP, false>), grid, SK_THREADS, 0, lb, la, ep, M, N, K, kps, splits > 1, ws);
+  if (splits > 1) {
+    auto rfn = k_splitk_reduce<EP>;
+    TP_LAUNCH(rfn, grid_for(M * N, 256), 256, 0, ws, splits, M, N, 0, ep);
+  }
+}
+
 }  // namespace tp

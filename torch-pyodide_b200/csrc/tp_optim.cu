@@ -29,6 +29,7 @@ struct OptRow {
   const float* g;
   float* s0;
   float* s1;
+  float* lo;  // SGD: the updated parameter's tf32 low parts (optional)
   int64_t n;
 };
 struct OptChunk {
@@ -123,6 +124,14 @@ __device__ __forceinline__ void sgd_elem(float& p, float g, float& buf, const Sg
   p = __fsub_rn(p, __fmul_rn(h.lr, upd));
 }
 
+// x - (x with its 13 low mantissa bits cleared) per lane: the 3xTF32 low part
+__device__ __forceinline__ float4 tf32_lo4(float4 v) {
+  return make_float4(v.x - __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u),
+                     v.y - __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u),
+                     v.z - __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u),
+                     v.w - __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u));
+}
+
 __global__ void __launch_bounds__(256) k_sgd_multi(const OptRow* __restrict__ rows, const OptChunk* __restrict__ chunks,
                                                    int nchunks, SgdHP h) {
   for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
@@ -135,6 +144,9 @@ __global__ void __launch_bounds__(256) k_sgd_multi(const OptRow* __restrict__ ro
     float4* P4 = reinterpret_cast<float4*>(P);
     const float4* G4 = reinterpret_cast<const float4*>(G);
     float4* B4 = reinterpret_cast<float4*>(B);
+    // the updated parameter's tf32 low parts, for rows that keep them
+    float* __restrict__ LO = r.lo ? r.lo + ch.start : nullptr;
+    float4* LO4 = reinterpret_cast<float4*>(LO);
     int i = threadIdx.x;
     for (; i + (int)blockDim.x < len4; i += 2 * blockDim.x) {
       int j = i + blockDim.x;
@@ -147,6 +159,7 @@ __global__ void __launch_bounds__(256) k_sgd_multi(const OptRow* __restrict__ ro
       sgd_elem(p1.z, g1.z, b1.z, h); sgd_elem(p1.w, g1.w, b1.w, h);
       P4[i] = p0; P4[j] = p1;
       if (h.has_m) { B4[i] = b0; B4[j] = b1; }
+      if (LO4) { LO4[i] = tf32_lo4(p0); LO4[j] = tf32_lo4(p1); }
     }
     for (; i < len4; i += blockDim.x) {
       float4 p0 = P4[i], g0 = G4[i];
@@ -155,12 +168,14 @@ __global__ void __launch_bounds__(256) k_sgd_multi(const OptRow* __restrict__ ro
       sgd_elem(p0.z, g0.z, b0.z, h); sgd_elem(p0.w, g0.w, b0.w, h);
       P4[i] = p0;
       if (h.has_m) B4[i] = b0;
+      if (LO4) LO4[i] = tf32_lo4(p0);
     }
     for (int k = (len4 << 2) + threadIdx.x; k < len; k += blockDim.x) {
       float p = P[k], b = h.has_m ? B[k] : 0.0f;
       sgd_elem(p, G[k], b, h);
       P[k] = p;
       if (h.has_m) B[k] = b;
+      if (LO) LO[k] = p - __uint_as_float(__float_as_uint(p) & 0xFFFFE000u);
     }
   }
 }
@@ -181,7 +196,7 @@ static Group build_group(const std::vector<OptRow>& rows) {
   std::vector<OptChunk> chunks;
   for (size_t r = 0; r < rows.size(); ++r) {
     const OptRow& x = rows[r];
-    TP_REQUIRE((((uintptr_t)x.p | (uintptr_t)x.g | (uintptr_t)x.s0 | (uintptr_t)x.s1) & 15) == 0,
+    TP_REQUIRE((((uintptr_t)x.p | (uintptr_t)x.g | (uintptr_t)x.s0 | (uintptr_t)x.s1 | (uintptr_t)x.lo) & 15) == 0,
                "optimizer tensors must be 16-byte aligned");
     for (int64_t s = 0; s < x.n; s += OPT_CHUNK) {
       OptChunk c;
@@ -243,7 +258,7 @@ static std::vector<OptRow> rows_from_ids(const int64_t* p, const int64_t* gr, co
     Tensor* t1 = s1 ? &get(s1[i]) : nullptr;
     if (tg.numel != tp_.numel || t0.numel != tp_.numel || (t1 && t1->numel != tp_.numel))
       fail(TP_ERR_ARG, "%s: tensor lengths must match", what);
-    rows[i] = OptRow{tp_.f(), tg.f(), t0.f(), t1 ? t1->f() : t0.f(), tp_.numel};
+    rows[i] = OptRow{tp_.f(), tg.f(), t0.f(), t1 ? t1->f() : t0.f(), nullptr, tp_.numel};
   }
   return rows;
 }
@@ -296,18 +311,24 @@ TP_API int tp_sgd_step(int64_t p, int64_t g, int64_t b, float lr, float mom, flo
   return tp_sgd_step_multi(&p, &g, &b, 1, lr, mom, wd, damp, nesterov);
 }
 
-TP_API int tpk_group_create(int n, float* const* params, float* const* grads, float* const* state0,
-                            float* const* state1, const int64_t* numels, int64_t* out_group) {
+TP_API int tpk_group_create_lo(int n, float* const* params, float* const* grads, float* const* state0,
+                               float* const* state1, float* const* lo, const int64_t* numels, int64_t* out_group) {
   return guard([&] {
     TP_REQUIRE(n >= 0, "negative group size");
     std::vector<OptRow> rows((size_t)n);
     for (int i = 0; i < n; ++i)
-      rows[i] = OptRow{params[i], grads[i], state0[i], state1 ? state1[i] : state0[i], numels[i]};
+      rows[i] = OptRow{params[i], grads[i], state0[i], state1 ? state1[i] : state0[i], lo ? lo[i] : nullptr,
+                       numels[i]};
     Group g = build_group(rows);
     int64_t id = g_next_group++;
     g_groups[id] = g;
     *out_group = id;
   });
+}
+
+TP_API int tpk_group_create(int n, float* const* params, float* const* grads, float* const* state0,
+                            float* const* state1, const int64_t* numels, int64_t* out_group) {
+  return tpk_group_create_lo(n, params, grads, state0, state1, nullptr, numels, out_group);
 }
 
 TP_API int tpk_group_destroy(int64_t group) {

@@ -60,6 +60,11 @@ SIGNATURES: dict[str, list] = {
     "tp_last_error": [],
     "tp_synchronize": [],
     "tp_get_stream": [PP],
+    "tp_aux_fork": [],
+    "tp_aux_return": [],
+    "tp_aux_record": [INT],
+    "tp_main_wait": [INT],
+    "tp_aux_join": [],
     "tp_memory_allocated": [I64P],
     "tp_memory_reserved": [I64P],
     "tp_device_name": [ctypes.c_char_p, INT],
@@ -134,6 +139,7 @@ SIGNATURES: dict[str, list] = {
     "tp_adam_step_multi": [I64P, I64P, I64P, I64P, INT] + [F32] * 7,
     "tp_sgd_step_multi": [I64P, I64P, I64P, INT, F32, F32, F32, F32, INT],
     "tpk_group_create": [INT, PP, PP, PP, PP, I64P, I64P],
+    "tpk_group_create_lo": [INT, PP, PP, PP, PP, PP, I64P, I64P],
     "tpk_group_destroy": [I64],
     "tpk_adam_group": [I64, INT] + [F32] * 7,
     "tpk_sgd_group": [I64, F32, F32, F32, F32, INT, F32],
@@ -151,6 +157,9 @@ SIGNATURES: dict[str, list] = {
     "tpk_conv2d_fwd_nhwc": [P, P, P, P, I64, I64, I64, I64, I64, INT, INT, INT, INT, INT],
     "tpk_conv2d_dgrad_nhwc": [P, P, P, I64, I64, I64, I64, I64, INT, INT, INT, INT, INT],
     "tpk_conv2d_wgrad_nhwc": [P, P, P, I64, I64, I64, I64, I64, INT, INT, INT, INT, INT],
+    "tpk_conv2d_fwd_nhwc_lo": [P, P, P, P, P, I64, I64, I64, I64, I64, INT, INT, INT, INT, INT],
+    "tpk_conv2d_dgrad_nhwc_lo": [P, P, P, P, I64, I64, I64, I64, I64, INT, INT, INT, INT, INT],
+    "tpk_tf32_lo": [P, P, I64],
     "tpk_channel_sum": [P, I64, I64, I64, P],
     "tpk_bn_train": [P, P, P, P, P, P, P, P, I64, I64, I64, F32, F32, INT],
     "tpk_bn_backward": [P, P, P, P, P, P, P, P, P, I64, I64, I64],

@@ -215,6 +215,11 @@ class VGG11BN:
         self.grads = self._alloc(self.flat_len * 4)
         self.moms = self._alloc(self.flat_len * 4)
         self._h2d(self.params, init_params(specs, self.offsets, self.flat_len, seed, self.cin0, self.khwc))
+        # tf32 low parts of the parameters, which the conv kernels read beside the
+        # filters (channels-last step only); the SGD step keeps them current
+        self.params_lo = self._alloc(self.flat_len * 4) if self.khwc else 0
+        if self.params_lo:
+            check(self.lib.tpk_tf32_lo(_vp(self.params), _vp(self.params_lo), self.flat_len))
         check(self.lib.tp_memset(_vp(self.grads), 0, self.flat_len * 4))
         check(self.lib.tp_memset(_vp(self.moms), 0, self.flat_len * 4))
 
@@ -251,15 +256,26 @@ class VGG11BN:
         self.loss_rows = self._alloc(Bn * 4)
         self.loss = self._alloc(4)
         self.dfeat = self._alloc(Bn * self.feat * 4)
-        self.gbuf = [self._alloc(max_act * 4), self._alloc(max_act * 4)]
+        # gradient buffers, used in rotation; channels-last steps run each weight
+        # gradient on the auxiliary stream beside the next data gradient, so a
+        # buffer is reused only after the weight gradient that read it is done
+        self.overlap = layout == "nhwc"
+        self.gbuf = [self._alloc(max_act * 4) for _ in range(4 if self.overlap else 2)]
 
         # ---- optimizer group: every parameter tensor, fused SGD ----
         names = [n for n, _, _ in specs]
         ptr = lambda base: (ctypes.c_void_p * len(names))(*[base + 4 * self.offsets[n][0] for n in names])  # noqa
         numels = (ctypes.c_int64 * len(names))(*[self.offsets[n][1] for n in names])
+        # the SGD step also writes the updated tf32 low parts of the conv filters
+        # that the tensor-core kernels read in place (all but the first)
+        lo_rows = None
+        if self.params_lo:
+            lo_rows = (ctypes.c_void_p * len(names))(*[
+                self.params_lo + 4 * self.offsets[n][0] if (n.startswith("conv") and n.endswith(".w")
+                                                            and n != "conv0.w") else None for n in names])
         g = ctypes.c_int64(0)
-        check(self.lib.tpk_group_create(len(names), ptr(self.params), ptr(self.grads), ptr(self.moms), None, numels,
-                                        ctypes.byref(g)))
+        check(self.lib.tpk_group_create_lo(len(names), ptr(self.params), ptr(self.grads), ptr(self.moms), None,
+                                           lo_rows, numels, ctypes.byref(g)))
         self.group = g.value
 
         # gradient buckets (contiguous ranges of the flat gradient buffer)
@@ -279,6 +295,10 @@ class VGG11BN:
 
     def p(self, name: str) -> int:
         return self.params + 4 * self.offsets[name][0]
+
+    def p_lo(self, name: str):
+        """Device pointer to the tf32 low parts of parameter `name` (None without them)."""
+        return _vp(self.params_lo + 4 * self.offsets[name][0]) if self.params_lo else None
 
     def g(self, name: str) -> int:
         return self.grads + 4 * self.offsets[name][0]
@@ -302,8 +322,8 @@ class VGG11BN:
             gam, bet = _vp(self.p(f"bn{li}.g")), _vp(self.p(f"bn{li}.b"))
             stats = (_vp(b["rm"]), _vp(b["rv"]), _vp(b["a"]), _vp(b["mean"]), _vp(b["invstd"]))
             if nhwc:
-                check(L.tpk_conv2d_fwd_nhwc(_vp(x), w, bias, _vp(b["z"]), Bn, cin, H, W, C, 3, 3, 1, 1,
-                                            self.filter_layout(li)))
+                check(L.tpk_conv2d_fwd_nhwc_lo(_vp(x), w, self.p_lo(f"conv{li}.w"), bias, _vp(b["z"]), Bn, cin, H,
+                                               W, C, 3, 3, 1, 1, self.filter_layout(li)))
                 if b["pool"]:
                     check(L.tpk_bn_train_pool_nhwc(_vp(b["z"]), gam, bet, _vp(b["rm"]), _vp(b["rv"]), _vp(b["p"]),
                                                    _vp(b["idx"]), _vp(b["a"]) if b["a"] else None, _vp(b["mean"]),
@@ -331,7 +351,6 @@ class VGG11BN:
     def _backward(self) -> None:
         L = self.lib
         Bn = self.B
-        nhwc = self.layout == "nhwc"
         check(L.tpk_cross_entropy_backward(_vp(self.logits), _vp(self.y), _vp(self.dlogits), Bn, NUM_CLASSES,
                                            1.0 / Bn))
         check(L.tpk_gemm(_vp(self.dlogits), 1, _vp(self.feat_ptr), 0, _vp(self.g("fc.w")), NUM_CLASSES, self.feat,
@@ -341,13 +360,15 @@ class VGG11BN:
                          None))
         self._reduce("fc")
         gout = self.dfeat
+        if self.overlap:
+            self._backward_blocks_overlapped(gout)
+            return
         buf = 0
         for li in reversed(range(len(self.blocks))):
             b = self.blocks[li]
             C, H, W = b["cout"], b["H"], b["W"]
-            P = Bn * H * W
             cin = self.cin0 if li == 0 else b["cin"]
-            if b["pool"] and not nhwc:
+            if b["pool"]:
                 da = self.gbuf[buf]
                 buf ^= 1
                 check(L.tpk_maxpool_bwd(_vp(gout), _vp(b["idx"]), _vp(da), Bn, C, H, W, 2, 2, 0))
@@ -357,33 +378,67 @@ class VGG11BN:
             buf ^= 1
             xin = self.x0 if li == 0 else self.blocks[li - 1]["out"]
             w, dw, db = _vp(self.p(f"conv{li}.w")), _vp(self.g(f"conv{li}.w")), _vp(self.g(f"conv{li}.b"))
-            if nhwc:
-                # the max-pool backward is read in place (da is the pooled gradient) and the
-                # ReLU mask is recomputed from z; the conv bias gradient (the per-channel sum
-                # of dz) comes out of the same pass
-                check(L.tpk_bn_backward_fused_nhwc(_vp(da), _vp(b["idx"]) if b["pool"] else None, _vp(b["z"]),
-                                                   _vp(self.p(f"bn{li}.g")), _vp(self.p(f"bn{li}.b")),
-                                                   _vp(b["mean"]), _vp(b["invstd"]), _vp(dz),
-                                                   _vp(self.g(f"bn{li}.g")), _vp(self.g(f"bn{li}.b")), db, Bn, H, W,
-                                                   C, 1))
-                check(L.tpk_conv2d_wgrad_nhwc(_vp(dz), _vp(xin), dw, Bn, cin, H, W, C, 3, 3, 1, 1,
-                                              self.filter_layout(li)))
-            else:
-                bn_args = (_vp(da), _vp(b["z"]), _vp(b["a"]), _vp(self.p(f"bn{li}.g")), _vp(b["mean"]),
-                           _vp(b["invstd"]), _vp(dz), _vp(self.g(f"bn{li}.g")), _vp(self.g(f"bn{li}.b")))
-                check(L.tpk_bn_backward(*bn_args, Bn, C, H * W))
-                check(L.tpk_channel_sum(_vp(dz), Bn, C, H * W, db))
-                check(L.tpk_conv2d_wgrad(_vp(dz), _vp(xin), dw, Bn, cin, H, W, C, 3, 3, 1, 1, 1, 1))
+            bn_args = (_vp(da), _vp(b["z"]), _vp(b["a"]), _vp(self.p(f"bn{li}.g")), _vp(b["mean"]),
+                       _vp(b["invstd"]), _vp(dz), _vp(self.g(f"bn{li}.g")), _vp(self.g(f"bn{li}.b")))
+            check(L.tpk_bn_backward(*bn_args, Bn, C, H * W))
+            check(L.tpk_channel_sum(_vp(dz), Bn, C, H * W, db))
+            check(L.tpk_conv2d_wgrad(_vp(dz), _vp(xin), dw, Bn, cin, H, W, C, 3, 3, 1, 1, 1, 1))
             self._reduce(f"blk{li}")
             if li > 0:
                 dx = self.gbuf[buf]
                 buf ^= 1
-                if nhwc:
-                    check(L.tpk_conv2d_dgrad_nhwc(_vp(dz), w, _vp(dx), Bn, cin, H, W, C, 3, 3, 1, 1,
-                                                  self.filter_layout(li)))
-                else:
-                    check(L.tpk_conv2d_dgrad(_vp(dz), w, _vp(dx), Bn, cin, H, W, C, 3, 3, 1, 1, 1, 1))
+                check(L.tpk_conv2d_dgrad(_vp(dz), w, _vp(dx), Bn, cin, H, W, C, 3, 3, 1, 1, 1, 1))
                 gout = dx
+
+    def _backward_blocks_overlapped(self, gout: int) -> None:
+        """Channels-last block backward: BN backward (pool gradient read in
+        place, ReLU mask from z, conv bias gradient from the same pass) and the
+        data gradient on the library stream; each weight gradient, and the
+        gradient all-reduce of the bucket it closes, on the auxiliary stream
+        beside them.  Four gradient buffers in rotation; before the library
+        stream writes a buffer that held dz of layer j, it waits for layer j's
+        weight gradient (event slot j)."""
+        L = self.lib
+        Bn = self.B
+        holder = [None] * len(self.gbuf)  # layer whose weight gradient reads the buffer's dz
+        nxt = [0]
+
+        def take() -> int:
+            i = nxt[0]
+            nxt[0] = (i + 1) % len(self.gbuf)
+            if holder[i] is not None:
+                check(L.tp_main_wait(holder[i]))
+                holder[i] = None
+            return i
+
+        for li in reversed(range(len(self.blocks))):
+            b = self.blocks[li]
+            C, H, W = b["cout"], b["H"], b["W"]
+            cin = self.cin0 if li == 0 else b["cin"]
+            iz = take()
+            dz = self.gbuf[iz]
+            xin = self.x0 if li == 0 else self.blocks[li - 1]["out"]
+            w, dw, db = _vp(self.p(f"conv{li}.w")), _vp(self.g(f"conv{li}.w")), _vp(self.g(f"conv{li}.b"))
+            # gout is the pooled gradient for pooled blocks (read in place with the pool's indices)
+            check(L.tpk_bn_backward_fused_nhwc(_vp(gout), _vp(b["idx"]) if b["pool"] else None, _vp(b["z"]),
+                                               _vp(self.p(f"bn{li}.g")), _vp(self.p(f"bn{li}.b")), _vp(b["mean"]),
+                                               _vp(b["invstd"]), _vp(dz), _vp(self.g(f"bn{li}.g")),
+                                               _vp(self.g(f"bn{li}.b")), db, Bn, H, W, C, 1))
+            check(L.tp_aux_fork())
+            try:
+                check(L.tpk_conv2d_wgrad_nhwc(_vp(dz), _vp(xin), dw, Bn, cin, H, W, C, 3, 3, 1, 1,
+                                              self.filter_layout(li)))
+                self._reduce(f"blk{li}")
+                check(L.tp_aux_record(li))
+            finally:
+                check(L.tp_aux_return())
+            holder[iz] = li
+            if li > 0:
+                dx = self.gbuf[take()]
+                check(L.tpk_conv2d_dgrad_nhwc_lo(_vp(dz), w, self.p_lo(f"conv{li}.w"), _vp(dx), Bn, cin, H, W, C,
+                                                 3, 3, 1, 1, self.filter_layout(li)))
+                gout = dx
+        check(L.tp_aux_join())
 
     def _update(self) -> None:
         if self.comm is not None:
