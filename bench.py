@@ -564,19 +564,20 @@ def run_conv_layer(args):
     check(lib.tp_set_gemm_path(args.gemm_path))
     rt.setSeed(0)
     hx = rt.randn([B, hw, hw, cin], "float32")
-    hw_ = rt.randn([cout, 3, 3, cin], "float32")
+    fl = args.filter_layout
+    hw_ = rt.randn([cout, 3, 3, cin] if fl else [cout, cin, 3, 3], "float32")
     hb = rt.randn([cout], "float32")
     hy = rt.randn([B, hw, hw, cout], "float32")
     hdx = rt.randn([B, hw, hw, cin], "float32")
-    hdw = rt.randn([cout, 3, 3, cin], "float32")
+    hdw = rt.randn([cout, 3, 3, cin], "float32")  # same size in either filter layout
     p = lambda h: ctypes.c_void_p(rt.devicePtr(h["id"]))  # noqa: E731
     x, w, b, y, dx, dw = (p(h) for h in (hx, hw_, hb, hy, hdx, hdw))
     if args.pass_ == "fwd":
-        fn = lambda: lib.tpk_conv2d_fwd_nhwc(x, w, b, y, B, cin, hw, hw, cout, 3, 3, 1, 1, 1)  # noqa: E731
+        fn = lambda: lib.tpk_conv2d_fwd_nhwc(x, w, b, y, B, cin, hw, hw, cout, 3, 3, 1, 1, fl)  # noqa: E731
     elif args.pass_ == "dgrad":
-        fn = lambda: lib.tpk_conv2d_dgrad_nhwc(y, w, dx, B, cin, hw, hw, cout, 3, 3, 1, 1, 1)  # noqa: E731
+        fn = lambda: lib.tpk_conv2d_dgrad_nhwc(y, w, dx, B, cin, hw, hw, cout, 3, 3, 1, 1, fl)  # noqa: E731
     else:
-        fn = lambda: lib.tpk_conv2d_wgrad_nhwc(y, x, dw, B, cin, hw, hw, cout, 3, 3, 1, 1, 1)  # noqa: E731
+        fn = lambda: lib.tpk_conv2d_wgrad_nhwc(y, x, dw, B, cin, hw, hw, cout, 3, 3, 1, 1, fl)  # noqa: E731
     for _ in range(args.warmup):
         check(fn())
     rt.synchronize()
@@ -593,6 +594,7 @@ def run_conv_layer(args):
     peak3, _, peak_kind = tf32x3_peak()
     tf = flops / (ms * 1e-3) / 1e12
     print(json.dumps({"conv": [cin, cout, hw], "pass": args.pass_, "batch": B, "gemm_path": args.gemm_path,
+                      "filter_layout": fl,
                       "ms": round(ms, 4), "TFLOP/s": round(tf, 2), "frac_of_3xtf32": round(tf / peak3, 3),
                       "peak": round(peak3, 1), "peak_source": peak_kind, "status": st.value}), flush=True)
     for h in (hx, hw_, hb, hy, hdx, hdw):
@@ -743,6 +745,9 @@ def main():
     ap.add_argument("--pass", dest="pass_", choices=["fwd", "dgrad", "wgrad"], default="fwd",
                     help="--workload conv: which pass")
     ap.add_argument("--gemm-path", type=int, default=0, help="--workload conv: tp_set_gemm_path value")
+    ap.add_argument("--filter-layout", type=int, default=1,
+                    help="--workload conv: 1 = [Cout][3][3][Cin] (the step's), 0 = [Cout][Cin][3][3] (with Cin = 4: "
+                         "the first layer's CUDA-core kernels)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--launch-list", action="store_true",
                     help="profiling aid: two eager VGG steps at --batch with launch counts (1 GPU, no timing)")

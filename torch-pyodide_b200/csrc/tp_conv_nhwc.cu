@@ -356,6 +356,17 @@ static void conv_wgrad_nhwc(const NhwcShape& s, const float* dy, const float* x,
   if (nhwc_tma_ok() && s.Cout >= 64 && P > 0 && pixel_tiling(s.N, s.OH, s.OW, 32, tl) &&
       nhwc_mn_map(nullptr, dy, s.N, s.OH, s.OW, s.Cout, tl.pt, tc::BM, false) &&
       nhwc_mn_map(nullptr, x, s.N, s.H, s.W, s.Cin, tl.pt, 32, false)) {
+    // 64 input channels: two taps per GEMM (N = 128), the dy tile shared by both
+    if (s.khwc && s.Cin == 64 && khw > 1) {
+      CUtensorMap ma, mb;
+      nhwc_mn_map(&ma, dy, s.N, s.OH, s.OW, s.Cout, tl.pt, tc::BM, true);
+      nhwc_mn_map(&mb, x, s.N, s.H, s.W, s.Cin, tl.pt, 64, true);
+      tma::SrcPixMN sa{tl.pt, s.KW, s.PH, s.PW, 0};
+      tma::SrcPixMN2 sb{tl.pt, s.KW, s.PH, s.PW, khw};
+      gemm_tma_launch<tma::SrcPixMN, tma::SrcPixMN2, EpWgradTap2Khwc, 128, 4>(
+          ma, mb, sa, sb, EpWgradTap2Khwc{dw, s.Cin, khw}, s.Cout, 128, tl.span, (khw + 1) / 2);
+      return;
+    }
     const uint32_t bn = tma_b_rows(s.Cout, s.Cin, tl.span, khw);
     CUtensorMap ma, mb;
     nhwc_mn_map(&ma, dy, s.N, s.OH, s.OW, s.Cout, tl.pt, tc::BM, true);

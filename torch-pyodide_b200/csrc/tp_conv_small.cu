@@ -94,22 +94,24 @@ __global__ void __launch_bounds__(SC_THREADS, 2)
   }
 }
 
-// Weight gradient: thread = (pixel-chunk lane r, input channel ci, 4 output
-// channels); a lane walks OW / R consecutive pixels of each image row with the
-// 3x3 input window in registers, loading one new window column (3 values) and
-// one 16-byte dy vector per pixel.  Rows [row0, row1) per CTA.
-__global__ void __launch_bounds__(SC_THREADS)
+// Weight gradient: thread = (row lane r, input channel ci, 4 output channels).
+// Lane r takes rows row0 + r, row0 + r + R, ... of the CTA's range [row0,
+// row1) and walks each whole output row with the 3x3 input window in
+// registers, loading one new window column (3 values) and one 16-byte dy
+// vector per pixel, 8 pixels' loads issued before their 288 multiply-adds so
+// the loads' latency is covered by the other warps' arithmetic.
+constexpr int C4W_PIX = 8;
+__global__ void __launch_bounds__(SC_THREADS, 2)
     k_conv_c4_wgrad(const float4* __restrict__ dy, const float* __restrict__ x, float* __restrict__ part, int rows,
                     int H, int W, int OH, int OW, int PH, int PW, int Cout, int rows_per_split) {
   extern __shared__ float sh[];  // [R][Cout][4][9]
   const int G = Cout >> 2, R = SC_THREADS / (4 * G);
   const int g = threadIdx.x % G, ci = (threadIdx.x / G) & 3, r = threadIdx.x / (4 * G);
-  const int chunk = OW / R, ow0 = r * chunk;
   const int row0 = blockIdx.x * rows_per_split, row1 = min(row0 + rows_per_split, rows);
   float acc[9][4];
 #pragma unroll
   for (int t = 0; t < 9; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0f;
-  for (int row = row0; row < row1; ++row) {
+  for (int row = row0 + r; row < row1 && r < R; row += R) {
     const int n = row / OH, oh = row - n * OH;
     const float* xr[3];
     bool rok[3];
@@ -124,23 +126,22 @@ __global__ void __launch_bounds__(SC_THREADS)
     for (int kh = 0; kh < 3; ++kh)
 #pragma unroll
       for (int kw = 0; kw < 2; ++kw) {
-        const int iw = ow0 - PW + kw;
+        const int iw = kw - PW;
         win[kh][kw] = (rok[kh] && iw >= 0 && iw < W) ? xr[kh][iw * 4] : 0.0f;
       }
     const float4* dr = dy + (int64_t)row * OW * G + g;
-    // 4 pixels per step with all their loads issued first
-    for (int ow4 = ow0; ow4 < ow0 + chunk; ow4 += 4) {
-      float col[4][3];
-      float4 d[4];
+    for (int ow8 = 0; ow8 < OW; ow8 += C4W_PIX) {
+      float col[C4W_PIX][3];
+      float4 d[C4W_PIX];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int iw = ow4 + q - PW + 2;
+      for (int q = 0; q < C4W_PIX; ++q) {
+        const int iw = ow8 + q - PW + 2;
 #pragma unroll
         for (int kh = 0; kh < 3; ++kh) col[q][kh] = (rok[kh] && iw >= 0 && iw < W) ? xr[kh][iw * 4] : 0.0f;
-        d[q] = dr[(int64_t)(ow4 + q) * G];
+        d[q] = dr[(int64_t)(ow8 + q) * G];
       }
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < C4W_PIX; ++q) {
 #pragma unroll
         for (int kh = 0; kh < 3; ++kh) win[kh][2] = col[q][kh];
 #pragma unroll
@@ -316,7 +317,7 @@ void conv_c4_wgrad(const float* dy, const float* x, float* dw, int64_t N, int64_
   const int64_t rows = N * OH;
   const int per = (int)(Cout * 36);
   const int G = (int)(Cout / 4), R = SC_THREADS / (4 * G);
-  TP_REQUIRE(R >= 1 && OW % (4 * R) == 0, "conv2d weight gradient (4 channels): unsupported width");
+  TP_REQUIRE(R >= 1 && OW % C4W_PIX == 0, "conv2d weight gradient (4 channels): unsupported width");
   int64_t splits = (int64_t)sm_count() * 2;
   if (splits > rows) splits = rows;
   if (splits < 1) splits = 1;

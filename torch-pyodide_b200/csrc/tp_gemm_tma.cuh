@@ -264,6 +264,51 @@ struct SrcPixMN {
   }
 };
 
+// SrcPixMN for the input operand of the two-tap weight gradient (Cin = 64):
+// batch b = taps (2b, 2b + 1); the B tile's 128 rows are the 64 channels shifted
+// by tap 2b (32-row groups 0-1) then by tap 2b + 1 (groups 2-3, 8 KB further),
+// one 64-channel box each.  The odd ninth tap's partner repeats it (its columns
+// are dropped by the epilogue).
+struct SrcPixMN2 {
+  static constexpr bool kMN = true;
+  PixTile pt;
+  int KW, PH, PW, KHW;
+  struct Cur {
+    int n0, th, tw, dh0, dw0, dh1, dw1;
+  };
+  template <int ROWS>
+  __device__ __forceinline__ Cur begin(int b, int64_t, int64_t k0) const {
+    static_assert(ROWS == 128, "two taps of 64 channels");
+    Cur c;
+    int oh0, ow0;
+    pt.origin(k0 >> 5, c.n0, oh0, ow0);
+    c.th = pt.TN > 1 ? 0 : oh0 / pt.TH;
+    c.tw = pt.TN > 1 ? 0 : ow0 / pt.TW;
+    const int t0 = 2 * b, t1 = 2 * b + 1 < KHW ? 2 * b + 1 : 2 * b;
+    c.dh0 = t0 / KW - PH;
+    c.dw0 = t0 - (t0 / KW) * KW - PW;
+    c.dh1 = t1 / KW - PH;
+    c.dw1 = t1 - (t1 / KW) * KW - PW;
+    return c;
+  }
+  __device__ __forceinline__ void issue(const CUtensorMap* map, uint32_t dst, uint64_t* bar, const Cur& c) const {
+    const int ow = c.tw * pt.TW, oh = c.th * pt.TH;
+    load5(dst, map, 0, ow + c.dw0, oh + c.dh0, c.n0, 0, bar);
+    load5(dst + 8192, map, 0, ow + c.dw1, oh + c.dh1, c.n0, 0, bar);
+  }
+  __device__ __forceinline__ void next(Cur& c) const {
+    if (pt.TN > 1) {
+      c.n0 += pt.TN;
+    } else if (++c.tw == pt.tiles_w) {
+      c.tw = 0;
+      if (++c.th == pt.tiles_h) {
+        c.th = 0;
+        ++c.n0;
+      }
+    }
+  }
+};
+
 // MN-major B of the flipped-filter data gradient, read from filters stored
 // [Cout][KH*KW][Cin]: rows = input channels, k = (flipped tap, output channel)
 // with taps outermost, 32 output channels per k-block.  Map dims
