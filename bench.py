@@ -695,6 +695,11 @@ def run_vgg(args, rank, world, local):
     k_ms = g0.elapsed_time(g1) / reps
     achieved = flops / (k_ms * 1e-3) / 1e12
     peak3, bf16, peak_kind = tf32x3_peak()
+    hbm_peak, _ = measured_peaks()
+    sm_mhz_max = float((clk or {}).get("sm_max_mhz") or 1965.0)
+    n_sm = torch.cuda.get_device_properties(local).multi_processor_count
+    cuda_peak = n_sm * 128 * 2 * sm_mhz_max * 1e6 / 1e12
+    sr = model.step_roofline_ms(peak3, cuda_peak, hbm_peak)
 
     if comm is not None:
         comm.sync(60000)
@@ -724,6 +729,13 @@ def run_vgg(args, rank, world, local):
                      "kernel_ms": round(k_ms, 4), "step_tflops": round(model.step_flops() * world / 1e12, 4)},
         "e2e": {"value": round(e2e_value, 1), "unit": "imgs/s", "h2d_bytes_per_step": int(hx.numel() * 4 + hy.numel() * 4),
                 "d2h_bytes_per_step": 4, "path": "tp_memcpy_h2d(pinned batch) + tp_graph_launch(step) + loss readback"},
+        "step_roofline": {"min_ms": round(sr["min_ms"], 4), "frac": round(sr["min_ms"] / ms_step, 4),
+                          "tensor_ms": round(sr["tensor_ms"], 4), "cuda_core_ms": round(sr["cuda_core_ms"], 4),
+                          "hbm_ms": round(sr["hbm_ms"], 4), "hbm_gb": round(sr["hbm_bytes"] / 1e9, 3),
+                          "basis": (f"per-rank step: contractions at the 3xTF32 peak {round(peak3, 1)} TFLOP/s, the "
+                                    f"first layer at the CUDA-core fp32 peak {round(cuda_peak, 1)} TFLOP/s "
+                                    f"({n_sm} SMs x 128 lanes x 2 x max SM clock), BatchNorm / pool / SGD bytes at "
+                                    f"the measured HBM {hbm_peak} GB/s")},
     }
     if world == 1 and not args.no_cpu_baseline:
         os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))

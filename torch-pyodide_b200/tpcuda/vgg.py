@@ -520,6 +520,33 @@ class VGG11BN:
         self._allocs = []
 
     # algorithmic work of one step at this batch (for the roofline)
+    def step_roofline_ms(self, tensor_tflops: float, cuda_tflops: float, hbm_gbs: float) -> dict:
+        """Lower bound of the step's time from its algorithmic work: the
+        tensor-core convolutions (3xTF32 flops of fwd + data gradient + weight
+        gradient) at `tensor_tflops`, the first layer (CUDA cores, 3 real input
+        channels) at `cuda_tflops`, and the HBM-bound passes at `hbm_gbs` --
+        BatchNorm statistics / apply (+ pool) / backward (two passes, the pooled
+        gradient and argmax read in place) and the fused SGD."""
+        tensor = cuda = hbm = 0.0
+        for li, b in enumerate(self.blocks):
+            macs = self.B * b["cout"] * b["H"] * b["W"] * (3 if li == 0 else b["cin"]) * 9
+            if li == 0:
+                cuda += 2 * macs * 2 / (cuda_tflops * 1e12)
+            else:
+                tensor += 2 * macs * 3 / (tensor_tflops * 1e12)
+            e = 4.0 * self.B * b["cout"] * b["H"] * b["W"]  # bytes of one activation tensor
+            if b["pool"]:
+                hbm += e + e * 1.5  # statistics; apply + ReLU + pool (read z, write pooled value and index)
+                hbm += 1.5 * e + 2.5 * e  # backward: sums (z, pooled g, index); apply (same + write dz)
+            else:
+                hbm += e + 2 * e  # statistics; apply + ReLU
+                hbm += 2 * e + 3 * e  # backward: sums (z, g); apply (z, g, write dz)
+        hbm += 24.0 * self.nparams  # SGD: param, grad, momentum read; param, momentum, tf32 low part written
+        hbm_s = hbm / (hbm_gbs * 1e9)
+        total = tensor + cuda + hbm_s
+        return {"min_ms": total * 1e3, "tensor_ms": tensor * 1e3, "cuda_core_ms": cuda * 1e3, "hbm_ms": hbm_s * 1e3,
+                "hbm_bytes": hbm}
+
     def step_flops(self) -> float:
         f = 0.0
         for li, b in enumerate(self.blocks):
