@@ -12,6 +12,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "tp_fastdiv.cuh"
+
 namespace tp {
 
 // Each functor: acc4 / acc1 for one float4 / float at a flat index; load4 +
@@ -106,9 +108,10 @@ struct ChanBnBwdF {
   }
 };
 
+// fs4 / fs: division by S/4 and by S (flat index -> image, position)
 template <class F>
 __global__ void __launch_bounds__(256) k_chan_reduce(F f, int64_t N, int64_t C, int64_t S, int splits,
-                                                     double* __restrict__ part) {
+                                                     double* __restrict__ part, FastDiv fs4, FastDiv fs) {
   __shared__ double sh_a[32], sh_b[32];
   const int64_t c = blockIdx.x;
   const int split = blockIdx.y;
@@ -126,14 +129,14 @@ __global__ void __launch_bounds__(256) k_chan_reduce(F f, int64_t N, int64_t C, 
         typename F::V v[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const uint32_t ii = i + u * step, dn = ii / S4, s4 = ii - dn * S4;
+          const uint32_t ii = i + u * step, dn = fs4.div(ii), s4 = ii - dn * S4;
           v[u] = f.load4(((n0 + dn) * C + c) * (int64_t)S4 + s4);
         }
 #pragma unroll
         for (int u = 0; u < 4; ++u) f.use4(v[u], c, a, b);
       }
       for (; i < cnt; i += step) {
-        uint32_t dn = i / S4, s4 = i - dn * S4;
+        uint32_t dn = fs4.div(i), s4 = i - dn * S4;
         int64_t i4 = ((n0 + dn) * C + c) * (int64_t)S4 + s4;
         f.acc4(i4, c, a, b);
       }
@@ -141,7 +144,7 @@ __global__ void __launch_bounds__(256) k_chan_reduce(F f, int64_t N, int64_t C, 
       const uint32_t Su = (uint32_t)S;
       const uint32_t cnt = (uint32_t)((n1 - n0) * S);
       for (uint32_t i = threadIdx.x; i < cnt; i += blockDim.x) {
-        uint32_t dn = i / Su, s = i - dn * Su;
+        uint32_t dn = fs.div(i), s = i - dn * Su;
         f.acc1(((n0 + dn) * C + c) * S + s, c, a, b);
       }
     }
@@ -166,6 +169,10 @@ __global__ void __launch_bounds__(256) k_chan_reduce(F f, int64_t N, int64_t C, 
     part[(c * splits + split) * 2 + 1] = tb;
   }
 }
+
+// The fast divisors k_chan_reduce takes (the flat counts stay below 2^31).
+inline FastDiv chan_div4(int64_t S) { return fast_div((uint32_t)((S >> 2) > 0 ? (S >> 2) : 1)); }
+inline FastDiv chan_div1(int64_t S) { return fast_div((uint32_t)(S > 0 ? S : 1)); }
 
 // Splits per channel: enough CTAs for a few waves, each with >= ~4K values.
 inline int chan_splits(int64_t C, int64_t N, int64_t S, int sms) {

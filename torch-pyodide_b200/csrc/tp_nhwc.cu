@@ -17,6 +17,7 @@
 #include <cuda_runtime.h>
 
 #include "tp_core.h"
+#include "tp_fastdiv.cuh"
 #include "tp_launch.h"
 
 namespace tp {
@@ -160,22 +161,6 @@ __device__ __forceinline__ void relu_mask_from_x(float4& g, const float4& x, con
   if (!(bn_val(x.y, c.mu[1], c.sc[1], c.bs[1]) > 0.0f)) g.y = 0.0f;
   if (!(bn_val(x.z, c.mu[2], c.sc[2], c.bs[2]) > 0.0f)) g.z = 0.0f;
   if (!(bn_val(x.w, c.mu[3], c.sc[3], c.bs[3]) > 0.0f)) g.w = 0.0f;
-}
-
-// Unsigned division by a runtime constant d for n < 2^31: with l = ceil(log2 d)
-// and m = floor(2^32 (2^l - d) / d) + 1, n / d = (umulhi(n, m) + n) >> l
-// (Granlund & Montgomery, "Division by invariant integers using
-// multiplication", 1994; the sum stays below 2^32 because n < 2^31).
-struct FastDiv {
-  uint32_t d, m, l;
-  __device__ __forceinline__ uint32_t div(uint32_t n) const { return (__umulhi(n, m) + n) >> l; }
-};
-
-static FastDiv fast_div(uint32_t d) {
-  uint32_t l = 0;
-  while (((uint64_t)1 << l) < d) ++l;
-  const uint64_t m = ((uint64_t)1 << 32) * (((uint64_t)1 << l) - d) / d + 1;
-  return {d, (uint32_t)m, l};
 }
 
 // Where the BatchNorm backward takes the gradient g at its output and its

@@ -58,18 +58,19 @@ __global__ void k_bn_finish(const double* __restrict__ part, int64_t C, int spli
   if (rv) rv[c] = (float)(var * M / (M - 1.0) * momentum + (double)rv[c] * (1.0 - momentum));
 }
 
-// y = (x - mean) * invstd * w + b, optionally ReLU'd.
+// y = (x - mean) * invstd * w + b, optionally ReLU'd.  fs4 / fc divide by S/4
+// and by C (flat float4 index -> plane -> channel; N*C*S/4 < 2^31).
 __global__ void k_bn_apply(const float* __restrict__ x, const float* __restrict__ mean,
                            const float* __restrict__ invstd, const float* __restrict__ w, const float* __restrict__ b,
-                           float* __restrict__ y, int64_t N, int64_t C, int64_t S, int relu) {
+                           float* __restrict__ y, int64_t N, int64_t C, int64_t S, int relu, FastDiv fs4, FastDiv fc) {
   int64_t total = N * C * S;
   int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  if ((S & 3) == 0) {
-    int64_t t4 = total >> 2, S4 = S >> 2;
+  if ((S & 3) == 0 && (total >> 2) < ((int64_t)1 << 31)) {
+    int64_t t4 = total >> 2;
     const float4* x4 = reinterpret_cast<const float4*>(x);
     float4* y4 = reinterpret_cast<float4*>(y);
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < t4; i += stride) {
-      int64_t c = (i / S4) % C;
+      const int64_t c = fc.mod(fs4.div((uint32_t)i));
       float mu = mean[c], is = invstd[c], wt = w ? w[c] : 1.0f, bs = b ? b[c] : 0.0f;
       float sc = is * wt;
       float4 v = x4[i];
@@ -112,12 +113,35 @@ __global__ void k_bn_bwd_finish(const double* __restrict__ part, int64_t C, int 
   if (db) db[c] = (float)a;
 }
 
+__device__ __forceinline__ float bn_bwd1(float g, float r, bool has_r, float x, float mu, float is, float k0,
+                                         float k1, float k2) {
+  if (has_r && !(r > 0.0f)) g = 0.0f;
+  const float xh = (x - mu) * is;
+  return k0 * (g - k1 - xh * k2);
+}
+
+// dx = coef0 * (g - coef1 - x_hat * coef2); 16-byte vectors when S % 4 == 0
+// (fs4 / fc: division by S/4 and by C), else one element per step.
 __global__ void k_bn_bwd_apply(const float* __restrict__ dy, const float* __restrict__ x,
                                const float* __restrict__ relu_src, const float* __restrict__ mean,
                                const float* __restrict__ invstd, const float* __restrict__ coef,
-                               float* __restrict__ dx, int64_t N, int64_t C, int64_t S) {
+                               float* __restrict__ dx, int64_t N, int64_t C, int64_t S, FastDiv fs4, FastDiv fc) {
   int64_t total = N * C * S;
   int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  if ((S & 3) == 0 && (total >> 2) < ((int64_t)1 << 31)) {
+    const int64_t t4 = total >> 2;
+    const bool hr = relu_src != nullptr;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < t4; i += stride) {
+      const int64_t c = fc.mod(fs4.div((uint32_t)i));
+      const float4 g = reinterpret_cast<const float4*>(dy)[i], xv = reinterpret_cast<const float4*>(x)[i];
+      const float4 r = hr ? reinterpret_cast<const float4*>(relu_src)[i] : make_float4(1.f, 1.f, 1.f, 1.f);
+      const float mu = mean[c], is = invstd[c], k0 = coef[c * 3], k1 = coef[c * 3 + 1], k2 = coef[c * 3 + 2];
+      reinterpret_cast<float4*>(dx)[i] =
+          make_float4(bn_bwd1(g.x, r.x, hr, xv.x, mu, is, k0, k1, k2), bn_bwd1(g.y, r.y, hr, xv.y, mu, is, k0, k1, k2),
+                      bn_bwd1(g.z, r.z, hr, xv.z, mu, is, k0, k1, k2), bn_bwd1(g.w, r.w, hr, xv.w, mu, is, k0, k1, k2));
+    }
+    return;
+  }
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
     int64_t c = (i / S) % C;
     float g = dy[i];
@@ -135,11 +159,12 @@ void launch_bn_train(const float* x, const float* w, const float* b, float* rm, 
   int splits = chan_splits(C, N, S, sm_count());
   double* part = (double*)scratch((size_t)C * splits * 2 * sizeof(double));
   auto kst = k_chan_reduce<ChanStatsF>;
-  TP_LAUNCH(kst, dim3((unsigned)C, (unsigned)splits), 256, 0, ChanStatsF{x}, N, C, S, splits, part);
+  TP_LAUNCH(kst, dim3((unsigned)C, (unsigned)splits), 256, 0, ChanStatsF{x}, N, C, S, splits, part, chan_div4(S),
+            chan_div1(S));
   TP_LAUNCH(k_bn_finish, (unsigned)((C + 127) / 128), 128, 0, part, C, splits, (double)(N * S), eps, momentum,
             save_mean, save_invstd, rm, rv);
   TP_LAUNCH(k_bn_apply, grid_for(N * C * S, 256, 4), 256, 0, x, save_mean, save_invstd, w, b, y, N, C, S,
-            relu ? 1 : 0);
+            relu ? 1 : 0, chan_div4(S), fast_div((uint32_t)C));
 }
 
 void launch_bn_backward(const float* dy, const float* x, const float* relu_src, const float* w, const float* mean,
@@ -151,10 +176,11 @@ void launch_bn_backward(const float* dy, const float* x, const float* relu_src, 
   float* coef = (float*)(ws + ((pb + 15) & ~(size_t)15));
   auto kbs = k_chan_reduce<ChanBnBwdF>;
   TP_LAUNCH(kbs, dim3((unsigned)C, (unsigned)splits), 256, 0, ChanBnBwdF{dy, x, relu_src, mean, invstd}, N, C, S,
-            splits, part);
+            splits, part, chan_div4(S), chan_div1(S));
   TP_LAUNCH(k_bn_bwd_finish, (unsigned)((C + 127) / 128), 128, 0, part, C, splits, (double)(N * S), w, invstd, coef,
             dw, db);
-  TP_LAUNCH(k_bn_bwd_apply, grid_for(N * C * S, 256), 256, 0, dy, x, relu_src, mean, invstd, coef, dx, N, C, S);
+  TP_LAUNCH(k_bn_bwd_apply, grid_for(N * C * S, 256, 4), 256, 0, dy, x, relu_src, mean, invstd, coef, dx, N, C, S,
+            chan_div4(S), fast_div((uint32_t)C));
 }
 
 // ---- LayerNorm --------------------------------------------------------------------------
@@ -301,23 +327,30 @@ __global__ void k_ln_bwd(const float* __restrict__ dy, const float* __restrict__
 }
 
 // Rows of D <= 256*PER: each thread owns PER columns for all the CTA's rows, so
-// a row's dy and x are read once, and its share of dgamma / dbeta stays in
-// registers until one partial row per CTA is written.
+// a row's dy and x are read once.  gamma and the CTA's dgamma / dbeta partial
+// rows live in shared memory (the thread's own columns: conflict-free), which
+// keeps the registers low enough for several CTAs -- several rows' loads in
+// flight -- per SM; one partial row per CTA is written at the end.
 template <int PER>
 __global__ void __launch_bounds__(256) k_ln_bwd_reg(const float* __restrict__ dy, const float* __restrict__ x,
                                                     const float* __restrict__ g, const float* __restrict__ smean,
                                                     const float* __restrict__ srstd, float* __restrict__ dx,
                                                     float* __restrict__ ws, int64_t rows, int64_t D, int rpb) {
   __shared__ float sh[2][8];
+  extern __shared__ float colsh[];  // gamma [D], dgamma partial [D], dbeta partial [D]
+  float* sgam = colsh;
+  float* spgx = colsh + D;
+  float* spgd = colsh + 2 * D;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int64_t r0 = (int64_t)blockIdx.x * rpb;
-  float gv[PER], pgx[PER], pgd[PER];
 #pragma unroll
   for (int k = 0; k < PER; ++k) {
     const int64_t i = threadIdx.x + (int64_t)k * 256;
-    gv[k] = (i < D) ? (g ? g[i] : 1.0f) : 0.0f;
-    pgx[k] = 0.0f;
-    pgd[k] = 0.0f;
+    if (i < D) {
+      sgam[i] = g ? g[i] : 1.0f;
+      spgx[i] = 0.0f;
+      spgd[i] = 0.0f;
+    }
   }
   const float inv_d = 1.0f / (float)D;
   for (int64_t r = r0; r < r0 + rpb && r < rows; ++r) {
@@ -330,15 +363,19 @@ __global__ void __launch_bounds__(256) k_ln_bwd_reg(const float* __restrict__ dy
     for (int k = 0; k < PER; ++k) {
       const int64_t i = threadIdx.x + (int64_t)k * 256;
       dv[k] = i < D ? dyr[i] : 0.0f;
-      xh[k] = i < D ? (xr[i] - mu) * rs : 0.0f;
+      xh[k] = i < D ? xr[i] : 0.0f;
     }
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
-      const float gd = gv[k] * dv[k];
-      a += gd;
-      bb += gd * xh[k];
-      pgx[k] += dv[k] * xh[k];
-      pgd[k] += dv[k];
+      const int64_t i = threadIdx.x + (int64_t)k * 256;
+      if (i < D) {
+        xh[k] = (xh[k] - mu) * rs;
+        const float gd = sgam[i] * dv[k];
+        a += gd;
+        bb += gd * xh[k];
+        spgx[i] += dv[k] * xh[k];
+        spgd[i] += dv[k];
+      }
     }
     for (int o = 16; o > 0; o >>= 1) {
       a += __shfl_xor_sync(0xffffffffu, a, o);
@@ -359,7 +396,7 @@ __global__ void __launch_bounds__(256) k_ln_bwd_reg(const float* __restrict__ dy
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
       const int64_t i = threadIdx.x + (int64_t)k * 256;
-      if (i < D) dx[r * D + i] = rs * (gv[k] * dv[k] - ta * inv_d - xh[k] * tb * inv_d);
+      if (i < D) dx[r * D + i] = rs * (sgam[i] * dv[k] - ta * inv_d - xh[k] * tb * inv_d);
     }
   }
   if (ws) {
@@ -368,8 +405,8 @@ __global__ void __launch_bounds__(256) k_ln_bwd_reg(const float* __restrict__ dy
     for (int k = 0; k < PER; ++k) {
       const int64_t i = threadIdx.x + (int64_t)k * 256;
       if (i < D) {
-        pg[i] = pgx[k];
-        pg[D + i] = pgd[k];
+        pg[i] = spgx[i];
+        pg[D + i] = spgd[i];
       }
     }
   }
@@ -402,16 +439,28 @@ void launch_ln_fwd(const float* x, const float* g, const float* b, float* y, flo
 void launch_ln_bwd(const float* dy, const float* x, const float* g, const float* sm, const float* sr, float* dx,
                    float* dg, float* db, int64_t rows, int64_t D) {
   if (rows == 0 || D == 0) return;
-  int64_t target = (int64_t)sm_count() * 2;
+  // ~4 CTAs per SM, each a run of rows (the register kernels hold 3 D-float
+  // columns in shared memory: 48 KB at D = 4096)
+  int64_t target = (int64_t)sm_count() * 4;
   int rpb = (int)((rows + target - 1) / target);
   if (rpb < 1) rpb = 1;
   int nblk = (int)((rows + rpb - 1) / rpb);
   float* ws = (dg || db) ? (float*)scratch((size_t)nblk * 2 * D * sizeof(float)) : nullptr;
-  if (D <= 256 * 4) TP_LAUNCH(k_ln_bwd_reg<4>, (unsigned)nblk, 256, 0, dy, x, g, sm, sr, dx, ws, rows, D, rpb);
-  else if (D <= 256 * 8) TP_LAUNCH(k_ln_bwd_reg<8>, (unsigned)nblk, 256, 0, dy, x, g, sm, sr, dx, ws, rows, D, rpb);
-  else if (D <= 256 * 16)
-    TP_LAUNCH(k_ln_bwd_reg<16>, (unsigned)nblk, 256, 0, dy, x, g, sm, sr, dx, ws, rows, D, rpb);
+  const size_t shb = (size_t)3 * D * sizeof(float);
+#define TP_LN_BWD_REG(P)                                                                                  \
+  do {                                                                                                    \
+    static bool attr = false;                                                                             \
+    if (!attr) {                                                                                          \
+      TP_CUDA(cudaFuncSetAttribute(k_ln_bwd_reg<P>, cudaFuncAttributeMaxDynamicSharedMemorySize, 3 * 256 * P * 4)); \
+      attr = true;                                                                                        \
+    }                                                                                                     \
+    TP_LAUNCH(k_ln_bwd_reg<P>, (unsigned)nblk, 256, shb, dy, x, g, sm, sr, dx, ws, rows, D, rpb);          \
+  } while (0)
+  if (D <= 256 * 4) TP_LN_BWD_REG(4);
+  else if (D <= 256 * 8) TP_LN_BWD_REG(8);
+  else if (D <= 256 * 16) TP_LN_BWD_REG(16);
   else TP_LAUNCH(k_ln_bwd, (unsigned)nblk, 256, 0, dy, x, g, sm, sr, dx, ws, rows, D, rpb);
+#undef TP_LN_BWD_REG
   if (ws) TP_LAUNCH(k_colsum_partials, (unsigned)((D + 255) / 256), 256, 0, ws, nblk, D, dg, db);
 }
 
