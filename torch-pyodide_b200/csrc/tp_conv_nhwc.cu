@@ -178,6 +178,42 @@ struct EpPixTile {
   }
 };
 
+// NCHW output [N][C][HW] of a channels-last GEMM (row m = pixel, linear or
+// through pixel tiles): writes the per-op NCHW tensor directly, so no
+// channels-last copy is transposed back.  For a fixed column a warp's lanes
+// hold consecutive pixels, so each store instruction covers a contiguous run.
+struct EpNchwOut {
+  float* y;
+  const float* bias;
+  int64_t C, HW, N;
+  tma::PixTile pt;
+  int linear;
+  __device__ __forceinline__ bool pix(int64_t m, int64_t& img, int64_t& p) const {
+    if (linear) {
+      img = m / HW;
+      p = m - img * HW;
+      return img < N;
+    }
+    int n, oh, ow;
+    if (!pt.pixel(m, 128, N, n, oh, ow)) return false;
+    img = n;
+    p = (int64_t)oh * pt.OW + ow;
+    return true;
+  }
+  __device__ __forceinline__ void operator()(int, int64_t m, int64_t c, float v) const {
+    int64_t img, p;
+    if (pix(m, img, p)) y[(img * C + c) * HW + p] = bias ? v + bias[c] : v;
+  }
+  __device__ __forceinline__ void row16(int, int64_t m, int64_t n0, int64_t Nn, const float (&v)[16]) const {
+    int64_t img, p;
+    if (!pix(m, img, p)) return;
+    float* dst = y + (img * C + n0) * HW + p;
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      if (n0 + i < Nn) dst[(int64_t)i * HW] = bias ? v[i] + bias[n0 + i] : v[i];
+  }
+};
+
 // K-major (im2col) map: dims (C, W, H, N), box (32, TW, TH, TN).
 static bool nhwc_map(CUtensorMap* m, const float* t, int64_t N, int64_t H, int64_t W, int64_t C,
                      const tma::PixTile& pt, bool make) {
@@ -245,15 +281,17 @@ void conv_c4_wgrad(const float* dy, const float* x, float* dw, int64_t N, int64_
 // y[N][OH][OW][Cout] = conv(x[N][H][W][Cin], w) + bias
 // w_lo (optional): the tf32 low parts of w (tf32_lo_plane), kept by the caller
 // beside w; used when the filters are read in place (filter layout 1).
-static void conv_fwd_nhwc(const NhwcShape& s, const float* x, const float* w, const float* bias, float* y,
-                          const float* w_lo = nullptr) {
+// y_nchw (optional): when the TMA path runs, the output goes straight to this
+// NCHW tensor instead of y (returns true); otherwise y gets it (false).
+static bool conv_fwd_nhwc(const NhwcShape& s, const float* x, const float* w, const float* bias, float* y,
+                          const float* w_lo = nullptr, float* y_nchw = nullptr) {
   const int khw = s.KH * s.KW;
   const int64_t M = s.N * s.OH * s.OW, K = s.Cin * khw;
-  if (M == 0) return;
+  if (M == 0) return false;
   if (!s.khwc && conv_c4_ok(s.N, s.H, s.W, s.Cin, s.KH, s.KW, s.Cout, x, y) &&
       (bias == nullptr || ((uintptr_t)bias & 15) == 0)) {
     conv_c4_fwd(x, w, bias, y, s.N, s.H, s.W, s.Cout, s.PH, s.PW);
-    return;
+    return false;
   }
   // K order (kh, kw, c): filters stored that way are used as they are
   const float* wp = w;
@@ -280,21 +318,27 @@ static void conv_fwd_nhwc(const NhwcShape& s, const float* x, const float* w, co
     }
     mat_map(&mbl, MatOp{wlo, false, K, 0, false}, s.Cout, K, 1, brows);
     tma::SrcConvK sa{tl.pt, (int)(s.Cin / 32), s.KW, s.PH, s.PW};
+    if (y_nchw) {
+      EpNchwOut eo{y_nchw, bias, s.Cout, s.OH * s.OW, s.N, tl.pt, tl.linear ? 1 : 0};
+      gemm_tma_bn(ma, mb, sa, tma::SrcK{0}, eo, tl.linear ? M : tl.span, s.Cout, K, 1, &mbl);
+      return true;
+    }
     if (tl.linear) gemm_tma_bn(ma, mb, sa, tma::SrcK{0}, ep, M, s.Cout, K, 1, &mbl);
     else gemm_tma_bn(ma, mb, sa, tma::SrcK{0}, EpPixTile{y, s.Cout, s.N, bias, tl.pt}, tl.span, s.Cout, K, 1, &mbl);
-    return;
+    return false;
   }
   LdNhwcIm2col la{x, s.H, s.W, s.Cin, s.OH, s.OW, s.KW, s.PH, s.PW, M};
   gemm_auto(la, LdRowMajor{wp, K, 0}, ep, M, s.Cout, K, 1);
+  return false;
 }
 
 // dx[N][H][W][Cin] from dy[N][OH][OW][Cout]: the forward convolution of dy
 // with the flipped, transposed filters and padding K-1-P.
-static void conv_dgrad_nhwc(const NhwcShape& s, const float* dy, const float* w, float* dx,
-                            const float* w_lo = nullptr) {
+static bool conv_dgrad_nhwc(const NhwcShape& s, const float* dy, const float* w, float* dx,
+                            const float* w_lo = nullptr, float* dx_nchw = nullptr) {
   const int khw = s.KH * s.KW;
   const int64_t M = s.N * s.H * s.W, K = s.Cout * khw;
-  if (M == 0) return;
+  if (M == 0) return false;
   TP_REQUIRE(s.PH <= s.KH - 1 && s.PW <= s.KW - 1, "conv2d data gradient (channels-last): padding exceeds kernel-1");
   EpRowMajor ep{dx, s.Cin, 0, nullptr, 0};
   const int qh = s.KH - 1 - s.PH, qw = s.KW - 1 - s.PW;
@@ -319,9 +363,14 @@ static void conv_dgrad_nhwc(const NhwcShape& s, const float* dy, const float* w,
     make_map_f32(&mbl, wlo, 4, dims, st, box, true);
     tma::SrcConvK sa{tl.pt, (int)(s.Cout / 32), s.KW, qh, qw};
     tma::SrcFilterMN sb{(int)(s.Cout / 32), khw};
+    if (dx_nchw) {
+      EpNchwOut eo{dx_nchw, nullptr, s.Cin, s.H * s.W, s.N, tl.pt, tl.linear ? 1 : 0};
+      gemm_tma_bn(ma, mb, sa, sb, eo, tl.linear ? M : tl.span, s.Cin, K, 1, &mbl);
+      return true;
+    }
     if (tl.linear) gemm_tma_bn(ma, mb, sa, sb, ep, M, s.Cin, K, 1, &mbl);
     else gemm_tma_bn(ma, mb, sa, sb, EpPixTile{dx, s.Cin, s.N, nullptr, tl.pt}, tl.span, s.Cin, K, 1, &mbl);
-    return;
+    return false;
   }
   float* wp = (float*)scratch2((size_t)s.Cin * K * sizeof(float));
   TP_LAUNCH(k_pack_filters, grid_for(s.Cout * s.Cin * khw, 256), 256, 0, w, wp, s.Cout, s.Cin, khw, s.khwc ? 2 : 1);
@@ -335,13 +384,19 @@ static void conv_dgrad_nhwc(const NhwcShape& s, const float* dy, const float* w,
     tf32_lo_plane(wp, wlo, s.Cin * K);
     mat_map(&mbl, MatOp{wlo, false, K, 0, false}, s.Cin, K, 1, brows);
     tma::SrcConvK sa{tl.pt, (int)(s.Cout / 32), s.KW, qh, qw};
+    if (dx_nchw) {
+      EpNchwOut eo{dx_nchw, nullptr, s.Cin, s.H * s.W, s.N, tl.pt, tl.linear ? 1 : 0};
+      gemm_tma_bn(ma, mb, sa, tma::SrcK{0}, eo, tl.linear ? M : tl.span, s.Cin, K, 1, &mbl);
+      return true;
+    }
     if (tl.linear) gemm_tma_bn(ma, mb, sa, tma::SrcK{0}, ep, M, s.Cin, K, 1, &mbl);
     else gemm_tma_bn(ma, mb, sa, tma::SrcK{0}, EpPixTile{dx, s.Cin, s.N, nullptr, tl.pt}, tl.span, s.Cin, K, 1,
                      &mbl);
-    return;
+    return false;
   }
   LdNhwcIm2col la{dy, s.OH, s.OW, s.Cout, s.H, s.W, s.KW, qh, qw, M};
   gemm_auto(la, LdRowMajor{wp, K, 0}, ep, M, s.Cin, K, 1);
+  return false;
 }
 
 // dw[Cout][Cin][KH][KW] = sum over output pixels of dy x (x shifted by the tap)
@@ -407,8 +462,7 @@ bool conv_fwd_via_nhwc(const ConvShape& s, const float* x, const float* w, const
   float* xn = (float*)dalloc((size_t)s.N * s.H * s.W * s.Cin * 4);
   float* yn = (float*)dalloc((size_t)s.N * s.OH * s.OW * s.Cout * 4);
   transpose_nchw_nhwc(x, xn, s.N, s.Cin, s.H * s.W, true);
-  conv_fwd_nhwc(nhwc_of(s), xn, w, bias, yn);
-  transpose_nchw_nhwc(yn, y, s.N, s.Cout, s.OH * s.OW, false);
+  if (!conv_fwd_nhwc(nhwc_of(s), xn, w, bias, yn, nullptr, y)) transpose_nchw_nhwc(yn, y, s.N, s.Cout, s.OH * s.OW, false);
   dfree(xn);
   dfree(yn);
   return true;
@@ -419,8 +473,7 @@ bool conv_dgrad_via_nhwc(const ConvShape& s, const float* dy, const float* w, fl
   float* dyn = (float*)dalloc((size_t)s.N * s.OH * s.OW * s.Cout * 4);
   float* dxn = (float*)dalloc((size_t)s.N * s.H * s.W * s.Cin * 4);
   transpose_nchw_nhwc(dy, dyn, s.N, s.Cout, s.OH * s.OW, true);
-  conv_dgrad_nhwc(nhwc_of(s), dyn, w, dxn);
-  transpose_nchw_nhwc(dxn, dx, s.N, s.Cin, s.H * s.W, false);
+  if (!conv_dgrad_nhwc(nhwc_of(s), dyn, w, dxn, nullptr, dx)) transpose_nchw_nhwc(dxn, dx, s.N, s.Cin, s.H * s.W, false);
   dfree(dyn);
   dfree(dxn);
   return true;

@@ -607,8 +607,58 @@ __global__ void k_transpose_cs(const float* __restrict__ in, float* __restrict__
   }
 }
 
+// The same with 16-byte accesses on both sides (C % 4 == 0, HW % 4 == 0, both
+// buffers 16-byte aligned): a 32-channel x 64-pixel tile per CTA, read as
+// float4 along the contiguous dimension of `in`, written as float4 along the
+// contiguous dimension of `out` through a padded shared-memory tile.
+// grid (ceil(HW/64), ceil(C/32), N), 256 threads.
+template <bool TO_NHWC>
+__global__ void __launch_bounds__(256) k_transpose_cs4(const float* __restrict__ in, float* __restrict__ out,
+                                                       int64_t C, int64_t HW) {
+  __shared__ float t[32][65];  // [channel][pixel]
+  const int64_t n = blockIdx.z, p0 = (int64_t)blockIdx.x * 64, c0 = (int64_t)blockIdx.y * 32;
+  const float* src = in + n * C * HW;
+  float* dst = out + n * C * HW;
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int e = threadIdx.x + 256 * j;  // 512 float4 per tile
+    if (TO_NHWC) {  // in[c][p]: 32 rows of 16 float4
+      const int c = e >> 4, q = (e & 15) * 4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (c0 + c < C && p0 + q < HW) v = *reinterpret_cast<const float4*>(src + (c0 + c) * HW + p0 + q);
+      t[c][q] = v.x, t[c][q + 1] = v.y, t[c][q + 2] = v.z, t[c][q + 3] = v.w;
+    } else {  // in[p][c]: 64 rows of 8 float4
+      const int p = e >> 3, q = (e & 7) * 4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (p0 + p < HW && c0 + q < C) v = *reinterpret_cast<const float4*>(src + (p0 + p) * C + c0 + q);
+      t[q][p] = v.x, t[q + 1][p] = v.y, t[q + 2][p] = v.z, t[q + 3][p] = v.w;
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int e = threadIdx.x + 256 * j;
+    if (TO_NHWC) {  // out[p][c]: 64 rows of 8 float4
+      const int p = e >> 3, q = (e & 7) * 4;
+      if (p0 + p < HW && c0 + q < C)
+        *reinterpret_cast<float4*>(dst + (p0 + p) * C + c0 + q) = make_float4(t[q][p], t[q + 1][p], t[q + 2][p], t[q + 3][p]);
+    } else {  // out[c][p]: 32 rows of 16 float4
+      const int c = e >> 4, q = (e & 15) * 4;
+      if (c0 + c < C && p0 + q < HW)
+        *reinterpret_cast<float4*>(dst + (c0 + c) * HW + p0 + q) = make_float4(t[c][q], t[c][q + 1], t[c][q + 2], t[c][q + 3]);
+    }
+  }
+}
+
 void transpose_nchw_nhwc(const float* in, float* out, int64_t N, int64_t C, int64_t HW, bool to_nhwc) {
   if (N == 0 || C == 0 || HW == 0) return;
+  if (C % 4 == 0 && HW % 4 == 0 && (((uintptr_t)in | (uintptr_t)out) & 15) == 0 && N <= 65535 &&
+      (C + 31) / 32 <= 65535) {
+    dim3 grid((unsigned)((HW + 63) / 64), (unsigned)((C + 31) / 32), (unsigned)N);
+    if (to_nhwc) TP_LAUNCH(k_transpose_cs4<true>, grid, 256, 0, in, out, C, HW);
+    else TP_LAUNCH(k_transpose_cs4<false>, grid, 256, 0, in, out, C, HW);
+    return;
+  }
   TP_REQUIRE(N <= 65535 && (C + 31) / 32 <= 65535, "layout transpose: tensor too large for the grid");
   dim3 grid((unsigned)((HW + 31) / 32), (unsigned)((C + 31) / 32), (unsigned)N), block(32, 8);
   if (to_nhwc) TP_LAUNCH(k_transpose_cs<true>, grid, block, 0, in, out, C, HW);
