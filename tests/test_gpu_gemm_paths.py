@@ -91,11 +91,15 @@ def test_vgg_conv_shapes(cuda_rt, oracle_rt, path, cin, cout, hw, batch):
 
 
 @pytest.mark.parametrize("xs,ws,st,pd", [([2, 3, 20, 20], [16, 3, 7, 7], 2, 3), ([3, 2, 11, 13], [8, 2, 3, 3], 2, 1),
-                                         ([2, 4, 9, 9], [12, 4, 5, 5], 3, 2)])
+                                         ([2, 4, 9, 9], [12, 4, 5, 5], 3, 2),
+                                         # the network stem at a small batch: all three passes take the
+                                         # space-to-depth route onto the TMA kernels on the default engine
+                                         ([2, 3, 64, 64], [64, 3, 7, 7], 2, 3), ([1, 3, 37, 30], [32, 3, 5, 5], 2, 2)])
 def test_conv_strided_few_channels(cuda_rt, oracle_rt, path, xs, ws, st, pd):
     """Strided convolutions with few input channels (a network stem): forward,
-    data gradient (the phase-decomposed CUDA-core kernel on engine 0) and
-    weight gradient against the oracle."""
+    data gradient and weight gradient against the oracle (stride 2 on the
+    default engine: space-to-depth onto the TMA kernels; other strides: the
+    phase-decomposed CUDA-core data gradient and the gather kernels)."""
     rng = np.random.default_rng(sum(xs) + st)
     cx, ox = both(cuda_rt, oracle_rt, rng.standard_normal(xs))
     cw, ow = both(cuda_rt, oracle_rt, rng.standard_normal(ws) * 0.1)

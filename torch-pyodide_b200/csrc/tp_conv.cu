@@ -110,6 +110,7 @@ static bool tc_ok(int64_t M) { return g_gemm_path != 1 && M >= 64; }
 
 void conv_fwd(const ConvShape& s, const float* x, const float* w, const float* bias, float* y) {
   if (conv_fwd_via_nhwc(s, x, w, bias, y)) return;
+  if (conv_fwd_s2d(s, x, w, bias, y)) return;
   int groups = (int)(s.Cin / s.icpg);
   int khw = s.KH * s.KW;
   int64_t M = s.N * s.OH * s.OW, K = (int64_t)s.icpg * khw;
@@ -130,6 +131,7 @@ void conv_fwd(const ConvShape& s, const float* x, const float* w, const float* b
 
 void conv_dgrad(const ConvShape& s, const float* dy, const float* w, float* dx) {
   if (conv_dgrad_via_nhwc(s, dy, w, dx)) return;
+  if (conv_dgrad_s2d(s, dy, w, dx)) return;
   if (g_gemm_path == 0 && s.icpg == s.Cin &&
       conv_dgrad_smallc(dy, w, dx, s.N, s.Cin, s.H, s.W, s.Cout, s.OH, s.OW, s.KH, s.KW, s.SH, s.PH, s.PW,
                         s.SH == s.SW))
@@ -155,6 +157,7 @@ void conv_dgrad(const ConvShape& s, const float* dy, const float* w, float* dx) 
 
 void conv_wgrad(const ConvShape& s, const float* dy, const float* x, float* dw) {
   if (conv_wgrad_via_nhwc(s, dy, x, dw)) return;
+  if (conv_wgrad_s2d(s, dy, x, dw)) return;
   int khw = s.KH * s.KW;
   int64_t K = s.N * s.OH * s.OW;
   if (tc_ok(s.Cout) && s.icpg == s.Cin && s.Cin >= 32) {

@@ -17,6 +17,7 @@
 #include <cuda_runtime.h>
 
 #include "tp_core.h"
+#include "tp_fastdiv.cuh"
 #include "tp_gemm_dispatch.cuh"
 #include "tp_launch.h"
 
@@ -411,15 +412,21 @@ static void conv_wgrad_nhwc(const NhwcShape& s, const float* dy, const float* x,
   if (nhwc_tma_ok() && s.Cout >= 64 && P > 0 && pixel_tiling(s.N, s.OH, s.OW, 32, tl) &&
       nhwc_mn_map(nullptr, dy, s.N, s.OH, s.OW, s.Cout, tl.pt, tc::BM, false) &&
       nhwc_mn_map(nullptr, x, s.N, s.H, s.W, s.Cin, tl.pt, 32, false)) {
-    // 64 input channels: two taps per GEMM (N = 128), the dy tile shared by both
-    if (s.khwc && s.Cin == 64 && khw > 1) {
+    // 64 / 32 input channels: 2 / 4 taps per GEMM (N = 128), the dy tile shared by them
+    if (s.khwc && (s.Cin == 64 || s.Cin == 32) && khw > 1) {
       CUtensorMap ma, mb;
       nhwc_mn_map(&ma, dy, s.N, s.OH, s.OW, s.Cout, tl.pt, tc::BM, true);
-      nhwc_mn_map(&mb, x, s.N, s.H, s.W, s.Cin, tl.pt, 64, true);
+      nhwc_mn_map(&mb, x, s.N, s.H, s.W, s.Cin, tl.pt, (uint32_t)s.Cin, true);
       tma::SrcPixMN sa{tl.pt, s.KW, s.PH, s.PW, 0};
-      tma::SrcPixMN2 sb{tl.pt, s.KW, s.PH, s.PW, khw};
-      gemm_tma_launch<tma::SrcPixMN, tma::SrcPixMN2, EpWgradTap2Khwc, 128, 4>(
-          ma, mb, sa, sb, EpWgradTap2Khwc{dw, s.Cin, khw}, s.Cout, 128, tl.span, (khw + 1) / 2);
+      if (s.Cin == 64) {
+        tma::SrcPixMNT<2> sb{tl.pt, s.KW, s.PH, s.PW, khw};
+        gemm_tma_launch<tma::SrcPixMN, tma::SrcPixMNT<2>, EpWgradTapsKhwc<2>, 128, 4>(
+            ma, mb, sa, sb, EpWgradTapsKhwc<2>{dw, s.Cin, khw}, s.Cout, 128, tl.span, (khw + 1) / 2);
+      } else {
+        tma::SrcPixMNT<4> sb{tl.pt, s.KW, s.PH, s.PW, khw};
+        gemm_tma_launch<tma::SrcPixMN, tma::SrcPixMNT<4>, EpWgradTapsKhwc<4>, 128, 4>(
+            ma, mb, sa, sb, EpWgradTapsKhwc<4>{dw, s.Cin, khw}, s.Cout, 128, tl.span, (khw + 3) / 4);
+      }
       return;
     }
     const uint32_t bn = tma_b_rows(s.Cout, s.Cin, tl.span, khw);
@@ -488,6 +495,166 @@ bool conv_wgrad_via_nhwc(const ConvShape& s, const float* dy, const float* x, fl
   conv_wgrad_nhwc(nhwc_of(s), dyn, xn, dw);
   dfree(dyn);
   dfree(xn);
+  return true;
+}
+
+// ---- stride-2 convolutions of few channels through space-to-depth ------------------------------
+// A stride-2 KxK convolution of C <= 8 channels equals a stride-1 AxA
+// convolution (A = ((K - 1 + (P & 1)) >> 1) + 1) over the space-to-depth image
+// x'[n][Y][X][(dy*2 + dx)*C + ci] = x[n][ci][2Y + dy - O][2X + dx - O] (O = P
+// rounded up to even, zeros outside), with filters w'[co][a][b][(dy*2+dx)*C+ci]
+// = w[co][ci][2a + dy + P - O][2b + dx + P - O] (zero where that tap does not
+// exist).  x' is padded to 32 channels, so all three passes run on the TMA
+// tensor-core kernels (the 7x7 / 3-channel network stem: K = 16 taps x 32
+// instead of 147 gathered values) and the results map back exactly.
+struct S2d {
+  int C, K, P, O, A;
+  int64_t N, H, W, OH, OW, HY, WX;
+};
+
+static bool s2d_plan(const ConvShape& s, S2d& d) {
+  if (!tma_enabled() || s.SH != 2 || s.SW != 2 || s.KH != s.KW || s.PH != s.PW || s.icpg != s.Cin) return false;
+  if (s.Cin > 8 || s.KH > 8 || s.Cout % 4) return false;
+  d.C = (int)s.Cin;
+  d.K = s.KH;
+  d.P = s.PH;
+  d.O = s.PH + (s.PH & 1);
+  d.A = ((s.KH - 1 + (s.PH & 1)) >> 1) + 1;
+  d.N = s.N;
+  d.H = s.H;
+  d.W = s.W;
+  d.OH = s.OH;
+  d.OW = s.OW;
+  d.HY = s.OH + d.A - 1;
+  d.WX = s.OW + d.A - 1;
+  return d.N * d.HY * d.WX >= 128 && d.N * d.HY * d.WX * 32 < ((int64_t)1 << 31);
+}
+
+// x (NCHW, C channels) -> x' [N][HY][WX][32]; one thread per x' pixel, 8 16-byte stores
+template <int C>
+__global__ void k_s2d_in(const float* __restrict__ x, float* __restrict__ xs, S2d d, FastDiv fwx, FastDiv fhy) {
+  const uint32_t total = (uint32_t)(d.N * d.HY * d.WX);
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const uint32_t t = fwx.div(i), X = i - t * (uint32_t)d.WX;
+    const uint32_t n = fhy.div(t), Y = t - n * (uint32_t)d.HY;
+    float v[32];
+#pragma unroll
+    for (int q = 0; q < 32; ++q) v[q] = 0.0f;
+#pragma unroll
+    for (int ph = 0; ph < 4; ++ph) {
+      const int64_t ih = 2 * (int64_t)Y + (ph >> 1) - d.O, iw = 2 * (int64_t)X + (ph & 1) - d.O;
+      if (ih < 0 || ih >= d.H || iw < 0 || iw >= d.W) continue;
+      const float* src = x + ((int64_t)n * C * d.H + ih) * d.W + iw;
+#pragma unroll
+      for (int ci = 0; ci < C; ++ci) v[ph * C + ci] = src[(int64_t)ci * d.H * d.W];
+    }
+    float4* dst = reinterpret_cast<float4*>(xs + (int64_t)i * 32);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) dst[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+  }
+}
+
+static void s2d_in(const float* x, float* xs, const S2d& d) {
+  const int g = grid_for(d.N * d.HY * d.WX, 256);
+  const FastDiv fwx = fast_div((uint32_t)d.WX), fhy = fast_div((uint32_t)d.HY);
+  switch (d.C) {
+#define TP_S2D_IN(c) \
+  case c: TP_LAUNCH(k_s2d_in<c>, g, 256, 0, x, xs, d, fwx, fhy); break;
+    TP_S2D_IN(1) TP_S2D_IN(2) TP_S2D_IN(3) TP_S2D_IN(4) TP_S2D_IN(5) TP_S2D_IN(6) TP_S2D_IN(7) TP_S2D_IN(8)
+#undef TP_S2D_IN
+    default: TP_REQUIRE(false, "space-to-depth: 1 to 8 channels");
+  }
+}
+// dx' [N][HY][WX][32] -> dx (NCHW): every input pixel has exactly one (Y, dy) / (X, dx)
+__global__ void k_s2d_out(const float* __restrict__ dxs, float* __restrict__ dx, S2d d) {
+  const int64_t total = d.N * d.C * d.H * d.W;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t iw = i % d.W;
+    int64_t t = i / d.W;
+    const int64_t ih = t % d.H;
+    t /= d.H;
+    const int ci = (int)(t % d.C);
+    const int64_t n = t / d.C;
+    const int64_t ry = ih + d.O, rx = iw + d.O;
+    const int64_t Y = ry >> 1, X = rx >> 1;
+    const int q = (int)(((ry & 1) * 2 + (rx & 1)) * d.C + ci);
+    dx[i] = (Y < d.HY && X < d.WX) ? dxs[((n * d.HY + Y) * d.WX + X) * 32 + q] : 0.0f;
+  }
+}
+
+// w [Cout][C][K][K] <-> w' [Cout][A][A][32]; to_s2d = 1 builds w' (zeros where no
+// tap), 0 maps a w'-shaped gradient back onto w's taps.
+__global__ void k_s2d_filters(const float* __restrict__ src, float* __restrict__ dst, int64_t Cout, S2d d,
+                              int to_s2d) {
+  const int64_t total = Cout * d.A * d.A * 32;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int q = (int)(i & 31);
+    int64_t t = i >> 5;
+    const int b = (int)(t % d.A);
+    t /= d.A;
+    const int a = (int)(t % d.A);
+    const int64_t co = t / d.A;
+    int kh = -1, kw = -1, ci = 0;
+    if (q < 4 * d.C) {
+      const int ph = q / d.C;
+      ci = q - ph * d.C;
+      kh = 2 * a + (ph >> 1) + d.P - d.O;
+      kw = 2 * b + (ph & 1) + d.P - d.O;
+    }
+    const bool tap = kh >= 0 && kh < d.K && kw >= 0 && kw < d.K;
+    const int64_t wi = ((co * d.C + ci) * d.K + kh) * d.K + kw;
+    if (to_s2d) dst[i] = tap ? src[wi] : 0.0f;
+    else if (tap) dst[wi] = src[i];
+  }
+}
+
+bool conv_fwd_s2d(const ConvShape& s, const float* x, const float* w, const float* bias, float* y) {
+  S2d d;
+  if (!s2d_plan(s, d) || (bias && ((uintptr_t)bias & 15))) return false;
+  const NhwcShape t = nhwc_shape(d.N, 32, d.HY, d.WX, s.Cout, d.A, d.A, 0, 0, 1);
+  float* xs = (float*)dalloc((size_t)d.N * d.HY * d.WX * 32 * 4);
+  float* ws = (float*)dalloc((size_t)s.Cout * d.A * d.A * 32 * 4);
+  float* yn = (float*)dalloc((size_t)d.N * d.OH * d.OW * s.Cout * 4);
+  s2d_in(x, xs, d);
+  TP_LAUNCH(k_s2d_filters, grid_for(s.Cout * d.A * d.A * 32, 256), 256, 0, w, ws, s.Cout, d, 1);
+  if (!conv_fwd_nhwc(t, xs, ws, bias, yn, nullptr, y)) transpose_nchw_nhwc(yn, y, d.N, s.Cout, d.OH * d.OW, false);
+  dfree(xs);
+  dfree(ws);
+  dfree(yn);
+  return true;
+}
+
+bool conv_dgrad_s2d(const ConvShape& s, const float* dy, const float* w, float* dx) {
+  S2d d;
+  if (!s2d_plan(s, d) || s.Cout % 32) return false;
+  const NhwcShape t = nhwc_shape(d.N, 32, d.HY, d.WX, s.Cout, d.A, d.A, 0, 0, 1);
+  float* dyn = (float*)dalloc((size_t)d.N * d.OH * d.OW * s.Cout * 4);
+  float* ws = (float*)dalloc((size_t)s.Cout * d.A * d.A * 32 * 4);
+  float* dxs = (float*)dalloc((size_t)d.N * d.HY * d.WX * 32 * 4);
+  transpose_nchw_nhwc(dy, dyn, d.N, s.Cout, d.OH * d.OW, true);
+  TP_LAUNCH(k_s2d_filters, grid_for(s.Cout * d.A * d.A * 32, 256), 256, 0, w, ws, s.Cout, d, 1);
+  conv_dgrad_nhwc(t, dyn, ws, dxs);
+  TP_LAUNCH(k_s2d_out, grid_for(d.N * d.C * d.H * d.W, 256), 256, 0, dxs, dx, d);
+  dfree(dyn);
+  dfree(ws);
+  dfree(dxs);
+  return true;
+}
+
+bool conv_wgrad_s2d(const ConvShape& s, const float* dy, const float* x, float* dw) {
+  S2d d;
+  if (!s2d_plan(s, d) || s.Cout % 32 || s.Cout < 64) return false;
+  const NhwcShape t = nhwc_shape(d.N, 32, d.HY, d.WX, s.Cout, d.A, d.A, 0, 0, 1);
+  float* dyn = (float*)dalloc((size_t)d.N * d.OH * d.OW * s.Cout * 4);
+  float* xs = (float*)dalloc((size_t)d.N * d.HY * d.WX * 32 * 4);
+  float* dws = (float*)dalloc((size_t)s.Cout * d.A * d.A * 32 * 4);
+  transpose_nchw_nhwc(dy, dyn, d.N, s.Cout, d.OH * d.OW, true);
+  s2d_in(x, xs, d);
+  conv_wgrad_nhwc(t, dyn, xs, dws);
+  TP_LAUNCH(k_s2d_filters, grid_for(s.Cout * d.A * d.A * 32, 256), 256, 0, dws, dw, s.Cout, d, 0);
+  dfree(dyn);
+  dfree(xs);
+  dfree(dws);
   return true;
 }
 

@@ -434,19 +434,20 @@ struct EpWgradTapKhwc {
   }
 };
 
-// Per-tap weight gradient of two taps at once (Cin = 64): batch b covers taps
-// 2b and 2b + 1, GEMM column n = (n / Cin)-th tap of the pair, channel n % Cin;
-// columns of a tap past KHW (the ninth tap's partner) are dropped.
-struct EpWgradTap2Khwc {
+// Per-tap weight gradient of TAPS taps at once (Cin = 128 / TAPS): batch b
+// covers taps TAPS*b .., GEMM column n = (n / Cin)-th tap of the group, channel
+// n % Cin; columns of a tap past KHW are dropped.
+template <int TAPS>
+struct EpWgradTapsKhwc {
   float* dw;
   int64_t Cin;
   int KHW;
   __device__ __forceinline__ void operator()(int b, int64_t oc, int64_t n, float v) const {
-    const int tap = 2 * b + (int)(n / Cin);
+    const int tap = TAPS * b + (int)(n / Cin);
     if (tap < KHW) dw[(oc * KHW + tap) * Cin + n % Cin] = v;
   }
   __device__ __forceinline__ void row16(int b, int64_t m, int64_t n0, int64_t, const float (&v)[16]) const {
-    const int tap = 2 * b + (int)(n0 / Cin);  // Cin % 16 == 0: the 16 columns share a tap
+    const int tap = TAPS * b + (int)(n0 / Cin);  // Cin % 16 == 0: the 16 columns share a tap
     if (tap >= KHW) return;
     EpRowMajor{dw + (m * KHW + tap) * Cin, 0, 0, nullptr, 0}.row16(0, 0, n0 % Cin, Cin, v);
   }

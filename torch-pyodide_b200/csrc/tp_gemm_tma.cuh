@@ -264,37 +264,41 @@ struct SrcPixMN {
   }
 };
 
-// SrcPixMN for the input operand of the two-tap weight gradient (Cin = 64):
-// batch b = taps (2b, 2b + 1); the B tile's 128 rows are the 64 channels shifted
-// by tap 2b (32-row groups 0-1) then by tap 2b + 1 (groups 2-3, 8 KB further),
-// one 64-channel box each.  The odd ninth tap's partner repeats it (its columns
-// are dropped by the epilogue).
-struct SrcPixMN2 {
+// SrcPixMN for the input operand of a several-tap weight gradient: batch b =
+// taps (TAPS*b .. TAPS*b + TAPS - 1), the B tile's 128 rows are the 128/TAPS
+// input channels shifted by each tap in turn (Cin = 64: 2 taps; Cin = 32: 4),
+// one box of 128/TAPS channels per tap, 4 KB x 32/TAPS... apart.  Taps past KHW
+// repeat the last one (their columns are dropped by the epilogue).
+template <int TAPS>
+struct SrcPixMNT {
   static constexpr bool kMN = true;
+  static constexpr uint32_t kTapBytes = 16384 / TAPS;  // (128 / TAPS) rows of the MN-major tile
   PixTile pt;
   int KW, PH, PW, KHW;
   struct Cur {
-    int n0, th, tw, dh0, dw0, dh1, dw1;
+    int n0, th, tw;
+    int dh[TAPS], dw[TAPS];
   };
   template <int ROWS>
   __device__ __forceinline__ Cur begin(int b, int64_t, int64_t k0) const {
-    static_assert(ROWS == 128, "two taps of 64 channels");
+    static_assert(ROWS == 128, "128-row B tiles");
     Cur c;
     int oh0, ow0;
     pt.origin(k0 >> 5, c.n0, oh0, ow0);
     c.th = pt.TN > 1 ? 0 : oh0 / pt.TH;
     c.tw = pt.TN > 1 ? 0 : ow0 / pt.TW;
-    const int t0 = 2 * b, t1 = 2 * b + 1 < KHW ? 2 * b + 1 : 2 * b;
-    c.dh0 = t0 / KW - PH;
-    c.dw0 = t0 - (t0 / KW) * KW - PW;
-    c.dh1 = t1 / KW - PH;
-    c.dw1 = t1 - (t1 / KW) * KW - PW;
+#pragma unroll
+    for (int j = 0; j < TAPS; ++j) {
+      const int t = TAPS * b + j < KHW ? TAPS * b + j : KHW - 1;
+      c.dh[j] = t / KW - PH;
+      c.dw[j] = t - (t / KW) * KW - PW;
+    }
     return c;
   }
   __device__ __forceinline__ void issue(const CUtensorMap* map, uint32_t dst, uint64_t* bar, const Cur& c) const {
     const int ow = c.tw * pt.TW, oh = c.th * pt.TH;
-    load5(dst, map, 0, ow + c.dw0, oh + c.dh0, c.n0, 0, bar);
-    load5(dst + 8192, map, 0, ow + c.dw1, oh + c.dh1, c.n0, 0, bar);
+#pragma unroll
+    for (int j = 0; j < TAPS; ++j) load5(dst + j * kTapBytes, map, 0, ow + c.dw[j], oh + c.dh[j], c.n0, 0, bar);
   }
   __device__ __forceinline__ void next(Cur& c) const {
     if (pt.TN > 1) {

@@ -60,6 +60,10 @@ void transpose_nchw_nhwc(const float* in, float* out, int64_t N, int64_t C, int6
 bool conv_fwd_via_nhwc(const ConvShape& s, const float* x, const float* w, const float* bias, float* y);
 bool conv_dgrad_via_nhwc(const ConvShape& s, const float* dy, const float* w, float* dx);
 bool conv_wgrad_via_nhwc(const ConvShape& s, const float* dy, const float* x, float* dw);
+// stride-2 convolutions of <= 8 channels through space-to-depth (tp_conv_nhwc.cu)
+bool conv_fwd_s2d(const ConvShape& s, const float* x, const float* w, const float* bias, float* y);
+bool conv_dgrad_s2d(const ConvShape& s, const float* dy, const float* w, float* dx);
+bool conv_wgrad_s2d(const ConvShape& s, const float* dy, const float* x, float* dw);
 
 // tp_conv_small.cu: NCHW data gradient for Cin <= 4 (any stride) on CUDA cores
 bool conv_dgrad_smallc(const float* dy, const float* w, float* dx, int64_t N, int64_t Cin, int64_t H, int64_t W,
