@@ -156,7 +156,7 @@ def cpu_adamw(sample_tensors: int, steps: int) -> dict:
 
 def run_reference(args, rank, world):
     """--impl reference: the reference algorithm on host cores (the WGSL
-    shaders cannot run here: no WebGPU), same metric."""
+    shaders cannot run here: there is no WebGPU device), same metric."""
     if rank != 0:
         return
     cores = os.cpu_count() or 1
@@ -397,8 +397,8 @@ def cpu_vgg(batch: int, steps: int) -> dict:
 
 
 def run_ops(args):
-    """Per-op throughput of the reductions / norms and dense
-    contractions through the reference-facing runtime surface
+    """Per-op throughput of the reductions / norms, the dense contractions and
+    the multi-tensor SGD / Adam steps through the reference-facing runtime surface
     (CudaRuntime, handle API, outputs allocated per call from the pool), each
     against its roofline: HBM for the reductions and norms (algorithmic bytes:
     every input read once, every output written once), the 3xTF32 tensor rate
@@ -442,7 +442,7 @@ def run_ops(args):
                             "frac_of_3xtf32": round(achieved / peak3, 3)})
 
     one = lambda h: [h]  # noqa: E731
-    # ---- configs[2]: reductions and norms ----
+    # ---- reductions and norms ----
     x = rt.randn([16384, 4096], "float32")
     g = rt.full([4096], 1.0, "float32")
     b = rt.full([4096], 0.0, "float32")
@@ -483,7 +483,7 @@ def run_ops(args):
     add("batch_norm bwd", shp, ms, 3 * nb, "hbm")
     for h in (y, mean, inv, x, dy, g, b, rm, rv):
         rt.destroy(h["id"])
-    # ---- configs[3]: dense contractions ----
+    # ---- dense contractions ----
     for n in (512, 2048, 8192):
         a = rt.rand([n, n], "float32")
         bb = rt.rand([n, n], "float32")
@@ -514,11 +514,142 @@ def run_ops(args):
             "tensor")
         for h in (xc, wc, gy):
             rt.destroy(h["id"])
-    print(json.dumps({"metric": "per-op throughput vs roofline (reductions/norms: GB/s of HBM; contractions: "
-                                "TFLOP/s of 3xTF32)", "n_gpus": 1, "reps": reps, "hbm_peak_gbs": hbm,
+    # ---- multi-tensor optimizer steps over the 64-tensor set (402.7 M elements) ----
+    # (AdamW is the default workload's kernel; here the handle-API entries the
+    # reference optimizers call: SGD momentum 0.9 nesterov, and Adam with L2 decay)
+    rt.setSeed(1000)
+    P = [rt.normal(SHAPES[i % 4], "float32", 0.0, 0.02) for i in range(NTENSORS)]
+    G = [rt.normal(SHAPES[i % 4], "float32", 0.0, 1e-3) for i in range(NTENSORS)]
+    S0 = [rt.zeros(SHAPES[i % 4], "float32") for i in range(NTENSORS)]
+    S1 = [rt.zeros(SHAPES[i % 4], "float32") for i in range(NTENSORS)]
+    elems = sum(numel(h["shape"]) for h in P)
+    ids = lambda hs: [h["id"] for h in hs]  # noqa: E731
+
+    def timed_inplace(fn):
+        for _ in range(3):
+            fn()
+        rt.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    ms = timed_inplace(lambda: rt.sgdStepMulti(ids(P), ids(G), ids(S0), 1e-3, 0.9, 0.0, 0.0, True))
+    add("sgd momentum 0.9 nesterov (multi-tensor)", [NTENSORS, elems], ms, 20 * elems, "hbm")
+    ss, isb = adam_scalars(1)
+    ms = timed_inplace(lambda: rt.adamStepMulti(ids(P), ids(G), ids(S0), ids(S1), LR, B1, B2, EPS, WD, ss, isb))
+    add("adam L2 wd (multi-tensor)", [NTENSORS, elems], ms, 28 * elems, "hbm")
+    for h in P + G + S0 + S1:
+        rt.destroy(h["id"])
+    print(json.dumps({"metric": "per-op throughput vs roofline (reductions/norms/optimizers: GB/s of HBM; "
+                                "contractions: TFLOP/s of 3xTF32)", "n_gpus": 1, "reps": reps, "hbm_peak_gbs": hbm,
                       "tf32x3_peak_tflops": round(peak3, 1), "peak_source": f"{peak_kind} bf16 {bf16}",
                       "path": "CudaRuntime handle API (the reference-facing surface), NCHW",
                       "results": results}), flush=True)
+
+
+TINY_TRACE = os.path.join(ROOT, "tests", "golden", "traces", "tiny_cnn.json")
+TRACE_ID_BASE = 1_000_000_000
+
+
+def replay_trace(rt, calls):
+    """Issue a recorded runtime-call stream on ``rt`` (tensor ids remapped).
+
+    Returns (wall time of each training step in s, largest deviation of any
+    ``toList`` result from the recorded one relative to its scale).  A step
+    starts at the bias readback before every second ``conv2d`` (the reference's
+    conv2d takes its bias as a host list) and ends with the loss readback, so
+    each step ends on a host sync and wall time is its duration."""
+    conv = [i for i, c in enumerate(calls) if c["m"] == "conv2d"]
+    starts = [conv[k] - 1 for k in range(0, len(conv), 2)]
+    assert all(calls[i]["m"] == "toList" for i in starts) and calls[-1]["m"] == "toList"
+    ids: dict[int, int] = {}
+
+    def remap(v):
+        if isinstance(v, bool):
+            return v
+        if isinstance(v, int) and v >= TRACE_ID_BASE:
+            return ids[v]
+        if isinstance(v, list):
+            return [remap(x) for x in v]
+        return v
+
+    def learn(rec, res):
+        if isinstance(rec, dict) and "id" in rec:
+            ids[rec["id"]] = res["id"]
+        elif isinstance(rec, list) and rec and isinstance(rec[0], dict):
+            for r, q in zip(rec, res):
+                learn(r, q)
+
+    bounds = set(starts)
+    marks, dev = [], 0.0
+    for i, c in enumerate(calls):
+        if i in bounds:
+            marks.append(time.perf_counter())
+        res = getattr(rt, c["m"])(*remap(c["a"]))
+        if c["m"] == "toList":
+            want = [float(v) for v in c["r"]]
+            if want:
+                scale = max(1.0, max(abs(v) for v in want))
+                dev = max(dev, max(abs(a - float(b)) for a, b in zip(want, res)) / scale)
+        else:
+            learn(c["r"], res)
+    marks.append(time.perf_counter())
+    return [b - a for a, b in zip(marks, marks[1:])], dev
+
+
+def run_tiny(args):
+    """The Tiny-CNN training step (batch 64, 1x28x28 -> conv 1->8 -> pool ->
+    conv 8->16 -> pool -> linear 784->10, Adam) as the reference package issues
+    it: the runtime-call stream the unmodified reference ``torch`` package made
+    for 10 training steps (tests/golden/traces/tiny_cnn.json), replayed on
+    CudaRuntime, the reference-facing surface.  Latency-bound (37 MFLOP per
+    forward): the metric is wall-clock ms per step, host readbacks included
+    (the reference reads the conv bias back each call and the loss each step).
+    The trace is replayed 1 + --steps//10 times (the first untimed); the same
+    replay on the CPU oracle runtime is the CPU baseline."""
+    import torch
+    from tpcuda import CudaRuntime
+    from tpcuda._lib import check
+    import ctypes
+    calls = json.load(open(TINY_TRACE))["calls"]
+    rt = CudaRuntime(0)
+    torch.cuda.set_device(0)
+    reps = max(1, args.steps // 10)
+    for _ in range(max(1, args.warmup // 10)):
+        replay_trace(rt, calls)
+    rt.synchronize()
+    l0 = ctypes.c_int64(0)
+    check(rt.lib.tp_kernel_launches(ctypes.byref(l0)))
+    steps, dev = [], 0.0
+    for _ in range(reps):
+        t, d = replay_trace(rt, calls)
+        steps += t
+        dev = max(dev, d)
+    l1 = ctypes.c_int64(0)
+    check(rt.lib.tp_kernel_launches(ctypes.byref(l1)))
+    ms = statistics.median(steps) * 1e3
+    line = {"metric": "Tiny CNN train step (replayed reference runtime-call stream)", "value": round(ms, 4),
+            "unit": "ms/step", "n_gpus": 1, "steps": len(steps), "warmup": 10 * max(1, args.warmup // 10),
+            "ms_per_step": round(ms, 4), "higher_is_better": False, "scaling": "replicas only",
+            "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded device RNG, as recorded)",
+            "config": {"workload": "Tiny CNN, batch 64, Adam lr 1e-3, 10 recorded steps per replay",
+                       "path": "CudaRuntime handle API, calls as the reference package issued them"},
+            "gpu_launches": int((l1.value - l0.value) / max(1, len(steps))),
+            "max_rel_dev_from_recorded": dev, "bound": "latency (host round trips per step)"}
+    if not args.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        from oracle_runtime import OracleRuntime
+        orc = OracleRuntime()
+        replay_trace(orc, calls)
+        t, _ = replay_trace(orc, calls)
+        line["cpu_baseline"] = {"value": round(statistics.median(t) * 1e3, 4), "unit": "ms/step",
+                                "cores": os.cpu_count(), "kind": "port",
+                                "sample": "the same recorded 10-step stream on the oracle runtime"}
+    print(json.dumps(line), flush=True)
 
 
 def vgg_launch_list(args):
@@ -752,7 +883,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["adamw", "vgg", "ops", "conv"], default="adamw")
+    ap.add_argument("--workload", choices=["adamw", "vgg", "ops", "conv", "tiny"], default="adamw")
     ap.add_argument("--conv", default="256,256,8", help="--workload conv: Cin,Cout,H=W of the layer")
     ap.add_argument("--pass", dest="pass_", choices=["fwd", "dgrad", "wgrad"], default="fwd",
                     help="--workload conv: which pass")
@@ -777,6 +908,9 @@ def main():
         return
     if args.workload == "conv" and args.impl == "ours":
         run_conv_layer(args)
+        return
+    if args.workload == "tiny" and args.impl == "ours":
+        run_tiny(args)
         return
     rank, world, local = dist_setup(args.gpus)
     if args.impl == "reference":

@@ -236,6 +236,14 @@ TP_API int tp_conv2d_bias_backward(int64_t grad_out, int64_t out_ch, const int64
  * 3 = as 0 with single-CTA TMA tiles only; 4 = as 0 with CTA pairs wherever
  * they fit (N > 32, two row tiles; cross-checks of the pair kernel) */
 TP_API int tp_set_gemm_path(int path);
+/* 1 (default; environment TP_PDL=0 turns it off at load) = every kernel is
+ * launched as a programmatic dependent of the kernel before it on its stream:
+ * its CTAs may be scheduled while that kernel's last CTAs drain and wait on the
+ * device for its completion before touching memory, which hides launch latency
+ * between the many short kernels of a training step.  0 = plain stream order.
+ * Results are identical either way.  Applies to launches made (or captured)
+ * after the call. */
+TP_API int tp_set_pdl(int on);
 /* synchronises, then reports the tensor-core kernel's status word: 0 = ok,
  * else the code of a bounded wait that expired; reset != 0 clears it */
 TP_API int tp_gemm_status(int* out, int reset);

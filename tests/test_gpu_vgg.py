@@ -147,3 +147,35 @@ def test_vgg_fused_pool_step_matches_kept_activations(cuda_rt):
     assert res[0][0] == res[1][0]
     for n in res[0][1]:
         assert np.array_equal(res[0][1][n], res[1][1][n]), n
+
+
+@pytest.mark.parametrize("batch", [8, 128])
+def test_vgg_step_same_with_and_without_dependent_launch(cuda_rt, batch):
+    """Programmatic dependent launch only changes when CTAs are scheduled: the
+    graph-replayed step captured with it gives the same bits as the step
+    captured in plain stream order."""
+    from tpcuda._lib import check
+    from tpcuda.vgg import VGG11BN
+    rng = np.random.default_rng(batch)
+    x = rng.standard_normal((batch, 3, 32, 32)).astype(np.float32)
+    y = rng.integers(0, 10, batch).astype(np.float32)
+    res = []
+    try:
+        for pdl in (1, 0):
+            check(cuda_rt.lib.tp_set_pdl(pdl))
+            m = VGG11BN(cuda_rt, batch, seed=4)
+            m._h2d(m.x, x)
+            m._h2d(m.y, y)
+            m.capture()
+            losses = []
+            for _ in range(3):
+                m.step()
+                losses.append(m.read_loss())
+            cuda_rt.synchronize()
+            res.append((losses, {n: m.param_array(n) for n, _, _ in m.param_specs}))
+            m.close()
+    finally:
+        check(cuda_rt.lib.tp_set_pdl(1))
+    assert res[0][0] == res[1][0]
+    for n in res[0][1]:
+        assert np.array_equal(res[0][1][n], res[1][1][n]), n

@@ -42,3 +42,21 @@ def test_oracle_rand_reproduces_recording_directly():
     vals = O.random(6, 42, 0)
     rec = np.asarray(GOLDEN["rand_tensor"]["recorded"]["values"], np.float32).reshape(-1)
     assert np.array_equal(vals, rec)
+
+
+def test_tiny_cnn_trace_replays_on_oracle_in_ten_steps():
+    """bench.py --workload tiny splits the recorded Tiny-CNN stream into its 10
+    training steps; replayed on the oracle it reproduces every recorded
+    readback exactly (the stream was recorded on the oracle)."""
+    import importlib.util
+    import sys
+    root = os.path.dirname(HERE)
+    sys.path.insert(0, os.path.join(root, "oracle"))
+    from oracle_runtime import OracleRuntime
+    spec = importlib.util.spec_from_file_location("bench_mod", os.path.join(root, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    calls = json.load(open(bench.TINY_TRACE))["calls"]
+    times, dev = bench.replay_trace(OracleRuntime(), calls)
+    assert len(times) == 10 and all(t > 0 for t in times)
+    assert dev == 0.0

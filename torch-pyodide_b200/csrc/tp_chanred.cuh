@@ -112,6 +112,7 @@ struct ChanBnBwdF {
 template <class F>
 __global__ void __launch_bounds__(256) k_chan_reduce(F f, int64_t N, int64_t C, int64_t S, int splits,
                                                      double* __restrict__ part, FastDiv fs4, FastDiv fs) {
+  ::tp::pdl_enter();
   __shared__ double sh_a[32], sh_b[32];
   const int64_t c = blockIdx.x;
   const int split = blockIdx.y;

@@ -39,6 +39,7 @@ int tc_status(bool reset) {
 // ---- per-channel sum of an NCHW tensor (conv_backward.wgsl:103-119) ---------------
 __global__ void k_channel_sum_finish(const double* __restrict__ part, int64_t C, int splits,
                                      float* __restrict__ out) {
+  ::tp::pdl_enter();
   int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (c >= C) return;
   double s = 0.0;
@@ -87,6 +88,7 @@ ConvShape conv_shape(int64_t N, int64_t Cin, int64_t H, int64_t W, int64_t Cout,
 //   mode 2 (dgrad):    the same from filters stored w[o][tap][i]
 __global__ void k_pack_filters(const float* __restrict__ w, float* __restrict__ wp, int64_t Cout, int64_t Cin_pg,
                                int khw, int mode) {
+  ::tp::pdl_enter();
   int64_t total = Cout * Cin_pg * khw;
   int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {

@@ -533,6 +533,7 @@ static bool s2d_plan(const ConvShape& s, S2d& d) {
 // x (NCHW, C channels) -> x' [N][HY][WX][32]; one thread per x' pixel, 8 16-byte stores
 template <int C>
 __global__ void k_s2d_in(const float* __restrict__ x, float* __restrict__ xs, S2d d, FastDiv fwx, FastDiv fhy) {
+  ::tp::pdl_enter();
   const uint32_t total = (uint32_t)(d.N * d.HY * d.WX);
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
     const uint32_t t = fwx.div(i), X = i - t * (uint32_t)d.WX;
@@ -567,6 +568,7 @@ static void s2d_in(const float* x, float* xs, const S2d& d) {
 }
 // dx' [N][HY][WX][32] -> dx (NCHW): every input pixel has exactly one (Y, dy) / (X, dx)
 __global__ void k_s2d_out(const float* __restrict__ dxs, float* __restrict__ dx, S2d d) {
+  ::tp::pdl_enter();
   const int64_t total = d.N * d.C * d.H * d.W;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t iw = i % d.W;
@@ -586,6 +588,7 @@ __global__ void k_s2d_out(const float* __restrict__ dxs, float* __restrict__ dx,
 // tap), 0 maps a w'-shaped gradient back onto w's taps.
 __global__ void k_s2d_filters(const float* __restrict__ src, float* __restrict__ dst, int64_t Cout, S2d d,
                               int to_s2d) {
+  ::tp::pdl_enter();
   const int64_t total = Cout * d.A * d.A * 32;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int q = (int)(i & 31);

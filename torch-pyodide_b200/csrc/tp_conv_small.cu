@@ -38,6 +38,7 @@ template <int CH>
 __global__ void __launch_bounds__(SC_THREADS, 2)
     k_conv_c4_fwd(const float4* __restrict__ x, const float* __restrict__ w, const float* __restrict__ bias,
                   float4* __restrict__ y, int rows, int H, int W, int OH, int OW, int PH, int PW, int Cout) {
+  ::tp::pdl_enter();
   extern __shared__ float4 wsm[];  // [tap][ci][G]: (w[4g..4g+3][ci][tap])
   const int G = Cout >> 2;
   for (int i = threadIdx.x; i < 9 * 4 * G; i += blockDim.x) {
@@ -104,6 +105,7 @@ constexpr int C4W_PIX = 8;
 __global__ void __launch_bounds__(SC_THREADS, 2)
     k_conv_c4_wgrad(const float4* __restrict__ dy, const float* __restrict__ x, float* __restrict__ part, int rows,
                     int H, int W, int OH, int OW, int PH, int PW, int Cout, int rows_per_split) {
+  ::tp::pdl_enter();
   extern __shared__ float sh[];  // [R][Cout][4][9]
   const int G = Cout >> 2, R = SC_THREADS / (4 * G);
   const int g = threadIdx.x % G, ci = (threadIdx.x / G) & 3, r = threadIdx.x / (4 * G);
@@ -182,6 +184,7 @@ __global__ void __launch_bounds__(SC_THREADS, 2)
 // sums a contiguous slice of splits for 32 consecutive i, then the slices are
 // added in slice order (deterministic).  i = (co*4 + ci)*9 + tap
 __global__ void k_conv_c4_wgrad_finish(const float* __restrict__ part, int splits, int per, float* __restrict__ dw) {
+  ::tp::pdl_enter();
   __shared__ double sl[8][32];
   const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
   const int i = blockIdx.x * 32 + lane;
@@ -209,6 +212,7 @@ __global__ void k_conv_c4_wgrad_finish(const float* __restrict__ part, int split
 __global__ void __launch_bounds__(256)
     k_conv_dgrad_smallc(const float4* __restrict__ dy, const float* __restrict__ w, float* __restrict__ dx, int N,
                         int Cin, int H, int W, int Cout, int OH, int OW, int KH, int KW, int S, int P) {
+  ::tp::pdl_enter();
   extern __shared__ float4 wt[];  // [kh][kw][co]: (w[co][0..3][kh][kw])
   const int T = KH * KW, G = Cout >> 2;
   for (int i = threadIdx.x; i < T * Cout; i += blockDim.x) {

@@ -7,6 +7,8 @@
 #include <mutex>
 #include <unordered_map>
 
+#include <cstdlib>
+
 #include "tp_core.h"
 
 namespace tp {
@@ -27,6 +29,11 @@ static int64_t g_allocated = 0;
 static void* g_scratch[2] = {nullptr, nullptr};
 static size_t g_scratch_bytes[2] = {0, 0};
 std::atomic<int64_t> g_launches{0};
+static int pdl_default() {
+  const char* e = getenv("TP_PDL");
+  return e && e[0] == '0' ? 0 : 1;
+}
+int g_pdl = pdl_default();
 
 void set_error(const char* msg) { g_err = msg ? msg : ""; }
 
@@ -216,6 +223,7 @@ int64_t emit(const Tensor& t, tp_handle* out) {
 }
 
 __global__ void k_i32_to_f32(const int32_t* in, float* out, int64_t n) {
+  ::tp::pdl_enter();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
     out[i] = (float)in[i];
 }
@@ -292,6 +300,13 @@ TP_API int tp_device_name(char* buf, int len) {
 }
 
 TP_API int tp_kernel_launches(int64_t* out) { return guard([&] { *out = g_launches.load(); }); }
+
+TP_API int tp_set_pdl(int on) {
+  return guard([&] {
+    TP_REQUIRE(on == 0 || on == 1, "tp_set_pdl: 0 (plain stream order) or 1 (programmatic dependent launch)");
+    g_pdl = on;
+  });
+}
 
 TP_API int tp_tensor_from_data(const float* host, const int64_t* shape, int ndim, int dtype, tp_handle* out) {
   return guard([&] {

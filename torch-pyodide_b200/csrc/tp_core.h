@@ -16,6 +16,7 @@
 #include <cstdio>
 #include <stdexcept>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "../../include/tpcuda.h"
@@ -120,12 +121,47 @@ void* scratch3(size_t bytes);
 
 namespace tp {
 extern std::atomic<int64_t> g_launches;
+// 1: kernels are launched as programmatic dependents of their stream
+// predecessor (set by tp_set_pdl, default from TP_PDL, on unless "0").
+extern int g_pdl;
+
+// Programmatic dependent launch.  A kernel launched with
+// programmaticStreamSerializationAllowed may be scheduled once every CTA of the
+// kernel before it in the stream has executed pdl_trigger() (or exited), so its
+// launch and prologue overlap that kernel's last CTAs.  Every kernel of this
+// library therefore starts with pdl_wait(), which returns once the predecessor
+// grid has completed and its memory is visible: no global access precedes it.
+// Kernels that allocate tensor memory trigger only after the allocation, so a
+// CTA that waits never holds TMEM a running CTA might need, and a dependent grid
+// only starts when all CTAs of its predecessor are resident: neither can block
+// the kernel it waits for.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_enter() {
+  pdl_wait();
+  pdl_trigger();
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_on(cudaStream_t st, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                             Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = g_pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 }  // namespace tp
 
 // Launch a kernel on the library stream, count it and check the launch.
-#define TP_LAUNCH(kernel, grid, block, smem, ...)                          \
-  do {                                                                     \
-    kernel<<<(grid), (block), (smem), ::tp::stream()>>>(__VA_ARGS__);      \
-    ::tp::g_launches++;                                                    \
-    TP_LAUNCH_CHECK();                                                     \
+#define TP_LAUNCH(kernel, grid, block, smem, ...)                                              \
+  do {                                                                                         \
+    TP_CUDA(::tp::launch_on(::tp::stream(), kernel, dim3(grid), dim3(block), (smem), __VA_ARGS__)); \
+    ::tp::g_launches++;                                                                        \
   } while (0)

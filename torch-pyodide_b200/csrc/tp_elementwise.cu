@@ -73,6 +73,7 @@ __device__ __forceinline__ float unop(int op, float x) {
 // ---- kernels ----------------------------------------------------------------
 
 __global__ void k_fill(float* __restrict__ out, int64_t n, float v) {
+  ::tp::pdl_enter();
   int64_t n4 = n >> 2;
   float4 v4 = make_float4(v, v, v, v);
   float4* o4 = reinterpret_cast<float4*>(out);
@@ -91,6 +92,7 @@ __device__ __forceinline__ uint32_t xorshift32(uint32_t x) {
 __device__ __forceinline__ float u32_to_unit(uint32_t x) { return __fmul_rn(__uint2float_rn(x), 2.3283064365386963e-10f); }
 
 __global__ void k_random(float* __restrict__ out, int64_t n, uint32_t seed, int kind, float p0, float p1) {
+  ::tp::pdl_enter();
   int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride) {
     uint32_t idx = (uint32_t)i;
@@ -117,6 +119,7 @@ __global__ void k_random(float* __restrict__ out, int64_t n, uint32_t seed, int 
 
 __global__ void k_binary_same(int op, const float* __restrict__ a, const float* __restrict__ b,
                               float* __restrict__ out, int64_t n) {
+  ::tp::pdl_enter();
   int64_t n4 = n >> 2;
   int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const float4* a4 = reinterpret_cast<const float4*>(a);
@@ -140,6 +143,7 @@ struct BcastGeom {
 
 __global__ void k_binary_bcast(int op, const float* __restrict__ a, const float* __restrict__ b,
                                float* __restrict__ out, int64_t n, BcastGeom g) {
+  ::tp::pdl_enter();
   int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride) {
     int64_t rem = i, ia = 0, ib = 0;
@@ -154,6 +158,7 @@ __global__ void k_binary_bcast(int op, const float* __restrict__ a, const float*
 }
 
 __global__ void k_unary(int op, const float* __restrict__ in, float* __restrict__ out, int64_t n) {
+  ::tp::pdl_enter();
   int64_t n4 = n >> 2;
   int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const float4* i4 = reinterpret_cast<const float4*>(in);
@@ -167,12 +172,14 @@ __global__ void k_unary(int op, const float* __restrict__ in, float* __restrict_
 }
 
 __global__ void k_mul_scalar(const float* __restrict__ in, float v, float* __restrict__ out, int64_t n) {
+  ::tp::pdl_enter();
   int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride) out[i] = __fmul_rn(in[i], v);
 }
 
 // Generic strided gather: out[i] = in[sum coord_d * s_d] (expand, permute).
 __global__ void k_gather(const float* __restrict__ in, float* __restrict__ out, int64_t n, BcastGeom g) {
+  ::tp::pdl_enter();
   int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride) {
     int64_t rem = i, src = 0;
@@ -187,6 +194,7 @@ __global__ void k_gather(const float* __restrict__ in, float* __restrict__ out, 
 
 // 32x32 shared-memory tile transpose (transpose.wgsl semantics, coalesced).
 __global__ void k_transpose2d(const float* __restrict__ in, float* __restrict__ out, int64_t rows, int64_t cols) {
+  ::tp::pdl_enter();
   __shared__ float tile[32][33];
   int64_t r0 = (int64_t)blockIdx.y * 32, c0 = (int64_t)blockIdx.x * 32;
   for (int j = threadIdx.y; j < 32; j += blockDim.y) {

@@ -51,6 +51,7 @@ __device__ __forceinline__ void sg_stash(float (*S)[ROWS + SG_PAD], const float 
 template <class LA, class LB, class EP>
 __global__ void __launch_bounds__(256) k_gemm_simt(LA la, LB lb, EP ep, int64_t M, int64_t N, int64_t K,
                                                    int64_t k_per_split, int splitk, float* __restrict__ ws) {
+  ::tp::pdl_enter();
   __shared__ __align__(16) float As[2][SG_BK][SG_BM + SG_PAD];
   __shared__ __align__(16) float Bs[2][SG_BK][SG_BN + SG_PAD];
   int tid = threadIdx.x, tx = tid % 16, ty = tid / 16;
@@ -113,6 +114,7 @@ __global__ void __launch_bounds__(256) k_gemm_simt(LA la, LB lb, EP ep, int64_t 
 
 template <class EP>
 __global__ void k_splitk_reduce(const float* __restrict__ ws, int splits, int64_t M, int64_t N, int b, EP ep) {
+  ::tp::pdl_enter();
   int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < M * N; i += stride) {
     float s = 0.0f;
@@ -173,6 +175,7 @@ constexpr int SK_S = 16, SK_KC = 32, SK_THREADS = 128;
 template <class LS, class LL, class EP, bool SMALL_IS_M>
 __global__ void __launch_bounds__(SK_THREADS) k_gemm_skinny(LS ls, LL ll, EP ep, int64_t M, int64_t N, int64_t K,
                                                             int64_t k_per_split, int splitk, float* __restrict__ ws) {
+  ::tp::pdl_enter();
   __shared__ float sm[SK_KC][SK_S];
   const int64_t S = SMALL_IS_M ? M : N, L = SMALL_IS_M ? N : M;
   const int64_t l = (int64_t)blockIdx.x * SK_THREADS + threadIdx.x;

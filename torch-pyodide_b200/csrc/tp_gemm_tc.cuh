@@ -259,6 +259,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     mbar_init(done, 1);
     fence_barrier_init();
   }
+  // the predecessor kernel has finished before this CTA allocates tensor memory
+  // or touches global memory; dependents may launch once all CTAs hold theirs
+  ::tp::pdl_wait();
   if (warp == MMA_WARP) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"((uint32_t)S::TMEM_COLS));
@@ -266,6 +269,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   }
   tc_fence_before();
   __syncthreads();
+  ::tp::pdl_trigger();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   bool ok = true;
@@ -372,6 +376,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 // (16-byte partial loads when N % 4 == 0).
 template <class EP>
 __global__ void k_splitk_reduce_b(const float* __restrict__ ws, int splits, int64_t M, int64_t N, EP ep) {
+  ::tp::pdl_enter();
   const int b = blockIdx.y;
   const int64_t MN = M * N;
   const float* base = ws + (int64_t)b * splits * MN;

@@ -155,6 +155,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
     tc::mbar_init(done, 1);
     tc::fence_barrier_init();
   }
+  // the predecessor kernel has finished before this CTA allocates tensor memory
+  // or touches global memory; dependents may launch once all CTAs hold theirs
+  ::tp::pdl_wait();
   if (warp == MMA_WARP) {
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      tc::smem_u32(tmem_slot)),
@@ -164,6 +167,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
   tc::tc_fence_before();
   __syncthreads();
   cluster_sync();  // both CTAs' barriers are initialised before any remote arrive
+  ::tp::pdl_trigger();
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   bool ok = true;

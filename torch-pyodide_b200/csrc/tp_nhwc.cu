@@ -45,6 +45,7 @@ __device__ __forceinline__ void warp_part_sum(const double* __restrict__ part, i
 __global__ void k_col_bn_finish(const double* __restrict__ part, int64_t C, int splits, double M, float eps,
                                 float momentum, float* __restrict__ save_mean, float* __restrict__ save_invstd,
                                 float* __restrict__ rm, float* __restrict__ rv) {
+  ::tp::pdl_enter();
   const int64_t c = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (c >= C) return;
   double s, q;
@@ -63,6 +64,7 @@ __global__ void k_col_bn_finish(const double* __restrict__ part, int64_t C, int 
 __global__ void k_col_bn_bwd_finish(const double* __restrict__ part, int64_t C, int splits, double M,
                                     const float* __restrict__ w, const float* __restrict__ invstd,
                                     float* __restrict__ coef, float* __restrict__ dw, float* __restrict__ db) {
+  ::tp::pdl_enter();
   const int64_t c = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (c >= C) return;
   double a, b;
@@ -76,6 +78,7 @@ __global__ void k_col_bn_bwd_finish(const double* __restrict__ part, int64_t C, 
 }
 
 __global__ void k_col_sum_finish(const double* __restrict__ part, int64_t C, int splits, float* __restrict__ out) {
+  ::tp::pdl_enter();
   const int64_t c = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (c >= C) return;
   double a, b;
@@ -306,6 +309,7 @@ constexpr int COL_THREADS = 256;
 template <class F>
 __global__ void __launch_bounds__(COL_THREADS, F::kMinBlocks) k_col_reduce(F f, int64_t P, int C, int CB, int64_t rows_per_split,
                                                             int splits, double* __restrict__ part) {
+  ::tp::pdl_enter();
   extern __shared__ double sh[];  // [R][CB][2]
   const int GB = CB >> 2, R = COL_THREADS / GB;
   const int t = threadIdx.x, g = t % GB, r = t / GB;
@@ -402,6 +406,7 @@ __device__ __forceinline__ float4 bn_apply4(float4 v, const float (&mu)[4], cons
 __global__ void k_bn_apply_nhwc(const float4* __restrict__ x, const float* __restrict__ mean,
                                 const float* __restrict__ invstd, const float* __restrict__ w,
                                 const float* __restrict__ b, float4* __restrict__ y, int64_t n4, int G, int relu) {
+  ::tp::pdl_enter();
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (stride % G == 0) {
@@ -490,6 +495,7 @@ __device__ __forceinline__ void bn_params4(int c, const float* mean, const float
 __global__ void __launch_bounds__(256) k_bn_pool_nhwc(PoolFwd f, const float* __restrict__ mean,
                                                       const float* __restrict__ invstd, const float* __restrict__ w,
                                                       const float* __restrict__ b, int64_t n4) {
+  ::tp::pdl_enter();
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   float mu[4], sc[4], bs[4];
@@ -511,6 +517,7 @@ __global__ void __launch_bounds__(256) k_bn_pool_nhwc(PoolFwd f, const float* __
 // window row-major with strict >.
 __global__ void k_maxpool2x2_nhwc_fwd(const float4* __restrict__ x, float4* __restrict__ y, int4* __restrict__ idx,
                                       int64_t n4, int H, int W, int G) {
+  ::tp::pdl_enter();
   const int OH = H >> 1, OW = W >> 1;
   int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
@@ -543,6 +550,7 @@ __global__ void k_maxpool2x2_nhwc_fwd(const float4* __restrict__ x, float4* __re
 
 __global__ void k_maxpool2x2_nhwc_bwd(const float4* __restrict__ gy, const int4* __restrict__ idx,
                                       float4* __restrict__ gx, int64_t n4, int H, int W, int G) {
+  ::tp::pdl_enter();
   const int OH = H >> 1, OW = W >> 1;
   int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
@@ -569,6 +577,7 @@ __global__ void k_maxpool2x2_nhwc_bwd(const float4* __restrict__ gy, const int4*
 // NCHW [N][C][H][W] -> channels-last [N][H][W][Cp], channels C..Cp-1 zero.
 __global__ void k_nchw_to_nhwc(const float* __restrict__ x, float* __restrict__ y, int64_t N, int C, int64_t HW,
                                int Cp) {
+  ::tp::pdl_enter();
   int64_t total = N * HW * Cp;
   int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
@@ -582,6 +591,7 @@ __global__ void k_nchw_to_nhwc(const float* __restrict__ x, float* __restrict__ 
 // coalesced).  grid (ceil(HW/32), ceil(C/32), N), block (32, 8).
 template <bool TO_NHWC>
 __global__ void k_transpose_cs(const float* __restrict__ in, float* __restrict__ out, int64_t C, int64_t HW) {
+  ::tp::pdl_enter();
   __shared__ float t[32][33];
   const int64_t n = blockIdx.z, p0 = (int64_t)blockIdx.x * 32, c0 = (int64_t)blockIdx.y * 32;
   const float* src = in + n * C * HW;
@@ -615,6 +625,7 @@ __global__ void k_transpose_cs(const float* __restrict__ in, float* __restrict__
 template <bool TO_NHWC>
 __global__ void __launch_bounds__(256) k_transpose_cs4(const float* __restrict__ in, float* __restrict__ out,
                                                        int64_t C, int64_t HW) {
+  ::tp::pdl_enter();
   __shared__ float t[32][65];  // [channel][pixel]
   const int64_t n = blockIdx.z, p0 = (int64_t)blockIdx.x * 64, c0 = (int64_t)blockIdx.y * 32;
   const float* src = in + n * C * HW;

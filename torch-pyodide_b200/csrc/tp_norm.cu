@@ -27,6 +27,7 @@ namespace tp {
 __global__ void k_bn_eval(const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ b,
                           const float* __restrict__ rm, const float* __restrict__ rv, float* __restrict__ y,
                           int64_t total, int64_t C, int64_t S, float eps) {
+  ::tp::pdl_enter();
   int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
     int64_t c = (i / S) % C;
@@ -42,6 +43,7 @@ __global__ void k_bn_eval(const float* __restrict__ x, const float* __restrict__
 __global__ void k_bn_finish(const double* __restrict__ part, int64_t C, int splits, double M, float eps,
                             float momentum, float* __restrict__ save_mean, float* __restrict__ save_invstd,
                             float* __restrict__ rm, float* __restrict__ rv) {
+  ::tp::pdl_enter();
   int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (c >= C) return;
   double s = 0.0, q = 0.0;
@@ -63,6 +65,7 @@ __global__ void k_bn_finish(const double* __restrict__ part, int64_t C, int spli
 __global__ void k_bn_apply(const float* __restrict__ x, const float* __restrict__ mean,
                            const float* __restrict__ invstd, const float* __restrict__ w, const float* __restrict__ b,
                            float* __restrict__ y, int64_t N, int64_t C, int64_t S, int relu, FastDiv fs4, FastDiv fc) {
+  ::tp::pdl_enter();
   int64_t total = N * C * S;
   int64_t stride = (int64_t)gridDim.x * blockDim.x;
   if ((S & 3) == 0 && (total >> 2) < ((int64_t)1 << 31)) {
@@ -99,6 +102,7 @@ __global__ void k_bn_apply(const float* __restrict__ x, const float* __restrict_
 __global__ void k_bn_bwd_finish(const double* __restrict__ part, int64_t C, int splits, double M,
                                 const float* __restrict__ w, const float* __restrict__ invstd,
                                 float* __restrict__ coef, float* __restrict__ dw, float* __restrict__ db) {
+  ::tp::pdl_enter();
   int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (c >= C) return;
   double a = 0.0, b = 0.0;
@@ -126,6 +130,7 @@ __global__ void k_bn_bwd_apply(const float* __restrict__ dy, const float* __rest
                                const float* __restrict__ relu_src, const float* __restrict__ mean,
                                const float* __restrict__ invstd, const float* __restrict__ coef,
                                float* __restrict__ dx, int64_t N, int64_t C, int64_t S, FastDiv fs4, FastDiv fc) {
+  ::tp::pdl_enter();
   int64_t total = N * C * S;
   int64_t stride = (int64_t)gridDim.x * blockDim.x;
   if ((S & 3) == 0 && (total >> 2) < ((int64_t)1 << 31)) {
@@ -190,6 +195,7 @@ __global__ void __launch_bounds__(256) k_ln_fwd(const float* __restrict__ x, con
                                                 const float* __restrict__ b, float* __restrict__ y,
                                                 float* __restrict__ smean, float* __restrict__ srstd, int64_t D,
                                                 float eps) {
+  ::tp::pdl_enter();
   __shared__ float sh[32];
   const float* xr = x + (int64_t)blockIdx.x * D;
   float* yr = y + (int64_t)blockIdx.x * D;
@@ -242,6 +248,7 @@ __global__ void __launch_bounds__(256) k_ln_fwd(const float* __restrict__ x, con
 __global__ void k_ln_fwd_long(const float* __restrict__ x, const float* __restrict__ g,
                               const float* __restrict__ b, float* __restrict__ y, float* __restrict__ smean,
                               float* __restrict__ srstd, int64_t D, float eps) {
+  ::tp::pdl_enter();
   __shared__ float sh[32];
   const float* xr = x + (int64_t)blockIdx.x * D;
   float* yr = y + (int64_t)blockIdx.x * D;
@@ -279,6 +286,7 @@ __global__ void k_ln_fwd_long(const float* __restrict__ x, const float* __restri
 __global__ void k_ln_bwd(const float* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ g,
                          const float* __restrict__ smean, const float* __restrict__ srstd, float* __restrict__ dx,
                          float* __restrict__ ws, int64_t rows, int64_t D, int rpb) {
+  ::tp::pdl_enter();
   __shared__ float sh[2][32];
   int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
   int64_t r0 = (int64_t)blockIdx.x * rpb;
@@ -336,6 +344,7 @@ __global__ void __launch_bounds__(256) k_ln_bwd_reg(const float* __restrict__ dy
                                                     const float* __restrict__ g, const float* __restrict__ smean,
                                                     const float* __restrict__ srstd, float* __restrict__ dx,
                                                     float* __restrict__ ws, int64_t rows, int64_t D, int rpb) {
+  ::tp::pdl_enter();
   __shared__ float sh[2][8];
   extern __shared__ float colsh[];  // gamma [D], dgamma partial [D], dbeta partial [D]
   float* sgam = colsh;
@@ -414,6 +423,7 @@ __global__ void __launch_bounds__(256) k_ln_bwd_reg(const float* __restrict__ dy
 
 __global__ void k_colsum_partials(const float* __restrict__ ws, int nblk, int64_t D, float* __restrict__ dg,
                                   float* __restrict__ db) {
+  ::tp::pdl_enter();
   int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (i >= D) return;
   float sg = 0.0f, sb = 0.0f;

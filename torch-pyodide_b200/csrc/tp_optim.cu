@@ -60,6 +60,7 @@ __device__ __forceinline__ void adam_elem(float& p, float g, float& m, float& v,
 template <bool ADAMW>
 __global__ void __launch_bounds__(256) k_adam_multi(const OptRow* __restrict__ rows, const OptChunk* __restrict__ chunks,
                                                     int nchunks, AdamHP h) {
+  ::tp::pdl_enter();
   for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
     OptChunk ch = chunks[c];
     OptRow r = rows[ch.row];
@@ -134,6 +135,7 @@ __device__ __forceinline__ float4 tf32_lo4(float4 v) {
 
 __global__ void __launch_bounds__(256) k_sgd_multi(const OptRow* __restrict__ rows, const OptChunk* __restrict__ chunks,
                                                    int nchunks, SgdHP h) {
+  ::tp::pdl_enter();
   for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
     OptChunk ch = chunks[c];
     OptRow r = rows[ch.row];

@@ -14,6 +14,7 @@ namespace tp {
 
 __global__ void k_maxpool_fwd(const float* __restrict__ x, float* __restrict__ y, int32_t* __restrict__ idx,
                               PoolGeom g, int64_t total) {
+  ::tp::pdl_enter();
   int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
     int64_t ow = i % g.OW, oh = (i / g.OW) % g.OH, bc = i / (g.OW * g.OH);
@@ -43,6 +44,7 @@ __global__ void k_maxpool_fwd(const float* __restrict__ x, float* __restrict__ y
 // oracle accumulates in), so overlapping windows sum identically.
 __global__ void k_maxpool_bwd(const float* __restrict__ gy, const int32_t* __restrict__ idx, float* __restrict__ gx,
                               PoolGeom g, int64_t total) {
+  ::tp::pdl_enter();
   int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
     int64_t iw = i % g.W, ih = (i / g.W) % g.H, bc = i / (g.W * g.H);
@@ -102,6 +104,7 @@ static PoolGeom pool_geom(const Tensor& x, const int64_t* k, int nk, const int64
 // Same visiting order and strict > as the general kernel.
 __global__ void k_maxpool2x2_fwd(const float* __restrict__ x, float* __restrict__ y, int32_t* __restrict__ idx,
                                  int64_t planes, int H, int W) {
+  ::tp::pdl_enter();
   const int OH = H >> 1, OW = W >> 1;
   const int64_t total = planes * OH * OW;
   int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -127,6 +130,7 @@ __global__ void k_maxpool2x2_fwd(const float* __restrict__ x, float* __restrict_
 
 __global__ void k_maxpool2x2_bwd(const float* __restrict__ gy, const int32_t* __restrict__ idx,
                                  float* __restrict__ gx, int64_t planes, int H, int W) {
+  ::tp::pdl_enter();
   const int OH = H >> 1, OW = W >> 1;
   const int64_t total = planes * OH * OW;
   int64_t stride = (int64_t)gridDim.x * blockDim.x;

@@ -69,6 +69,7 @@ __device__ float block_reduce(float v, float* sh) {
 // ws layout: [RED_MAX_BLOCKS partial floats][uint32 ticket]
 __global__ void k_reduce_all(const float* __restrict__ x, int64_t n, int mode, float* __restrict__ out,
                              float* __restrict__ partials, unsigned int* __restrict__ ticket) {
+  ::tp::pdl_enter();
   __shared__ float sh[32];
   __shared__ bool last;
   const bool is_max = mode == 2;
@@ -134,6 +135,7 @@ void launch_reduce_all(const float* x, int64_t n, int mode, float* out) {
 // mode 0 sum, 1 mean, 2 max, 3 max+index (first index), 4 argmax (index only)
 __global__ void k_reduce_rows_warp(const float* __restrict__ x, int64_t rows, int64_t red, int mode,
                                    float* __restrict__ out, int32_t* __restrict__ idx) {
+  ::tp::pdl_enter();
   int lane = threadIdx.x & 31;
   int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   if (row >= rows) return;
@@ -163,6 +165,7 @@ __global__ void k_reduce_rows_warp(const float* __restrict__ x, int64_t rows, in
 
 __global__ void k_reduce_rows_block(const float* __restrict__ x, int64_t rows, int64_t red, int mode,
                                     float* __restrict__ out, int32_t* __restrict__ idx) {
+  ::tp::pdl_enter();
   __shared__ float shv[32];
   __shared__ int shi[32];
   int64_t row = blockIdx.x;
@@ -231,6 +234,7 @@ __global__ void k_reduce_rows_block(const float* __restrict__ x, int64_t rows, i
 __global__ void k_reduce_cols(const float* __restrict__ x, int64_t outer, int64_t red, int64_t inner, int mode,
                               int splits, float* __restrict__ out, int32_t* __restrict__ idx,
                               float* __restrict__ wsv, int32_t* __restrict__ wsi) {
+  ::tp::pdl_enter();
   __shared__ float shv[8][33];
   __shared__ int shi[8][33];
   int64_t col = (int64_t)blockIdx.x * 32 + threadIdx.x;
@@ -282,6 +286,7 @@ __global__ void k_reduce_cols(const float* __restrict__ x, int64_t outer, int64_
 __global__ void k_reduce_cols4(const float* __restrict__ x, int64_t outer, int64_t red, int64_t inner, int mode,
                                int splits, float* __restrict__ out, int32_t* __restrict__ idx,
                                float* __restrict__ wsv, int32_t* __restrict__ wsi) {
+  ::tp::pdl_enter();
   __shared__ float4 shv[8][32];
   __shared__ int4 shi[8][32];
   const int64_t c4 = (int64_t)blockIdx.x * 32 + threadIdx.x, col = 4 * c4;
@@ -366,6 +371,7 @@ __global__ void k_reduce_cols4(const float* __restrict__ x, int64_t outer, int64
 __global__ void k_reduce_cols_finish(int64_t n, int64_t red, int mode, int splits, const float* __restrict__ wsv,
                                      const int32_t* __restrict__ wsi, float* __restrict__ out,
                                      int32_t* __restrict__ idx) {
+  ::tp::pdl_enter();
   int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (i >= n) return;
   bool is_sum = mode <= 1;
@@ -430,6 +436,7 @@ void launch_reduce_dim(const float* x, int64_t outer, int64_t red, int64_t inner
 template <int PER, bool LOG>
 __global__ void __launch_bounds__(256) k_softmax_rows(const float* __restrict__ x, float* __restrict__ y,
                                                       int64_t C) {
+  ::tp::pdl_enter();
   __shared__ float sh[32];
   const float* xr = x + (int64_t)blockIdx.x * C;
   float* yr = y + (int64_t)blockIdx.x * C;
@@ -477,6 +484,7 @@ __global__ void __launch_bounds__(256) k_softmax_rows(const float* __restrict__ 
 // Short rows (C <= 32*8): one warp per row, values in registers.
 template <bool LOG>
 __global__ void k_softmax_rows_warp(const float* __restrict__ x, float* __restrict__ y, int64_t rows, int64_t C) {
+  ::tp::pdl_enter();
   int lane = threadIdx.x & 31;
   int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   if (row >= rows) return;
@@ -511,6 +519,7 @@ __global__ void k_softmax_rows_warp(const float* __restrict__ x, float* __restri
 // per (outer, inner) row, three passes with stride `inner`.
 __global__ void k_softmax_strided(const float* __restrict__ x, float* __restrict__ y, int64_t rows, int64_t axis,
                                   int64_t inner, int log_mode) {
+  ::tp::pdl_enter();
   int64_t row = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (row >= rows) return;
   int64_t base = (row / inner) * axis * inner + (row % inner);
@@ -560,6 +569,7 @@ void launch_softmax(const float* x, float* y, int64_t outer, int64_t axis, int64
 template <bool LOG>
 __global__ void k_softmax_bwd(const float* __restrict__ go, const float* __restrict__ s, float* __restrict__ gi,
                               int64_t rows, int64_t C) {
+  ::tp::pdl_enter();
   int lane = threadIdx.x & 31;
   int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   if (row >= rows) return;
@@ -581,6 +591,7 @@ __device__ __forceinline__ int ce_target(float t, int64_t C) {
 
 __global__ void k_cross_entropy(const float* __restrict__ x, const float* __restrict__ tgt, float* __restrict__ loss,
                                 int64_t B, int64_t C) {
+  ::tp::pdl_enter();
   int lane = threadIdx.x & 31;
   int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   if (row >= B) return;
@@ -598,6 +609,7 @@ __global__ void k_cross_entropy(const float* __restrict__ x, const float* __rest
 __global__ void k_cross_entropy_bwd(const float* __restrict__ go, int go_scalar, const float* __restrict__ x,
                                     const float* __restrict__ tgt, float* __restrict__ gi, int64_t B, int64_t C,
                                     float scale) {
+  ::tp::pdl_enter();
   int lane = threadIdx.x & 31;
   int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   if (row >= B) return;

@@ -56,6 +56,7 @@ void make_map_f32(CUtensorMap* map, const void* base, int rank, const uint64_t* 
 }
 
 __global__ void k_tf32_lo(const float4* __restrict__ x, float4* __restrict__ lo, int64_t n4) {
+  ::tp::pdl_enter();
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
     const float4 v = x[i];
@@ -67,6 +68,7 @@ __global__ void k_tf32_lo(const float4* __restrict__ x, float4* __restrict__ lo,
 }
 
 __global__ void k_tf32_lo_tail(const float* __restrict__ x, float* __restrict__ lo, int64_t i0, int64_t n) {
+  ::tp::pdl_enter();
   const int64_t i = i0 + threadIdx.x;
   if (i < n) lo[i] = x[i] - __uint_as_float(__float_as_uint(x[i]) & 0xFFFFE000u);
 }

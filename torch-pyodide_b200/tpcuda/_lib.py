@@ -117,6 +117,7 @@ SIGNATURES: dict[str, list] = {
     "tp_cross_entropy": [I64, I64, HP],
     "tp_cross_entropy_backward": [I64, I64, I64, INT, HP],
     "tp_set_gemm_path": [INT],
+    "tp_set_pdl": [INT],
     "tp_gemm_status": [ctypes.POINTER(INT), INT],
     "tp_matmul": [I64, I64, HP],
     "tp_linear": [I64, I64, I64, HP],
