@@ -165,7 +165,11 @@ def test_batchnorm_fused_relu_matches_composition(cuda_rt):
     assert np.array_equal(vals(cuda_rt, a), vals(cuda_rt, b))
 
 
-@pytest.mark.parametrize("rows,D", [(4, 10), (33, 300), (16, 1024), (8, 4096), (3, 9000)])
+# D % 4 == 0 takes the 16-byte kernels (1 / 2 / 4 / 8 float4 per thread; 2052: a
+# partly filled last group); hundreds of rows make the dgamma / dbeta column sum
+# run over hundreds of per-CTA partial rows
+@pytest.mark.parametrize("rows,D", [(4, 10), (33, 300), (16, 1024), (8, 4096), (3, 9000), (600, 2048),
+                                    (5000, 512), (64, 8192), (40, 2052), (700, 1030)])
 def test_layernorm_forward_backward(cuda_rt, oracle_rt, rows, D):
     rng = np.random.default_rng(5)
     cx, ox = both(cuda_rt, oracle_rt, rng.standard_normal((rows, D)))

@@ -184,8 +184,11 @@ def test_argmax_bit_exact_first_index(cuda_rt, oracle_rt, shape):
     check(cuda_rt, oracle_rt, cuda_rt.argmax(cx["id"]), oracle_rt.argmax(ox["id"]))
 
 
+# rows of C % 4 == 0 up to 8192 take the 16-byte kernels (2052 / 4100: partly
+# filled last float4 groups); 1030 and 9000 the scalar ones
 @pytest.mark.parametrize("shape,dim", [([4, 10], -1), ([33, 300], -1), ([3, 1500], -1), ([2, 8192], -1),
-                                       ([2, 9000], -1), ([3, 5, 7], 1), ([6, 4], 0)])
+                                       ([2, 9000], -1), ([3, 5, 7], 1), ([6, 4], 0), ([5, 2052], -1),
+                                       ([7, 4100], -1), ([3, 1030], -1)])
 def test_softmax_logsoftmax(cuda_rt, oracle_rt, shape, dim):
     rng = np.random.default_rng(13)
     x = (rng.standard_normal(shape) * 3).astype(np.float32)

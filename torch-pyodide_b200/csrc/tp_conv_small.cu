@@ -182,7 +182,9 @@ __global__ void __launch_bounds__(SC_THREADS, 2)
 
 // dw[i] = sum over splits of part[split][i] in f64: each of a block's 8 warps
 // sums a contiguous slice of splits for 32 consecutive i, then the slices are
-// added in slice order (deterministic).  i = (co*4 + ci)*9 + tap
+// added in slice order (deterministic).  i = (co*4 + ci)*9 + tap.  A slice's
+// values are loaded 8 at a time before they are added (in order), so the loads
+// overlap instead of each waiting for the previous add.
 __global__ void k_conv_c4_wgrad_finish(const float* __restrict__ part, int splits, int per, float* __restrict__ dw) {
   ::tp::pdl_enter();
   __shared__ double sl[8][32];
@@ -190,8 +192,17 @@ __global__ void k_conv_c4_wgrad_finish(const float* __restrict__ part, int split
   const int i = blockIdx.x * 32 + lane;
   const int per_w = (splits + 7) / 8, k0 = wp * per_w, k1 = min(k0 + per_w, splits);
   double s = 0.0;
-  if (i < per)
-    for (int k = k0; k < k1; ++k) s += part[(int64_t)k * per + i];
+  if (i < per) {
+    int k = k0;
+    for (; k + 8 <= k1; k += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = part[(int64_t)(k + u) * per + i];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) s += v[u];
+    }
+    for (; k < k1; ++k) s += part[(int64_t)k * per + i];
+  }
   sl[wp][lane] = s;
   __syncthreads();
   if (wp == 0 && i < per) {

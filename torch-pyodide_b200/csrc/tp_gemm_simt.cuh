@@ -117,8 +117,17 @@ __global__ void k_splitk_reduce(const float* __restrict__ ws, int splits, int64_
   ::tp::pdl_enter();
   int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < M * N; i += stride) {
+    // eight splits' loads in flight at a time, added in split order
     float s = 0.0f;
-    for (int z = 0; z < splits; ++z) s += ws[(int64_t)z * M * N + i];
+    int z = 0;
+    for (; z + 8 <= splits; z += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = ws[(int64_t)(z + u) * M * N + i];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) s += v[u];
+    }
+    for (; z < splits; ++z) s += ws[(int64_t)z * M * N + i];
     ep(b, i / N, i % N, s);
   }
 }

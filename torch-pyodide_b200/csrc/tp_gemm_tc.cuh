@@ -384,8 +384,22 @@ __global__ void k_splitk_reduce_b(const float* __restrict__ ws, int splits, int6
   if ((N & 3) == 0) {
     const int64_t n4 = MN >> 2;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
+      // four splits' loads in flight at a time, added in split order
       float4 s = reinterpret_cast<const float4*>(base)[i];
-      for (int z = 1; z < splits; ++z) {
+      int z = 1;
+      for (; z + 4 <= splits; z += 4) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) v[u] = reinterpret_cast<const float4*>(base + (int64_t)(z + u) * MN)[i];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          s.x += v[u].x;
+          s.y += v[u].y;
+          s.z += v[u].z;
+          s.w += v[u].w;
+        }
+      }
+      for (; z < splits; ++z) {
         float4 v = reinterpret_cast<const float4*>(base + (int64_t)z * MN)[i];
         s.x += v.x;
         s.y += v.y;
@@ -402,7 +416,15 @@ __global__ void k_splitk_reduce_b(const float* __restrict__ ws, int splits, int6
   }
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < MN; i += stride) {
     float s = 0.0f;
-    for (int z = 0; z < splits; ++z) s += base[(int64_t)z * MN + i];
+    int z = 0;
+    for (; z + 8 <= splits; z += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = base[(int64_t)(z + u) * MN + i];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) s += v[u];
+    }
+    for (; z < splits; ++z) s += base[(int64_t)z * MN + i];
     ep(b, i / N, i % N, s);
   }
 }

@@ -244,6 +244,66 @@ __global__ void __launch_bounds__(256) k_ln_fwd(const float* __restrict__ x, con
   }
 }
 
+// As k_ln_fwd with 16-byte accesses: thread t owns the float4 columns
+// t + 256 k of the row (D % 4 == 0, 16-byte aligned rows and parameters).
+template <int V>
+__global__ void __launch_bounds__(256) k_ln_fwd_vec(const float4* __restrict__ x, const float4* __restrict__ g,
+                                                    const float4* __restrict__ b, float4* __restrict__ y,
+                                                    float* __restrict__ smean, float* __restrict__ srstd,
+                                                    int64_t D, float eps) {
+  ::tp::pdl_enter();
+  __shared__ float sh[32];
+  const int64_t D4 = D >> 2;
+  const float4* xr = x + (int64_t)blockIdx.x * D4;
+  float4* yr = y + (int64_t)blockIdx.x * D4;
+  float4 v[V];
+  float s = 0.0f;
+#pragma unroll
+  for (int k = 0; k < V; ++k) {
+    const int64_t i = threadIdx.x + (int64_t)k * 256;
+    v[k] = i < D4 ? xr[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+  }
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  if (lane == 0) sh[w] = s;
+  __syncthreads();
+  float tot = 0.0f;
+  for (int k = 0; k < 8; ++k) tot += sh[k];
+  const float mean = tot / (float)D;
+  __syncthreads();
+  float q = 0.0f;
+#pragma unroll
+  for (int k = 0; k < V; ++k) {
+    const int64_t i = threadIdx.x + (int64_t)k * 256;
+    if (i < D4) {
+      const float a = v[k].x - mean, bq = v[k].y - mean, c = v[k].z - mean, d = v[k].w - mean;
+      q += (a * a + bq * bq) + (c * c + d * d);
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+  if (lane == 0) sh[w] = q;
+  __syncthreads();
+  float tq = 0.0f;
+  for (int k = 0; k < 8; ++k) tq += sh[k];
+  const float var = tq / (float)D;
+  const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(var + eps));
+#pragma unroll
+  for (int k = 0; k < V; ++k) {
+    const int64_t i = threadIdx.x + (int64_t)k * 256;
+    if (i < D4) {
+      const float4 gg = g ? g[i] : make_float4(1.0f, 1.0f, 1.0f, 1.0f);
+      const float4 bb = b ? b[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      yr[i] = make_float4(gg.x * ((v[k].x - mean) * rstd) + bb.x, gg.y * ((v[k].y - mean) * rstd) + bb.y,
+                          gg.z * ((v[k].z - mean) * rstd) + bb.z, gg.w * ((v[k].w - mean) * rstd) + bb.w);
+    }
+  }
+  if (threadIdx.x == 0) {
+    if (smean) smean[blockIdx.x] = mean;
+    if (srstd) srstd[blockIdx.x] = rstd;
+  }
+}
+
 // Rows too long for registers: three passes from global memory.
 __global__ void k_ln_fwd_long(const float* __restrict__ x, const float* __restrict__ g,
                               const float* __restrict__ b, float* __restrict__ y, float* __restrict__ smean,
@@ -421,24 +481,168 @@ __global__ void __launch_bounds__(256) k_ln_bwd_reg(const float* __restrict__ dy
   }
 }
 
-__global__ void k_colsum_partials(const float* __restrict__ ws, int nblk, int64_t D, float* __restrict__ dg,
-                                  float* __restrict__ db) {
+// k_ln_bwd_reg with 16-byte accesses: thread t owns the float4 columns
+// t + 256 k (D % 4 == 0, 16-byte aligned rows and gamma).
+template <int V>
+__global__ void __launch_bounds__(256) k_ln_bwd_vec(const float4* __restrict__ dy, const float4* __restrict__ x,
+                                                    const float4* __restrict__ g, const float* __restrict__ smean,
+                                                    const float* __restrict__ srstd, float4* __restrict__ dx,
+                                                    float* __restrict__ ws, int64_t rows, int64_t D, int rpb) {
   ::tp::pdl_enter();
-  int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (i >= D) return;
-  float sg = 0.0f, sb = 0.0f;
-  for (int k = 0; k < nblk; ++k) {
-    sg += ws[(int64_t)k * 2 * D + i];
-    sb += ws[(int64_t)k * 2 * D + D + i];
+  __shared__ float sh[2][8];
+  extern __shared__ float4 colsh4[];  // gamma [D/4], dgamma partial [D/4], dbeta partial [D/4]
+  const int64_t D4 = D >> 2;
+  float4* sgam = colsh4;
+  float4* spgx = colsh4 + D4;
+  float4* spgd = colsh4 + 2 * D4;
+  const float4 zero4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t r0 = (int64_t)blockIdx.x * rpb;
+#pragma unroll
+  for (int k = 0; k < V; ++k) {
+    const int64_t i = threadIdx.x + (int64_t)k * 256;
+    if (i < D4) {
+      sgam[i] = g ? g[i] : make_float4(1.0f, 1.0f, 1.0f, 1.0f);
+      spgx[i] = zero4;
+      spgd[i] = zero4;
+    }
   }
-  if (dg) dg[i] = sg;
-  if (db) db[i] = sb;
+  const float inv_d = 1.0f / (float)D;
+  for (int64_t r = r0; r < r0 + rpb && r < rows; ++r) {
+    const float4* dyr = dy + r * D4;
+    const float4* xr = x + r * D4;
+    const float mu = smean[r], rs = srstd[r];
+    float4 dv[V], xh[V];
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      const int64_t i = threadIdx.x + (int64_t)k * 256;
+      dv[k] = i < D4 ? dyr[i] : zero4;
+      xh[k] = i < D4 ? xr[i] : zero4;
+    }
+    float a = 0.0f, bb = 0.0f;
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      const int64_t i = threadIdx.x + (int64_t)k * 256;
+      if (i < D4) {
+        xh[k] = make_float4((xh[k].x - mu) * rs, (xh[k].y - mu) * rs, (xh[k].z - mu) * rs, (xh[k].w - mu) * rs);
+        const float4 gm = sgam[i];
+        const float gx = gm.x * dv[k].x, gy = gm.y * dv[k].y, gz = gm.z * dv[k].z, gw = gm.w * dv[k].w;
+        a += (gx + gy) + (gz + gw);
+        bb += (gx * xh[k].x + gy * xh[k].y) + (gz * xh[k].z + gw * xh[k].w);
+        float4 px = spgx[i], pd = spgd[i];
+        px.x += dv[k].x * xh[k].x;
+        px.y += dv[k].y * xh[k].y;
+        px.z += dv[k].z * xh[k].z;
+        px.w += dv[k].w * xh[k].w;
+        pd.x += dv[k].x;
+        pd.y += dv[k].y;
+        pd.z += dv[k].z;
+        pd.w += dv[k].w;
+        spgx[i] = px;
+        spgd[i] = pd;
+      }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+      a += __shfl_xor_sync(0xffffffffu, a, o);
+      bb += __shfl_xor_sync(0xffffffffu, bb, o);
+    }
+    if (lane == 0) {
+      sh[0][w] = a;
+      sh[1][w] = bb;
+    }
+    __syncthreads();
+    float ta = 0.0f, tb = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      ta += sh[0][k];
+      tb += sh[1][k];
+    }
+    __syncthreads();
+    const float ma = ta * inv_d, mb = tb * inv_d;
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      const int64_t i = threadIdx.x + (int64_t)k * 256;
+      if (i < D4) {
+        const float4 gm = sgam[i];
+        dx[r * D4 + i] = make_float4(rs * (gm.x * dv[k].x - ma - xh[k].x * mb), rs * (gm.y * dv[k].y - ma - xh[k].y * mb),
+                                     rs * (gm.z * dv[k].z - ma - xh[k].z * mb), rs * (gm.w * dv[k].w - ma - xh[k].w * mb));
+      }
+    }
+  }
+  if (ws) {
+    float4* pg = reinterpret_cast<float4*>(ws + (int64_t)blockIdx.x * 2 * D);
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      const int64_t i = threadIdx.x + (int64_t)k * 256;
+      if (i < D4) {
+        pg[i] = spgx[i];
+        pg[D4 + i] = spgd[i];
+      }
+    }
+  }
 }
+
+// dgamma / dbeta from the per-CTA partial rows: lane = one column of a 32-column
+// block, warp w sums partial rows w, w + 8, ... (coalesced 128-byte rows, several
+// loads in flight), then warp 0 adds the 8 warp sums in order: a fixed order for
+// every launch.
+__global__ void __launch_bounds__(256) k_colsum_partials(const float* __restrict__ ws, int nblk, int64_t D,
+                                                         float* __restrict__ dg, float* __restrict__ db) {
+  ::tp::pdl_enter();
+  __shared__ float sh[2][8][32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t i = blockIdx.x * (int64_t)32 + lane;
+  float sg = 0.0f, sb = 0.0f;
+  if (i < D) {
+    int k = w;
+    for (; k + 24 < nblk; k += 32) {
+      float g4[4], b4[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        g4[u] = ws[(int64_t)(k + 8 * u) * 2 * D + i];
+        b4[u] = ws[(int64_t)(k + 8 * u) * 2 * D + D + i];
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        sg += g4[u];
+        sb += b4[u];
+      }
+    }
+    for (; k < nblk; k += 8) {
+      sg += ws[(int64_t)k * 2 * D + i];
+      sb += ws[(int64_t)k * 2 * D + D + i];
+    }
+  }
+  sh[0][w][lane] = sg;
+  sh[1][w][lane] = sb;
+  __syncthreads();
+  if (w == 0 && i < D) {
+    float tg = 0.0f, tb = 0.0f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      tg += sh[0][q][lane];
+      tb += sh[1][q][lane];
+    }
+    if (dg) dg[i] = tg;
+    if (db) db[i] = tb;
+  }
+}
+
+static inline bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
 void launch_ln_fwd(const float* x, const float* g, const float* b, float* y, float* sm, float* sr, int64_t rows,
                    int64_t D, float eps) {
   if (rows == 0 || D == 0) return;
   unsigned gr = (unsigned)rows;
+  if (D % 4 == 0 && D <= 256 * 32 && aligned16(x) && aligned16(y) && aligned16(g) && aligned16(b)) {
+    const float4 *x4 = (const float4*)x, *g4 = (const float4*)g, *b4 = (const float4*)b;
+    float4* y4 = (float4*)y;
+    if (D <= 256 * 4) TP_LAUNCH(k_ln_fwd_vec<1>, gr, 256, 0, x4, g4, b4, y4, sm, sr, D, eps);
+    else if (D <= 256 * 8) TP_LAUNCH(k_ln_fwd_vec<2>, gr, 256, 0, x4, g4, b4, y4, sm, sr, D, eps);
+    else if (D <= 256 * 16) TP_LAUNCH(k_ln_fwd_vec<4>, gr, 256, 0, x4, g4, b4, y4, sm, sr, D, eps);
+    else TP_LAUNCH(k_ln_fwd_vec<8>, gr, 256, 0, x4, g4, b4, y4, sm, sr, D, eps);
+    return;
+  }
   if (D <= 256 * 4) TP_LAUNCH(k_ln_fwd<4>, gr, 256, 0, x, g, b, y, sm, sr, D, eps);
   else if (D <= 256 * 8) TP_LAUNCH(k_ln_fwd<8>, gr, 256, 0, x, g, b, y, sm, sr, D, eps);
   else if (D <= 256 * 16) TP_LAUNCH(k_ln_fwd<16>, gr, 256, 0, x, g, b, y, sm, sr, D, eps);
@@ -457,6 +661,26 @@ void launch_ln_bwd(const float* dy, const float* x, const float* g, const float*
   int nblk = (int)((rows + rpb - 1) / rpb);
   float* ws = (dg || db) ? (float*)scratch((size_t)nblk * 2 * D * sizeof(float)) : nullptr;
   const size_t shb = (size_t)3 * D * sizeof(float);
+  if (D % 4 == 0 && D <= 256 * 16 && aligned16(dy) && aligned16(x) && aligned16(g) && aligned16(dx) &&
+      aligned16(ws)) {
+    const float4 *dy4 = (const float4*)dy, *x4 = (const float4*)x, *g4 = (const float4*)g;
+    float4* dx4 = (float4*)dx;
+#define TP_LN_BWD_VEC(V)                                                                                       \
+  do {                                                                                                         \
+    static bool attr = false;                                                                                  \
+    if (!attr) {                                                                                               \
+      TP_CUDA(cudaFuncSetAttribute(k_ln_bwd_vec<V>, cudaFuncAttributeMaxDynamicSharedMemorySize, 3 * 1024 * V * 4)); \
+      attr = true;                                                                                             \
+    }                                                                                                          \
+    TP_LAUNCH(k_ln_bwd_vec<V>, (unsigned)nblk, 256, shb, dy4, x4, g4, sm, sr, dx4, ws, rows, D, rpb);           \
+  } while (0)
+    if (D <= 256 * 4) TP_LN_BWD_VEC(1);
+    else if (D <= 256 * 8) TP_LN_BWD_VEC(2);
+    else TP_LN_BWD_VEC(4);
+#undef TP_LN_BWD_VEC
+    if (ws) TP_LAUNCH(k_colsum_partials, (unsigned)((D + 31) / 32), 256, 0, ws, nblk, D, dg, db);
+    return;
+  }
 #define TP_LN_BWD_REG(P)                                                                                  \
   do {                                                                                                    \
     static bool attr = false;                                                                             \
@@ -471,7 +695,7 @@ void launch_ln_bwd(const float* dy, const float* x, const float* g, const float*
   else if (D <= 256 * 16) TP_LN_BWD_REG(16);
   else TP_LAUNCH(k_ln_bwd, (unsigned)nblk, 256, 0, dy, x, g, sm, sr, dx, ws, rows, D, rpb);
 #undef TP_LN_BWD_REG
-  if (ws) TP_LAUNCH(k_colsum_partials, (unsigned)((D + 255) / 256), 256, 0, ws, nblk, D, dg, db);
+  if (ws) TP_LAUNCH(k_colsum_partials, (unsigned)((D + 31) / 32), 256, 0, ws, nblk, D, dg, db);
 }
 
 static void nchw_dims(const Tensor& x, int64_t& N, int64_t& C, int64_t& S) {

@@ -481,6 +481,49 @@ __global__ void __launch_bounds__(256) k_softmax_rows(const float* __restrict__ 
   }
 }
 
+// As k_softmax_rows with 16-byte accesses: thread t owns the float4 columns
+// t + 256 k (C % 4 == 0, 16-byte aligned rows).
+template <int V, bool LOG>
+__global__ void __launch_bounds__(256) k_softmax_rows_vec(const float4* __restrict__ x, float4* __restrict__ y,
+                                                          int64_t C) {
+  ::tp::pdl_enter();
+  __shared__ float sh[32];
+  const int64_t C4 = C >> 2;
+  const float4* xr = x + (int64_t)blockIdx.x * C4;
+  float4* yr = y + (int64_t)blockIdx.x * C4;
+  float4 v[V];
+  float m = -FLT_MAX;
+#pragma unroll
+  for (int k = 0; k < V; ++k) {
+    const int64_t i = threadIdx.x + (int64_t)k * 256;
+    v[k] = i < C4 ? xr[i] : make_float4(-FLT_MAX, -FLT_MAX, -FLT_MAX, -FLT_MAX);
+    m = fmaxf(m, fmaxf(fmaxf(v[k].x, v[k].y), fmaxf(v[k].z, v[k].w)));
+  }
+  m = block_reduce<true>(m, sh);
+  float s = 0.0f;
+#pragma unroll
+  for (int k = 0; k < V; ++k) {
+    const int64_t i = threadIdx.x + (int64_t)k * 256;
+    if (i < C4) {
+      const float4 e = make_float4(expf(v[k].x - m), expf(v[k].y - m), expf(v[k].z - m), expf(v[k].w - m));
+      s += (e.x + e.y) + (e.z + e.w);
+      if (!LOG) v[k] = e;  // kept for the output pass: one exp per element
+    }
+  }
+  s = block_reduce<false>(s, sh);
+  const float lse = LOG ? logf(s) : 0.0f, inv = LOG ? 0.0f : 1.0f / s;
+#pragma unroll
+  for (int k = 0; k < V; ++k) {
+    const int64_t i = threadIdx.x + (int64_t)k * 256;
+    if (i < C4) {
+      if (LOG)
+        yr[i] = make_float4((v[k].x - m) - lse, (v[k].y - m) - lse, (v[k].z - m) - lse, (v[k].w - m) - lse);
+      else
+        yr[i] = make_float4(v[k].x * inv, v[k].y * inv, v[k].z * inv, v[k].w * inv);
+    }
+  }
+}
+
 // Short rows (C <= 32*8): one warp per row, values in registers.
 template <bool LOG>
 __global__ void k_softmax_rows_warp(const float* __restrict__ x, float* __restrict__ y, int64_t rows, int64_t C) {
@@ -545,6 +588,24 @@ void launch_softmax(const float* x, float* y, int64_t outer, int64_t axis, int64
     unsigned blocks = (unsigned)((rows * 32 + 255) / 256);
     if (log_mode) TP_LAUNCH(k_softmax_rows_warp<true>, blocks, 256, 0, x, y, rows, axis);
     else TP_LAUNCH(k_softmax_rows_warp<false>, blocks, 256, 0, x, y, rows, axis);
+    return;
+  }
+  if (axis % 4 == 0 && axis <= 256 * 32 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)y & 15) == 0) {
+    const float4* x4 = (const float4*)x;
+    float4* y4 = (float4*)y;
+#define TP_SOFTMAX_VEC(V)                                                                                   \
+  if (log_mode) TP_LAUNCH((k_softmax_rows_vec<V, true>), (unsigned)rows, 256, 0, x4, y4, axis);           \
+  else TP_LAUNCH((k_softmax_rows_vec<V, false>), (unsigned)rows, 256, 0, x4, y4, axis);
+    if (axis <= 256 * 4) {
+      TP_SOFTMAX_VEC(1)
+    } else if (axis <= 256 * 8) {
+      TP_SOFTMAX_VEC(2)
+    } else if (axis <= 256 * 16) {
+      TP_SOFTMAX_VEC(4)
+    } else {
+      TP_SOFTMAX_VEC(8)
+    }
+#undef TP_SOFTMAX_VEC
     return;
   }
 #define TP_SOFTMAX_CASE(P)                                                                    \
