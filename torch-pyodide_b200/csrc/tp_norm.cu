@@ -17,6 +17,8 @@
 //     dbeta via per-CTA column partials reduced in a fixed order.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "tp_core.h"
 #include "tp_launch.h"
 #include "tp_chanred.cuh"
@@ -481,42 +483,43 @@ __global__ void __launch_bounds__(256) k_ln_bwd_reg(const float* __restrict__ dy
   }
 }
 
-// k_ln_bwd_reg with 16-byte accesses: thread t owns the float4 columns
-// t + 256 k (D % 4 == 0, 16-byte aligned rows and gamma).
+// LayerNorm backward with 16-byte accesses (D % 4 == 0, 16-byte aligned rows
+// and gamma): thread t owns the float4 columns t + 256 k for all the CTA's rows,
+// so its dgamma / dbeta partial columns stay in registers (no shared-memory
+// read-modify-write per element); gamma is read once per row from shared
+// memory; one partial row per CTA is written at the end.  3 CTAs per SM.
 template <int V>
-__global__ void __launch_bounds__(256) k_ln_bwd_vec(const float4* __restrict__ dy, const float4* __restrict__ x,
-                                                    const float4* __restrict__ g, const float* __restrict__ smean,
-                                                    const float* __restrict__ srstd, float4* __restrict__ dx,
-                                                    float* __restrict__ ws, int64_t rows, int64_t D, int rpb) {
+__global__ void __launch_bounds__(256, 3) k_ln_bwd_vreg(const float4* __restrict__ dy, const float4* __restrict__ x,
+                                                        const float4* __restrict__ g, const float* __restrict__ smean,
+                                                        const float* __restrict__ srstd, float4* __restrict__ dx,
+                                                        float* __restrict__ ws, int64_t rows, int64_t D, int rpb) {
   ::tp::pdl_enter();
   __shared__ float sh[2][8];
-  extern __shared__ float4 colsh4[];  // gamma [D/4], dgamma partial [D/4], dbeta partial [D/4]
+  extern __shared__ float4 colsh4[];  // gamma [D/4]
   const int64_t D4 = D >> 2;
   float4* sgam = colsh4;
-  float4* spgx = colsh4 + D4;
-  float4* spgd = colsh4 + 2 * D4;
   const float4 zero4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int64_t r0 = (int64_t)blockIdx.x * rpb;
+  float4 pgx[V], pgd[V];
 #pragma unroll
   for (int k = 0; k < V; ++k) {
     const int64_t i = threadIdx.x + (int64_t)k * 256;
-    if (i < D4) {
-      sgam[i] = g ? g[i] : make_float4(1.0f, 1.0f, 1.0f, 1.0f);
-      spgx[i] = zero4;
-      spgd[i] = zero4;
-    }
+    if (i < D4) sgam[i] = g ? g[i] : make_float4(1.0f, 1.0f, 1.0f, 1.0f);
+    pgx[k] = zero4;
+    pgd[k] = zero4;
   }
+  __syncthreads();
   const float inv_d = 1.0f / (float)D;
   for (int64_t r = r0; r < r0 + rpb && r < rows; ++r) {
     const float4* dyr = dy + r * D4;
     const float4* xr = x + r * D4;
     const float mu = smean[r], rs = srstd[r];
-    float4 dv[V], xh[V];
+    float4 gd[V], xh[V];
 #pragma unroll
     for (int k = 0; k < V; ++k) {
       const int64_t i = threadIdx.x + (int64_t)k * 256;
-      dv[k] = i < D4 ? dyr[i] : zero4;
+      gd[k] = i < D4 ? dyr[i] : zero4;
       xh[k] = i < D4 ? xr[i] : zero4;
     }
     float a = 0.0f, bb = 0.0f;
@@ -525,21 +528,18 @@ __global__ void __launch_bounds__(256) k_ln_bwd_vec(const float4* __restrict__ d
       const int64_t i = threadIdx.x + (int64_t)k * 256;
       if (i < D4) {
         xh[k] = make_float4((xh[k].x - mu) * rs, (xh[k].y - mu) * rs, (xh[k].z - mu) * rs, (xh[k].w - mu) * rs);
+        pgx[k].x += gd[k].x * xh[k].x;
+        pgx[k].y += gd[k].y * xh[k].y;
+        pgx[k].z += gd[k].z * xh[k].z;
+        pgx[k].w += gd[k].w * xh[k].w;
+        pgd[k].x += gd[k].x;
+        pgd[k].y += gd[k].y;
+        pgd[k].z += gd[k].z;
+        pgd[k].w += gd[k].w;
         const float4 gm = sgam[i];
-        const float gx = gm.x * dv[k].x, gy = gm.y * dv[k].y, gz = gm.z * dv[k].z, gw = gm.w * dv[k].w;
-        a += (gx + gy) + (gz + gw);
-        bb += (gx * xh[k].x + gy * xh[k].y) + (gz * xh[k].z + gw * xh[k].w);
-        float4 px = spgx[i], pd = spgd[i];
-        px.x += dv[k].x * xh[k].x;
-        px.y += dv[k].y * xh[k].y;
-        px.z += dv[k].z * xh[k].z;
-        px.w += dv[k].w * xh[k].w;
-        pd.x += dv[k].x;
-        pd.y += dv[k].y;
-        pd.z += dv[k].z;
-        pd.w += dv[k].w;
-        spgx[i] = px;
-        spgd[i] = pd;
+        gd[k] = make_float4(gm.x * gd[k].x, gm.y * gd[k].y, gm.z * gd[k].z, gm.w * gd[k].w);
+        a += (gd[k].x + gd[k].y) + (gd[k].z + gd[k].w);
+        bb += (gd[k].x * xh[k].x + gd[k].y * xh[k].y) + (gd[k].z * xh[k].z + gd[k].w * xh[k].w);
       }
     }
     for (int o = 16; o > 0; o >>= 1) {
@@ -562,11 +562,9 @@ __global__ void __launch_bounds__(256) k_ln_bwd_vec(const float4* __restrict__ d
 #pragma unroll
     for (int k = 0; k < V; ++k) {
       const int64_t i = threadIdx.x + (int64_t)k * 256;
-      if (i < D4) {
-        const float4 gm = sgam[i];
-        dx[r * D4 + i] = make_float4(rs * (gm.x * dv[k].x - ma - xh[k].x * mb), rs * (gm.y * dv[k].y - ma - xh[k].y * mb),
-                                     rs * (gm.z * dv[k].z - ma - xh[k].z * mb), rs * (gm.w * dv[k].w - ma - xh[k].w * mb));
-      }
+      if (i < D4)
+        dx[r * D4 + i] = make_float4(rs * (gd[k].x - ma - xh[k].x * mb), rs * (gd[k].y - ma - xh[k].y * mb),
+                                     rs * (gd[k].z - ma - xh[k].z * mb), rs * (gd[k].w - ma - xh[k].w * mb));
     }
   }
   if (ws) {
@@ -575,8 +573,8 @@ __global__ void __launch_bounds__(256) k_ln_bwd_vec(const float4* __restrict__ d
     for (int k = 0; k < V; ++k) {
       const int64_t i = threadIdx.x + (int64_t)k * 256;
       if (i < D4) {
-        pg[i] = spgx[i];
-        pg[D4 + i] = spgd[i];
+        pg[i] = pgx[k];
+        pg[D4 + i] = pgd[k];
       }
     }
   }
@@ -661,24 +659,19 @@ void launch_ln_bwd(const float* dy, const float* x, const float* g, const float*
   int nblk = (int)((rows + rpb - 1) / rpb);
   float* ws = (dg || db) ? (float*)scratch((size_t)nblk * 2 * D * sizeof(float)) : nullptr;
   const size_t shb = (size_t)3 * D * sizeof(float);
-  if (D % 4 == 0 && D <= 256 * 16 && aligned16(dy) && aligned16(x) && aligned16(g) && aligned16(dx) &&
-      aligned16(ws)) {
+  if (D % 4 == 0 && D <= 256 * 16 && aligned16(dy) && aligned16(x) && aligned16(g)) {
+    // 16-byte kernel, dgamma / dbeta partials in registers: 3 CTAs per SM, each a run of rows
+    const int64_t target3 = (int64_t)sm_count() * 3;
+    const int rpb3 = (int)std::max<int64_t>(1, (rows + target3 - 1) / target3);
+    const int nblk3 = (int)((rows + rpb3 - 1) / rpb3);
+    float* ws3 = (dg || db) ? (float*)scratch((size_t)nblk3 * 2 * D * sizeof(float)) : nullptr;
     const float4 *dy4 = (const float4*)dy, *x4 = (const float4*)x, *g4 = (const float4*)g;
     float4* dx4 = (float4*)dx;
-#define TP_LN_BWD_VEC(V)                                                                                       \
-  do {                                                                                                         \
-    static bool attr = false;                                                                                  \
-    if (!attr) {                                                                                               \
-      TP_CUDA(cudaFuncSetAttribute(k_ln_bwd_vec<V>, cudaFuncAttributeMaxDynamicSharedMemorySize, 3 * 1024 * V * 4)); \
-      attr = true;                                                                                             \
-    }                                                                                                          \
-    TP_LAUNCH(k_ln_bwd_vec<V>, (unsigned)nblk, 256, shb, dy4, x4, g4, sm, sr, dx4, ws, rows, D, rpb);           \
-  } while (0)
-    if (D <= 256 * 4) TP_LN_BWD_VEC(1);
-    else if (D <= 256 * 8) TP_LN_BWD_VEC(2);
-    else TP_LN_BWD_VEC(4);
-#undef TP_LN_BWD_VEC
-    if (ws) TP_LAUNCH(k_colsum_partials, (unsigned)((D + 31) / 32), 256, 0, ws, nblk, D, dg, db);
+    const size_t shg = (size_t)D * sizeof(float);
+    if (D <= 256 * 4) TP_LAUNCH(k_ln_bwd_vreg<1>, (unsigned)nblk3, 256, shg, dy4, x4, g4, sm, sr, dx4, ws3, rows, D, rpb3);
+    else if (D <= 256 * 8) TP_LAUNCH(k_ln_bwd_vreg<2>, (unsigned)nblk3, 256, shg, dy4, x4, g4, sm, sr, dx4, ws3, rows, D, rpb3);
+    else TP_LAUNCH(k_ln_bwd_vreg<4>, (unsigned)nblk3, 256, shg, dy4, x4, g4, sm, sr, dx4, ws3, rows, D, rpb3);
+    if (ws3) TP_LAUNCH(k_colsum_partials, (unsigned)((D + 31) / 32), 256, 0, ws3, nblk3, D, dg, db);
     return;
   }
 #define TP_LN_BWD_REG(P)                                                                                  \
