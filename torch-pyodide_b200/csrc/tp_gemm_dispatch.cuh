@@ -76,8 +76,9 @@ void gemm_tma_bn(const CUtensorMap& ma, const CUtensorMap& mb, const SA& sa, con
     else gemm_tma2_launch<SA, SB, EP, 128, 4>(ma, mb, sa, sb, ep, M, N, K, batch, mbl);
     return;
   }
-  if (N <= 32) gemm_tma_launch<SA, SB, EP, 32, 4>(ma, mb, sa, sb, ep, M, N, K, batch, mbl);
-  else if (N <= 64) gemm_tma_launch<SA, SB, EP, 64, 4>(ma, mb, sa, sb, ep, M, N, K, batch, mbl);
+  // N <= 64: 3-stage tiles, two CTAs per SM (one's epilogue under the other's main loop)
+  if (N <= 32) gemm_tma_launch<SA, SB, EP, 32, 3>(ma, mb, sa, sb, ep, M, N, K, batch, mbl);
+  else if (N <= 64) gemm_tma_launch<SA, SB, EP, 64, 3>(ma, mb, sa, sb, ep, M, N, K, batch, mbl);
   else gemm_tma_launch<SA, SB, EP, 128, 4>(ma, mb, sa, sb, ep, M, N, K, batch, mbl);
 }
 

@@ -340,21 +340,27 @@ struct SrcFilterMN {
   }
 };
 
+// TMEM columns: the accumulator at [0, BN); stage s of A at A_TMEM0 + 64 s
+// (hi: +0..31, lo: +32..63).  Tiles of N <= 64 with 3 stages run two CTAs per
+// SM (97 KB of shared memory and 256 TMEM columns each: the accumulator at
+// [0, 64), A stages at 64, 128, 192), so one CTA's epilogue and prologue overlap
+// the other's main loop; otherwise a CTA holds the SM (120 KB floor, all 512
+// columns: the accumulator in [0, 256), 4 A stages from 256).
 template <int BN, int STAGES>
 struct Smem {
+  static constexpr bool TWO = STAGES <= 3 && BN <= 64;
   static constexpr uint32_t A_BYTES = BM * BK * 4;  // raw A (TMA); its hi/lo go to TMEM
   static constexpr uint32_t B_BYTES = BN * BK * 4;
   static constexpr uint32_t STAGE = A_BYTES + 2 * B_BYTES;  // raw A | B raw -> hi | B lo
   static constexpr uint32_t TILES = STAGES * STAGE;
-  // at least 120 KB so one CTA holds an SM (it allocates all of TMEM)
-  static constexpr uint32_t BYTES = TILES + 1280 > 122880u ? TILES + 1280 : 122880u;
+  static constexpr uint32_t BYTES = TWO || TILES + 1280 > 122880u ? TILES + 1280 : 122880u;
+  static constexpr uint32_t TMEM_COLS = TWO ? 256 : 512;
+  static constexpr uint32_t A_TMEM0 = TWO ? 64 : 256;
+  static constexpr int MIN_BLOCKS = TWO ? 2 : 1;
   static_assert(STAGE % 1024 == 0, "stages must keep 1 KB swizzle alignment");
   static_assert(STAGES <= 4 && BN <= 256, "TMEM holds the accumulator (256 columns) and 4 A stages");
+  static_assert(A_TMEM0 + 64 * STAGES <= TMEM_COLS && BN <= (int)A_TMEM0, "TMEM regions overlap");
 };
-
-// TMEM columns: the accumulator at [0, BN); stage s of A at 256 + 64 s (hi: +0..31, lo: +32..63).
-constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t A_TMEM0 = 256;
 
 __device__ __forceinline__ void mma_tf32_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc,
                                             uint32_t acc) {
@@ -403,7 +409,7 @@ __device__ __forceinline__ void read_a16(const uint8_t* tile, int r, int k0, flo
 }
 
 template <class SA, class SB, class EP, int BN, int STAGES>
-__global__ void __launch_bounds__(NTHREADS, 1)
+__global__ void __launch_bounds__(NTHREADS, (Smem<BN, STAGES>::MIN_BLOCKS))
     k_gemm_tma(const __grid_constant__ CUtensorMap ma, const __grid_constant__ CUtensorMap mb,
                const __grid_constant__ CUtensorMap mbl, SA sa, SB sb, EP ep, int64_t M, int64_t N, int64_t K,
                int64_t k_per_split, int splits, float* __restrict__ ws, int b_lo) {
@@ -441,7 +447,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   if (warp == MMA_WARP) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      tc::smem_u32(tmem_slot)),
-                 "r"(TMEM_COLS));
+                 "r"(S::TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   tc::tc_fence_before();
@@ -486,7 +492,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         tc::tc_fence_after();
         const uint32_t base = tc::smem_u32(smem + s * S::STAGE);
         const uint32_t b_hi = base + S::A_BYTES, b_lo = base + S::A_BYTES + S::B_BYTES;
-        const uint32_t a_hi = tmem + A_TMEM0 + 64 * s, a_lo = a_hi + 32;
+        const uint32_t a_hi = tmem + S::A_TMEM0 + 64 * s, a_lo = a_hi + 32;
 #pragma unroll
         for (int kk = 0; kk < BK / 8; ++kk) {
           // k-step of 8: 8 TMEM columns of A; +32 B inside a K-major B row, +1 KB (8 rows) when MN-major
@@ -522,7 +528,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           h[i] = __float_as_uint(hf);
           l[i] = __float_as_uint(lf);
         }
-        const uint32_t col = tmem + lane_base + A_TMEM0 + 64 * s + kh;
+        const uint32_t col = tmem + lane_base + S::A_TMEM0 + 64 * s + kh;
         tmem_st16(col, h);
         tmem_st16(col + 32, l);
       }
@@ -582,7 +588,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   __syncthreads();
   if (warp == MMA_WARP) {
     tc::tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(S::TMEM_COLS));
   }
 }
 
