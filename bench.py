@@ -868,6 +868,12 @@ def run_vgg(args, rank, world, local):
                                     f"({n_sm} SMs x 128 lanes x 2 x max SM clock), BatchNorm / pool / SGD bytes at "
                                     f"the measured HBM {hbm_peak} GB/s")},
     }
+    # DRAM traffic of the dominant kernel from one ncu capture at batch 1024
+    # (profiles/), scaled by the per-rank batch
+    tf = os.path.join(ROOT, "profiles", "conv3x3_tma2_pair_fwd_256to256_8x8_b1024_traffic.json")
+    if os.path.exists(tf) and model.layout == "nhwc":
+        t = json.load(open(tf))
+        line["roofline"]["traffic"] = int(t["bytes_per_launch"] * B / t["batch"])
     if world == 1 and not args.no_cpu_baseline:
         os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
         r = cpu_vgg(2, 2)
