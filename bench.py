@@ -459,7 +459,26 @@ def run_ops(args):
     nb = 32768 * 8192 * 4
     add("softmax", [32768, 8192], timed(lambda: one(rt.softmax(x["id"], -1)), 1), 2 * nb, "hbm")
     add("log_softmax", [32768, 8192], timed(lambda: one(rt.logSoftmax(x["id"], -1)), 1), 2 * nb, "hbm")
+    # backward: read the upstream gradient and the forward output, write the input gradient
+    sm_out = rt.softmax(x["id"], -1)
+    gy = rt.randn([32768, 8192], "float32")
+    add("softmax bwd", [32768, 8192], timed(lambda: one(rt.softmaxBackward(gy["id"], sm_out["id"], 32768, 8192)), 1),
+        3 * nb, "hbm")
+    add("log_softmax bwd", [32768, 8192],
+        timed(lambda: one(rt.logSoftmaxBackward(gy["id"], sm_out["id"], 32768, 8192)), 1), 3 * nb, "hbm")
+    for h in (sm_out, gy):
+        rt.destroy(h["id"])
     rt.destroy(x["id"])
+    # element-wise chain with a zero-stride broadcast (the linear layer's bias add)
+    xa = rt.randn([16384, 11008], "float32")
+    ba = rt.randn([11008], "float32")
+    add("add broadcast [M,N]+[N]", [16384, 11008], timed(lambda: one(rt.add(xa["id"], ba["id"])), 1),
+        2 * 16384 * 11008 * 4 + 11008 * 4, "hbm")
+    xb = rt.randn([16384, 11008], "float32")
+    add("mul same-shape", [16384, 11008], timed(lambda: one(rt.mul(xa["id"], xb["id"])), 1),
+        3 * 16384 * 11008 * 4, "hbm")
+    for h in (xa, xb, ba):
+        rt.destroy(h["id"])
     x = rt.randn([8192, 8192], "float32")
     nb = 8192 * 8192 * 4
     add("sum all", [8192, 8192], timed(lambda: one(rt.sum(x["id"])), 1), nb, "hbm")

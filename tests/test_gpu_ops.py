@@ -70,8 +70,12 @@ def test_binary_same_shape_bit_exact(cuda_rt, oracle_rt, op, n):
     check(cuda_rt, oracle_rt, getattr(cuda_rt, op)(ca["id"], cb["id"]), getattr(oracle_rt, op)(oa["id"], ob["id"]))
 
 
+# the last six hit the 16-byte [R][N] kernel: a bias row, a per-row column, a
+# scalar, a 3-D shape that merges to 2-D, the row operand on the left
 @pytest.mark.parametrize("sa,sb", [([2, 3], [3]), ([4, 1], [1, 5]), ([2, 3, 4, 5], [1, 3, 1, 1]),
-                                   ([6, 1, 5], [7, 1]), ([3, 4], [1]), ([1], [2, 3, 2]), ([8, 16, 4], [16, 1])])
+                                   ([6, 1, 5], [7, 1]), ([3, 4], [1]), ([1], [2, 3, 2]), ([8, 16, 4], [16, 1]),
+                                   ([64, 1024], [1024]), ([37, 20], [37, 1]), ([1], [256, 8]), ([5, 8, 16], [8, 16]),
+                                   ([12], [9, 12]), ([3, 4], [3, 1])])
 @pytest.mark.parametrize("op", ["add", "mul", "sub", "div", "gt"])
 def test_binary_broadcast_bit_exact(cuda_rt, oracle_rt, sa, sb, op):
     rng = np.random.default_rng(len(sa) * 10 + len(sb))
@@ -200,7 +204,9 @@ def test_softmax_logsoftmax(cuda_rt, oracle_rt, shape, dim):
               rtol=1e-5, atol=1e-5)
 
 
-@pytest.mark.parametrize("B,C", [(4, 10), (64, 10), (3, 1000)])
+# C % 4 == 0 rows above 256 take the one-CTA-per-row 16-byte kernel (2052 / 4100:
+# partly filled last float4 groups); 1030 the warp-per-row one
+@pytest.mark.parametrize("B,C", [(4, 10), (64, 10), (3, 1000), (5, 2052), (3, 8192), (7, 4100), (2, 1030)])
 def test_softmax_backward_family(cuda_rt, oracle_rt, B, C):
     rng = np.random.default_rng(17)
     g = rng.standard_normal((B, C)).astype(np.float32)

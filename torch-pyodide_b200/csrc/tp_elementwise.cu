@@ -11,6 +11,7 @@
 
 #include "tp_core.h"
 #include "tp_launch.h"
+#include "tp_fastdiv.cuh"
 
 namespace tp {
 
@@ -154,6 +155,25 @@ __global__ void k_binary_bcast(int op, const float* __restrict__ a, const float*
       ib += c * g.sb[d];
     }
     out[i] = binop(op, a[ia], b[ib]);
+  }
+}
+
+// The common broadcast shapes after dim merging: [R][N] (R = 1 for a scalar
+// operand) where each operand's inner stride is 1 (a full row) or 0 (one value
+// per row), N % 4 == 0: 16-byte accesses along N and the row from one
+// multiply-high instead of a 64-bit divide per dim and element.
+__global__ void k_binary_2d(int op, const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ out,
+                            uint32_t n4, FastDiv fq, int64_t sa0, int sa1, int64_t sb0, int sb1) {
+  ::tp::pdl_enter();
+  const uint32_t stride = gridDim.x * blockDim.x;
+  float4* o4 = reinterpret_cast<float4*>(out);
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+    const uint32_t r = fq.div(i), c = (i - r * fq.d) * 4;
+    const float* pa = a + (int64_t)r * sa0;
+    const float* pb = b + (int64_t)r * sb0;
+    const float4 x = sa1 ? *reinterpret_cast<const float4*>(pa + c) : make_float4(pa[0], pa[0], pa[0], pa[0]);
+    const float4 y = sb1 ? *reinterpret_cast<const float4*>(pb + c) : make_float4(pb[0], pb[0], pb[0], pb[0]);
+    o4[i] = make_float4(binop(op, x.x, y.x), binop(op, x.y, y.y), binop(op, x.z, y.z), binop(op, x.w, y.w));
   }
 }
 
@@ -319,7 +339,20 @@ static int64_t binary_impl(int op, int64_t ida, int64_t idb, tp_handle* out) {
     launch_binary(op, a.f(), b.f(), o.f(), o.numel);
   } else if (o.numel > 0) {
     BcastGeom g = make_geom(oshape, a, &b);
-    TP_LAUNCH(k_binary_bcast, grid_for(o.numel, 256), 256, 0, op, a.f(), b.f(), o.f(), o.numel, g);
+    // [R][N] fast path (see k_binary_2d)
+    const bool two = g.nd == 2;
+    const int64_t N = g.size[g.nd - 1], R = two ? g.size[0] : 1;
+    const int64_t sa1 = g.sa[g.nd - 1], sb1 = g.sb[g.nd - 1], sa0 = two ? g.sa[0] : 0, sb0 = two ? g.sb[0] : 0;
+    const bool fast = g.nd <= 2 && N % 4 == 0 && (sa1 == 0 || sa1 == 1) && (sb1 == 0 || sb1 == 1) &&
+                      (sa1 == 0 || sa0 % 4 == 0) && (sb1 == 0 || sb0 % 4 == 0) && R * N / 4 < ((int64_t)1 << 31) &&
+                      aligned16(a.f()) && aligned16(b.f()) && aligned16(o.f());
+    if (fast) {
+      const int64_t n4 = R * N / 4;
+      TP_LAUNCH(k_binary_2d, grid_for(n4, 256), 256, 0, op, a.f(), b.f(), o.f(), (uint32_t)n4,
+                fast_div((uint32_t)(N / 4)), sa0, (int)sa1, sb0, (int)sb1);
+    } else {
+      TP_LAUNCH(k_binary_bcast, grid_for(o.numel, 256), 256, 0, op, a.f(), b.f(), o.f(), o.numel, g);
+    }
   }
   return emit(o, out);
 }

@@ -642,6 +642,41 @@ __global__ void k_softmax_bwd(const float* __restrict__ go, const float* __restr
   for (int64_t i = lane; i < C; i += 32) gi[row * C + i] = LOG ? g[i] - sr[i] * acc : sr[i] * (g[i] - acc);
 }
 
+// Rows of 256 < C <= 8192, C % 4 == 0, 16-byte aligned: one CTA per row with
+// the row's go and s in registers as float4 (thread t owns columns t + 256 k),
+// so both are read from HBM once (the warp-per-row kernel's second pass re-reads
+// rows that no longer fit in L1).
+template <int V, bool LOG>
+__global__ void __launch_bounds__(256) k_softmax_bwd_vec(const float4* __restrict__ go, const float4* __restrict__ s,
+                                                         float4* __restrict__ gi, int64_t C) {
+  ::tp::pdl_enter();
+  __shared__ float sh[32];
+  const int64_t C4 = C >> 2;
+  const int64_t base = (int64_t)blockIdx.x * C4;
+  float4 g[V], sv[V];
+  float acc = 0.0f;
+#pragma unroll
+  for (int k = 0; k < V; ++k) {
+    const int64_t i = threadIdx.x + (int64_t)k * 256;
+    if (i < C4) {
+      g[k] = go[base + i];
+      sv[k] = s[base + i];
+      acc += LOG ? (g[k].x + g[k].y) + (g[k].z + g[k].w)
+                 : (g[k].x * sv[k].x + g[k].y * sv[k].y) + (g[k].z * sv[k].z + g[k].w * sv[k].w);
+    }
+  }
+  acc = block_reduce<false>(acc, sh);
+#pragma unroll
+  for (int k = 0; k < V; ++k) {
+    const int64_t i = threadIdx.x + (int64_t)k * 256;
+    if (i < C4) {
+      const float4 a = g[k], b = sv[k];
+      gi[base + i] = LOG ? make_float4(a.x - b.x * acc, a.y - b.y * acc, a.z - b.z * acc, a.w - b.w * acc)
+                         : make_float4(b.x * (a.x - acc), b.y * (a.y - acc), b.z * (a.z - acc), b.w * (a.w - acc));
+    }
+  }
+}
+
 // cross_entropy.wgsl: loss[row] = logsumexp(x[row]) - x[row, t], t = clamp(i32(target), 0, C-1).
 __device__ __forceinline__ int ce_target(float t, int64_t C) {
   int ti = (int)t;
@@ -852,7 +887,26 @@ static int softmax_bwd_impl(bool log_mode, int64_t go, int64_t s, int64_t B, int
                (long long)(B * C));
     int64_t shp[2] = {B, C};
     Tensor o = make(shp, 2, g.dtype);
-    if (B * C > 0) {
+    const bool vec = C > 256 && C <= 256 * 32 && C % 4 == 0 && ((uintptr_t)g.f() & 15) == 0 &&
+                     ((uintptr_t)sm.f() & 15) == 0 && ((uintptr_t)o.f() & 15) == 0;
+    if (B * C > 0 && vec) {
+      const float4 *g4 = (const float4*)g.f(), *s4 = (const float4*)sm.f();
+      float4* o4 = (float4*)o.f();
+      const unsigned rows = (unsigned)B;
+#define TP_SMBWD_VEC(V)                                                                           \
+  if (log_mode) TP_LAUNCH((k_softmax_bwd_vec<V, true>), rows, 256, 0, g4, s4, o4, C);           \
+  else TP_LAUNCH((k_softmax_bwd_vec<V, false>), rows, 256, 0, g4, s4, o4, C);
+      if (C <= 256 * 4) {
+        TP_SMBWD_VEC(1)
+      } else if (C <= 256 * 8) {
+        TP_SMBWD_VEC(2)
+      } else if (C <= 256 * 16) {
+        TP_SMBWD_VEC(4)
+      } else {
+        TP_SMBWD_VEC(8)
+      }
+#undef TP_SMBWD_VEC
+    } else if (B * C > 0) {
       unsigned blocks = (unsigned)((B * 32 + 255) / 256);
       if (log_mode) TP_LAUNCH(k_softmax_bwd<true>, blocks, 256, 0, g.f(), sm.f(), o.f(), B, C);
       else TP_LAUNCH(k_softmax_bwd<false>, blocks, 256, 0, g.f(), sm.f(), o.f(), B, C);
