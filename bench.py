@@ -1,21 +1,29 @@
 #!/usr/bin/env python3
 """Benchmark of the B200 backend for the torch-pyodide hot path.
 
-Default workload: the fused AdamW optimizer step over 64 parameter tensors
-cycling [4096,4096], [4096], [1024,4096], [4096,1024] (402,718,720 fp32
-elements), params ~N(0,0.02), grads ~N(0,1e-3), moments zero-initialised and
-warmed for 3 steps.  One step = one fused multi-tensor AdamW launch over the
-whole group; the metric is algorithmic HBM bandwidth, 28 B per element (read
-param, grad, exp_avg, exp_avg_sq; write param, exp_avg, exp_avg_sq).  The
-working set (11.3 GB per step) is ~90x the 126 MB L2, so no flush is needed.
+Default workload (every --gpus N): the VGG-11-BN data-parallel training step,
+global batch 1024 split over the ranks (1024/N images per rank), SGD momentum
+0.9, weight decay 5e-4, lr 0.05; input [B,3,32,32] ~N(0,1), labels uniform in
+[0,10).  One step = forward, backward, the bucketed NCCL gradient all-reduce
+overlapped with backward, and the fused SGD update, replayed as one CUDA
+graph per rank.  value = 1024 images / the slowest rank's step time.
 
-Multi-GPU: the optimizer step does not shard (each rank updates its own
-replica), so --gpus N runs N independent replicas, one process per GPU; value is
-the bytes all ranks moved divided by the slowest rank's time.
+At N = 1 the same JSON line also carries, under "adamw", the other half of the
+headline metric: the fused AdamW optimizer step over 64 parameter tensors
+cycling [4096,4096], [4096], [1024,4096], [4096,1024] (402,718,720 fp32
+elements; params ~N(0,0.02), grads ~N(0,1e-3), moments zero-initialised and
+warmed for 3 steps), one multi-tensor launch per step, 28 B of HBM traffic per
+element (read param, grad, exp_avg, exp_avg_sq; write param, exp_avg,
+exp_avg_sq).  Its working set (11.3 GB per step) is ~90x the 126 MB L2.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload vgg|adamw|ops|conv|tiny]
 
-Prints one JSON line on rank 0.
+--impl reference times the reference algorithm on the host cores (the oracle:
+a C/OpenMP restatement of the reference's WGSL shaders, which cannot run here
+without a WebGPU device) for the same workload and metric; under torchrun only
+rank 0 runs it.  Ranks meet through tpcuda.store (a file rendezvous), not
+torch.distributed.  Prints one JSON line on rank 0.
 """
 from __future__ import annotations
 
@@ -120,12 +128,19 @@ def dist_setup(gpus):
     return rank, world, local
 
 
+def make_store(rank, world):
+    """The ranks' rendezvous (tpcuda.store): NCCL unique id, barriers, max over ranks."""
+    from tpcuda.store import FileStore
+    return FileStore(rank, world, timeout_s=300)
+
+
 # ---------------------------------------------------------------------------
 # CPU arms: the oracle (a C/OpenMP restatement of adamw_step.wgsl)
 
-def cpu_adamw(sample_tensors: int, steps: int) -> dict:
+def cpu_adamw(sample_tensors: int, steps: int, warmup: int = 1) -> dict:
     """Time the oracle's AdamW on the first `sample_tensors` tensors of the
-    workload with all host threads; returns GB/s of algorithmic traffic."""
+    workload (64 = the whole workload) with the host threads OMP_NUM_THREADS
+    allows; returns GB/s of algorithmic traffic (28 B per element)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import numpy as np
     import oracle_runtime as O
@@ -134,8 +149,8 @@ def cpu_adamw(sample_tensors: int, steps: int) -> dict:
     ts = []
     for i in range(sample_tensors):
         n = numel(SHAPES[i % 4])
-        p = (rng.standard_normal(n, dtype=np.float32) * 0.02)
-        g = (rng.standard_normal(n, dtype=np.float32) * 1e-3)
+        p = (rng.standard_normal(n, dtype=np.float32) * np.float32(0.02))
+        g = (rng.standard_normal(n, dtype=np.float32) * np.float32(1e-3))
         ts.append((p, g, np.zeros(n, np.float32), np.zeros(n, np.float32)))
     elems = sum(t[0].size for t in ts)
 
@@ -144,64 +159,99 @@ def cpu_adamw(sample_tensors: int, steps: int) -> dict:
         for p, g, m, v in ts:
             L.or_adamw_step(O.fp(p), O.fp(g), O.fp(m), O.fp(v), p.size, LR, B1, B2, EPS, WD, ss, isb)
 
-    step(1)  # warm-up
+    for k in range(max(1, warmup)):
+        step(k + 1)
     times = []
     for k in range(steps):
         t0 = time.perf_counter()
-        step(k + 2)
+        step(k + 1 + max(1, warmup))
         times.append(time.perf_counter() - t0)
     t = statistics.median(times)
     return {"gbs": BYTES_PER_ELEM * elems / t / 1e9, "elems": elems, "sec": t, "times": times}
 
 
+VGG_CPU_BATCH = 16  # images per oracle step: the bounded CPU sample of the 1024-image step
+
+
 def run_reference(args, rank, world):
-    """--impl reference: the reference algorithm on host cores (the WGSL
-    shaders cannot run here: there is no WebGPU device), same metric."""
+    """--impl reference: the reference algorithm of the same workload on the
+    host cores (the reference's WGSL shaders cannot run here: there is no
+    WebGPU device; the oracle restates their arithmetic in C/OpenMP), same
+    metric, unit and config.  Rank 0 alone runs it."""
     if rank != 0:
         return
     cores = os.cpu_count() or 1
-    os.environ.setdefault("OMP_NUM_THREADS", str(cores))
-    sample = 8
-    r = cpu_adamw(sample, max(1, args.steps))
-    elems = r["elems"]
-    line = {
-        "impl": "reference", "metric": "fused AdamW HBM GB/s", "value": round(r["gbs"], 3), "unit": "GB/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(r["sec"] * 1e3, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "adamw 64 tensors cycling [4096,4096],[4096],[1024,4096],[4096,1024]",
-                   "sample": f"first {sample} tensors ({elems} elements) per step"},
-        "cpu_baseline": {"value": round(r["gbs"], 3), "unit": "GB/s", "cores": cores, "kind": "port",
-                         "sample": f"{sample} of 64 tensors, {elems} elements, median of {len(r['times'])} steps"},
-        "e2e": {"value": round(r["gbs"], 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
+    os.environ["OMP_NUM_THREADS"] = str(cores)
+    steps, warmup = max(1, args.steps), max(1, args.warmup)
+    if args.workload == "tiny":
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        from oracle_runtime import OracleRuntime
+        orc = OracleRuntime()
+        calls = json.load(open(TINY_TRACE))["calls"]
+        for _ in range(max(1, warmup // 10)):
+            replay_trace(orc, calls)
+        t = []
+        for _ in range(max(1, steps // 10)):
+            t += replay_trace(orc, calls)[0]
+        ms = statistics.median(t) * 1e3
+        line = {"impl": "reference", "metric": "Tiny CNN train step (replayed reference runtime-call stream)",
+                "value": round(ms, 4), "unit": "ms/step", "n_gpus": args.gpus, "steps": len(t),
+                "warmup": 10 * max(1, warmup // 10), "ms_per_step": round(ms, 4), "higher_is_better": False,
+                "scaling": "replicas only", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": "Tiny CNN, batch 64, Adam lr 1e-3, 10 recorded steps per replay"},
+                "cpu_baseline": {"value": round(ms, 4), "unit": "ms/step", "cores": cores, "kind": "port",
+                                 "sample": "the recorded 10-step stream on the oracle runtime"},
+                "e2e": {"value": round(ms, 4), "unit": "ms/step", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    elif args.workload == "adamw":
+        r = cpu_adamw(NTENSORS, steps, warmup)
+        elems = r["elems"]
+        line = {
+            "impl": "reference", "metric": "fused AdamW HBM GB/s", "value": round(r["gbs"], 3), "unit": "GB/s",
+            "n_gpus": args.gpus, "steps": steps, "warmup": warmup, "ms_per_step": round(r["sec"] * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": ADAMW_WORKLOAD, "same_config": True, "elements": elems},
+            "cpu_baseline": {"value": round(r["gbs"], 3), "unit": "GB/s", "cores": cores, "kind": "port",
+                             "sample": f"all 64 tensors ({elems} elements), median of {len(r['times'])} steps"},
+            "e2e": {"value": round(r["gbs"], 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
+    else:
+        r = cpu_vgg(VGG_CPU_BATCH, steps, warmup)
+        line = {
+            "impl": "reference", "metric": "VGG-11-BN train imgs/s", "value": round(r["imgs_per_s"], 4),
+            "unit": "imgs/s", "n_gpus": args.gpus, "steps": steps, "warmup": warmup,
+            "ms_per_step": round(r["sec"] * 1e3, 3), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": VGG_WORKLOAD, "global_batch": VGG_GLOBAL_BATCH,
+                       "sample": f"{VGG_CPU_BATCH} images per step (model resident, SGD each step)"},
+            "cpu_baseline": {"value": round(r["imgs_per_s"], 4), "unit": "imgs/s", "cores": cores, "kind": "port",
+                             "sample": f"oracle VGG-11-BN step at batch {VGG_CPU_BATCH}, median of {steps} steps"},
+            "e2e": {"value": round(r["imgs_per_s"], 4), "unit": "imgs/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+        }
     print(json.dumps(line), flush=True)
 
 
 # ---------------------------------------------------------------------------
+# The fused AdamW step (device-resident and end to end)
 
-def run_ours(args, rank, world, local):
+ADAMW_WORKLOAD = "adamw 64 tensors cycling [4096,4096],[4096],[1024,4096],[4096,1024]"
+
+
+def measure_adamw(args, rt, rank, world, store, ntensors):
+    """Build the 64-tensor AdamW workload with the library's own creation
+    kernels, warm the moments for 3 steps, then time --steps fused launches
+    (device-resident) and end-to-end steps (grads copied from pinned host
+    memory through the C ABI, one value read back).  Returns a dict."""
     import ctypes
 
     import numpy as np
     import torch
-    import torch.distributed as dist
-
-    torch.cuda.set_device(local)
-    if world > 1:
-        dist.init_process_group("nccl", init_method="env://", device_id=torch.device("cuda", local),
-                                timeout=__import__("datetime").timedelta(seconds=300))
-    from tpcuda import CudaRuntime
     from tpcuda._lib import check
-    rt = CudaRuntime(local)
     lib = rt.lib
-    stream = torch.cuda.ExternalStream(rt.stream(), device=torch.device("cuda", local))
-
-    # parameters and state, built with the library's own creation kernels
+    stream = torch.cuda.ExternalStream(rt.stream(), device=torch.device("cuda", torch.cuda.current_device()))
     rt.setSeed(1000 + rank)
     P, G, M, V = [], [], [], []
-    nt = args.tensors
-    for i in range(nt):
+    for i in range(ntensors):
         s = SHAPES[i % 4]
         P.append(rt.normal(s, "float32", 0.0, 0.02))
         G.append(rt.normal(s, "float32", 0.0, 1e-3))
@@ -209,10 +259,9 @@ def run_ours(args, rank, world, local):
         V.append(rt.zeros(s, "float32"))
     elems = sum(numel(h["shape"]) for h in P)
     ptr = lambda hs: (ctypes.c_void_p * len(hs))(*[rt.devicePtr(h["id"]) for h in hs])  # noqa: E731
-    numels = (ctypes.c_int64 * nt)(*[numel(h["shape"]) for h in P])
+    numels = (ctypes.c_int64 * ntensors)(*[numel(h["shape"]) for h in P])
     group = ctypes.c_int64(0)
-    check(lib.tpk_group_create(nt, ptr(P), ptr(G), ptr(M), ptr(V), numels, ctypes.byref(group)))
-
+    check(lib.tpk_group_create(ntensors, ptr(P), ptr(G), ptr(M), ptr(V), numels, ctypes.byref(group)))
     step_no = [0]
 
     def step():
@@ -222,25 +271,22 @@ def run_ours(args, rank, world, local):
 
     # 3 warm steps of the moments with regenerated grads (seed + step)
     for k in range(3):
-        for i, h in enumerate(G):
+        for h in G:
             rt.destroy(h["id"])
         rt.setSeed(2000 + 97 * rank + k)
-        G = [rt.normal(SHAPES[i % 4], "float32", 0.0, 1e-3) for i in range(nt)]
+        G = [rt.normal(SHAPES[i % 4], "float32", 0.0, 1e-3) for i in range(ntensors)]
         check(lib.tpk_group_destroy(group.value))
-        check(lib.tpk_group_create(nt, ptr(P), ptr(G), ptr(M), ptr(V), numels, ctypes.byref(group)))
+        check(lib.tpk_group_create(ntensors, ptr(P), ptr(G), ptr(M), ptr(V), numels, ctypes.byref(group)))
         step()
     for _ in range(args.warmup):
         step()
     rt.synchronize()
 
     def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
         rt.synchronize()
+        store.barrier()
 
-    # ---- device-resident timed region ----
-    clocks = ClockSampler(local)
+    clocks = ClockSampler(torch.cuda.current_device())
     barrier()
     clocks.start()
     launches0 = rt.kernelLaunches()
@@ -253,18 +299,14 @@ def run_ours(args, rank, world, local):
     launches = rt.kernelLaunches() - launches0
     clk = clocks.stop()
     ms = e0.elapsed_time(e1)
-    t = torch.tensor([ms], device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
-    ms_step = ms_max / args.steps
+    ms_step = store.max(ms) / args.steps
     total_bytes = BYTES_PER_ELEM * elems * world
     value = total_bytes / (ms_step * 1e-3) / 1e9
     kernel_gbs = BYTES_PER_ELEM * elems / (ms / args.steps * 1e-3) / 1e9
 
     # ---- end to end through the handle-level C ABI, grads from pinned host ----
-    host_g = [torch.empty(numel(SHAPES[i % 4]), dtype=torch.float32, pin_memory=True) for i in range(nt)]
-    for i, hg in enumerate(host_g):
+    host_g = [torch.empty(numel(SHAPES[i % 4]), dtype=torch.float32, pin_memory=True) for i in range(ntensors)]
+    for hg in host_g:
         hg.normal_(0.0, 1e-3)
     ids = lambda hs: [h["id"] for h in hs]  # noqa: E731
     gptr = [rt.devicePtr(h["id"]) for h in G]
@@ -289,49 +331,55 @@ def run_ours(args, rank, world, local):
         e2e_step()
     f1.record(stream)
     f1.synchronize()
-    t2 = torch.tensor([f0.elapsed_time(f1)], device="cuda")
-    if world > 1:
-        dist.all_reduce(t2, op=dist.ReduceOp.MAX)
-    e2e_ms = float(t2.item()) / e2e_steps
+    e2e_ms = store.max(f0.elapsed_time(f1)) / e2e_steps
     e2e_value = total_bytes / (e2e_ms * 1e-3) / 1e9
-
-    line = None
-    if rank == 0:
-        peak, peak_kind = measured_peaks()
-        line = {
-            "metric": "fused AdamW HBM GB/s", "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic",
-            "config": {"workload": "adamw 64 tensors cycling [4096,4096],[4096],[1024,4096],[4096,1024]",
-                       "elements_per_rank": elems, "bytes_per_element": BYTES_PER_ELEM,
-                       "l2": "working set 11.3 GB per step >> 126 MB L2, no flush",
-                       "parallelism": f"replicas x{world}", "lr": LR, "betas": [B1, B2], "eps": EPS,
-                       "weight_decay": WD},
-            "gpu_launches": int(launches),
-            "clocks": clk,
-            "roofline": {"bound": "hbm", "achieved": round(kernel_gbs, 2), "peak": peak, "unit": "GB/s",
-                         "frac": round(kernel_gbs / peak, 4), "traffic": None,
-                         "peak_source": f"{peak_kind} hbm_gbs", "kernel": "k_adam_multi<true>"},
-            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": 4,
-                    "path": "tp_memcpy_h2d(pinned grads) + tp_adamw_step_multi(ids) + tp_memcpy_d2h"},
-        }
-        tf = os.path.join(ROOT, "profiles", "adamw_traffic.json")
-        if os.path.exists(tf):
-            line["roofline"]["traffic"] = json.load(open(tf)).get("bytes_per_launch")
     check(lib.tpk_group_destroy(group.value))
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    for h in P + G + M + V:
+        rt.destroy(h["id"])
+    del host_g
+    rt.synchronize()
+    peak, peak_kind = measured_peaks()
+    rec = {
+        "metric": "fused AdamW HBM GB/s", "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": ADAMW_WORKLOAD, "elements_per_rank": elems, "bytes_per_element": BYTES_PER_ELEM,
+                   "l2": "working set 11.3 GB per step >> 126 MB L2, no flush",
+                   "parallelism": f"replicas x{world}", "lr": LR, "betas": [B1, B2], "eps": EPS,
+                   "weight_decay": WD},
+        "gpu_launches": int(launches),
+        "clocks": clk,
+        "roofline": {"bound": "hbm", "achieved": round(kernel_gbs, 2), "peak": peak, "unit": "GB/s",
+                     "frac": round(kernel_gbs / peak, 4), "traffic": None,
+                     "peak_source": f"{peak_kind} hbm_gbs", "kernel": "k_adam_multi<true>"},
+        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
+                "path": "tp_memcpy_h2d(pinned grads) + tp_adamw_step_multi(ids) + tp_memcpy_d2h"},
+    }
+    tf = os.path.join(ROOT, "profiles", "adamw_traffic.json")
+    if os.path.exists(tf):
+        rec["roofline"]["traffic"] = json.load(open(tf)).get("bytes_per_launch")
+    return rec
+
+
+def adamw_cpu_baseline():
+    os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
+    r = cpu_adamw(8, 5)
+    return {"value": round(r["gbs"], 3), "unit": "GB/s", "cores": int(os.environ["OMP_NUM_THREADS"]),
+            "kind": "port", "sample": f"oracle AdamW on 8 of 64 tensors ({r['elems']} elements), median of 5 steps"}
+
+
+def run_ours(args, rank, world, local):
+    """--workload adamw: the fused AdamW step alone (N replicas for --gpus N)."""
+    import torch
+    torch.cuda.set_device(local)
+    from tpcuda import CudaRuntime
+    rt = CudaRuntime(local)
+    store = make_store(rank, world)
+    line = measure_adamw(args, rt, rank, world, store, args.tensors)
+    store.close()
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
-            os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
-            r = cpu_adamw(8, 5)
-            line["cpu_baseline"] = {"value": round(r["gbs"], 3), "unit": "GB/s", "cores": os.cpu_count() or 1,
-                                    "kind": "port",
-                                    "sample": f"oracle AdamW on 8 of 64 tensors ({r['elems']} elements), "
-                                              f"median of 5 steps"}
+            line["cpu_baseline"] = adamw_cpu_baseline()
         print(json.dumps(line), flush=True)
 
 
@@ -354,14 +402,9 @@ def tf32x3_peak():
     return 1590.0 / 2 / 3, 1590.0, "fallback"
 
 
-def cpu_vgg(batch: int, steps: int) -> dict:
-    """The oracle composition of the same training step, on host cores."""
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import numpy as np
-    from oracle_runtime import OracleRuntime
-    from vgg_oracle import oracle_step
-
-    class Plan:  # the block plan of tpcuda.vgg without touching the GPU
+def vgg_plan_cpu():
+    """The VGG-11-BN block plan (tpcuda.vgg's) built without touching the GPU."""
+    class Plan:
         blocks = []
 
     cfg = [64, "M", 128, "M", 256, 256, "M", 512, 512, "M", 512, 512, "M"]
@@ -372,7 +415,21 @@ def cpu_vgg(batch: int, steps: int) -> dict:
         cin = cfg[i]
         H = H // 2 if pool else H
         i += 2 if pool else 1
-    rng = np.random.default_rng(0)
+    return Plan
+
+
+def cpu_vgg_trainer(batch: int, seed: int = 0):
+    """The oracle composition of the VGG-11-BN training step (conv, BN train,
+    ReLU, max-pool with indices, linear, cross-entropy, their backward rules,
+    multi-tensor SGD momentum 0.9 wd 5e-4 lr 0.05), model resident in the
+    oracle runtime; returns (trainer, x, y) for a seeded batch."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    from oracle_runtime import OracleRuntime
+    from vgg_oracle import OracleTrainer
+
+    Plan = vgg_plan_cpu()
+    rng = np.random.default_rng(seed)
     params = {"fc.w": (rng.uniform(-0.04, 0.04, 5120).astype(np.float32), [10, 512]),
               "fc.b": (np.zeros(10, np.float32), [10])}
     stats = []
@@ -386,14 +443,22 @@ def cpu_vgg(batch: int, steps: int) -> dict:
         stats.append((np.zeros(b["cout"], np.float32), np.ones(b["cout"], np.float32)))
     x = rng.standard_normal((batch, 3, 32, 32)).astype(np.float32)
     y = rng.integers(0, 10, batch).astype(np.float32)
-    orc = OracleRuntime()
+    return OracleTrainer(OracleRuntime(), Plan, params, stats, 0.05, 0.9, 5e-4), x, y
+
+
+def cpu_vgg(batch: int, steps: int, warmup: int = 1) -> dict:
+    """Time the oracle's VGG-11-BN training step at `batch` images on the host
+    cores (OpenMP threads = OMP_NUM_THREADS); median over `steps` timed steps."""
+    tr, x, y = cpu_vgg_trainer(batch)
+    for _ in range(warmup):
+        tr.step(x, y)
     times = []
-    for _ in range(steps + 1):
+    for _ in range(steps):
         t0 = time.perf_counter()
-        oracle_step(orc, Plan, params, x, y, stats, 0.05, 0.9, 5e-4)
+        tr.step(x, y)
         times.append(time.perf_counter() - t0)
-    t = statistics.median(times[1:])
-    return {"imgs_per_s": batch / t, "sec": t, "batch": batch}
+    t = statistics.median(times)
+    return {"imgs_per_s": batch / t, "sec": t, "batch": batch, "times": times}
 
 
 def run_ops(args):
@@ -756,18 +821,15 @@ def run_vgg(args, rank, world, local):
 
     import numpy as np
     import torch
-    import torch.distributed as dist
 
     torch.cuda.set_device(local)
-    if world > 1:
-        dist.init_process_group("nccl", init_method="env://", device_id=torch.device("cuda", local),
-                                timeout=__import__("datetime").timedelta(seconds=300))
     from tpcuda import CudaRuntime
-    from tpcuda.dp import comm_from_torch_dist
+    from tpcuda.dp import comm_from_store
     from tpcuda.vgg import VGG11BN
     rt = CudaRuntime(local)
+    store = make_store(rank, world)
     stream = torch.cuda.ExternalStream(rt.stream(), device=torch.device("cuda", local))
-    comm = comm_from_torch_dist(rt.lib)
+    comm = comm_from_store(rt.lib, store)
     B = VGG_GLOBAL_BATCH // world
     model = VGG11BN(rt, B, seed=0, world=world, comm=comm)
     rng = np.random.default_rng(100 + rank)
@@ -780,16 +842,8 @@ def run_vgg(args, rank, world, local):
     rt.synchronize()
 
     def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
         rt.synchronize()
-
-    def tmax(ms):
-        t = torch.tensor([ms], device="cuda")
-        if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        store.barrier()
 
     # ---- device-resident timed region: graph replays of the whole step ----
     clocks = ClockSampler(local)
@@ -804,7 +858,7 @@ def run_vgg(args, rank, world, local):
     e1.synchronize()
     launches = rt.kernelLaunches() - launches0
     clk = clocks.stop()
-    ms_step = tmax(e0.elapsed_time(e1)) / args.steps
+    ms_step = store.max(e0.elapsed_time(e1)) / args.steps
     value = VGG_GLOBAL_BATCH / (ms_step * 1e-3)
     loss_after = model.read_loss()
 
@@ -819,7 +873,7 @@ def run_vgg(args, rank, world, local):
         model.read_loss()
     f1.record(stream)
     f1.synchronize()
-    e2e_ms = tmax(f0.elapsed_time(f1)) / e2e_steps
+    e2e_ms = store.max(f0.elapsed_time(f1)) / e2e_steps
     e2e_value = VGG_GLOBAL_BATCH / (e2e_ms * 1e-3)
 
     # ---- dominant kernel: the implicit-GEMM convolution of block 4 (256->256 @ 8x8),
@@ -850,15 +904,22 @@ def run_vgg(args, rank, world, local):
     n_sm = torch.cuda.get_device_properties(local).multi_processor_count
     cuda_peak = n_sm * 128 * 2 * sm_mhz_max * 1e6 / 1e12
     sr = model.step_roofline_ms(peak3, cuda_peak, hbm_peak)
+    gemm_status = ctypes.c_int(0)
+    lib.tp_gemm_status(ctypes.byref(gemm_status), 1)
 
     if comm is not None:
         comm.sync(60000)
     model.close()
     if comm is not None:
         comm.close()
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    del hx, hy
+    barrier()
+
+    # ---- the fused AdamW step (the metric's other half), on one GPU ----
+    adamw = None
+    if world == 1 and not args.no_adamw:
+        adamw = measure_adamw(args, rt, rank, world, store, args.tensors)
+    store.close()
     if rank != 0:
         return
     line = {
@@ -867,7 +928,9 @@ def run_vgg(args, rank, world, local):
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": VGG_WORKLOAD, "global_batch": VGG_GLOBAL_BATCH, "per_rank_batch": B,
                    "parallelism": f"dp{world}", "l2": "per-step activations ~1.6 GB per rank at batch 1024 > L2",
-                   "loss_after_timed_steps": round(loss_after, 5)},
+                   "loss_after_timed_steps": round(loss_after, 5),
+                   "collective": "bucketed NCCL all-reduce of the gradients, overlapped with backward" if world > 1
+                   else "none (one rank)"},
         "gpu_launches": int(launches),
         "clocks": clk,
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak3, 1), "unit": "TFLOP/s",
@@ -876,9 +939,12 @@ def run_vgg(args, rank, world, local):
                      "kernel": ("conv3x3 forward, TMA-fed tcgen05 implicit GEMM, channels-last"
                                 if model.layout == "nhwc" else "conv3x3 forward, gather-GEMM, NCHW")
                      + ", block 4 (256->256 @ 8x8)",
-                     "kernel_ms": round(k_ms, 4), "step_tflops": round(model.step_flops() * world / 1e12, 4)},
-        "e2e": {"value": round(e2e_value, 1), "unit": "imgs/s", "h2d_bytes_per_step": int(hx.numel() * 4 + hy.numel() * 4),
-                "d2h_bytes_per_step": 4, "path": "tp_memcpy_h2d(pinned batch) + tp_graph_launch(step) + loss readback"},
+                     "kernel_ms": round(k_ms, 4), "step_tflops": round(model.step_flops() * world / 1e12, 4),
+                     "gemm_status": gemm_status.value},
+        "e2e": {"value": round(e2e_value, 1), "unit": "imgs/s",
+                "h2d_bytes_per_step": int(VGG_GLOBAL_BATCH * (3 * 32 * 32 + 1) * 4),
+                "d2h_bytes_per_step": 4 * world,
+                "path": "per rank: tp_memcpy_h2d(pinned batch) + tp_graph_launch(step) + loss readback"},
         "step_roofline": {"min_ms": round(sr["min_ms"], 4), "frac": round(sr["min_ms"] / ms_step, 4),
                           "tensor_ms": round(sr["tensor_ms"], 4), "cuda_core_ms": round(sr["cuda_core_ms"], 4),
                           "hbm_ms": round(sr["hbm_ms"], 4), "hbm_gb": round(sr["hbm_bytes"] / 1e9, 3),
@@ -895,10 +961,15 @@ def run_vgg(args, rank, world, local):
         line["roofline"]["traffic"] = int(t["bytes_per_launch"] * B / t["batch"])
     if world == 1 and not args.no_cpu_baseline:
         os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
-        r = cpu_vgg(2, 2)
-        line["cpu_baseline"] = {"value": round(r["imgs_per_s"], 4), "unit": "imgs/s", "cores": os.cpu_count() or 1,
-                                "kind": "port", "sample": "oracle composition of the same step at batch 2, "
-                                                          "median of 2 steps"}
+        r = cpu_vgg(VGG_CPU_BATCH, 3)
+        line["cpu_baseline"] = {"value": round(r["imgs_per_s"], 4), "unit": "imgs/s",
+                                "cores": int(os.environ["OMP_NUM_THREADS"]), "kind": "port",
+                                "sample": f"oracle composition of the same step at batch {VGG_CPU_BATCH} (model "
+                                          f"resident, SGD each step), median of 3 steps after 1 warm-up"}
+    if adamw is not None:
+        if not args.no_cpu_baseline:
+            adamw["cpu_baseline"] = adamw_cpu_baseline()
+        line["adamw"] = adamw
     print(json.dumps(line), flush=True)
 
 
@@ -908,7 +979,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["adamw", "vgg", "ops", "conv", "tiny"], default="adamw")
+    ap.add_argument("--workload", choices=["vgg", "adamw", "ops", "conv", "tiny"], default="vgg")
     ap.add_argument("--conv", default="256,256,8", help="--workload conv: Cin,Cout,H=W of the layer")
     ap.add_argument("--pass", dest="pass_", choices=["fwd", "dgrad", "wgrad"], default="fwd",
                     help="--workload conv: which pass")
@@ -917,6 +988,7 @@ def main():
                     help="--workload conv: 1 = [Cout][3][3][Cin] (the step's), 0 = [Cout][Cin][3][3] (with Cin = 4: "
                          "the first layer's CUDA-core kernels)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-adamw", action="store_true", help="vgg workload at N=1: skip the fused AdamW sub-record")
     ap.add_argument("--launch-list", action="store_true",
                     help="profiling aid: two eager VGG steps at --batch with launch counts (1 GPU, no timing)")
     ap.add_argument("--batch", type=int, default=VGG_GLOBAL_BATCH, help="per-GPU batch for --launch-list")

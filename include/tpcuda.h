@@ -245,8 +245,17 @@ TP_API int tp_set_gemm_path(int path);
  * after the call. */
 TP_API int tp_set_pdl(int on);
 /* synchronises, then reports the tensor-core kernel's status word: 0 = ok,
- * else the code of a bounded wait that expired; reset != 0 clears it */
+ * else the code of a bounded wait that expired; reset != 0 clears it.
+ * tp_synchronize and tp_comm_sync read (and clear) the same word and return
+ * TP_ERR_TIMEOUT when it is set, so an expired wait reaches every caller that
+ * synchronises. */
 TP_API int tp_gemm_status(int* out, int reset);
+/* New, for testing the path above: one CTA waits on an mbarrier nothing
+ * arrives on, with the tensor-core kernels' own bounded-wait function and a
+ * limit of limit_ns (1e3 .. 2e9); the wait runs out, records code 99 in the
+ * status word and the kernel returns.  No copy or tensor memory is involved.
+ * The next tp_synchronize then returns TP_ERR_TIMEOUT. */
+TP_API int tp_wait_probe(int64_t limit_ns);
 
 /* ---- pooling (poolingOps.ts:18-48, max_pool2d.wgsl:22-49) ------------------------ */
 TP_API int tp_max_pool2d(int64_t input, const int64_t* kernel, int nk, const int64_t* stride, int ns,
@@ -432,9 +441,10 @@ TP_API int tpk_cross_entropy_mean(const float* logits, const float* targets, flo
  * caller passes only inputs and the one-float output; the per-row losses and
  * reduction partials live in a fixed device array reserved when the library
  * loads (about 1 MB per GPU, kept until exit), so B <= 262144 rows, larger B is
- * rejected with TP_ERR_ARG.  The first call on a device looks up that array's
- * address; make it before any stream capture.  Calls share the array: calls
- * that overlap on the GPU race. */
+ * rejected with TP_ERR_ARG; B = 0 writes 0, as tpk_cross_entropy_mean does.
+ * The first call on a device looks up that array's address (guarded, so
+ * concurrent first calls are safe); make it before any stream capture.  Calls
+ * share the array: calls that overlap on the GPU race. */
 TP_API int tpk_cross_entropy_mean_noalloc(const float* logits, const float* targets, float* loss_mean, int64_t B,
                                           int64_t C);
 /* grad = (softmax(logits) - onehot(target)) * scale (cross_entropy_backward.wgsl) */

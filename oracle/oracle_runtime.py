@@ -278,6 +278,10 @@ class OracleRuntime:
     # ---- creation (creationOps.ts) ---------------------------------------
     def tensorFromData(self, data, shape, dtype):
         n = _prod(shape)
+        if isinstance(data, np.ndarray) and dtype.startswith("float"):
+            if data.size != n:
+                raise RuntimeError(f"tensorFromData expected {n} values, got {data.size}.")
+            return self._reg(np.array(data, dtype=np.float32).reshape(-1), shape, dtype)
         vals = list(data)
         if len(vals) != n:
             raise RuntimeError(f"tensorFromData expected {n} values, got {len(vals)}.")

@@ -1,5 +1,6 @@
 """One rank of the data-parallel VGG-11-BN check, launched by
-tests/test_gpu_dp.py through torch.distributed.run (one process per GPU).
+tests/test_gpu_dp.py through torch.distributed.run (one process per GPU; the
+ranks meet through tpcuda.store, not torch.distributed).
 
 Per rank, on its shard of a seeded global batch:
   1. a single-GPU model (no communicator) takes one eager step: its gradient
@@ -11,7 +12,6 @@ Per rank, on its shard of a seeded global batch:
      included) and replayed a few steps.
 Rank 0 writes the comparisons to the JSON file named by argv[1].
 """
-import datetime
 import json
 import os
 import sys
@@ -20,30 +20,24 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(os.path.dirname(HERE), "torch-pyodide_b200"))
 
 import numpy as np  # noqa: E402
-import torch  # noqa: E402
-import torch.distributed as dist  # noqa: E402
 
 from tpcuda import CudaRuntime  # noqa: E402
-from tpcuda.dp import comm_from_torch_dist  # noqa: E402
+from tpcuda.dp import comm_from_store, env_ranks  # noqa: E402
+from tpcuda.store import FileStore  # noqa: E402
 from tpcuda.vgg import VGG11BN  # noqa: E402
 
 PER_RANK = 8
 REPLAYS = 3
 
 
-def gather(vec: np.ndarray, world: int) -> list[np.ndarray]:
-    t = torch.from_numpy(vec).cuda()
-    out = [torch.empty_like(t) for _ in range(world)]
-    dist.all_gather(out, t)
-    return [o.cpu().numpy() for o in out]
-
-
 def main(out_path: str) -> None:
-    rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
-    torch.cuda.set_device(local)
-    dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=datetime.timedelta(seconds=120))
+    rank, world, local = env_ranks()
+    store = FileStore(rank, world, timeout_s=120)
     rt = CudaRuntime(local)
-    comm = comm_from_torch_dist(rt.lib)
+    comm = comm_from_store(rt.lib, store)
+
+    def gather(vec: np.ndarray, world: int) -> list[np.ndarray]:
+        return store.all_gather_array(vec)
     rng = np.random.default_rng(7)
     x = rng.standard_normal((PER_RANK * world, 3, 32, 32)).astype(np.float32)[rank * PER_RANK:(rank + 1) * PER_RANK]
     y = rng.integers(0, 10, PER_RANK * world).astype(np.float32)[rank * PER_RANK:(rank + 1) * PER_RANK]
@@ -82,8 +76,7 @@ def main(out_path: str) -> None:
     params2 = gather(dp.read(dp.params, dp.flat_len), world)
     dp.close()
     comm.close()
-    dist.barrier()
-    dist.destroy_process_group()
+    store.close()
     if rank == 0:
         scale = float(np.max(np.abs(expect)))
         res = {

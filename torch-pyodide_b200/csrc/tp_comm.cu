@@ -164,6 +164,8 @@ TP_API int tp_comm_sync(int timeout_ms) {
       }
       std::this_thread::sleep_for(std::chrono::microseconds(200));
     }
+    const int st = tc_status(true);
+    if (st) fail(TP_ERR_TIMEOUT, "a device-side wait gave up (code %d): this step's results are incomplete", st);
   });
 }
 

@@ -228,6 +228,25 @@ TP_API int tp_set_gemm_path(int path) {
   });
 }
 
+// One CTA waits, bounded by limit_ns, on an mbarrier that nothing arrives on:
+// the wait function of the tensor-core kernels runs out, records `code` in the
+// status word and returns.  No copy or tensor memory is involved.
+__global__ void k_wait_probe(unsigned long long limit_ns, int code) {
+  ::tp::pdl_enter();
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) tc::mbar_init(&bar, 1);
+  __syncthreads();
+  if (threadIdx.x == 0) tc::mbar_wait_for(&bar, 0, code, limit_ns);
+  __syncthreads();
+}
+
+TP_API int tp_wait_probe(int64_t limit_ns) {
+  return guard([&] {
+    TP_REQUIRE(limit_ns >= 1000 && limit_ns <= 2000000000, "tp_wait_probe: limit_ns must be in [1e3, 2e9]");
+    TP_LAUNCH(k_wait_probe, 1, 32, 0, (unsigned long long)limit_ns, 99);
+  });
+}
+
 TP_API int tp_gemm_status(int* out, int reset) {
   return guard([&] {
     TP_CUDA(cudaStreamSynchronize(stream()));

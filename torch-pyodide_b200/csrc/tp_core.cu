@@ -268,6 +268,11 @@ TP_API int tp_synchronize(void) {
     ensure_init();
     TP_CUDA(cudaStreamSynchronize(g_stream));
     if (g_aux) TP_CUDA(cudaStreamSynchronize(g_aux));
+    // A tensor-core kernel whose bounded wait ran out skipped its output: the
+    // results queued so far are not to be trusted, so the caller hears of it.
+    const int st = tc_status(true);
+    if (st) fail(TP_ERR_TIMEOUT, "a device-side wait gave up (code %d): the results of the work synchronised are "
+                                 "incomplete", st);
   });
 }
 

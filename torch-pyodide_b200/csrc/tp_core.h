@@ -87,6 +87,11 @@ cudaStream_t stream();
 int device();
 int sm_count();
 
+// First nonzero code a bounded device-side wait of a tensor-core kernel
+// recorded since the last reset (0: none); reset clears it.  Reading it copies
+// from device memory, so call it only once the library streams are idle.
+int tc_status(bool reset);
+
 // ---- allocator -----------------------------------------------------------
 void* dalloc(size_t bytes);
 void dfree(void* p);

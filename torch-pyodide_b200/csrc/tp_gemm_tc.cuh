@@ -70,17 +70,23 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait; returns false (and records `code`) if the phase never completed.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
+// Bounded wait; returns false (and records `code`) if the phase never
+// completed within limit_ns.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, int code,
+                                              unsigned long long limit_ns) {
   if (mbar_try(bar, parity)) return true;
   unsigned long long t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try(bar, parity)) return true;
-    if ((i & 255) == 0 && globaltimer() - t0 > WAIT_NS) {
+    if ((i & 255) == 0 && globaltimer() - t0 > limit_ns) {
       atomicCAS(&g_status, 0, code);
       return false;
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
+  return mbar_wait_for(bar, parity, code, WAIT_NS);
 }
 
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }

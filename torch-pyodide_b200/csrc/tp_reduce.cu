@@ -14,6 +14,8 @@
 //     and the write (one HBM read, one write).
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include <cfloat>
 #include <climits>
 #include <cmath>
@@ -745,17 +747,24 @@ constexpr int64_t CE_NOALLOC_MAX_ROWS = 262144;
 constexpr int64_t CE_NOALLOC_FLOATS = CE_NOALLOC_MAX_ROWS + RED_MAX_BLOCKS + 64;
 static __device__ __align__(256) float g_ce_noalloc_scratch[CE_NOALLOC_FLOATS];
 
-// Device address of the array, looked up once per device with that device
-// current (host code cannot use the symbol itself as a device pointer).
+// Device address of the array on the library's device (the one its stream
+// belongs to), looked up once with that device current: host code cannot use
+// the symbol itself as a device pointer.  The lookup is guarded, so a first
+// call from several threads at once is safe.
 static float* g_ce_noalloc_addr[64] = {};
+static std::mutex g_ce_noalloc_mu;
 
 static float* ce_noalloc_scratch() {
-  int dev = -1;
-  TP_CUDA(cudaGetDevice(&dev));
+  const int dev = device();  // initialises the library (device, stream) if needed
   TP_REQUIRE(dev >= 0 && dev < 64, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_ce_noalloc_mu);
   if (!g_ce_noalloc_addr[dev]) {
+    int cur = -1;
+    TP_CUDA(cudaGetDevice(&cur));
+    if (cur != dev) TP_CUDA(cudaSetDevice(dev));
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_ce_noalloc_scratch);
+    if (cur != dev) cudaSetDevice(cur);
     if (e != cudaSuccess) fail(TP_ERR_CUDA, "cudaGetSymbolAddress(g_ce_noalloc_scratch) failed: %s",
                                cudaGetErrorString(e));
     g_ce_noalloc_addr[dev] = static_cast<float*>(p);
@@ -951,10 +960,14 @@ TP_API int tp_cross_entropy(int64_t input, int64_t targets, tp_handle* out) {
 TP_API int tpk_cross_entropy_mean_noalloc(const float* logits, const float* targets, float* loss_mean, int64_t B,
                                           int64_t C) {
   return guard([&] {
-    TP_REQUIRE(B >= 1 && B <= CE_NOALLOC_MAX_ROWS,
-               "cross_entropy_mean_noalloc: %lld rows is outside [1, %lld], the size of its fixed work area",
+    TP_REQUIRE(B >= 0 && B <= CE_NOALLOC_MAX_ROWS,
+               "cross_entropy_mean_noalloc: %lld rows is outside [0, %lld], the size of its fixed work area",
                (long long)B, (long long)CE_NOALLOC_MAX_ROWS);
     TP_REQUIRE(C >= 1, "cross_entropy_mean_noalloc: need at least one class");
+    if (B == 0) {  // the mean of no rows is 0, as tpk_cross_entropy_mean writes
+      TP_CUDA(cudaMemsetAsync(loss_mean, 0, sizeof(float), stream()));
+      return;
+    }
     float* base = ce_noalloc_scratch();
     float* rows = base;
     float* partials = base + CE_NOALLOC_MAX_ROWS;

@@ -1,12 +1,14 @@
 """Data-parallel plumbing: one process per GPU, NCCL communicator owned by
-libtpcuda, bootstrapped through torch.distributed (used only to hand the NCCL
-unique id from rank 0 to the other ranks and for barriers / timing maxima).
+libtpcuda, bootstrapped through the ranks' own file store (tpcuda.store),
+which hands the NCCL unique id from rank 0 to the other ranks.
 """
 from __future__ import annotations
 
 import ctypes
+import os
 
 from ._lib import check
+from .store import FileStore
 
 UID_BYTES = 128
 
@@ -37,13 +39,18 @@ class NcclComm:
         check(self.lib.tp_comm_destroy())
 
 
-def comm_from_torch_dist(lib) -> NcclComm | None:
-    """Create the NCCL communicator for the current torch.distributed group
-    (None for a single process)."""
-    import torch.distributed as dist
-    if not dist.is_initialized() or dist.get_world_size() == 1:
+def env_ranks() -> tuple[int, int, int]:
+    """(rank, world, local rank) from the launcher's environment (torchrun's
+    RANK / WORLD_SIZE / LOCAL_RANK; a single process when absent)."""
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+def comm_from_store(lib, store: FileStore) -> NcclComm | None:
+    """Create the NCCL communicator of the store's ranks (None for one rank):
+    rank 0 draws the unique id and publishes it, the others wait for it."""
+    if store.world == 1:
         return None
-    rank, world = dist.get_rank(), dist.get_world_size()
-    obj = [NcclComm.unique_id(lib) if rank == 0 else None]
-    dist.broadcast_object_list(obj, src=0)
-    return NcclComm(lib, rank, world, obj[0])
+    uid = NcclComm.unique_id(lib) if store.rank == 0 else None
+    uid = store.broadcast_bytes(uid, "nccl-unique-id")
+    return NcclComm(lib, store.rank, store.world, uid)
