@@ -123,6 +123,26 @@ TP_API int tp_memcpy_h2d(void* dst, const void* src, int64_t bytes);
 TP_API int tp_memcpy_d2h(void* dst, const void* src, int64_t bytes);
 TP_API int tp_memcpy_d2d(void* dst, const void* src, int64_t bytes);
 TP_API int tp_memset(void* dst, int value, int64_t bytes);
+/* New, checkpoint I/O (python/torch/_save.py:109-125 packs every tensor through
+ * tolist() and struct.pack; _save.py:77-103 unpacks into a Python list for
+ * tensorFromData): the tensor's values in one copy.  format 0: little-endian
+ * float32 (nbytes = 4 numel); 1: little-endian int64, each value truncated
+ * toward zero as toList decodes integer dtypes (nbytes = 8 numel).  Both
+ * synchronise, so `dst` / `src` may be pageable and reused on return. */
+TP_API int tp_to_bytes(int64_t id, void* dst, int64_t nbytes, int format);
+TP_API int tp_from_bytes(const void* src, int64_t nbytes, int format, const int64_t* shape, int ndim, int dtype,
+                         tp_handle* out);
+/* New, input pipeline (python/torch/tensor_factories_ops.py:18-25 flattens the
+ * data to a Python list per tensor): pinned host buffers, and an upload from
+ * one that runs on a dedicated copy stream, overlapping the kernels already
+ * queued; later work on the library streams waits for it.  *ticket names the
+ * copy: tp_ticket_wait(ticket) returns once it has finished and the host
+ * buffer may be refilled. */
+TP_API int tp_host_alloc(int64_t bytes, void** out);
+TP_API int tp_host_free(void* ptr);
+TP_API int tp_tensor_from_host_async(const void* pinned_host, const int64_t* shape, int ndim, int dtype,
+                                     tp_handle* out, int64_t* ticket);
+TP_API int tp_ticket_wait(int64_t ticket);
 
 /* ---- creation (creationOps.ts, random.wgsl, fill.wgsl) -------------------- */
 /* zeros/ones/full/empty: creationOps.ts:39-45,107-145 (fill.wgsl) */
@@ -217,6 +237,12 @@ TP_API int tp_linear(int64_t x, int64_t weight, int64_t bias, tp_handle* out);
  * or NULL; dilation is accepted and ignored, as in the reference */
 TP_API int tp_conv2d(int64_t input, int64_t weight, const float* bias, int nbias, const int64_t* stride, int ns,
                      const int64_t* padding, int np, const int64_t* dilation, int nd, int groups, tp_handle* out);
+/* New: conv2d with the bias as a tensor id (0 = none) instead of a host list,
+ * so a convolution needs no readback of its bias (tensor_nn_ops.py:27 reads
+ * it back on every call); same values as tp_conv2d */
+TP_API int tp_conv2d_dev_bias(int64_t input, int64_t weight, int64_t bias, const int64_t* stride, int ns,
+                              const int64_t* padding, int np, const int64_t* dilation, int nd, int groups,
+                              tp_handle* out);
 /* convOps.ts:64-108 conv2dInputBackward (conv_backward.wgsl:24-61) */
 TP_API int tp_conv2d_input_backward(int64_t grad_out, int64_t weight, const int64_t* input_shape,
                                     const int64_t* grad_out_shape, const int64_t* stride, int ns,
@@ -316,6 +342,42 @@ TP_API int tp_adam_step_multi(const int64_t* params, const int64_t* grads, const
                               float weight_decay, float step_size, float inv_sqrt_bc2);
 TP_API int tp_sgd_step_multi(const int64_t* params, const int64_t* grads, const int64_t* momentum_bufs, int n,
                              float lr, float momentum, float weight_decay, float dampening, int nesterov);
+/* runtime.ts:683-705 rmspropStep (rmsprop_step.wgsl); momentum != 0 uses
+ * momentum_buf, as the shader's use_momentum flag (reductionOps.ts:655-688) */
+TP_API int tp_rmsprop_step(int64_t param, int64_t grad, int64_t square_avg, int64_t momentum_buf, float lr,
+                           float alpha, float eps, float weight_decay, float momentum);
+/* runtime.ts:707-716 adagradStep (extended_step.wgsl adagrad_step) */
+TP_API int tp_adagrad_step(int64_t param, int64_t grad, int64_t sum_squares, float lr, float eps,
+                           float weight_decay);
+/* runtime.ts:718-744 adamaxStep (extended_step.wgsl adamax_step) */
+TP_API int tp_adamax_step(int64_t param, int64_t grad, int64_t exp_avg, int64_t exp_inf, float lr, float beta1,
+                          float beta2, float eps, float weight_decay, float step_size, float bias_correction1);
+/* runtime.ts:746-772 nadamStep (extended_step.wgsl nadam_step) */
+TP_API int tp_nadam_step(int64_t param, int64_t grad, int64_t exp_avg, int64_t exp_avg_sq, float lr, float beta1,
+                         float beta2, float eps, float weight_decay, float step_size, float mu);
+/* runtime.ts:774-801 radamStep (extended_step.wgsl radam_step); `step` is the
+ * integer step count the shader reads from dims.y (the reference's Python
+ * passes it, optim/__init__.py:825-839, but runtime.ts drops it, so the shader
+ * sees 0 and uses 1; here the count is used as intended) */
+TP_API int tp_radam_step(int64_t param, int64_t grad, int64_t exp_avg, int64_t exp_avg_sq, float lr, float beta1,
+                         float beta2, float eps, float weight_decay, float step_size, float beta1_pow_t,
+                         float beta2_pow_t, int64_t step);
+/* New: the same five as one fused launch per parameter group */
+TP_API int tp_rmsprop_step_multi(const int64_t* params, const int64_t* grads, const int64_t* square_avgs,
+                                 const int64_t* momentum_bufs, int n, float lr, float alpha, float eps,
+                                 float weight_decay, float momentum);
+TP_API int tp_adagrad_step_multi(const int64_t* params, const int64_t* grads, const int64_t* sum_squares, int n,
+                                 float lr, float eps, float weight_decay);
+TP_API int tp_adamax_step_multi(const int64_t* params, const int64_t* grads, const int64_t* exp_avgs,
+                                const int64_t* exp_infs, int n, float lr, float beta1, float beta2, float eps,
+                                float weight_decay, float step_size, float bias_correction1);
+TP_API int tp_nadam_step_multi(const int64_t* params, const int64_t* grads, const int64_t* exp_avgs,
+                               const int64_t* exp_avg_sqs, int n, float lr, float beta1, float beta2, float eps,
+                               float weight_decay, float step_size, float mu);
+TP_API int tp_radam_step_multi(const int64_t* params, const int64_t* grads, const int64_t* exp_avgs,
+                               const int64_t* exp_avg_sqs, int n, float lr, float beta1, float beta2, float eps,
+                               float weight_decay, float step_size, float beta1_pow_t, float beta2_pow_t,
+                               int64_t step);
 
 /* ---- pointer-level optimizer kernels ---------------------------------------- */
 /* A tensor group is a device-side table of n (param, grad, state0, state1,

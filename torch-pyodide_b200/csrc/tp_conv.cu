@@ -358,6 +358,39 @@ TP_API int tp_conv2d(int64_t input, int64_t weight, const float* bias, int nbias
   });
 }
 
+// New: conv2d with the bias as a device tensor (bias_id 0: none).  The
+// reference passes the bias as a host list, read back from the device on every
+// call (tensor_nn_ops.py:27), which makes each convolution a host sync; this
+// entry keeps it on the device and gives the same values.
+TP_API int tp_conv2d_dev_bias(int64_t input, int64_t weight, int64_t bias_id, const int64_t* stride, int ns,
+                              const int64_t* padding, int np, const int64_t* dilation, int nd, int groups,
+                              tp_handle* out) {
+  (void)dilation;
+  (void)nd;
+  return guard([&] {
+    Tensor& X = get(input);
+    Tensor& Wt = get(weight);
+    TP_REQUIRE(X.ndim == 4 && Wt.ndim == 4, "conv2d expects NCHW input and OIHW weight");
+    int g = groups > 0 ? groups : 1;
+    TP_REQUIRE(Wt.shape[1] * g == X.shape[1], "conv2d: weight in_channels %lld x groups %d != input channels %lld",
+               (long long)Wt.shape[1], g, (long long)X.shape[1]);
+    ConvShape s = conv_shape(X.shape[0], X.shape[1], X.shape[2], X.shape[3], Wt.shape[0], (int)Wt.shape[2],
+                             (int)Wt.shape[3], at(stride, ns, 0, 1), at(stride, ns, 1, 1), at(padding, np, 0, 0),
+                             at(padding, np, 1, 0), g);
+    const float* db = nullptr;
+    if (bias_id) {
+      Tensor& Bt = get(bias_id);
+      TP_REQUIRE(Bt.numel == s.Cout, "conv2d: bias has %lld values, expected %lld", (long long)Bt.numel,
+                 (long long)s.Cout);
+      db = Bt.f();
+    }
+    int64_t shp[4] = {s.N, s.Cout, s.OH, s.OW};
+    Tensor Y = make(shp, 4, X.dtype);
+    conv_fwd(s, X.f(), Wt.f(), db, Y.f());
+    emit(Y, out);
+  });
+}
+
 // convOps.ts:64-108 (groups forced to 1 by the reference).
 TP_API int tp_conv2d_input_backward(int64_t grad_out, int64_t weight, const int64_t* input_shape,
                                     const int64_t* grad_out_shape, const int64_t* stride, int ns,

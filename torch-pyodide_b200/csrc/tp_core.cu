@@ -222,6 +222,20 @@ int64_t emit(const Tensor& t, tp_handle* out) {
   return id;
 }
 
+// int64 element <-> the f32 value the runtime stores for an integer dtype
+// (truncation toward zero on the way out, as toList decodes, device.ts:38-54)
+__global__ void k_f32_to_i64(const float* in, long long* out, int64_t n) {
+  ::tp::pdl_enter();
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = (long long)truncf(in[i]);
+}
+
+__global__ void k_i64_to_f32(const long long* in, float* out, int64_t n) {
+  ::tp::pdl_enter();
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = (float)in[i];
+}
+
 __global__ void k_i32_to_f32(const int32_t* in, float* out, int64_t n) {
   ::tp::pdl_enter();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
@@ -338,6 +352,145 @@ TP_API int tp_to_host(int64_t id, float* dst, int64_t numel) {
       TP_CUDA(cudaMemcpyAsync(dst, t.ptr, (size_t)t.numel * 4, cudaMemcpyDeviceToHost, stream()));
     }
     TP_CUDA(cudaStreamSynchronize(stream()));
+  });
+}
+
+// ---- bulk byte I/O (checkpoints) and pinned uploads -----------------------------------
+
+TP_API int tp_to_bytes(int64_t id, void* dst, int64_t nbytes, int format) {
+  return guard([&] {
+    Tensor& t = get(id);
+    TP_REQUIRE(format == 0 || format == 1, "toBytes: format 0 (float32) or 1 (int64)");
+    const int64_t esz = format == 0 ? 4 : 8;
+    TP_REQUIRE(nbytes == t.numel * esz, "toBytes: buffer holds %lld bytes, tensor needs %lld", (long long)nbytes,
+               (long long)(t.numel * esz));
+    if (t.numel == 0) return;
+    const float* src = t.f();
+    float* tmp = nullptr;
+    if (t.phys == PHYS_I32) {
+      tmp = (float*)dalloc((size_t)t.numel * 4);
+      TP_LAUNCH(k_i32_to_f32, grid_for(t.numel, 256), 256, 0, (const int32_t*)t.ptr, tmp, t.numel);
+      src = tmp;
+    }
+    if (format == 0) {
+      TP_CUDA(cudaMemcpyAsync(dst, src, (size_t)nbytes, cudaMemcpyDeviceToHost, stream()));
+    } else {
+      long long* wide = (long long*)dalloc((size_t)nbytes);
+      TP_LAUNCH(k_f32_to_i64, grid_for(t.numel, 256), 256, 0, src, wide, t.numel);
+      TP_CUDA(cudaMemcpyAsync(dst, wide, (size_t)nbytes, cudaMemcpyDeviceToHost, stream()));
+      dfree(wide);
+    }
+    if (tmp) dfree(tmp);
+    TP_CUDA(cudaStreamSynchronize(stream()));
+  });
+}
+
+TP_API int tp_from_bytes(const void* src, int64_t nbytes, int format, const int64_t* shape, int ndim, int dtype,
+                         tp_handle* out) {
+  return guard([&] {
+    TP_REQUIRE(format == 0 || format == 1, "fromBytes: format 0 (float32) or 1 (int64)");
+    Tensor t = make(shape, ndim, dtype);
+    const int64_t esz = format == 0 ? 4 : 8;
+    if (nbytes != t.numel * esz) {
+      dfree(t.ptr);
+      fail(TP_ERR_ARG, "fromBytes: %lld bytes for %lld elements of %lld bytes", (long long)nbytes,
+           (long long)t.numel, (long long)esz);
+    }
+    if (t.numel > 0) {
+      if (format == 0) {
+        TP_CUDA(cudaMemcpyAsync(t.ptr, src, (size_t)nbytes, cudaMemcpyHostToDevice, stream()));
+      } else {
+        long long* wide = (long long*)dalloc((size_t)nbytes);
+        TP_CUDA(cudaMemcpyAsync(wide, src, (size_t)nbytes, cudaMemcpyHostToDevice, stream()));
+        TP_LAUNCH(k_i64_to_f32, grid_for(t.numel, 256), 256, 0, (const long long*)wide, t.f(), t.numel);
+        dfree(wide);
+      }
+      // the caller's buffer may be pageable and released on return
+      TP_CUDA(cudaStreamSynchronize(stream()));
+    }
+    emit(t, out);
+  });
+}
+
+TP_API int tp_host_alloc(int64_t bytes, void** out) {
+  return guard([&] {
+    TP_REQUIRE(bytes >= 0, "negative allocation size");
+    ensure_init();
+    void* p = nullptr;
+    cudaError_t e = cudaHostAlloc(&p, (size_t)(bytes > 0 ? bytes : 16), cudaHostAllocPortable);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      fail(TP_ERR_OOM, "pinned host allocation of %lld bytes failed: %s", (long long)bytes, cudaGetErrorString(e));
+    }
+    *out = p;
+  });
+}
+
+TP_API int tp_host_free(void* p) {
+  return guard([&] {
+    if (p) TP_CUDA(cudaFreeHost(p));
+  });
+}
+
+// Uploads from pinned host memory run on their own copy stream, so the copy of
+// the next batch overlaps the kernels of the current one; the destination is
+// allocated in the copy stream's order (the pool makes cross-stream reuse safe)
+// and the library streams wait for the copy's event before any later kernel.
+// Each upload gets a ticket: tp_ticket_wait(ticket) returns once that copy has
+// finished, after which the host buffer may be reused.
+static cudaStream_t g_copy = nullptr;
+constexpr int TICKETS = 256;
+static cudaEvent_t g_ticket_ev[TICKETS];
+static bool g_ticket_made[TICKETS];
+static int64_t g_next_ticket = 1;
+
+TP_API int tp_tensor_from_host_async(const void* host, const int64_t* shape, int ndim, int dtype, tp_handle* out,
+                                     int64_t* ticket) {
+  return guard([&] {
+    ensure_init();
+    if (!g_copy) TP_CUDA(cudaStreamCreateWithFlags(&g_copy, cudaStreamNonBlocking));
+    cudaPointerAttributes attr;
+    TP_CUDA(cudaPointerGetAttributes(&attr, host));
+    TP_REQUIRE(attr.type == cudaMemoryTypeHost, "tensorFromHostAsync: the source must be pinned host memory "
+                                                "(tp_host_alloc)");
+    TP_REQUIRE(ndim >= 0 && ndim <= TP_MAX_DIMS, "tensor rank %d exceeds %d", ndim, TP_MAX_DIMS);
+    TP_REQUIRE(dtype >= TP_FLOAT32 && dtype <= TP_BOOL, "Unsupported dtype code: %d.", dtype);
+    Tensor t;
+    t.ndim = ndim;
+    t.dtype = dtype;
+    t.phys = PHYS_F32;
+    for (int i = 0; i < ndim; ++i) {
+      TP_REQUIRE(shape[i] >= 0, "negative dimension %lld", (long long)shape[i]);
+      t.shape[i] = shape[i];
+    }
+    t.numel = prod(shape, ndim);
+    t.bytes = (size_t)(t.numel > 0 ? t.numel : 1) * 4;
+    cudaError_t e = cudaMallocAsync(&t.ptr, t.bytes, g_copy);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      fail(TP_ERR_OOM, "device allocation of %zu bytes failed: %s", t.bytes, cudaGetErrorString(e));
+    }
+    if (t.numel > 0) TP_CUDA(cudaMemcpyAsync(t.ptr, host, (size_t)t.numel * 4, cudaMemcpyHostToDevice, g_copy));
+    const int64_t tk = g_next_ticket++;
+    const int slot = (int)(tk % TICKETS);
+    if (!g_ticket_made[slot]) {
+      TP_CUDA(cudaEventCreateWithFlags(&g_ticket_ev[slot], cudaEventDisableTiming));
+      g_ticket_made[slot] = true;
+    }
+    TP_CUDA(cudaEventRecord(g_ticket_ev[slot], g_copy));
+    TP_CUDA(cudaStreamWaitEvent(g_stream, g_ticket_ev[slot], 0));
+    if (g_aux) TP_CUDA(cudaStreamWaitEvent(g_aux, g_ticket_ev[slot], 0));
+    emit(t, out);
+    *ticket = tk;
+  });
+}
+
+TP_API int tp_ticket_wait(int64_t ticket) {
+  return guard([&] {
+    TP_REQUIRE(ticket > 0 && ticket < g_next_ticket, "unknown upload ticket %lld", (long long)ticket);
+    // A slot reused by a later upload holds that later copy's event, which
+    // completes after this one (one copy stream, in order): still a safe wait.
+    TP_CUDA(cudaEventSynchronize(g_ticket_ev[ticket % TICKETS]));
   });
 }
 

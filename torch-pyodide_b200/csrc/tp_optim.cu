@@ -182,6 +182,114 @@ __global__ void __launch_bounds__(256) k_sgd_multi(const OptRow* __restrict__ ro
   }
 }
 
+// ---- the other fused steps (rmsprop_step.wgsl, extended_step.wgsl) ---------------------
+// Same multi-tensor walk; the per-element arithmetic is each entry point's,
+// operation by operation, with round-to-nearest intrinsics (no contraction), so
+// the results are bit-identical to the oracle's restatement.
+enum ExtKind { EXT_RMSPROP = 0, EXT_ADAGRAD = 1, EXT_ADAMAX = 2, EXT_NADAM = 3, EXT_RADAM = 4 };
+
+struct ExtHP {
+  float lr, b1, b2, eps, wd;  // RMSprop: b1 = alpha; Adagrad uses lr, eps, wd
+  float step_size;            // Adamax, NAdam, RAdam
+  float x0, x1;               // RMSprop: momentum; Adamax: bias_correction1; NAdam: mu;
+                              // RAdam: beta1^t, beta2^t
+  float t;                    // RAdam: the step count as f32 (at least 1)
+  int use_momentum;           // RMSprop
+};
+
+template <int KIND>
+__device__ __forceinline__ void ext_elem(float& p, float g, float& s0, float& s1, const ExtHP& h) {
+  if (h.wd != 0.0f) g = __fadd_rn(g, __fmul_rn(h.wd, p));
+  if (KIND == EXT_RMSPROP) {  // rmsprop_step.wgsl:22-41
+    const float sq = __fadd_rn(__fmul_rn(s0, h.b1), __fmul_rn(__fmul_rn(__fsub_rn(1.0f, h.b1), g), g));
+    s0 = sq;
+    const float denom = __fadd_rn(__fsqrt_rn(sq), h.eps);
+    float upd = __fdiv_rn(g, denom);
+    if (h.use_momentum) {
+      s1 = __fadd_rn(__fmul_rn(s1, h.x0), upd);
+      upd = s1;
+    }
+    p = __fsub_rn(p, __fmul_rn(h.lr, upd));
+  } else if (KIND == EXT_ADAGRAD) {  // extended_step.wgsl adagrad_step
+    const float s = __fadd_rn(s0, __fmul_rn(g, g));
+    s0 = s;
+    const float sd = __fadd_rn(__fsqrt_rn(s), h.eps);
+    p = __fsub_rn(p, __fdiv_rn(__fmul_rn(h.lr, g), sd));
+  } else if (KIND == EXT_ADAMAX) {  // extended_step.wgsl adamax_step
+    const float m = __fadd_rn(__fmul_rn(s0, h.b1), __fmul_rn(__fsub_rn(1.0f, h.b1), g));
+    const float u = fmaxf(__fmul_rn(s1, h.b2), fabsf(g));
+    s0 = m;
+    s1 = u;
+    const float denom = __fadd_rn(u, h.eps);
+    p = __fsub_rn(p, __fmul_rn(__fmul_rn(__fdiv_rn(m, denom), h.step_size), h.x0));
+  } else {
+    const float m = __fadd_rn(__fmul_rn(s0, h.b1), __fmul_rn(__fsub_rn(1.0f, h.b1), g));
+    const float v = __fadd_rn(__fmul_rn(s1, h.b2), __fmul_rn(__fmul_rn(__fsub_rn(1.0f, h.b2), g), g));
+    s0 = m;
+    s1 = v;
+    if (KIND == EXT_NADAM) {  // extended_step.wgsl nadam_step
+      const float m_hat = __fadd_rn(__fmul_rn(h.x0, m), __fmul_rn(__fsub_rn(1.0f, h.x0), g));
+      const float denom = __fadd_rn(__fsqrt_rn(v), h.eps);
+      p = __fsub_rn(p, __fmul_rn(__fdiv_rn(m_hat, denom), h.step_size));
+    } else {  // extended_step.wgsl radam_step
+      const float m_hat = __fdiv_rn(m, __fsub_rn(1.0f, h.x0));
+      const float rho_inf = __fsub_rn(__fdiv_rn(2.0f, __fsub_rn(1.0f, h.b2)), 1.0f);
+      const float omb2t = __fsub_rn(1.0f, h.x1);
+      const float rho_t =
+          __fsub_rn(rho_inf, __fdiv_rn(__fmul_rn(__fmul_rn(2.0f, h.t), h.x1), fmaxf(omb2t, 1e-10f)));
+      float upd;
+      if (rho_t > 5.0f) {
+        const float num = __fmul_rn(__fmul_rn(__fsub_rn(rho_t, 4.0f), __fsub_rn(rho_t, 2.0f)), rho_inf);
+        const float den = __fmul_rn(__fmul_rn(__fsub_rn(rho_inf, 4.0f), __fsub_rn(rho_inf, 2.0f)), rho_t);
+        const float rect = __fsqrt_rn(__fdiv_rn(num, den));
+        upd = __fmul_rn(__fmul_rn(h.step_size, m_hat), rect);
+      } else {
+        upd = __fmul_rn(h.step_size, m_hat);
+      }
+      p = __fsub_rn(p, upd);
+    }
+  }
+}
+
+template <int KIND>
+__global__ void __launch_bounds__(256) k_ext_multi(const OptRow* __restrict__ rows, const OptChunk* __restrict__ chunks,
+                                                   int nchunks, ExtHP h) {
+  ::tp::pdl_enter();
+  for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
+    OptChunk ch = chunks[c];
+    OptRow r = rows[ch.row];
+    float* __restrict__ P = r.p + ch.start;
+    const float* __restrict__ G = r.g + ch.start;
+    float* __restrict__ S0 = r.s0 + ch.start;
+    float* __restrict__ S1 = r.s1 + ch.start;
+    // Adagrad keeps one state tensor, RMSprop without momentum never touches the second
+    const bool two = KIND != EXT_ADAGRAD && (KIND != EXT_RMSPROP || h.use_momentum);
+    const int len = ch.len, len4 = len >> 2;
+    float4* P4 = reinterpret_cast<float4*>(P);
+    const float4* G4 = reinterpret_cast<const float4*>(G);
+    float4* A4 = reinterpret_cast<float4*>(S0);
+    float4* B4 = reinterpret_cast<float4*>(S1);
+    for (int i = threadIdx.x; i < len4; i += blockDim.x) {
+      float4 p = P4[i], g = G4[i], a = A4[i];
+      float4 b = two ? B4[i] : make_float4(0, 0, 0, 0);
+      ext_elem<KIND>(p.x, g.x, a.x, b.x, h);
+      ext_elem<KIND>(p.y, g.y, a.y, b.y, h);
+      ext_elem<KIND>(p.z, g.z, a.z, b.z, h);
+      ext_elem<KIND>(p.w, g.w, a.w, b.w, h);
+      P4[i] = p;
+      A4[i] = a;
+      if (two) B4[i] = b;
+    }
+    for (int k = (len4 << 2) + threadIdx.x; k < len; k += blockDim.x) {
+      float p = P[k], a = S0[k], b = two ? S1[k] : 0.0f;
+      ext_elem<KIND>(p, G[k], a, b, h);
+      P[k] = p;
+      S0[k] = a;
+      if (two) S1[k] = b;
+    }
+  }
+}
+
 // ---- groups --------------------------------------------------------------------
 
 struct Group {
@@ -248,6 +356,24 @@ void launch_adam_group(const Group& g, bool adamw, const AdamHP& h) {
 void launch_sgd_group(const Group& g, const SgdHP& h) {
   if (g.nchunks == 0) return;
   TP_LAUNCH(k_sgd_multi, opt_grid(g.nchunks), 256, 0, g.rows, g.chunks, g.nchunks, h);
+}
+
+static unsigned opt_grid(int nchunks);
+
+template <int KIND>
+static void launch_ext(const Group& g, const ExtHP& h) {
+  if (g.nchunks == 0) return;
+  TP_LAUNCH(k_ext_multi<KIND>, opt_grid(g.nchunks), 256, 0, g.rows, g.chunks, g.nchunks, h);
+}
+
+static void launch_ext_kind(int kind, const Group& g, const ExtHP& h) {
+  switch (kind) {
+    case EXT_RMSPROP: launch_ext<EXT_RMSPROP>(g, h); break;
+    case EXT_ADAGRAD: launch_ext<EXT_ADAGRAD>(g, h); break;
+    case EXT_ADAMAX: launch_ext<EXT_ADAMAX>(g, h); break;
+    case EXT_NADAM: launch_ext<EXT_NADAM>(g, h); break;
+    default: launch_ext<EXT_RADAM>(g, h); break;
+  }
 }
 
 static std::vector<OptRow> rows_from_ids(const int64_t* p, const int64_t* gr, const int64_t* s0, const int64_t* s1,
@@ -358,6 +484,81 @@ TP_API int tpk_sgd_group(int64_t group, float lr, float mom, float wd, float dam
     SgdHP h{lr, mom, wd, 1.0f - damp, grad_scale, mom != 0.0f ? 1 : 0, nesterov ? 1 : 0};
     launch_sgd_group(it->second, h);
   });
+}
+
+static int ext_multi(int kind, const int64_t* p, const int64_t* g, const int64_t* s0, const int64_t* s1, int n,
+                     const ExtHP& h, const char* what) {
+  return guard([&] {
+    TP_REQUIRE(n >= 0, "%s: negative tensor count", what);
+    Group grp = build_group(rows_from_ids(p, g, s0, s1, n, what));
+    launch_ext_kind(kind, grp, h);
+    free_group(grp);
+  });
+}
+
+static ExtHP ext_hp(float lr, float b1, float b2, float eps, float wd, float ss, float x0, float x1, float t,
+                    int use_m) {
+  ExtHP h;
+  h.lr = lr; h.b1 = b1; h.b2 = b2; h.eps = eps; h.wd = wd; h.step_size = ss; h.x0 = x0; h.x1 = x1;
+  h.t = t; h.use_momentum = use_m;
+  return h;
+}
+
+TP_API int tp_rmsprop_step_multi(const int64_t* p, const int64_t* g, const int64_t* sq, const int64_t* mb, int n,
+                                 float lr, float alpha, float eps, float wd, float momentum) {
+  return ext_multi(EXT_RMSPROP, p, g, sq, mb, n,
+                   ext_hp(lr, alpha, 0.0f, eps, wd, 0.0f, momentum, 0.0f, 0.0f, momentum != 0.0f ? 1 : 0),
+                   "rmspropStep");
+}
+
+TP_API int tp_rmsprop_step(int64_t p, int64_t g, int64_t sq, int64_t mb, float lr, float alpha, float eps, float wd,
+                           float momentum) {
+  return tp_rmsprop_step_multi(&p, &g, &sq, &mb, 1, lr, alpha, eps, wd, momentum);
+}
+
+TP_API int tp_adagrad_step_multi(const int64_t* p, const int64_t* g, const int64_t* sum, int n, float lr, float eps,
+                                 float wd) {
+  return ext_multi(EXT_ADAGRAD, p, g, sum, nullptr, n, ext_hp(lr, 0.0f, 0.0f, eps, wd, 0.0f, 0.0f, 0.0f, 0.0f, 0),
+                   "adagradStep");
+}
+
+TP_API int tp_adagrad_step(int64_t p, int64_t g, int64_t sum, float lr, float eps, float wd) {
+  return tp_adagrad_step_multi(&p, &g, &sum, 1, lr, eps, wd);
+}
+
+TP_API int tp_adamax_step_multi(const int64_t* p, const int64_t* g, const int64_t* m, const int64_t* u, int n,
+                                float lr, float b1, float b2, float eps, float wd, float step_size, float bc1) {
+  return ext_multi(EXT_ADAMAX, p, g, m, u, n, ext_hp(lr, b1, b2, eps, wd, step_size, bc1, 0.0f, 0.0f, 0),
+                   "adamaxStep");
+}
+
+TP_API int tp_adamax_step(int64_t p, int64_t g, int64_t m, int64_t u, float lr, float b1, float b2, float eps,
+                          float wd, float step_size, float bc1) {
+  return tp_adamax_step_multi(&p, &g, &m, &u, 1, lr, b1, b2, eps, wd, step_size, bc1);
+}
+
+TP_API int tp_nadam_step_multi(const int64_t* p, const int64_t* g, const int64_t* m, const int64_t* v, int n,
+                               float lr, float b1, float b2, float eps, float wd, float step_size, float mu) {
+  return ext_multi(EXT_NADAM, p, g, m, v, n, ext_hp(lr, b1, b2, eps, wd, step_size, mu, 0.0f, 0.0f, 0),
+                   "nadamStep");
+}
+
+TP_API int tp_nadam_step(int64_t p, int64_t g, int64_t m, int64_t v, float lr, float b1, float b2, float eps,
+                         float wd, float step_size, float mu) {
+  return tp_nadam_step_multi(&p, &g, &m, &v, 1, lr, b1, b2, eps, wd, step_size, mu);
+}
+
+TP_API int tp_radam_step_multi(const int64_t* p, const int64_t* g, const int64_t* m, const int64_t* v, int n,
+                               float lr, float b1, float b2, float eps, float wd, float step_size, float b1pow,
+                               float b2pow, int64_t step) {
+  const float t = (float)(step > 1 ? (uint32_t)step : 1u);  // max(f32(u32 step), 1.0)
+  return ext_multi(EXT_RADAM, p, g, m, v, n, ext_hp(lr, b1, b2, eps, wd, step_size, b1pow, b2pow, t, 0),
+                   "radamStep");
+}
+
+TP_API int tp_radam_step(int64_t p, int64_t g, int64_t m, int64_t v, float lr, float b1, float b2, float eps,
+                         float wd, float step_size, float b1pow, float b2pow, int64_t step) {
+  return tp_radam_step_multi(&p, &g, &m, &v, 1, lr, b1, b2, eps, wd, step_size, b1pow, b2pow, step);
 }
 
 }  // extern "C"

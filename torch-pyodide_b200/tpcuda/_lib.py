@@ -79,6 +79,23 @@ SIGNATURES: dict[str, list] = {
     "tp_memcpy_h2d": [P, P, I64],
     "tp_memcpy_d2h": [P, P, I64],
     "tp_memcpy_d2d": [P, P, I64],
+    "tp_to_bytes": [I64, P, I64, INT],
+    "tp_from_bytes": [P, I64, INT, I64P, INT, INT, HP],
+    "tp_host_alloc": [I64, PP],
+    "tp_host_free": [P],
+    "tp_tensor_from_host_async": [P, I64P, INT, INT, HP, I64P],
+    "tp_ticket_wait": [I64],
+    "tp_conv2d_dev_bias": [I64, I64, I64, I64P, INT, I64P, INT, I64P, INT, INT, HP],
+    "tp_rmsprop_step": [I64, I64, I64, I64, F32, F32, F32, F32, F32],
+    "tp_adagrad_step": [I64, I64, I64, F32, F32, F32],
+    "tp_adamax_step": [I64, I64, I64, I64] + [F32] * 7,
+    "tp_nadam_step": [I64, I64, I64, I64] + [F32] * 7,
+    "tp_radam_step": [I64, I64, I64, I64] + [F32] * 8 + [I64],
+    "tp_rmsprop_step_multi": [I64P, I64P, I64P, I64P, INT, F32, F32, F32, F32, F32],
+    "tp_adagrad_step_multi": [I64P, I64P, I64P, INT, F32, F32, F32],
+    "tp_adamax_step_multi": [I64P, I64P, I64P, I64P, INT] + [F32] * 7,
+    "tp_nadam_step_multi": [I64P, I64P, I64P, I64P, INT] + [F32] * 7,
+    "tp_radam_step_multi": [I64P, I64P, I64P, I64P, INT] + [F32] * 8 + [I64],
     "tp_memset": [P, INT, I64],
     "tp_full": [I64P, INT, INT, F32, HP],
     "tp_full_like": [I64, INT, F32, HP],
