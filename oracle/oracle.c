@@ -752,3 +752,117 @@ OR_EXPORT void or_sgd_step(float *param, const float *grad, float *buf_, int64_t
         param[i] = p - lr * update;
     }
 }
+
+/* ------------------------------------------------------------------------- */
+/* rmsprop_step.wgsl:11-42 (reductionOps.ts:655-688): use_momentum is
+ * momentum != 0; the momentum buffer is read and written only then.         */
+OR_EXPORT void or_rmsprop_step(float *param, const float *grad, float *sq_, float *mb_, int64_t n, float lr,
+                               float alpha, float eps, float wd, float momentum) {
+    int use_m = momentum != 0.0f;
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; ++i) {
+        float p = param[i];
+        float g = grad[i];
+        if (wd != 0.0f) g = g + wd * p;
+        float sq = sq_[i] * alpha + (1.0f - alpha) * g * g;
+        sq_[i] = sq;
+        float denom = sqrtf(sq) + eps;
+        float update = g / denom;
+        if (use_m) {
+            float buf = mb_[i] * momentum + update;
+            mb_[i] = buf;
+            update = buf;
+        }
+        param[i] = p - lr * update;
+    }
+}
+
+/* extended_step.wgsl adagrad_step (reductionOps.ts:690-737): hp = [lr, 0, 0,
+ * eps], extra = [weight_decay, ...].                                         */
+OR_EXPORT void or_adagrad_step(float *param, const float *grad, float *sum_, int64_t n, float lr, float eps,
+                               float wd) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; ++i) {
+        float p = param[i];
+        float g = grad[i];
+        if (wd != 0.0f) g = g + wd * p;
+        float s = sum_[i] + g * g;
+        sum_[i] = s;
+        float sd = sqrtf(s) + eps;
+        param[i] = p - lr * g / sd;
+    }
+}
+
+/* extended_step.wgsl adamax_step (reductionOps.ts:739-780): extra =
+ * [weight_decay, step_size, bias_correction1, 0].                           */
+OR_EXPORT void or_adamax_step(float *param, const float *grad, float *m_, float *u_, int64_t n, float lr, float beta1,
+                              float beta2, float eps, float wd, float step_size, float bc1) {
+    (void)lr;
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; ++i) {
+        float p = param[i];
+        float g = grad[i];
+        if (wd != 0.0f) g = g + wd * p;
+        float m = m_[i] * beta1 + (1.0f - beta1) * g;
+        float u = fmaxf(u_[i] * beta2, fabsf(g));
+        m_[i] = m;
+        u_[i] = u;
+        float denom = u + eps;
+        float update = (m / denom) * step_size * bc1;
+        param[i] = p - update;
+    }
+}
+
+/* extended_step.wgsl nadam_step (reductionOps.ts:782-823): extra =
+ * [weight_decay, step_size, mu, 0]; m_hat = mu m + (1 - mu) g.               */
+OR_EXPORT void or_nadam_step(float *param, const float *grad, float *m_, float *v_, int64_t n, float lr, float beta1,
+                             float beta2, float eps, float wd, float step_size, float mu) {
+    (void)lr;
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; ++i) {
+        float p = param[i];
+        float g = grad[i];
+        if (wd != 0.0f) g = g + wd * p;
+        float m = m_[i] * beta1 + (1.0f - beta1) * g;
+        float v = v_[i] * beta2 + (1.0f - beta2) * g * g;
+        m_[i] = m;
+        v_[i] = v;
+        float m_hat = mu * m + (1.0f - mu) * g;
+        float denom = sqrtf(v) + eps;
+        float update = (m_hat / denom) * step_size;
+        param[i] = p - update;
+    }
+}
+
+/* extended_step.wgsl radam_step (reductionOps.ts:825-868): extra =
+ * [weight_decay, step_size, beta1^t, beta2^t], t = max(f32(step), 1).        */
+OR_EXPORT void or_radam_step(float *param, const float *grad, float *m_, float *v_, int64_t n, float lr, float beta1,
+                             float beta2, float eps, float wd, float step_size, float b1pow, float b2pow,
+                             int64_t step) {
+    (void)lr;
+    (void)eps;
+    float t_int = (float)(uint32_t)step;
+    if (t_int < 1.0f) t_int = 1.0f;
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; ++i) {
+        float p = param[i];
+        float g = grad[i];
+        if (wd != 0.0f) g = g + wd * p;
+        float m = m_[i] * beta1 + (1.0f - beta1) * g;
+        float v = v_[i] * beta2 + (1.0f - beta2) * g * g;
+        m_[i] = m;
+        v_[i] = v;
+        float m_hat = m / (1.0f - b1pow);
+        float rho_inf = 2.0f / (1.0f - beta2) - 1.0f;
+        float one_minus_b2t = 1.0f - b2pow;
+        float rho_t = rho_inf - 2.0f * t_int * b2pow / fmaxf(one_minus_b2t, 1e-10f);
+        float update;
+        if (rho_t > 5.0f) {
+            float rect = sqrtf((rho_t - 4.0f) * (rho_t - 2.0f) * rho_inf / ((rho_inf - 4.0f) * (rho_inf - 2.0f) * rho_t));
+            update = step_size * m_hat * rect;
+        } else {
+            update = step_size * m_hat;
+        }
+        param[i] = p - update;
+    }
+}

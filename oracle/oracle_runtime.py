@@ -104,6 +104,11 @@ def lib():
         for nm in ("or_adamw_step", "or_adam_step"):
             getattr(L, nm).argtypes = [F32P, F32P, F32P, F32P, ctypes.c_int64] + [ctypes.c_float] * 7
         L.or_sgd_step.argtypes = [F32P, F32P, F32P, ctypes.c_int64] + [ctypes.c_float] * 4 + [ctypes.c_int]
+        L.or_rmsprop_step.argtypes = [F32P, F32P, F32P, F32P, ctypes.c_int64] + [ctypes.c_float] * 5
+        L.or_adagrad_step.argtypes = [F32P, F32P, F32P, ctypes.c_int64] + [ctypes.c_float] * 3
+        for nm in ("or_adamax_step", "or_nadam_step"):
+            getattr(L, nm).argtypes = [F32P, F32P, F32P, F32P, ctypes.c_int64] + [ctypes.c_float] * 7
+        L.or_radam_step.argtypes = [F32P, F32P, F32P, F32P, ctypes.c_int64] + [ctypes.c_float] * 8 + [ctypes.c_int64]
         _lib = L
     return _lib
 
@@ -278,10 +283,17 @@ class OracleRuntime:
     # ---- creation (creationOps.ts) ---------------------------------------
     def tensorFromData(self, data, shape, dtype):
         n = _prod(shape)
-        if isinstance(data, np.ndarray) and dtype.startswith("float"):
+        if isinstance(data, np.ndarray):  # the same coercions as the list path, array-wide
             if data.size != n:
                 raise RuntimeError(f"tensorFromData expected {n} values, got {data.size}.")
-            return self._reg(np.array(data, dtype=np.float32).reshape(-1), shape, dtype)
+            a = np.asarray(data).reshape(-1)
+            if dtype == "bool":
+                a = (a != 0)
+            elif dtype.startswith("uint"):
+                a = np.maximum(np.trunc(a.astype(np.float64)), 0)
+            elif dtype.startswith("int"):
+                a = np.trunc(a.astype(np.float64))
+            return self._reg(np.array(a, dtype=np.float32), shape, dtype)
         vals = list(data)
         if len(vals) != n:
             raise RuntimeError(f"tensorFromData expected {n} values, got {len(vals)}.")
@@ -813,6 +825,67 @@ class OracleRuntime:
     def sgdStepMulti(self, ps, gs, bufs, lr, momentum, wd, dampening, nesterov):
         for p, g, b in zip(ps, gs, bufs):
             self.sgdStep(p, g, b, lr, momentum, wd, dampening, nesterov)
+
+    def rmspropStep(self, p, g, squareAvg, momentumBuf, lr, alpha, eps, weightDecay, momentum):
+        P, G, S, B = self._check4(p, g, squareAvg, momentumBuf)
+        lib().or_rmsprop_step(fp(P), fp(G), fp(S), fp(B), P.size, lr, alpha, eps, weightDecay, momentum)
+
+    def adagradStep(self, p, g, sumSquares, lr, eps, weightDecay):
+        P, G, S = self._check4(p, g, sumSquares)
+        lib().or_adagrad_step(fp(P), fp(G), fp(S), P.size, lr, eps, weightDecay)
+
+    def adamaxStep(self, p, g, expAvg, expInf, lr, b1, b2, eps, wd, stepSize, biasCorrection1):
+        P, G, M, U = self._check4(p, g, expAvg, expInf)
+        lib().or_adamax_step(fp(P), fp(G), fp(M), fp(U), P.size, lr, b1, b2, eps, wd, stepSize, biasCorrection1)
+
+    def nadamStep(self, p, g, expAvg, expAvgSq, lr, b1, b2, eps, wd, stepSize, mu):
+        P, G, M, V = self._check4(p, g, expAvg, expAvgSq)
+        lib().or_nadam_step(fp(P), fp(G), fp(M), fp(V), P.size, lr, b1, b2, eps, wd, stepSize, mu)
+
+    def radamStep(self, p, g, expAvg, expAvgSq, lr, b1, b2, eps, wd, stepSize, beta1PowT, beta2PowT, stepCount=0):
+        P, G, M, V = self._check4(p, g, expAvg, expAvgSq)
+        lib().or_radam_step(fp(P), fp(G), fp(M), fp(V), P.size, lr, b1, b2, eps, wd, stepSize, beta1PowT, beta2PowT,
+                            int(stepCount))
+
+    def rmspropStepMulti(self, ps, gs, sqs, mbs, lr, alpha, eps, weightDecay, momentum):
+        for a in zip(ps, gs, sqs, mbs):
+            self.rmspropStep(*a, lr, alpha, eps, weightDecay, momentum)
+
+    def adagradStepMulti(self, ps, gs, sums, lr, eps, weightDecay):
+        for a in zip(ps, gs, sums):
+            self.adagradStep(*a, lr, eps, weightDecay)
+
+    def adamaxStepMulti(self, ps, gs, ms, us, *hp):
+        for a in zip(ps, gs, ms, us):
+            self.adamaxStep(*a, *hp)
+
+    def nadamStepMulti(self, ps, gs, ms, vs, *hp):
+        for a in zip(ps, gs, ms, vs):
+            self.nadamStep(*a, *hp)
+
+    def radamStepMulti(self, ps, gs, ms, vs, *hp):
+        for a in zip(ps, gs, ms, vs):
+            self.radamStep(*a, *hp)
+
+    # ---- conv2d with a bias tensor; bulk bytes ----------------------------
+    def conv2dDevBias(self, inp, weight, bias, stride, padding, dilation, groups):
+        blist = self.array(bias).tolist() if bias is not None else None
+        return self.conv2d(inp, weight, blist, stride, padding, dilation, groups)
+
+    def toBytes(self, tid, fmt: str = "float32") -> bytes:
+        x = self.array(tid)
+        if fmt == "int64":
+            return np.trunc(x).astype("<i8").tobytes()
+        return x.astype("<f4").tobytes()
+
+    def fromBytes(self, data, shape, dtype, fmt: str = "float32"):
+        if fmt == "int64":
+            arr = np.frombuffer(bytes(data), dtype="<i8").astype(np.float32)
+        else:
+            arr = np.frombuffer(bytes(data), dtype="<f4").astype(np.float32)
+        if arr.size != _prod(shape):
+            raise RuntimeError(f"fromBytes: {arr.size} values for shape {list(shape)}")
+        return self._reg(arr, shape, dtype)
 
     # ---- readback / lifetime ---------------------------------------------
     def toList(self, tid):

@@ -23,6 +23,13 @@ namespace tp {
 static int g_gemm_path = 0;
 int gemm_path() { return g_gemm_path; }
 
+// Most k-blocks (32 k each) one split of a tensor-core GEMM accumulates in
+// TMEM (0: no cap).  The accumulator's additions are not round-to-nearest over
+// very long sums, so long reductions (a weight gradient over 10^6 pixels) are
+// cut into splits whose partials are then added on CUDA cores.
+static int g_gemm_kmax = 0;
+int gemm_kmax() { return g_gemm_kmax; }
+
 // Each translation unit that holds tensor-core kernels has its own copy of
 // tc::g_status (this one and tp_conv_nhwc.cu); the status is the first nonzero.
 int tc_status(bool reset) {
@@ -225,6 +232,13 @@ TP_API int tp_set_gemm_path(int path) {
                "gemm path must be 0 (tensor cores, TMA-fed where possible, CTA pairs for large N), 1 (CUDA cores), "
                "2 (tensor cores without TMA), 3 (as 0 on single CTAs) or 4 (as 0 with CTA pairs wherever they fit)");
     g_gemm_path = path;
+  });
+}
+
+TP_API int tp_set_gemm_kmax(int kblocks) {
+  return guard([&] {
+    TP_REQUIRE(kblocks >= 0, "tp_set_gemm_kmax: k-blocks per split must be >= 0 (0: no cap)");
+    g_gemm_kmax = kblocks;
   });
 }
 

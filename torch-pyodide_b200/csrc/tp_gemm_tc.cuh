@@ -446,9 +446,16 @@ int tc_status_nhwc(bool reset);  // the channels-last conv module's status word
 // (each split writes and the reduce reads out_elems floats; one unit ~ one
 // k-block of time per ~0.7 M floats of the whole GPU's traffic), keeping
 // >= 8 k-blocks per split.
+int gemm_kmax();
+
 inline int gemm_splits(int64_t tiles, int64_t K, int sms, int64_t out_elems) {
   if (K <= 0 || tiles <= 0) return 1;
   const int64_t nk = (K + 31) / 32;
+  const int kmax = gemm_kmax();
+  if (kmax > 0 && nk > kmax) {  // accuracy floor first: no split accumulates more than kmax k-blocks
+    const int64_t need = (nk + kmax - 1) / kmax;
+    return (int)(need < 2048 ? need : 2048);
+  }
   int64_t maxs = nk / 8;
   if (maxs > 64) maxs = 64;
   if (maxs <= 1) return 1;

@@ -1,0 +1,563 @@
+"""Drop-in rebinding of the reference package's hot composites onto the
+runtime's fused entries.
+
+``tpcuda.shim.install(runtime)`` alone lets the unmodified reference ``torch``
+package run on the CUDA runtime, with the reference's own behaviour, defects
+included.  ``apply()`` then rebinds, inside the already imported reference
+package, the few functions whose reference form either cannot train a CNN or
+issues a chain of tiny kernels where one fused entry exists:
+
+* ``max_pool2d_from_tensor`` (python/torch/tensor_nn_ops.py:57-72) registers no
+  autograd node, so gradients stop at every max-pool (defect D2).  Rebound onto
+  ``maxPool2dWithIndices`` with a node whose backward is ``maxPool2dBackward``.
+* ``batch_norm_from_tensor`` training path (tensor_nn_ops.py:92-254) is a
+  ~14-dispatch Python composite whose backward (autograd_rules.py:1049-1130)
+  throws for W != C (D3) and scales the parameter gradients by gamma (D4).
+  Rebound onto ``batchNormTrain`` / ``batchNormBackward`` (PyTorch's rule; the
+  running statistics are updated in place with the same momentum and unbiased
+  variance as tensor_nn_ops.py:206-217).  The eval path is unchanged.
+* ``layer_norm_from_tensor`` autograd path (tensor_nn_ops.py:363-453,
+  autograd_rules.py:1133-1209): rebound onto ``layerNormForward`` /
+  ``layerNormBackward``.  The no-grad path is unchanged.
+* ``conv2d_from_tensors`` (tensor_nn_ops.py:12-54) reads the bias back to the
+  host on every call (``bias.tolist()``); rebound onto ``conv2dDevBias``, the
+  same convolution with the bias left on the device.
+* the ``step`` of SGD, Adam, AdamW, RMSprop, Adagrad, Adamax, NAdam and RAdam
+  (optim/__init__.py:158-900) loop over parameters with one runtime call each;
+  rebound onto one ``*StepMulti`` call per parameter group (per distinct step
+  count where the hyper-parameters depend on it), with the same state layout
+  (``self.state[id(p)]``), the same host-side scalars and the same fused step.
+* checkpoint I/O: ``_save._tensor_to_raw_bytes`` (_save.py:109-125) and
+  ``_save._rebuild_tensor_v2`` (_save.py:77-103) move every value through a
+  Python list; rebound onto ``toBytes`` / ``fromBytes``, one copy per tensor,
+  producing byte-identical archives.
+* ``tensor_from_data`` (tensor_factories_ops.py:18-25) flattens its data to a
+  Python list; a numpy array now goes to the runtime as one buffer.
+* ``tensor_shape_utils._scalar_to_tensor`` (tensor_shape_utils.py:13-24), the
+  Python-scalar operand of every ``x + 1.0``-style op, makes a zeros([1])
+  tensor, fills a second one and never frees the first (D10): rebound onto one
+  ``full([1], value)``.
+* tensor lifetime (D7): ``Tensor._set`` rebinds an id without freeing the old
+  buffer and ``Tensor`` has no finaliser (_tensor.py:27,1308-1313), so every
+  intermediate stays allocated until an explicit ``destroy``.  ``apply()``
+  counts, per runtime id, the live ``Tensor`` objects that hold it (the ``_id``
+  slot is wrapped by a counting descriptor and ``__del__`` is added); when the
+  count reaches zero the id is destroyed.  Ids are never reused by the runtime,
+  so an explicit ``destroy`` followed by the count's own is harmless.  Tensors
+  caught in reference cycles (autograd nodes) are freed when Python's cycle
+  collector runs.
+
+Every rebinding keeps the reference's signature and argument meaning;
+``remove()`` restores the originals.
+"""
+from __future__ import annotations
+
+import sys
+
+import numpy as np
+
+_saved: list[tuple[object, str, object]] = []
+_life = None
+_MISSING = object()
+
+
+def _set(obj, name, value):
+    old = obj.__dict__.get(name, _MISSING) if isinstance(obj, type) else getattr(obj, name)
+    _saved.append((obj, name, old))
+    setattr(obj, name, value)
+
+
+def _mods():
+    m = sys.modules
+    return (m["torch"], m["torch._tensor"], m["torch._runtime"], m["torch.autograd"], m["torch.grad_mode"],
+            m["torch.tensor_ops"])
+
+
+def _rt():
+    from torch._runtime import _get_runtime
+    return _get_runtime()
+
+
+def _run(x):
+    from torch._runtime import _run_js_awaitable
+    return _run_js_awaitable(x)
+
+
+def _wrap(meta, requires_grad=False):
+    from torch._tensor import Tensor
+    from torch.tensor_ops import _js_meta_to_tuple
+    tid, shape, dtype = _js_meta_to_tuple(meta)
+    return Tensor(tid, shape, dtype, _requires_grad=requires_grad)
+
+
+# ---- tensor lifetime (D7) --------------------------------------------------------------------
+
+class _Lifetime:
+    """Live Tensor objects per runtime id; the id is destroyed at zero."""
+
+    def __init__(self):
+        self.count: dict[int, int] = {}
+        self.enabled = True
+
+    def inc(self, tid):
+        if tid is not None:
+            self.count[tid] = self.count.get(tid, 0) + 1
+
+    def dec(self, tid):
+        c = self.count.get(tid)
+        if c is None:
+            return
+        if c > 1:
+            self.count[tid] = c - 1
+            return
+        del self.count[tid]
+        if self.enabled:
+            try:
+                _rt().destroy(int(tid))
+            except Exception:  # interpreter shutdown, runtime already gone
+                pass
+
+
+def _install_lifetime(Tensor):
+    global _life
+    life = _Lifetime()
+    slot = Tensor.__dict__["_id"]
+
+    class _CountedId:
+        """The ``_id`` slot, counting the Tensor objects that hold each id."""
+
+        def __get__(self, obj, cls=None):
+            if obj is None:
+                return self
+            return slot.__get__(obj, cls)
+
+        def __set__(self, obj, value):
+            try:
+                old = slot.__get__(obj, type(obj))
+            except AttributeError:
+                old = None
+            slot.__set__(obj, value)
+            if value != old:
+                life.inc(value)
+                if old is not None:
+                    life.dec(old)
+
+    def __del__(self):
+        try:
+            tid = slot.__get__(self, type(self))
+        except AttributeError:
+            return
+        life.dec(tid)
+
+    _set(Tensor, "_id", _CountedId())
+    _set(Tensor, "__del__", __del__)
+    _life = life
+
+
+# ---- max-pool with indices and its backward (D2) ------------------------------------------------
+
+def max_pool2d_from_tensor(input, kernel_size, stride=None, padding=(0,), dilation=(1,)):
+    from torch.autograd import _Node, is_grad_enabled
+    rt = _rt()
+    ksize = [int(k) for k in kernel_size]
+    strd = [int(s) for s in (stride if stride is not None else kernel_size)]
+    pad = [int(p) for p in padding]
+    dil = [int(d) for d in dilation]
+    if not (is_grad_enabled() and input._requires_grad):
+        return _wrap(_run(rt.maxPool2d(input._id, ksize, strd, pad, dil)))
+    y_meta, idx_meta = _run(rt.maxPool2dWithIndices(input._id, ksize, strd, pad, dil))
+    out = _wrap(y_meta, requires_grad=True)
+    idx = _wrap(idx_meta)
+    in_shape = list(input._shape)
+
+    def grad_fn(g, idx=idx):
+        return (_wrap(_run(rt.maxPool2dBackward(g._id, idx._id, in_shape, ksize, strd, pad, dil))),)
+
+    out._node = _Node(out, grad_fn, [input])
+    return out
+
+
+# ---- BatchNorm training (D3, D4) ------------------------------------------------------------------
+
+def _make_batch_norm(original):
+    def batch_norm_from_tensor(input, weight=None, bias=None, running_mean=None, running_var=None, eps=1e-5,
+                               training=False, momentum=0.1):
+        if not training:
+            return original(input, weight, bias, running_mean, running_var, eps, training, momentum)
+        from torch.autograd import _Node, is_grad_enabled
+        if len(input._shape) < 2:
+            raise RuntimeError("batch_norm expects at least 2D input (N, C, ...)")
+        rt = _rt()
+        oid = lambda t: t._id if t is not None else None  # noqa: E731
+        y_m, mean_m, inv_m = _run(rt.batchNormTrain(input._id, oid(weight), oid(bias), oid(running_mean),
+                                                    oid(running_var), float(eps), float(momentum)))
+        any_grad = input._requires_grad or (weight is not None and weight._requires_grad) or (
+            bias is not None and bias._requires_grad)
+        if not (is_grad_enabled() and any_grad):
+            _wrap(mean_m), _wrap(inv_m)  # released at once
+            return _wrap(y_m)
+        out = _wrap(y_m, requires_grad=True)
+        mean, inv = _wrap(mean_m), _wrap(inv_m)
+        parents = [input] + [t for t in (weight, bias) if t is not None]
+
+        def grad_fn(g, mean=mean, inv=inv):
+            dx, dw, db = (_wrap(m) for m in _run(rt.batchNormBackward(g._id, input._id, oid(weight), mean._id,
+                                                                       inv._id)))
+            grads = [dx]
+            if weight is not None:
+                grads.append(dw)
+            if bias is not None:
+                grads.append(db)
+            return tuple(grads)
+
+        out._node = _Node(out, grad_fn, parents)
+        return out
+    return batch_norm_from_tensor
+
+
+# ---- LayerNorm with autograd ------------------------------------------------------------------------
+
+def _make_layer_norm(original):
+    def layer_norm_from_tensor(input, normalized_shape, weight=None, bias=None, eps=1e-5):
+        from torch.autograd import _Node, is_grad_enabled
+        if len(normalized_shape) > len(input._shape):
+            raise RuntimeError("layer_norm normalized_shape has more dims than input")
+        any_grad = input._requires_grad or (weight is not None and weight._requires_grad) or (
+            bias is not None and bias._requires_grad)
+        if not (is_grad_enabled() and any_grad):
+            return original(input, normalized_shape, weight, bias, eps)
+        rt = _rt()
+        ns = [int(s) for s in normalized_shape]
+        oid = lambda t: t._id if t is not None else None  # noqa: E731
+        y_m, mean_m, rstd_m = _run(rt.layerNormForward(input._id, ns, oid(weight), oid(bias), float(eps)))
+        out = _wrap(y_m, requires_grad=True)
+        mean, rstd = _wrap(mean_m), _wrap(rstd_m)
+        parents = [input] + [t for t in (weight, bias) if t is not None]
+
+        def grad_fn(g, mean=mean, rstd=rstd):
+            dx, dw, db = (_wrap(m) for m in _run(rt.layerNormBackward(g._id, input._id, ns, oid(weight), mean._id,
+                                                                       rstd._id)))
+            grads = [dx]
+            if weight is not None:
+                grads.append(dw)
+            if bias is not None:
+                grads.append(db)
+            return tuple(grads)
+
+        out._node = _Node(out, grad_fn, parents)
+        return out
+    return layer_norm_from_tensor
+
+
+# ---- conv2d with the bias on the device -----------------------------------------------------------------
+
+def conv2d_from_tensors(input, weight, bias=None, stride=(1,), padding=(0,), dilation=(1,), groups=1):
+    from torch.autograd import _grad_conv2d, _Node, is_grad_enabled
+    rt = _rt()
+    meta = _run(rt.conv2dDevBias(input._id, weight._id, bias._id if bias is not None else None,
+                                 [int(s) for s in stride], [int(p) for p in padding], [int(d) for d in dilation],
+                                 int(groups)))
+    need = input._requires_grad or weight._requires_grad or (bias is not None and bias._requires_grad)
+    if not (is_grad_enabled() and need):
+        return _wrap(meta)
+    result = _wrap(meta, requires_grad=True)
+    out_shape = list(result._shape)
+    params = (tuple(stride), tuple(padding), tuple(dilation), int(groups), bias)
+    parents = [p for p in (input, weight, bias) if p is not None]
+    gidx = [i for i, p in enumerate((input, weight, bias)) if p is not None]
+
+    def grad_fn(g, inp=input, wt=weight, out_sh=out_shape, pr=params, gidx=gidx):
+        all_grads = _grad_conv2d(g, inp, wt, out_sh, pr)
+        return tuple(all_grads[i] for i in gidx)
+
+    result._node = _Node(result, grad_fn, parents)
+    return result
+
+
+# ---- optimizers: one fused launch per group -------------------------------------------------------------
+
+def _zeros_like(p):
+    import torch
+    return torch.zeros_like(p)
+
+
+def _params_with_grad(group):
+    return [p for p in group["params"] if p.grad is not None]
+
+
+def _by_step(opt, ps, init):
+    """Advance each parameter's step count (creating its state with `init`
+    on first use) and group the parameters by their new count."""
+    groups: dict[int, list] = {}
+    for p in ps:
+        st = opt.state.get(id(p))
+        if st is None:
+            st = opt.state[id(p)] = init(p)
+        st["step"] = int(st["step"]) + 1
+        groups.setdefault(st["step"], []).append(p)
+    return groups
+
+
+def _sgd_step(self, closure=None):
+    from torch.grad_mode import no_grad
+    from torch.optim import Optimizer
+    loss = Optimizer.step(self, closure)
+    rt = _rt()
+    with no_grad():
+        for group in self.param_groups:
+            ps = _params_with_grad(group)
+            bufs = []
+            for p in ps:
+                st = self.state.setdefault(id(p), {})
+                if st.get("momentum_buffer") is None:
+                    st["momentum_buffer"] = _zeros_like(p)
+                bufs.append(st["momentum_buffer"]._id)
+            if ps:
+                _run(rt.sgdStepMulti([p._id for p in ps], [p.grad._id for p in ps], bufs, float(group["lr"]),
+                                     float(group["momentum"]), float(group["weight_decay"]),
+                                     float(group["dampening"]), bool(group["nesterov"])))
+    return loss
+
+
+def _adam_like(kind):
+    def step(self, closure=None):
+        from torch.grad_mode import no_grad
+        from torch.optim import Optimizer
+        loss = Optimizer.step(self, closure)
+        rt = _rt()
+        init = lambda p: {"step": 0, "exp_avg": _zeros_like(p), "exp_avg_sq": _zeros_like(p),  # noqa: E731
+                          "max_exp_avg_sq": None}
+        with no_grad():
+            for group in self.param_groups:
+                lr = float(group["lr"])
+                beta1, beta2 = group["betas"]
+                eps, wd = float(group["eps"]), float(group["weight_decay"])
+                for stp, ps in _by_step(self, _params_with_grad(group), init).items():
+                    for p in ps:  # states made by the reference's own step start as None
+                        st = self.state[id(p)]
+                        for k in ("exp_avg", "exp_avg_sq"):
+                            if st.get(k) is None:
+                                st[k] = _zeros_like(p)
+                    bc1 = 1.0 - beta1 ** stp
+                    bc2 = 1.0 - beta2 ** stp
+                    step_size = lr / bc1
+                    inv_sqrt_bc2 = 1.0 / (bc2 ** 0.5)
+                    fn = rt.adamWStepMulti if kind == "adamw" else rt.adamStepMulti
+                    _run(fn([p._id for p in ps], [p.grad._id for p in ps],
+                            [self.state[id(p)]["exp_avg"]._id for p in ps],
+                            [self.state[id(p)]["exp_avg_sq"]._id for p in ps], lr, float(beta1), float(beta2), eps,
+                            wd, float(step_size), float(inv_sqrt_bc2)))
+        return loss
+    return step
+
+
+def _rmsprop_step(self, closure=None):
+    from torch.grad_mode import no_grad
+    from torch.optim import Optimizer
+    loss = Optimizer.step(self, closure)
+    rt = _rt()
+    with no_grad():
+        for group in self.param_groups:
+            ps = _params_with_grad(group)
+            for p in ps:
+                st = self.state.setdefault(id(p), {"square_avg": None, "momentum_buffer": None})
+                for k in ("square_avg", "momentum_buffer"):
+                    if st.get(k) is None:
+                        st[k] = _zeros_like(p)
+            if ps:
+                _run(rt.rmspropStepMulti([p._id for p in ps], [p.grad._id for p in ps],
+                                         [self.state[id(p)]["square_avg"]._id for p in ps],
+                                         [self.state[id(p)]["momentum_buffer"]._id for p in ps],
+                                         float(group["lr"]), float(group["alpha"]), float(group["eps"]),
+                                         float(group["weight_decay"]), float(group["momentum"])))
+    return loss
+
+
+def _adagrad_step(self, closure=None):
+    import torch
+    from torch.grad_mode import no_grad
+    from torch.optim import Optimizer
+    loss = Optimizer.step(self, closure)
+    rt = _rt()
+    with no_grad():
+        for group in self.param_groups:
+            lr, lr_decay = float(group["lr"]), float(group["lr_decay"])
+            init = lambda p: {"step": 0, "sum": torch.full_like(p, float(group["initial_accumulator_value"]))}  # noqa
+            for stp, ps in _by_step(self, _params_with_grad(group), init).items():
+                clr = lr / (1.0 + (stp - 1) * lr_decay)
+                _run(rt.adagradStepMulti([p._id for p in ps], [p.grad._id for p in ps],
+                                         [self.state[id(p)]["sum"]._id for p in ps], float(clr), float(group["eps"]),
+                                         float(group["weight_decay"])))
+    return loss
+
+
+def _adamax_step(self, closure=None):
+    from torch.grad_mode import no_grad
+    from torch.optim import Optimizer
+    loss = Optimizer.step(self, closure)
+    rt = _rt()
+    init = lambda p: {"step": 0, "exp_avg": _zeros_like(p), "exp_inf": _zeros_like(p)}  # noqa: E731
+    with no_grad():
+        for group in self.param_groups:
+            lr = float(group["lr"])
+            beta1, beta2 = group["betas"]
+            for stp, ps in _by_step(self, _params_with_grad(group), init).items():
+                step_size = lr / (1.0 - beta1 ** stp)
+                _run(rt.adamaxStepMulti([p._id for p in ps], [p.grad._id for p in ps],
+                                        [self.state[id(p)]["exp_avg"]._id for p in ps],
+                                        [self.state[id(p)]["exp_inf"]._id for p in ps], lr, float(beta1),
+                                        float(beta2), float(group["eps"]), float(group["weight_decay"]),
+                                        float(step_size), 1.0))
+    return loss
+
+
+def _nadam_step(self, closure=None):
+    from torch.grad_mode import no_grad
+    from torch.optim import Optimizer
+    loss = Optimizer.step(self, closure)
+    rt = _rt()
+    init = lambda p: {"step": 0, "exp_avg": _zeros_like(p), "exp_avg_sq": _zeros_like(p)}  # noqa: E731
+    with no_grad():
+        for group in self.param_groups:
+            lr = float(group["lr"])
+            beta1, beta2 = group["betas"]
+            md = float(group["momentum_decay"])
+            for stp, ps in _by_step(self, _params_with_grad(group), init).items():
+                mu_next = beta1 * (1.0 - 0.5 * (0.96 ** ((stp + 1) * md)))
+                step_size = lr / (1.0 - beta1 ** stp)
+                _run(rt.nadamStepMulti([p._id for p in ps], [p.grad._id for p in ps],
+                                       [self.state[id(p)]["exp_avg"]._id for p in ps],
+                                       [self.state[id(p)]["exp_avg_sq"]._id for p in ps], lr, float(beta1),
+                                       float(beta2), float(group["eps"]), float(group["weight_decay"]),
+                                       float(step_size), float(mu_next)))
+    return loss
+
+
+def _radam_step(self, closure=None):
+    from torch.grad_mode import no_grad
+    from torch.optim import Optimizer
+    loss = Optimizer.step(self, closure)
+    rt = _rt()
+    init = lambda p: {"step": 0, "exp_avg": _zeros_like(p), "exp_avg_sq": _zeros_like(p)}  # noqa: E731
+    with no_grad():
+        for group in self.param_groups:
+            lr = float(group["lr"])
+            beta1, beta2 = group["betas"]
+            for stp, ps in _by_step(self, _params_with_grad(group), init).items():
+                step_size = lr / (1.0 - beta1 ** stp)
+                _run(rt.radamStepMulti([p._id for p in ps], [p.grad._id for p in ps],
+                                       [self.state[id(p)]["exp_avg"]._id for p in ps],
+                                       [self.state[id(p)]["exp_avg_sq"]._id for p in ps], lr, float(beta1),
+                                       float(beta2), float(group["eps"]), float(group["weight_decay"]),
+                                       float(step_size), float(beta1 ** stp), float(beta2 ** stp), int(stp)))
+    return loss
+
+
+# ---- checkpoint bytes -----------------------------------------------------------------------------
+
+def _tensor_to_raw_bytes(t) -> bytes:
+    dtype_str = str(t.dtype).replace("torch.", "")
+    if dtype_str == "float32":
+        return _run(_rt().toBytes(t._id, "float32"))
+    if dtype_str in ("int64", "long"):
+        return _run(_rt().toBytes(t._id, "int64"))
+    raise NotImplementedError(f"save: dtype {dtype_str!r} is not supported (only float32, int64).")
+
+
+def _rebuild_tensor_v2(storage, storage_offset, size, stride, requires_grad, backward_hooks):
+    raw = storage._raw
+    elem_size = getattr(storage, "_elem_size", 4)
+    if storage_offset:
+        raw = raw[storage_offset * elem_size:]
+    n = len(raw) // elem_size
+    if elem_size == 4:
+        fmt, dtype = "float32", "float32"
+    elif elem_size == 8:
+        fmt, dtype = "int64", "int64"
+    else:
+        raise NotImplementedError(f"Unsupported storage element size: {elem_size}")
+    size_list = list(size) if hasattr(size, "__iter__") else [int(size)]
+    rt = _rt()
+    if not size_list:
+        return _wrap(_run(rt.fromBytes(raw[:elem_size], [1], dtype, fmt))).reshape([])
+    return _wrap(_run(rt.fromBytes(raw[:n * elem_size], size_list, dtype, fmt)))
+
+
+# ---- Python scalars as one-element tensors -------------------------------------------------------
+
+def _scalar_to_tensor(value, dtype="float32"):
+    return _wrap(_run(_rt().full([1], float(value), dtype)))
+
+
+# ---- numpy data without a Python list ------------------------------------------------------------
+
+def _make_tensor_from_data(original):
+    def tensor_from_data(data, shape=None, dtype="float32", requires_grad=False):
+        if not isinstance(data, np.ndarray):
+            return original(data, shape, dtype, requires_grad)
+        a = np.asarray(data)
+        shp = list(a.shape) if shape is None else [int(s) for s in shape]
+        if dtype == "bool":
+            a = (a != 0)
+        elif str(dtype).startswith("uint"):
+            a = np.maximum(np.trunc(a.astype(np.float64)), 0)
+        elif str(dtype).startswith("int"):
+            a = np.trunc(a.astype(np.float64))
+        flat = np.ascontiguousarray(a, dtype=np.float32).reshape(-1)
+        return _wrap(_run(_rt().tensorFromData(flat, shp, dtype)), requires_grad=requires_grad)
+    return tensor_from_data
+
+
+# ---- apply / remove -------------------------------------------------------------------------------
+
+def apply(lifetime: bool = True) -> None:
+    """Rebind the functions listed in the module docstring inside the imported
+    reference ``torch`` package (import it first, after ``shim.install``)."""
+    if _saved:
+        return
+    torch, _tensor, _runtime, autograd, grad_mode, tensor_ops = _mods()
+    import torch._save as _save
+    import torch.optim as optim
+    import torch.tensor_factories_ops as tfo
+    _set(_tensor, "max_pool2d_from_tensor", max_pool2d_from_tensor)
+    _set(_tensor, "batch_norm_from_tensor", _make_batch_norm(_tensor.batch_norm_from_tensor))
+    _set(_tensor, "layer_norm_from_tensor", _make_layer_norm(_tensor.layer_norm_from_tensor))
+    _set(_tensor, "conv2d_from_tensors", conv2d_from_tensors)
+    _set(optim.SGD, "step", _sgd_step)
+    _set(optim.Adam, "step", _adam_like("adam"))
+    _set(optim.AdamW, "step", _adam_like("adamw"))
+    _set(optim.RMSprop, "step", _rmsprop_step)
+    _set(optim.Adagrad, "step", _adagrad_step)
+    _set(optim.Adamax, "step", _adamax_step)
+    _set(optim.NAdam, "step", _nadam_step)
+    _set(optim.RAdam, "step", _radam_step)
+    import torch.tensor_shape_utils as tsu
+    _set(tsu, "_scalar_to_tensor", _scalar_to_tensor)
+    _set(_save, "_tensor_to_raw_bytes", _tensor_to_raw_bytes)
+    _set(_save, "_rebuild_tensor_v2", _rebuild_tensor_v2)
+    orig_tfd = tfo.tensor_from_data
+    fast = _make_tensor_from_data(orig_tfd)
+    for name, mod in list(sys.modules.items()):
+        if (name == "torch" or name.startswith("torch.")) and getattr(mod, "tensor_from_data", None) is orig_tfd:
+            _set(mod, "tensor_from_data", fast)
+    if lifetime:
+        _install_lifetime(_tensor.Tensor)
+
+
+def remove() -> None:
+    """Put back every original the last ``apply()`` replaced."""
+    global _life
+    if _life is not None:
+        _life.enabled = False
+    while _saved:
+        obj, name, value = _saved.pop()
+        if value is _MISSING:
+            delattr(obj, name)
+        else:
+            setattr(obj, name, value)
+    _life = None
+
+
+def live_ids() -> int:
+    """Number of runtime ids currently held by live Tensor objects."""
+    return len(_life.count) if _life is not None else 0

@@ -490,6 +490,83 @@ class CudaRuntime:
         check(self.lib.tp_sgd_step_multi(i64arr(ps), i64arr(gs), i64arr(bufs), len(ps), lr, momentum, wd, dampening,
                                          1 if nesterov else 0))
 
+    # ---- the other fused optimizer steps (runtime.ts:683-801), in place ----------
+    def rmspropStep(self, p, g, squareAvg, momentumBuf, lr, alpha, eps, weightDecay, momentum):
+        check(self.lib.tp_rmsprop_step(int(p), int(g), int(squareAvg), int(momentumBuf), lr, alpha, eps, weightDecay,
+                                       momentum))
+
+    def adagradStep(self, p, g, sumSquares, lr, eps, weightDecay):
+        check(self.lib.tp_adagrad_step(int(p), int(g), int(sumSquares), lr, eps, weightDecay))
+
+    def adamaxStep(self, p, g, expAvg, expInf, lr, b1, b2, eps, wd, stepSize, biasCorrection1):
+        check(self.lib.tp_adamax_step(int(p), int(g), int(expAvg), int(expInf), lr, b1, b2, eps, wd, stepSize,
+                                      biasCorrection1))
+
+    def nadamStep(self, p, g, expAvg, expAvgSq, lr, b1, b2, eps, wd, stepSize, mu):
+        check(self.lib.tp_nadam_step(int(p), int(g), int(expAvg), int(expAvgSq), lr, b1, b2, eps, wd, stepSize, mu))
+
+    def radamStep(self, p, g, expAvg, expAvgSq, lr, b1, b2, eps, wd, stepSize, beta1PowT, beta2PowT, stepCount=0):
+        check(self.lib.tp_radam_step(int(p), int(g), int(expAvg), int(expAvgSq), lr, b1, b2, eps, wd, stepSize,
+                                     beta1PowT, beta2PowT, int(stepCount)))
+
+    def rmspropStepMulti(self, ps, gs, sqs, mbs, lr, alpha, eps, weightDecay, momentum):
+        check(self.lib.tp_rmsprop_step_multi(i64arr(ps), i64arr(gs), i64arr(sqs), i64arr(mbs), len(ps), lr, alpha,
+                                             eps, weightDecay, momentum))
+
+    def adagradStepMulti(self, ps, gs, sums, lr, eps, weightDecay):
+        check(self.lib.tp_adagrad_step_multi(i64arr(ps), i64arr(gs), i64arr(sums), len(ps), lr, eps, weightDecay))
+
+    def adamaxStepMulti(self, ps, gs, ms, us, lr, b1, b2, eps, wd, stepSize, biasCorrection1):
+        check(self.lib.tp_adamax_step_multi(i64arr(ps), i64arr(gs), i64arr(ms), i64arr(us), len(ps), lr, b1, b2, eps,
+                                            wd, stepSize, biasCorrection1))
+
+    def nadamStepMulti(self, ps, gs, ms, vs, lr, b1, b2, eps, wd, stepSize, mu):
+        check(self.lib.tp_nadam_step_multi(i64arr(ps), i64arr(gs), i64arr(ms), i64arr(vs), len(ps), lr, b1, b2, eps,
+                                           wd, stepSize, mu))
+
+    def radamStepMulti(self, ps, gs, ms, vs, lr, b1, b2, eps, wd, stepSize, beta1PowT, beta2PowT, stepCount):
+        check(self.lib.tp_radam_step_multi(i64arr(ps), i64arr(gs), i64arr(ms), i64arr(vs), len(ps), lr, b1, b2, eps,
+                                           wd, stepSize, beta1PowT, beta2PowT, int(stepCount)))
+
+    # ---- conv2d with a device bias (no readback of the bias) ---------------------
+    def conv2dDevBias(self, inp, weight, bias, stride, padding, dilation, groups):
+        st, pd, dl = list(stride), list(padding), list(dilation)
+        return self._call(self.lib.tp_conv2d_dev_bias, int(inp), int(weight), int(bias) if bias is not None else 0,
+                          i64arr(st), len(st), i64arr(pd), len(pd), i64arr(dl), len(dl), int(groups))
+
+    # ---- bulk bytes (checkpoints) and pinned uploads ------------------------------
+    def toBytes(self, tid, fmt: str = "float32") -> bytes:
+        """The tensor's values as little-endian float32 (or int64) bytes."""
+        code = {"float32": 0, "int64": 1}[fmt]
+        n = _prod(self._meta(tid)["shape"])
+        buf = ctypes.create_string_buffer(n * (4 if code == 0 else 8))
+        check(self.lib.tp_to_bytes(int(tid), buf, len(buf), code))
+        return buf.raw
+
+    def fromBytes(self, data, shape, dtype, fmt: str = "float32"):
+        code = {"float32": 0, "int64": 1}[fmt]
+        mv = memoryview(data).cast("B")
+        arr = (ctypes.c_char * len(mv)).from_buffer_copy(mv) if mv.readonly else (ctypes.c_char * len(mv)).from_buffer(mv)
+        return self._call(self.lib.tp_from_bytes, arr, len(mv), code, i64arr(shape), len(shape), _dtype_code(dtype))
+
+    def hostAlloc(self, nbytes: int) -> int:
+        p = ctypes.c_void_p()
+        check(self.lib.tp_host_alloc(int(nbytes), ctypes.byref(p)))
+        return int(p.value or 0)
+
+    def hostFree(self, ptr: int) -> None:
+        check(self.lib.tp_host_free(ctypes.c_void_p(ptr)))
+
+    def tensorFromHostAsync(self, host_ptr: int, shape, dtype="float32"):
+        """Upload from pinned host memory on the copy stream; returns (handle, ticket)."""
+        h, t = Handle(), ctypes.c_int64(0)
+        check(self.lib.tp_tensor_from_host_async(ctypes.c_void_p(host_ptr), i64arr(shape), len(shape),
+                                                 _dtype_code(dtype), ctypes.byref(h), ctypes.byref(t)))
+        return h.to_dict(), int(t.value)
+
+    def ticketWait(self, ticket: int) -> None:
+        check(self.lib.tp_ticket_wait(int(ticket)))
+
     # ---- readback / lifetime (runtime.ts:1046-1054) -------------------------------
     def toNumpy(self, tid) -> np.ndarray:
         meta = self._meta(tid)
