@@ -610,6 +610,14 @@ class OracleRuntime:
         lib().or_argmax(fp(x), ip(out), rows, shape[-1])
         return self._reg(out.astype(np.float32), shape[:-1] if len(shape) > 1 else [1], "int32")
 
+    def argmin(self, tid):
+        """argmin.wgsl (reductionOps.ts:140-160): first index of the minimum over
+        the last dim (used only to run the reference's argmax/argmin example)."""
+        x, shape, _ = self._get(tid)
+        rows = _prod(shape[:-1])
+        out = np.argmin(x.reshape(rows, shape[-1]), axis=1).astype(np.float32)
+        return self._reg(out, shape[:-1] if len(shape) > 1 else [1], "int32")
+
     def softmax(self, tid, dim):
         x, shape, dt = self._get(tid)
         d = dim + len(shape) if dim < 0 else dim

@@ -13,8 +13,8 @@ the drop-in tests in a subprocess on one of three back ends:
 
 Every back end starts from the same numpy-seeded weights (loaded with
 load_state_dict) and batch, and writes the per-step losses, the last step's
-parameter gradients and the final parameters to out.npz, plus the number of
-runtime ids alive after each step (the lifetime check).
+parameter gradients (and the first step's), the final parameters to out.npz,
+plus the runtime's allocated bytes after each step (the lifetime check).
 """
 import gc
 import os
@@ -102,20 +102,23 @@ def main():
         opt = torch.optim.Adam(params, lr=1e-3, betas=(0.9, 0.999), eps=1e-8)
     elif opt_name == "adamw":
         opt = torch.optim.AdamW(params, lr=1e-3, weight_decay=0.01)
-    else:
-        opt = torch.optim.SGD(params, lr=0.05, momentum=0.9, weight_decay=5e-4)
+    else:  # momentum and weight decay of the data-parallel config; a smaller lr on
+        # the deep net keeps 3 steps of batch 8 away from chaotic ReLU / max-pool flips
+        opt = torch.optim.SGD(params, lr=0.005 if model_name == "vgg" else 0.05, momentum=0.9, weight_decay=5e-4)
 
     def arr(t):
         return np.asarray(t.detach().tolist() if hasattr(t, "detach") else t.tolist(), np.float32)
 
     losses, live = [], []
-    grads = {}
+    grads, first_grads = {}, {}
     for _ in range(steps):
         opt.zero_grad()
         loss = F.cross_entropy(model(x), y)
         loss.backward()
         losses.append(float(loss.item()))
         grads = {n: arr(p.grad) for n, p in zip(names, params)}
+        if not first_grads:
+            first_grads.update(grads)
         opt.step()
         del loss
         gc.collect()
@@ -125,6 +128,7 @@ def main():
     for n, p in zip(names, params):
         res["param:" + n] = arr(p)
         res["grad:" + n] = grads[n]
+        res["grad0:" + n] = first_grads[n]
     np.savez(out, **res)
 
 

@@ -37,6 +37,12 @@ issues a chain of tiny kernels where one fused entry exists:
   Python-scalar operand of every ``x + 1.0``-style op, makes a zeros([1])
   tensor, fills a second one and never frees the first (D10): rebound onto one
   ``full([1], value)``.
+* ``argmax_from_tensor`` with a ``dim`` (_tensor_runtime_bridge.py:155-165) and
+  ``max_dim_from_tensor`` (tensor_ops.py:1531-1537) go through a full sort of
+  the dimension (topk -> ``runtime.sort``, D9), which is out of range for long
+  rows; rebound onto ``maxDim`` (one reduction, first index of the maximum, as
+  argmax.wgsl).  ``max_dim_from_tensor`` keeps the sort path when a gradient
+  has to flow through it.
 * tensor lifetime (D7): ``Tensor._set`` rebinds an id without freeing the old
   buffer and ``Tensor`` has no finaliser (_tensor.py:27,1308-1313), so every
   intermediate stays allocated until an explicit ``destroy``.  ``apply()``
@@ -483,6 +489,47 @@ def _rebuild_tensor_v2(storage, storage_offset, size, stride, requires_grad, bac
     return _wrap(_run(rt.fromBytes(raw[:n * elem_size], size_list, dtype, fmt)))
 
 
+# ---- max / argmax along a dim as one reduction (D9) ------------------------------------------------
+
+def _norm_dim(tensor, dim):
+    r = len(tensor._shape)
+    d = dim if dim >= 0 else dim + r
+    if d < 0 or d >= r:
+        raise IndexError(f"Dimension out of range (expected to be in range of [{-r}, {r - 1}], got {dim})")
+    return d
+
+
+def _make_argmax(original):
+    def argmax_from_tensor(tensor, dim=None, keepdim=False):
+        if dim is None:
+            return original(tensor)
+        d = _norm_dim(tensor, dim)
+        _, idx = _run(_rt().maxDim(tensor._id, d, bool(keepdim)))
+        return _wrap(idx)
+    return argmax_from_tensor
+
+
+def _make_max_dim(original):
+    def max_dim_from_tensor(tensor, dim, keepdim=False):
+        from torch.autograd import is_grad_enabled
+        if is_grad_enabled() and tensor._requires_grad:
+            return original(tensor, dim, keepdim)
+        d = _norm_dim(tensor, dim)
+        vals, idx = _run(_rt().maxDim(tensor._id, d, bool(keepdim)))
+        return _wrap(vals), _wrap(idx)
+    return max_dim_from_tensor
+
+
+def _rebind(orig, new):
+    """Replace `orig` by `new` in every loaded module of the reference package
+    that holds it at module level."""
+    for name, mod in list(sys.modules.items()):
+        if (name == "torch" or name.startswith("torch.")) and mod is not None:
+            for attr, val in list(vars(mod).items()):
+                if val is orig:
+                    _set(mod, attr, new)
+
+
 # ---- Python scalars as one-element tensors -------------------------------------------------------
 
 def _scalar_to_tensor(value, dtype="float32"):
@@ -535,11 +582,10 @@ def apply(lifetime: bool = True) -> None:
     _set(tsu, "_scalar_to_tensor", _scalar_to_tensor)
     _set(_save, "_tensor_to_raw_bytes", _tensor_to_raw_bytes)
     _set(_save, "_rebuild_tensor_v2", _rebuild_tensor_v2)
-    orig_tfd = tfo.tensor_from_data
-    fast = _make_tensor_from_data(orig_tfd)
-    for name, mod in list(sys.modules.items()):
-        if (name == "torch" or name.startswith("torch.")) and getattr(mod, "tensor_from_data", None) is orig_tfd:
-            _set(mod, "tensor_from_data", fast)
+    _rebind(tfo.tensor_from_data, _make_tensor_from_data(tfo.tensor_from_data))
+    import torch._tensor_runtime_bridge as bridge
+    _rebind(bridge.argmax_from_tensor, _make_argmax(bridge.argmax_from_tensor))
+    _rebind(tensor_ops.max_dim_from_tensor, _make_max_dim(tensor_ops.max_dim_from_tensor))
     if lifetime:
         _install_lifetime(_tensor.Tensor)
 
