@@ -135,14 +135,23 @@ TP_API int tp_from_bytes(const void* src, int64_t nbytes, int format, const int6
 /* New, input pipeline (python/torch/tensor_factories_ops.py:18-25 flattens the
  * data to a Python list per tensor): pinned host buffers, and an upload from
  * one that runs on a dedicated copy stream, overlapping the kernels already
- * queued; later work on the library streams waits for it.  *ticket names the
- * copy: tp_ticket_wait(ticket) returns once it has finished and the host
- * buffer may be refilled. */
+ * queued.  defer == 0: work queued on the library streams after the call waits
+ * for the copy; defer != 0: nothing waits until tp_ticket_use(ticket), which
+ * the caller makes before the tensor's first use (a loader uploads batch i+2
+ * while batch i computes and marks each batch used just before handing it
+ * out).  *ticket names the copy: tp_ticket_wait(ticket) returns once it has
+ * finished and the host buffer may be refilled. */
 TP_API int tp_host_alloc(int64_t bytes, void** out);
 TP_API int tp_host_free(void* ptr);
-TP_API int tp_tensor_from_host_async(const void* pinned_host, const int64_t* shape, int ndim, int dtype,
+TP_API int tp_tensor_from_host_async(const void* pinned_host, const int64_t* shape, int ndim, int dtype, int defer,
                                      tp_handle* out, int64_t* ticket);
+TP_API int tp_ticket_use(int64_t ticket);
 TP_API int tp_ticket_wait(int64_t ticket);
+/* New, batches of a device-resident dataset: out = src[rows] along dim 0 (the
+ * reference DataLoader selects each sample of a TensorDataset with one runtime
+ * call and stacks them, utils/data/__init__.py:24-37,205-210); rows are
+ * checked against dim 0 */
+TP_API int tp_gather_rows(int64_t src, const int64_t* rows, int64_t n, tp_handle* out);
 
 /* ---- creation (creationOps.ts, random.wgsl, fill.wgsl) -------------------- */
 /* zeros/ones/full/empty: creationOps.ts:39-45,107-145 (fill.wgsl) */

@@ -895,6 +895,31 @@ class OracleRuntime:
             raise RuntimeError(f"fromBytes: {arr.size} values for shape {list(shape)}")
         return self._reg(arr, shape, dtype)
 
+    # shapeOps.ts select / cat (runtime.ts:876-897): the reference DataLoader's
+    # per-sample path (TensorDataset indexing, then stack = unsqueeze + cat);
+    # copies, as every reference shape op
+    def select(self, tid, dim, index):
+        x, shape, dt = self._get(tid)
+        d = dim + len(shape) if dim < 0 else dim
+        i = index + shape[d] if index < 0 else index
+        if not 0 <= i < shape[d]:
+            raise RuntimeError(f"select: index {index} out of range for dim {dim} of size {shape[d]}")
+        out = np.take(x.reshape(shape), i, axis=d)
+        return self._reg(np.ascontiguousarray(out).reshape(-1), list(out.shape), dt)
+
+    def cat(self, ids, dim):
+        arrs = [self._get(t) for t in ids]
+        d = dim + len(arrs[0][1]) if dim < 0 else dim
+        out = np.concatenate([a.reshape(sh) for a, sh, _ in arrs], axis=d)
+        return self._reg(out.reshape(-1), list(out.shape), arrs[0][2])
+
+    def gatherRows(self, tid, rows):
+        x, shape, dt = self._get(tid)
+        rows = [int(r) for r in rows]
+        if any(r < 0 or r >= shape[0] for r in rows):
+            raise RuntimeError("gatherRows: index out of bounds for dimension 0")
+        return self._reg(x.reshape(shape[0], -1)[rows].reshape(-1), [len(rows)] + list(shape[1:]), dt)
+
     # ---- readback / lifetime ---------------------------------------------
     def toList(self, tid):
         x, _, dt = self._get(tid)

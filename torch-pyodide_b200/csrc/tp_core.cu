@@ -6,6 +6,7 @@
 #include <cstring>
 #include <mutex>
 #include <unordered_map>
+#include <vector>
 
 #include <cstdlib>
 
@@ -222,6 +223,24 @@ int64_t emit(const Tensor& t, tp_handle* out) {
   return id;
 }
 
+// rows[i] of a [R][row] tensor -> out[i]: one CTA per output row, 16-byte
+// accesses when the row length allows it
+__global__ void k_gather_rows(const float* __restrict__ src, const int64_t* __restrict__ rows, int64_t n,
+                              int64_t row, float* __restrict__ out) {
+  ::tp::pdl_enter();
+  for (int64_t i = blockIdx.x; i < n; i += gridDim.x) {
+    const float* s = src + rows[i] * row;
+    float* d = out + i * row;
+    if ((row & 3) == 0) {
+      const float4* s4 = reinterpret_cast<const float4*>(s);
+      float4* d4 = reinterpret_cast<float4*>(d);
+      for (int64_t k = threadIdx.x; k < (row >> 2); k += blockDim.x) d4[k] = s4[k];
+    } else {
+      for (int64_t k = threadIdx.x; k < row; k += blockDim.x) d[k] = s[k];
+    }
+  }
+}
+
 // int64 element <-> the f32 value the runtime stores for an integer dtype
 // (truncation toward zero on the way out, as toList decodes, device.ts:38-54)
 __global__ void k_f32_to_i64(const float* in, long long* out, int64_t n) {
@@ -355,6 +374,33 @@ TP_API int tp_to_host(int64_t id, float* dst, int64_t numel) {
   });
 }
 
+// ---- batches of a device-resident dataset ----------------------------------------------
+
+TP_API int tp_gather_rows(int64_t src, const int64_t* rows, int64_t n, tp_handle* out) {
+  return guard([&] {
+    Tensor& S = get(src);
+    TP_REQUIRE(S.ndim >= 1, "gatherRows: the source needs a first dimension");
+    TP_REQUIRE(S.phys == PHYS_F32, "gatherRows: index tensors are not supported");
+    TP_REQUIRE(n >= 0, "gatherRows: negative row count");
+    for (int64_t i = 0; i < n; ++i)
+      TP_REQUIRE(rows[i] >= 0 && rows[i] < S.shape[0], "index %lld is out of bounds for dimension 0 with size %lld",
+                 (long long)rows[i], (long long)S.shape[0]);
+    std::vector<int64_t> shp(S.shape, S.shape + S.ndim);
+    shp[0] = n;
+    Tensor O = make_like_shape(shp, S.dtype);
+    const int64_t row = S.shape[0] > 0 ? S.numel / S.shape[0] : 0;
+    if (n > 0 && row > 0) {
+      int64_t* drows = (int64_t*)dalloc((size_t)n * sizeof(int64_t));
+      TP_CUDA(cudaMemcpyAsync(drows, rows, (size_t)n * sizeof(int64_t), cudaMemcpyHostToDevice, stream()));
+      const int64_t cap = (int64_t)sm_count() * 16;
+      TP_LAUNCH(k_gather_rows, (unsigned)(n < cap ? n : cap), 256, 0, S.f(), drows, n, row, O.f());
+      dfree(drows);
+      TP_CUDA(cudaStreamSynchronize(stream()));  // the caller's row list may be released on return
+    }
+    emit(O, out);
+  });
+}
+
 // ---- bulk byte I/O (checkpoints) and pinned uploads -----------------------------------
 
 TP_API int tp_to_bytes(int64_t id, void* dst, int64_t nbytes, int format) {
@@ -444,8 +490,8 @@ static cudaEvent_t g_ticket_ev[TICKETS];
 static bool g_ticket_made[TICKETS];
 static int64_t g_next_ticket = 1;
 
-TP_API int tp_tensor_from_host_async(const void* host, const int64_t* shape, int ndim, int dtype, tp_handle* out,
-                                     int64_t* ticket) {
+TP_API int tp_tensor_from_host_async(const void* host, const int64_t* shape, int ndim, int dtype, int defer,
+                                     tp_handle* out, int64_t* ticket) {
   return guard([&] {
     ensure_init();
     if (!g_copy) TP_CUDA(cudaStreamCreateWithFlags(&g_copy, cudaStreamNonBlocking));
@@ -478,10 +524,21 @@ TP_API int tp_tensor_from_host_async(const void* host, const int64_t* shape, int
       g_ticket_made[slot] = true;
     }
     TP_CUDA(cudaEventRecord(g_ticket_ev[slot], g_copy));
-    TP_CUDA(cudaStreamWaitEvent(g_stream, g_ticket_ev[slot], 0));
-    if (g_aux) TP_CUDA(cudaStreamWaitEvent(g_aux, g_ticket_ev[slot], 0));
+    if (!defer) {
+      TP_CUDA(cudaStreamWaitEvent(g_stream, g_ticket_ev[slot], 0));
+      if (g_aux) TP_CUDA(cudaStreamWaitEvent(g_aux, g_ticket_ev[slot], 0));
+    }
     emit(t, out);
     *ticket = tk;
+  });
+}
+
+TP_API int tp_ticket_use(int64_t ticket) {
+  return guard([&] {
+    TP_REQUIRE(ticket > 0 && ticket < g_next_ticket, "unknown upload ticket %lld", (long long)ticket);
+    cudaEvent_t ev = g_ticket_ev[ticket % TICKETS];  // a later copy's event in a reused slot: a later wait
+    TP_CUDA(cudaStreamWaitEvent(g_stream, ev, 0));
+    if (g_aux) TP_CUDA(cudaStreamWaitEvent(g_aux, ev, 0));
   });
 }
 

@@ -83,8 +83,10 @@ SIGNATURES: dict[str, list] = {
     "tp_from_bytes": [P, I64, INT, I64P, INT, INT, HP],
     "tp_host_alloc": [I64, PP],
     "tp_host_free": [P],
-    "tp_tensor_from_host_async": [P, I64P, INT, INT, HP, I64P],
+    "tp_tensor_from_host_async": [P, I64P, INT, INT, INT, HP, I64P],
+    "tp_ticket_use": [I64],
     "tp_ticket_wait": [I64],
+    "tp_gather_rows": [I64, I64P, I64, HP],
     "tp_conv2d_dev_bias": [I64, I64, I64, I64P, INT, I64P, INT, I64P, INT, INT, HP],
     "tp_rmsprop_step": [I64, I64, I64, I64, F32, F32, F32, F32, F32],
     "tp_adagrad_step": [I64, I64, I64, F32, F32, F32],

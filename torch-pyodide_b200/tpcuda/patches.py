@@ -43,6 +43,11 @@ issues a chain of tiny kernels where one fused entry exists:
   rows; rebound onto ``maxDim`` (one reduction, first index of the maximum, as
   argmax.wgsl).  ``max_dim_from_tensor`` keeps the sort path when a gradient
   has to flow through it.
+* ``DataLoader.__iter__`` over a ``TensorDataset`` with the default collate
+  (utils/data/__init__.py:205-210) selects each sample with its own runtime
+  call and stacks them; rebound onto one ``gatherRows`` per dataset tensor
+  and batch, same batches in the same sampler order.  Host-resident (numpy)
+  datasets go through ``tpcuda.data.PinnedLoader``.
 * tensor lifetime (D7): ``Tensor._set`` rebinds an id without freeing the old
   buffer and ``Tensor`` has no finaliser (_tensor.py:27,1308-1313), so every
   intermediate stays allocated until an explicit ``destroy``.  ``apply()``
@@ -530,6 +535,25 @@ def _rebind(orig, new):
                     _set(mod, attr, new)
 
 
+# ---- DataLoader batches of a device-resident TensorDataset ---------------------------------------
+
+def _make_loader_iter(original):
+    def __iter__(self):
+        from torch.utils.data import TensorDataset, default_collate
+        ds = self.dataset
+        if not (isinstance(ds, TensorDataset) and self.collate_fn is default_collate
+                and not any(t._requires_grad for t in ds.tensors)):
+            yield from original(self)
+            return
+        if self.worker_init_fn is not None:
+            self.worker_init_fn(0)
+        rt = _rt()
+        for batch_indices in self.batch_sampler:
+            rows = [int(i) for i in batch_indices]
+            yield tuple(_wrap(_run(rt.gatherRows(t._id, rows))) for t in ds.tensors)
+    return __iter__
+
+
 # ---- Python scalars as one-element tensors -------------------------------------------------------
 
 def _scalar_to_tensor(value, dtype="float32"):
@@ -583,6 +607,8 @@ def apply(lifetime: bool = True) -> None:
     _set(_save, "_tensor_to_raw_bytes", _tensor_to_raw_bytes)
     _set(_save, "_rebuild_tensor_v2", _rebuild_tensor_v2)
     _rebind(tfo.tensor_from_data, _make_tensor_from_data(tfo.tensor_from_data))
+    import torch.utils.data as tud
+    _set(tud.DataLoader, "__iter__", _make_loader_iter(tud.DataLoader.__dict__["__iter__"]))
     import torch._tensor_runtime_bridge as bridge
     _rebind(bridge.argmax_from_tensor, _make_argmax(bridge.argmax_from_tensor))
     _rebind(tensor_ops.max_dim_from_tensor, _make_max_dim(tensor_ops.max_dim_from_tensor))

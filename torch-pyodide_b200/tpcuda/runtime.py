@@ -557,12 +557,22 @@ class CudaRuntime:
     def hostFree(self, ptr: int) -> None:
         check(self.lib.tp_host_free(ctypes.c_void_p(ptr)))
 
-    def tensorFromHostAsync(self, host_ptr: int, shape, dtype="float32"):
-        """Upload from pinned host memory on the copy stream; returns (handle, ticket)."""
+    def tensorFromHostAsync(self, host_ptr: int, shape, dtype="float32", defer: bool = False):
+        """Upload from pinned host memory on the copy stream; returns (handle,
+        ticket).  defer: later kernels wait only after ticketUse(ticket)."""
         h, t = Handle(), ctypes.c_int64(0)
         check(self.lib.tp_tensor_from_host_async(ctypes.c_void_p(host_ptr), i64arr(shape), len(shape),
-                                                 _dtype_code(dtype), ctypes.byref(h), ctypes.byref(t)))
+                                                 _dtype_code(dtype), 1 if defer else 0, ctypes.byref(h),
+                                                 ctypes.byref(t)))
         return h.to_dict(), int(t.value)
+
+    def ticketUse(self, ticket: int) -> None:
+        check(self.lib.tp_ticket_use(int(ticket)))
+
+    def gatherRows(self, tid, rows):
+        """src[rows] along dim 0 as a new tensor (a DataLoader batch)."""
+        rows = [int(r) for r in rows]
+        return self._call(self.lib.tp_gather_rows, int(tid), i64arr(rows), len(rows))
 
     def ticketWait(self, ticket: int) -> None:
         check(self.lib.tp_ticket_wait(int(ticket)))
