@@ -461,6 +461,109 @@ def cpu_vgg(batch: int, steps: int, warmup: int = 1) -> dict:
     return {"imgs_per_s": batch / t, "sec": t, "batch": batch, "times": times}
 
 
+def cpu_ops(reps: int = 3) -> dict:
+    """The oracle (C/OpenMP restatement of the reference shaders, all host
+    threads) on the reductions / norms and dense configs: per op the same rate
+    the GPU line reports (GB/s of algorithmic traffic, or TFLOP/s), measured on
+    the full input where the oracle takes seconds, else on a stated sample of
+    the output (rows of a matmul, whole images of a convolution, output
+    channels of a weight gradient) -- each sampled output value is computed as
+    in the full op, so the rate carries over.  Keyed by the GPU line's op names."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    from oracle_runtime import OracleRuntime
+    o = OracleRuntime()
+    rng = np.random.default_rng(0)
+    res = {}
+
+    def T(a):
+        a = np.ascontiguousarray(a, np.float32)
+        return o.tensorFromData(a.ravel(), list(a.shape), "float32")["id"]
+
+    def best(fn):
+        fn()
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            out = fn()
+            ts.append(time.perf_counter() - t0)
+            for h in (out if isinstance(out, list) else [out]):
+                if isinstance(h, dict):
+                    o.destroy(h["id"])
+        return statistics.median(ts)
+
+    def put(name, sec, work, kind, sample="full size"):
+        rate = work / sec / (1e9 if kind == "hbm" else 1e12)
+        res[name] = {"value": round(rate, 4), "unit": "GB/s" if kind == "hbm" else "TFLOP/s",
+                     "ms": round(sec * 1e3, 3), "sample": sample}
+
+    x = T(rng.standard_normal((16384, 4096), dtype=np.float32))
+    g, b = T(np.ones(4096)), T(np.zeros(4096))
+    nb = 16384 * 4096 * 4
+    put("layer_norm fwd", best(lambda: o.layerNormForward(x, [4096], g, b, 1e-5)), 2 * nb, "hbm")
+    y, m, r = o.layerNormForward(x, [4096], g, b, 1e-5)
+    put("layer_norm bwd", best(lambda: o.layerNormBackward(x, x, [4096], g, m["id"], r["id"])), 3 * nb, "hbm")
+    for h in (x, g, b, y["id"], m["id"], r["id"]):
+        o.destroy(h)
+    x = T(rng.standard_normal((32768, 8192), dtype=np.float32))
+    nb = 32768 * 8192 * 4
+    put("softmax", best(lambda: o.softmax(x, -1)), 2 * nb, "hbm")
+    put("log_softmax", best(lambda: o.logSoftmax(x, -1)), 2 * nb, "hbm")
+    # the backward as the reference computes it is O(C^2) per row: 64 of the rows
+    xs = T(rng.standard_normal((64, 8192), dtype=np.float32))
+    s = o.softmax(xs, -1)["id"]
+    nbs = 64 * 8192 * 4
+    put("softmax bwd", best(lambda: o.softmaxBackward(xs, s, 64, 8192)), 3 * nbs, "hbm", "64 of 32768 rows")
+    put("log_softmax bwd", best(lambda: o.logSoftmaxBackward(xs, s, 64, 8192)), 3 * nbs, "hbm", "64 of 32768 rows")
+    o.destroy(s)
+    o.destroy(xs)
+    o.destroy(x)
+    x = T(rng.standard_normal((8192, 8192), dtype=np.float32))
+    nb = 8192 * 8192 * 4
+    put("sum all", best(lambda: o.sum(x)), nb, "hbm")
+    for d in (0, -1):
+        put(f"sum dim {d}", best(lambda: o.sumDim(x, d, False)), nb, "hbm")
+        put(f"mean dim {d}", best(lambda: o.meanDim(x, d, False)), nb, "hbm")
+        put(f"max dim {d}", best(lambda: o.maxDim(x, d, False)), nb, "hbm")
+    o.destroy(x)
+    shp = [256, 128, 56, 56]
+    x = T(rng.standard_normal(shp, dtype=np.float32))
+    g, b, rm, rv = T(np.ones(128)), T(np.zeros(128)), T(np.zeros(128)), T(np.ones(128))
+    nb = 256 * 128 * 56 * 56 * 4
+    put("batch_norm train fwd", best(lambda: o.batchNormTrain(x, g, b, rm, rv, 1e-5, 0.1)), 2 * nb, "hbm")
+    _, mean, inv = o.batchNormTrain(x, g, b, rm, rv, 1e-5, 0.1)
+    put("batch_norm bwd", best(lambda: o.batchNormBackward(x, x, g, mean["id"], inv["id"])), 3 * nb, "hbm")
+    for h in (x, g, b, rm, rv):
+        o.destroy(h)
+    for n, rows in ((512, 512), (2048, 128), (8192, 16)):
+        a, bb = rng.uniform(-1, 1, (rows, n)).astype(np.float32), rng.uniform(-1, 1, (n, n)).astype(np.float32)
+        ta, tb = T(a), T(bb)
+        put("matmul", best(lambda: o.matmul(ta, tb)), 2.0 * rows * n * n, "tensor",
+            "full size" if rows == n else f"{rows} of {n} output rows")
+        res[f"matmul {n}"] = res.pop("matmul")
+        o.destroy(ta)
+        o.destroy(tb)
+    xl = T(rng.uniform(-1, 1, (16, 4096)).astype(np.float32))
+    wt = o.transpose2d(T(rng.uniform(-1, 1, (11008, 4096)).astype(np.float32)))["id"]
+    bl = T(rng.uniform(-1, 1, 11008).astype(np.float32))
+    put("linear +bias", best(lambda: o.add(o.matmul(xl, wt)["id"], bl)), 2.0 * 16 * 4096 * 11008, "tensor",
+        "16 of 16384 output rows")
+    for xs, ws, st, pd in (([2, 64, 56, 56], [64, 64, 3, 3], 1, 1), ([2, 3, 224, 224], [64, 3, 7, 7], 2, 3)):
+        tag = f"{ws[2]}x{ws[3]} s{st}"
+        xc, wc = T(rng.standard_normal(xs, dtype=np.float32)), T(rng.standard_normal(ws, dtype=np.float32))
+        oh = (xs[2] + 2 * pd - ws[2]) // st + 1
+        ys = [2, ws[0], oh, oh]
+        gy = T(rng.standard_normal(ys, dtype=np.float32))
+        fl = 2.0 * 2 * ws[0] * oh * oh * xs[1] * ws[2] * ws[3]
+        put(f"conv2d fwd {tag}", best(lambda: o.conv2d(xc, wc, None, [st], [pd], [1], 1)), fl, "tensor",
+            "2 of 128 images")
+        put(f"conv2d dgrad {tag}", best(lambda: o.conv2dInputBackward(gy, wc, xs, ys, [st], [pd])), fl, "tensor",
+            "2 of 128 images")
+        put(f"conv2d wgrad {tag}", best(lambda: o.conv2dWeightBackward(gy, xc, ws, ys, xs, [st], [pd])), fl, "tensor",
+            "2 of 128 images")
+    return res
+
+
 def run_ops(args):
     """Per-op throughput of the reductions / norms, the dense contractions and
     the multi-tensor SGD / Adam steps through the reference-facing runtime surface
@@ -628,11 +731,20 @@ def run_ops(args):
     add("adam L2 wd (multi-tensor)", [NTENSORS, elems], ms, 28 * elems, "hbm")
     for h in P + G + S0 + S1:
         rt.destroy(h["id"])
+    cpu_cores = None
+    if not args.no_cpu_baseline:
+        os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
+        cpu_cores = int(os.environ["OMP_NUM_THREADS"])
+        cpu = cpu_ops()
+        for r in results:
+            key = f"matmul {r['shape'][0]}" if r["op"] == "matmul" else r["op"]
+            if key in cpu:
+                r["cpu_baseline"] = dict(cpu[key], kind="port", cores=cpu_cores)
     print(json.dumps({"metric": "per-op throughput vs roofline (reductions/norms/optimizers: GB/s of HBM; "
                                 "contractions: TFLOP/s of 3xTF32)", "n_gpus": 1, "reps": reps, "hbm_peak_gbs": hbm,
                       "tf32x3_peak_tflops": round(peak3, 1), "peak_source": f"{peak_kind} bf16 {bf16}",
                       "path": "CudaRuntime handle API (the reference-facing surface), NCHW",
-                      "results": results}), flush=True)
+                      "cpu_baseline_cores": cpu_cores, "results": results}), flush=True)
 
 
 TINY_TRACE = os.path.join(ROOT, "tests", "golden", "traces", "tiny_cnn.json")

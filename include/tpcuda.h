@@ -285,10 +285,10 @@ TP_API int tp_set_pdl(int on);
  * TP_ERR_TIMEOUT when it is set, so an expired wait reaches every caller that
  * synchronises. */
 TP_API int tp_gemm_status(int* out, int reset);
-/* Accuracy switch of the tensor-core GEMMs: no split-K split accumulates more
- * than `kblocks` k-blocks of 32 in tensor memory (0 = no cap); longer
- * reductions are cut into more splits (at most 2048) whose partials are added
- * in fp32 on CUDA cores. */
+/* Accuracy switch of the tensor-core GEMMs: for K above 4 x kblocks x 32, no
+ * split-K split accumulates more than `kblocks` k-blocks of 32 in tensor memory
+ * (default 64; 0 = no cap); such reductions are cut into more splits (at most
+ * 2048) whose partials are added in fp32 on CUDA cores. */
 TP_API int tp_set_gemm_kmax(int kblocks);
 /* New, for testing the path above: one CTA waits on an mbarrier nothing
  * arrives on, with the tensor-core kernels' own bounded-wait function and a

@@ -5,8 +5,9 @@ At these sizes the tensor-map extents, split-K counts, grid limits and 32-bit
 index products differ from the small parity cases, so every op here runs on
 the device at its configured size and is checked against the CPU oracle:
 
-* reductions, norms and softmax: the oracle runs at the full size too (its C
-  loops finish in about a second each);
+* reductions, norms and the softmax forward: the oracle runs at the full size
+  too (its C loops finish in about a second each); the softmax backwards, which
+  the reference computes in O(C^2) per row, on a seeded sample of 256 rows;
 * the contractions: the oracle computes a seeded sample of the output (rows x
   columns of a matmul or linear layer, whole images of a convolution's forward
   and data gradient, a few output channels of a weight gradient); each
@@ -106,11 +107,17 @@ def test_softmax_logsoftmax_32768x8192_fwd_bwd(cuda_rt, oracle_rt):
         s = getattr(rt, fwd)(x["id"], -1)
         os_ = getattr(orc, fwd)(ox["id"], -1)
         assert_scaled(rt.toNumpy(s["id"]), orc.array(os_["id"]), what=fwd)
-        # the backward from the device's own forward output, on both sides
-        os_dev = orc_t(orc, host(rt, s))
+        # the backward from the device's own forward output, on both sides; the
+        # reference shader recomputes each row's dot product per element (O(C^2)
+        # per row), so the oracle does a seeded sample of rows (rows are independent)
+        rows = np.sort(np.random.default_rng(5).choice(R, 254, replace=False))
+        rows = np.unique(np.concatenate([[0, R - 1], rows]))
+        S, GY = host(rt, s), host(rt, gy)
+        os_dev, ogs = orc_t(orc, S[rows]), orc_t(orc, GY[rows])
         d = getattr(rt, bwd)(gy["id"], s["id"], R, C)
-        od = getattr(orc, bwd)(ogy["id"], os_dev["id"], R, C)
-        assert_scaled(rt.toNumpy(d["id"]), orc.array(od["id"]), what=bwd)
+        od = getattr(orc, bwd)(ogs["id"], os_dev["id"], len(rows), C)
+        assert_scaled(host(rt, d)[rows], orc.array(od["id"]).reshape(len(rows), C), what=bwd)
+        orc.destroy(ogs["id"])
         free(rt, s, d)
         for h in (os_, os_dev, od):
             orc.destroy(h["id"])

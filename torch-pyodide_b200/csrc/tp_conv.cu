@@ -24,10 +24,12 @@ static int g_gemm_path = 0;
 int gemm_path() { return g_gemm_path; }
 
 // Most k-blocks (32 k each) one split of a tensor-core GEMM accumulates in
-// TMEM (0: no cap).  The accumulator's additions are not round-to-nearest over
-// very long sums, so long reductions (a weight gradient over 10^6 pixels) are
-// cut into splits whose partials are then added on CUDA cores.
-static int g_gemm_kmax = 0;
+// TMEM once K exceeds 4x that (0: no cap).  Over thousands of MMAs into one
+// fp32 accumulator the sum drifts (measured on the 7x7 stride-2 weight
+// gradient over 1.6 M pixels: 3.0e-4 of the output scale uncapped, 1.1e-4 at
+// 512, 3.1e-5 at 128, 1.5e-5 at 64 k-blocks per split), so long reductions are
+// cut into splits whose partials are added on CUDA cores.
+static int g_gemm_kmax = 64;
 int gemm_kmax() { return g_gemm_kmax; }
 
 // Each translation unit that holds tensor-core kernels has its own copy of

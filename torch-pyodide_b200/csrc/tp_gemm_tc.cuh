@@ -451,8 +451,12 @@ int gemm_kmax();
 inline int gemm_splits(int64_t tiles, int64_t K, int sms, int64_t out_elems) {
   if (K <= 0 || tiles <= 0) return 1;
   const int64_t nk = (K + 31) / 32;
+  // Accuracy floor for long reductions (weight gradients over many pixels): the
+  // tensor core's fp32 accumulation drifts over thousands of MMAs into one
+  // accumulator, so no split of such a GEMM accumulates more than kmax k-blocks.
+  // Forward / data-gradient K (<= 4 kmax k-blocks) keeps the cost-model split.
   const int kmax = gemm_kmax();
-  if (kmax > 0 && nk > kmax) {  // accuracy floor first: no split accumulates more than kmax k-blocks
+  if (kmax > 0 && nk > 4 * (int64_t)kmax) {
     const int64_t need = (nk + kmax - 1) / kmax;
     return (int)(need < 2048 ? need : 2048);
   }
