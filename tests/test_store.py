@@ -63,3 +63,30 @@ def test_default_dir_is_per_launch(monkeypatch):
     assert "29511" in d and str(os.getppid()) in d
     monkeypatch.setenv("TPCUDA_STORE_DIR", "/tmp/x-store")
     assert default_dir() == "/tmp/x-store"
+
+
+def _leaver(rank, world, path, q):
+    st = FileStore(rank, world, path, timeout_s=30)
+    st.barrier()
+    if rank == 1:
+        st.leave()
+        q.put((rank, []))
+        return
+    import time as _t
+    t0 = _t.monotonic()
+    while not st.departed() and _t.monotonic() - t0 < 20:
+        _t.sleep(0.01)
+    q.put((rank, st.departed()))
+
+
+def test_departed_rank_is_seen_before_the_next_step(tmp_path):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    path = str(tmp_path / "s")
+    ps = [ctx.Process(target=_leaver, args=(r, 2, path, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = dict(q.get(timeout=60) for _ in range(2))
+    for p in ps:
+        p.join(timeout=30)
+    assert res[0] == [1] and res[1] == []

@@ -38,6 +38,18 @@ class NcclComm:
     def close(self) -> None:
         check(self.lib.tp_comm_destroy())
 
+    def check_peers(self, store: FileStore) -> None:
+        """Between steps: raise if a rank has left (FileStore.leave), before any
+        collective is issued that would wait for it."""
+        gone = store.departed()
+        if gone:
+            raise RuntimeError(f"rank(s) {gone} left the job; no further collective is issued")
+
+    def world_now(self) -> int:
+        r, w = ctypes.c_int(0), ctypes.c_int(0)
+        check(self.lib.tp_comm_info(ctypes.byref(r), ctypes.byref(w)))
+        return int(w.value)
+
 
 def env_ranks() -> tuple[int, int, int]:
     """(rank, world, local rank) from the launcher's environment (torchrun's

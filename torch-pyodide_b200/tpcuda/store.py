@@ -101,6 +101,16 @@ class FileStore:
             return value
         return self.get(key)
 
+    # ---- departures ---------------------------------------------------------
+    def leave(self) -> None:
+        """Mark this rank as gone, between steps, before it exits early; the
+        others see it with ``departed()`` before their next collective instead
+        of launching one that would wait for this rank."""
+        self.set(f"left.{self.rank}", b"")
+
+    def departed(self) -> list[int]:
+        return [k for k in range(self.world) if k != self.rank and os.path.exists(self._file(f"left.{k}"))]
+
     def close(self) -> None:
         """Every rank leaves a last mark and reads nothing after it; rank 0
         waits for all marks, then removes the directory."""
