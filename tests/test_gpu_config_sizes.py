@@ -18,7 +18,8 @@ the device at its configured size and is checked against the CPU oracle:
   steps one tensor of each of the four shapes, which must match bit for bit.
 
 Tolerances: 1e-4 relative to the output's scale (max |oracle|) for
-contractions, norms and reductions; bit-exact for max / argmax indices and
+contractions, norms and reductions (the weight gradients, whose sums run over
+0.4-1.6 M products, also against the exact float64 sum, see below); bit-exact for max / argmax indices and
 the optimizer steps.  Inputs come from the device RNG (seeded) and are read
 back for the oracle.
 """
@@ -245,7 +246,24 @@ def test_conv2d_fwd_dgrad_wgrad_sampled(cuda_rt, oracle_rt, xs, ws, st, pd):
     chans = [0, Cout // 2 + 1, Cout - 1]
     odw = orc.conv2dWeightBackward(orc_t(orc, GY[:, chans])["id"], orc_t(orc, X)["id"], [len(chans), Cin, KH, KW],
                                    [N, len(chans), OH, OW], xs, [st], [pd])
-    assert_scaled(DW[chans], orc.array(odw["id"]).reshape(len(chans), Cin, KH, KW), what="conv wgrad")
+    ODW = orc.array(odw["id"]).reshape(len(chans), Cin, KH, KW).astype(np.float64)
+    # Each weight-gradient value sums N*OH*OW = 0.4 M / 1.6 M products.  The
+    # reference's sequential fp32 sum itself drifts from the exact value by
+    # ~1e-5..1e-4 of the scale at this length, so the device result is held to
+    # 1e-4 of the exact (float64) sum, and to the oracle within 1e-4 plus the
+    # oracle's own distance from the exact sum.
+    G = GY[:, chans].astype(np.float64)
+    Xp = np.pad(X.astype(np.float64), ((0, 0), (0, 0), (pd, pd), (pd, pd)))
+    exact = np.zeros((len(chans), Cin, KH, KW))
+    for kh in range(KH):
+        for kw in range(KW):
+            xsl = Xp[:, :, kh:kh + st * (OH - 1) + 1:st, kw:kw + st * (OW - 1) + 1:st]
+            exact[:, :, kh, kw] = np.einsum("nohw,nchw->oc", G, xsl, optimize=True)
+    scale = float(np.max(np.abs(exact)))
+    assert_scaled(DW[chans], exact, what="conv wgrad vs exact")
+    orc_drift = float(np.max(np.abs(ODW - exact)))
+    err = float(np.max(np.abs(DW[chans].astype(np.float64) - ODW)))
+    assert err <= REL * scale + orc_drift, ("conv wgrad vs oracle", err, scale, orc_drift)
     free(rt, x, w, gy, y, dx, dw)
 
 

@@ -150,8 +150,10 @@ def test_conv_nhwc_matches_nchw(cuda_rt, engine, cin, cout, hw, batch, nhwc_path
     ref_dw = read(rt, dw0, (cout, cin, 3, 3))
     got_dw = read(rt, dw1, (cout, cin, 3, 3))
     free(rt, px, pxn, pw, pb, pdy, pdyn, y0, y1, dx0, dx1, dw0, dw1)
+    # two fp32 summation orders of the same products (different tile shapes and
+    # split-K plans): the parity bar, 1e-4 of the output scale
     for got, ref in ((got_y, ref_y), (got_dx, ref_dx), (got_dw, ref_dw)):
-        close64(got, ref.astype(np.float64), rel=1e-5)
+        close64(got, ref.astype(np.float64), rel=1e-4)
 
 
 @pytest.mark.parametrize("cin,cout,hw,batch", [(64, 128, 16, 4), (256, 256, 8, 8), (3, 64, 32, 2), (4, 64, 32, 2)])
