@@ -186,50 +186,3 @@ def test_layernorm_forward_backward(cuda_rt, oracle_rt, rows, D):
     for c_, o_ in zip(cd, od):
         close_scaled(cuda_rt, oracle_rt, c_, o_)
 
-
-BN_GROUP_SCRIPT = r"""
-import sys, json
-import numpy as np
-sys.path[:0] = [{pkg!r}, {orc!r}]
-from tpcuda import CudaRuntime
-from oracle_runtime import OracleRuntime
-cu, orc = CudaRuntime(0), OracleRuntime()
-rng = np.random.default_rng(8)
-shape = {shape!r}
-C = shape[1]
-def both(a):
-    a = np.ascontiguousarray(a, np.float32)
-    return cu.tensorFromData(a.ravel(), list(a.shape), "float32"), orc.tensorFromData(a.ravel(), list(a.shape), "float32")
-x = both(rng.standard_normal(shape) * 2 + 0.5)
-w, b = both(1 + 0.1 * rng.standard_normal(C)), both(0.1 * rng.standard_normal(C))
-rm, rv = both(np.zeros(C)), both(np.ones(C))
-dy = both(rng.standard_normal(shape))
-cy, cm, cs = cu.batchNormTrain(x[0]["id"], w[0]["id"], b[0]["id"], rm[0]["id"], rv[0]["id"], 1e-5, 0.1)
-oy, om, os_ = orc.batchNormTrain(x[1]["id"], w[1]["id"], b[1]["id"], rm[1]["id"], rv[1]["id"], 1e-5, 0.1)
-cd = cu.batchNormBackward(dy[0]["id"], x[0]["id"], w[0]["id"], cm["id"], cs["id"])
-od = orc.batchNormBackward(dy[1]["id"], x[1]["id"], w[1]["id"], om["id"], os_["id"])
-out = {{}}
-for nm, c, o in [("y", cy, oy), ("mean", cm, om), ("invstd", cs, os_), ("rm", rm[0], rm[1]), ("rv", rv[0], rv[1]),
-                 ("dx", cd[0], od[0]), ("dw", cd[1], od[1]), ("db", cd[2], od[2])]:
-    a, r = cu.toNumpy(c["id"]).astype(np.float64), orc.array(o["id"]).astype(np.float64)
-    out[nm] = float(np.max(np.abs(a - r)) / max(1e-30, np.max(np.abs(r))))
-print(json.dumps(out))
-"""
-
-
-@pytest.mark.parametrize("shape", [[16, 37, 28, 28], [8, 5, 12, 12]])
-def test_batchnorm_channel_groups_match_oracle(shape):
-    """NCHW BatchNorm in L2-sized channel groups (a 1 MB group budget here
-    forces several groups, the last one partial) against the oracle."""
-    import json
-    import os
-    import subprocess
-    import sys
-    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    code = BN_GROUP_SCRIPT.format(pkg=os.path.join(root, "torch-pyodide_b200"), orc=os.path.join(root, "oracle"),
-                                  shape=shape)
-    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300,
-                       env=dict(os.environ, TP_BN_GROUP_MB="1"))
-    assert r.returncode == 0, r.stderr[-3000:]
-    errs = json.loads(r.stdout.strip().splitlines()[-1])
-    assert all(v <= 1e-4 for v in errs.values()), errs

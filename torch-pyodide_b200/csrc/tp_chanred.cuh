@@ -109,16 +109,12 @@ struct ChanBnBwdF {
 };
 
 // fs4 / fs: division by S/4 and by S (flat index -> image, position)
-// c0: first channel of the group this launch reduces (grid.x channels from
-// c0; partials indexed by the channel's place in the group).
 template <class F>
 __global__ void __launch_bounds__(256) k_chan_reduce(F f, int64_t N, int64_t C, int64_t S, int splits,
-                                                     double* __restrict__ part, FastDiv fs4, FastDiv fs,
-                                                     int64_t c0 = 0) {
+                                                     double* __restrict__ part, FastDiv fs4, FastDiv fs) {
   ::tp::pdl_enter();
   __shared__ double sh_a[32], sh_b[32];
-  const int64_t c = c0 + blockIdx.x;
-  const int64_t cg = blockIdx.x;
+  const int64_t c = blockIdx.x;
   const int split = blockIdx.y;
   const int64_t per = (N + splits - 1) / splits;
   const int64_t n0 = split * per, n1 = n0 + per < N ? n0 + per : N;
@@ -170,8 +166,8 @@ __global__ void __launch_bounds__(256) k_chan_reduce(F f, int64_t N, int64_t C, 
       ta += sh_a[k];
       tb += sh_b[k];
     }
-    part[(cg * splits + split) * 2] = ta;
-    part[(cg * splits + split) * 2 + 1] = tb;
+    part[(c * splits + split) * 2] = ta;
+    part[(c * splits + split) * 2 + 1] = tb;
   }
 }
 

@@ -62,7 +62,7 @@ void launch_channel_sum(const float* x, int64_t N, int64_t C, int64_t P, float* 
   double* part = (double*)scratch((size_t)C * splits * 2 * sizeof(double));
   auto kcs = k_chan_reduce<ChanSumF>;
   TP_LAUNCH(kcs, dim3((unsigned)C, (unsigned)splits), 256, 0, ChanSumF{x}, N, C, P, splits, part, chan_div4(P),
-            chan_div1(P), (int64_t)0);
+            chan_div1(P));
   TP_LAUNCH(k_channel_sum_finish, (unsigned)((C + 127) / 128), 128, 0, part, C, splits, out);
 }
 

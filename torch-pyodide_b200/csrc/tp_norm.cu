@@ -18,7 +18,6 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
-#include <cstdlib>
 
 #include "tp_core.h"
 #include "tp_launch.h"
@@ -43,18 +42,16 @@ __global__ void k_bn_eval(const float* __restrict__ x, const float* __restrict__
 // ---- BatchNorm train: statistics (k_chan_reduce in tp_chanred.cuh) -------------------
 // Per channel: mean, biased var -> inv_std; running stats with the unbiased
 // variance.  Writes save_mean / save_invstd (f32) for the normalise pass.
-// C: channels of this group, starting at c0 (part is indexed within the group).
 __global__ void k_bn_finish(const double* __restrict__ part, int64_t C, int splits, double M, float eps,
                             float momentum, float* __restrict__ save_mean, float* __restrict__ save_invstd,
-                            float* __restrict__ rm, float* __restrict__ rv, int64_t c0) {
+                            float* __restrict__ rm, float* __restrict__ rv) {
   ::tp::pdl_enter();
-  const int64_t cg = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (cg >= C) return;
-  const int64_t c = c0 + cg;
+  int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (c >= C) return;
   double s = 0.0, q = 0.0;
   for (int k = 0; k < splits; ++k) {
-    s += part[(cg * splits + k) * 2];
-    q += part[(cg * splits + k) * 2 + 1];
+    s += part[(c * splits + k) * 2];
+    q += part[(c * splits + k) * 2 + 1];
   }
   double mean = s / M;
   double var = q / M - mean * mean;
@@ -77,7 +74,10 @@ __global__ void k_bn_apply(const float* __restrict__ x, const float* __restrict_
     int64_t t4 = total >> 2;
     const float4* x4 = reinterpret_cast<const float4*>(x);
     float4* y4 = reinterpret_cast<float4*>(y);
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < t4; i += stride) {
+    // from the end of the tensor backwards: the statistics pass read the last
+    // images last, so the first of these reads still find them in L2
+    for (int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < t4; j += stride) {
+      const int64_t i = t4 - 1 - j;
       const int64_t c = fc.mod(fs4.div((uint32_t)i));
       float mu = mean[c], is = invstd[c], wt = w ? w[c] : 1.0f, bs = b ? b[c] : 0.0f;
       float sc = is * wt;
@@ -106,16 +106,14 @@ __global__ void k_bn_apply(const float* __restrict__ x, const float* __restrict_
 // coef[c] = {w*invstd, sum_dy/M, sum_dyxh/M}; dw, db written here.
 __global__ void k_bn_bwd_finish(const double* __restrict__ part, int64_t C, int splits, double M,
                                 const float* __restrict__ w, const float* __restrict__ invstd,
-                                float* __restrict__ coef, float* __restrict__ dw, float* __restrict__ db,
-                                int64_t c0) {
+                                float* __restrict__ coef, float* __restrict__ dw, float* __restrict__ db) {
   ::tp::pdl_enter();
-  const int64_t cg = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (cg >= C) return;
-  const int64_t c = c0 + cg;
+  int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (c >= C) return;
   double a = 0.0, b = 0.0;
   for (int k = 0; k < splits; ++k) {
-    a += part[(cg * splits + k) * 2];
-    b += part[(cg * splits + k) * 2 + 1];
+    a += part[(c * splits + k) * 2];
+    b += part[(c * splits + k) * 2 + 1];
   }
   coef[c * 3] = (w ? w[c] : 1.0f) * invstd[c];
   coef[c * 3 + 1] = (float)(a / M);
@@ -143,7 +141,8 @@ __global__ void k_bn_bwd_apply(const float* __restrict__ dy, const float* __rest
   if ((S & 3) == 0 && (total >> 2) < ((int64_t)1 << 31)) {
     const int64_t t4 = total >> 2;
     const bool hr = relu_src != nullptr;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < t4; i += stride) {
+    for (int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < t4; j += stride) {
+      const int64_t i = t4 - 1 - j;  // backwards, as k_bn_apply: the sums' last reads are still in L2
       const int64_t c = fc.mod(fs4.div((uint32_t)i));
       const float4 g = reinterpret_cast<const float4*>(dy)[i], xv = reinterpret_cast<const float4*>(x)[i];
       const float4 r = hr ? reinterpret_cast<const float4*>(relu_src)[i] : make_float4(1.f, 1.f, 1.f, 1.f);
@@ -165,143 +164,32 @@ __global__ void k_bn_bwd_apply(const float* __restrict__ dy, const float* __rest
 
 
 
-// ---- channel groups that stay in L2 -------------------------------------------------
-// An NCHW tensor of C channels is processed in groups of G consecutive
-// channels (G x N x S values, small enough for L2): the statistics pass and
-// the normalising pass of a group run back to back, so the second read of x
-// (and of dy in the backward) hits L2 instead of HBM.  In image n the group is
-// one contiguous run of G*S values; q4 = G*S/4 float4s per image.
-__global__ void k_bn_apply_grp(const float4* __restrict__ x, const float* __restrict__ mean,
-                               const float* __restrict__ invstd, const float* __restrict__ w,
-                               const float* __restrict__ b, float4* __restrict__ y, int64_t N, int64_t C, int64_t S4,
-                               int64_t c0, int64_t G, int relu, FastDiv fq4, FastDiv fs4) {
-  ::tp::pdl_enter();
-  const uint32_t q4 = (uint32_t)(G * S4);
-  const uint32_t total = (uint32_t)(N * q4);
-  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
-    const uint32_t n = fq4.div(i), r = i - n * q4;
-    const int64_t c = c0 + fs4.div(r);
-    const int64_t f4 = (int64_t)n * C * S4 + c0 * S4 + r;
-    const float mu = mean[c], sc = invstd[c] * (w ? w[c] : 1.0f), bs = b ? b[c] : 0.0f;
-    const float4 v = x[f4];
-    float r0 = (v.x - mu) * sc + bs, r1 = (v.y - mu) * sc + bs, r2 = (v.z - mu) * sc + bs, r3 = (v.w - mu) * sc + bs;
-    if (relu) {
-      r0 = fmaxf(r0, 0.0f);
-      r1 = fmaxf(r1, 0.0f);
-      r2 = fmaxf(r2, 0.0f);
-      r3 = fmaxf(r3, 0.0f);
-    }
-    y[f4] = make_float4(r0, r1, r2, r3);
-  }
-}
-
-__global__ void k_bn_bwd_apply_grp(const float4* __restrict__ dy, const float4* __restrict__ x,
-                                   const float4* __restrict__ relu_src, const float* __restrict__ mean,
-                                   const float* __restrict__ invstd, const float* __restrict__ coef,
-                                   float4* __restrict__ dx, int64_t N, int64_t C, int64_t S4, int64_t c0, int64_t G,
-                                   FastDiv fq4, FastDiv fs4) {
-  ::tp::pdl_enter();
-  const uint32_t q4 = (uint32_t)(G * S4);
-  const uint32_t total = (uint32_t)(N * q4);
-  const bool hr = relu_src != nullptr;
-  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
-    const uint32_t n = fq4.div(i), r = i - n * q4;
-    const int64_t c = c0 + fs4.div(r);
-    const int64_t f4 = (int64_t)n * C * S4 + c0 * S4 + r;
-    const float4 g = dy[f4], xv = x[f4];
-    const float4 rr = hr ? relu_src[f4] : make_float4(1.f, 1.f, 1.f, 1.f);
-    const float mu = mean[c], is = invstd[c], k0 = coef[c * 3], k1 = coef[c * 3 + 1], k2 = coef[c * 3 + 2];
-    dx[f4] = make_float4(bn_bwd1(g.x, rr.x, hr, xv.x, mu, is, k0, k1, k2), bn_bwd1(g.y, rr.y, hr, xv.y, mu, is, k0, k1, k2),
-                         bn_bwd1(g.z, rr.z, hr, xv.z, mu, is, k0, k1, k2), bn_bwd1(g.w, rr.w, hr, xv.w, mu, is, k0, k1, k2));
-  }
-}
-
-// Channels per group: the group's reads (`streams` tensors of N x S floats per
-// channel) fit in a share of L2 that leaves room for the pass's writes (the
-// budget in MB from TP_BN_GROUP_MB, default 48; 0 = no grouping); one group
-// when the whole tensor fits.
-static double bn_group_budget() {
-  static double mb = -1.0;
-  if (mb < 0.0) {
-    const char* e = getenv("TP_BN_GROUP_MB");
-    mb = e ? atof(e) : 48.0;
-  }
-  return mb * 1.0e6;
-}
-
-static int64_t bn_group(int64_t N, int64_t C, int64_t S, int streams) {
-  const double per = (double)N * (double)S * 4.0 * streams;
-  const double budget = bn_group_budget();
-  if (budget <= 0.0) return C;
-  if (per * C <= 2 * budget) return C;
-  int64_t g = (int64_t)(budget / per);
-  if (g < 1) g = 1;
-  while (N * g * (S >> 2) >= ((int64_t)1 << 31) && g > 1) g >>= 1;
-  return g < C ? g : C;
-}
-
 void launch_bn_train(const float* x, const float* w, const float* b, float* rm, float* rv, float* y,
                      float* save_mean, float* save_invstd, int64_t N, int64_t C, int64_t S, float eps,
                      float momentum, bool relu) {
-  auto kst = k_chan_reduce<ChanStatsF>;
-  const int64_t G = (S & 3) == 0 ? bn_group(N, C, S, 1) : C;
-  if (G < C) {
-    const int splits = chan_splits(G, N, S, sm_count());
-    double* part = (double*)scratch((size_t)G * splits * 2 * sizeof(double));
-    for (int64_t c0 = 0; c0 < C; c0 += G) {
-      const int64_t g = C - c0 < G ? C - c0 : G;
-      TP_LAUNCH(kst, dim3((unsigned)g, (unsigned)splits), 256, 0, ChanStatsF{x}, N, C, S, splits, part,
-                chan_div4(S), chan_div1(S), c0);
-      TP_LAUNCH(k_bn_finish, (unsigned)((g + 127) / 128), 128, 0, part, g, splits, (double)(N * S), eps, momentum,
-                save_mean, save_invstd, rm, rv, c0);
-      TP_LAUNCH(k_bn_apply_grp, grid_for(N * g * S, 256, 4), 256, 0, reinterpret_cast<const float4*>(x), save_mean,
-                save_invstd, w, b, reinterpret_cast<float4*>(y), N, C, S >> 2, c0, g, relu ? 1 : 0,
-                fast_div((uint32_t)(g * (S >> 2))), fast_div((uint32_t)(S >> 2)));
-    }
-    return;
-  }
   int splits = chan_splits(C, N, S, sm_count());
   double* part = (double*)scratch((size_t)C * splits * 2 * sizeof(double));
+  auto kst = k_chan_reduce<ChanStatsF>;
   TP_LAUNCH(kst, dim3((unsigned)C, (unsigned)splits), 256, 0, ChanStatsF{x}, N, C, S, splits, part, chan_div4(S),
-            chan_div1(S), (int64_t)0);
+            chan_div1(S));
   TP_LAUNCH(k_bn_finish, (unsigned)((C + 127) / 128), 128, 0, part, C, splits, (double)(N * S), eps, momentum,
-            save_mean, save_invstd, rm, rv, (int64_t)0);
+            save_mean, save_invstd, rm, rv);
   TP_LAUNCH(k_bn_apply, grid_for(N * C * S, 256, 4), 256, 0, x, save_mean, save_invstd, w, b, y, N, C, S,
             relu ? 1 : 0, chan_div4(S), fast_div((uint32_t)C));
 }
 
 void launch_bn_backward(const float* dy, const float* x, const float* relu_src, const float* w, const float* mean,
                         const float* invstd, float* dx, float* dw, float* db, int64_t N, int64_t C, int64_t S) {
-  auto kbs = k_chan_reduce<ChanBnBwdF>;
-  const int64_t G = (S & 3) == 0 ? bn_group(N, C, S, relu_src ? 3 : 2) : C;
-  if (G < C) {
-    const int splits = chan_splits(G, N, S, sm_count());
-    size_t pb = (size_t)G * splits * 2 * sizeof(double);
-    char* ws = (char*)scratch(pb + (size_t)C * 3 * sizeof(float) + 64);
-    double* part = (double*)ws;
-    float* coef = (float*)(ws + ((pb + 15) & ~(size_t)15));
-    for (int64_t c0 = 0; c0 < C; c0 += G) {
-      const int64_t g = C - c0 < G ? C - c0 : G;
-      TP_LAUNCH(kbs, dim3((unsigned)g, (unsigned)splits), 256, 0, ChanBnBwdF{dy, x, relu_src, mean, invstd}, N, C,
-                S, splits, part, chan_div4(S), chan_div1(S), c0);
-      TP_LAUNCH(k_bn_bwd_finish, (unsigned)((g + 127) / 128), 128, 0, part, g, splits, (double)(N * S), w, invstd,
-                coef, dw, db, c0);
-      TP_LAUNCH(k_bn_bwd_apply_grp, grid_for(N * g * S, 256, 4), 256, 0, reinterpret_cast<const float4*>(dy),
-                reinterpret_cast<const float4*>(x), reinterpret_cast<const float4*>(relu_src), mean, invstd, coef,
-                reinterpret_cast<float4*>(dx), N, C, S >> 2, c0, g, fast_div((uint32_t)(g * (S >> 2))),
-                fast_div((uint32_t)(S >> 2)));
-    }
-    return;
-  }
   int splits = chan_splits(C, N, S, sm_count());
   size_t pb = (size_t)C * splits * 2 * sizeof(double);
   char* ws = (char*)scratch(pb + (size_t)C * 3 * sizeof(float) + 64);
   double* part = (double*)ws;
   float* coef = (float*)(ws + ((pb + 15) & ~(size_t)15));
+  auto kbs = k_chan_reduce<ChanBnBwdF>;
   TP_LAUNCH(kbs, dim3((unsigned)C, (unsigned)splits), 256, 0, ChanBnBwdF{dy, x, relu_src, mean, invstd}, N, C, S,
-            splits, part, chan_div4(S), chan_div1(S), (int64_t)0);
+            splits, part, chan_div4(S), chan_div1(S));
   TP_LAUNCH(k_bn_bwd_finish, (unsigned)((C + 127) / 128), 128, 0, part, C, splits, (double)(N * S), w, invstd, coef,
-            dw, db, (int64_t)0);
+            dw, db);
   TP_LAUNCH(k_bn_bwd_apply, grid_for(N * C * S, 256, 4), 256, 0, dy, x, relu_src, mean, invstd, coef, dx, N, C, S,
             chan_div4(S), fast_div((uint32_t)C));
 }
