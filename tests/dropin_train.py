@@ -125,6 +125,17 @@ def main():
         if rt is not None:
             live.append(rt.memoryAllocated())
     res = {"losses": np.asarray(losses), "live": np.asarray(live, np.int64)}
+    ckpt = os.environ.get("DROPIN_CKPT")
+    if ckpt:  # the trained state dict through torch.save / torch.load (PyTorch's zip format)
+        torch.save(model.state_dict(), ckpt)
+        back = torch.load(ckpt, weights_only=False)
+        mine = model.state_dict(keep_vars=True) if rt is not None else model.state_dict()
+        same = set(back) == set(mine) and all(
+            np.array_equal(np.asarray(back[k].tolist(), np.float64), np.asarray(mine[k].tolist(), np.float64))
+            for k in mine)
+        res["ckpt_roundtrip_exact"] = np.asarray(same)
+        for k, v in mine.items():
+            res["state:" + k] = np.asarray(v.tolist(), np.float64)
     for n, p in zip(names, params):
         res["param:" + n] = arr(p)
         res["grad:" + n] = grads[n]

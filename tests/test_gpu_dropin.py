@@ -59,3 +59,24 @@ def test_pretrained_bundle_eval_on_cuda(tmp_path, name, tol):
     assert float(np.max(np.abs(a - w))) < tol
     assert float(np.max(np.abs(a - b))) <= 1e-4 * float(np.max(np.abs(b)))
     assert cu["keys"] == orc["keys"]
+
+
+def test_trained_vgg_state_dict_checkpoint_roundtrip(tmp_path):
+    """A VGG-11-BN trained 2 steps on the CUDA runtime, saved with the reference's
+    torch.save (tensor bytes through tp_to_bytes) and loaded back with its
+    torch.load (tp_from_bytes): every entry bit-exact, running statistics and
+    num_batches_tracked included; real PyTorch loads the same file to the same
+    values."""
+    ckpt = tmp_path / "vgg.pt"
+    env = dict(os.environ, DROPIN_CKPT=str(ckpt))
+    res = run_train("cuda", "vgg", 2, tmp_path / "c.npz", "sgd", env=env)
+    assert bool(res["ckpt_roundtrip_exact"])
+    code = ("import json, torch; sd = torch.load(%r, weights_only=False); "
+            "print(json.dumps({k: v.double().flatten().tolist() for k, v in sd.items()}))" % str(ckpt))
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-3000:]
+    real = json.loads(r.stdout.strip().splitlines()[-1])
+    states = {k[len("state:"):]: res[k] for k in res.files if k.startswith("state:")}
+    assert set(real) == set(states) and len(real) > 40
+    for k, v in real.items():
+        assert np.array_equal(np.asarray(v), states[k].ravel()), k
