@@ -254,6 +254,7 @@ struct NhwcShape {
   int64_t N, Cin, H, W, Cout, OH, OW;
   int KH, KW, PH, PW;
   bool khwc;  // filters stored [Cout][KH][KW][Cin] (else the reference's [Cout][Cin][KH][KW])
+  int DW = 1;  // tap spacing along W (the TMA paths only; the paired space-to-depth stem uses 2)
 };
 
 static NhwcShape nhwc_shape(int64_t N, int64_t Cin, int64_t H, int64_t W, int64_t Cout, int KH, int KW, int PH,
@@ -318,7 +319,7 @@ static bool conv_fwd_nhwc(const NhwcShape& s, const float* x, const float* w, co
       wlo = t;
     }
     mat_map(&mbl, MatOp{wlo, false, K, 0, false}, s.Cout, K, 1, brows);
-    tma::SrcConvK sa{tl.pt, (int)(s.Cin / 32), s.KW, s.PH, s.PW};
+    tma::SrcConvK sa{tl.pt, (int)(s.Cin / 32), s.KW, s.PH, s.PW, s.DW};
     if (y_nchw) {
       EpNchwOut eo{y_nchw, bias, s.Cout, s.OH * s.OW, s.N, tl.pt, tl.linear ? 1 : 0};
       gemm_tma_bn(ma, mb, sa, tma::SrcK{0}, eo, tl.linear ? M : tl.span, s.Cout, K, 1, &mbl);
@@ -328,6 +329,7 @@ static bool conv_fwd_nhwc(const NhwcShape& s, const float* x, const float* w, co
     else gemm_tma_bn(ma, mb, sa, tma::SrcK{0}, EpPixTile{y, s.Cout, s.N, bias, tl.pt}, tl.span, s.Cout, K, 1, &mbl);
     return false;
   }
+  TP_REQUIRE(s.DW == 1, "conv2d (channels-last): spaced taps need the TMA path");
   LdNhwcIm2col la{x, s.H, s.W, s.Cin, s.OH, s.OW, s.KW, s.PH, s.PW, M};
   gemm_auto(la, LdRowMajor{wp, K, 0}, ep, M, s.Cout, K, 1);
   return false;
@@ -340,9 +342,10 @@ static bool conv_dgrad_nhwc(const NhwcShape& s, const float* dy, const float* w,
   const int khw = s.KH * s.KW;
   const int64_t M = s.N * s.H * s.W, K = s.Cout * khw;
   if (M == 0) return false;
-  TP_REQUIRE(s.PH <= s.KH - 1 && s.PW <= s.KW - 1, "conv2d data gradient (channels-last): padding exceeds kernel-1");
+  TP_REQUIRE(s.PH <= s.KH - 1 && s.PW <= (s.KW - 1) * s.DW,
+             "conv2d data gradient (channels-last): padding exceeds the kernel's extent - 1");
   EpRowMajor ep{dx, s.Cin, 0, nullptr, 0};
-  const int qh = s.KH - 1 - s.PH, qw = s.KW - 1 - s.PW;
+  const int qh = s.KH - 1 - s.PH, qw = (s.KW - 1) * s.DW - s.PW;
   Tiling tl;
   const bool tma_a = nhwc_tma_ok() && M >= 64 && s.Cout % 32 == 0 && pixel_tiling(s.N, s.H, s.W, tc::BM, tl) &&
                      nhwc_map(nullptr, dy, s.N, s.OH, s.OW, s.Cout, tl.pt, false);
@@ -362,7 +365,7 @@ static bool conv_dgrad_nhwc(const NhwcShape& s, const float* dy, const float* w,
     }
     TP_REQUIRE(((uintptr_t)wlo & 15) == 0, "conv2d data gradient (channels-last): w_lo must be 16-byte aligned");
     make_map_f32(&mbl, wlo, 4, dims, st, box, true);
-    tma::SrcConvK sa{tl.pt, (int)(s.Cout / 32), s.KW, qh, qw};
+    tma::SrcConvK sa{tl.pt, (int)(s.Cout / 32), s.KW, qh, qw, s.DW};
     tma::SrcFilterMN sb{(int)(s.Cout / 32), khw};
     if (dx_nchw) {
       EpNchwOut eo{dx_nchw, nullptr, s.Cin, s.H * s.W, s.N, tl.pt, tl.linear ? 1 : 0};
@@ -384,7 +387,7 @@ static bool conv_dgrad_nhwc(const NhwcShape& s, const float* dy, const float* w,
     float* wlo = (float*)scratch3((size_t)s.Cin * K * sizeof(float));
     tf32_lo_plane(wp, wlo, s.Cin * K);
     mat_map(&mbl, MatOp{wlo, false, K, 0, false}, s.Cin, K, 1, brows);
-    tma::SrcConvK sa{tl.pt, (int)(s.Cout / 32), s.KW, qh, qw};
+    tma::SrcConvK sa{tl.pt, (int)(s.Cout / 32), s.KW, qh, qw, s.DW};
     if (dx_nchw) {
       EpNchwOut eo{dx_nchw, nullptr, s.Cin, s.H * s.W, s.N, tl.pt, tl.linear ? 1 : 0};
       gemm_tma_bn(ma, mb, sa, tma::SrcK{0}, eo, tl.linear ? M : tl.span, s.Cin, K, 1, &mbl);
@@ -395,6 +398,7 @@ static bool conv_dgrad_nhwc(const NhwcShape& s, const float* dy, const float* w,
                      &mbl);
     return false;
   }
+  TP_REQUIRE(s.DW == 1, "conv2d data gradient (channels-last): spaced taps need the TMA path");
   LdNhwcIm2col la{dy, s.OH, s.OW, s.Cout, s.H, s.W, s.KW, qh, qw, M};
   gemm_auto(la, LdRowMajor{wp, K, 0}, ep, M, s.Cin, K, 1);
   return false;
@@ -417,13 +421,13 @@ static void conv_wgrad_nhwc(const NhwcShape& s, const float* dy, const float* x,
       CUtensorMap ma, mb;
       nhwc_mn_map(&ma, dy, s.N, s.OH, s.OW, s.Cout, tl.pt, tc::BM, true);
       nhwc_mn_map(&mb, x, s.N, s.H, s.W, s.Cin, tl.pt, (uint32_t)s.Cin, true);
-      tma::SrcPixMN sa{tl.pt, s.KW, s.PH, s.PW, 0};
+      tma::SrcPixMN sa{tl.pt, s.KW, s.PH, s.PW, 0, s.DW};
       if (s.Cin == 64) {
-        tma::SrcPixMNT<2> sb{tl.pt, s.KW, s.PH, s.PW, khw};
+        tma::SrcPixMNT<2> sb{tl.pt, s.KW, s.PH, s.PW, khw, s.DW};
         gemm_tma_launch<tma::SrcPixMN, tma::SrcPixMNT<2>, EpWgradTapsKhwc<2>, 128, 4>(
             ma, mb, sa, sb, EpWgradTapsKhwc<2>{dw, s.Cin, khw}, s.Cout, 128, tl.span, (khw + 1) / 2);
       } else {
-        tma::SrcPixMNT<4> sb{tl.pt, s.KW, s.PH, s.PW, khw};
+        tma::SrcPixMNT<4> sb{tl.pt, s.KW, s.PH, s.PW, khw, s.DW};
         gemm_tma_launch<tma::SrcPixMN, tma::SrcPixMNT<4>, EpWgradTapsKhwc<4>, 128, 4>(
             ma, mb, sa, sb, EpWgradTapsKhwc<4>{dw, s.Cin, khw}, s.Cout, 128, tl.span, (khw + 3) / 4);
       }
@@ -433,12 +437,13 @@ static void conv_wgrad_nhwc(const NhwcShape& s, const float* dy, const float* x,
     CUtensorMap ma, mb;
     nhwc_mn_map(&ma, dy, s.N, s.OH, s.OW, s.Cout, tl.pt, tc::BM, true);
     nhwc_mn_map(&mb, x, s.N, s.H, s.W, s.Cin, tl.pt, bn, true);
-    tma::SrcPixMN sa{tl.pt, s.KW, s.PH, s.PW, 0};
-    tma::SrcPixMN sb{tl.pt, s.KW, s.PH, s.PW, 1};
+    tma::SrcPixMN sa{tl.pt, s.KW, s.PH, s.PW, 0, s.DW};
+    tma::SrcPixMN sb{tl.pt, s.KW, s.PH, s.PW, 1, s.DW};
     if (s.khwc) gemm_tma_bn(ma, mb, sa, sb, EpWgradTapKhwc{dw, s.Cin, khw}, s.Cout, s.Cin, tl.span, khw);
     else gemm_tma_bn(ma, mb, sa, sb, EpWgradTap{dw, s.Cin, khw}, s.Cout, s.Cin, tl.span, khw);
     return;
   }
+  TP_REQUIRE(s.DW == 1, "conv2d weight gradient (channels-last): spaced taps need the TMA path");
   const int64_t R = s.Cin * khw;
   EpRowMajor ep{dw, R, 0, nullptr, 0};
   if (P == 0) {
@@ -611,9 +616,142 @@ __global__ void k_s2d_filters(const float* __restrict__ src, float* __restrict__
   }
 }
 
+// ---- paired space-to-depth (C <= 4): two x' pixels per 32-channel vector ---------------------
+// x''[n][Y][X][q*4C + ph*C + ci] = x'[n][Y][X + q][ph*C + ci] (q = 0, 1; zeros past WX): the
+// AxA convolution over x' becomes an A x ceil(A/2) one over x'' whose column taps are 2
+// pixels apart (tap (a, p) reads x'' at (Y + a, X + 2p), i.e. x' at X + 2p + q), so a
+// 32-wide k-block carries 8C real values instead of 4C and K halves (7x7 / 3-channel stem:
+// 8 taps x 32 = 256 instead of 16 x 32 = 512 for 147 real products).
+template <int C>
+__global__ void k_s2d_pair_in(const float* __restrict__ x, float* __restrict__ xs, S2d d, FastDiv fwx,
+                              FastDiv fhy) {
+  ::tp::pdl_enter();
+  const uint32_t total = (uint32_t)(d.N * d.HY * d.WX);
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const uint32_t t = fwx.div(i), X = i - t * (uint32_t)d.WX;
+    const uint32_t n = fhy.div(t), Y = t - n * (uint32_t)d.HY;
+    float v[32];
+#pragma unroll
+    for (int k = 0; k < 32; ++k) v[k] = 0.0f;
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      if (X + q >= (uint32_t)d.WX) continue;
+#pragma unroll
+      for (int ph = 0; ph < 4; ++ph) {
+        const int64_t ih = 2 * (int64_t)Y + (ph >> 1) - d.O, iw = 2 * (int64_t)(X + q) + (ph & 1) - d.O;
+        if (ih < 0 || ih >= d.H || iw < 0 || iw >= d.W) continue;
+        const float* src = x + ((int64_t)n * C * d.H + ih) * d.W + iw;
+#pragma unroll
+        for (int ci = 0; ci < C; ++ci) v[q * 4 * C + ph * C + ci] = src[(int64_t)ci * d.H * d.W];
+      }
+    }
+    float4* dst = reinterpret_cast<float4*>(xs + (int64_t)i * 32);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) dst[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+  }
+}
+
+static void s2d_pair_in(const float* x, float* xs, const S2d& d) {
+  const int g = grid_for(d.N * d.HY * d.WX, 256);
+  const FastDiv fwx = fast_div((uint32_t)d.WX), fhy = fast_div((uint32_t)d.HY);
+  switch (d.C) {
+    case 1: TP_LAUNCH(k_s2d_pair_in<1>, g, 256, 0, x, xs, d, fwx, fhy); break;
+    case 2: TP_LAUNCH(k_s2d_pair_in<2>, g, 256, 0, x, xs, d, fwx, fhy); break;
+    case 3: TP_LAUNCH(k_s2d_pair_in<3>, g, 256, 0, x, xs, d, fwx, fhy); break;
+    case 4: TP_LAUNCH(k_s2d_pair_in<4>, g, 256, 0, x, xs, d, fwx, fhy); break;
+    default: TP_REQUIRE(false, "paired space-to-depth: 1 to 4 channels");
+  }
+}
+
+// w [Cout][C][K][K] <-> w'' [Cout][A][AP][32], AP = (A + 1) / 2: slot q*4C + ph*C + ci of
+// tap (a, p) is w' tap (a, 2p + q), phase ph, channel ci (zero where that tap does not exist);
+// to_s2d = 0 maps a w''-shaped gradient back (each w tap has exactly one slot).
+__global__ void k_s2d_pair_filters(const float* __restrict__ src, float* __restrict__ dst, int64_t Cout, S2d d,
+                                   int to_s2d) {
+  ::tp::pdl_enter();
+  const int AP = (d.A + 1) / 2;
+  const int64_t total = Cout * d.A * AP * 32;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int sl = (int)(i & 31);
+    int64_t t = i >> 5;
+    const int p = (int)(t % AP);
+    t /= AP;
+    const int a = (int)(t % d.A);
+    const int64_t co = t / d.A;
+    int kh = -1, kw = -1, ci = 0;
+    if (sl < 8 * d.C) {
+      const int q = sl / (4 * d.C), r = sl - q * 4 * d.C, ph = r / d.C;
+      ci = r - ph * d.C;
+      const int b = 2 * p + q;
+      if (b < d.A) {
+        kh = 2 * a + (ph >> 1) + d.P - d.O;
+        kw = 2 * b + (ph & 1) + d.P - d.O;
+      }
+    }
+    const bool tap = kh >= 0 && kh < d.K && kw >= 0 && kw < d.K;
+    const int64_t wi = ((co * d.C + ci) * d.K + kh) * d.K + kw;
+    if (to_s2d) dst[i] = tap ? src[wi] : 0.0f;
+    else if (tap) dst[wi] = src[i];
+  }
+}
+
+// dx'' [N][HY][WX][32] -> dx (NCHW): x' pixel (Y, X) was copied to x'' (Y, X) slot q = 0 and
+// (Y, X - 1) slot q = 1, so its gradient is the sum of those two.
+__global__ void k_s2d_pair_out(const float* __restrict__ dxs, float* __restrict__ dx, S2d d) {
+  ::tp::pdl_enter();
+  const int64_t total = d.N * d.C * d.H * d.W;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t iw = i % d.W;
+    int64_t t = i / d.W;
+    const int64_t ih = t % d.H;
+    t /= d.H;
+    const int ci = (int)(t % d.C);
+    const int64_t n = t / d.C;
+    const int64_t ry = ih + d.O, rx = iw + d.O;
+    const int64_t Y = ry >> 1, X = rx >> 1;
+    const int r = (int)(((ry & 1) * 2 + (rx & 1)) * d.C + ci);
+    float v = 0.0f;
+    if (Y < d.HY && X < d.WX) {
+      const float* row = dxs + (n * d.HY + Y) * d.WX * 32;
+      v = row[X * 32 + r];
+      if (X >= 1) v += row[(X - 1) * 32 + 4 * d.C + r];
+    }
+    dx[i] = v;
+  }
+}
+
+static NhwcShape pair_shape(const S2d& d, int64_t Cout) {
+  NhwcShape t = nhwc_shape(d.N, 32, d.HY, d.WX, Cout, d.A, (d.A + 1) / 2, 0, 0, 1);
+  t.DW = 2;
+  t.OH = d.OH;  // the paired taps reach past the last output column; the grid is the s2d one
+  t.OW = d.OW;
+  return t;
+}
+
+// the paired taps exist only on the TMA paths: every pass's pixel tiling must be possible
+static bool pair_ok(const S2d& d) {
+  Tiling tl;
+  return d.C <= 4 && nhwc_tma_ok() && pixel_tiling(d.N, d.OH, d.OW, tc::BM, tl) &&
+         pixel_tiling(d.N, d.HY, d.WX, tc::BM, tl) && pixel_tiling(d.N, d.OH, d.OW, 32, tl);
+}
+
 bool conv_fwd_s2d(const ConvShape& s, const float* x, const float* w, const float* bias, float* y) {
   S2d d;
   if (!s2d_plan(s, d) || (bias && ((uintptr_t)bias & 15))) return false;
+  if (pair_ok(d) && s.Cout % 4 == 0) {
+    const NhwcShape t = pair_shape(d, s.Cout);
+    const int AP = (d.A + 1) / 2;
+    float* xs = (float*)dalloc((size_t)d.N * d.HY * d.WX * 32 * 4);
+    float* ws = (float*)dalloc((size_t)s.Cout * d.A * AP * 32 * 4);
+    float* yn = (float*)dalloc((size_t)d.N * d.OH * d.OW * s.Cout * 4);
+    s2d_pair_in(x, xs, d);
+    TP_LAUNCH(k_s2d_pair_filters, grid_for(s.Cout * d.A * AP * 32, 256), 256, 0, w, ws, s.Cout, d, 1);
+    if (!conv_fwd_nhwc(t, xs, ws, bias, yn, nullptr, y)) transpose_nchw_nhwc(yn, y, d.N, s.Cout, d.OH * d.OW, false);
+    dfree(xs);
+    dfree(ws);
+    dfree(yn);
+    return true;
+  }
   const NhwcShape t = nhwc_shape(d.N, 32, d.HY, d.WX, s.Cout, d.A, d.A, 0, 0, 1);
   float* xs = (float*)dalloc((size_t)d.N * d.HY * d.WX * 32 * 4);
   float* ws = (float*)dalloc((size_t)s.Cout * d.A * d.A * 32 * 4);
@@ -630,6 +768,21 @@ bool conv_fwd_s2d(const ConvShape& s, const float* x, const float* w, const floa
 bool conv_dgrad_s2d(const ConvShape& s, const float* dy, const float* w, float* dx) {
   S2d d;
   if (!s2d_plan(s, d) || s.Cout % 32) return false;
+  if (pair_ok(d)) {
+    const NhwcShape t = pair_shape(d, s.Cout);
+    const int AP = (d.A + 1) / 2;
+    float* dyn = (float*)dalloc((size_t)d.N * d.OH * d.OW * s.Cout * 4);
+    float* ws = (float*)dalloc((size_t)s.Cout * d.A * AP * 32 * 4);
+    float* dxs = (float*)dalloc((size_t)d.N * d.HY * d.WX * 32 * 4);
+    transpose_nchw_nhwc(dy, dyn, d.N, s.Cout, d.OH * d.OW, true);
+    TP_LAUNCH(k_s2d_pair_filters, grid_for(s.Cout * d.A * AP * 32, 256), 256, 0, w, ws, s.Cout, d, 1);
+    conv_dgrad_nhwc(t, dyn, ws, dxs);
+    TP_LAUNCH(k_s2d_pair_out, grid_for(d.N * d.C * d.H * d.W, 256), 256, 0, dxs, dx, d);
+    dfree(dyn);
+    dfree(ws);
+    dfree(dxs);
+    return true;
+  }
   const NhwcShape t = nhwc_shape(d.N, 32, d.HY, d.WX, s.Cout, d.A, d.A, 0, 0, 1);
   float* dyn = (float*)dalloc((size_t)d.N * d.OH * d.OW * s.Cout * 4);
   float* ws = (float*)dalloc((size_t)s.Cout * d.A * d.A * 32 * 4);
@@ -647,6 +800,21 @@ bool conv_dgrad_s2d(const ConvShape& s, const float* dy, const float* w, float* 
 bool conv_wgrad_s2d(const ConvShape& s, const float* dy, const float* x, float* dw) {
   S2d d;
   if (!s2d_plan(s, d) || s.Cout % 32 || s.Cout < 64) return false;
+  if (pair_ok(d)) {
+    const NhwcShape t = pair_shape(d, s.Cout);
+    const int AP = (d.A + 1) / 2;
+    float* dyn = (float*)dalloc((size_t)d.N * d.OH * d.OW * s.Cout * 4);
+    float* xs = (float*)dalloc((size_t)d.N * d.HY * d.WX * 32 * 4);
+    float* dws = (float*)dalloc((size_t)s.Cout * d.A * AP * 32 * 4);
+    transpose_nchw_nhwc(dy, dyn, d.N, s.Cout, d.OH * d.OW, true);
+    s2d_pair_in(x, xs, d);
+    conv_wgrad_nhwc(t, dyn, xs, dws);
+    TP_LAUNCH(k_s2d_pair_filters, grid_for(s.Cout * d.A * AP * 32, 256), 256, 0, dws, dw, s.Cout, d, 0);
+    dfree(dyn);
+    dfree(xs);
+    dfree(dws);
+    return true;
+  }
   const NhwcShape t = nhwc_shape(d.N, 32, d.HY, d.WX, s.Cout, d.A, d.A, 0, 0, 1);
   float* dyn = (float*)dalloc((size_t)d.N * d.OH * d.OW * s.Cout * 4);
   float* xs = (float*)dalloc((size_t)d.N * d.HY * d.WX * 32 * 4);

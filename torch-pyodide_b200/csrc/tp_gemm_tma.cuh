@@ -192,6 +192,7 @@ struct SrcConvK {
   static constexpr bool kMN = false;
   PixTile pt;
   int cblocks, KW, PH, PW;
+  int DW = 1;  // spacing of the taps along W (2: the paired space-to-depth stem)
   struct Cur {
     int c0, kh, kw, n0, oh0, ow0;
   };
@@ -206,7 +207,7 @@ struct SrcConvK {
     return c;
   }
   __device__ __forceinline__ void issue(const CUtensorMap* map, uint32_t dst, uint64_t* bar, const Cur& c) const {
-    load4(dst, map, c.c0, c.ow0 + c.kw - PW, c.oh0 + c.kh - PH, c.n0, bar);
+    load4(dst, map, c.c0, c.ow0 + c.kw * DW - PW, c.oh0 + c.kh - PH, c.n0, bar);
   }
   __device__ __forceinline__ void next(Cur& c) const {
     c.c0 += 32;
@@ -232,6 +233,7 @@ struct SrcPixMN {
   static constexpr bool kMN = true;
   PixTile pt;
   int KW, PH, PW, shift;
+  int DW = 1;  // tap spacing along W
   // k-block = one 32-pixel tile (n0, tile row th, tile column tw)
   struct Cur {
     int n0, th, tw, dh, dw, cg;
@@ -244,7 +246,7 @@ struct SrcPixMN {
     c.th = pt.TN > 1 ? 0 : oh0 / pt.TH;
     c.tw = pt.TN > 1 ? 0 : ow0 / pt.TW;
     c.dh = shift ? b / KW - PH : 0;
-    c.dw = shift ? b - (b / KW) * KW - PW : 0;
+    c.dw = shift ? (b - (b / KW) * KW) * DW - PW : 0;
     c.cg = (int)(r0 >> 5);
     return c;
   }
@@ -275,6 +277,7 @@ struct SrcPixMNT {
   static constexpr uint32_t kTapBytes = 16384 / TAPS;  // (128 / TAPS) rows of the MN-major tile
   PixTile pt;
   int KW, PH, PW, KHW;
+  int DW = 1;  // tap spacing along W
   struct Cur {
     int n0, th, tw;
     int dh[TAPS], dw[TAPS];
@@ -291,7 +294,7 @@ struct SrcPixMNT {
     for (int j = 0; j < TAPS; ++j) {
       const int t = TAPS * b + j < KHW ? TAPS * b + j : KHW - 1;
       c.dh[j] = t / KW - PH;
-      c.dw[j] = t - (t / KW) * KW - PW;
+      c.dw[j] = (t - (t / KW) * KW) * DW - PW;
     }
     return c;
   }
