@@ -3,7 +3,7 @@ launched under torch.distributed.run with NCCL_NVLS_ENABLE=0.
 
 Both ranks build the NCCL communicator through the file store and complete one
 all-reduce step.  Then rank 1 leaves between steps (no collective in flight:
-it destroys its communicator, leaves a store mark and exits).  Rank 0 learns of it on the host before its
+it leaves a store mark, destroys its communicator and exits).  Rank 0 learns of it on the host before its
 next step, so it issues no collective that would wait for rank 1; it then keeps
 its library stream busy with a bounded device wait (tp_wait_probe, 400 ms) and
 calls the watchdog tp_comm_sync with a 50 ms limit, which must give up with
@@ -38,8 +38,10 @@ def main(out_path):
     first = float(rt.toNumpy(x["id"])[0])
     store.barrier()
     if rank == 1:
-        comm.close()  # nothing in flight: release this rank's communicator, then leave
+        # nothing in flight: leave the mark first (destroying the communicator
+        # can wait for the peer's own teardown), then release it and exit
         store.leave()
+        comm.close()
         return
     seen = None
     for _ in range(2000):  # the next step's check, before any collective
