@@ -729,6 +729,20 @@ def run_ops(args):
     ss, isb = adam_scalars(1)
     ms = timed_inplace(lambda: rt.adamStepMulti(ids(P), ids(G), ids(S0), ids(S1), LR, B1, B2, EPS, WD, ss, isb))
     add("adam L2 wd (multi-tensor)", [NTENSORS, elems], ms, 28 * elems, "hbm")
+    # the other fused steps (rmsprop_step.wgsl, extended_step.wgsl) over the same set:
+    # bytes per element read + written (Adagrad keeps one state tensor)
+    ext = [("rmsprop momentum 0.9 (multi-tensor)", 28,
+            lambda: rt.rmspropStepMulti(ids(P), ids(G), ids(S0), ids(S1), 0.01, 0.99, 1e-8, 0.0, 0.9)),
+           ("adagrad (multi-tensor)", 20, lambda: rt.adagradStepMulti(ids(P), ids(G), ids(S0), 0.01, 1e-10, 0.0)),
+           ("adamax (multi-tensor)", 28,
+            lambda: rt.adamaxStepMulti(ids(P), ids(G), ids(S0), ids(S1), 0.002, 0.9, 0.999, 1e-8, 0.0, 0.02, 1.0)),
+           ("nadam (multi-tensor)", 28,
+            lambda: rt.nadamStepMulti(ids(P), ids(G), ids(S0), ids(S1), 0.002, 0.9, 0.999, 1e-8, 0.0, 0.02, 0.9)),
+           ("radam (multi-tensor)", 28,
+            lambda: rt.radamStepMulti(ids(P), ids(G), ids(S0), ids(S1), 1e-3, 0.9, 0.999, 1e-8, 0.0, 0.01, 0.53, 0.994,
+                                      6))]
+    for name, bpe, fn in ext:
+        add(name, [NTENSORS, elems], timed_inplace(fn), bpe * elems, "hbm")
     for h in P + G + S0 + S1:
         rt.destroy(h["id"])
     cpu_cores = None

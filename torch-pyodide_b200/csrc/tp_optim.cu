@@ -269,7 +269,31 @@ __global__ void __launch_bounds__(256) k_ext_multi(const OptRow* __restrict__ ro
     const float4* G4 = reinterpret_cast<const float4*>(G);
     float4* A4 = reinterpret_cast<float4*>(S0);
     float4* B4 = reinterpret_cast<float4*>(S1);
-    for (int i = threadIdx.x; i < len4; i += blockDim.x) {
+    int i = threadIdx.x;
+    // two float4 per thread per iteration, all loads issued before the math
+    for (; i + (int)blockDim.x < len4; i += 2 * blockDim.x) {
+      const int j = i + blockDim.x;
+      float4 p0 = P4[i], g0 = G4[i], a0 = A4[i], p1 = P4[j], g1 = G4[j], a1 = A4[j];
+      float4 b0 = two ? B4[i] : make_float4(0, 0, 0, 0);
+      float4 b1 = two ? B4[j] : make_float4(0, 0, 0, 0);
+      ext_elem<KIND>(p0.x, g0.x, a0.x, b0.x, h);
+      ext_elem<KIND>(p0.y, g0.y, a0.y, b0.y, h);
+      ext_elem<KIND>(p0.z, g0.z, a0.z, b0.z, h);
+      ext_elem<KIND>(p0.w, g0.w, a0.w, b0.w, h);
+      ext_elem<KIND>(p1.x, g1.x, a1.x, b1.x, h);
+      ext_elem<KIND>(p1.y, g1.y, a1.y, b1.y, h);
+      ext_elem<KIND>(p1.z, g1.z, a1.z, b1.z, h);
+      ext_elem<KIND>(p1.w, g1.w, a1.w, b1.w, h);
+      P4[i] = p0;
+      A4[i] = a0;
+      P4[j] = p1;
+      A4[j] = a1;
+      if (two) {
+        B4[i] = b0;
+        B4[j] = b1;
+      }
+    }
+    for (; i < len4; i += blockDim.x) {
       float4 p = P4[i], g = G4[i], a = A4[i];
       float4 b = two ? B4[i] : make_float4(0, 0, 0, 0);
       ext_elem<KIND>(p.x, g.x, a.x, b.x, h);
