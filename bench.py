@@ -887,6 +887,49 @@ def vgg_launch_list(args):
     m.close()
 
 
+def profile_case(args):
+    """Profiling aid (1 GPU, no timing): two identical iterations of one per-op
+    case on the handle API, so an ncu capture can select the second one.
+      bn     BatchNorm2d train fwd + bwd on [256,128,56,56] (4 kernels per
+             iteration: statistics, normalise, backward sums, backward apply)
+      stem   the 7x7 stride-2 3 -> 64 convolution forward on [32,3,224,224]
+             (one tensor-core GEMM per iteration)
+      optim  RMSprop (momentum 0.9) then NAdam over 8 tensors of the optimizer
+             workload's shapes (one fused launch each per iteration)"""
+    from tpcuda import CudaRuntime
+    rt = CudaRuntime(0)
+    rt.setSeed(0)
+    ids = lambda hs: [h["id"] for h in hs]  # noqa: E731
+    if args.profile_case == "bn":
+        shp = [256, 128, 56, 56]
+        x, dy = rt.randn(shp, "float32"), rt.randn(shp, "float32")
+        g, b = rt.full([128], 1.0, "float32"), rt.full([128], 0.0, "float32")
+        rm, rv = rt.full([128], 0.0, "float32"), rt.full([128], 1.0, "float32")
+
+        def it():
+            y, mean, inv = rt.batchNormTrain(x["id"], g["id"], b["id"], rm["id"], rv["id"], 1e-5, 0.1)
+            for h in [y, mean, inv] + rt.batchNormBackward(dy["id"], x["id"], g["id"], mean["id"], inv["id"]):
+                rt.destroy(h["id"])
+    elif args.profile_case == "stem":
+        x, w = rt.randn([32, 3, 224, 224], "float32"), rt.randn([64, 3, 7, 7], "float32")
+
+        def it():
+            rt.destroy(rt.conv2d(x["id"], w["id"], None, [2], [3], [1], 1)["id"])
+    else:
+        P = [rt.normal(SHAPES[i % 4], "float32", 0.0, 0.02) for i in range(8)]
+        G = [rt.normal(SHAPES[i % 4], "float32", 0.0, 1e-3) for i in range(8)]
+        S0 = [rt.zeros(SHAPES[i % 4], "float32") for i in range(8)]
+        S1 = [rt.zeros(SHAPES[i % 4], "float32") for i in range(8)]
+
+        def it():
+            rt.rmspropStepMulti(ids(P), ids(G), ids(S0), ids(S1), 0.01, 0.99, 1e-8, 0.0, 0.9)
+            rt.nadamStepMulti(ids(P), ids(G), ids(S0), ids(S1), 0.002, 0.9, 0.999, 1e-8, 0.0, 0.02, 0.9)
+    for _ in range(2):
+        it()
+    rt.synchronize()
+    print(json.dumps({"profile_case": args.profile_case, "iterations": 2}), flush=True)
+
+
 def run_conv_layer(args):
     """One VGG-11-BN convolution pass on channels-last buffers with packed
     [Cout][3][3][Cin] filters (the step's own layout and entries), timed with
@@ -1120,9 +1163,14 @@ def main():
     ap.add_argument("--batch", type=int, default=VGG_GLOBAL_BATCH, help="per-GPU batch for --launch-list")
     ap.add_argument("--tensors", type=int, default=NTENSORS,
                     help="number of parameter tensors (64 = the benchmark; fewer for profiler captures)")
+    ap.add_argument("--profile-case", choices=["bn", "stem", "optim"], default=None,
+                    help="profiling aid: two iterations of one per-op case (1 GPU, no timing)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.profile_case:
+        profile_case(args)
+        return
     if args.launch_list:
         vgg_launch_list(args)
         return
