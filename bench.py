@@ -583,9 +583,33 @@ def run_ops(args):
     rt.setSeed(0)
     results = []
 
-    def timed(fn, n_out):
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        nvml_dev = pynvml.nvmlDeviceGetHandleByIndex(torch.cuda.current_device())
+    except Exception:  # noqa: BLE001 - no NVML: rows carry no clock
+        pynvml, nvml_dev = None, None
+    last_clk = {}
+
+    def read_clock():
+        if nvml_dev is None:
+            return {}
+        try:
+            r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(nvml_dev)
+            return {"sm_mhz_end": pynvml.nvmlDeviceGetClockInfo(nvml_dev, pynvml.NVML_CLOCK_SM),
+                    "sw_power_cap_end": bool(r & pynvml.nvmlClocksEventReasonSwPowerCap)}
+        except Exception:  # noqa: BLE001
+            return {}
+
+    def timed(fn, n_out, idle=False):
         # outputs are destroyed as soon as they are made (stream-ordered), so the
-        # pool serves every rep from the blocks of the warm-up call
+        # pool serves every rep from the blocks of the warm-up call.  idle: a
+        # contraction row starts after 0.25 s without GPU work, so it is timed in
+        # the burst regime of the burst GEMM peak it is divided by, not under the
+        # power cap that the previous rows' seconds of tensor work engage
+        if idle:
+            rt.synchronize()
+            time.sleep(0.25)
         for _ in range(2):
             for o in fn()[:n_out]:
                 rt.destroy(o["id"])
@@ -597,6 +621,8 @@ def run_ops(args):
                 rt.destroy(o["id"])
         e1.record(stream)
         e1.synchronize()
+        last_clk.clear()
+        last_clk.update(read_clock())
         return e0.elapsed_time(e1) / reps
 
     def add(name, shape, ms, work, bound):
@@ -608,6 +634,7 @@ def run_ops(args):
             achieved = work / (ms * 1e-3) / 1e12
             results.append({"op": name, "shape": shape, "ms": round(ms, 4), "TFLOP/s": round(achieved, 2),
                             "frac_of_3xtf32": round(achieved / peak3, 3)})
+        results[-1].update(last_clk)
 
     one = lambda h: [h]  # noqa: E731
     # ---- reductions and norms ----
@@ -674,13 +701,13 @@ def run_ops(args):
     for n in (512, 2048, 8192):
         a = rt.rand([n, n], "float32")
         bb = rt.rand([n, n], "float32")
-        add("matmul", [n, n, n], timed(lambda: one(rt.matmul(a["id"], bb["id"])), 1), 2.0 * n ** 3, "tensor")
+        add("matmul", [n, n, n], timed(lambda: one(rt.matmul(a["id"], bb["id"])), 1, True), 2.0 * n ** 3, "tensor")
         rt.destroy(a["id"])
         rt.destroy(bb["id"])
     xl = rt.rand([16384, 4096], "float32")
     wl = rt.rand([11008, 4096], "float32")
     bl = rt.rand([11008], "float32")
-    add("linear +bias", [16384, 4096, 11008], timed(lambda: one(rt.linear(xl["id"], wl["id"], bl["id"])), 1),
+    add("linear +bias", [16384, 4096, 11008], timed(lambda: one(rt.linear(xl["id"], wl["id"], bl["id"])), 1, True),
         2.0 * 16384 * 4096 * 11008, "tensor")
     for h in (xl, wl, bl):
         rt.destroy(h["id"])
@@ -692,12 +719,13 @@ def run_ops(args):
         gy = rt.randn(ys, "float32")
         fl = 2.0 * ys[0] * ys[1] * oh * oh * xs[1] * ws[2] * ws[3]
         tag = f"{ws[2]}x{ws[3]} s{st}"
-        add(f"conv2d fwd {tag}", xs, timed(lambda: one(rt.conv2d(xc["id"], wc["id"], None, [st], [pd], [1], 1)), 1),
-            fl, "tensor")
+        add(f"conv2d fwd {tag}", xs,
+            timed(lambda: one(rt.conv2d(xc["id"], wc["id"], None, [st], [pd], [1], 1)), 1, True), fl, "tensor")
         add(f"conv2d dgrad {tag}", xs,
-            timed(lambda: one(rt.conv2dInputBackward(gy["id"], wc["id"], xs, ys, [st], [pd])), 1), fl, "tensor")
+            timed(lambda: one(rt.conv2dInputBackward(gy["id"], wc["id"], xs, ys, [st], [pd])), 1, True), fl,
+            "tensor")
         add(f"conv2d wgrad {tag}", xs,
-            timed(lambda: one(rt.conv2dWeightBackward(gy["id"], xc["id"], ws, ys, xs, [st], [pd])), 1), fl,
+            timed(lambda: one(rt.conv2dWeightBackward(gy["id"], xc["id"], ws, ys, xs, [st], [pd])), 1, True), fl,
             "tensor")
         for h in (xc, wc, gy):
             rt.destroy(h["id"])
@@ -758,6 +786,9 @@ def run_ops(args):
                                 "contractions: TFLOP/s of 3xTF32)", "n_gpus": 1, "reps": reps, "hbm_peak_gbs": hbm,
                       "tf32x3_peak_tflops": round(peak3, 1), "peak_source": f"{peak_kind} bf16 {bf16}",
                       "path": "CudaRuntime handle API (the reference-facing surface), NCHW",
+                      "timing": ("CUDA events over the reps after 2 warm-up calls; contraction rows start after "
+                                 "0.25 s idle (burst regime, as the burst bf16 peak); sm_mhz_end: NVML SM clock "
+                                 "right after each row's timed region"),
                       "cpu_baseline_cores": cpu_cores, "results": results}), flush=True)
 
 

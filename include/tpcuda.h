@@ -523,6 +523,20 @@ TP_API int tpk_cross_entropy_mean(const float* logits, const float* targets, flo
  * share the array: calls that overlap on the GPU race. */
 TP_API int tpk_cross_entropy_mean_noalloc(const float* logits, const float* targets, float* loss_mean, int64_t B,
                                           int64_t C);
+/* New: a classifier head's forward and backward in one launch.  x [B][F],
+ * w [K][F], b [K] (NULL: none), targets [B] (class indices as floats, clamped
+ * as cross_entropy.wgsl does); writes logits [B][K] = x w^T + b, loss_rows [B],
+ * loss_mean [1], and with g = (softmax(logits) - onehot(target)) * scale
+ * (scale 1/B for the mean loss): dx [B][F] = g w, dw [K][F] = g^T x,
+ * db [K] = sum_rows g.  Any output may be NULL.  Replaces tpk_gemm +
+ * tpk_cross_entropy_mean + tpk_cross_entropy_backward + two tpk_gemm +
+ * tpk_channel_sum of the per-op path (the linear layer of
+ * python/torch/nn/modules.py with the loss of reductionOps.ts:471-531).
+ * K <= 32, F <= 1024; every sum runs in a fixed order (deterministic).  Uses
+ * one device-wide ticket word: calls must not overlap on the GPU. */
+TP_API int tpk_linear_cross_entropy_step(const float* x, const float* w, const float* b, const float* targets,
+                                         float* logits, float* loss_rows, float* loss_mean, float* dx, float* dw,
+                                         float* db, int64_t B, int64_t F, int64_t K, float scale);
 /* grad = (softmax(logits) - onehot(target)) * scale (cross_entropy_backward.wgsl) */
 TP_API int tpk_cross_entropy_backward(const float* logits, const float* targets, float* grad, int64_t B, int64_t C,
                                       float scale);

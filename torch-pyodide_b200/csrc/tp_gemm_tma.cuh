@@ -58,6 +58,10 @@ constexpr int NSPLIT = 256;  // splitter threads (warps 0-7)
 constexpr int MMA_WARP = 8;
 constexpr int TMA_WARP = 9;
 
+__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
 __device__ __forceinline__ void expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc::smem_u32(bar)), "r"(bytes)
                : "memory");
@@ -427,6 +431,13 @@ __global__ void __launch_bounds__(NTHREADS, (Smem<BN, STAGES>::MIN_BLOCKS))
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // the tensor maps are kernel parameters, not data of the predecessor kernel: fetch them
+  // while it drains
+  if (warp == TMA_WARP && lane == 0) {
+    tma::prefetch_map(&ma);
+    tma::prefetch_map(&mb);
+    if (b_lo) tma::prefetch_map(&mbl);
+  }
   const int64_t m0 = (int64_t)blockIdx.x * BM, n0 = (int64_t)blockIdx.y * BN;
   // z = split * batch + b: the batches (filter taps) of one k range run side by side and share L2
   const int batch = (int)(gridDim.z / splits);

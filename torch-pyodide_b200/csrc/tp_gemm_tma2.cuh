@@ -136,6 +136,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // the tensor maps are kernel parameters, not data of the predecessor kernel: fetch them
+  // while it drains
+  if (warp == TMA_WARP && lane == 0) {
+    tma::prefetch_map(&ma);
+    tma::prefetch_map(&mb);
+    if (b_lo) tma::prefetch_map(&mbl);
+  }
   const uint32_t rank = cluster_rank();
   const int64_t m0 = (int64_t)blockIdx.x * BM;  // this CTA's rows
   const int64_t n0p = (int64_t)blockIdx.y * BNP;  // the pair's columns

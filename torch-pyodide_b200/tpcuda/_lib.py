@@ -190,6 +190,7 @@ SIGNATURES: dict[str, list] = {
     "tpk_gemm": [P, INT, P, INT, P, I64, I64, I64, P],
     "tpk_cross_entropy_mean": [P, P, P, P, I64, I64],
     "tpk_cross_entropy_mean_noalloc": [P, P, P, I64, I64],
+    "tpk_linear_cross_entropy_step": [P, P, P, P, P, P, P, P, P, P, I64, I64, I64, F32],
     "tpk_cross_entropy_backward": [P, P, P, I64, I64, F32],
     "tpk_fill": [P, I64, F32],
     "tp_comm_unique_id": [ctypes.c_char_p, INT],

@@ -8,9 +8,10 @@ python/torch/tensor_nn_ops.py:57-72).  Here the step is a fixed sequence of
 fused kernels on preallocated HBM buffers:
 
   forward   per block: conv3x3 (+bias) -> BN (batch stats, running stats) + ReLU
-            -> [2x2 max-pool with indices]; then linear 512->10 and the
-            cross-entropy mean, both left in HBM
-  backward  CE -> linear -> per block: [pool backward] -> BN backward with the
+            -> [2x2 max-pool with indices]; then the classifier head in one
+            launch: linear 512->10, the cross-entropy mean (left in HBM) and
+            the gradients of both (fc weight / bias, the feature gradient)
+  backward  per block: [pool backward] -> BN backward with the
             ReLU mask folded in -> conv bias / weight / data gradients
   update    data-parallel: gradient all-reduce (NCCL, bucketed, issued as soon
             as each block's gradients are final); one fused SGD-momentum launch
@@ -252,7 +253,6 @@ class VGG11BN:
                 b["idx"] = self._alloc(m * 4)
             b["out"] = b["p"] if b["pool"] else b["a"]
         self.logits = self._alloc(Bn * NUM_CLASSES * 4)
-        self.dlogits = self._alloc(Bn * NUM_CLASSES * 4)
         self.loss_rows = self._alloc(Bn * 4)
         self.loss = self._alloc(4)
         self.dfeat = self._alloc(Bn * self.feat * 4)
@@ -336,12 +336,14 @@ class VGG11BN:
                 if b["pool"]:
                     check(L.tpk_maxpool_fwd(_vp(b["a"]), _vp(b["p"]), _vp(b["idx"]), Bn, C, H, W, 2, 2, 0))
             x = b["out"]
-        # the last block ends at 1x1, where both layouts are [B][512]
+        # the last block ends at 1x1, where both layouts are [B][512]; the classifier's
+        # forward and backward (logits, mean cross-entropy, fc gradients, feature
+        # gradient) are one launch
         self.feat_ptr = x
-        check(L.tpk_gemm(_vp(x), 0, _vp(self.p("fc.w")), 1, _vp(self.logits), Bn, NUM_CLASSES, self.feat,
-                         _vp(self.p("fc.b"))))
-        check(L.tpk_cross_entropy_mean(_vp(self.logits), _vp(self.y), _vp(self.loss_rows), _vp(self.loss), Bn,
-                                       NUM_CLASSES))
+        check(L.tpk_linear_cross_entropy_step(_vp(x), _vp(self.p("fc.w")), _vp(self.p("fc.b")), _vp(self.y),
+                                              _vp(self.logits), _vp(self.loss_rows), _vp(self.loss),
+                                              _vp(self.dfeat), _vp(self.g("fc.w")), _vp(self.g("fc.b")), Bn,
+                                              self.feat, NUM_CLASSES, 1.0 / Bn))
 
     def _reduce(self, key: str) -> None:
         if self.comm is not None and key in self.bucket_after:
@@ -351,13 +353,7 @@ class VGG11BN:
     def _backward(self) -> None:
         L = self.lib
         Bn = self.B
-        check(L.tpk_cross_entropy_backward(_vp(self.logits), _vp(self.y), _vp(self.dlogits), Bn, NUM_CLASSES,
-                                           1.0 / Bn))
-        check(L.tpk_gemm(_vp(self.dlogits), 1, _vp(self.feat_ptr), 0, _vp(self.g("fc.w")), NUM_CLASSES, self.feat,
-                         Bn, None))
-        check(L.tpk_channel_sum(_vp(self.dlogits), Bn, NUM_CLASSES, 1, _vp(self.g("fc.b"))))
-        check(L.tpk_gemm(_vp(self.dlogits), 0, _vp(self.p("fc.w")), 0, _vp(self.dfeat), Bn, self.feat, NUM_CLASSES,
-                         None))
+        # the classifier's gradients were written by the forward's head launch
         self._reduce("fc")
         gout = self.dfeat
         if self.overlap:
