@@ -177,6 +177,11 @@ struct EpPixTile {
     if (!at(m, row)) return;
     EpRowMajor{c, ldc, 0, bias, 0}.row16(b, row, n0, Nn, v);
   }
+  __device__ __forceinline__ void row4(int b, int64_t m, int64_t n0, int64_t Nn, float4 v) const {
+    int64_t row;
+    if (!at(m, row)) return;
+    EpRowMajor{c, ldc, 0, bias, 0}.row4(b, row, n0, Nn, v);
+  }
 };
 
 // NCHW output [N][C][HW] of a channels-last GEMM (row m = pixel, linear or

@@ -24,6 +24,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 namespace tp {
 
 constexpr int GB_K = 32;  // k values per producer block
@@ -358,6 +360,35 @@ struct EpRowMajor {
     if (relu) v = fmaxf(v, 0.0f);
     c[b * bs + m * ldc + n] = v;
   }
+  // 4 consecutive columns of row m (columns >= N skipped), one 128-bit store
+  // when whole and 16-byte aligned
+  __device__ __forceinline__ void row4(int b, int64_t m, int64_t n0, int64_t N, float4 v) const {
+    if (n0 >= N) return;
+    float* dst = c + b * bs + m * ldc + n0;
+    if (bias) {
+      const float4 z = n0 + 4 <= N ? make_float4(bias[n0], bias[n0 + 1], bias[n0 + 2], bias[n0 + 3])
+                                   : make_float4(bias[n0], n0 + 1 < N ? bias[n0 + 1] : 0.0f,
+                                                 n0 + 2 < N ? bias[n0 + 2] : 0.0f, n0 + 3 < N ? bias[n0 + 3] : 0.0f);
+      v.x += z.x;
+      v.y += z.y;
+      v.z += z.z;
+      v.w += z.w;
+    }
+    if (relu) {
+      v.x = fmaxf(v.x, 0.0f);
+      v.y = fmaxf(v.y, 0.0f);
+      v.z = fmaxf(v.z, 0.0f);
+      v.w = fmaxf(v.w, 0.0f);
+    }
+    if (n0 + 4 <= N && ((uintptr_t)dst & 15) == 0) {
+      *reinterpret_cast<float4*>(dst) = v;
+      return;
+    }
+    const float o[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (n0 + i < N) dst[i] = o[i];
+  }
   // 16 consecutive columns of row m (columns >= N skipped); 128-bit stores
   // when the row segment is whole and 16-byte aligned
   __device__ __forceinline__ void row16(int b, int64_t m, int64_t n0, int64_t N, const float (&v)[16]) const {
@@ -432,6 +463,9 @@ struct EpWgradTapKhwc {
   __device__ __forceinline__ void row16(int b, int64_t m, int64_t n0, int64_t N, const float (&v)[16]) const {
     EpRowMajor{dw + (m * KHW + b) * Cin, 0, 0, nullptr, 0}.row16(0, 0, n0, N, v);
   }
+  __device__ __forceinline__ void row4(int b, int64_t m, int64_t n0, int64_t N, float4 v) const {
+    EpRowMajor{dw + (m * KHW + b) * Cin, 0, 0, nullptr, 0}.row4(0, 0, n0, N, v);
+  }
 };
 
 // Per-tap weight gradient of TAPS taps at once (Cin = 128 / TAPS): batch b
@@ -451,6 +485,20 @@ struct EpWgradTapsKhwc {
     if (tap >= KHW) return;
     EpRowMajor{dw + (m * KHW + tap) * Cin, 0, 0, nullptr, 0}.row16(0, 0, n0 % Cin, Cin, v);
   }
+  __device__ __forceinline__ void row4(int b, int64_t m, int64_t n0, int64_t, float4 v) const {
+    const int tap = TAPS * b + (int)(n0 / Cin);
+    if (tap >= KHW) return;
+    EpRowMajor{dw + (m * KHW + tap) * Cin, 0, 0, nullptr, 0}.row4(0, 0, n0 % Cin, Cin, v);
+  }
 };
+
+// Epilogues whose row m is one contiguous run of columns provide row4(b, m, n,
+// N, float4); the TMA kernels then stage the accumulator tile in shared memory
+// and store whole rows (each warp instruction a contiguous 256-512 B run)
+// instead of 16 columns per thread (a row per lane: 32 rows per instruction).
+template <class E, class = void>
+struct HasRow4 : std::false_type {};
+template <class E>
+struct HasRow4<E, std::void_t<decltype(&E::row4)>> : std::true_type {};
 
 }  // namespace tp

@@ -367,6 +367,7 @@ struct Smem {
   static_assert(STAGE % 1024 == 0, "stages must keep 1 KB swizzle alignment");
   static_assert(STAGES <= 4 && BN <= 256, "TMEM holds the accumulator (256 columns) and 4 A stages");
   static_assert(A_TMEM0 + 64 * STAGES <= TMEM_COLS && BN <= (int)A_TMEM0, "TMEM regions overlap");
+  static_assert(128u * (BN + 4) * 4 <= TILES, "the staged epilogue tile must fit in the operand ring");
 };
 
 __device__ __forceinline__ void mma_tf32_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc,
@@ -411,6 +412,57 @@ __device__ __forceinline__ void read_a16(const uint8_t* tile, int r, int k0, flo
     for (int i = 0; i < 16; ++i) {
       const int k = k0 + i;
       v[i] = *reinterpret_cast<const float*>(grp + k * 128 + ((((rr >> 3) ^ (k & 3)) << 5) | ((rr & 7) << 2)));
+    }
+  }
+}
+
+// Epilogue through shared memory for warp (quadrant q, column half h) of a
+// 128 x BN accumulator at TMEM column 0: tcgen05.ld 16 columns at a time into
+// the warp's 32 staged rows (pitch BN + 4 floats: the float4 stores of 8 lanes
+// hit distinct banks), then each pass stores RPI whole row segments of HALF
+// columns with float4 per lane -- split-K partials into ws[b][split], else
+// through ep.row4.  Only this warp's rows and columns are touched, so a
+// __syncwarp orders the two phases.
+template <int BN, class EP>
+__device__ __forceinline__ void staged_rows(float* stage, int q, int h, int lane, uint32_t tmem, bool have,
+                                            int64_t m0, int64_t n0, int64_t M, int64_t N, int b, int split,
+                                            int splits, float* __restrict__ ws, const EP& ep) {
+  constexpr int HALF = BN / 2, PITCH = BN + 4, LPR = HALF / 4, RPI = 32 / LPR;
+  static_assert(HALF % 16 == 0 && 32 % LPR == 0, "column half must be 16..128 columns");
+  float* st = stage + (size_t)(q * 32) * PITCH;
+#pragma unroll 1
+  for (int c0 = h * HALF; c0 < (h + 1) * HALF; c0 += 16) {
+    float v[16];
+    if (have) {
+      tc::tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = 0.0f;
+    }
+    float4* d = reinterpret_cast<float4*>(st + lane * PITCH + c0);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) d[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  }
+  __syncwarp();
+  const int cl = h * HALF + (lane % LPR) * 4;
+  if (n0 + cl >= N) return;
+#pragma unroll 4
+  for (int rr = lane / LPR; rr < 32; rr += RPI) {
+    const int64_t mm = m0 + q * 32 + rr;
+    if (mm >= M) break;
+    const float4 v4 = *reinterpret_cast<const float4*>(st + rr * PITCH + cl);
+    if (splits > 1) {
+      float* w = ws + (((int64_t)b * splits + split) * M + mm) * N + n0 + cl;
+      if (n0 + cl + 4 <= N && ((uintptr_t)w & 15) == 0) {
+        *reinterpret_cast<float4*>(w) = v4;
+      } else {
+        const float o[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (n0 + cl + i < N) w[i] = o[i];
+      }
+    } else if constexpr (HasRow4<EP>::value) {
+      ep.row4(b, mm, n0 + cl, N, v4);
     }
   }
 }
@@ -577,6 +629,13 @@ __global__ void __launch_bounds__(NTHREADS, (Smem<BN, STAGES>::MIN_BLOCKS))
     const int q = warp & 3, h = warp >> 2;
     const int64_t m = m0 + q * 32 + lane;
     constexpr int HALF = BN / 2;
+    if (HasRow4<EP>::value || splits > 1) {
+      // through shared memory (the operand ring is idle once `done` completed): the
+      // warp stages its 32 rows x HALF columns, then stores them a row at a time
+      if (have || nk == 0)
+        staged_rows<BN>(reinterpret_cast<float*>(smem), q, h, lane, tmem, have, m0, n0, M, N, b, split, splits, ws,
+                        ep);
+    } else {
 #pragma unroll 1
     for (int c0 = h * HALF; c0 < (h + 1) * HALF; c0 += 16) {
       float v[16];
@@ -596,6 +655,7 @@ __global__ void __launch_bounds__(NTHREADS, (Smem<BN, STAGES>::MIN_BLOCKS))
           ep.row16(b, m, n0 + c0, N, v);
         }
       }
+    }
     }
   }
   tc::tc_fence_before();

@@ -281,6 +281,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
     const int q = warp & 3, h = warp >> 2;
     const int64_t m = m0 + q * 32 + lane;
     constexpr int HALF = BNP / 2;
+    static_assert(128u * (BNP + 4) * 4 <= S::TILES, "the staged epilogue tile must fit in the operand ring");
+    if (HasRow4<EP>::value || splits > 1) {
+      if (have || nk == 0)
+        tma::staged_rows<BNP>(reinterpret_cast<float*>(smem), q, h, lane, tmem, have, m0, n0p, M, N, b, split,
+                              splits, ws, ep);
+    } else {
 #pragma unroll 1
     for (int c0 = h * HALF; c0 < (h + 1) * HALF; c0 += 16) {
       float v[16];
@@ -300,6 +306,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
           ep.row16(b, m, n0p + c0, N, v);
         }
       }
+    }
     }
   }
   tc::tc_fence_before();
