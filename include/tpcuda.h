@@ -290,6 +290,12 @@ TP_API int tp_gemm_status(int* out, int reset);
  * (default 64; 0 = no cap); such reductions are cut into more splits (at most
  * 2048) whose partials are added in fp32 on CUDA cores. */
 TP_API int tp_set_gemm_kmax(int kblocks);
+/* Tuning switch of the single-CTA TMA GEMM's 128-column tiles: 0 = 4-stage
+ * operand ring, one CTA per SM; 1 (default) = a 2-stage ring with two CTAs per
+ * SM (one's prologue and epilogue under the other's main loop) when the GEMM
+ * has more CTAs (tiles x split-K splits) than SMs; 2 = always two CTAs per SM.
+ * Same bits either way. */
+TP_API int tp_set_gemm_twocta(int mode);
 /* New, for testing the path above: one CTA waits on an mbarrier nothing
  * arrives on, with the tensor-core kernels' own bounded-wait function and a
  * limit of limit_ns (1e3 .. 2e9); the wait runs out, records code 99 in the

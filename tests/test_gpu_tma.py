@@ -285,3 +285,35 @@ def test_sgd_group_writes_low_parts(cuda_rt):
         p = c["p"][i]
         hi = (p.view(np.uint32) & np.uint32(0xFFFFE000)).view(np.float32)
         assert np.array_equal(c["lo"][i], p - hi)
+
+
+@pytest.mark.parametrize("cin,cout,hw,batch", [(64, 128, 16, 16), (128, 256, 8, 16), (128, 128, 12, 8)])
+def test_conv_nhwc_two_ctas_per_sm_bitwise(cuda_rt, cin, cout, hw, batch):
+    """128-column tiles on the 2-stage ring, two CTAs per SM (tp_set_gemm_twocta 2),
+    against the 4-stage, one-per-SM kernel (0): the same split and MMA sequence,
+    so the same bits for the forward, data and weight gradients."""
+    rt = cuda_rt
+    rng = np.random.default_rng(cin + cout + hw)
+    x = rng.standard_normal((batch, hw, hw, cin)).astype(np.float32)
+    w = (rng.standard_normal((cout, 3, 3, cin)) * 0.05).astype(np.float32)
+    b = rng.standard_normal(cout).astype(np.float32)
+    dy = rng.standard_normal((batch, hw, hw, cout)).astype(np.float32)
+    px, pw, pb, pdy = dev(rt, x), dev(rt, w), dev(rt, b), dev(rt, dy)
+    vp = ctypes.c_void_p
+    L = rt.lib
+    outs = {}
+    try:
+        for mode in (0, 2):
+            assert L.tp_set_gemm_twocta(mode) == 0
+            y, dx, dw = empty(rt, x.size // cin * cout), empty(rt, x.size), empty(rt, w.size)
+            assert L.tpk_conv2d_fwd_nhwc(vp(px), vp(pw), vp(pb), vp(y), batch, cin, hw, hw, cout, 3, 3, 1, 1, 1) == 0
+            assert L.tpk_conv2d_dgrad_nhwc(vp(pdy), vp(pw), vp(dx), batch, cin, hw, hw, cout, 3, 3, 1, 1, 1) == 0
+            assert L.tpk_conv2d_wgrad_nhwc(vp(pdy), vp(px), vp(dw), batch, cin, hw, hw, cout, 3, 3, 1, 1, 1) == 0
+            assert status(rt) == 0
+            outs[mode] = [read(rt, y, (x.size // cin * cout,)), read(rt, dx, (x.size,)), read(rt, dw, (w.size,))]
+            free(rt, y, dx, dw)
+    finally:
+        assert L.tp_set_gemm_twocta(1) == 0
+        free(rt, px, pw, pb, pdy)
+    for a, c in zip(outs[0], outs[2]):
+        assert np.array_equal(a, c)

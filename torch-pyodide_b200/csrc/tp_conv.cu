@@ -22,6 +22,8 @@ namespace tp {
 // as 0 without CTA pairs, 4 as 0 with CTA pairs wherever they fit.
 static int g_gemm_path = 0;
 int gemm_path() { return g_gemm_path; }
+static int g_gemm_twocta = 1;
+int gemm_twocta() { return g_gemm_twocta; }
 
 // Most k-blocks (32 k each) one split of a tensor-core GEMM accumulates in
 // TMEM once K exceeds 4x that (0: no cap).  Over thousands of MMAs into one
@@ -234,6 +236,13 @@ TP_API int tp_set_gemm_path(int path) {
                "gemm path must be 0 (tensor cores, TMA-fed where possible, CTA pairs for large N), 1 (CUDA cores), "
                "2 (tensor cores without TMA), 3 (as 0 on single CTAs) or 4 (as 0 with CTA pairs wherever they fit)");
     g_gemm_path = path;
+  });
+}
+
+TP_API int tp_set_gemm_twocta(int mode) {
+  return guard([&] {
+    TP_REQUIRE(mode >= 0 && mode <= 2, "tp_set_gemm_twocta: 0 (never), 1 (more CTAs than SMs) or 2 (always)");
+    g_gemm_twocta = mode;
   });
 }
 

@@ -20,6 +20,10 @@
 namespace tp {
 
 int gemm_path();
+// 128-wide single-CTA tiles: 0 = 4 stages, one CTA per SM; 1 = 2 stages, two
+// CTAs per SM when there are more CTAs than SMs; 2 = two per SM always
+// (tp_set_gemm_twocta)
+int gemm_twocta();
 // paths 0 and 3 use the TMA kernels
 inline bool tma_enabled() { return gemm_path() == 0 || gemm_path() == 3 || gemm_path() == 4; }
 
@@ -66,6 +70,24 @@ inline uint32_t tma_b_rows(int64_t M, int64_t N, int64_t K, int batch) {
   return tma_pair(M, N, K, batch) ? tma_bnp(N) / 2 : tma_bn(N);
 }
 
+// Single-CTA TMA kernel with 128-column tiles: when there are more CTAs (tiles x
+// split-K splits, the split gemm_tma_launch computes) than SMs, two per SM on a
+// 2-stage ring, each one's prologue and epilogue under the other's main loop; a
+// single wave keeps the deeper 4-stage ring (measured on the VGG convolutions:
+// 64 -> 128 channels at batch 1024, 2048 CTAs, 220 -> 178 us with two per SM;
+// 512 -> 512 at 2x2, 128 CTAs, 97 -> 122 us).
+template <class SA, class SB, class EP>
+void gemm_tma_128(const CUtensorMap& ma, const CUtensorMap& mb, const SA& sa, const SB& sb, const EP& ep, int64_t M,
+                  int64_t N, int64_t K, int batch, const CUtensorMap* mbl = nullptr) {
+  const int two = gemm_twocta();
+  const int64_t tiles = ((M + tc::BM - 1) / tc::BM) * ((N + 127) / 128) * batch;
+  const int64_t ctas = tiles * gemm_splits(tiles, K, sm_count(), M * N * batch);
+  if (two == 2 || (two == 1 && ctas > sm_count()))
+    gemm_tma_launch<SA, SB, EP, 128, 2>(ma, mb, sa, sb, ep, M, N, K, batch, mbl);
+  else
+    gemm_tma_launch<SA, SB, EP, 128, 4>(ma, mb, sa, sb, ep, M, N, K, batch, mbl);
+}
+
 // TMA kernel with the N tile following N; the maps' B box must be tma_b_rows(M, N, K, batch).
 template <class SA, class SB, class EP>
 void gemm_tma_bn(const CUtensorMap& ma, const CUtensorMap& mb, const SA& sa, const SB& sb, const EP& ep, int64_t M,
@@ -77,9 +99,13 @@ void gemm_tma_bn(const CUtensorMap& ma, const CUtensorMap& mb, const SA& sa, con
     return;
   }
   // N <= 64: 3-stage tiles, two CTAs per SM (one's epilogue under the other's main loop)
-  if (N <= 32) gemm_tma_launch<SA, SB, EP, 32, 3>(ma, mb, sa, sb, ep, M, N, K, batch, mbl);
-  else if (N <= 64) gemm_tma_launch<SA, SB, EP, 64, 3>(ma, mb, sa, sb, ep, M, N, K, batch, mbl);
-  else gemm_tma_launch<SA, SB, EP, 128, 4>(ma, mb, sa, sb, ep, M, N, K, batch, mbl);
+  if (N <= 32) {
+    gemm_tma_launch<SA, SB, EP, 32, 3>(ma, mb, sa, sb, ep, M, N, K, batch, mbl);
+  } else if (N <= 64) {
+    gemm_tma_launch<SA, SB, EP, 64, 3>(ma, mb, sa, sb, ep, M, N, K, batch, mbl);
+  } else {
+    gemm_tma_128(ma, mb, sa, sb, ep, M, N, K, batch, mbl);
+  }
 }
 
 // A dense operand: element (r, k) of batch b at p[b*bs + r*ld + k] (K-major)

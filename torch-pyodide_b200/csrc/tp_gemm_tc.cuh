@@ -454,15 +454,16 @@ inline int gemm_splits(int64_t tiles, int64_t K, int sms, int64_t out_elems) {
   // Accuracy floor for long reductions (weight gradients over many pixels): the
   // tensor core's fp32 accumulation drifts over thousands of MMAs into one
   // accumulator, so no split of such a GEMM accumulates more than kmax k-blocks.
-  // Forward / data-gradient K (<= 4 kmax k-blocks) keeps the cost-model split.
+  // Forward / data-gradient K (<= 4 kmax k-blocks) keeps the cost-model split;
+  // longer reductions take at least ceil(nk / kmax) splits, more where the
+  // cost model wants more CTAs than that (few output tiles).
   const int kmax = gemm_kmax();
-  if (kmax > 0 && nk > 4 * (int64_t)kmax) {
-    const int64_t need = (nk + kmax - 1) / kmax;
-    return (int)(need < 2048 ? need : 2048);
-  }
+  int64_t need = 1;
+  if (kmax > 0 && nk > 4 * (int64_t)kmax) need = (nk + kmax - 1) / kmax;
+  if (need > 2048) need = 2048;
   int64_t maxs = nk / 8;
   if (maxs > 64) maxs = 64;
-  if (maxs <= 1) return 1;
+  if (maxs <= 1) return (int)need;
   int best = 1;
   double best_t = 1e300;
   for (int s = 1; s <= maxs; ++s) {
@@ -473,7 +474,7 @@ inline int gemm_splits(int64_t tiles, int64_t K, int sms, int64_t out_elems) {
       best = s;
     }
   }
-  return best;
+  return best > need ? best : (int)need;
 }
 
 template <class LA, class LB, class EP, int BN, int STAGES>

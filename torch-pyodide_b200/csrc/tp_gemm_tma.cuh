@@ -351,18 +351,20 @@ struct SrcFilterMN {
 // (hi: +0..31, lo: +32..63).  Tiles of N <= 64 with 3 stages run two CTAs per
 // SM (97 KB of shared memory and 256 TMEM columns each: the accumulator at
 // [0, 64), A stages at 64, 128, 192), so one CTA's epilogue and prologue overlap
-// the other's main loop; otherwise a CTA holds the SM (120 KB floor, all 512
-// columns: the accumulator in [0, 256), 4 A stages from 256).
+// the other's main loop; so do 128-wide tiles with 2 stages (97 KB, the
+// accumulator at [0, 128), A stages at 128 and 192); otherwise a CTA holds the
+// SM (120 KB floor, all 512 columns: the accumulator in [0, 256), 4 A stages
+// from 256).
 template <int BN, int STAGES>
 struct Smem {
-  static constexpr bool TWO = STAGES <= 3 && BN <= 64;
+  static constexpr bool TWO = (STAGES <= 3 && BN <= 64) || (STAGES == 2 && BN == 128);
   static constexpr uint32_t A_BYTES = BM * BK * 4;  // raw A (TMA); its hi/lo go to TMEM
   static constexpr uint32_t B_BYTES = BN * BK * 4;
   static constexpr uint32_t STAGE = A_BYTES + 2 * B_BYTES;  // raw A | B raw -> hi | B lo
   static constexpr uint32_t TILES = STAGES * STAGE;
   static constexpr uint32_t BYTES = TWO || TILES + 1280 > 122880u ? TILES + 1280 : 122880u;
   static constexpr uint32_t TMEM_COLS = TWO ? 256 : 512;
-  static constexpr uint32_t A_TMEM0 = TWO ? 64 : 256;
+  static constexpr uint32_t A_TMEM0 = TWO ? (BN > 64 ? BN : 64) : 256;
   static constexpr int MIN_BLOCKS = TWO ? 2 : 1;
   static_assert(STAGE % 1024 == 0, "stages must keep 1 KB swizzle alignment");
   static_assert(STAGES <= 4 && BN <= 256, "TMEM holds the accumulator (256 columns) and 4 A stages");
