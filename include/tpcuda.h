@@ -94,6 +94,13 @@ TP_API int tp_aux_return(void);
 TP_API int tp_aux_record(int slot);
 TP_API int tp_main_wait(int slot);
 TP_API int tp_aux_join(void);
+/* New: tp_comm_fork makes the communicator's stream wait for the library
+ * stream's work so far and sends the calling thread's launches there (behind
+ * the all-reduces already issued) until tp_comm_return; tp_comm_wait then also
+ * joins them.  Requires a communicator (tp_comm_init).  Used to run a
+ * bucket's optimizer step right after its gradient all-reduce. */
+TP_API int tp_comm_fork(void);
+TP_API int tp_comm_return(void);
 /* runtime.ts:1084-1090 memoryAllocated / memoryReserved */
 TP_API int tp_memory_allocated(int64_t* out);
 TP_API int tp_memory_reserved(int64_t* out);

@@ -39,6 +39,11 @@ struct NcclApi {
 static NcclApi g_nccl;
 static ncclComm_t g_comm = nullptr;
 static cudaStream_t g_comm_stream = nullptr;
+
+cudaStream_t comm_stream() {
+  TP_REQUIRE(g_comm_stream != nullptr, "no communicator: its stream does not exist");
+  return g_comm_stream;
+}
 static std::vector<cudaEvent_t> g_events;
 static size_t g_next_event = 0;
 static bool g_pending = false;

@@ -21,14 +21,16 @@ static cudaStream_t g_stream = nullptr;
 // weight gradient beside its data gradient); launches go to g_aux between
 // tp_aux_fork and tp_aux_return on the calling thread.
 static cudaStream_t g_aux = nullptr;
+// 0: library stream, 1: auxiliary stream, 2: the communicator's stream (between
+// tp_comm_fork and tp_comm_return: work that must follow a gradient all-reduce)
 static thread_local int g_cur = 0;
 static int g_sms = 148;
 static std::unordered_map<int64_t, Tensor> g_tensors;
 static int64_t g_next_id = 1;
 static int64_t g_allocated = 0;
 // scratch areas per stream (index g_cur), so overlapping work never shares one
-static void* g_scratch[2] = {nullptr, nullptr};
-static size_t g_scratch_bytes[2] = {0, 0};
+static void* g_scratch[3] = {nullptr, nullptr, nullptr};
+static size_t g_scratch_bytes[3] = {0, 0, 0};
 std::atomic<int64_t> g_launches{0};
 static int pdl_default() {
   const char* e = getenv("TP_PDL");
@@ -76,7 +78,7 @@ static cudaStream_t aux_stream() {
 
 cudaStream_t stream() {
   ensure_init();
-  return g_cur ? aux_stream() : g_stream;
+  return g_cur == 0 ? g_stream : (g_cur == 1 ? aux_stream() : comm_stream());
 }
 int device() {
   ensure_init();
@@ -115,18 +117,18 @@ static void* grow(void** slot, size_t* have, size_t bytes) {
 
 void* scratch(size_t bytes) { return grow(&g_scratch[g_cur], &g_scratch_bytes[g_cur], bytes); }
 
-static void* g_scratch2[2] = {nullptr, nullptr};
-static size_t g_scratch2_bytes[2] = {0, 0};
+static void* g_scratch2[3] = {nullptr, nullptr, nullptr};
+static size_t g_scratch2_bytes[3] = {0, 0, 0};
 
 void* scratch2(size_t bytes) { return grow(&g_scratch2[g_cur], &g_scratch2_bytes[g_cur], bytes); }
 
-static void* g_scratch3[2] = {nullptr, nullptr};
-static size_t g_scratch3_bytes[2] = {0, 0};
+static void* g_scratch3[3] = {nullptr, nullptr, nullptr};
+static size_t g_scratch3_bytes[3] = {0, 0, 0};
 
 void* scratch3(size_t bytes) { return grow(&g_scratch3[g_cur], &g_scratch3_bytes[g_cur], bytes); }
 
 // ---- the auxiliary stream ----------------------------------------------------------------
-static cudaEvent_t g_fork_ev = nullptr, g_join_ev = nullptr;
+static cudaEvent_t g_fork_ev = nullptr, g_join_ev = nullptr, g_cfork_ev = nullptr;
 static cudaEvent_t g_slot_ev[64];
 static bool g_slot_made[64];
 
@@ -134,6 +136,16 @@ static cudaEvent_t make_event(cudaEvent_t* e) {
   if (!*e) TP_CUDA(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
   return *e;
 }
+
+void comm_fork() {
+  TP_REQUIRE(g_cur == 0, "tp_comm_fork: not on the library stream");
+  cudaStream_t c = comm_stream();
+  TP_CUDA(cudaEventRecord(make_event(&g_cfork_ev), g_stream));
+  TP_CUDA(cudaStreamWaitEvent(c, g_cfork_ev, 0));
+  g_cur = 2;
+}
+
+void comm_return() { g_cur = 0; }
 
 void aux_fork() {
   TP_REQUIRE(g_cur == 0, "tp_aux_fork: already on the auxiliary stream");
@@ -314,6 +326,8 @@ TP_API int tp_aux_return(void) { return guard([&] { aux_return(); }); }
 TP_API int tp_aux_record(int slot) { return guard([&] { aux_record(slot); }); }
 TP_API int tp_main_wait(int slot) { return guard([&] { main_wait(slot); }); }
 TP_API int tp_aux_join(void) { return guard([&] { aux_join(); }); }
+TP_API int tp_comm_fork(void) { return guard([&] { comm_fork(); }); }
+TP_API int tp_comm_return(void) { return guard([&] { comm_return(); }); }
 
 TP_API int tp_get_stream(void** out) { return guard([&] { *out = (void*)stream(); }); }
 

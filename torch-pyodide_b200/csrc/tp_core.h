@@ -117,6 +117,8 @@ inline unsigned grid_for(int64_t n, int threads, int per_thread = 1) {
 // Scratch space reused across launches on the library stream (stream order
 // makes reuse safe).  Grows on demand; never shrinks.
 void* scratch(size_t bytes);
+// The communicator's stream (tp_comm.cu); fails when no communicator exists.
+cudaStream_t comm_stream();
 // A second, independent scratch area (repacked filters), same rules.
 void* scratch2(size_t bytes);
 // A third one (the tf32 low parts of a GEMM operand), same rules.

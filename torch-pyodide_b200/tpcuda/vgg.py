@@ -14,8 +14,12 @@ fused kernels on preallocated HBM buffers:
   backward  per block: [pool backward] -> BN backward with the
             ReLU mask folded in -> conv bias / weight / data gradients
   update    data-parallel: gradient all-reduce (NCCL, bucketed, issued as soon
-            as each block's gradients are final); one fused SGD-momentum launch
-            over all parameters with the 1/world averaging folded in
+            as each block's gradients are final); fused SGD-momentum with the
+            1/world averaging folded in: data-parallel channels-last steps update
+            each bucket as soon as its all-reduce is done and its block's data
+            gradient (the last reader of its filters) has run, beside the rest of
+            the backward; one GPU (and the NCHW cross-check) updates everything
+            in one launch at the end
 
 Activations are channels-last ([N][H][W][C], layout="nhwc", the default):
 each implicit-GEMM tile of the convolutions is then one TMA box, and the
@@ -182,7 +186,7 @@ class VGG11BN:
 
     def __init__(self, rt, batch: int, seed: int = 0, lr: float = 0.05, momentum: float = 0.9,
                  weight_decay: float = 5e-4, world: int = 1, comm=None, bucket_bytes: int = 8 << 20,
-                 layout: str = "nhwc", keep_acts: bool = False):
+                 layout: str = "nhwc", keep_acts: bool = False, early_update: bool = True):
         if layout not in ("nhwc", "nchw"):
             raise ValueError(f"layout must be 'nhwc' or 'nchw', got {layout!r}")
         self.layout = layout
@@ -280,6 +284,23 @@ class VGG11BN:
 
         # gradient buckets (contiguous ranges of the flat gradient buffer)
         self._plan_buckets()
+        # data-parallel channels-last steps update each bucket's parameters right after
+        # its all-reduce, once nothing later in the step reads them: one SGD group per
+        # bucket, on the communicator's stream (2 GPUs: 2.73 -> 2.70 ms per step).  One
+        # GPU keeps a single update at the end: on the auxiliary stream the per-bucket
+        # updates delayed the weight gradients (batch 128: 0.94 -> 1.06 ms)
+        self.bucket_groups = {}
+        if self.overlap and early_update and comm is not None:
+            for start, count, key in self.buckets:
+                idx = [i for i, n in enumerate(names) if start <= self.offsets[n][0] < start + count]
+                pp = (ctypes.c_void_p * len(idx))(*[self.params + 4 * self.offsets[names[i]][0] for i in idx])
+                gg = (ctypes.c_void_p * len(idx))(*[self.grads + 4 * self.offsets[names[i]][0] for i in idx])
+                mm = (ctypes.c_void_p * len(idx))(*[self.moms + 4 * self.offsets[names[i]][0] for i in idx])
+                ll = (ctypes.c_void_p * len(idx))(*[lo_rows[i] for i in idx]) if lo_rows is not None else None
+                nn = (ctypes.c_int64 * len(idx))(*[self.offsets[names[i]][1] for i in idx])
+                gb = ctypes.c_int64(0)
+                check(self.lib.tpk_group_create_lo(len(idx), pp, gg, mm, None, ll, nn, ctypes.byref(gb)))
+                self.bucket_groups[key] = gb.value
 
     # ---- helpers --------------------------------------------------------------------
     def _alloc(self, nbytes: int) -> int:
@@ -345,6 +366,20 @@ class VGG11BN:
                                               _vp(self.dfeat), _vp(self.g("fc.w")), _vp(self.g("fc.b")), Bn,
                                               self.feat, NUM_CLASSES, 1.0 / Bn))
 
+    def _update_bucket(self, key: str) -> None:
+        """SGD on the bucket that closes at `key`, once its gradients are all-reduced
+        and nothing later in the step reads its parameters: on the communicator's
+        stream behind the bucket's all-reduce (the library stream joins it before
+        the step ends)."""
+        if key not in self.bucket_groups:
+            return
+        L = self.lib
+        check(L.tp_comm_fork())
+        try:
+            check(L.tpk_sgd_group(self.bucket_groups[key], self.lr, self.momentum, self.wd, 0.0, 0, 1.0 / self.world))
+        finally:
+            check(L.tp_comm_return())
+
     def _reduce(self, key: str) -> None:
         if self.comm is not None and key in self.bucket_after:
             start, count, _ = self.bucket_after[key]
@@ -357,6 +392,7 @@ class VGG11BN:
         self._reduce("fc")
         gout = self.dfeat
         if self.overlap:
+            self._update_bucket("fc")  # nothing after the head reads fc.w / fc.b
             self._backward_blocks_overlapped(gout)
             return
         buf = 0
@@ -434,12 +470,15 @@ class VGG11BN:
                 check(L.tpk_conv2d_dgrad_nhwc_lo(_vp(dz), w, self.p_lo(f"conv{li}.w"), _vp(dx), Bn, cin, H, W, C,
                                                  3, 3, 1, 1, self.filter_layout(li)))
                 gout = dx
+            # the data gradient was the last reader of this block's filters
+            self._update_bucket(f"blk{li}")
         check(L.tp_aux_join())
 
     def _update(self) -> None:
         if self.comm is not None:
             self.comm.wait()
-        check(self.lib.tpk_sgd_group(self.group, self.lr, self.momentum, self.wd, 0.0, 0, 1.0 / self.world))
+        if not self.bucket_groups:  # channels-last steps updated every bucket during the backward
+            check(self.lib.tpk_sgd_group(self.group, self.lr, self.momentum, self.wd, 0.0, 0, 1.0 / self.world))
 
     def step_eager(self) -> None:
         self._forward()
@@ -511,6 +550,9 @@ class VGG11BN:
             self.lib.tp_graph_destroy(self.graph)
             self.graph = None
         self.lib.tpk_group_destroy(self.group)
+        for g in self.bucket_groups.values():
+            self.lib.tpk_group_destroy(g)
+        self.bucket_groups = {}
         for p in self._allocs:
             self.lib.tp_free(_vp(p))
         self._allocs = []
