@@ -94,13 +94,17 @@ TP_API int tp_aux_return(void);
 TP_API int tp_aux_record(int slot);
 TP_API int tp_main_wait(int slot);
 TP_API int tp_aux_join(void);
-/* New: tp_comm_fork makes the communicator's stream wait for the library
- * stream's work so far and sends the calling thread's launches there (behind
- * the all-reduces already issued) until tp_comm_return; tp_comm_wait then also
- * joins them.  Requires a communicator (tp_comm_init).  Used to run a
- * bucket's optimizer step right after its gradient all-reduce. */
-TP_API int tp_comm_fork(void);
-TP_API int tp_comm_return(void);
+/* New: a third stream for work that may run beside the rest of a step.  It is
+ * the communicator's stream when one exists (so its work also follows the
+ * all-reduces issued so far), else a library stream of its own.
+ * tp_side_fork makes it wait for everything queued on the library and
+ * auxiliary streams and sends the calling thread's launches there until
+ * tp_side_return; tp_side_join (and, with a communicator, tp_comm_wait) makes
+ * the library stream wait for it.  Used to run each gradient bucket's
+ * optimizer step as soon as its gradients are final. */
+TP_API int tp_side_fork(void);
+TP_API int tp_side_return(void);
+TP_API int tp_side_join(void);
 /* runtime.ts:1084-1090 memoryAllocated / memoryReserved */
 TP_API int tp_memory_allocated(int64_t* out);
 TP_API int tp_memory_reserved(int64_t* out);

@@ -179,3 +179,35 @@ def test_vgg_step_same_with_and_without_dependent_launch(cuda_rt, batch):
     assert res[0][0] == res[1][0]
     for n in res[0][1]:
         assert np.array_equal(res[0][1][n], res[1][1][n]), n
+
+
+@pytest.mark.parametrize("batch", [8, 128])
+def test_vgg_per_bucket_update_same_as_one_update(cuda_rt, batch):
+    """Updating each gradient bucket on the side stream as soon as its gradients
+    are final (the data-parallel schedule, forced here on one GPU) gives the
+    same bits as one SGD launch over every parameter at the end of the step:
+    the side stream's waits order every update after its gradients' writers
+    and its filters' last reader."""
+    from tpcuda.vgg import VGG11BN
+    rng = np.random.default_rng(batch + 1)
+    x = rng.standard_normal((batch, 3, 32, 32)).astype(np.float32)
+    y = rng.integers(0, 10, batch).astype(np.float32)
+    res = []
+    for early in (True, False):
+        m = VGG11BN(cuda_rt, batch, seed=5, early_update=early, bucket_bytes=1 << 20)
+        assert bool(m.bucket_groups) == early
+        m._h2d(m.x, x)
+        m._h2d(m.y, y)
+        losses = []
+        m.step_eager()
+        losses.append(m.read_loss())
+        m.capture()
+        for _ in range(3):
+            m.step()
+            losses.append(m.read_loss())
+        cuda_rt.synchronize()
+        res.append((losses, {n: m.param_array(n) for n, _, _ in m.param_specs}))
+        m.close()
+    assert res[0][0] == res[1][0]
+    for n in res[0][1]:
+        assert np.array_equal(res[0][1][n], res[1][1][n]), n

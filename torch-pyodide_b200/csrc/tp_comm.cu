@@ -44,6 +44,7 @@ cudaStream_t comm_stream() {
   TP_REQUIRE(g_comm_stream != nullptr, "no communicator: its stream does not exist");
   return g_comm_stream;
 }
+bool comm_active() { return g_comm_stream != nullptr; }
 static std::vector<cudaEvent_t> g_events;
 static size_t g_next_event = 0;
 static bool g_pending = false;

@@ -21,9 +21,11 @@ static cudaStream_t g_stream = nullptr;
 // weight gradient beside its data gradient); launches go to g_aux between
 // tp_aux_fork and tp_aux_return on the calling thread.
 static cudaStream_t g_aux = nullptr;
-// 0: library stream, 1: auxiliary stream, 2: the communicator's stream (between
-// tp_comm_fork and tp_comm_return: work that must follow a gradient all-reduce)
+// 0: library stream, 1: auxiliary stream, 2: the side stream (between
+// tp_side_fork and tp_side_return): the communicator's stream when one exists
+// (work that must follow a gradient all-reduce), else a library stream of its own
 static thread_local int g_cur = 0;
+static cudaStream_t g_side = nullptr;
 static int g_sms = 148;
 static std::unordered_map<int64_t, Tensor> g_tensors;
 static int64_t g_next_id = 1;
@@ -76,9 +78,16 @@ static cudaStream_t aux_stream() {
   return g_aux;
 }
 
+static cudaStream_t side_stream() {
+  ensure_init();
+  if (comm_active()) return comm_stream();
+  if (!g_side) TP_CUDA(cudaStreamCreateWithFlags(&g_side, cudaStreamNonBlocking));
+  return g_side;
+}
+
 cudaStream_t stream() {
   ensure_init();
-  return g_cur == 0 ? g_stream : (g_cur == 1 ? aux_stream() : comm_stream());
+  return g_cur == 0 ? g_stream : (g_cur == 1 ? aux_stream() : side_stream());
 }
 int device() {
   ensure_init();
@@ -128,7 +137,9 @@ static size_t g_scratch3_bytes[3] = {0, 0, 0};
 void* scratch3(size_t bytes) { return grow(&g_scratch3[g_cur], &g_scratch3_bytes[g_cur], bytes); }
 
 // ---- the auxiliary stream ----------------------------------------------------------------
-static cudaEvent_t g_fork_ev = nullptr, g_join_ev = nullptr, g_cfork_ev = nullptr;
+static cudaEvent_t g_fork_ev = nullptr, g_join_ev = nullptr, g_sfork_ev = nullptr, g_sfork_aux_ev = nullptr,
+                   g_sjoin_ev = nullptr;
+static bool g_aux_live = false;
 static cudaEvent_t g_slot_ev[64];
 static bool g_slot_made[64];
 
@@ -137,21 +148,35 @@ static cudaEvent_t make_event(cudaEvent_t* e) {
   return *e;
 }
 
-void comm_fork() {
-  TP_REQUIRE(g_cur == 0, "tp_comm_fork: not on the library stream");
-  cudaStream_t c = comm_stream();
-  TP_CUDA(cudaEventRecord(make_event(&g_cfork_ev), g_stream));
-  TP_CUDA(cudaStreamWaitEvent(c, g_cfork_ev, 0));
+// The side stream waits for everything queued so far on the library and
+// auxiliary streams, then takes the calling thread's launches.
+void side_fork() {
+  TP_REQUIRE(g_cur == 0, "tp_side_fork: not on the library stream");
+  cudaStream_t c = side_stream();
+  TP_CUDA(cudaEventRecord(make_event(&g_sfork_ev), g_stream));
+  TP_CUDA(cudaStreamWaitEvent(c, g_sfork_ev, 0));
+  if (g_aux_live) {  // the auxiliary stream was forked and not yet joined
+    TP_CUDA(cudaEventRecord(make_event(&g_sfork_aux_ev), g_aux));
+    TP_CUDA(cudaStreamWaitEvent(c, g_sfork_aux_ev, 0));
+  }
   g_cur = 2;
 }
 
-void comm_return() { g_cur = 0; }
+void side_return() { g_cur = 0; }
+
+void side_join() {
+  ensure_init();
+  if (!comm_active() && !g_side) return;
+  TP_CUDA(cudaEventRecord(make_event(&g_sjoin_ev), side_stream()));
+  TP_CUDA(cudaStreamWaitEvent(g_stream, g_sjoin_ev, 0));
+}
 
 void aux_fork() {
   TP_REQUIRE(g_cur == 0, "tp_aux_fork: already on the auxiliary stream");
   cudaStream_t a = aux_stream();
   TP_CUDA(cudaEventRecord(make_event(&g_fork_ev), g_stream));
   TP_CUDA(cudaStreamWaitEvent(a, g_fork_ev, 0));
+  g_aux_live = true;
   g_cur = 1;
 }
 
@@ -177,6 +202,7 @@ void aux_join() {
   if (!g_aux) return;
   TP_CUDA(cudaEventRecord(make_event(&g_join_ev), g_aux));
   TP_CUDA(cudaStreamWaitEvent(g_stream, g_join_ev, 0));
+  g_aux_live = false;
 }
 
 int64_t prod(const int64_t* s, int n) {
@@ -326,8 +352,9 @@ TP_API int tp_aux_return(void) { return guard([&] { aux_return(); }); }
 TP_API int tp_aux_record(int slot) { return guard([&] { aux_record(slot); }); }
 TP_API int tp_main_wait(int slot) { return guard([&] { main_wait(slot); }); }
 TP_API int tp_aux_join(void) { return guard([&] { aux_join(); }); }
-TP_API int tp_comm_fork(void) { return guard([&] { comm_fork(); }); }
-TP_API int tp_comm_return(void) { return guard([&] { comm_return(); }); }
+TP_API int tp_side_fork(void) { return guard([&] { side_fork(); }); }
+TP_API int tp_side_return(void) { return guard([&] { side_return(); }); }
+TP_API int tp_side_join(void) { return guard([&] { side_join(); }); }
 
 TP_API int tp_get_stream(void** out) { return guard([&] { *out = (void*)stream(); }); }
 

@@ -119,6 +119,7 @@ inline unsigned grid_for(int64_t n, int threads, int per_thread = 1) {
 void* scratch(size_t bytes);
 // The communicator's stream (tp_comm.cu); fails when no communicator exists.
 cudaStream_t comm_stream();
+bool comm_active();
 // A second, independent scratch area (repacked filters), same rules.
 void* scratch2(size_t bytes);
 // A third one (the tf32 low parts of a GEMM operand), same rules.

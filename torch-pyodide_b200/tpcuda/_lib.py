@@ -65,8 +65,9 @@ SIGNATURES: dict[str, list] = {
     "tp_aux_record": [INT],
     "tp_main_wait": [INT],
     "tp_aux_join": [],
-    "tp_comm_fork": [],
-    "tp_comm_return": [],
+    "tp_side_fork": [],
+    "tp_side_return": [],
+    "tp_side_join": [],
     "tp_memory_allocated": [I64P],
     "tp_memory_reserved": [I64P],
     "tp_device_name": [ctypes.c_char_p, INT],

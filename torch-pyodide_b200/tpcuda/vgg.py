@@ -18,8 +18,8 @@ fused kernels on preallocated HBM buffers:
             1/world averaging folded in: data-parallel channels-last steps update
             each bucket as soon as its all-reduce is done and its block's data
             gradient (the last reader of its filters) has run, beside the rest of
-            the backward; one GPU (and the NCHW cross-check) updates everything
-            in one launch at the end
+            the backward on a side stream; one GPU (unless early_update=True)
+            and the NCHW cross-check update everything in one launch at the end
 
 Activations are channels-last ([N][H][W][C], layout="nhwc", the default):
 each implicit-GEMM tile of the convolutions is then one TMA box, and the
@@ -186,7 +186,7 @@ class VGG11BN:
 
     def __init__(self, rt, batch: int, seed: int = 0, lr: float = 0.05, momentum: float = 0.9,
                  weight_decay: float = 5e-4, world: int = 1, comm=None, bucket_bytes: int = 8 << 20,
-                 layout: str = "nhwc", keep_acts: bool = False, early_update: bool = True):
+                 layout: str = "nhwc", keep_acts: bool = False, early_update=None):
         if layout not in ("nhwc", "nchw"):
             raise ValueError(f"layout must be 'nhwc' or 'nchw', got {layout!r}")
         self.layout = layout
@@ -284,13 +284,16 @@ class VGG11BN:
 
         # gradient buckets (contiguous ranges of the flat gradient buffer)
         self._plan_buckets()
-        # data-parallel channels-last steps update each bucket's parameters right after
-        # its all-reduce, once nothing later in the step reads them: one SGD group per
-        # bucket, on the communicator's stream (2 GPUs: 2.73 -> 2.70 ms per step).  One
-        # GPU keeps a single update at the end: on the auxiliary stream the per-bucket
-        # updates delayed the weight gradients (batch 128: 0.94 -> 1.06 ms)
+        # data-parallel channels-last steps update each bucket's parameters as soon as its
+        # gradients are all-reduced and nothing later in the step reads them: one SGD group
+        # per bucket, on the side stream, which is then the communicator's (2 GPUs: 2.73 ->
+        # 2.70 ms per step).  One GPU keeps a single update at the end unless asked
+        # (early_update=True): there the per-bucket launches cost more than they hide
+        # (batch 128: 0.927 -> 0.944 ms on the side stream, 1.06 on the auxiliary one)
+        if early_update is None:
+            early_update = comm is not None
         self.bucket_groups = {}
-        if self.overlap and early_update and comm is not None:
+        if self.overlap and early_update:
             for start, count, key in self.buckets:
                 idx = [i for i, n in enumerate(names) if start <= self.offsets[n][0] < start + count]
                 pp = (ctypes.c_void_p * len(idx))(*[self.params + 4 * self.offsets[names[i]][0] for i in idx])
@@ -367,18 +370,18 @@ class VGG11BN:
                                               self.feat, NUM_CLASSES, 1.0 / Bn))
 
     def _update_bucket(self, key: str) -> None:
-        """SGD on the bucket that closes at `key`, once its gradients are all-reduced
-        and nothing later in the step reads its parameters: on the communicator's
-        stream behind the bucket's all-reduce (the library stream joins it before
-        the step ends)."""
+        """SGD on the bucket that closes at `key`, once its gradients are final (and
+        all-reduced) and nothing later in the step reads its parameters: on the side
+        stream, behind the library and auxiliary streams' work so far and the
+        bucket's all-reduce; the library stream joins it before the step ends."""
         if key not in self.bucket_groups:
             return
         L = self.lib
-        check(L.tp_comm_fork())
+        check(L.tp_side_fork())
         try:
             check(L.tpk_sgd_group(self.bucket_groups[key], self.lr, self.momentum, self.wd, 0.0, 0, 1.0 / self.world))
         finally:
-            check(L.tp_comm_return())
+            check(L.tp_side_return())
 
     def _reduce(self, key: str) -> None:
         if self.comm is not None and key in self.bucket_after:
@@ -477,7 +480,9 @@ class VGG11BN:
     def _update(self) -> None:
         if self.comm is not None:
             self.comm.wait()
-        if not self.bucket_groups:  # channels-last steps updated every bucket during the backward
+        if self.bucket_groups:  # every bucket was updated during the backward
+            check(self.lib.tp_side_join())
+        else:
             check(self.lib.tpk_sgd_group(self.group, self.lr, self.momentum, self.wd, 0.0, 0, 1.0 / self.world))
 
     def step_eager(self) -> None:
