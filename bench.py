@@ -561,6 +561,43 @@ def cpu_ops(reps: int = 3) -> dict:
             "2 of 128 images")
         put(f"conv2d wgrad {tag}", best(lambda: o.conv2dWeightBackward(gy, xc, ws, ys, xs, [st], [pd])), fl, "tensor",
             "2 of 128 images")
+        for h in (xc, wc, gy):
+            o.destroy(h)
+    # element-wise rows, full size
+    xa = T(rng.standard_normal((16384, 11008), dtype=np.float32))
+    ba = T(rng.standard_normal(11008, dtype=np.float32))
+    put("add broadcast [M,N]+[N]", best(lambda: o.add(xa, ba)), 2 * 16384 * 11008 * 4 + 11008 * 4, "hbm")
+    xb = T(rng.standard_normal((16384, 11008), dtype=np.float32))
+    put("mul same-shape", best(lambda: o.mul(xa, xb)), 3 * 16384 * 11008 * 4, "hbm")
+    for h in (xa, ba, xb):
+        o.destroy(h)
+    # multi-tensor optimizer rows on the first 8 of the 64 tensors (the oracle's
+    # per-element loop has the same cost per element on every tensor); the same
+    # hyper-parameters and bytes per element as the GPU rows
+    sample = 8
+    shp = [SHAPES[i % 4] for i in range(sample)]
+    P = [T(rng.standard_normal(s, dtype=np.float32) * np.float32(0.02)) for s in shp]
+    G = [T(rng.standard_normal(s, dtype=np.float32) * np.float32(1e-3)) for s in shp]
+    S0 = [T(np.zeros(s, np.float32)) for s in shp]
+    S1 = [T(np.zeros(s, np.float32)) for s in shp]
+    el = sum(numel(s) for s in shp)
+    tag = f"{sample} of {NTENSORS} tensors ({el} of the elements)"
+    ss, isb = adam_scalars(1)
+    for name, bpe, fn in (
+            ("sgd momentum 0.9 nesterov (multi-tensor)", 20,
+             lambda: o.sgdStepMulti(P, G, S0, 1e-3, 0.9, 0.0, 0.0, True)),
+            ("adam L2 wd (multi-tensor)", 28, lambda: o.adamStepMulti(P, G, S0, S1, LR, B1, B2, EPS, WD, ss, isb)),
+            ("rmsprop momentum 0.9 (multi-tensor)", 28,
+             lambda: o.rmspropStepMulti(P, G, S0, S1, 0.01, 0.99, 1e-8, 0.0, 0.9)),
+            ("adagrad (multi-tensor)", 20, lambda: o.adagradStepMulti(P, G, S0, 0.01, 1e-10, 0.0)),
+            ("adamax (multi-tensor)", 28,
+             lambda: o.adamaxStepMulti(P, G, S0, S1, 0.002, 0.9, 0.999, 1e-8, 0.0, 0.02, 1.0)),
+            ("nadam (multi-tensor)", 28, lambda: o.nadamStepMulti(P, G, S0, S1, 0.002, 0.9, 0.999, 1e-8, 0.0, 0.02, 0.9)),
+            ("radam (multi-tensor)", 28,
+             lambda: o.radamStepMulti(P, G, S0, S1, 1e-3, 0.9, 0.999, 1e-8, 0.0, 0.01, 0.53, 0.994, 6))):
+        put(name, best(fn), bpe * el, "hbm", tag)
+    for h in P + G + S0 + S1:
+        o.destroy(h)
     return res
 
 

@@ -66,7 +66,7 @@ def _inputs(B, F, K, seed, bias=True):
 
 
 @pytest.mark.parametrize("B,F,K", [(1024, 512, 10), (128, 512, 10), (1000, 100, 7), (7, 1024, 32), (1, 33, 1),
-                                   (300, 256, 10)])
+                                   (300, 256, 10), (1025, 512, 10), (20000, 64, 17)])
 def test_head_matches_oracle_and_float64(cuda_rt, oracle_rt, B, F, K):
     x, w, b, t = _inputs(B, F, K, B + F + K)
     r = _run(cuda_rt, x, w, b, t)
@@ -110,8 +110,10 @@ def test_head_matches_per_op_composition(cuda_rt):
 def test_head_is_deterministic_and_skips_null_outputs(cuda_rt):
     x, w, b, t = _inputs(1024, 512, 10, 9)
     a = _run(cuda_rt, x, w, b, t)
-    small = _inputs(5, 512, 10, 10)  # one CTA: the ticket wraps at a different count
+    small = _inputs(5, 512, 10, 10)  # one CTA: the tickets wrap at different counts
     _run(cuda_rt, *small)
+    ragged = _inputs(1000, 512, 10, 11)  # 125 CTAs: a last group of 5
+    _run(cuda_rt, *ragged)
     c = _run(cuda_rt, x, w, b, t)
     for k in a:
         assert np.array_equal(a[k], c[k]), k

@@ -11,17 +11,21 @@
 // classes) each of those is a few microseconds of launch and ramp for
 // nanoseconds of work, so the head is one kernel:
 //
-//   CTA j owns rows [j R, (j + 1) R), a warp per row at a time (W in shared memory):
+//   CTA j owns rows [j R, (j + 1) R), a warp per row at a time (W in shared memory,
+//   the warp's next row loaded while it works on the current one):
 //     logits[r][k] = x[r] . w[k] + b[k]              (warp dot products)
 //     loss[r] = logsumexp(logits[r]) - logits[r][t]   (k_cross_entropy's arithmetic)
 //     g[r][k] = (softmax(logits[r])[k] - [k == t]) * scale
 //     dx[r][f] = sum_k g[r][k] w[k][f]
 //   then, over its rows in order: partial dW = sum_r g[r]^T x[r], partial db,
-//   partial loss sum; the last CTA to finish (a self-resetting ticket) adds the
-//   partials of all CTAs in CTA order.  Every sum runs in a fixed order, so
-//   the result does not depend on scheduling.
+//   partial loss sum; the last CTA of each group of 8 to finish (a self-resetting
+//   ticket) adds its group's partials in CTA order, and the last group adds the
+//   group sums in group order.  Every sum runs in a fixed order, so the result
+//   does not depend on scheduling.  Up to 128 CTAs of one warp-row per warp: the
+//   work is a few microseconds of latency-bound dot products, so it is spread
+//   over as many SMs as there are rows for.
 //
-// The ticket is one word per device: calls must not overlap on the GPU (all
+// The tickets are words per device: calls must not overlap on the GPU (all
 // library launches go to its one stream, in order).
 #include <cuda_runtime.h>
 #include <float.h>
@@ -33,9 +37,12 @@ namespace tp {
 constexpr int HEAD_THREADS = 256;
 constexpr int HEAD_MAX_K = 32;
 constexpr int HEAD_MAX_F = 1024;
-constexpr int HEAD_MAX_CTAS = 16;  // grid size bound (rows per CTA = ceil(B / 16), at least 8)
+constexpr int HEAD_GROUP = 8;        // CTAs whose partials one CTA adds first
+constexpr int HEAD_MAX_GROUPS = 16;
+constexpr int HEAD_MAX_CTAS = HEAD_GROUP * HEAD_MAX_GROUPS;  // rows per CTA = max(8, ceil(B / 128))
 
 static __device__ unsigned int g_head_ticket;
+static __device__ unsigned int g_head_group_ticket[HEAD_MAX_GROUPS];
 
 __device__ __forceinline__ float head_warp_sum(float v) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -63,49 +70,127 @@ struct HeadArgs {
   float* dx;          // [B][F] or null
   float* dw;          // [K][F] or null
   float* db;          // [K] or null
-  float* part;        // [grid][K*F + K + 1]
+  float* part;        // [grid + groups][K*F + K + 1]: CTA partials, then group sums
   int B, F, K, R;     // R: rows per CTA
   float scale;
 };
 
+// out(i, sum over j < n of src[j * stride + i]) for every i < stride, j in order;
+// four outputs per thread and step, all n partials of each loaded before any is
+// added (the adding CTA's time is the launch's tail).
+template <int NMAX, class Out>
+__device__ __forceinline__ void head_add_partials(const float* src, int n, int stride, int tid, Out&& out) {
+  for (int i0 = tid; i0 < stride; i0 += 4 * HEAD_THREADS) {
+    float v[4][NMAX];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = i0 + u * HEAD_THREADS;
+#pragma unroll
+      for (int j = 0; j < NMAX; ++j) v[u][j] = (j < n && i < stride) ? __ldcg(src + (size_t)j * stride + i) : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = i0 + u * HEAD_THREADS;
+      if (i >= stride) continue;
+      float acc = 0.0f;
+#pragma unroll
+      for (int j = 0; j < NMAX; ++j)
+        if (j < n) acc += v[u][j];
+      out(i, acc);
+    }
+  }
+}
+
+// Lane l ends with the warp's sum of v[l % KP] (KP = 16 or 32 partial logits per
+// lane): a reduce-scatter, each xor stage keeps the half of the values whose
+// index bit matches the lane's and adds the partner's copy of them (KP = 16:
+// stages 8 .. 1 inside each half-warp, then one xor-16 add).  31 shuffles in 5
+// dependent steps instead of a 5-step tree per logit.
+template <int KP>
+__device__ __forceinline__ float head_reduce_scatter(float (&v)[KP], int lane) {
+  static_assert(KP == 16 || KP == 32, "16 or 32 partial logits per lane");
+#pragma unroll
+  for (int o = KP / 2; o > 0; o >>= 1) {
+    const bool up = (lane & o) != 0;
+#pragma unroll
+    for (int j = 0; j < o; ++j) {
+      const float send = up ? v[j] : v[j + o];
+      const float keep = up ? v[j + o] : v[j];
+      v[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+  if (KP == 16) v[0] += __shfl_xor_sync(0xffffffffu, v[0], 16);
+  return v[0];
+}
+
 // dynamic shared memory: w [K][F], then g [R][K], then loss [R]
-template <int FPL>  // features per lane (F <= 32 * FPL)
+template <int FPL, int KP>  // features per lane (F <= 32 * FPL), logits per lane (K <= KP)
 __global__ void __launch_bounds__(HEAD_THREADS) k_linear_ce_step(HeadArgs a) {
-  extern __shared__ float sm[];
+  extern __shared__ __align__(16) float sm[];
   float* ws = sm;
   float* gs = ws + (size_t)a.K * a.F;
   float* ls = gs + (size_t)a.R * a.K;
   __shared__ unsigned int last;
   ::tp::pdl_enter();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarp = HEAD_THREADS / 32;
-  for (int i = tid; i < a.K * a.F; i += HEAD_THREADS) ws[i] = a.w[i];
-  __syncthreads();
+  {  // W into shared memory, 16-byte vectors 8 per thread in flight (W is 16-byte aligned
+     // and K*F a multiple of 4, else one float at a time)
+    const int n = a.K * a.F;
+    if ((n & 3) == 0 && ((uintptr_t)a.w & 15) == 0) {
+      const float4* w4 = reinterpret_cast<const float4*>(a.w);
+      float4* s4 = reinterpret_cast<float4*>(ws);
+#pragma unroll 8
+      for (int i = tid; i < n / 4; i += HEAD_THREADS) s4[i] = __ldg(w4 + i);
+    } else {
+#pragma unroll 8
+      for (int i = tid; i < n; i += HEAD_THREADS) ws[i] = __ldg(a.w + i);
+    }
+  }
   const int r0 = blockIdx.x * a.R;
   const int r1 = min(r0 + a.R, a.B);
-  for (int r = r0 + warp; r < r1; r += nwarp) {
-    float xv[FPL];
+  // the warp's first row is loaded while W is staged; each row's successor while it is used
+  float xv[FPL], xn[FPL];
+  float tv = 0.0f, tn = 0.0f;
+  const float bias = (a.b && lane < a.K) ? a.b[lane] : 0.0f;
+  if (r0 + warp < r1) {
 #pragma unroll
     for (int i = 0; i < FPL; ++i) {
       const int f = lane + 32 * i;
-      xv[i] = f < a.F ? a.x[(int64_t)r * a.F + f] : 0.0f;
+      xv[i] = f < a.F ? a.x[(int64_t)(r0 + warp) * a.F + f] : 0.0f;
     }
-    // lane k keeps logit k
-    float mine = -FLT_MAX;
-    for (int k = 0; k < a.K; ++k) {
-      float s = 0.0f;
+    tv = a.tgt[r0 + warp];
+  }
+  __syncthreads();
+  for (int r = r0 + warp; r < r1; r += nwarp) {
+    const int rn = r + nwarp;
+    if (rn < r1) {
 #pragma unroll
       for (int i = 0; i < FPL; ++i) {
         const int f = lane + 32 * i;
-        if (f < a.F) s = fmaf(xv[i], ws[k * a.F + f], s);
+        xn[i] = f < a.F ? a.x[(int64_t)rn * a.F + f] : 0.0f;
       }
-      s = head_warp_sum(s) + (a.b ? a.b[k] : 0.0f);
-      if (lane == k) mine = s;
+      tn = a.tgt[rn];
+    }
+    // partial dot products of all logits, then lane k keeps logit k
+    float s[KP];
+#pragma unroll
+    for (int k = 0; k < KP; ++k) {
+      s[k] = 0.0f;
+      if (k < a.K) {
+#pragma unroll
+        for (int i = 0; i < FPL; ++i) {
+          const int f = lane + 32 * i;
+          if (f < a.F) s[k] = fmaf(xv[i], ws[k * a.F + f], s[k]);
+        }
+      }
     }
     const bool has = lane < a.K;
-    const float m = head_warp_max(has ? mine : -FLT_MAX);
+    float mine = head_reduce_scatter<KP>(s, lane);
+    mine = has ? mine + bias : -FLT_MAX;
+    const float m = head_warp_max(mine);
     const float e = has ? expf(mine - m) : 0.0f;
     const float se = head_warp_sum(e);
-    const int t = head_target(a.tgt[r], a.K);
+    const int t = head_target(tv, a.K);
     const float lt = __shfl_sync(0xffffffffu, mine, t);
     const float g = has ? (e / se - (lane == t ? 1.0f : 0.0f)) * a.scale : 0.0f;
     if (has) {
@@ -135,24 +220,63 @@ __global__ void __launch_bounds__(HEAD_THREADS) k_linear_ce_step(HeadArgs a) {
         if (f < a.F) a.dx[(int64_t)r * a.F + f] = d[i];
       }
     }
+#pragma unroll
+    for (int i = 0; i < FPL; ++i) xv[i] = xn[i];
+    tv = tn;
   }
   __syncthreads();
   // this CTA's partials, rows in order
   const int stride = a.K * a.F + a.K + 1;
   float* pp = a.part + (size_t)blockIdx.x * stride;
-  for (int f = tid; f < a.F; f += HEAD_THREADS) {
-    float acc[HEAD_MAX_K];
+  // every (k, f) over the CTA's rows in order; a thread owns FT features, and
+  // fetches RB rows of them at a time (32 loads in flight)
+  constexpr int FT = FPL / 8;  // F <= 256 FT
+  constexpr int RB = 32 / FT;
+  {
+    float acc[FT][KP];
 #pragma unroll
-    for (int k = 0; k < HEAD_MAX_K; ++k) acc[k] = 0.0f;
-    for (int r = r0; r < r1; ++r) {
-      const float xf = a.x[(int64_t)r * a.F + f];
+    for (int ft = 0; ft < FT; ++ft)
 #pragma unroll
-      for (int k = 0; k < HEAD_MAX_K; ++k)
-        if (k < a.K) acc[k] = fmaf(gs[(r - r0) * a.K + k], xf, acc[k]);
+      for (int k = 0; k < KP; ++k) acc[ft][k] = 0.0f;
+    int r = r0;
+    for (; r + RB <= r1; r += RB) {
+      float xf[RB][FT];
+#pragma unroll
+      for (int u = 0; u < RB; ++u)
+#pragma unroll
+        for (int ft = 0; ft < FT; ++ft) {
+          const int f = tid + HEAD_THREADS * ft;
+          xf[u][ft] = f < a.F ? a.x[(int64_t)(r + u) * a.F + f] : 0.0f;
+        }
+#pragma unroll
+      for (int u = 0; u < RB; ++u)
+#pragma unroll
+        for (int k = 0; k < KP; ++k)
+          if (k < a.K) {
+            const float gk = gs[(r + u - r0) * a.K + k];
+#pragma unroll
+            for (int ft = 0; ft < FT; ++ft) acc[ft][k] = fmaf(gk, xf[u][ft], acc[ft][k]);
+          }
+    }
+    for (; r < r1; ++r) {
+#pragma unroll
+      for (int ft = 0; ft < FT; ++ft) {
+        const int f = tid + HEAD_THREADS * ft;
+        const float xf = f < a.F ? a.x[(int64_t)r * a.F + f] : 0.0f;
+#pragma unroll
+        for (int k = 0; k < KP; ++k)
+          if (k < a.K) acc[ft][k] = fmaf(gs[(r - r0) * a.K + k], xf, acc[ft][k]);
+      }
     }
 #pragma unroll
-    for (int k = 0; k < HEAD_MAX_K; ++k)
-      if (k < a.K) pp[k * a.F + f] = acc[k];
+    for (int ft = 0; ft < FT; ++ft) {
+      const int f = tid + HEAD_THREADS * ft;
+      if (f < a.F) {
+#pragma unroll
+        for (int k = 0; k < KP; ++k)
+          if (k < a.K) pp[k * a.F + f] = acc[ft][k];
+      }
+    }
   }
   if (tid < a.K) {
     float s = 0.0f;
@@ -164,54 +288,58 @@ __global__ void __launch_bounds__(HEAD_THREADS) k_linear_ce_step(HeadArgs a) {
     for (int r = r0; r < r1; ++r) s += ls[r - r0];
     pp[a.K * a.F + a.K] = s;
   }
-  // the last CTA adds every CTA's partials (ticket returns to 0 after gridDim.x arrivals)
+  // Two levels of fixed-order sums: the last CTA of each group of HEAD_GROUP adds
+  // its group's partials in CTA order, the last group to finish adds the group
+  // sums in group order (each ticket returns to 0 after its arrivals).
+  const int ngroups = (int)((gridDim.x + HEAD_GROUP - 1) / HEAD_GROUP);
+  const int grp = (int)(blockIdx.x / HEAD_GROUP);
+  const int g0 = grp * HEAD_GROUP;
+  const int gn = min(HEAD_GROUP, (int)gridDim.x - g0);
   __syncthreads();
   if (tid == 0) {
     __threadfence();
-    last = atomicInc(&g_head_ticket, gridDim.x - 1) == gridDim.x - 1;
+    last = atomicInc(&g_head_group_ticket[grp], (unsigned)gn - 1) == (unsigned)gn - 1;
   }
   __syncthreads();
   if (!last) return;
   __threadfence();
-  // four outputs per thread and step, all HEAD_MAX_CTAS partials of each loaded before
-  // any is added (this CTA's time is the launch's tail), then added in CTA order
-  const int nb = gridDim.x;
-  for (int i0 = tid; i0 < stride; i0 += 4 * HEAD_THREADS) {
-    float v[4][HEAD_MAX_CTAS];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int i = i0 + u * HEAD_THREADS;
-#pragma unroll
-      for (int j = 0; j < HEAD_MAX_CTAS; ++j)
-        v[u][j] = (j < nb && i < stride) ? __ldcg(a.part + (size_t)j * stride + i) : 0.0f;
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int i = i0 + u * HEAD_THREADS;
-      if (i >= stride) continue;
-      float s = 0.0f;
-#pragma unroll
-      for (int j = 0; j < HEAD_MAX_CTAS; ++j)
-        if (j < nb) s += v[u][j];
-      if (i < a.K * a.F) {
-        if (a.dw) a.dw[i] = s;
-      } else if (i < a.K * a.F + a.K) {
-        if (a.db) a.db[i - a.K * a.F] = s;
-      } else if (a.loss_mean) {
-        a.loss_mean[0] = a.B > 0 ? s / (float)a.B : 0.0f;
-      }
-    }
+  float* gsum = a.part + ((size_t)gridDim.x + grp) * stride;
+  head_add_partials<HEAD_GROUP>(a.part + (size_t)g0 * stride, gn, stride, tid,
+                                [&](int i, float v) { gsum[i] = v; });
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    last = atomicInc(&g_head_ticket, (unsigned)ngroups - 1) == (unsigned)ngroups - 1;
   }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  head_add_partials<HEAD_MAX_GROUPS>(a.part + (size_t)gridDim.x * stride, ngroups, stride, tid, [&](int i, float v) {
+    if (i < a.K * a.F) {
+      if (a.dw) a.dw[i] = v;
+    } else if (i < a.K * a.F + a.K) {
+      if (a.db) a.db[i - a.K * a.F] = v;
+    } else if (a.loss_mean) {
+      a.loss_mean[0] = a.B > 0 ? v / (float)a.B : 0.0f;
+    }
+  });
+}
+
+template <int FPL, int KP>
+static void head_launch_k(int grid, size_t smem, const HeadArgs& a) {
+  static bool attr = false;  // one per instantiation
+  if (!attr) {
+    TP_CUDA(cudaFuncSetAttribute(k_linear_ce_step<FPL, KP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 200 * 1024));
+    attr = true;
+  }
+  TP_LAUNCH((k_linear_ce_step<FPL, KP>), (unsigned)grid, HEAD_THREADS, smem, a);
 }
 
 template <int FPL>
 static void head_launch(int grid, size_t smem, const HeadArgs& a) {
-  static bool attr = false;  // one per instantiation
-  if (!attr) {
-    TP_CUDA(cudaFuncSetAttribute(k_linear_ce_step<FPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-    attr = true;
-  }
-  TP_LAUNCH(k_linear_ce_step<FPL>, (unsigned)grid, HEAD_THREADS, smem, a);
+  if (a.K <= 16) head_launch_k<FPL, 16>(grid, smem, a);
+  else head_launch_k<FPL, 32>(grid, smem, a);
 }
 
 }  // namespace tp
@@ -228,16 +356,18 @@ TP_API int tpk_linear_cross_entropy_step(const float* x, const float* w, const f
     TP_REQUIRE(F >= 1 && F <= HEAD_MAX_F, "linear_cross_entropy_step: 1 <= F <= %d features", HEAD_MAX_F);
     TP_REQUIRE(K >= 1 && K <= HEAD_MAX_K, "linear_cross_entropy_step: 1 <= K <= %d classes", HEAD_MAX_K);
     TP_REQUIRE(x && w && targets, "linear_cross_entropy_step: x, w and targets are required");
-    // about 16 CTAs: each adds its rows' dW in order, the last adds 16 partials
-    int R = (int)((B + 15) / 16);
+    // up to 128 CTAs of at least 8 rows (a warp per row): each adds its rows' dW in
+    // order, then the two levels of HEAD_GROUP and HEAD_MAX_GROUPS partials
+    int64_t R = (B + HEAD_MAX_CTAS - 1) / HEAD_MAX_CTAS;
     if (R < 8) R = 8;
     const int grid = (int)((B + R - 1) / R);
     TP_REQUIRE(grid <= HEAD_MAX_CTAS, "linear_cross_entropy_step: grid of %d CTAs", grid);
     const size_t smem = ((size_t)K * F + (size_t)R * K + R) * sizeof(float);
     TP_REQUIRE(smem <= 200 * 1024, "linear_cross_entropy_step: K*F + R*(K+1) floats exceed shared memory");
-    float* part = (float*)scratch((size_t)grid * (K * F + K + 1) * sizeof(float));
+    const int ngroups = (grid + HEAD_GROUP - 1) / HEAD_GROUP;
+    float* part = (float*)scratch((size_t)(grid + ngroups) * (K * F + K + 1) * sizeof(float));
     HeadArgs a{x, w, b, targets, logits, loss_rows, loss_mean, dx, dw, db, part,
-               (int)B, (int)F, (int)K, R, scale};
+               (int)B, (int)F, (int)K, (int)R, scale};
     if (F <= 256)
       head_launch<8>(grid, smem, a);
     else if (F <= 512)
