@@ -562,6 +562,10 @@ TP_API int tpk_fill(float* x, int64_t n, float value);
 /* ---- data-parallel gradient exchange (new: the reference has no parallelism) ---- */
 /* NCCL unique id of rank 0 (128 bytes) to hand to every rank */
 TP_API int tp_comm_unique_id(char* out, int len);
+/* New: before tp_comm_init, 1 (the default) creates the communicator's stream
+ * at the device's highest stream priority (its all-reduces then start ahead of
+ * pending compute CTAs); 0 at the normal priority. */
+TP_API int tp_set_comm_priority(int high);
 TP_API int tp_comm_init(int rank, int world, const char* unique_id, int len);
 /* in-place sum over ranks, queued after the work already on the library stream,
  * run on the communication stream */

@@ -135,7 +135,9 @@ TP_API int tp_graph_end(int64_t* out_graph) {
     cudaGraph_t graph = nullptr;
     TP_CUDA(cudaStreamEndCapture(stream(), &graph));
     cudaGraphExec_t exec = nullptr;
-    cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+    // kernels keep the priority of the stream they were captured on (the
+    // communicator's stream may run at a higher one)
+    cudaError_t e = cudaGraphInstantiate(&exec, graph, cudaGraphInstantiateFlagUseNodePriority);
     cudaGraphDestroy(graph);
     if (e != cudaSuccess) fail(TP_ERR_CUDA, "cudaGraphInstantiate failed: %s", cudaGetErrorString(e));
     int64_t id = g_next_graph++;

@@ -198,6 +198,7 @@ SIGNATURES: dict[str, list] = {
     "tpk_cross_entropy_backward": [P, P, P, I64, I64, F32],
     "tpk_fill": [P, I64, F32],
     "tp_comm_unique_id": [ctypes.c_char_p, INT],
+    "tp_set_comm_priority": [INT],
     "tp_comm_init": [INT, INT, ctypes.c_char_p, INT],
     "tp_comm_allreduce_async": [P, I64],
     "tp_comm_wait": [],
