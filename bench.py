@@ -1066,6 +1066,8 @@ def run_vgg(args, rank, world, local):
     rt = CudaRuntime(local)
     store = make_store(rank, world)
     stream = torch.cuda.ExternalStream(rt.stream(), device=torch.device("cuda", local))
+    from tpcuda._lib import check as _check
+    _check(rt.lib.tp_set_comm_priority(args.comm_priority))
     comm = comm_from_store(rt.lib, store)
     B = VGG_GLOBAL_BATCH // world
     model = VGG11BN(rt, B, seed=0, world=world, comm=comm)
@@ -1225,6 +1227,9 @@ def main():
                     help="--workload conv: 1 = [Cout][3][3][Cin] (the step's), 0 = [Cout][Cin][3][3] (with Cin = 4: "
                          "the first layer's CUDA-core kernels)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--comm-priority", type=int, choices=[0, 1], default=1,
+                    help="vgg workload at N>1: 1 = the communicator's stream at the highest priority (the "
+                         "default), 0 = normal priority")
     ap.add_argument("--no-adamw", action="store_true", help="vgg workload at N=1: skip the fused AdamW sub-record")
     ap.add_argument("--launch-list", action="store_true",
                     help="profiling aid: two eager VGG steps at --batch with launch counts (1 GPU, no timing)")
