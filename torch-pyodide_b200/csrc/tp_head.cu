@@ -18,9 +18,9 @@
 //     g[r][k] = (softmax(logits[r])[k] - [k == t]) * scale
 //     dx[r][f] = sum_k g[r][k] w[k][f]
 //   then, over its rows in order: partial dW = sum_r g[r]^T x[r], partial db,
-//   partial loss sum; the last CTA of each group of 8 to finish (a self-resetting
-//   ticket) adds its group's partials in CTA order, and the last group adds the
-//   group sums in group order.  Every sum runs in a fixed order, so the result
+//   partial loss sum; the last CTA of each group to finish (a self-resetting
+//   ticket) adds its group's partials in CTA order (one group of up to 16 CTAs,
+//   else groups of 8 whose sums the last group adds in group order).  Every sum runs in a fixed order, so the result
 //   does not depend on scheduling.  Up to 128 CTAs of one warp-row per warp: the
 //   work is a few microseconds of latency-bound dot products, so it is spread
 //   over as many SMs as there are rows for.
@@ -288,13 +288,24 @@ __global__ void __launch_bounds__(HEAD_THREADS) k_linear_ce_step(HeadArgs a) {
     for (int r = r0; r < r1; ++r) s += ls[r - r0];
     pp[a.K * a.F + a.K] = s;
   }
-  // Two levels of fixed-order sums: the last CTA of each group of HEAD_GROUP adds
-  // its group's partials in CTA order, the last group to finish adds the group
-  // sums in group order (each ticket returns to 0 after its arrivals).
-  const int ngroups = (int)((gridDim.x + HEAD_GROUP - 1) / HEAD_GROUP);
-  const int grp = (int)(blockIdx.x / HEAD_GROUP);
-  const int g0 = grp * HEAD_GROUP;
-  const int gn = min(HEAD_GROUP, (int)gridDim.x - g0);
+  // Fixed-order sums: the last CTA of each group to finish adds its group's partials
+  // in CTA order; with more than one group (more than HEAD_MAX_GROUPS CTAs, groups of
+  // HEAD_GROUP) the last group to finish then adds the group sums in group order
+  // (each ticket returns to 0 after its arrivals).
+  auto emit = [&](int i, float v) {
+    if (i < a.K * a.F) {
+      if (a.dw) a.dw[i] = v;
+    } else if (i < a.K * a.F + a.K) {
+      if (a.db) a.db[i - a.K * a.F] = v;
+    } else if (a.loss_mean) {
+      a.loss_mean[0] = a.B > 0 ? v / (float)a.B : 0.0f;
+    }
+  };
+  const int gsz = gridDim.x <= (unsigned)HEAD_MAX_GROUPS ? (int)gridDim.x : HEAD_GROUP;
+  const int ngroups = ((int)gridDim.x + gsz - 1) / gsz;
+  const int grp = (int)blockIdx.x / gsz;
+  const int g0 = grp * gsz;
+  const int gn = min(gsz, (int)gridDim.x - g0);
   __syncthreads();
   if (tid == 0) {
     __threadfence();
@@ -303,6 +314,10 @@ __global__ void __launch_bounds__(HEAD_THREADS) k_linear_ce_step(HeadArgs a) {
   __syncthreads();
   if (!last) return;
   __threadfence();
+  if (ngroups == 1) {
+    head_add_partials<HEAD_MAX_GROUPS>(a.part, gn, stride, tid, emit);
+    return;
+  }
   float* gsum = a.part + ((size_t)gridDim.x + grp) * stride;
   head_add_partials<HEAD_GROUP>(a.part + (size_t)g0 * stride, gn, stride, tid,
                                 [&](int i, float v) { gsum[i] = v; });
@@ -314,15 +329,7 @@ __global__ void __launch_bounds__(HEAD_THREADS) k_linear_ce_step(HeadArgs a) {
   __syncthreads();
   if (!last) return;
   __threadfence();
-  head_add_partials<HEAD_MAX_GROUPS>(a.part + (size_t)gridDim.x * stride, ngroups, stride, tid, [&](int i, float v) {
-    if (i < a.K * a.F) {
-      if (a.dw) a.dw[i] = v;
-    } else if (i < a.K * a.F + a.K) {
-      if (a.db) a.db[i - a.K * a.F] = v;
-    } else if (a.loss_mean) {
-      a.loss_mean[0] = a.B > 0 ? v / (float)a.B : 0.0f;
-    }
-  });
+  head_add_partials<HEAD_MAX_GROUPS>(a.part + (size_t)gridDim.x * stride, ngroups, stride, tid, emit);
 }
 
 template <int FPL, int KP>
@@ -357,7 +364,8 @@ TP_API int tpk_linear_cross_entropy_step(const float* x, const float* w, const f
     TP_REQUIRE(K >= 1 && K <= HEAD_MAX_K, "linear_cross_entropy_step: 1 <= K <= %d classes", HEAD_MAX_K);
     TP_REQUIRE(x && w && targets, "linear_cross_entropy_step: x, w and targets are required");
     // up to 128 CTAs of at least 8 rows (a warp per row): each adds its rows' dW in
-    // order, then the two levels of HEAD_GROUP and HEAD_MAX_GROUPS partials
+    // order, then one group of up to HEAD_MAX_GROUPS partials, or groups of HEAD_GROUP
+    // and their sums
     int64_t R = (B + HEAD_MAX_CTAS - 1) / HEAD_MAX_CTAS;
     if (R < 8) R = 8;
     const int grid = (int)((B + R - 1) / R);
