@@ -998,20 +998,35 @@ def profile_case(args):
     print(json.dumps({"profile_case": args.profile_case, "iterations": 2}), flush=True)
 
 
+VGG_CONVS = ((64, 128, 16), (128, 256, 8), (256, 256, 8), (256, 512, 4), (512, 512, 4), (512, 512, 2))
+
+
 def run_conv_layer(args):
     """One VGG-11-BN convolution pass on channels-last buffers with packed
     [Cout][3][3][Cin] filters (the step's own layout and entries), timed with
     CUDA events over --steps launches after --warmup; doubles as a small,
-    few-launch target for ncu captures of one GEMM kernel.  One JSON line."""
-    import ctypes
+    few-launch target for ncu captures of one GEMM kernel.  One JSON line.
+    --conv all: every tensor-core layer of the network (the 3x3 convolutions
+    after the first), all three passes, one line each."""
     import torch
     from tpcuda import CudaRuntime
-    from tpcuda._lib import check
     rt = CudaRuntime(0)
-    lib = rt.lib
     torch.cuda.set_device(0)
     stream = torch.cuda.ExternalStream(rt.stream())
-    cin, cout, hw = (int(v) for v in args.conv.split(","))
+    if args.conv == "all":
+        for cin, cout, hw in VGG_CONVS:
+            for ps in ("fwd", "dgrad", "wgrad"):
+                conv_pass(args, rt, stream, cin, cout, hw, ps)
+    else:
+        cin, cout, hw = (int(v) for v in args.conv.split(","))
+        conv_pass(args, rt, stream, cin, cout, hw, args.pass_)
+
+
+def conv_pass(args, rt, stream, cin, cout, hw, pass_):
+    import ctypes
+    import torch
+    from tpcuda._lib import check
+    lib = rt.lib
     B = args.batch
     check(lib.tp_set_gemm_path(args.gemm_path))
     rt.setSeed(0)
@@ -1024,9 +1039,9 @@ def run_conv_layer(args):
     hdw = rt.randn([cout, 3, 3, cin], "float32")  # same size in either filter layout
     p = lambda h: ctypes.c_void_p(rt.devicePtr(h["id"]))  # noqa: E731
     x, w, b, y, dx, dw = (p(h) for h in (hx, hw_, hb, hy, hdx, hdw))
-    if args.pass_ == "fwd":
+    if pass_ == "fwd":
         fn = lambda: lib.tpk_conv2d_fwd_nhwc(x, w, b, y, B, cin, hw, hw, cout, 3, 3, 1, 1, fl)  # noqa: E731
-    elif args.pass_ == "dgrad":
+    elif pass_ == "dgrad":
         fn = lambda: lib.tpk_conv2d_dgrad_nhwc(y, w, dx, B, cin, hw, hw, cout, 3, 3, 1, 1, fl)  # noqa: E731
     else:
         fn = lambda: lib.tpk_conv2d_wgrad_nhwc(y, x, dw, B, cin, hw, hw, cout, 3, 3, 1, 1, fl)  # noqa: E731
@@ -1045,7 +1060,7 @@ def run_conv_layer(args):
     flops = 2.0 * B * hw * hw * cout * cin * 9
     peak3, _, peak_kind = tf32x3_peak()
     tf = flops / (ms * 1e-3) / 1e12
-    print(json.dumps({"conv": [cin, cout, hw], "pass": args.pass_, "batch": B, "gemm_path": args.gemm_path,
+    print(json.dumps({"conv": [cin, cout, hw], "pass": pass_, "batch": B, "gemm_path": args.gemm_path,
                       "filter_layout": fl,
                       "ms": round(ms, 4), "TFLOP/s": round(tf, 2), "frac_of_3xtf32": round(tf / peak3, 3),
                       "peak": round(peak3, 1), "peak_source": peak_kind, "status": st.value}), flush=True)
@@ -1219,7 +1234,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["vgg", "adamw", "ops", "conv", "tiny"], default="vgg")
-    ap.add_argument("--conv", default="256,256,8", help="--workload conv: Cin,Cout,H=W of the layer")
+    ap.add_argument("--conv", default="256,256,8",
+                    help="--workload conv: Cin,Cout,H=W of the layer, or 'all' (every tensor-core layer, 3 passes)")
     ap.add_argument("--pass", dest="pass_", choices=["fwd", "dgrad", "wgrad"], default="fwd",
                     help="--workload conv: which pass")
     ap.add_argument("--gemm-path", type=int, default=0, help="--workload conv: tp_set_gemm_path value")
