@@ -331,9 +331,9 @@ TP_API int tp_max_pool2d_backward(int64_t grad_out, int64_t indices, const int64
  * 0 mean "null" (weight 1, bias 0, mean 0, var 1) */
 TP_API int tp_batch_norm(int64_t input, int64_t weight, int64_t bias, int64_t running_mean, int64_t running_var,
                          float eps, tp_handle* out);
-/* New: training-mode forward of tensor_nn_ops.py:92-254 in three launches;
- * updates running stats in place, returns y and the saved mean / inv_std;
- * fuse_relu applies ReLU to y */
+/* New: training-mode forward of tensor_nn_ops.py:92-254 (three launches, or
+ * one for large tensors, tp_set_bn_flow); updates running stats in place,
+ * returns y and the saved mean / inv_std; fuse_relu applies ReLU to y */
 TP_API int tp_batch_norm_train(int64_t input, int64_t weight, int64_t bias, int64_t running_mean,
                                int64_t running_var, float eps, float momentum, int fuse_relu, tp_handle* out,
                                tp_handle* save_mean, tp_handle* save_invstd);
@@ -343,6 +343,19 @@ TP_API int tp_batch_norm_train(int64_t input, int64_t weight, int64_t bias, int6
 TP_API int tp_batch_norm_backward(int64_t grad_out, int64_t input, int64_t weight, int64_t save_mean,
                                   int64_t save_invstd, int64_t relu_out, tp_handle* dx, tp_handle* dweight,
                                   tp_handle* dbias);
+/* New, a tuning switch of the NCHW BatchNorm training kernels (tp_batch_norm_train,
+ * tp_batch_norm_backward, tpk_bn_train, tpk_bn_backward): mode 0 = two passes
+ * (per-channel sums, then the element-wise pass; a tensor larger than L2 is
+ * read twice from HBM); 1 (default) = for tensors of 32 MB or more with
+ * H*W % 4 == 0, one launch whose CTAs claim work items in a fixed order --
+ * the sums of a channel, then, `lag` channels later, its element-wise pass,
+ * which re-reads the channel from L2; 2 = that launch whenever H*W % 4 == 0.
+ * lag 0 = automatic; ctas_per_sm 0 = 4; item_values 0 = 16384 values of one
+ * channel per work item (rounded down to whole images).  Same formulas either
+ * way; the f64 sums are grouped differently, so mean and inv_std may differ in
+ * the last bit.  A wait of that launch that expires (2 s) is reported like the
+ * tensor-core kernels' (tp_gemm_status, tp_synchronize). */
+TP_API int tp_set_bn_flow(int mode, int lag, int ctas_per_sm, int item_values);
 /* normalizationOps.ts:128-171 layerNorm (layernorm.wgsl:14-42) over the last
  * normalized_size values; save_mean / save_rstd may be NULL */
 TP_API int tp_layer_norm(int64_t input, int64_t normalized_size, int64_t gamma, int64_t beta, float eps,

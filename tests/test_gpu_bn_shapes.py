@@ -80,3 +80,48 @@ def test_bn_train_matches_oracle(cuda_rt, oracle_rt, shape, relu):
         _close(got[k].ravel(), want[k].ravel(), 1e-4, k)
     for k in ("mean", "invstd", "rm", "rv"):
         _close(got[k].ravel(), want[k].ravel(), 1e-5, k)
+
+
+# The one-launch form (statistics and normalisation as work items claimed in a
+# fixed order, tp_set_bn_flow) runs by default only on tensors of 32 MB or
+# more; mode 2 forces it on these shapes.  Lags of 1 and 3 channels make
+# apply items wait for their channel's sums (and more channels than the lag),
+# 1 and 4 CTAs per SM change which CTA takes which item.  An item covers about
+# 16 K values of one channel: [64, 40, 28, 28] (20 + 20 + 20 + 4 images) and
+# [37, 9, 32, 32] (16 + 16 + 5) end in a short range, [512, 6, 8, 8] has two
+# full ranges, the others one range per channel.
+FLOW_SHAPES = [s for s in SHAPES if (s[2] * s[3]) % 4 == 0] + [[37, 9, 32, 32], [512, 6, 8, 8]]
+
+
+@pytest.mark.parametrize("shape", FLOW_SHAPES)
+@pytest.mark.parametrize("relu", [False, True])
+@pytest.mark.parametrize("lag,ctas", [(0, 0), (1, 4), (3, 1)])
+def test_bn_one_launch_matches_oracle(cuda_rt, oracle_rt, shape, relu, lag, ctas):
+    import ctypes
+    rng = np.random.default_rng(sum(shape) + 2 * relu + 7 * lag)
+    C = shape[1]
+    x = (rng.standard_normal(shape) * 1.5 + 0.7).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(C)).astype(np.float32)
+    b = (0.1 * rng.standard_normal(C)).astype(np.float32)
+    gy = rng.standard_normal(shape).astype(np.float32)
+    want = _run_oracle(oracle_rt, x, w, b, gy, relu)
+    lib = cuda_rt.lib
+    assert lib.tp_set_bn_flow(2, lag, ctas, 0) == 0
+    try:
+        got = _run_cuda(cuda_rt, x, w, b, gy, relu)
+    finally:
+        assert lib.tp_set_bn_flow(1, 0, 0, 0) == 0
+    status = ctypes.c_int(-1)
+    assert lib.tp_gemm_status(ctypes.byref(status), 1) == 0 and status.value == 0, "a bounded wait expired"
+    for k in ("y", "dx", "dw", "db"):
+        _close(got[k].ravel(), want[k].ravel(), 1e-4, k)
+    for k in ("mean", "invstd", "rm", "rv"):
+        _close(got[k].ravel(), want[k].ravel(), 1e-5, k)
+
+
+def test_bn_flow_switch_rejects_bad_values(cuda_rt):
+    lib = cuda_rt.lib
+    assert lib.tp_set_bn_flow(3, 0, 0, 0) != 0
+    assert lib.tp_set_bn_flow(1, -1, 0, 0) != 0
+    assert lib.tp_set_bn_flow(1, 0, 9, 0) != 0
+    assert lib.tp_set_bn_flow(1, 0, 0, 0) == 0

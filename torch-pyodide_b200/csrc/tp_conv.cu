@@ -35,7 +35,8 @@ static int g_gemm_kmax = 64;
 int gemm_kmax() { return g_gemm_kmax; }
 
 // Each translation unit that holds tensor-core kernels has its own copy of
-// tc::g_status (this one and tp_conv_nhwc.cu); the status is the first nonzero.
+// tc::g_status (this one and tp_conv_nhwc.cu), and the one-launch BatchNorm of
+// tp_norm.cu has its own word; the status is the first nonzero.
 int tc_status(bool reset) {
   int v = 0;
   TP_CUDA(cudaMemcpyFromSymbol(&v, tc::g_status, sizeof(int)));
@@ -44,7 +45,8 @@ int tc_status(bool reset) {
     TP_CUDA(cudaMemcpyToSymbol(tc::g_status, &z, sizeof(int)));
   }
   const int w = tc_status_nhwc(reset);
-  return v ? v : w;
+  const int n = norm_status(reset);
+  return v ? v : (w ? w : n);
 }
 
 // ---- per-channel sum of an NCHW tensor (conv_backward.wgsl:103-119) ---------------

@@ -38,6 +38,8 @@ void launch_bn_train(const float* x, const float* w, const float* b, float* rm, 
                      float momentum, bool relu);
 void launch_bn_backward(const float* dy, const float* x, const float* relu_src, const float* w, const float* mean,
                         const float* invstd, float* dx, float* dw, float* db, int64_t N, int64_t C, int64_t S);
+// status word of the one-launch BatchNorm's bounded waits (0: none expired)
+int norm_status(bool reset);
 void launch_ln_fwd(const float* x, const float* g, const float* b, float* y, float* sm, float* sr, int64_t rows,
                    int64_t D, float eps);
 void launch_ln_bwd(const float* dy, const float* x, const float* g, const float* sm, const float* sr, float* dx,

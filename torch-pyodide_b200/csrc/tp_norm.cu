@@ -162,11 +162,468 @@ __global__ void k_bn_bwd_apply(const float* __restrict__ dy, const float* __rest
   }
 }
 
+// ---- BatchNorm train forward / backward in one launch (large tensors) -------------------
+// The two-pass form reads x (and dy) twice from HBM once the tensor outgrows
+// L2.  Here a persistent grid claims work items from one atomic counter, so
+// items start in a fixed global order: "sum" items (channel c, image range k)
+// publish f64 partials of channel c; "apply" items over the same ranges
+// combine channel c's partials (fixed order, so every item of the channel
+// derives the same mean / inv_std or coefficients) and write y (dx).  The
+// apply items of channel c come `lag` channels after its sum items, so most of
+// the bytes they re-read are still in L2 (measured on [256, 128, 56, 56]: the
+// forward reads 565 MB from DRAM for its 411 MB tensor where the two passes
+// read 822 MB; the backward 1.38 GB for 822 MB of dy and x, against 1.64 GB).
+// Deadlock-free without co-residency: an apply item waits only for
+// sum items claimed before it, a CTA's prefetched next item waits only for its
+// current one, so the earliest unfinished item can always proceed.  Every wait
+// is bounded (2 s of %globaltimer); on expiry the item records code 31 in the
+// status word, skips its writes and the kernel carries on.
 
+__device__ int g_norm_status;  // 0 ok; else the code of the first wait that expired
+
+__device__ __forceinline__ unsigned long long norm_timer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+struct FlowGeom {
+  int64_t N, C, S;   // NCHW, S = H*W (S % 4 == 0)
+  int per;           // images per item
+  int ch;            // items per channel per phase = ceil(N / per)
+  int lag;           // channels between a channel's sum items and its apply items
+  int64_t total;     // 2 * C * ch
+};
+
+// item -> (apply?, channel, range): sum(0..lag-1), then [apply(j), sum(lag+j)]
+// for j = 0..C-lag-1, then apply(C-lag..C-1); each bracket is ch items per channel.
+__device__ __forceinline__ void flow_item(const FlowGeom& g, int64_t i, bool& apply, int64_t& c, int& k) {
+  const int64_t L = g.lag < g.C ? g.lag : g.C, ch = g.ch;
+  const int64_t head = L * ch, pairs = (g.C - L) * 2 * ch;
+  if (i < head) {
+    apply = false;
+    c = i / ch;
+    k = (int)(i % ch);
+  } else if (i < head + pairs) {
+    const int64_t j = (i - head) / (2 * ch), r = (i - head) % (2 * ch);
+    apply = r < ch;
+    c = apply ? j : L + j;
+    k = (int)(apply ? r : r - ch);
+  } else {
+    const int64_t t = i - head - pairs;
+    apply = true;
+    c = (g.C - L) + t / ch;
+    k = (int)(t % ch);
+  }
+}
+
+// Sum over the item's (image, position) float4s of channel c with F (a
+// ChanStatsF / ChanBnBwdF of tp_chanred.cuh), 4 loads in flight per thread,
+// block-combined in a fixed order; thread 0 gets the totals.
+template <class F>
+__device__ __forceinline__ void flow_sum(const F& f, const FlowGeom& g, int64_t c, int64_t n0, int64_t n1,
+                                         FastDiv fs4, double* sh, double& ta, double& tb) {
+  double a = 0.0, b = 0.0;
+  const uint32_t S4 = (uint32_t)(g.S >> 2), cnt = (uint32_t)((n1 - n0) * S4), step = blockDim.x;
+  uint32_t i = threadIdx.x;
+  for (; i + 3 * step < cnt; i += 4 * step) {
+    typename F::V v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const uint32_t ii = i + u * step, dn = fs4.div(ii), s4 = ii - dn * S4;
+      v[u] = f.load4(((n0 + dn) * g.C + c) * (int64_t)S4 + s4);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) f.use4(v[u], c, a, b);
+  }
+  for (; i < cnt; i += step) {
+    const uint32_t dn = fs4.div(i), s4 = i - dn * S4;
+    f.acc4(((n0 + dn) * g.C + c) * (int64_t)S4 + s4, c, a, b);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a += __shfl_xor_sync(0xffffffffu, a, o);
+    b += __shfl_xor_sync(0xffffffffu, b, o);
+  }
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if (lane == 0) {
+    sh[2 * w] = a;
+    sh[2 * w + 1] = b;
+  }
+  __syncthreads();
+  ta = 0.0;
+  tb = 0.0;
+  if (threadIdx.x == 0)
+    for (int k = 0; k < nw; ++k) {
+      ta += sh[2 * k];
+      tb += sh[2 * k + 1];
+    }
+}
+
+// Thread 0, after flow_sum: publish this item's partials and count it for
+// channel c.  The release add orders the two stores before the count and does
+// not wait for a reply, so the CTA moves on at once.
+__device__ __forceinline__ void flow_publish(double* part, int* cnt, const FlowGeom& g, int64_t c, int k, double ta,
+                                             double tb) {
+  __stcg(&part[(c * g.ch + k) * 2], ta);
+  __stcg(&part[(c * g.ch + k) * 2 + 1], tb);
+  asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(cnt + c) : "memory");
+}
+
+// Warp 0 of an apply item: wait (bounded) until all ch sum items of channel c
+// are counted, then combine their partials lane-strided with a fixed xor tree
+// (the same order on every item and run).  Returns false on every lane if the
+// wait expired (code 31 in the status word).
+__device__ __forceinline__ bool flow_combine(const double* part, const int* cnt, const FlowGeom& g, int64_t c,
+                                             double& a, double& b) {
+  const int lane = threadIdx.x & 31;
+  int ok = 1;
+  if (lane == 0) {
+    const int* p = cnt + c;
+    unsigned long long t0 = 0;
+    for (uint32_t it = 0;; ++it) {
+      int v;
+      asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+      if (v >= g.ch) break;
+      if (it == 0) {
+        t0 = norm_timer();
+      } else if ((it & 63) == 0 && norm_timer() - t0 > 2000000000ull) {
+        atomicCAS(&g_norm_status, 0, 31);
+        ok = 0;
+        break;
+      }
+      __nanosleep(128);
+    }
+  }
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  a = 0.0;
+  b = 0.0;
+  if (!ok) return false;
+  __threadfence();
+  for (int j = lane; j < g.ch; j += 32) {
+    a += __ldcg(&part[(c * g.ch + j) * 2]);
+    b += __ldcg(&part[(c * g.ch + j) * 2 + 1]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a += __shfl_xor_sync(0xffffffffu, a, o);
+    b += __shfl_xor_sync(0xffffffffu, b, o);
+  }
+  return true;
+}
+
+__device__ __forceinline__ unsigned long long flow_claim(unsigned long long* head) {
+  return atomicAdd(head, 1ull);
+}
+
+// 16-byte vectors per thread in flight in an apply item: 4 of x forward, 2 each of
+// dy, x (and relu_src) backward, so both kernels fit four CTAs per SM
+constexpr int FLOW_U = 4, FLOW_UB = 2;
+
+__device__ __forceinline__ float4 bn_fwd4(float4 v, float mu, float sc, float bs, int relu) {
+  float r0 = (v.x - mu) * sc + bs, r1 = (v.y - mu) * sc + bs, r2 = (v.z - mu) * sc + bs, r3 = (v.w - mu) * sc + bs;
+  if (relu) {
+    r0 = fmaxf(r0, 0.0f);
+    r1 = fmaxf(r1, 0.0f);
+    r2 = fmaxf(r2, 0.0f);
+    r3 = fmaxf(r3, 0.0f);
+  }
+  return make_float4(r0, r1, r2, r3);
+}
+
+// y = relu?((x - mean) * (inv_std * w) + b) over the tensor, statistics and
+// running stats as launch_bn_train's two-pass form; the apply items with k == 0
+// write save_mean / save_invstd and the running statistics.
+__global__ void __launch_bounds__(256, 4) k_bn_flow_fwd(const float* __restrict__ x, const float* __restrict__ w,
+                                                        const float* __restrict__ b, float* __restrict__ rm,
+                                                        float* __restrict__ rv, float* __restrict__ y,
+                                                        float* __restrict__ save_mean,
+                                                        float* __restrict__ save_invstd, FlowGeom g, float eps,
+                                                        float momentum, int relu, FastDiv fs4,
+                                                        double* __restrict__ part, int* __restrict__ cnt,
+                                                        unsigned long long* __restrict__ head) {
+  ::tp::pdl_enter();
+  __shared__ double sh[64];
+  __shared__ float s_par[3];
+  __shared__ int s_ok;
+  __shared__ unsigned long long s_item[2];
+  const double M = (double)(g.N * g.S);
+  const uint32_t S4 = (uint32_t)(g.S >> 2), step = blockDim.x;
+  const float4* x4 = reinterpret_cast<const float4*>(x);
+  float4* y4 = reinterpret_cast<float4*>(y);
+  if (threadIdx.x == 0) s_item[0] = flow_claim(head);
+  __syncthreads();
+  int par = 0;
+  unsigned long long item = s_item[0];
+  while (item < (unsigned long long)g.total) {
+    // the claim of the next item is in flight while this one runs
+    unsigned long long nxt = 0;
+    if (threadIdx.x == 0) nxt = flow_claim(head);
+    bool apply;
+    int64_t c;
+    int k;
+    flow_item(g, (int64_t)item, apply, c, k);
+    const int64_t n0 = (int64_t)k * g.per, n1 = n0 + g.per < g.N ? n0 + g.per : g.N;
+    const uint32_t n = (uint32_t)((n1 - n0) * S4);
+    auto at = [&](uint32_t i) {
+      const uint32_t dn = fs4.div(i), s4 = i - dn * S4;
+      return ((n0 + dn) * g.C + c) * (int64_t)S4 + s4;
+    };
+    if (!apply) {
+      double ta, tb;
+      flow_sum(ChanStatsF{x}, g, c, n0, n1, fs4, sh, ta, tb);
+      if (threadIdx.x == 0) flow_publish(part, cnt, g, c, k, ta, tb);
+    } else {
+      // the first vectors are requested before the channel's statistics arrive
+      float4 v[FLOW_U];
+#pragma unroll
+      for (int u = 0; u < FLOW_U; ++u)
+        if (threadIdx.x + u * step < n) v[u] = __ldcs(x4 + at(threadIdx.x + u * step));
+      if (threadIdx.x < 32) {
+        double s, q;
+        const bool ok = flow_combine(part, cnt, g, c, s, q);
+        if (threadIdx.x == 0) {
+          s_ok = ok ? 1 : 0;
+          if (ok) {
+            // the formulas of k_bn_finish
+            const double mean = s / M;
+            double var = q / M - mean * mean;
+            if (var < 0.0) var = 0.0;
+            const float mu = (float)mean, is = (float)(1.0 / sqrt(var + (double)eps));
+            s_par[0] = mu;
+            s_par[1] = is * (w ? w[c] : 1.0f);
+            s_par[2] = b ? b[c] : 0.0f;
+            if (k == 0) {
+              save_mean[c] = mu;
+              save_invstd[c] = is;
+              if (rm) rm[c] = (float)(mean * momentum + (double)rm[c] * (1.0 - momentum));
+              if (rv) rv[c] = (float)(var * M / (M - 1.0) * momentum + (double)rv[c] * (1.0 - momentum));
+            }
+          }
+        }
+      }
+      __syncthreads();
+      if (s_ok) {
+        const float mu = s_par[0], sc = s_par[1], bs = s_par[2];
+        uint32_t i = threadIdx.x;
+        for (;;) {
+#pragma unroll
+          for (int u = 0; u < FLOW_U; ++u)
+            if (i + u * step < n) __stcs(y4 + at(i + u * step), bn_fwd4(v[u], mu, sc, bs, relu));
+          i += FLOW_U * step;
+          if (i >= n) break;
+#pragma unroll
+          for (int u = 0; u < FLOW_U; ++u)
+            if (i + u * step < n) v[u] = __ldcs(x4 + at(i + u * step));
+        }
+      }
+    }
+    // one barrier per item: this item's shared state is consumed and the next
+    // item's index (the other slot) is visible
+    if (threadIdx.x == 0) s_item[par ^ 1] = nxt;
+    __syncthreads();
+    par ^= 1;
+    item = s_item[par];
+  }
+}
+
+// dx = w*inv_std * (g - mean(g) - x_hat * mean(g*x_hat)) with g masked by
+// relu_src > 0 when given; dw = sum(g*x_hat), db = sum(g) (written by the apply
+// items with k == 0), as launch_bn_backward.
+__global__ void __launch_bounds__(256, 3) k_bn_flow_bwd(const float* __restrict__ dy, const float* __restrict__ x,
+                                                        const float* __restrict__ relu_src,
+                                                        const float* __restrict__ w, const float* __restrict__ mean,
+                                                        const float* __restrict__ invstd, float* __restrict__ dx,
+                                                        float* __restrict__ dw, float* __restrict__ db, FlowGeom g,
+                                                        FastDiv fs4, double* __restrict__ part,
+                                                        int* __restrict__ cnt,
+                                                        unsigned long long* __restrict__ head) {
+  ::tp::pdl_enter();
+  __shared__ double sh[64];
+  __shared__ float s_par[5];
+  __shared__ int s_ok;
+  __shared__ unsigned long long s_item[2];
+  const double M = (double)(g.N * g.S);
+  const uint32_t S4 = (uint32_t)(g.S >> 2), step = blockDim.x;
+  const bool hr = relu_src != nullptr;
+  const float4* g4 = reinterpret_cast<const float4*>(dy);
+  const float4* x4 = reinterpret_cast<const float4*>(x);
+  const float4* r4 = reinterpret_cast<const float4*>(relu_src);
+  float4* dx4 = reinterpret_cast<float4*>(dx);
+  if (threadIdx.x == 0) s_item[0] = flow_claim(head);
+  __syncthreads();
+  int par = 0;
+  unsigned long long item = s_item[0];
+  while (item < (unsigned long long)g.total) {
+    unsigned long long nxt = 0;
+    if (threadIdx.x == 0) nxt = flow_claim(head);
+    bool apply;
+    int64_t c;
+    int k;
+    flow_item(g, (int64_t)item, apply, c, k);
+    const int64_t n0 = (int64_t)k * g.per, n1 = n0 + g.per < g.N ? n0 + g.per : g.N;
+    const uint32_t n = (uint32_t)((n1 - n0) * S4);
+    auto at = [&](uint32_t i) {
+      const uint32_t dn = fs4.div(i), s4 = i - dn * S4;
+      return ((n0 + dn) * g.C + c) * (int64_t)S4 + s4;
+    };
+    if (!apply) {
+      double ta, tb;
+      flow_sum(ChanBnBwdF{dy, x, relu_src, mean, invstd}, g, c, n0, n1, fs4, sh, ta, tb);
+      if (threadIdx.x == 0) flow_publish(part, cnt, g, c, k, ta, tb);
+    } else {
+      float4 gv[FLOW_UB], xv[FLOW_UB], rv[FLOW_UB];
+#pragma unroll
+      for (int u = 0; u < FLOW_UB; ++u)
+        if (threadIdx.x + u * step < n) {
+          const int64_t j = at(threadIdx.x + u * step);
+          gv[u] = __ldcs(g4 + j);
+          xv[u] = __ldcs(x4 + j);
+          if (hr) rv[u] = __ldcs(r4 + j);
+        }
+      if (threadIdx.x < 32) {
+        double sa, sb;
+        const bool ok = flow_combine(part, cnt, g, c, sa, sb);
+        if (threadIdx.x == 0) {
+          s_ok = ok ? 1 : 0;
+          if (ok) {
+            // the coefficients of k_bn_bwd_finish
+            s_par[0] = mean[c];
+            s_par[1] = invstd[c];
+            s_par[2] = (w ? w[c] : 1.0f) * invstd[c];
+            s_par[3] = (float)(sa / M);
+            s_par[4] = (float)(sb / M);
+            if (k == 0) {
+              if (dw) dw[c] = (float)sb;
+              if (db) db[c] = (float)sa;
+            }
+          }
+        }
+      }
+      __syncthreads();
+      if (s_ok) {
+        const float mu = s_par[0], is = s_par[1], k0 = s_par[2], k1 = s_par[3], k2 = s_par[4];
+        uint32_t i = threadIdx.x;
+        for (;;) {
+#pragma unroll
+          for (int u = 0; u < FLOW_UB; ++u)
+            if (i + u * step < n) {
+              const float4 r = hr ? rv[u] : make_float4(1.f, 1.f, 1.f, 1.f);
+              __stcs(dx4 + at(i + u * step),
+                     make_float4(bn_bwd1(gv[u].x, r.x, hr, xv[u].x, mu, is, k0, k1, k2),
+                                 bn_bwd1(gv[u].y, r.y, hr, xv[u].y, mu, is, k0, k1, k2),
+                                 bn_bwd1(gv[u].z, r.z, hr, xv[u].z, mu, is, k0, k1, k2),
+                                 bn_bwd1(gv[u].w, r.w, hr, xv[u].w, mu, is, k0, k1, k2)));
+            }
+          i += FLOW_UB * step;
+          if (i >= n) break;
+#pragma unroll
+          for (int u = 0; u < FLOW_UB; ++u)
+            if (i + u * step < n) {
+              const int64_t j = at(i + u * step);
+              gv[u] = __ldcs(g4 + j);
+              xv[u] = __ldcs(x4 + j);
+              if (hr) rv[u] = __ldcs(r4 + j);
+            }
+        }
+      }
+    }
+    if (threadIdx.x == 0) s_item[par ^ 1] = nxt;
+    __syncthreads();
+    par ^= 1;
+    item = s_item[par];
+  }
+}
+
+// 0 = always the two-pass kernels; 1 (default) = the one-launch form for
+// tensors of at least 32 MB with H*W % 4 == 0; 2 = the one-launch form whenever
+// H*W % 4 == 0 (testing).  g_bn_flow_lag > 0 overrides the lag in channels,
+// g_bn_flow_ctas > 0 the CTAs per SM.
+static int g_bn_flow = 1;
+static int g_bn_flow_lag = 0;
+static int g_bn_flow_ctas = 4;
+static int g_bn_flow_item = 16384;  // values per item (whole images of one channel)
+
+static bool use_flow(int64_t N, int64_t C, int64_t S) {
+  if (g_bn_flow == 0 || (S & 3) != 0 || N < 1 || C < 1) return false;
+  if ((N * C * S >> 2) >= ((int64_t)1 << 31) || (N * (S >> 2)) >= ((int64_t)1 << 31)) return false;
+  return g_bn_flow == 2 || N * C * S * 4 >= ((int64_t)32 << 20);
+}
+
+// Items of about 16 K values (a few images of one channel).  A channel's apply
+// items are claimed 2 x lag x ch claims after its sum items while about one
+// item per CTA is in progress, so a lag near grid / ch channels lets most apply
+// items find their channel complete; each channel of lag adds the channel's
+// bytes read (and written) to what L2 must hold until the re-read.  Measured
+// on [256, 128, 56, 56] (grid 592 forward, 444 backward, 52 items per channel):
+// lag 10 / 8 = 7/8 of grid / ch, plus one, beat 6 (apply items wait) and 12-14
+// (fewer re-reads hit L2): forward 0.191 ms, backward 0.315 ms, against 0.207 /
+// 0.358 ms for the two passes; 8 K-value items lose to their overheads, 32 K
+// ones to the wider window.
+static FlowGeom flow_geom(int64_t N, int64_t C, int64_t S, int grid) {
+  FlowGeom g;
+  g.N = N;
+  g.C = C;
+  g.S = S;
+  int64_t per = g_bn_flow_item / S;
+  if (per < 1) per = 1;
+  if (per > N) per = N;
+  g.per = (int)per;
+  g.ch = (int)((N + per - 1) / per);
+  int64_t lag = ((int64_t)grid * 7 / 8) / g.ch + 1;
+  if (g_bn_flow_lag > 0) lag = g_bn_flow_lag;
+  g.lag = (int)(lag < C ? lag : C);
+  g.total = 2 * C * g.ch;
+  return g;
+}
+
+template <class K>
+static int flow_grid(K kernel) {
+  static int fit = 0;
+  if (!fit) {
+    int n = 0;
+    TP_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, 256, 0));
+    fit = n < 1 ? 1 : n;
+  }
+  const int per_sm = g_bn_flow_ctas < fit ? g_bn_flow_ctas : fit;
+  return sm_count() * per_sm;
+}
+
+// part | cnt | head in one scratch area; the counters and the head start at zero.
+static void flow_scratch(const FlowGeom& g, double*& part, int*& cnt, unsigned long long*& head) {
+  const size_t pb = ((size_t)g.C * g.ch * 2 * sizeof(double) + 255) & ~(size_t)255;
+  const size_t cb = ((size_t)g.C * sizeof(int) + 255) & ~(size_t)255;
+  char* ws = (char*)scratch(pb + cb + 256);
+  part = (double*)ws;
+  cnt = (int*)(ws + pb);
+  head = (unsigned long long*)(ws + pb + cb);
+  TP_CUDA(cudaMemsetAsync(ws + pb, 0, cb + 256, stream()));
+}
+
+int norm_status(bool reset) {
+  int v = 0;
+  TP_CUDA(cudaMemcpyFromSymbol(&v, g_norm_status, sizeof(int)));
+  if (reset && v) {
+    int z = 0;
+    TP_CUDA(cudaMemcpyToSymbol(g_norm_status, &z, sizeof(int)));
+  }
+  return v;
+}
 
 void launch_bn_train(const float* x, const float* w, const float* b, float* rm, float* rv, float* y,
                      float* save_mean, float* save_invstd, int64_t N, int64_t C, int64_t S, float eps,
                      float momentum, bool relu) {
+  if (use_flow(N, C, S)) {
+    const int grid = flow_grid(k_bn_flow_fwd);
+    const FlowGeom g = flow_geom(N, C, S, grid);
+    double* part;
+    int* cnt;
+    unsigned long long* head;
+    flow_scratch(g, part, cnt, head);
+    TP_LAUNCH(k_bn_flow_fwd, grid, 256, 0, x, w, b, rm, rv, y, save_mean, save_invstd, g, eps, momentum,
+              relu ? 1 : 0, chan_div4(S), part, cnt, head);
+    return;
+  }
   int splits = chan_splits(C, N, S, sm_count());
   double* part = (double*)scratch((size_t)C * splits * 2 * sizeof(double));
   auto kst = k_chan_reduce<ChanStatsF>;
@@ -180,6 +637,17 @@ void launch_bn_train(const float* x, const float* w, const float* b, float* rm, 
 
 void launch_bn_backward(const float* dy, const float* x, const float* relu_src, const float* w, const float* mean,
                         const float* invstd, float* dx, float* dw, float* db, int64_t N, int64_t C, int64_t S) {
+  if (use_flow(N, C, S)) {
+    const int grid = flow_grid(k_bn_flow_bwd);
+    const FlowGeom g = flow_geom(N, C, S, grid);
+    double* part;
+    int* cnt;
+    unsigned long long* head;
+    flow_scratch(g, part, cnt, head);
+    TP_LAUNCH(k_bn_flow_bwd, grid, 256, 0, dy, x, relu_src, w, mean, invstd, dx, dw, db, g, chan_div4(S), part, cnt,
+              head);
+    return;
+  }
   int splits = chan_splits(C, N, S, sm_count());
   size_t pb = (size_t)C * splits * 2 * sizeof(double);
   char* ws = (char*)scratch(pb + (size_t)C * 3 * sizeof(float) + 64);
@@ -715,6 +1183,20 @@ static const float* opt_ptr(int64_t id, int64_t expect) {
 using namespace tp;
 
 extern "C" {
+
+TP_API int tp_set_bn_flow(int mode, int lag, int ctas_per_sm, int item_values) {
+  return guard([&] {
+    TP_REQUIRE(mode >= 0 && mode <= 2, "tp_set_bn_flow: mode 0 (two passes), 1 (one launch for large tensors) or 2 "
+                                       "(one launch whenever H*W %% 4 == 0)");
+    TP_REQUIRE(lag >= 0 && ctas_per_sm >= 0 && ctas_per_sm <= 8 && item_values >= 0,
+               "tp_set_bn_flow: lag >= 0 (0: automatic), CTAs per SM in [0, 8] (0: 4), values per item >= 0 "
+               "(0: 16384)");
+    g_bn_flow = mode;
+    g_bn_flow_lag = lag;
+    g_bn_flow_ctas = ctas_per_sm > 0 ? ctas_per_sm : 4;
+    g_bn_flow_item = item_values > 0 ? item_values : 16384;
+  });
+}
 
 TP_API int tp_batch_norm(int64_t input, int64_t weight, int64_t bias, int64_t running_mean, int64_t running_var,
                          float eps, tp_handle* out) {

@@ -144,6 +144,7 @@ SIGNATURES: dict[str, list] = {
     "tp_wait_probe": [I64],
     "tp_set_gemm_kmax": [INT],
     "tp_set_gemm_twocta": [INT],
+    "tp_set_bn_flow": [INT, INT, INT, INT],
     "tp_matmul": [I64, I64, HP],
     "tp_linear": [I64, I64, I64, HP],
     "tp_conv2d": [I64, I64, F32P, INT, I64P, INT, I64P, INT, I64P, INT, INT, HP],
