@@ -23,7 +23,7 @@ Two kinds of fixture:
    each with both values and the reason (the recording disagrees with the
    reference's own shader arithmetic, or its seed cannot be recovered).  ``pretrained/<name>.json`` -- the real-PyTorch pretrained
    bundles the reference's browser tests load (state dict, sample input,
-   predictions), for tests/test_gpu_dropin.py.
+   predictions), for tests/test_gpu_zz_dropin.py.
 
 Usage: python tests/golden/make_golden.py [--reference /root/reference]
 """

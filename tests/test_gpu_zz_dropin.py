@@ -14,7 +14,9 @@ runtime, against the same scripts on the CPU oracle runtime.
   oracle's.
 
 Runs only where the reference package travels with the repository
-(baseline/_ref); each script runs in its own process.
+(baseline/_ref); each script runs in its own process.  These whole-program
+runs (minutes of CPU oracle work) are named to be collected after the kernel
+tests, so a run that stops at its first failure has checked every kernel.
 """
 import json
 import os
