@@ -51,3 +51,23 @@ def test_no_device_reports_unavailable(lib):
     assert lib.tp_init(0) != 0  # an error status, not a crash or a CPU fallback
     lib.tp_last_error.restype = ctypes.c_char_p
     assert b"CUDA" in lib.tp_last_error()
+
+
+def test_tuning_switches_check_arguments_without_a_device(lib):
+    """The tuning setters only record a value: they work with no GPU, refuse
+    values outside their documented ranges with a message, and are left at
+    their defaults (the library is one copy per process)."""
+    lib.tp_last_error.restype = ctypes.c_char_p
+    lib.tp_set_bn_flow.argtypes = [ctypes.c_int] * 4
+    lib.tp_set_gemm_kmax.argtypes = [ctypes.c_int]
+    lib.tp_set_gemm_twocta.argtypes = [ctypes.c_int]
+    bad = [(lib.tp_set_bn_flow, (3, 0, 0, 0)), (lib.tp_set_bn_flow, (1, -1, 0, 0)),
+           (lib.tp_set_bn_flow, (1, 0, 9, 0)), (lib.tp_set_bn_flow, (1, 0, 0, -5)),
+           (lib.tp_set_gemm_kmax, (-1,)), (lib.tp_set_gemm_twocta, (3,))]
+    for fn, args in bad:
+        assert fn(*args) != 0, (fn, args)
+        assert lib.tp_last_error(), (fn, args)
+    assert lib.tp_set_bn_flow(0, 4, 2, 8192) == 0
+    assert lib.tp_set_bn_flow(1, 0, 0, 0) == 0
+    assert lib.tp_set_gemm_kmax(64) == 0
+    assert lib.tp_set_gemm_twocta(1) == 0
